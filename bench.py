@@ -1,0 +1,369 @@
+#!/usr/bin/env python
+"""Benchmark of the IQ3_XXS routed-expert MoE layer (BASELINE.json metric:
+MoE-layer tokens/s and achieved HBM GB/s against the measured B200 peak).
+
+Default workload (--workload decode1): BASELINE config 2, one MoE layer at
+batch 1 - hidden 5120, 160 routed experts + 1 shared, intermediate 1536,
+top-8, IQ3_XXS experts from the counter-based generator, fp32 router
+N(0, 0.02), x bf16 N(0, 1).  One step = one token through one layer.  Steps
+cycle through --layers distinct layer copies (8 x 1.45 GB) so consecutive
+steps never find their 85 MB of weights in the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gpeed|reference]
+
+N > 1 (launched by torchrun): every rank runs its own replica of the layer
+stack on its GPU (weak scaling, no data-path collective); value sums tokens
+over ranks and divides by the slowest rank's time.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MoE-layer tokens/s (IQ3_XXS dequant-GEMM); achieved HBM GB/s vs B200 peak"
+H, I, E, K_TOP = 5120, 1536, 160, 8
+EXPERT_BYTES = 3 * I * (H // 256) * 98            # one expert, 3 matrices: 9,031,680 B
+ROUTER_BYTES = E * H * 4
+LAYER_TOKEN_BYTES = (K_TOP + 1) * EXPERT_BYTES + ROUTER_BYTES + H * 2 + H * 4   # ~84.59 MB per token-layer
+GATEUP_BYTES = (K_TOP + 1) * 2 * I * (H // 256) * 98 + H * 2 + (K_TOP + 1) * I * 4  # dominant kernel, per launch
+
+
+def peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d.get("bf16_tflops"), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def env_rank():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.rows = []
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 9:
+                self.rows.append(parts)
+
+    def summary(self, extra_rows=()):
+        rows = list(getattr(self, "rows", [])) + list(extra_rows)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def traffic_from_profiles(name: str):
+    """DRAM bytes per launch recorded from an ncu capture in profiles/ (or None)."""
+    p = os.path.join(REPO, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+def host_layer(seed, stream0, router_seed):
+    from oracle import oracle
+    nb = lambda rows, inn: rows * inn // 256
+    sizes = [nb(E * I, H), nb(E * I, H), nb(E * H, I), nb(I, H), nb(I, H), nb(H, I)]
+    names = ("gate", "up", "down", "gate_sh", "up_sh", "down_sh")
+    layer = {n: oracle.synth_iq3xxs(seed, stream0 + m, sizes[m]) for m, n in enumerate(names)}
+    layer["router"] = router_for(router_seed)
+    layer["corr"] = np.zeros(E, np.float32)
+    return layer
+
+
+def router_for(seed):
+    return (np.random.default_rng(seed).standard_normal((E, H)) * 0.02).astype(np.float32)
+
+
+def tokens(n, seed):
+    import torch
+    return torch.from_numpy(np.random.default_rng(seed).standard_normal((n, H)).astype(np.float32)).to(torch.bfloat16)
+
+
+def cpu_time_layer(kind: str, budget_s: float, max_tokens: int):
+    """The reference CPU expert path (oracle/_ref, or the oracle port) on this host."""
+    from oracle import oracle
+    chk = oracle.Checker(kind)
+    layer = host_layer(1000, 0, 0)
+    shape = oracle.Shape(H, I, E, K_TOP, 2.5, 1, 10.0)
+    X = tokens(max_tokens + 1, 7).float().numpy()
+    chk.moe_forward(shape, layer, X[0])  # warm-up
+    t0 = time.perf_counter()
+    done = 0
+    while done < max_tokens and time.perf_counter() - t0 < budget_s:
+        chk.moe_forward(shape, layer, X[1 + done])
+        done += 1
+    dt = time.perf_counter() - t0
+    return done / dt, done, dt, chk.num_threads()
+
+
+def run_reference(args, world):
+    from oracle import oracle
+    kind = "reference" if oracle.available("reference") else "port"
+    steps = args.steps
+    # each step = one token through one layer on the host cores; the run is
+    # capped at ~120 s of timed work
+    budget = float(os.environ.get("GPEED_REF_BUDGET_S", "120"))
+    chk = oracle.Checker(kind)
+    layer = host_layer(1000, 0, 0)
+    shape = oracle.Shape(H, I, E, K_TOP, 2.5, 1, 10.0)
+    X = tokens(args.warmup + steps, 7).float().numpy()
+    for i in range(args.warmup):
+        chk.moe_forward(shape, layer, X[i])
+    t0 = time.perf_counter()
+    done = 0
+    while done < steps and time.perf_counter() - t0 < budget:
+        chk.moe_forward(shape, layer, X[args.warmup + done])
+        done += 1
+    dt = time.perf_counter() - t0
+    tps = done / dt
+    sample = (f"{done} of {steps} steps (1 token x 1 layer each, H=5120 E=160+1 I=1536 top-8) "
+              f"within a {budget:.0f} s cap; weights RAM-resident")
+    line = {
+        "metric": METRIC, "value": tps, "unit": "tokens/s", "n_gpus": world, "steps": done, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * dt / max(done, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "decode1: MoE layer decode, batch 1 (BASELINE config 2)", "hidden": H,
+                   "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS"},
+        "impl": "reference",
+        "cpu_baseline": {"value": tps, "unit": "tokens/s", "cores": chk.num_threads(), "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": tps, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_gpu(args, rank, local_rank, world):
+    import torch
+    import torch.distributed as dist
+
+    from gpeed_b200 import Context, MoeConfig, MoeLayer
+    from gpeed_b200 import _capi
+
+    torch.cuda.set_device(local_rank)
+    ctx = Context(local_rank)
+    cfg = MoeConfig()
+    L = args.layers
+    layers = [MoeLayer(ctx, cfg, layer_id=l).synth(router_for(l), None, seed=1000 + l, stream0=0) for l in range(L)]
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    # one static token per layer copy; graphs of one forward each
+    xs = [tokens(1, 100 + l).cuda() for l in range(L)]
+    ys = [torch.empty(1, H, device="cuda") for _ in range(L)]
+    with torch.cuda.stream(stream):
+        for l in range(L):  # sizes scratch, configures kernels (outside capture)
+            layers[l].forward(xs[l], ys[l], stream=stream)
+    stream.synchronize()
+    ctx.check(stream)
+    graphs = []
+    for l in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            layers[l].forward(xs[l], ys[l], stream=stream)
+        graphs.append(g)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- device-resident throughput (value) ----
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % L].replay()
+    stream.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for i in range(args.steps):
+                graphs[i % L].replay()
+            ev1.record(stream)
+        stream.synchronize()
+        ms_total = ev0.elapsed_time(ev1)
+        # keep the same work running ~1.5 s so the sampler sees the clocks under this load
+        soak_t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            while time.perf_counter() - soak_t0 < 1.5:
+                for i in range(200):
+                    graphs[i % L].replay()
+                stream.synchronize()
+    barrier()
+    ctx.check(stream)
+    ms_step = ms_total / args.steps
+    if world > 1:
+        t = torch.tensor([ms_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    value = world * args.steps / (ms_total / 1000.0)
+
+    # ---- per-kernel timing of the dominant kernel (events on the launch stream) ----
+    _capi.call("gpeed_ctx_profile", ctx.handle, 1)
+    with torch.cuda.stream(stream):
+        for i in range(max(8 * L, 64)):
+            layers[i % L].forward(xs[i % L], ys[i % L], stream=stream)
+    stage = (ctypes.c_float * 5)()
+    calls = ctypes.c_int()
+    _capi.call("gpeed_ctx_profile_read", ctx.handle, stage, ctypes.byref(calls))
+    _capi.call("gpeed_ctx_profile", ctx.handle, 0)
+    stage_ms = list(stage)
+
+    # ---- end to end through the public API with host buffers ----
+    x_host = tokens(args.steps, 555).pin_memory()
+    y_host = torch.empty(H, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty(1, H, dtype=torch.bfloat16, device="cuda")
+    y_dev = torch.empty(1, H, dtype=torch.float32, device="cuda")
+    e2e_graphs = []
+    with torch.cuda.stream(stream):
+        layers[0].forward(x_dev, y_dev, stream=stream)
+    stream.synchronize()
+    x_slot = x_host[0:1].clone().pin_memory()
+    for l in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            x_dev.copy_(x_slot, non_blocking=True)
+            layers[l].forward(x_dev, y_dev, stream=stream)
+            y_host.copy_(y_dev[0], non_blocking=True)
+        e2e_graphs.append(g)
+    for i in range(args.warmup):
+        with torch.cuda.stream(stream):
+            e2e_graphs[i % L].replay()
+        stream.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        x_slot.copy_(x_host[i:i + 1])       # the step's input lands in the pinned staging buffer
+        with torch.cuda.stream(stream):
+            e2e_graphs[i % L].replay()
+        stream.synchronize()                # the step's result is on the host
+    e2e_s = time.perf_counter() - t0
+    if world > 1:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * args.steps / e2e_s
+    ctx.check(stream)
+
+    hbm_peak, _, peak_src = peaks()
+    gu_ms = stage_ms[2]
+    achieved = GATEUP_BYTES / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else None
+    traffic = traffic_from_profiles("gemv_gateup_decode1.txt")
+    line = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu and world == 1:
+            from oracle import oracle
+            kind = "reference" if oracle.available("reference") else "port"
+            tps, done, dt, cores = cpu_time_layer(kind, args.cpu_seconds, 64)
+            cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
+                   "sample": f"{done} tokens x 1 layer (config 2 shapes) in {dt:.1f} s, weights RAM-resident"}
+        layer_gbs = LAYER_TOKEN_BYTES * value / world / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "iq3_xxs(int8)xint16->f32", "data": "synthetic",
+            "config": {"workload": "decode1: MoE layer decode, batch 1 (BASELINE config 2)", "hidden": H,
+                       "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
+                       "layer_copies": L, "l2": f"inputs larger than L2: steps rotate over {L} layer copies "
+                                              f"({L * 1.454:.1f} GB of weights)",
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "per_gpu_layer_hbm_gbs": layer_gbs,
+                       "per_gpu_layer_hbm_frac": layer_gbs / hbm_peak,
+                       "stage_ms": dict(zip(["router", "route", "gateup", "down", "combine"], stage_ms))},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
+                         "kernel": "gemv_kernel<32,1,gateup> (9 experts x gate+up, batch 1)",
+                         "peak_source": peak_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 4},
+            "gpu_launches": 5 * args.steps,
+            "clocks": clk.summary(),
+        }
+    del graphs, e2e_graphs
+    ctx.close()
+    return line
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="gpeed", choices=["gpeed", "reference"])
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank, local_rank, world = env_rank()
+    if args.impl == "reference":
+        if rank == 0:
+            run_reference(args, world)
+        return 0
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    line = run_gpu(args, rank, local_rank, world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

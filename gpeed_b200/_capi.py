@@ -1,0 +1,80 @@
+"""ctypes binding of libgpeed_moe.so (include/gpeed_moe.h).
+
+The library is the product: there is no Python or CPU fallback.  Loading
+fails loudly when the shared object is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libgpeed_moe.so")
+
+OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_UNSUPPORTED, ERR_NCCL = range(6)
+DTYPE_F32, DTYPE_IQ3_XXS, DTYPE_BF16 = 0, 18, 30
+
+
+class GpeedError(RuntimeError):
+    """Raised for a non-zero status; mirrors the reference's std::runtime_error."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"gpeed error {code}: {msg}")
+        self.code = code
+
+
+class MoeShape(ctypes.Structure):
+    _fields_ = [("hidden", ctypes.c_int), ("inter", ctypes.c_int), ("n_experts", ctypes.c_int),
+                ("top_k", ctypes.c_int), ("n_shared", ctypes.c_int), ("routed_scale", ctypes.c_float),
+                ("norm_topk", ctypes.c_int), ("swiglu_limit", ctypes.c_float)]
+
+
+_vp, _i, _u64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_float
+# name -> argtypes (every function returns int status unless listed in _RESTYPES)
+SIGNATURES = {
+    "gpeed_last_error": [],
+    "gpeed_version": [],
+    "gpeed_ctx_create": [_i, ctypes.POINTER(_vp)],
+    "gpeed_ctx_destroy": [_vp],
+    "gpeed_ctx_check": [_vp, _vp],
+    "gpeed_ctx_profile": [_vp, _i],
+    "gpeed_ctx_profile_read": [_vp, _vp, ctypes.POINTER(_i)],
+    "gpeed_iq3xxs_dequantize": [_vp, _vp, _u64, _vp],
+    "gpeed_tensor_upload": [_vp, _vp, _i, _i, _u64, _i, ctypes.POINTER(_i)],
+    "gpeed_tensor_download": [_vp, _i, _vp],
+    "gpeed_matvec_quant": [_vp, _i, _u64, _i, _i, _vp, _vp, _vp],
+    "gpeed_matmul_quant": [_vp, _i, _u64, _i, _i, _vp, _i, _vp, _vp],
+    "gpeed_moe_load_layer": [_vp, _i, ctypes.POINTER(MoeShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i],
+    "gpeed_moe_synth_layer": [_vp, _i, ctypes.POINTER(MoeShape), _vp, _vp, _i, _u64, _u64],
+    "gpeed_synth_iq3xxs": [_vp, _u64, _u64, _u64, _u64, _vp],
+    "gpeed_moe_forward": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
+}
+_RESTYPES = {"gpeed_last_error": ctypes.c_char_p}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'` "
+                "(or `make -C gpeed_b200/csrc`); there is no CPU fallback")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, args in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = lib
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        msg = load().gpeed_last_error()
+        raise GpeedError(rc, msg.decode() if msg else "")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args))

@@ -1,0 +1,168 @@
+// Block-level IQ3_XXS kernels: the bit-exact fp32 dequantizer (reference
+// cpp/core/src/quant.cpp:186-210 blk_iq3_xxs, :521-573 dequantize), the
+// lossless raw <-> repacked layout conversion used for library-owned weights,
+// the decode-table image, and the device side of the synthetic generator.
+#include <cuda_fp16.h>
+
+#include "iq3xxs.cuh"
+#include "kernels.h"
+#include "synth.h"
+
+namespace gp {
+namespace {
+
+// One warp per 4 blocks: the 392 contiguous bytes are read as 98 aligned
+// 32-bit words (the group of 4 blocks starts 8-byte aligned whenever the
+// tensor is 16-byte aligned), staged in shared memory, then each lane decodes
+// one 32-weight sub-block and writes 32 floats with 16-byte stores.
+constexpr int kDqWarps = 8;
+
+__global__ void __launch_bounds__(32 * kDqWarps) dequant_kernel(const uint8_t* __restrict__ raw, float* __restrict__ dst,
+                                                                int64_t nblocks) {
+    __shared__ uint32_t s_grid[256];
+    __shared__ __align__(16) uint8_t s_blk[kDqWarps][4 * 98 + 8];
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_grid[i] = gp_iq3xxs_grid_dev[i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t ngroups = (nblocks + 3) / 4;
+    for (int64_t grp = (int64_t)blockIdx.x * kDqWarps + warp; grp < ngroups; grp += (int64_t)gridDim.x * kDqWarps) {
+        const int64_t b0 = grp * 4;
+        const int nb = (int)gp_min64(4, nblocks - b0);
+        const uint8_t* src = raw + b0 * 98;
+        // byte-granular staging (keeps any source alignment legal)
+        for (int i = lane; i < nb * 98; i += 32) s_blk[warp][i] = src[i];
+        __syncwarp();
+        const int blk = lane >> 3, ib = lane & 7;
+        if (blk < nb) {
+            const uint8_t* p = s_blk[warp] + blk * 98;
+            const uint16_t dh = (uint16_t)(p[0] | (p[1] << 8));
+            const float d = __half2float(__ushort_as_half(dh));  // exact, incl. subnormals
+            const uint8_t* qs = p + 2 + 8 * ib;
+            const uint8_t* sa = p + 66 + 4 * ib;
+            const uint32_t aux = (uint32_t)sa[0] | ((uint32_t)sa[1] << 8) | ((uint32_t)sa[2] << 16) |
+                                 ((uint32_t)sa[3] << 24);
+            const float db = iq3_db(d, aux);
+            float out[32];
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const uint32_t k7 = (aux >> (7 * l)) & 127u;
+                const uint32_t signs = k7 | ((uint32_t)(__popc(k7) & 1) << 7);
+                const uint32_t g1 = s_grid[qs[2 * l]], g2 = s_grid[qs[2 * l + 1]];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    out[8 * l + j] = iq3_weight_f32(db, (g1 >> (8 * j)) & 0xFF, (signs >> j) & 1);
+                    out[8 * l + j + 4] = iq3_weight_f32(db, (g2 >> (8 * j)) & 0xFF, (signs >> (j + 4)) & 1);
+                }
+            }
+            float4* o = reinterpret_cast<float4*>(dst + (b0 + blk) * 256 + 32 * ib);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
+        }
+        __syncwarp();
+    }
+}
+
+// raw row-major blocks -> row groups of 8: [qs 8 x nblk x 64][aux 8 x nblk x 32][d 8 x nblk x 2]
+// One thread per (row, block); rows past `rows` in the last group are zero-filled.
+__global__ void repack_kernel(uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int64_t rows, int nblk,
+                              bool unpack) {
+    const int64_t rows_pad = (rows + 7) / 8 * 8;
+    const int64_t total = rows_pad * nblk;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = i / nblk;
+        const int b = (int)(i % nblk);
+        const int64_t grp = row / 8;
+        const int ri = (int)(row % 8);
+        uint8_t* g = out + grp * 784 * nblk;
+        uint8_t* qs = g + (ri * nblk + b) * 64;
+        uint8_t* ax = g + 512 * nblk + (ri * nblk + b) * 32;
+        uint8_t* dd = g + 768 * nblk + (ri * nblk + b) * 2;
+        if (!unpack) {
+            if (row < rows) {
+                const uint8_t* s = raw + (row * nblk + b) * 98;
+                dd[0] = s[0];
+                dd[1] = s[1];
+                for (int j = 0; j < 64; ++j) qs[j] = s[2 + j];
+                for (int j = 0; j < 32; ++j) ax[j] = s[66 + j];
+            } else {
+                dd[0] = dd[1] = 0;
+                for (int j = 0; j < 64; ++j) qs[j] = 0;
+                for (int j = 0; j < 32; ++j) ax[j] = 0;
+            }
+        } else if (row < rows) {
+            uint8_t* s = raw + (row * nblk + b) * 98;  // raw is the destination when unpacking
+            s[0] = dd[0];
+            s[1] = dd[1];
+            for (int j = 0; j < 64; ++j) s[2 + j] = qs[j];
+            for (int j = 0; j < 32; ++j) s[66 + j] = ax[j];
+        }
+    }
+}
+
+__global__ void tables_kernel(uint8_t* dst) {
+    iq3_build_tables(dst, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
+}
+
+// 128 blocks per CTA, generated into shared memory, written out with 16-byte stores
+// when the destination run is 16-byte aligned (it is for block0 % 8 == 0).
+__global__ void synth_kernel(uint8_t* __restrict__ dst, uint64_t seed, uint64_t stream, uint64_t block0,
+                             int64_t nblocks) {
+    __shared__ __align__(16) uint8_t s_buf[128 * 98];
+    for (int64_t base = (int64_t)blockIdx.x * 128; base < nblocks; base += (int64_t)gridDim.x * 128) {
+        const int nb = (int)gp_min64(128, nblocks - base);
+        if ((int)threadIdx.x < nb) gp_synth_iq3xxs_block(seed, stream, block0 + base + threadIdx.x, s_buf + threadIdx.x * 98);
+        __syncthreads();
+        uint8_t* out = dst + base * 98;
+        const int bytes = nb * 98;
+        if ((reinterpret_cast<uintptr_t>(out) & 15) == 0 && (bytes & 15) == 0) {
+            for (int i = threadIdx.x; i < bytes / 16; i += blockDim.x)
+                reinterpret_cast<uint4*>(out)[i] = reinterpret_cast<const uint4*>(s_buf)[i];
+        } else {
+            for (int i = threadIdx.x; i < bytes; i += blockDim.x) out[i] = s_buf[i];
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_dequantize(const uint8_t* raw, float* dst, int64_t nblocks, cudaStream_t st) {
+    if (nblocks <= 0) return cudaSuccess;
+    const int64_t groups = (nblocks + 3) / 4;
+    const int grid = (int)gp_min64((groups + kDqWarps - 1) / kDqWarps, 148 * 16);
+    dequant_kernel<<<grid, 32 * kDqWarps, 0, st>>>(raw, dst, nblocks);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack(const uint8_t* raw, uint8_t* packed, int64_t rows, int in_dim, cudaStream_t st) {
+    const int nblk = in_dim / 256;
+    const int64_t total = (rows + 7) / 8 * 8 * nblk;
+    if (total == 0) return cudaSuccess;
+    const int grid = (int)gp_min64((total + 255) / 256, 148 * 32);
+    repack_kernel<<<grid, 256, 0, st>>>(const_cast<uint8_t*>(raw), packed, rows, nblk, false);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_unpack(const uint8_t* packed, uint8_t* raw, int64_t rows, int in_dim, cudaStream_t st) {
+    const int nblk = in_dim / 256;
+    const int64_t total = (rows + 7) / 8 * 8 * nblk;
+    if (total == 0) return cudaSuccess;
+    const int grid = (int)gp_min64((total + 255) / 256, 148 * 32);
+    repack_kernel<<<grid, 256, 0, st>>>(raw, const_cast<uint8_t*>(packed), rows, nblk, true);
+    return cudaGetLastError();
+}
+
+cudaError_t build_tables(uint8_t* dst, cudaStream_t st) {
+    tables_kernel<<<64, 256, 0, st>>>(dst);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_synth(uint8_t* dst, uint64_t seed, uint64_t stream, uint64_t block0, int64_t nblocks,
+                         cudaStream_t st) {
+    if (nblocks <= 0) return cudaSuccess;
+    const int grid = (int)gp_min64((nblocks + 127) / 128, 148 * 64);
+    synth_kernel<<<grid, 128, 0, st>>>(dst, seed, stream, block0, nblocks);
+    return cudaGetLastError();
+}
+
+}  // namespace gp

@@ -1,0 +1,611 @@
+// C ABI of libgpeed_moe.so (declared in include/gpeed_moe.h): context,
+// weight registry, and the orchestration of the MoE layer forward
+//   router -> route (top-k, histogram, permutation, slots)
+//          -> gate/up GEMV + SwiGLU -> down GEMV -> weighted combine
+// as a chain of kernels on one stream with programmatic dependent launch.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "../../include/gpeed_moe.h"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+#define GP_CUDA(call)                                                                        \
+    do {                                                                                     \
+        cudaError_t e_ = (call);                                                             \
+        if (e_ != cudaSuccess) return fail(GPEED_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+struct Tensor {
+    uint8_t* packed = nullptr;
+    int64_t rows = 0;
+    int in_dim = 0;
+};
+
+struct Layer {
+    gpeed_moe_shape shape{};
+    float* router = nullptr;
+    float* corr = nullptr;
+    uint8_t* gate = nullptr;  // repacked, (E + n_shared) experts x I rows of H
+    uint8_t* up = nullptr;
+    uint8_t* down = nullptr;  // (E + n_shared) experts x H rows of I
+    int64_t gu_stride = 0, d_stride = 0;
+};
+
+template <typename T>
+struct DevBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    int ensure(size_t want) {
+        if (want <= n) return GPEED_OK;
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+        if (cudaMalloc(&p, want * sizeof(T)) != cudaSuccess)
+            return fail(GPEED_ERR_CUDA, "cudaMalloc(%zu bytes) failed", want * sizeof(T));
+        n = want;
+        return GPEED_OK;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+};
+
+int64_t padded_rows(int64_t rows) { return (rows + 7) / 8 * 8 + 32; }
+
+}  // namespace
+
+struct gpeed_ctx {
+    int device = 0;
+    int num_sms = 148;
+    uint8_t* tables = nullptr;
+    uint32_t* status = nullptr;
+    std::vector<Tensor> tensors;
+    std::map<int, Layer> layers;
+    // forward scratch (grown on demand; grow before capturing a graph)
+    DevBuf<float> partial, topk_w, h, D, mvout;
+    DevBuf<int> topk_ids, perm, inv_pos, counts, nslots;
+    DevBuf<gp::SlotDesc> slots;
+    // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
+    bool prof = false;
+    cudaEvent_t ev[6] = {};
+    double prof_ms[5] = {0, 0, 0, 0, 0};
+    long prof_calls = 0;
+};
+
+namespace {
+
+int set_device(const gpeed_ctx* c) {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != c->device) GP_CUDA(cudaSetDevice(c->device));
+    return GPEED_OK;
+}
+
+__global__ void make_slots_kernel(gp::SlotDesc* slots, int* nslots, int n_tok, int nt) {
+    const int ns = (n_tok + nt - 1) / nt;
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+        gp::SlotDesc s;
+        s.expert = 0;
+        s.begin = i * nt;
+        s.ntok = min(nt, n_tok - i * nt);
+        s.pad = 0;
+        slots[i] = s;
+    }
+    if (threadIdx.x == 0) *nslots = ns;
+}
+
+// Pipeline depth that fits the opt-in shared memory (227 KB) next to the
+// 64 KB decode tables, counting per-stage partial sums for up to 8 tokens.
+int stages_for(int in_dim, int nm, int tile_rows, int nkw) {
+    const int per_stage = nm * tile_rows * 98 * (in_dim / 256) + nm * tile_rows * nkw * 8 * 4;
+    const int budget = 227 * 1024 - 65536 - 1024;
+    return std::min(8, budget / per_stage);
+}
+
+// GEMV geometry for a given K (in_dim) and number of matrices per stage.
+struct Geo {
+    int unit, nkw, rpm, tile_rows, stages;
+};
+
+int pick_geo(int in_dim, int nm, Geo* g) {
+    if (in_dim % 1024 == 0 && in_dim / 1024 <= 15 / nm) {
+        g->unit = 32;
+        g->nkw = in_dim / 1024;
+    } else if (in_dim % 512 == 0 && in_dim / 512 <= 15 / nm) {
+        g->unit = 16;
+        g->nkw = in_dim / 512;
+    } else {
+        return fail(GPEED_ERR_UNSUPPORTED, "in_dim %d: the expert GEMV needs a multiple of 512 (<= %d)", in_dim,
+                    15 / nm * 1024);
+    }
+    g->rpm = 1;
+    while (g->rpm < 4 && nm * g->nkw * g->rpm * 2 <= 15) g->rpm *= 2;
+    g->tile_rows = 8 * g->rpm;
+    g->stages = stages_for(in_dim, nm, g->tile_rows, g->nkw);
+    if (g->stages > 8) g->stages = 8;
+    if (g->stages < 2) return fail(GPEED_ERR_UNSUPPORTED, "in_dim %d too large for the GEMV stage ring", in_dim);
+    return GPEED_OK;
+}
+
+int nt_for(int unit, int ntok) {
+    if (ntok <= 1) return 1;
+    if (ntok <= 2) return 2;
+    if (unit == 16 && ntok > 4) return 8;
+    return 4;
+}
+
+int upload_matrix(gpeed_ctx* c, const void* raw, int on_device, int64_t rows, int in_dim, uint8_t* dst,
+                  cudaStream_t st) {
+    const size_t raw_bytes = (size_t)rows * (in_dim / 256) * 98;
+    const uint8_t* src = static_cast<const uint8_t*>(raw);
+    uint8_t* tmp = nullptr;
+    if (!on_device) {
+        GP_CUDA(cudaMalloc(&tmp, raw_bytes));
+        GP_CUDA(cudaMemcpyAsync(tmp, raw, raw_bytes, cudaMemcpyHostToDevice, st));
+        src = tmp;
+    }
+    GP_CUDA(gp::launch_repack(src, dst, rows, in_dim, st));
+    if (tmp) {
+        GP_CUDA(cudaStreamSynchronize(st));
+        GP_CUDA(cudaFree(tmp));
+    }
+    return GPEED_OK;
+}
+
+int check_shape(const gpeed_moe_shape* s) {
+    if (!s) return fail(GPEED_ERR_INVALID, "shape is NULL");
+    if (s->hidden <= 0 || s->hidden % 512 || s->inter <= 0 || s->inter % 512)
+        return fail(GPEED_ERR_UNSUPPORTED, "hidden (%d) and inter (%d) must be positive multiples of 512", s->hidden,
+                    s->inter);
+    if (s->n_experts <= 0 || s->n_experts > 512) return fail(GPEED_ERR_UNSUPPORTED, "n_experts %d not in [1, 512]", s->n_experts);
+    if (s->top_k <= 0 || s->top_k > 32 || s->top_k > s->n_experts)
+        return fail(GPEED_ERR_INVALID, "top_k %d not in [1, min(32, n_experts)]", s->top_k);
+    if (s->n_shared < 0 || s->n_shared > 1) return fail(GPEED_ERR_UNSUPPORTED, "n_shared must be 0 or 1");
+    if (s->inter % 8 || s->hidden % 32) return fail(GPEED_ERR_UNSUPPORTED, "row tiling needs inter%%8 == hidden%%32 == 0");
+    return GPEED_OK;
+}
+
+int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
+                int on_device, Layer** out) {
+    const int H = s->hidden, I = s->inter, E = s->n_experts, NE = E + s->n_shared;
+    auto it = c->layers.find(layer);
+    if (it != c->layers.end()) {
+        Layer& old = it->second;
+        cudaFree(old.router); cudaFree(old.corr); cudaFree(old.gate); cudaFree(old.up); cudaFree(old.down);
+        c->layers.erase(it);
+    }
+    Layer L;
+    L.shape = *s;
+    L.gu_stride = gp::repacked_bytes(I, H);
+    L.d_stride = gp::repacked_bytes(H, I);
+    const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    GP_CUDA(cudaMalloc(&L.router, sizeof(float) * E * H));
+    GP_CUDA(cudaMemcpy(L.router, router_w, sizeof(float) * E * H, kind));
+    if (corr) {
+        GP_CUDA(cudaMalloc(&L.corr, sizeof(float) * E));
+        GP_CUDA(cudaMemcpy(L.corr, corr, sizeof(float) * E, kind));
+    }
+    // + 32 spare rows of padding after the last expert (tiles never read past the allocation)
+    GP_CUDA(cudaMalloc(&L.gate, L.gu_stride * NE + gp::repacked_bytes(32, H)));
+    GP_CUDA(cudaMalloc(&L.up, L.gu_stride * NE + gp::repacked_bytes(32, H)));
+    GP_CUDA(cudaMalloc(&L.down, L.d_stride * NE + gp::repacked_bytes(32, I)));
+    c->layers[layer] = L;
+    *out = &c->layers[layer];
+    return GPEED_OK;
+}
+
+int ensure_scratch(gpeed_ctx* c, int n, int E, int K, int H, int I) {
+    const size_t nk = (size_t)n * K, na = nk + n;
+    const int nsplit_max = 16;
+    const size_t max_slots = nk + E + n + 4;  // nt >= 1
+    int rc;
+    if ((rc = c->partial.ensure((size_t)nsplit_max * n * E))) return rc;
+    if ((rc = c->topk_w.ensure(nk))) return rc;
+    if ((rc = c->topk_ids.ensure(nk))) return rc;
+    if ((rc = c->perm.ensure(na))) return rc;
+    if ((rc = c->inv_pos.ensure(nk))) return rc;
+    if ((rc = c->counts.ensure(E))) return rc;
+    if ((rc = c->slots.ensure(max_slots))) return rc;
+    if ((rc = c->nslots.ensure(1))) return rc;
+    if ((rc = c->h.ensure(na * I))) return rc;
+    if ((rc = c->D.ensure(na * H))) return rc;
+    return GPEED_OK;
+}
+
+int pick_nsplit(int H) {
+    for (int s = 8; s >= 1; --s)
+        if (H % (128 * s) == 0) return s;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* gpeed_last_error(void) { return g_err.c_str(); }
+int gpeed_version(void) { return 1; }
+
+int gpeed_ctx_create(int device, gpeed_ctx** out) {
+    if (!out) return fail(GPEED_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    int ndev = 0;
+    GP_CUDA(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(GPEED_ERR_INVALID, "device %d not present (%d devices)", device, ndev);
+    GP_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    GP_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10) return fail(GPEED_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device,
+                                      prop.major, prop.minor);
+    gpeed_ctx* c = new gpeed_ctx();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    if (cudaMalloc(&c->tables, 65536) != cudaSuccess || cudaMalloc(&c->status, sizeof(uint32_t)) != cudaSuccess) {
+        delete c;
+        return fail(GPEED_ERR_CUDA, "cudaMalloc failed in ctx_create");
+    }
+    cudaMemset(c->status, 0, sizeof(uint32_t));
+    cudaError_t e = gp::build_tables(c->tables, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaFree(c->tables);
+        cudaFree(c->status);
+        delete c;
+        return fail(GPEED_ERR_CUDA, "table build: %s", cudaGetErrorString(e));
+    }
+    *out = c;
+    return GPEED_OK;
+}
+
+int gpeed_ctx_destroy(gpeed_ctx* c) {
+    if (!c) return GPEED_OK;
+    set_device(c);
+    cudaDeviceSynchronize();
+    for (auto& t : c->tensors) cudaFree(t.packed);
+    for (auto& kv : c->layers) {
+        Layer& L = kv.second;
+        cudaFree(L.router); cudaFree(L.corr); cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down);
+    }
+    c->partial.release(); c->topk_w.release(); c->h.release(); c->D.release(); c->mvout.release();
+    c->topk_ids.release(); c->perm.release(); c->inv_pos.release(); c->counts.release(); c->nslots.release();
+    c->slots.release();
+    for (auto& e : c->ev)
+        if (e) cudaEventDestroy(e);
+    cudaFree(c->tables);
+    cudaFree(c->status);
+    delete c;
+    return GPEED_OK;
+}
+
+int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    GP_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+    uint32_t st = 0;
+    GP_CUDA(cudaMemcpy(&st, c->status, sizeof(st), cudaMemcpyDeviceToHost));
+    if (st) {
+        GP_CUDA(cudaMemset(c->status, 0, sizeof(uint32_t)));
+        return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
+                                      "4: expert id out of range, 8: bad shape)", st);
+    }
+    return GPEED_OK;
+}
+
+int gpeed_ctx_profile(gpeed_ctx* c, int enable) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    if (enable && !c->ev[0])
+        for (auto& e : c->ev) GP_CUDA(cudaEventCreate(&e));
+    c->prof = enable != 0;
+    for (double& v : c->prof_ms) v = 0;
+    c->prof_calls = 0;
+    return GPEED_OK;
+}
+
+int gpeed_ctx_profile_read(gpeed_ctx* c, float* stage_ms, int* calls) {
+    if (!c || !stage_ms || !calls) return fail(GPEED_ERR_INVALID, "NULL argument");
+    for (int i = 0; i < 5; ++i) stage_ms[i] = c->prof_calls ? (float)(c->prof_ms[i] / c->prof_calls) : 0.f;
+    *calls = (int)c->prof_calls;
+    return GPEED_OK;
+}
+
+int gpeed_iq3xxs_dequantize(const void* src, float* dst, uint64_t n, void* stream) {
+    if (n % 256) return fail(GPEED_ERR_INVALID, "dequantize: element count not a multiple of block size");
+    if (!src || !dst) return fail(GPEED_ERR_INVALID, "NULL pointer");
+    if (reinterpret_cast<uintptr_t>(dst) & 15) return fail(GPEED_ERR_INVALID, "dst must be 16-byte aligned");
+    GP_CUDA(gp::launch_dequantize(static_cast<const uint8_t*>(src), dst, (int64_t)(n / 256), (cudaStream_t)stream));
+    return GPEED_OK;
+}
+
+int gpeed_synth_iq3xxs(void* dst, uint64_t seed, uint64_t stream, uint64_t block0, uint64_t nblocks, void* st) {
+    if (!dst) return fail(GPEED_ERR_INVALID, "NULL pointer");
+    GP_CUDA(gp::launch_synth(static_cast<uint8_t*>(dst), seed, stream, block0, (int64_t)nblocks, (cudaStream_t)st));
+    return GPEED_OK;
+}
+
+int gpeed_tensor_upload(gpeed_ctx* c, const void* raw, int on_device, int dtype, uint64_t rows, int in_dim, int* handle) {
+    if (!c || !raw || !handle) return fail(GPEED_ERR_INVALID, "NULL argument");
+    if (dtype != GPEED_DTYPE_IQ3_XXS) return fail(GPEED_ERR_UNSUPPORTED, "dtype %d: only IQ3_XXS (18) is supported", dtype);
+    if (in_dim <= 0 || in_dim % 256) return fail(GPEED_ERR_INVALID, "in_dim %d not a multiple of 256", in_dim);
+    if (rows == 0) return fail(GPEED_ERR_INVALID, "rows == 0");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    Tensor t;
+    t.rows = (int64_t)rows;
+    t.in_dim = in_dim;
+    GP_CUDA(cudaMalloc(&t.packed, gp::repacked_bytes(padded_rows(t.rows), in_dim)));
+    GP_CUDA(cudaMemset(t.packed, 0, gp::repacked_bytes(padded_rows(t.rows), in_dim)));
+    if ((rc = upload_matrix(c, raw, on_device, t.rows, in_dim, t.packed, 0))) return rc;
+    GP_CUDA(cudaDeviceSynchronize());
+    c->tensors.push_back(t);
+    *handle = (int)c->tensors.size() - 1;
+    return GPEED_OK;
+}
+
+int gpeed_tensor_download(gpeed_ctx* c, int handle, void* raw_host) {
+    if (!c || !raw_host || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    const Tensor& t = c->tensors[handle];
+    const size_t bytes = (size_t)t.rows * (t.in_dim / 256) * 98;
+    uint8_t* tmp = nullptr;
+    GP_CUDA(cudaMalloc(&tmp, bytes));
+    GP_CUDA(gp::launch_unpack(t.packed, tmp, t.rows, t.in_dim, 0));
+    GP_CUDA(cudaMemcpy(raw_host, tmp, bytes, cudaMemcpyDeviceToHost));
+    GP_CUDA(cudaFree(tmp));
+    return GPEED_OK;
+}
+
+int gpeed_matmul_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* X, int n_tok,
+                       float* Y, void* stream) {
+    if (!c || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
+    if (n_tok <= 0 || out_dim <= 0) return GPEED_OK;  // weights.cpp:88
+    const Tensor& t = c->tensors[handle];
+    if (in_dim != t.in_dim) return fail(GPEED_ERR_INVALID, "in_dim %d != tensor in_dim %d", in_dim, t.in_dim);
+    if ((int64_t)row0 + out_dim > t.rows)
+        return fail(GPEED_ERR_INVALID, "rows [%llu, %llu) past the tensor's %lld rows", (unsigned long long)row0,
+                    (unsigned long long)row0 + out_dim, (long long)t.rows);
+    if (!X || !Y || (reinterpret_cast<uintptr_t>(X) & 15)) return fail(GPEED_ERR_INVALID, "X must be a 16-byte aligned device pointer");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    Geo g;
+    if ((rc = pick_geo(in_dim, 1, &g))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int64_t g0 = (int64_t)row0 / 8 * 8, skip = (int64_t)row0 - g0;
+    const int64_t ntile = (skip + out_dim + g.tile_rows - 1) / g.tile_rows;
+    const int64_t rows_eff = ntile * g.tile_rows;
+    const int nt = nt_for(g.unit, n_tok);
+    const int ns = (n_tok + nt - 1) / nt;
+    if ((rc = c->slots.ensure(ns))) return rc;
+    if ((rc = c->nslots.ensure(1))) return rc;
+    const bool direct = skip == 0 && rows_eff == out_dim;
+    if (!direct && (rc = c->mvout.ensure((size_t)n_tok * rows_eff))) return rc;
+    make_slots_kernel<<<1, 256, 0, st>>>(c->slots.p, c->nslots.p, n_tok, nt);
+    GP_CUDA(cudaGetLastError());
+    gp::GemvArgs a{};
+    a.w0 = t.packed + (g0 / 8) * 784 * (in_dim / 256);
+    a.w1 = nullptr;
+    a.expert_stride = 0;
+    a.in_dim = in_dim;
+    a.rows = (int)rows_eff;
+    a.tile_rows = g.tile_rows;
+    a.rpm = g.rpm;
+    a.nkw = g.nkw;
+    a.stages = g.stages;
+    a.slots = c->slots.p;
+    a.nslots = c->nslots.p;
+    a.perm_tok = nullptr;
+    a.x = X;
+    a.x_bf16 = 0;
+    a.out = direct ? Y : c->mvout.p;
+    a.limit = 0.f;
+    a.tables = c->tables;
+    a.status = c->status;
+    const int grid = (int)std::min<int64_t>(c->num_sms, ntile * ns);
+    GP_CUDA(gp::launch_gemv(a, g.unit, nt, false, grid, st, false));
+    if (!direct)
+        GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * out_dim, c->mvout.p + skip, sizeof(float) * rows_eff,
+                                  sizeof(float) * out_dim, n_tok, cudaMemcpyDeviceToDevice, st));
+    return GPEED_OK;
+}
+
+int gpeed_matvec_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* x, float* dst,
+                       void* stream) {
+    return gpeed_matmul_quant(c, handle, row0, in_dim, out_dim, x, 1, dst, stream);
+}
+
+int gpeed_moe_load_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
+                         const void* gate, const void* up, const void* down, const void* gate_sh, const void* up_sh,
+                         const void* down_sh, int on_device) {
+    int rc;
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if ((rc = check_shape(s))) return rc;
+    if (!router_w || !gate || !up || !down) return fail(GPEED_ERR_INVALID, "NULL expert tensor");
+    if (s->n_shared && (!gate_sh || !up_sh || !down_sh)) return fail(GPEED_ERR_INVALID, "n_shared=1 needs the shared tensors");
+    if ((rc = set_device(c))) return rc;
+    Layer* L;
+    if ((rc = alloc_layer(c, layer, s, router_w, corr, on_device, &L))) return rc;
+    const int H = s->hidden, I = s->inter, E = s->n_experts;
+    if ((rc = upload_matrix(c, gate, on_device, (int64_t)E * I, H, L->gate, 0))) return rc;
+    if ((rc = upload_matrix(c, up, on_device, (int64_t)E * I, H, L->up, 0))) return rc;
+    if ((rc = upload_matrix(c, down, on_device, (int64_t)E * H, I, L->down, 0))) return rc;
+    if (s->n_shared) {
+        if ((rc = upload_matrix(c, gate_sh, on_device, I, H, L->gate + L->gu_stride * E, 0))) return rc;
+        if ((rc = upload_matrix(c, up_sh, on_device, I, H, L->up + L->gu_stride * E, 0))) return rc;
+        if ((rc = upload_matrix(c, down_sh, on_device, H, I, L->down + L->d_stride * E, 0))) return rc;
+    }
+    GP_CUDA(cudaDeviceSynchronize());
+    return GPEED_OK;
+}
+
+int gpeed_moe_synth_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
+                          int on_device, uint64_t seed, uint64_t stream0) {
+    int rc;
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if ((rc = check_shape(s))) return rc;
+    if (!router_w) return fail(GPEED_ERR_INVALID, "router_w is NULL");
+    if ((rc = set_device(c))) return rc;
+    Layer* L;
+    if ((rc = alloc_layer(c, layer, s, router_w, corr, on_device, &L))) return rc;
+    const int H = s->hidden, I = s->inter, E = s->n_experts;
+    const int64_t nb_gu = (int64_t)E * I * (H / 256), nb_d = (int64_t)E * H * (I / 256);
+    uint8_t* tmp = nullptr;
+    GP_CUDA(cudaMalloc(&tmp, (size_t)std::max(nb_gu, nb_d) * 98));
+    struct M { uint8_t* dst; int64_t rows; int in; int64_t nb; };
+    const M mats[6] = {{L->gate, (int64_t)E * I, H, nb_gu}, {L->up, (int64_t)E * I, H, nb_gu},
+                       {L->down, (int64_t)E * H, I, nb_d},  {L->gate + L->gu_stride * E, I, H, (int64_t)I * H / 256},
+                       {L->up + L->gu_stride * E, I, H, (int64_t)I * H / 256},
+                       {L->down + L->d_stride * E, H, I, (int64_t)H * I / 256}};
+    for (int m = 0; m < (s->n_shared ? 6 : 3); ++m) {
+        GP_CUDA(gp::launch_synth(tmp, seed, stream0 + m, 0, mats[m].nb, 0));
+        GP_CUDA(gp::launch_repack(tmp, mats[m].dst, mats[m].rows, mats[m].in, 0));
+    }
+    GP_CUDA(cudaDeviceSynchronize());
+    GP_CUDA(cudaFree(tmp));
+    return GPEED_OK;
+}
+
+int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, float* y, const int* forced,
+                      int* topk_ids, float* topk_w, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    if (n < 0) return fail(GPEED_ERR_INVALID, "n_tok < 0");
+    if (n == 0) return GPEED_OK;
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (!x || !y || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+        return fail(GPEED_ERR_INVALID, "x and y must be 16-byte aligned device pointers");
+    const Layer& L = it->second;
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k;
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    const int nsplit = pick_nsplit(H);
+    auto mark = [&](int i) {
+        if (c->prof) cudaEventRecord(c->ev[i], st);
+    };
+    mark(0);
+
+    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, nsplit, c->partial.p};
+    GP_CUDA(gp::launch_router(ra, st, false));
+    mark(1);
+
+    Geo ggu, gd;
+    if ((rc = pick_geo(H, 2, &ggu))) return rc;
+    if ((rc = pick_geo(I, 1, &gd))) return rc;
+    // one slot list serves both expert kernels: its token count must suit both
+    int nt = std::min(nt_for(ggu.unit, n), nt_for(gd.unit, n));
+    gp::RouteArgs ro{};
+    ro.partial = c->partial.p;
+    ro.nsplit = nsplit;
+    ro.corr = L.corr;
+    ro.forced = forced;
+    ro.n = n;
+    ro.E = E;
+    ro.K = K;
+    ro.routed_scale = s.routed_scale;
+    ro.norm_topk = s.norm_topk;
+    ro.nt = nt;
+    ro.with_shared = s.n_shared;
+    ro.expert_lo = 0;
+    ro.expert_hi = E;
+    ro.topk_ids = topk_ids ? topk_ids : c->topk_ids.p;
+    ro.topk_w = topk_w ? topk_w : c->topk_w.p;
+    ro.perm_tok = c->perm.p;
+    ro.inv_pos = c->inv_pos.p;
+    ro.counts = c->counts.p;
+    ro.slots = c->slots.p;
+    ro.max_slots = (int)c->slots.n;
+    ro.nslots = c->nslots.p;
+    ro.status = c->status;
+    GP_CUDA(gp::launch_route(ro, st, !c->prof));
+    mark(2);
+
+    gp::GemvArgs a{};
+    a.w0 = L.gate;
+    a.w1 = L.up;
+    a.expert_stride = L.gu_stride;
+    a.in_dim = H;
+    a.rows = I;
+    a.tile_rows = 8;  // I % 8 == 0; tiles never straddle experts
+    a.rpm = 1;
+    a.nkw = ggu.nkw;
+    a.stages = ggu.stages;
+    a.slots = c->slots.p;
+    a.nslots = c->nslots.p;
+    a.perm_tok = c->perm.p;
+    a.x = x;
+    a.x_bf16 = x_dtype == GPEED_DTYPE_BF16;
+    a.out = c->h.p;
+    a.limit = s.swiglu_limit;
+    a.tables = c->tables;
+    a.status = c->status;
+    if (I % a.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "inter %% 8 != 0");
+    a.stages = stages_for(H, 2, 8, ggu.nkw);
+    GP_CUDA(gp::launch_gemv(a, ggu.unit, nt, true, c->num_sms, st, !c->prof));
+    mark(3);
+
+    gp::GemvArgs d{};
+    d.w0 = L.down;
+    d.w1 = nullptr;
+    d.expert_stride = L.d_stride;
+    d.in_dim = I;
+    d.rows = H;
+    d.tile_rows = gd.tile_rows;
+    d.rpm = gd.rpm;
+    d.nkw = gd.nkw;
+    d.stages = gd.stages;
+    d.slots = c->slots.p;
+    d.nslots = c->nslots.p;
+    d.perm_tok = nullptr;
+    d.x = c->h.p;
+    d.x_bf16 = 0;
+    d.out = c->D.p;
+    d.tables = c->tables;
+    d.status = c->status;
+    if (H % d.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "hidden %% %d != 0", d.tile_rows);
+    GP_CUDA(gp::launch_gemv(d, gd.unit, nt, false, c->num_sms, st, !c->prof));
+    mark(4);
+
+    gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, s.n_shared, y};
+    GP_CUDA(gp::launch_combine(cb, st, !c->prof));
+    mark(5);
+    if (c->prof) {
+        GP_CUDA(cudaEventSynchronize(c->ev[5]));
+        for (int i = 0; i < 5; ++i) {
+            float ms = 0.f;
+            GP_CUDA(cudaEventElapsedTime(&ms, c->ev[i], c->ev[i + 1]));
+            c->prof_ms[i] += ms;
+        }
+        ++c->prof_calls;
+    }
+    return GPEED_OK;
+}
+
+}  // extern "C"

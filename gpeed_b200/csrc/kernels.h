@@ -1,0 +1,110 @@
+// Host-visible kernel launch interfaces (internal to libgpeed_moe.so).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace gp {
+
+// One unit of expert work: `ntok` consecutive assignments starting at `begin`
+// (positions in the expert-sorted assignment list) that all use `expert`.
+struct SlotDesc {
+    int expert;
+    int begin;
+    int ntok;
+    int pad;
+};
+
+// Repacked IQ3_XXS matrix layout ("row groups"): rows are grouped by 8; each
+// group of 8 rows x nblk blocks (784*nblk bytes, a multiple of 16) stores
+//   [qs  : 8 rows x nblk x 64 B][aux : 8 rows x nblk x 32 B][d : 8 rows x nblk x 2 B]
+// i.e. the same 98 bytes per block, regrouped so every lane load is aligned and
+// a warp's loads are bank-conflict free.  Lossless; see repack kernels.
+inline int64_t repacked_bytes(int64_t rows, int in_dim) {
+    return ((rows + 7) / 8) * 784 * (int64_t)(in_dim / 256);
+}
+
+struct GemvArgs {
+    const uint8_t* w0;         // repacked matrix (gate, or the single matrix)
+    const uint8_t* w1;         // repacked up matrix (gate/up mode) or nullptr
+    int64_t expert_stride;     // bytes between experts in w0 / w1
+    int in_dim;                // K (multiple of 512)
+    int rows;                  // output rows per expert
+    int tile_rows;             // rows per pipeline stage per matrix (multiple of 8)
+    int rpm;                   // row groups (warps along rows) per matrix
+    int nkw;                   // warps along K: in_dim / (32 * UNIT)
+    int stages;
+    const SlotDesc* slots;
+    const int* nslots;         // device-resident slot count
+    const int* perm_tok;       // assignment -> x row; nullptr: the assignment index is the x row
+    const void* x;             // activations: fp32 or bf16 rows of in_dim
+    int x_bf16;
+    float* out;                // [assignment][rows] fp32
+    float limit;               // SwiGLU clamp (gate/up mode)
+    const uint8_t* tables;     // 64 KB decode-table image in global memory
+    uint32_t* status;          // device status word (0 = ok)
+};
+
+// Launches the fused-decode GEMV.  unit: 32 or 16 weights per lane; nt: max
+// tokens per slot (1, 2, 4 or 8); gateup: w1 present, SwiGLU epilogue.
+cudaError_t launch_gemv(const GemvArgs& a, int unit, int nt, bool gateup, int grid, cudaStream_t st, bool pdl);
+size_t gemv_smem_bytes(const GemvArgs& a, int nt, bool gateup);
+
+// Builds the 64 KB decode-table image (codebook + sign selectors) in global memory.
+cudaError_t build_tables(uint8_t* dst, cudaStream_t st);
+
+// Raw GGUF IQ3_XXS rows -> repacked row groups (and back, for verification).
+cudaError_t launch_repack(const uint8_t* raw, uint8_t* packed, int64_t rows, int in_dim, cudaStream_t st);
+cudaError_t launch_unpack(const uint8_t* packed, uint8_t* raw, int64_t rows, int in_dim, cudaStream_t st);
+
+// Bit-exact IQ3_XXS -> fp32 (raw GGUF blocks).
+cudaError_t launch_dequantize(const uint8_t* raw, float* dst, int64_t nblocks, cudaStream_t st);
+
+// Synthetic IQ3_XXS blocks (counter-based generator, synth.h).
+cudaError_t launch_synth(uint8_t* dst, uint64_t seed, uint64_t stream, uint64_t block0, int64_t nblocks,
+                         cudaStream_t st);
+
+// Router: partial logits [nsplit][n][E] = X[n][H] . W[E][H] over K-chunks.
+struct RouterArgs {
+    const float* w;       // [E][H] fp32
+    const void* x;        // [n][H]
+    int x_bf16;
+    int n, H, E, nsplit;
+    float* partial;       // [nsplit][n][E]
+};
+cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl);
+
+// Top-k, histogram, stable expert-major permutation and slot list.
+struct RouteArgs {
+    const float* partial;  // [nsplit][n][E]
+    int nsplit;
+    const float* corr;     // [E] or nullptr
+    const int* forced;     // [n][K] or nullptr
+    int n, E, K;
+    float routed_scale;
+    int norm_topk;
+    int nt;                // tokens per slot
+    int with_shared;       // append shared-expert assignments/slots (expert id E)
+    int expert_lo, expert_hi;  // experts owned here (EP); others are not given slots
+    int* topk_ids;         // [n][K]
+    float* topk_w;         // [n][K]
+    int* perm_tok;         // [n*K + n]: assignment -> token
+    int* inv_pos;          // [n][K]: (t,k) -> assignment position
+    int* counts;           // [E]
+    SlotDesc* slots;       // capacity max_slots
+    int max_slots;
+    int* nslots;
+    uint32_t* status;
+};
+cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl);
+
+// Y[t] = sum_k w[t][k] * D[inv_pos[t][k]] (+ D[n*K + t] when with_shared).
+struct CombineArgs {
+    const float* D;
+    const int* inv_pos;
+    const float* topk_w;
+    int n, K, H, with_shared;
+    float* y;
+};
+cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl);
+
+}  // namespace gp

@@ -1,0 +1,188 @@
+"""Host-side mirror of the reference's expert-op interface, on the C ABI.
+
+* ``WeightStore``  - the reference's ``glm5::WeightStore`` expert entry points
+  (cpp/core/include/glm5/weights.h:38-48): tensors are registered by name and
+  ``matvec_quant`` / ``matmul_quant`` take the same (name, row0, in_dim,
+  out_dim, x, dst) arguments, on CUDA tensors.
+* ``MoeLayer``     - ``Model::moe_forward`` / ``Model::moe_batch``
+  (cpp/core/src/model.cpp:692-756, model_batch.cpp:165-281) for one layer.
+* ``dequantize``   - ``glm5::dequantize`` for IQ3_XXS (quant.cpp:521-573).
+
+Errors surface as ``GpeedError`` (a RuntimeError), as the reference throws
+std::runtime_error.  torch is used only for device buffers and streams.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from . import _capi
+from ._capi import GpeedError, MoeShape, call
+
+BLOCK_BYTES, QK = 98, 256
+
+
+def _ptr(t) -> ctypes.c_void_p | None:
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data_as(ctypes.c_void_p)
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream) -> ctypes.c_void_p:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class Context:
+    """One library context per CUDA device (owns uploaded weights and scratch)."""
+
+    def __init__(self, device: int = 0):
+        torch.cuda.init()
+        self.device = device
+        h = ctypes.c_void_p()
+        with torch.cuda.device(device):
+            call("gpeed_ctx_create", device, ctypes.byref(h))
+        self.handle = h
+
+    def check(self, stream=None) -> None:
+        call("gpeed_ctx_check", self.handle, _stream(stream))
+
+    def close(self) -> None:
+        if self.handle:
+            call("gpeed_ctx_destroy", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def dequantize(blocks: torch.Tensor, stream=None) -> torch.Tensor:
+    """IQ3_XXS bytes (uint8 CUDA tensor, n*98) -> float32 (n*256), bit-exact."""
+    if blocks.numel() % BLOCK_BYTES:
+        raise GpeedError(_capi.ERR_INVALID, "byte count not a multiple of the 98-byte block")
+    n = blocks.numel() // BLOCK_BYTES * QK
+    out = torch.empty(n, dtype=torch.float32, device=blocks.device)
+    call("gpeed_iq3xxs_dequantize", _ptr(blocks), _ptr(out), ctypes.c_uint64(n), _stream(stream))
+    return out
+
+
+class WeightStore:
+    """Expert tensors by name, like glm5::WeightStore (weights.h:15-76)."""
+
+    def __init__(self, ctx: Context):
+        self.ctx = ctx
+        self._handles: dict[str, tuple[int, int, int]] = {}
+
+    def add(self, name: str, raw, rows: int, in_dim: int) -> None:
+        """Registers an IQ3_XXS tensor of `rows` rows x `in_dim` weights (numpy/CPU or CUDA bytes)."""
+        on_dev = isinstance(raw, torch.Tensor) and raw.is_cuda
+        if isinstance(raw, torch.Tensor) and not on_dev:
+            raw = raw.numpy()
+        raw_c = raw.contiguous() if on_dev else np.ascontiguousarray(raw, np.uint8)
+        h = ctypes.c_int()
+        call("gpeed_tensor_upload", self.ctx.handle, _ptr(raw_c), int(on_dev), _capi.DTYPE_IQ3_XXS,
+             ctypes.c_uint64(rows), in_dim, ctypes.byref(h))
+        self._handles[name] = (h.value, rows, in_dim)
+
+    def has(self, name: str) -> bool:
+        return name in self._handles
+
+    def _h(self, name: str) -> int:
+        if name not in self._handles:
+            raise GpeedError(_capi.ERR_INVALID, f"weights: missing tensor {name}")
+        return self._handles[name][0]
+
+    def raw_bytes(self, name: str) -> np.ndarray:
+        h, rows, in_dim = self._handles[name]
+        out = np.empty(rows * (in_dim // QK) * BLOCK_BYTES, np.uint8)
+        call("gpeed_tensor_download", self.ctx.handle, h, _ptr(out))
+        return out
+
+    def matvec_quant(self, name: str, row0: int, in_dim: int, out_dim: int, x: torch.Tensor,
+                     dst: torch.Tensor, stream=None) -> None:
+        """dst[j] = sum_i W[row0 + j][i] * x[i] (weights.h:38-41)."""
+        call("gpeed_matvec_quant", self.ctx.handle, self._h(name), ctypes.c_uint64(row0), in_dim, out_dim,
+             _ptr(x), _ptr(dst), _stream(stream))
+
+    def matmul_quant(self, name: str, row0: int, in_dim: int, out_dim: int, X: torch.Tensor, n_tok: int,
+                     Y: torch.Tensor, stream=None) -> None:
+        """Y[t][j] = sum_i W[row0 + j][i] * X[t][i] (weights.h:43-48)."""
+        call("gpeed_matmul_quant", self.ctx.handle, self._h(name), ctypes.c_uint64(row0), in_dim, out_dim,
+             _ptr(X), n_tok, _ptr(Y), _stream(stream))
+
+
+@dataclass
+class MoeConfig:
+    """MoE fields of glm5::ModelConfig (model_config.h:57-70) at BASELINE sizes."""
+    hidden: int = 5120
+    inter: int = 1536
+    n_experts: int = 160
+    top_k: int = 8
+    n_shared: int = 1
+    routed_scale: float = 2.5
+    norm_topk: bool = True
+    swiglu_limit: float = 10.0
+
+    def shape(self) -> MoeShape:
+        return MoeShape(self.hidden, self.inter, self.n_experts, self.top_k, self.n_shared, self.routed_scale,
+                        int(self.norm_topk), self.swiglu_limit)
+
+
+class MoeLayer:
+    """One routed-expert MoE layer resident on the device."""
+
+    _next_id = 0
+
+    def __init__(self, ctx: Context, cfg: MoeConfig, layer_id: int | None = None):
+        self.ctx, self.cfg = ctx, cfg
+        if layer_id is None:
+            layer_id = MoeLayer._next_id
+            MoeLayer._next_id += 1
+        self.layer_id = layer_id
+        self._shape = cfg.shape()
+
+    def load(self, router: np.ndarray, corr: np.ndarray | None, gate, up, down, gate_sh=None, up_sh=None,
+             down_sh=None) -> "MoeLayer":
+        """Raw GGUF IQ3_XXS expert tensors (host numpy or CUDA uint8)."""
+        on_dev = isinstance(gate, torch.Tensor) and gate.is_cuda
+        conv = (lambda a: a.contiguous()) if on_dev else (lambda a: np.ascontiguousarray(a))
+        router = conv(router if on_dev else np.asarray(router, np.float32))
+        corr_c = None if corr is None else conv(corr if on_dev else np.asarray(corr, np.float32))
+        keep = [conv(t) if t is not None else None for t in (gate, up, down, gate_sh, up_sh, down_sh)]
+        call("gpeed_moe_load_layer", self.ctx.handle, self.layer_id, ctypes.byref(self._shape), _ptr(router),
+             _ptr(corr_c), *[_ptr(t) for t in keep], int(on_dev))
+        return self
+
+    def synth(self, router: np.ndarray, corr: np.ndarray | None, seed: int, stream0: int) -> "MoeLayer":
+        """Expert bytes from the device generator (seed, streams stream0..stream0+5)."""
+        router = np.ascontiguousarray(router, np.float32)
+        corr_c = None if corr is None else np.ascontiguousarray(corr, np.float32)
+        call("gpeed_moe_synth_layer", self.ctx.handle, self.layer_id, ctypes.byref(self._shape), _ptr(router),
+             _ptr(corr_c), 0, ctypes.c_uint64(seed), ctypes.c_uint64(stream0))
+        return self
+
+    def forward(self, x: torch.Tensor, y: torch.Tensor | None = None, forced_topk: torch.Tensor | None = None,
+                topk_ids: torch.Tensor | None = None, topk_w: torch.Tensor | None = None, stream=None):
+        """x [n, H] bf16/fp32 CUDA -> y [n, H] fp32 (Model::moe_forward / moe_batch)."""
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        n = x.shape[0]
+        if x.dtype == torch.bfloat16:
+            dt = _capi.DTYPE_BF16
+        elif x.dtype == torch.float32:
+            dt = _capi.DTYPE_F32
+        else:
+            raise GpeedError(_capi.ERR_UNSUPPORTED, f"x dtype {x.dtype}")
+        if y is None:
+            y = torch.empty(n, self.cfg.hidden, dtype=torch.float32, device=x.device)
+        call("gpeed_moe_forward", self.ctx.handle, self.layer_id, _ptr(x.contiguous()), dt, n, _ptr(y),
+             _ptr(forced_topk), _ptr(topk_ids), _ptr(topk_w), _stream(stream))
+        return y

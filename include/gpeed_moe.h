@@ -1,0 +1,139 @@
+/* gpeed_moe.h - C ABI of libgpeed_moe.so, the B200 (sm_100a) IQ3_XXS
+ * routed-expert MoE path.
+ *
+ * The entry points replace, one for one, the reference engine's expert-op
+ * interface (paths inside the reference project):
+ *
+ *   gpeed_iq3xxs_dequantize  <- glm5::dequantize / dequantize_row for IQ3_XXS
+ *                               (cpp/core/include/glm5/quant.h:17-22,
+ *                                cpp/core/src/quant.cpp:521-573)
+ *   gpeed_tensor_upload      <- WeightStore's resident payload for one tensor
+ *                               (cpp/core/include/glm5/weights.h:55-60,67-73;
+ *                                weights.cpp:62-84 payload / pin_nonexpert)
+ *   gpeed_matvec_quant       <- WeightStore::matvec_quant (weights.h:38-41,
+ *                               weights.cpp:167-203)
+ *   gpeed_matmul_quant       <- WeightStore::matmul_quant (weights.h:43-48,
+ *                               weights.cpp:86-165)
+ *   gpeed_moe_load_layer     <- the per-layer expert tensors Model::moe_forward
+ *                               reads by name (model.cpp:700-755)
+ *   gpeed_moe_forward        <- Model::moe_forward (model.cpp:692-756) for
+ *                               n_tok == 1 and Model::moe_batch
+ *                               (model_batch.cpp:165-281) for n_tok > 1
+ *   gpeed_ep_*               <- no counterpart: the reference has no
+ *                               multi-GPU path; expert parallelism over NCCL.
+ *
+ * Conventions: every function returns 0 (GPEED_OK) or a GPEED_ERR_* code and
+ * leaves a message for gpeed_last_error() (per calling thread); the C++ shim
+ * in gpeed_b200/csrc/weight_store.hpp turns non-zero codes into
+ * std::runtime_error like the reference.  Pointers named *_dev are device
+ * pointers; `stream` is a cudaStream_t (NULL = legacy default stream).  All
+ * compute calls are asynchronous on `stream`; device-side faults that the
+ * kernels detect (bounded waits that gave up, expert ids out of range) are
+ * reported by gpeed_ctx_check().  Buffers must be 16-byte aligned.
+ */
+#ifndef GPEED_MOE_H
+#define GPEED_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GPEED_OK 0
+#define GPEED_ERR_INVALID 1     /* bad argument (shape, alignment, handle) */
+#define GPEED_ERR_CUDA 2        /* CUDA runtime error */
+#define GPEED_ERR_DEVICE 3      /* a kernel reported a device-side error */
+#define GPEED_ERR_UNSUPPORTED 4 /* shape or dtype this build does not handle */
+#define GPEED_ERR_NCCL 5
+
+#define GPEED_DTYPE_F32 0       /* ggml type ids (reference common.h:10-44) */
+#define GPEED_DTYPE_IQ3_XXS 18
+#define GPEED_DTYPE_BF16 30
+
+#if defined(__GNUC__)
+#define GPEED_API __attribute__((visibility("default")))
+#else
+#define GPEED_API
+#endif
+
+typedef struct gpeed_ctx gpeed_ctx;
+
+/* MoE shape and routing constants (reference model_config.h:57-70, read from
+ * GGUF metadata at model_config.cpp:406-421). */
+typedef struct gpeed_moe_shape {
+    int hidden;          /* H, multiple of 512 */
+    int inter;           /* moe_inter I, multiple of 512 */
+    int n_experts;       /* E routed experts (<= 512) */
+    int top_k;           /* K (<= 32) */
+    int n_shared;        /* 0 or 1 shared expert */
+    float routed_scale;  /* 2.5 */
+    int norm_topk;       /* 1: renormalise top-k weights */
+    float swiglu_limit;  /* 10.0: silu(min(g, L)) * clamp(u, -L, L) */
+} gpeed_moe_shape;
+
+GPEED_API const char* gpeed_last_error(void);
+GPEED_API int gpeed_version(void);
+
+/* Context bound to one CUDA device; owns uploaded weights and scratch. */
+GPEED_API int gpeed_ctx_create(int device, gpeed_ctx** out);
+GPEED_API int gpeed_ctx_destroy(gpeed_ctx* ctx);
+/* Synchronises `stream` and reports (then clears) device-side error flags. */
+GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
+
+/* Per-stage timing of gpeed_moe_forward (no counterpart in the reference;
+ * its GLM5_PROFILE phase timer, model.cpp:21-38, is host wall-clock only).
+ * When enabled, each forward records CUDA events between its five kernels
+ * (router, route, gate/up, down, combine) on its stream and waits for them;
+ * gpeed_ctx_profile_read returns the mean milliseconds per stage. */
+GPEED_API int gpeed_ctx_profile(gpeed_ctx* ctx, int enable);
+GPEED_API int gpeed_ctx_profile_read(gpeed_ctx* ctx, float* stage_ms /* [5] */, int* calls);
+
+/* IQ3_XXS -> fp32, bit-exact with the reference codec.  n weights (multiple of
+ * 256; the reference throws otherwise, quant.cpp:523-524). */
+GPEED_API int gpeed_iq3xxs_dequantize(const void* src_dev, float* dst_dev, uint64_t n, void* stream);
+
+/* Uploads (or copies from device memory) an IQ3_XXS tensor of `rows` rows of
+ * `in_dim` weights in GGUF row-major block order; the library keeps its own
+ * device copy in a layout of its choosing.  Returns a handle (>= 0). */
+GPEED_API int gpeed_tensor_upload(gpeed_ctx* ctx, const void* raw, int src_on_device, int dtype, uint64_t rows, int in_dim,
+                        int* handle);
+/* Reads a tensor back in GGUF byte order (verifies the lossless layout). */
+GPEED_API int gpeed_tensor_download(gpeed_ctx* ctx, int handle, void* raw_host);
+
+/* dst[j] = sum_i W[row0 + j][i] * x[i], j < out_dim; x, dst fp32 device. */
+GPEED_API int gpeed_matvec_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim, const float* x_dev,
+                       float* dst_dev, void* stream);
+/* Y[t][j] = sum_i W[row0 + j][i] * X[t][i], t < n_tok; row-major fp32 device. */
+GPEED_API int gpeed_matmul_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim, const float* X_dev,
+                       int n_tok, float* Y_dev, void* stream);
+
+/* Registers layer `layer`: router weight fp32 [E][H], correction bias fp32 [E]
+ * (may be NULL), routed expert tensors [E][rows][blocks] in raw IQ3_XXS
+ * (gate/up: I rows of H; down: H rows of I) and the shared expert's three
+ * matrices (NULL when n_shared == 0).  Host or device sources. */
+GPEED_API int gpeed_moe_load_layer(gpeed_ctx* ctx, int layer, const gpeed_moe_shape* shape, const float* router_w,
+                         const float* corr_bias, const void* gate_exps, const void* up_exps, const void* down_exps,
+                         const void* gate_sh, const void* up_sh, const void* down_sh, int src_on_device);
+/* Same, with every expert byte produced on the device by the counter-based
+ * synthetic generator (seed, streams stream0 .. stream0+5); for benchmarks
+ * and tests.  router_w / corr_bias are host or device per src_on_device. */
+GPEED_API int gpeed_moe_synth_layer(gpeed_ctx* ctx, int layer, const gpeed_moe_shape* shape, const float* router_w,
+                          const float* corr_bias, int src_on_device, uint64_t seed, uint64_t stream0);
+/* Writes `nblocks` synthetic IQ3_XXS blocks (starting at block0 of the
+ * stream) to device memory. */
+GPEED_API int gpeed_synth_iq3xxs(void* dst_dev, uint64_t seed, uint64_t stream, uint64_t block0, uint64_t nblocks,
+                       void* stream_);
+
+/* y[t] = MoE(x[t]) for t < n_tok: x bf16 or fp32 [n_tok][H] (x_dtype =
+ * GPEED_DTYPE_BF16 / _F32), y fp32 [n_tok][H], device pointers.  forced_topk
+ * (device int [n_tok][K] or NULL) replaces the top-k choice; topk_ids /
+ * topk_w (device [n_tok][K] or NULL) receive the routing. */
+GPEED_API int gpeed_moe_forward(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, int n_tok, float* y_dev,
+                      const int* forced_topk_dev, int* topk_ids_dev, float* topk_w_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPEED_MOE_H */

@@ -17,7 +17,7 @@ Fixtures written (all small, committed):
   (zero, negative, subnormal and largest-normal fp16 scales; all-zero and
   all-one scale/sign words) and their decode by the reference's compiled
   dequantize() - bit patterns, for bit-exact comparison.
-* moe_tiny.npz           a tiny MoE layer (H=512, I=256, E=8, K=2, 1 shared
+* moe_tiny.npz           a tiny MoE layer (H=512, I=512, E=8, K=2, 1 shared
   expert; expert bytes from the counter-based generator, seed 7, streams
   gate..down_sh = 1..6) run through the reference harness: matvec_quant outputs, the
   single-token moe_forward path and the batched moe_batch path (top-k ids,
@@ -110,7 +110,7 @@ def main() -> int:
                         decoded_bits=out.view(np.uint32))
 
     # tiny MoE layer through the reference harness
-    H, I, E, K, N = 512, 256, 8, 2, 3
+    H, I, E, K, N = 512, 512, 8, 2, 3
 
     # expert weights come from the counter-based generator (seed 7, streams
     # 1..6), so the fixture stores only the seed; tests regenerate the bytes.

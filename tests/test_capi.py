@@ -1,0 +1,53 @@
+"""CPU checks of the C ABI: the library loads, exports every declared entry
+point, and rejects bad arguments before touching a device."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+from gpeed_b200 import _capi
+
+HDR = os.path.join(os.path.dirname(__file__), "..", "include", "gpeed_moe.h")
+
+
+def declared_functions():
+    text = open(HDR).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:GPEED_API\s+)?(?:const\s+)?\w+\*?\s+\**(gpeed_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_boundary():
+    names = declared_functions()
+    for must in ("gpeed_matvec_quant", "gpeed_matmul_quant", "gpeed_iq3xxs_dequantize", "gpeed_moe_forward",
+                 "gpeed_moe_load_layer", "gpeed_ctx_create", "gpeed_last_error"):
+        assert must in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _capi.load()
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    # and the binding covers them all
+    assert set(declared_functions()) <= set(_capi.SIGNATURES)
+
+
+def test_argument_errors_need_no_device():
+    lib = _capi.load()
+    rc = lib.gpeed_iq3xxs_dequantize(ctypes.c_void_p(16), ctypes.c_void_p(16), ctypes.c_uint64(255), None)
+    assert rc == _capi.ERR_INVALID
+    assert b"multiple of block size" in lib.gpeed_last_error()
+    rc = lib.gpeed_moe_forward(None, 0, None, 30, 1, None, None, None, None, None)
+    assert rc == _capi.ERR_INVALID
+
+
+def test_ctx_create_fails_cleanly_without_a_device():
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a device is present")
+    h = ctypes.c_void_p()
+    rc = _capi.load().gpeed_ctx_create(0, ctypes.byref(h))
+    assert rc != _capi.OK and not h.value
+    with pytest.raises(_capi.GpeedError):
+        _capi.check(rc)

@@ -17,8 +17,12 @@ GRID_H = os.path.join(os.path.dirname(__file__), "..", "gpeed_b200", "csrc", "iq
 
 def _grid_from_header(path, name):
     text = open(path).read()
-    m = re.search(name + r"\s*\[[^\]]*\]\s*=\s*\{(.*?)\};", text, re.S)
-    return [int(t.rstrip("u"), 0) for t in re.split(r"[,\s]+", m.group(1)) if t]
+    if name == "gpeed_iq3xxs_grid":  # values live in a macro shared by host and device copies
+        m = re.search(r"#define GPEED_IQ3XXS_GRID_VALUES(.*?)\n\n", text, re.S)
+        body = m.group(1).replace("\\", " ")
+    else:
+        body = re.search(name + r"\s*\[[^\]]*\]\s*=\s*\{(.*?)\};", text, re.S).group(1)
+    return [int(t.rstrip("u"), 0) for t in re.split(r"[,\s]+", body) if t]
 
 
 def test_grid_table_digest():
