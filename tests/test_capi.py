@@ -51,3 +51,32 @@ def test_ctx_create_fails_cleanly_without_a_device():
     assert rc != _capi.OK and not h.value
     with pytest.raises(_capi.GpeedError):
         _capi.check(rc)
+
+
+def test_cpp_shim_compiles_and_throws_like_the_reference(tmp_path):
+    """gpeed_b200/csrc/weight_store.hpp: reference signatures, std::runtime_error on failure."""
+    import subprocess
+    import torch
+    src = tmp_path / "shim.cpp"
+    src.write_text(r'''
+#include "weight_store.hpp"
+#include <cstdio>
+int main() {
+    try {
+        gpeed::WeightStore ws(0);               // throws without a B200
+        ws.matvec_quant("blk.3.ffn_gate_exps.weight", 0, 5120, 1536, nullptr, nullptr);
+    } catch (const std::runtime_error& e) {
+        std::printf("caught: %s\n", e.what());
+        return 0;
+    }
+    return 3;
+}
+''')
+    repo = os.path.abspath(os.path.join(os.path.dirname(__file__), ".."))
+    exe = tmp_path / "shim"
+    subprocess.run(["g++", "-std=c++17", "-O1", f"-I{repo}/gpeed_b200/csrc", str(src), "-o", str(exe),
+                    f"-L{repo}/gpeed_b200/lib", "-lgpeed_moe", f"-Wl,-rpath,{repo}/gpeed_b200/lib"], check=True)
+    if torch.cuda.is_available():
+        pytest.skip("compiled; the throw path needs a machine without a usable device")
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and "caught: gpeed:" in r.stdout
