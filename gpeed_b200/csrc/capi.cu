@@ -10,6 +10,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -605,6 +606,120 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         }
         ++c->prof_calls;
     }
+    return GPEED_OK;
+}
+
+}  // extern "C"
+
+// ---- allocation-free variant of gpeed_matmul_quant -------------------------
+// For callers that must not allocate device memory once they are serving: a
+// process inside CUDA graph capture, under a fixed memory budget, or embedded
+// in a host engine whose allocator owns the GPU.  The GEMV's work list and its
+// output staging live in this file-scope device array instead of ctx scratch.
+// Every GPU that loads the library holds the array until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[GPEED_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+constexpr int kMaxDevices = 64;
+unsigned char* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of g_noalloc_scratch on `device` (which must be current):
+// looked up once per device, on that device's first call.
+int noalloc_scratch(int device, unsigned char** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device < 0 || device >= kMaxDevices) return fail(GPEED_ERR_INVALID, "device %d out of range", device);
+    if (!g_noalloc_ptr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || !p)
+            return fail(GPEED_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+        g_noalloc_ptr[device] = static_cast<unsigned char*>(p);
+    }
+    *out = g_noalloc_ptr[device];
+    return GPEED_OK;
+}
+
+__global__ void noalloc_slots_kernel(gp::SlotDesc* slots, int* nslots, int n_tok, int nt) {
+    const int ns = (n_tok + nt - 1) / nt;
+    for (int i = threadIdx.x; i < ns; i += blockDim.x) {
+        gp::SlotDesc sd;
+        sd.expert = 0;
+        sd.begin = i * nt;
+        sd.ntok = min(nt, n_tok - i * nt);
+        sd.pad = 0;
+        slots[i] = sd;
+    }
+    if (threadIdx.x == 0) *nslots = ns;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+extern "C" {
+
+int gpeed_matmul_quant_noalloc(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* X,
+                               int n_tok, float* Y, void* stream) {
+    if (!c || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
+    if (n_tok <= 0 || out_dim <= 0) return GPEED_OK;
+    const Tensor& t = c->tensors[handle];
+    if (in_dim != t.in_dim) return fail(GPEED_ERR_INVALID, "in_dim %d != tensor in_dim %d", in_dim, t.in_dim);
+    if ((int64_t)row0 + out_dim > t.rows)
+        return fail(GPEED_ERR_INVALID, "rows [%llu, %llu) past the tensor's %lld rows", (unsigned long long)row0,
+                    (unsigned long long)row0 + out_dim, (long long)t.rows);
+    if (!X || !Y || (reinterpret_cast<uintptr_t>(X) & 15)) return fail(GPEED_ERR_INVALID, "X must be a 16-byte aligned device pointer");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    Geo g;
+    if ((rc = pick_geo(in_dim, 1, &g))) return rc;
+    const int64_t g0 = (int64_t)row0 / 8 * 8, skip = (int64_t)row0 - g0;
+    const int64_t ntile = (skip + out_dim + g.tile_rows - 1) / g.tile_rows;
+    const int64_t rows_eff = ntile * g.tile_rows;
+    const int nt = nt_for(g.unit, n_tok);
+    const int ns = (n_tok + nt - 1) / nt;
+    const bool direct = skip == 0 && rows_eff == out_dim;
+    // scratch layout: [slots][nslots][staged output]
+    const size_t off_n = align256((size_t)ns * sizeof(gp::SlotDesc));
+    const size_t off_y = off_n + 256;
+    const size_t need = off_y + (direct ? 0 : (size_t)n_tok * rows_eff * sizeof(float));
+    if (need > GPEED_NOALLOC_SCRATCH_BYTES)
+        return fail(GPEED_ERR_INVALID, "matmul_quant_noalloc: %zu bytes of scratch needed, the static limit is %u "
+                    "(n_tok * ceil(out_dim + row0 %% 8, %d) * 4 bytes of staging when row0 %% 8 != 0 or out_dim %% %d "
+                    "!= 0, plus the work list)", need, GPEED_NOALLOC_SCRATCH_BYTES, g.tile_rows, g.tile_rows);
+    unsigned char* scratch = nullptr;
+    if ((rc = noalloc_scratch(c->device, &scratch))) return rc;
+    gp::SlotDesc* slots = reinterpret_cast<gp::SlotDesc*>(scratch);
+    int* nslots = reinterpret_cast<int*>(scratch + off_n);
+    float* staged = reinterpret_cast<float*>(scratch + off_y);
+    cudaStream_t st = (cudaStream_t)stream;
+    noalloc_slots_kernel<<<1, 256, 0, st>>>(slots, nslots, n_tok, nt);
+    GP_CUDA(cudaGetLastError());
+    gp::GemvArgs a{};
+    a.w0 = t.packed + (g0 / 8) * 784 * (in_dim / 256);
+    a.w1 = nullptr;
+    a.expert_stride = 0;
+    a.in_dim = in_dim;
+    a.rows = (int)rows_eff;
+    a.tile_rows = g.tile_rows;
+    a.rpm = g.rpm;
+    a.nkw = g.nkw;
+    a.stages = g.stages;
+    a.slots = slots;
+    a.nslots = nslots;
+    a.perm_tok = nullptr;
+    a.x = X;
+    a.x_bf16 = 0;
+    a.out = direct ? Y : staged;
+    a.limit = 0.f;
+    a.tables = c->tables;
+    a.status = c->status;
+    const int grid = (int)std::min<int64_t>(c->num_sms, ntile * ns);
+    GP_CUDA(gp::launch_gemv(a, g.unit, nt, false, grid, st, false));
+    if (!direct)
+        GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * out_dim, staged + skip, sizeof(float) * rows_eff,
+                                  sizeof(float) * out_dim, n_tok, cudaMemcpyDeviceToDevice, st));
     return GPEED_OK;
 }
 

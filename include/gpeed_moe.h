@@ -109,6 +109,21 @@ GPEED_API int gpeed_matvec_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int 
 GPEED_API int gpeed_matmul_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim, const float* X_dev,
                        int n_tok, float* Y_dev, void* stream);
 
+/* Same result as gpeed_matmul_quant, for callers that cannot allocate device
+ * memory while they run (inside CUDA graph capture, under a fixed memory
+ * budget, or behind a host engine's own allocator).  No counterpart in the
+ * reference.  It allocates nothing: its work list and output staging use one
+ * static 4 MiB device array (GPEED_NOALLOC_SCRATCH_BYTES) that every GPU
+ * loading the library keeps until exit.  Calls needing more scratch than that
+ * fail with GPEED_ERR_INVALID: the staging is n_tok * (out_dim + row0 % 8
+ * rounded up to the row tile) * 4 bytes and is only used when row0 % 8 != 0
+ * or out_dim is not a multiple of the row tile.  The first call on a device
+ * looks the array's address up (make it before any stream capture).  All calls
+ * share the array, so calls that overlap on the GPU race; serialise them. */
+#define GPEED_NOALLOC_SCRATCH_BYTES (4u << 20)
+GPEED_API int gpeed_matmul_quant_noalloc(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim,
+                                         const float* X_dev, int n_tok, float* Y_dev, void* stream);
+
 /* Registers layer `layer`: router weight fp32 [E][H], correction bias fp32 [E]
  * (may be NULL), routed expert tensors [E][rows][blocks] in raw IQ3_XXS
  * (gate/up: I rows of H; down: H rows of I) and the shared expert's three
