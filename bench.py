@@ -294,9 +294,16 @@ def run_gpu(args, rank, local_rank, world):
     ctx.check(stream)
 
     hbm_peak, _, peak_src = peaks()
+    fused = stage_ms[0] == 0 and stage_ms[1] == 0 and stage_ms[3] == 0 and stage_ms[4] == 0
+    if fused:  # the whole layer is one persistent kernel
+        kern_name = "decode_layer_kernel (router, top-k, 9 experts gate/up/down, combine; batch 1)"
+        kern_bytes = LAYER_TOKEN_BYTES
+    else:
+        kern_name = "gemv_kernel<1,gateup> (9 experts x gate+up, batch 1)"
+        kern_bytes = GATEUP_BYTES
     gu_ms = stage_ms[2]
-    achieved = GATEUP_BYTES / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else None
-    traffic = traffic_from_profiles("gemv_gateup_decode1.txt")
+    achieved = kern_bytes / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else None
+    traffic = traffic_from_profiles("decode_layer_decode1.txt" if fused else "gemv_gateup_decode1.txt")
     line = None
     if rank == 0:
         cpu = None
@@ -318,14 +325,15 @@ def run_gpu(args, rank, local_rank, world):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
                        "per_gpu_layer_hbm_gbs": layer_gbs,
                        "per_gpu_layer_hbm_frac": layer_gbs / hbm_peak,
-                       "stage_ms": dict(zip(["router", "route", "gateup", "down", "combine"], stage_ms))},
+                       "stage_ms": ({"layer": stage_ms[2]} if fused else
+                                    dict(zip(["router", "route", "gateup", "down", "combine"], stage_ms)))},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
-                         "kernel": "gemv_kernel<32,1,gateup> (9 experts x gate+up, batch 1)",
+                         "kernel": kern_name, "bytes_per_launch": kern_bytes,
                          "peak_source": peak_src},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 4},
-            "gpu_launches": 5 * args.steps,
+            "gpu_launches": (1 if fused else 5) * args.steps,
             "clocks": clk.summary(),
         }
     del graphs, e2e_graphs

@@ -13,6 +13,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libgpeed_moe.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_UNSUPPORTED, ERR_NCCL = range(6)
 DTYPE_F32, DTYPE_IQ3_XXS, DTYPE_BF16 = 0, 18, 30
+OPT_FUSED_DECODE = 1
 
 
 class GpeedError(RuntimeError):
@@ -37,6 +38,7 @@ SIGNATURES = {
     "gpeed_ctx_create": [_i, ctypes.POINTER(_vp)],
     "gpeed_ctx_destroy": [_vp],
     "gpeed_ctx_check": [_vp, _vp],
+    "gpeed_ctx_set_option": [_vp, _i, _i],
     "gpeed_ctx_profile": [_vp, _i],
     "gpeed_ctx_profile_read": [_vp, _vp, ctypes.POINTER(_i)],
     "gpeed_iq3xxs_dequantize": [_vp, _vp, _u64, _vp],

@@ -89,6 +89,10 @@ struct gpeed_ctx {
     DevBuf<float> partial, topk_w, h, D, mvout;
     DevBuf<int> topk_ids, perm, inv_pos, counts, nslots;
     DevBuf<gp::SlotDesc> slots;
+    // batch-1 forward in one persistent kernel when the shape has a variant
+    bool fused_decode = true;
+    DevBuf<float> rpart;
+    unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
     bool prof = false;
     cudaEvent_t ev[6] = {};
@@ -118,42 +122,55 @@ __global__ void make_slots_kernel(gp::SlotDesc* slots, int* nslots, int n_tok, i
 }
 
 // Pipeline depth that fits the opt-in shared memory (227 KB) next to the
-// 64 KB decode tables, counting per-stage partial sums for up to 8 tokens.
-int stages_for(int in_dim, int nm, int tile_rows, int nkw) {
-    const int per_stage = nm * tile_rows * 98 * (in_dim / 256) + nm * tile_rows * nkw * 8 * 4;
+// 64 KB decode tables, counting the per-stage partial sums.
+int stages_for(int in_dim, int nm, int tile_rows, int nw, int nt) {
+    const int per_stage = nm * tile_rows * 98 * (in_dim / 256) + nm * tile_rows * nw * nt * 4 + 12;
     const int budget = 227 * 1024 - 65536 - 1024;
     return std::min(8, budget / per_stage);
 }
 
-// GEMV geometry for a given K (in_dim) and number of matrices per stage.
+// GEMV geometry for a given K (in_dim), matrices per stage (nm) and tokens per
+// slot (nt): the most consumer warps NW (the kernel's cap, gemv_max_warps) such
+// that 32*NW is a multiple of the sub-blocks per row SB, then the largest tile
+// TR (multiple of 8, <= 32) whose stage splits into P <= 8 whole passes, whose
+// reduction fits one butterfly (P * rows-per-warp * nt <= 32), that leaves at
+// least 3 stages, that divides rows_div (the rows of one expert, 0 = any),
+// and that has an instantiated kernel.
 struct Geo {
-    int unit, nkw, rpm, tile_rows, stages;
+    int nwarps, tile_rows, passes, rpw, stages;
 };
 
-int pick_geo(int in_dim, int nm, Geo* g) {
-    if (in_dim % 1024 == 0 && in_dim / 1024 <= 15 / nm) {
-        g->unit = 32;
-        g->nkw = in_dim / 1024;
-    } else if (in_dim % 512 == 0 && in_dim / 512 <= 15 / nm) {
-        g->unit = 16;
-        g->nkw = in_dim / 512;
-    } else {
-        return fail(GPEED_ERR_UNSUPPORTED, "in_dim %d: the expert GEMV needs a multiple of 512 (<= %d)", in_dim,
-                    15 / nm * 1024);
+int pick_geo(int in_dim, int nm, int nt, int rows_div, Geo* g) {
+    if (in_dim <= 0 || in_dim % 256) return fail(GPEED_ERR_UNSUPPORTED, "in_dim %d not a multiple of 256", in_dim);
+    const int SB = in_dim / 32;
+    const int maxw = gp::gemv_max_warps(nt, nm == 2);
+    for (int nw = maxw; nw >= 1; --nw) {
+        if ((32 * nw) % SB) continue;
+        const int rowstep = 32 * nw / SB;
+        int rpw = 1;
+        for (int w = 0; w < nw; ++w) rpw = std::max(rpw, (w * 32 + 31) / SB - (w * 32) / SB + 1);
+        for (int tr = 32; tr >= 8; tr -= 8) {
+            if ((nm * tr) % rowstep || (rows_div && rows_div % tr)) continue;
+            const int p = nm * tr / rowstep;
+            if (p > 8 || p * rpw * nt > 32) continue;
+            const int st = stages_for(in_dim, nm, tr, nw, nt);
+            if (st < 3 || !gp::gemv_variant_exists(nt, nm == 2, p, rpw)) continue;
+            if (nm * tr * 98 * (in_dim / 256) > 40 * 1024 && tr > 8) continue;  // keep stages small
+            g->nwarps = nw;
+            g->tile_rows = tr;
+            g->passes = p;
+            g->rpw = rpw;
+            g->stages = st;
+            return GPEED_OK;
+        }
     }
-    g->rpm = 1;
-    while (g->rpm < 4 && nm * g->nkw * g->rpm * 2 <= 15) g->rpm *= 2;
-    g->tile_rows = 8 * g->rpm;
-    g->stages = stages_for(in_dim, nm, g->tile_rows, g->nkw);
-    if (g->stages > 8) g->stages = 8;
-    if (g->stages < 2) return fail(GPEED_ERR_UNSUPPORTED, "in_dim %d too large for the GEMV stage ring", in_dim);
-    return GPEED_OK;
+    return fail(GPEED_ERR_UNSUPPORTED, "no expert GEMV geometry for in_dim %d, %d matrices, %d tokens per slot",
+                in_dim, nm, nt);
 }
 
-int nt_for(int unit, int ntok) {
+int nt_for(int ntok) {
     if (ntok <= 1) return 1;
     if (ntok <= 2) return 2;
-    if (unit == 16 && ntok > 4) return 8;
     return 4;
 }
 
@@ -219,10 +236,9 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* 
 
 int ensure_scratch(gpeed_ctx* c, int n, int E, int K, int H, int I) {
     const size_t nk = (size_t)n * K, na = nk + n;
-    const int nsplit_max = 16;
     const size_t max_slots = nk + E + n + 4;  // nt >= 1
     int rc;
-    if ((rc = c->partial.ensure((size_t)nsplit_max * n * E))) return rc;
+    if ((rc = c->partial.ensure((size_t)n * E))) return rc;
     if ((rc = c->topk_w.ensure(nk))) return rc;
     if ((rc = c->topk_ids.ensure(nk))) return rc;
     if ((rc = c->perm.ensure(na))) return rc;
@@ -233,12 +249,6 @@ int ensure_scratch(gpeed_ctx* c, int n, int E, int K, int H, int I) {
     if ((rc = c->h.ensure(na * I))) return rc;
     if ((rc = c->D.ensure(na * H))) return rc;
     return GPEED_OK;
-}
-
-int pick_nsplit(int H) {
-    for (int s = 8; s >= 1; --s)
-        if (H % (128 * s) == 0) return s;
-    return 0;
 }
 
 }  // namespace
@@ -267,6 +277,13 @@ int gpeed_ctx_create(int device, gpeed_ctx** out) {
         return fail(GPEED_ERR_CUDA, "cudaMalloc failed in ctx_create");
     }
     cudaMemset(c->status, 0, sizeof(uint32_t));
+    if (cudaMalloc(&c->sync, 4 * sizeof(unsigned)) != cudaSuccess) {
+        cudaFree(c->tables);
+        cudaFree(c->status);
+        delete c;
+        return fail(GPEED_ERR_CUDA, "cudaMalloc failed in ctx_create");
+    }
+    cudaMemset(c->sync, 0, 4 * sizeof(unsigned));
     cudaError_t e = gp::build_tables(c->tables, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -293,6 +310,8 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     c->slots.release();
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
+    c->rpart.release();
+    cudaFree(c->sync);
     cudaFree(c->tables);
     cudaFree(c->status);
     delete c;
@@ -308,10 +327,19 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
     GP_CUDA(cudaMemcpy(&st, c->status, sizeof(st), cudaMemcpyDeviceToHost));
     if (st) {
         GP_CUDA(cudaMemset(c->status, 0, sizeof(uint32_t)));
+        GP_CUDA(cudaMemset(c->sync, 0, 4 * sizeof(unsigned)));  // a kernel that gave up may leave them set
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape)", st);
     }
     return GPEED_OK;
+}
+
+int gpeed_ctx_set_option(gpeed_ctx* c, int option, int value) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    switch (option) {
+        case GPEED_OPT_FUSED_DECODE: c->fused_decode = value != 0; return GPEED_OK;
+        default: return fail(GPEED_ERR_INVALID, "unknown option %d", option);
+    }
 }
 
 int gpeed_ctx_profile(gpeed_ctx* c, int enable) {
@@ -393,12 +421,12 @@ int gpeed_matmul_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int 
     int rc;
     if ((rc = set_device(c))) return rc;
     Geo g;
-    if ((rc = pick_geo(in_dim, 1, &g))) return rc;
+    const int nt = nt_for(n_tok);
+    if ((rc = pick_geo(in_dim, 1, nt, 0, &g))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     const int64_t g0 = (int64_t)row0 / 8 * 8, skip = (int64_t)row0 - g0;
     const int64_t ntile = (skip + out_dim + g.tile_rows - 1) / g.tile_rows;
     const int64_t rows_eff = ntile * g.tile_rows;
-    const int nt = nt_for(g.unit, n_tok);
     const int ns = (n_tok + nt - 1) / nt;
     if ((rc = c->slots.ensure(ns))) return rc;
     if ((rc = c->nslots.ensure(1))) return rc;
@@ -413,8 +441,7 @@ int gpeed_matmul_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int 
     a.in_dim = in_dim;
     a.rows = (int)rows_eff;
     a.tile_rows = g.tile_rows;
-    a.rpm = g.rpm;
-    a.nkw = g.nkw;
+    a.nwarps = g.nwarps;
     a.stages = g.stages;
     a.slots = c->slots.p;
     a.nslots = c->nslots.p;
@@ -426,7 +453,7 @@ int gpeed_matmul_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int 
     a.tables = c->tables;
     a.status = c->status;
     const int grid = (int)std::min<int64_t>(c->num_sms, ntile * ns);
-    GP_CUDA(gp::launch_gemv(a, g.unit, nt, false, grid, st, false));
+    GP_CUDA(gp::launch_gemv(a, nt, false, g.passes, g.rpw, grid, st, false));
     if (!direct)
         GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * out_dim, c->mvout.p + skip, sizeof(float) * rows_eff,
                                   sizeof(float) * out_dim, n_tok, cudaMemcpyDeviceToDevice, st));
@@ -507,24 +534,72 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     if ((rc = set_device(c))) return rc;
     if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    const int nsplit = pick_nsplit(H);
     auto mark = [&](int i) {
         if (c->prof) cudaEventRecord(c->ev[i], st);
     };
+    if (n == 1 && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
+        if ((rc = c->rpart.ensure((size_t)8 * E))) return rc;
+        gp::DecodeLayerArgs da{};
+        da.router = L.router;
+        da.corr = L.corr;
+        da.gate = L.gate;
+        da.up = L.up;
+        da.down = L.down;
+        da.gu_stride = L.gu_stride;
+        da.d_stride = L.d_stride;
+        da.H = H;
+        da.I = I;
+        da.E = E;
+        da.K = K;
+        da.routed_scale = s.routed_scale;
+        da.norm_topk = s.norm_topk;
+        da.limit = s.swiglu_limit;
+        da.with_shared = s.n_shared;
+        da.x = x;
+        da.x_bf16 = x_dtype == GPEED_DTYPE_BF16;
+        da.y = y;
+        da.forced = forced;
+        da.topk_ids = topk_ids;
+        da.topk_w = topk_w;
+        da.rpart = c->rpart.p;
+        da.h = c->h.p;
+        da.D = c->D.p;
+        da.sync = c->sync;
+        da.tables = c->tables;
+        da.status = c->status;
+        da.stages = 4;
+        mark(0);
+        mark(1);
+        mark(2);
+        GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
+        mark(3);
+        mark(4);
+        mark(5);
+        if (c->prof) {
+            GP_CUDA(cudaEventSynchronize(c->ev[5]));
+            for (int i = 0; i < 5; ++i) {
+                float ms = 0.f;
+                GP_CUDA(cudaEventElapsedTime(&ms, c->ev[i], c->ev[i + 1]));
+                c->prof_ms[i] += ms;
+            }
+            ++c->prof_calls;
+        }
+        return GPEED_OK;
+    }
     mark(0);
 
-    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, nsplit, c->partial.p};
+    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p};
     GP_CUDA(gp::launch_router(ra, st, false));
     mark(1);
 
     Geo ggu, gd;
-    if ((rc = pick_geo(H, 2, &ggu))) return rc;
-    if ((rc = pick_geo(I, 1, &gd))) return rc;
     // one slot list serves both expert kernels: its token count must suit both
-    int nt = std::min(nt_for(ggu.unit, n), nt_for(gd.unit, n));
+    const int nt = nt_for(n);
+    if ((rc = pick_geo(H, 2, nt, I, &ggu))) return rc;
+    if ((rc = pick_geo(I, 1, nt, H, &gd))) return rc;
     gp::RouteArgs ro{};
-    ro.partial = c->partial.p;
-    ro.nsplit = nsplit;
+    ro.logits = c->partial.p;
+    ro.topk_ready = 0;
     ro.corr = L.corr;
     ro.forced = forced;
     ro.n = n;
@@ -554,9 +629,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     a.expert_stride = L.gu_stride;
     a.in_dim = H;
     a.rows = I;
-    a.tile_rows = 8;  // I % 8 == 0; tiles never straddle experts
-    a.rpm = 1;
-    a.nkw = ggu.nkw;
+    a.tile_rows = ggu.tile_rows;
+    a.nwarps = ggu.nwarps;
     a.stages = ggu.stages;
     a.slots = c->slots.p;
     a.nslots = c->nslots.p;
@@ -567,9 +641,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     a.limit = s.swiglu_limit;
     a.tables = c->tables;
     a.status = c->status;
-    if (I % a.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "inter %% 8 != 0");
-    a.stages = stages_for(H, 2, 8, ggu.nkw);
-    GP_CUDA(gp::launch_gemv(a, ggu.unit, nt, true, c->num_sms, st, !c->prof));
+    if (I % a.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "inter %% %d != 0", a.tile_rows);
+    GP_CUDA(gp::launch_gemv(a, nt, true, ggu.passes, ggu.rpw, c->num_sms, st, !c->prof));
     mark(3);
 
     gp::GemvArgs d{};
@@ -579,8 +652,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     d.in_dim = I;
     d.rows = H;
     d.tile_rows = gd.tile_rows;
-    d.rpm = gd.rpm;
-    d.nkw = gd.nkw;
+    d.nwarps = gd.nwarps;
     d.stages = gd.stages;
     d.slots = c->slots.p;
     d.nslots = c->nslots.p;
@@ -591,7 +663,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     d.tables = c->tables;
     d.status = c->status;
     if (H % d.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "hidden %% %d != 0", d.tile_rows);
-    GP_CUDA(gp::launch_gemv(d, gd.unit, nt, false, c->num_sms, st, !c->prof));
+    GP_CUDA(gp::launch_gemv(d, nt, false, gd.passes, gd.rpw, c->num_sms, st, !c->prof));
     mark(4);
 
     gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, s.n_shared, y};
@@ -673,11 +745,11 @@ int gpeed_matmul_quant_noalloc(gpeed_ctx* c, int handle, uint64_t row0, int in_d
     int rc;
     if ((rc = set_device(c))) return rc;
     Geo g;
-    if ((rc = pick_geo(in_dim, 1, &g))) return rc;
+    const int nt = nt_for(n_tok);
+    if ((rc = pick_geo(in_dim, 1, nt, 0, &g))) return rc;
     const int64_t g0 = (int64_t)row0 / 8 * 8, skip = (int64_t)row0 - g0;
     const int64_t ntile = (skip + out_dim + g.tile_rows - 1) / g.tile_rows;
     const int64_t rows_eff = ntile * g.tile_rows;
-    const int nt = nt_for(g.unit, n_tok);
     const int ns = (n_tok + nt - 1) / nt;
     const bool direct = skip == 0 && rows_eff == out_dim;
     // scratch layout: [slots][nslots][staged output]
@@ -703,8 +775,7 @@ int gpeed_matmul_quant_noalloc(gpeed_ctx* c, int handle, uint64_t row0, int in_d
     a.in_dim = in_dim;
     a.rows = (int)rows_eff;
     a.tile_rows = g.tile_rows;
-    a.rpm = g.rpm;
-    a.nkw = g.nkw;
+    a.nwarps = g.nwarps;
     a.stages = g.stages;
     a.slots = slots;
     a.nslots = nslots;
@@ -716,7 +787,7 @@ int gpeed_matmul_quant_noalloc(gpeed_ctx* c, int handle, uint64_t row0, int in_d
     a.tables = c->tables;
     a.status = c->status;
     const int grid = (int)std::min<int64_t>(c->num_sms, ntile * ns);
-    GP_CUDA(gp::launch_gemv(a, g.unit, nt, false, grid, st, false));
+    GP_CUDA(gp::launch_gemv(a, nt, false, g.passes, g.rpw, grid, st, false));
     if (!direct)
         GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * out_dim, staged + skip, sizeof(float) * rows_eff,
                                   sizeof(float) * out_dim, n_tok, cudaMemcpyDeviceToDevice, st));

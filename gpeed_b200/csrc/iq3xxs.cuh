@@ -58,19 +58,37 @@ GP_DEVINL void iq3_build_tables(uint8_t* tbl, int tid, int nthreads) {
     }
 }
 
+// The lookup tables sit at the start of the kernel's dynamic shared memory,
+// whose shared-window address is GP_DSMEM_BASE for kernels without static
+// shared memory (1 KB is reserved by the system below it).  Folding that
+// constant into the load's immediate offset makes each lookup one PRMT (or
+// LOP3) plus one LDS.  Kernels verify the base at entry (gp_tables_at_base).
+#define GP_DSMEM_BASE 1024u
+GP_DEVINL bool gp_tables_at_base(const void* dyn_smem) { return smem_u32(dyn_smem) == GP_DSMEM_BASE; }
+GP_DEVINL uint32_t tbl_grid(uint32_t off) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1+1024];" : "=r"(v) : "r"(off));
+    return v;
+}
+GP_DEVINL uint32_t tbl_sel(uint32_t off) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1+1152];" : "=r"(v) : "r"(off));  // words 32..63 of the row
+    return v;
+}
+
 // Codebook word for the index in byte `m` of q (selector constant 0x55m4:
 // byte0 <- lane offset, byte1 <- index, bytes 2,3 <- 0 => index*256 + lane*4).
 template <int M>
 GP_DEVINL uint32_t iq3_grid(const uint8_t* tbl, uint32_t q, uint32_t lane4) {
-    const uint32_t off = prmt(q, lane4, 0x5504u | (M << 4));
-    return *reinterpret_cast<const uint32_t*>(tbl + off);
+    (void)tbl;
+    return tbl_grid(prmt(q, lane4, 0x5504u | (M << 4)));
 }
 
 // Selector word for the 7-bit sign field whose bits sit at positions 8..14 of f
 // (the caller shifts aux so the field lands there).
 GP_DEVINL uint32_t iq3_sel(const uint8_t* tbl, uint32_t f, uint32_t lane4) {
-    const uint32_t off = (f & 0x7F00u) | (lane4 + 128u);
-    return *reinterpret_cast<const uint32_t*>(tbl + off);
+    (void)tbl;
+    return tbl_sel((f & 0x7F00u) | lane4);
 }
 
 // Signed int8 weights for 4 positions: magnitudes g, selector sel (low 16 bits).
@@ -125,6 +143,8 @@ GP_DEVINL int iq3_idot(const uint32_t (&sw)[N], const uint32_t* xq) {
 GP_DEVINL float iq3_subscale(float d, uint32_t aux) {
     return d * (float)((aux >> 27) | 1u) * 0.25f;
 }
+// The odd factor 2s+1 of a sub-block; |isum * (2s+1)| < 2^31 for int16 activations.
+GP_DEVINL int iq3_oddscale(uint32_t aux) { return (int)((aux >> 27) | 1u); }
 
 // Quantises UNIT activations to int16 pairs; returns the scale sx (x ~= sx*q).
 template <int UNIT>

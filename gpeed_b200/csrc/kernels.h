@@ -27,11 +27,10 @@ struct GemvArgs {
     const uint8_t* w0;         // repacked matrix (gate, or the single matrix)
     const uint8_t* w1;         // repacked up matrix (gate/up mode) or nullptr
     int64_t expert_stride;     // bytes between experts in w0 / w1
-    int in_dim;                // K (multiple of 512)
-    int rows;                  // output rows per expert
+    int in_dim;                // K (multiple of 256)
+    int rows;                  // output rows per expert (a multiple of tile_rows)
     int tile_rows;             // rows per pipeline stage per matrix (multiple of 8)
-    int rpm;                   // row groups (warps along rows) per matrix
-    int nkw;                   // warps along K: in_dim / (32 * UNIT)
+    int nwarps;                // consumer warps; 32 * nwarps is a multiple of in_dim / 32
     int stages;
     const SlotDesc* slots;
     const int* nslots;         // device-resident slot count
@@ -44,9 +43,13 @@ struct GemvArgs {
     uint32_t* status;          // device status word (0 = ok)
 };
 
-// Launches the fused-decode GEMV.  unit: 32 or 16 weights per lane; nt: max
-// tokens per slot (1, 2, 4 or 8); gateup: w1 present, SwiGLU epilogue.
-cudaError_t launch_gemv(const GemvArgs& a, int unit, int nt, bool gateup, int grid, cudaStream_t st, bool pdl);
+// Launches the fused-decode GEMV.  nt: max tokens per slot (1, 2, 4, 8);
+// gateup: w1 present, SwiGLU epilogue; passes / rows_per_warp describe the
+// work mapping (see gemv.cu) and must name an instantiated variant.
+bool gemv_variant_exists(int nt, bool gateup, int passes, int rows_per_warp);
+int gemv_max_warps(int nt, bool gateup);
+cudaError_t launch_gemv(const GemvArgs& a, int nt, bool gateup, int passes, int rows_per_warp, int grid,
+                        cudaStream_t st, bool pdl);
 size_t gemv_smem_bytes(const GemvArgs& a, int nt, bool gateup);
 
 // Builds the 64 KB decode-table image (codebook + sign selectors) in global memory.
@@ -63,20 +66,20 @@ cudaError_t launch_dequantize(const uint8_t* raw, float* dst, int64_t nblocks, c
 cudaError_t launch_synth(uint8_t* dst, uint64_t seed, uint64_t stream, uint64_t block0, int64_t nblocks,
                          cudaStream_t st);
 
-// Router: partial logits [nsplit][n][E] = X[n][H] . W[E][H] over K-chunks.
+// Router: logits [n][E] = X[n][H] . W[E][H] (fp32).
 struct RouterArgs {
     const float* w;       // [E][H] fp32
     const void* x;        // [n][H]
     int x_bf16;
-    int n, H, E, nsplit;
-    float* partial;       // [nsplit][n][E]
+    int n, H, E;
+    float* logits;        // [n][E]
 };
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl);
 
 // Top-k, histogram, stable expert-major permutation and slot list.
 struct RouteArgs {
-    const float* partial;  // [nsplit][n][E]
-    int nsplit;
+    const float* logits;   // [n][E]
+    int topk_ready;        // top-k already in topk_ids / topk_w (large batches)
     const float* corr;     // [E] or nullptr
     const int* forced;     // [n][K] or nullptr
     int n, E, K;
@@ -96,6 +99,7 @@ struct RouteArgs {
     uint32_t* status;
 };
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl);
+size_t route_smem_bytes(int n, int E, int K);
 
 // Y[t] = sum_k w[t][k] * D[inv_pos[t][k]] (+ D[n*K + t] when with_shared).
 struct CombineArgs {
@@ -106,5 +110,36 @@ struct CombineArgs {
     float* y;
 };
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl);
+
+// One MoE layer at batch 1 in one cooperative persistent kernel (decode_layer.cu).
+struct DecodeLayerArgs {
+    const float* router;       // [E][H] fp32
+    const float* corr;         // [E] or nullptr
+    const uint8_t* gate;       // repacked, experts 0..E-1 then the shared expert at E
+    const uint8_t* up;
+    const uint8_t* down;
+    int64_t gu_stride, d_stride;
+    int H, I, E, K;
+    float routed_scale;
+    int norm_topk;
+    float limit;
+    int with_shared;
+    const void* x;             // [H] bf16 or fp32
+    int x_bf16;
+    float* y;                  // [H]
+    const int* forced;         // [K] or nullptr
+    int* topk_ids;             // [K] or nullptr
+    float* topk_w;             // [K] or nullptr
+    float* rpart;              // [8][E] router slice sums
+    float* h;                  // [K+1][I]
+    float* D;                  // [K+1][H]
+    unsigned* sync;            // [4] grid counters, zero between launches
+    const uint8_t* tables;
+    uint32_t* status;
+    int stages;
+};
+bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
+size_t decode_layer_smem(int H, int I, int stages);
+cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st);
 
 }  // namespace gp

@@ -1,16 +1,19 @@
 // Router, top-k routing and the weighted un-permute of the MoE layer.
 //
 //  router_kernel   fp32 router logits (reference model.cpp:41-46/702 for one
-//                  token, model_batch.cpp:172 for a batch), split along K into
-//                  nsplit chunks whose partial sums are added in a fixed order
-//                  by route_kernel (deterministic, no atomics).
+//                  token, model_batch.cpp:172 for a batch): one CTA per expert
+//                  row, warps striding the row, partial sums added in a fixed
+//                  order (deterministic, no atomics).
 //  route_kernel    sigmoid scores, +correction bias, top-K by choice (ties to
 //                  the lower expert id), weights score/(1e-20 + sum)*scale
 //                  (model.cpp:704-725, model_batch.cpp:184-203), then the
 //                  expert histogram, exclusive scan and stable expert-major
 //                  permutation (model_batch.cpp:204-219), and the slot list
 //                  (experts split into runs of <= nt assignments) consumed by
-//                  the expert kernels.  One CTA; warp-level scans and ballots.
+//                  the expert kernels.  One CTA.  The stable permutation is
+//                  computed in parallel: each expert keeps a bitmap of the
+//                  tokens that chose it, and a token's rank inside its expert
+//                  is the popcount of the bitmap below it.
 //  combine_kernel  y[t] = sum_k w[t][k] * D[pos(t,k)] (+ shared-expert row),
 //                  in top-k order (model.cpp:741-755; the batched reference
 //                  adds in expert-id order, model_batch.cpp:257-280 - a
@@ -24,51 +27,58 @@ namespace gp {
 namespace {
 
 constexpr int kRouterWarps = 8;
-constexpr int kRouterTok = 8;   // tokens per warp task
+constexpr int kRouterTok = 8;     // tokens per CTA
+constexpr int kRouterMaxVec = 8;  // float4s per lane (H <= 8192)
 
-// One warp task = (expert row e, K-chunk c, token chunk); lane-strided float4s.
+// One CTA = one expert row e for up to 8 tokens.  The 8 warps stride the row
+// in float4s; every lane issues all of its weight loads before any arithmetic,
+// and the 8 warp sums are added in warp order (deterministic).
 __global__ void __launch_bounds__(32 * kRouterWarps) router_kernel(const RouterArgs a) {
+    __shared__ float s_part[kRouterWarps][kRouterTok];
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const int task = blockIdx.x * kRouterWarps + (threadIdx.x >> 5);
-    const int ntc = (a.n + kRouterTok - 1) / kRouterTok;
-    const int ntask = a.E * a.nsplit * ntc;
-    if (task >= ntask) return;
-    const int e = task % a.E;
-    const int c = (task / a.E) % a.nsplit;
-    const int tc = task / (a.E * a.nsplit);
-    const int chunk = a.H / a.nsplit;       // multiple of 128
-    const int k0 = c * chunk;
-    const float* w = a.w + (int64_t)e * a.H + k0;
-    float acc[kRouterTok];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int e = blockIdx.x;
+    const int tc = blockIdx.y;
+    const int nq = a.H / 4;                       // float4s per row
+    const int q0 = warp * 32 + lane;              // this lane's first float4
+    const float4* w = reinterpret_cast<const float4*>(a.w + (int64_t)e * a.H);
+    float4 wv[kRouterMaxVec];
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.f;
-    for (int k = lane * 4; k < chunk; k += 128) {
-        const float4 wv = *reinterpret_cast<const float4*>(w + k);
+    for (int i = 0; i < kRouterMaxVec; ++i)
+        if (q0 + 256 * i < nq) wv[i] = w[q0 + 256 * i];
+    const int ntok = min(kRouterTok, a.n - tc * kRouterTok);
+    for (int t = 0; t < ntok; ++t) {
+        const int64_t tok = tc * kRouterTok + t;
+        float acc = 0.f;
+        float4 xv[kRouterMaxVec];
 #pragma unroll
-        for (int t = 0; t < kRouterTok; ++t) {
-            const int tok = tc * kRouterTok + t;
-            if (tok >= a.n) break;
-            float4 xv;
+        for (int i = 0; i < kRouterMaxVec; ++i) {
+            const int q = q0 + 256 * i;
+            if (q >= nq) break;
             if (a.x_bf16) {
-                const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) +
-                                                                (int64_t)tok * a.H + k0 + k);
-                xv = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
-                                 __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+                const uint2 r = reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + tok * a.H)[q];
+                xv[i] = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                                    __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
             } else {
-                xv = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + (int64_t)tok * a.H + k0 + k);
+                xv[i] = reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + tok * a.H)[q];
             }
-            acc[t] = fmaf(wv.x, xv.x, acc[t]);
-            acc[t] = fmaf(wv.y, xv.y, acc[t]);
-            acc[t] = fmaf(wv.z, xv.z, acc[t]);
-            acc[t] = fmaf(wv.w, xv.w, acc[t]);
         }
-    }
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
-        const int tok = tc * kRouterTok + t;
-        const float v = warp_sum(acc[t]);
-        if (lane == 0 && tok < a.n) a.partial[((int64_t)c * a.n + tok) * a.E + e] = v;
+        for (int i = 0; i < kRouterMaxVec; ++i) {
+            if (q0 + 256 * i >= nq) break;
+            acc = fmaf(wv[i].x, xv[i].x, acc);
+            acc = fmaf(wv[i].y, xv[i].y, acc);
+            acc = fmaf(wv[i].z, xv[i].z, acc);
+            acc = fmaf(wv[i].w, xv[i].w, acc);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) s_part[warp][t] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x < ntok) {
+        float v = 0.f;
+        for (int w8 = 0; w8 < kRouterWarps; ++w8) v += s_part[w8][threadIdx.x];
+        a.logits[((int64_t)tc * kRouterTok + threadIdx.x) * a.E + e] = v;
     }
     pdl_launch_dependents();
 }
@@ -76,7 +86,71 @@ __global__ void __launch_bounds__(32 * kRouterWarps) router_kernel(const RouterA
 constexpr int kRouteThreads = 1024;
 constexpr int kMaxE = 512;
 
+// Warp-level top-K of one token: lane j holds experts j, j+32, ... (<= 16 each).
+GP_DEVINL void topk_token(const RouteArgs& a, int t, int lane, int* s_ids) {
+    const int E = a.E, K = a.K, n = a.n;
+    float lg[kMaxE / 32];
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+        const int e = lane + 32 * j;
+        lg[j] = e < E ? a.logits[(int64_t)t * E + e] : 0.f;
+    }
+    float score[kMaxE / 32], choice[kMaxE / 32];
+#pragma unroll
+    for (int j = 0; j < kMaxE / 32; ++j) {
+        const int e = lane + 32 * j;
+        score[j] = 1.0f / (1.0f + expf(-lg[j]));
+        choice[j] = e < E ? score[j] + (a.corr ? a.corr[e] : 0.f) : -INFINITY;
+    }
+    float denom = 1e-20f;
+    float my_s = 0.f;  // lane k keeps the score of the k-th pick
+    int my_e = 0;
+    for (int k = 0; k < K; ++k) {
+        int e_best;
+        if (a.forced) {
+            e_best = a.forced[(int64_t)t * K + k];
+            if (e_best < 0 || e_best >= E) {
+                if (lane == 0) atomicOr(a.status, GP_DEV_BAD_EXPERT);
+                e_best = 0;
+            }
+        } else {
+            float bv = -INFINITY;
+            int be = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < kMaxE / 32; ++j) {
+                const int e = lane + 32 * j;
+                if (e < E && (choice[j] > bv || (choice[j] == bv && e < be))) { bv = choice[j]; be = e; }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oe = __shfl_xor_sync(0xffffffffu, be, o);
+                if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+            }
+            e_best = be;
+        }
+        float sc = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMaxE / 32; ++j)
+            if (lane + 32 * j == e_best) { sc = score[j]; choice[j] = -INFINITY; }
+        sc = __shfl_sync(0xffffffffu, sc, e_best & 31);
+        denom += sc;  // model.cpp:718-721 order
+        if (lane == k) { my_s = sc; my_e = e_best; }
+    }
+    if (lane < K) {
+        const float w = a.norm_topk ? (my_s / denom) * a.routed_scale : my_s * a.routed_scale;
+        a.topk_ids[(int64_t)t * K + lane] = my_e;
+        a.topk_w[(int64_t)t * K + lane] = w;
+        if (s_ids) s_ids[t * K + lane] = my_e;
+    }
+}
+
+// Dynamic shared memory: bitmap [E][nw] + word prefix [E][nw] (nw = ceil(n/32))
+// + cached top-k ids [n*K] when n*K <= kCacheIds.
+constexpr int kCacheIds = 8192;
+
 __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a) {
+    extern __shared__ __align__(16) uint32_t dsm[];
     __shared__ int s_cnt[kMaxE];
     __shared__ int s_ptr[kMaxE + 1];
     __shared__ int s_slot0[kMaxE + 1];
@@ -87,75 +161,30 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
         if (tid == 0) { atomicOr(a.status, GP_DEV_BAD_SHAPE); *a.nslots = 0; }
         return;
     }
+    const int nw = (n + 31) / 32;
+    uint32_t* bitmap = dsm;
+    uint32_t* wpref = dsm + E * nw;
+    int* s_ids = (!a.topk_ready && n * K <= kCacheIds) ? reinterpret_cast<int*>(dsm + 2 * E * nw) : nullptr;
+    for (int i = tid; i < E * nw; i += kRouteThreads) bitmap[i] = 0;
     for (int e = tid; e < E; e += kRouteThreads) s_cnt[e] = 0;
     __syncthreads();
 
-    // 1. per token: logits -> scores -> top-K (warp per token)
-    for (int t = warp; t < n; t += nwarp) {
-        // each lane holds experts lane, lane+32, ...
-        float score[kMaxE / 32], choice[kMaxE / 32];
-#pragma unroll
-        for (int j = 0; j < kMaxE / 32; ++j) {
-            const int e = lane + 32 * j;
-            score[j] = 0.f;
-            choice[j] = -INFINITY;
-            if (e < E) {
-                float lg = 0.f;
-                for (int c = 0; c < a.nsplit; ++c) lg += a.partial[((int64_t)c * n + t) * E + e];
-                score[j] = 1.0f / (1.0f + expf(-lg));
-                choice[j] = score[j] + (a.corr ? a.corr[e] : 0.f);
-            }
-        }
-        int sel_e[32];
-        float sel_s[32];
-        float denom = 1e-20f;
-        for (int k = 0; k < K; ++k) {
-            int e_best;
-            if (a.forced) {
-                e_best = a.forced[(int64_t)t * K + k];
-                if (e_best < 0 || e_best >= E) {
-                    if (lane == 0) atomicOr(a.status, GP_DEV_BAD_EXPERT);
-                    e_best = 0;
-                }
-            } else {
-                float bv = -INFINITY;
-                int be = 0x7fffffff;
-#pragma unroll
-                for (int j = 0; j < kMaxE / 32; ++j) {
-                    const int e = lane + 32 * j;
-                    if (e < E && (choice[j] > bv || (choice[j] == bv && e < be))) { bv = choice[j]; be = e; }
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oe = __shfl_xor_sync(0xffffffffu, be, o);
-                    if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-                }
-                e_best = be;
-            }
-            // fetch the score of e_best from its owner lane, retire it
-            float sc = 0.f;
-#pragma unroll
-            for (int j = 0; j < kMaxE / 32; ++j)
-                if (lane + 32 * j == e_best) { sc = score[j]; choice[j] = -INFINITY; }
-            sc = __shfl_sync(0xffffffffu, sc, e_best & 31);
-            sel_e[k] = e_best;
-            sel_s[k] = sc;
-            denom += sc;
-        }
-        if (lane == 0) {
-            // model.cpp:718-725: w = score / denom (if norm) * scale
-            for (int k = 0; k < K; ++k) {
-                const float w = a.norm_topk ? (sel_s[k] / denom) * a.routed_scale : sel_s[k] * a.routed_scale;
-                a.topk_ids[(int64_t)t * K + k] = sel_e[k];
-                a.topk_w[(int64_t)t * K + k] = w;
-                atomicAdd(&s_cnt[sel_e[k]], 1);
-            }
-        }
+    // 1. top-K per token (warp per token)
+    if (!a.topk_ready)
+        for (int t = warp; t < n; t += nwarp) topk_token(a, t, lane, s_ids);
+    __syncthreads();
+
+    // 2. histogram and token bitmaps (thread per assignment)
+    const int nk = n * K;
+    for (int i = tid; i < nk; i += kRouteThreads) {
+        const int t = i / K;
+        const int e = s_ids ? s_ids[i] : a.topk_ids[i];
+        atomicAdd(&s_cnt[e], 1);
+        atomicOr(&bitmap[e * nw + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
 
-    // 2. exclusive scan of counts (single warp), and slot offsets per owned expert
+    // 3. exclusive scans: counts -> bucket starts; per-expert word prefixes
     if (warp == 0) {
         int run = 0, srun = 0;
         for (int base = 0; base < E; base += 32) {
@@ -176,44 +205,41 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
         }
         if (lane == 0) { s_ptr[E] = run; s_slot0[E] = srun; }
     }
+    for (int e = tid; e < E; e += kRouteThreads) {
+        uint32_t acc = 0;
+        for (int w = 0; w < nw; ++w) {
+            wpref[e * nw + w] = acc;
+            acc += __popc(bitmap[e * nw + w]);
+        }
+    }
     __syncthreads();
     for (int e = tid; e < E; e += kRouteThreads) a.counts[e] = s_cnt[e];
 
-    // 3. stable placement: warp per expert, ballot over tokens in order
-    const int nk = n * K;
+    // 4. stable positions (thread per assignment)
+    for (int i = tid; i < nk; i += kRouteThreads) {
+        const int t = i / K;
+        const int e = s_ids ? s_ids[i] : a.topk_ids[i];
+        const uint32_t below = bitmap[e * nw + (t >> 5)] & ((1u << (t & 31)) - 1u);
+        const int p = s_ptr[e] + (int)wpref[e * nw + (t >> 5)] + __popc(below);
+        a.perm_tok[p] = t;
+        a.inv_pos[i] = p;
+    }
+    // 5. slots: runs of <= nt assignments per owned expert, then the shared expert
     for (int e = warp; e < E; e += nwarp) {
-        int pos = s_ptr[e];
-        for (int t0 = 0; t0 < n; t0 += 32) {
-            const int t = t0 + lane;
-            int kk = -1;
-            if (t < n)
-                for (int k = 0; k < K; ++k)
-                    if (a.topk_ids[(int64_t)t * K + k] == e) { kk = k; break; }
-            const unsigned m = __ballot_sync(0xffffffffu, kk >= 0);
-            if (kk >= 0) {
-                const int p = pos + __popc(m & ((1u << lane) - 1u));
-                a.perm_tok[p] = t;
-                a.inv_pos[(int64_t)t * K + kk] = p;
-            }
-            pos += __popc(m);
-        }
-        // slots for this expert (only owned experts)
-        if (e >= a.expert_lo && e < a.expert_hi) {
-            const int c = s_cnt[e];
-            for (int i = lane; i * a.nt < c; i += 32) {
-                const int sidx = s_slot0[e] + i;
-                if (sidx < a.max_slots) {
-                    SlotDesc sd;
-                    sd.expert = e;
-                    sd.begin = s_ptr[e] + i * a.nt;
-                    sd.ntok = min(a.nt, c - i * a.nt);
-                    sd.pad = 0;
-                    a.slots[sidx] = sd;
-                }
+        if (e < a.expert_lo || e >= a.expert_hi) continue;
+        const int c = s_cnt[e];
+        for (int i = lane; i * a.nt < c; i += 32) {
+            const int sidx = s_slot0[e] + i;
+            if (sidx < a.max_slots) {
+                SlotDesc sd;
+                sd.expert = e;
+                sd.begin = s_ptr[e] + i * a.nt;
+                sd.ntok = min(a.nt, c - i * a.nt);
+                sd.pad = 0;
+                a.slots[sidx] = sd;
             }
         }
     }
-    // 4. shared expert: assignments nk .. nk+n-1 are tokens 0..n-1
     int total = s_slot0[E];
     if (a.with_shared) {
         for (int t = tid; t < n; t += kRouteThreads) a.perm_tok[nk + t] = t;
@@ -239,27 +265,49 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
     pdl_launch_dependents();
 }
 
+// Multi-CTA top-K for large batches (warp per token); route_kernel then skips step 1.
+__global__ void __launch_bounds__(256) topk_kernel(const RouteArgs a) {
+    pdl_wait();
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const int nwarps = (gridDim.x * blockDim.x) >> 5;
+    for (int t = warp; t < a.n; t += nwarps) topk_token(a, t, lane, nullptr);
+    pdl_launch_dependents();
+}
+
+constexpr int kCombineMaxK = 32;
+
 __global__ void combine_kernel(const CombineArgs a) {
     pdl_wait();
     const int t = blockIdx.y;
     const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
     if (j >= a.H) return;
+    int pos[kCombineMaxK];
+    float w[kCombineMaxK];
+#pragma unroll
+    for (int k = 0; k < kCombineMaxK; ++k)
+        if (k < a.K) {
+            pos[k] = a.inv_pos[(int64_t)t * a.K + k];
+            w[k] = a.topk_w[(int64_t)t * a.K + k];
+        }
+    float4 d[kCombineMaxK];
+#pragma unroll
+    for (int k = 0; k < kCombineMaxK; ++k)
+        if (k < a.K) d[k] = *reinterpret_cast<const float4*>(a.D + (int64_t)pos[k] * a.H + j);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < a.K; ++k) {
-        const float w = a.topk_w[(int64_t)t * a.K + k];
-        const int p = a.inv_pos[(int64_t)t * a.K + k];
-        const float4 d = *reinterpret_cast<const float4*>(a.D + (int64_t)p * a.H + j);
-        acc.x = fmaf(w, d.x, acc.x);
-        acc.y = fmaf(w, d.y, acc.y);
-        acc.z = fmaf(w, d.z, acc.z);
-        acc.w = fmaf(w, d.w, acc.w);
-    }
+#pragma unroll
+    for (int k = 0; k < kCombineMaxK; ++k)
+        if (k < a.K) {
+            acc.x = fmaf(w[k], d[k].x, acc.x);
+            acc.y = fmaf(w[k], d[k].y, acc.y);
+            acc.z = fmaf(w[k], d[k].z, acc.z);
+            acc.w = fmaf(w[k], d[k].w, acc.w);
+        }
     if (a.with_shared) {
-        const float4 d = *reinterpret_cast<const float4*>(a.D + ((int64_t)a.n * a.K + t) * a.H + j);
-        acc.x += d.x;
-        acc.y += d.y;
-        acc.z += d.z;
-        acc.w += d.w;
+        const float4 s = *reinterpret_cast<const float4*>(a.D + ((int64_t)a.n * a.K + t) * a.H + j);
+        acc.x += s.x;
+        acc.y += s.y;
+        acc.z += s.z;
+        acc.w += s.w;
     }
     *reinterpret_cast<float4*>(a.y + (int64_t)t * a.H + j) = acc;
 }
@@ -279,25 +327,43 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st,
 
 }  // namespace
 
+size_t route_smem_bytes(int n, int E, int K) {
+    const size_t nw = (n + 31) / 32;
+    return (2 * E * nw + ((size_t)n * K <= kCacheIds ? (size_t)n * K : 0)) * sizeof(uint32_t);
+}
+
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl) {
-    if (a.H % (128 * a.nsplit)) return cudaErrorInvalidValue;
+    if (a.H % 4 || a.H > 4 * 256 * kRouterMaxVec) return cudaErrorInvalidValue;
     const int ntc = (a.n + kRouterTok - 1) / kRouterTok;
-    const int ntask = a.E * a.nsplit * ntc;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg =
-        make_cfg(dim3((ntask + kRouterWarps - 1) / kRouterWarps), dim3(32 * kRouterWarps), 0, st, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(a.E, ntc), dim3(32 * kRouterWarps), 0, st, pdl, attr);
     return cudaLaunchKernelEx(&cfg, router_kernel, a);
 }
 
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl) {
     if (a.E > kMaxE || a.K > 32 || a.K > a.E || a.nt < 1) return cudaErrorInvalidValue;
+    const size_t smem = route_smem_bytes(a.n, a.E, a.K);
+    if (smem > 200 * 1024) return cudaErrorInvalidValue;
+    static size_t configured = 0;
+    if (smem > 48 * 1024 && configured < smem) {
+        cudaError_t e = cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (e != cudaSuccess) return e;
+        configured = 200 * 1024;
+    }
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(kRouteThreads), 0, st, pdl, attr);
-    return cudaLaunchKernelEx(&cfg, route_kernel, a);
+    RouteArgs b = a;
+    if (a.n > 64) {  // large batches: top-k on many CTAs first
+        cudaLaunchConfig_t cfg = make_cfg(dim3(min(1184, (a.n + 7) / 8)), dim3(256), 0, st, pdl, attr);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel, a);
+        if (e != cudaSuccess) return e;
+        b.topk_ready = 1;
+    }
+    cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(kRouteThreads), smem, st, pdl, attr);
+    return cudaLaunchKernelEx(&cfg, route_kernel, b);
 }
 
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl) {
-    if (a.H % 4) return cudaErrorInvalidValue;
+    if (a.H % 4 || a.K > kCombineMaxK) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3((a.H / 4 + 127) / 128, a.n), dim3(128), 0, st, pdl, attr);
     return cudaLaunchKernelEx(&cfg, combine_kernel, a);

@@ -49,6 +49,9 @@ class Context:
             call("gpeed_ctx_create", device, ctypes.byref(h))
         self.handle = h
 
+    def set_option(self, option: int, value: int) -> None:
+        call("gpeed_ctx_set_option", self.handle, option, value)
+
     def check(self, stream=None) -> None:
         call("gpeed_ctx_check", self.handle, _stream(stream))
 

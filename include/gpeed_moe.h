@@ -82,11 +82,19 @@ GPEED_API int gpeed_ctx_destroy(gpeed_ctx* ctx);
 /* Synchronises `stream` and reports (then clears) device-side error flags. */
 GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
 
+/* Context options.  GPEED_OPT_FUSED_DECODE (default 1): run a batch-1
+ * gpeed_moe_forward as one persistent kernel when the layer shape has a
+ * compiled variant; 0 forces the multi-kernel path (same results within
+ * rounding).  No counterpart in the reference. */
+#define GPEED_OPT_FUSED_DECODE 1
+GPEED_API int gpeed_ctx_set_option(gpeed_ctx* ctx, int option, int value);
+
 /* Per-stage timing of gpeed_moe_forward (no counterpart in the reference;
  * its GLM5_PROFILE phase timer, model.cpp:21-38, is host wall-clock only).
  * When enabled, each forward records CUDA events between its five kernels
  * (router, route, gate/up, down, combine) on its stream and waits for them;
- * gpeed_ctx_profile_read returns the mean milliseconds per stage. */
+ * gpeed_ctx_profile_read returns the mean milliseconds per stage.  A fused
+ * batch-1 forward is one kernel: its time is reported in the gate/up slot. */
 GPEED_API int gpeed_ctx_profile(gpeed_ctx* ctx, int enable);
 GPEED_API int gpeed_ctx_profile_read(gpeed_ctx* ctx, float* stage_ms /* [5] */, int* calls);
 
