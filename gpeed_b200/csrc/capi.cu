@@ -92,6 +92,7 @@ struct gpeed_ctx {
     // batch-1 forward in one persistent kernel when the shape has a variant
     bool fused_decode = true;
     DevBuf<float> rpart;
+    DevBuf<uint8_t> hq;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
     bool prof = false;
@@ -277,13 +278,13 @@ int gpeed_ctx_create(int device, gpeed_ctx** out) {
         return fail(GPEED_ERR_CUDA, "cudaMalloc failed in ctx_create");
     }
     cudaMemset(c->status, 0, sizeof(uint32_t));
-    if (cudaMalloc(&c->sync, 4 * sizeof(unsigned)) != cudaSuccess) {
+    if (cudaMalloc(&c->sync, gp::kDecodeSyncWords * sizeof(unsigned)) != cudaSuccess) {
         cudaFree(c->tables);
         cudaFree(c->status);
         delete c;
         return fail(GPEED_ERR_CUDA, "cudaMalloc failed in ctx_create");
     }
-    cudaMemset(c->sync, 0, 4 * sizeof(unsigned));
+    cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned));
     cudaError_t e = gp::build_tables(c->tables, 0);
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
@@ -311,6 +312,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
     c->rpart.release();
+    c->hq.release();
     cudaFree(c->sync);
     cudaFree(c->tables);
     cudaFree(c->status);
@@ -327,7 +329,7 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
     GP_CUDA(cudaMemcpy(&st, c->status, sizeof(st), cudaMemcpyDeviceToHost));
     if (st) {
         GP_CUDA(cudaMemset(c->status, 0, sizeof(uint32_t)));
-        GP_CUDA(cudaMemset(c->sync, 0, 4 * sizeof(unsigned)));  // a kernel that gave up may leave them set
+        GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));  // a kernel that gave up may leave them set
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape)", st);
     }
@@ -539,6 +541,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     };
     if (n == 1 && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
         if ((rc = c->rpart.ensure((size_t)8 * E))) return rc;
+        if ((rc = c->hq.ensure((size_t)(K + 1) * gp::decode_layer_hq_bytes(I)))) return rc;
         gp::DecodeLayerArgs da{};
         da.router = L.router;
         da.corr = L.corr;
@@ -563,25 +566,22 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         da.topk_w = topk_w;
         da.rpart = c->rpart.p;
         da.h = c->h.p;
+        da.hq = c->hq.p;
         da.D = c->D.p;
         da.sync = c->sync;
         da.tables = c->tables;
         da.status = c->status;
         da.stages = 4;
-        mark(0);
-        mark(1);
+        // profiling: the one kernel's time goes to the gate/up slot, the other
+        // stages read 0
         mark(2);
         GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
         mark(3);
-        mark(4);
-        mark(5);
         if (c->prof) {
-            GP_CUDA(cudaEventSynchronize(c->ev[5]));
-            for (int i = 0; i < 5; ++i) {
-                float ms = 0.f;
-                GP_CUDA(cudaEventElapsedTime(&ms, c->ev[i], c->ev[i + 1]));
-                c->prof_ms[i] += ms;
-            }
+            GP_CUDA(cudaEventSynchronize(c->ev[3]));
+            float ms = 0.f;
+            GP_CUDA(cudaEventElapsedTime(&ms, c->ev[2], c->ev[3]));
+            c->prof_ms[2] += ms;
             ++c->prof_calls;
         }
         return GPEED_OK;

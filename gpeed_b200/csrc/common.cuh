@@ -58,6 +58,12 @@ GP_DEVINL uint2 lds64(uint32_t addr) {
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
     return v;
 }
+GP_DEVINL uint4 lds128(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+    return v;
+}
+GP_DEVINL float ldsf(uint32_t addr) { return __uint_as_float(lds32(addr)); }
 GP_DEVINL uint32_t lds16(uint32_t addr) {
     uint16_t v;
     asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
@@ -110,6 +116,35 @@ GP_DEVINL float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
+}
+
+// ---- grid-scope ordering (counters between CTAs) ----------------------------
+GP_DEVINL void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// Orders this thread's earlier generic-proxy accesses (an acquire of data that
+// other CTAs wrote) before its later bulk-copy (async-proxy) reads of it.
+GP_DEVINL void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+GP_DEVINL void red_release_add(unsigned* p, unsigned v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Returns the old value; releases this thread's (and, through a preceding
+// warp/CTA barrier, its peers') writes and acquires those of earlier adders.
+GP_DEVINL unsigned atom_add_acq_rel(unsigned* p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+GP_DEVINL unsigned ld_acquire(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// Bounded wait for *p >= target (a counter other CTAs raise); false on timeout.
+GP_DEVINL bool wait_geq(const unsigned* p, unsigned target) {
+    for (uint32_t i = 0; i < GP_SPIN_LIMIT; ++i) {
+        if (ld_acquire(p) >= target) return true;
+        __nanosleep(32);
+    }
+    return false;
 }
 
 // Programmatic dependent launch: let the next kernel in the stream start its

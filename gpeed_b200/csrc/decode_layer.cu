@@ -4,43 +4,68 @@
 // Separate kernels for router, routing, gate/up, down and combine each pay a
 // launch, a prologue (decode tables, first bytes in flight) and a tail, which
 // at batch 1 costs more than streaming the 85 MB of weights.  Here one CTA per
-// SM runs the whole layer; the TMA producer streams weight tiles continuously
-// across the phases, and the phases meet at grid-wide counters:
+// SM runs the whole layer.  Warp roles: 24 compute warps, one TMA producer
+// warp streaming weight tiles through a ring of shared-memory stages, and one
+// epilogue warp that does the routing and turns each stage's partial sums
+// into results.  Under full HBM load a round trip to L2 costs microseconds,
+// so the layout keeps those out of the per-tile path:
 //
-//   router   every warp computes one 1/8-row slice of the fp32 router logits
-//            (fixed-order partial sums), then counter[0]
-//   top-k    every CTA reads the 8 partials per expert (added in order), applies
-//            sigmoid + bias, picks top-K (ties to the lower id) and the weights
-//            score/(1e-20 + sum)*scale (model.cpp:704-725)
-//   gate/up  the shared expert's tiles first (they need no routing, so they
-//            overlap the router phase), then the routed experts'; epilogue
-//            SwiGLU with the reference clamp into h[slot] (model.cpp:733-739);
-//            then counter[1]
-//   down     h[slot] -> D[slot] (model.cpp:740); the producer streams these
-//            tiles while the consumers wait for counter[1]; then counter[2]
-//   combine  y = sum_k w_k D[k] + D[shared] in top-k order (model.cpp:741-755)
+//   router   CTA c owns experts c, c+G, ...; 8 warps each compute one 1/8
+//            slice of an owned expert's fp32 logit (weights prefetched before
+//            the wait on the previous kernel), the epilogue warp adds the
+//            slices in order, stores the logit and bumps one counter per CTA
+//   top-k    every CTA's epilogue warp loads the E logits, applies sigmoid +
+//            bias and picks top-K by warp reductions (ties to the lower id),
+//            weights score/(1e-20 + sum)*scale (model.cpp:704-725)
+//   gate/up  units of 32 rows of h, dealt round-robin in slot order (the
+//            shared expert, storage slot K, first: it needs no routing; then
+//            routed slots 0..K-1); a unit is 4 consecutive tiles of 8 rows of
+//            gate and up.  The epilogue applies SwiGLU with the reference clamp
+//            (model.cpp:733-739), quantises the finished unit to int16 (hq)
+//            and counts it for its slot: no value of h leaves the CTA
+//            unquantised and no counter is read back
+//   down     tiles of 32 rows x (K+1) slots in tile-major order (shared slot
+//            first), a contiguous range per CTA; the producer copies each tile
+//            with its slot's hq once all units of that slot are counted
+//            (model.cpp:740).  The epilogue accumulates y = sum_k w_k D[k] +
+//            D[shared] for a whole row tile in top-k order (model.cpp:741-755);
+//            only tiles split between CTAs go through D in global memory and a
+//            counter whose last adder writes y
 //
-// Grid-wide waits need every CTA resident: the kernel is launched
+// Counters are reset by their last user, so they are zero between launches.
+// Waits on other CTAs need every CTA resident: the kernel is launched
 // cooperatively with one CTA per SM.  Every wait is bounded; a timeout sets a
 // status bit, the CTA stops waiting and finishes (results then invalid, the
-// host reports the status and resets the counters).
+// host reports the status and clears the counters).
 #include <cuda_fp16.h>
 
 #include "expert_common.cuh"
 #include "iq3xxs.cuh"
 #include "kernels.h"
 
+// Optional instrumentation hook (timestamps per CTA); compiled out here.
+#ifndef GP_STAMP
+#define GP_STAMP(i) ((void)0)
+#endif
+
 namespace gp {
 namespace {
 
-constexpr int NWC = 24;          // consumer warps
+constexpr int NWC = 24;          // compute warps
 constexpr int NWG = 20;          // of which compute gate/up (32*20 lanes = 4 rows of 5120)
-constexpr int NTHREADS = 32 * (NWC + 1);
-constexpr int TRG = 8;           // gate/up rows per matrix per stage
-constexpr int TRD = 32;          // down rows per stage
-constexpr int RSPLIT = 8;        // router row slices
-constexpr int MAXK = 32;
+constexpr int EPI = NWC;         // epilogue warp
+constexpr int PROD = NWC + 1;    // TMA producer warp
+constexpr int NTHREADS = 32 * (NWC + 2);
+constexpr int TRG = 8;           // gate/up rows per matrix per tile
+constexpr int TRD = 32;          // down rows per tile (one per epilogue lane)
+constexpr int UNIT = 32;         // activation quantisation unit = rows of h per gate/up unit
+constexpr int TPU = UNIT / TRG;  // gate/up tiles per unit
+constexpr int RSPLIT = 8;        // router slices per expert
+constexpr int MAXK = 31;         // K+1 slots fit one warp
 constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
+constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
+constexpr int kMaxUnits = 64;
+static_assert(TRD == 32, "the combine maps one row of a down tile to each epilogue lane");
 
 struct Smem {
     uint32_t stage_bytes, stages_off, partial_off, bar_off, misc_off, total;
@@ -48,32 +73,29 @@ struct Smem {
 
 __host__ __device__ inline Smem decode_smem(int H, int I, int S) {
     Smem L;
-    const uint32_t gu = 2u * TRG * 98u * (H / 256), dn = TRD * 98u * (I / 256);
+    const uint32_t gu = 2u * TRG * 98u * (H / 256);
+    const uint32_t dn = TRD * 98u * (I / 256) + (uint32_t)I * 2u + (uint32_t)(I / UNIT) * 4u;
     L.stage_bytes = ((gu > dn ? gu : dn) + 15u) & ~15u;
     L.stages_off = GP_IQ3_TABLE_BYTES;
     L.partial_off = L.stages_off + S * L.stage_bytes;
     const uint32_t pb = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC) * 4u;
     L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
-    L.misc_off = L.bar_off + (2u * S + 2u) * 8u;
-    L.total = L.misc_off + 16u + 4u * S + 8u * MAXK + 8u * kMaxEFused + 16u;
+    L.misc_off = L.bar_off + (3u * S + 3u) * 8u;
+    // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT]
+    L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT;
     return L;
 }
 
-GP_DEVINL void red_release_add(unsigned* p, unsigned v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-GP_DEVINL unsigned ld_acquire(const unsigned* p) {
+GP_DEVINL unsigned ld_relaxed(const unsigned* p) {
     unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-// Bounded grid-wide wait for *p >= target.
-GP_DEVINL bool wait_geq(const unsigned* p, unsigned target) {
-    for (uint32_t i = 0; i < GP_SPIN_LIMIT; ++i) {
-        if (ld_acquire(p) >= target) return true;
-        __nanosleep(64);
-    }
-    return false;
+
+// Monotonic map of a float onto u32 (for redux max); -0 is folded onto +0 first.
+GP_DEVINL uint32_t order_key(float f) {
+    const uint32_t u = __float_as_uint(f + 0.0f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 // Per-lane view of one GEMV phase (in_dim = IN, NW warps, P passes): this
@@ -160,34 +182,25 @@ GP_DEVINL float load_quant(const void* x, int x_bf16, int64_t row, int in_dim, i
     return 0.25f * quant_i16<32>(v, xq);
 }
 
-// Last of the NWC consumer warps to finish a stage?  (That warp then sums the
-// stage's per-warp partials in warp order.)
-GP_DEVINL bool stage_done(int* counter, int lane) {
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-        __threadfence_block();
-        last = atomicAdd(counter, 1) == NWC - 1;
-        if (last) *counter = 0;
-        __threadfence_block();
-    }
-    return __shfl_sync(0xffffffffu, last, 0) != 0;
-}
-
-// One warp: top-K by choice (ties to the lower id) from the CTA's scores in
-// shared memory, and the weights score/(1e-20 + sum)*scale (model.cpp:704-725);
-// publishes them to the CTA.
-GP_DEVINL void topk_warp(const DecodeLayerArgs& a, int lane, int c, const float* s_score, const float* s_choice,
+// Epilogue warp: sigmoid scores from the gathered logits, top-K by score +
+// bias (ties to the lower id), weights score/(1e-20 + sum)*scale
+// (model.cpp:704-725); publishes them to the CTA.  Each round takes the lanes'
+// best remaining key to a warp maximum (redux), then the lowest id holding it.
+GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float (&bias)[kMaxEFused / 32], int lane, int c,
                          int* s_ids, float* s_w, uint32_t topk_bar) {
     const int E = a.E, K = a.K;
     constexpr int EJ = kMaxEFused / 32;
-    float score[EJ], choice[EJ];
+    float lg[EJ];
+#pragma unroll
+    for (int j = 0; j < EJ; ++j) lg[j] = lane + 32 * j < E ? __ldcg(a.rpart + lane + 32 * j) : 0.f;
+    float score[EJ];
+    uint32_t key[EJ];
 #pragma unroll
     for (int j = 0; j < EJ; ++j) {
-        const int e = lane + 32 * j;
-        score[j] = e < E ? s_score[e] : 0.f;
-        choice[j] = e < E ? s_choice[e] : -INFINITY;
+        score[j] = 1.0f / (1.0f + expf(-lg[j]));
+        key[j] = lane + 32 * j < E ? order_key(score[j] + bias[j]) : 0u;  // 0: below every float's key
     }
+    if (lane == 0) GP_STAMP(13);
     float denom = 1e-20f, my_s = 0.f;
     int my_e = 0;
     for (int k = 0; k < K; ++k) {
@@ -199,24 +212,18 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, int lane, int c, const float*
                 eb = 0;
             }
         } else {
-            float bv = -INFINITY;
-            eb = 0x7fffffff;
+            uint32_t bk = 0;
+            int bj = 0;
 #pragma unroll
-            for (int j = 0; j < EJ; ++j) {
-                const int e = lane + 32 * j;
-                if (e < E && (choice[j] > bv || (choice[j] == bv && e < eb))) { bv = choice[j]; eb = e; }
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oe = __shfl_xor_sync(0xffffffffu, eb, o);
-                if (ov > bv || (ov == bv && oe < eb)) { bv = ov; eb = oe; }
-            }
+            for (int j = 0; j < EJ; ++j)
+                if (key[j] > bk) { bk = key[j]; bj = j; }  // strict: the lowest id of the lane on ties
+            const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+            eb = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
         }
         float sc = 0.f;
 #pragma unroll
         for (int j = 0; j < EJ; ++j)
-            if (lane + 32 * j == eb) { sc = score[j]; choice[j] = -INFINITY; }
+            if (lane + 32 * j == eb) { sc = score[j]; key[j] = 0u; }
         sc = __shfl_sync(0xffffffffu, sc, eb & 31);
         denom += sc;  // model.cpp:718-721 order
         if (lane == k) { my_s = sc; my_e = eb; }
@@ -232,8 +239,52 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, int lane, int c, const float*
     if (lane == 0) mbar_arrive(topk_bar);  // release: the producer reads s_ids
 }
 
-// Shared-expert gate/up tiles of CTA cc: tiles cc, cc+G, ... below tg.
-GP_DEVINL int shared_tiles(int cc, int G, int tg) { return cc < tg ? (tg - 1 - cc) / G + 1 : 0; }
+// Work item i of a phase in slot order: the shared expert (storage slot K)
+// first, then routed slots 0..K-1; `per_slot` items each.
+struct Item {
+    int slot, idx;
+};
+GP_DEVINL Item item_of(int i, int per_slot, int K) {
+    if (i < per_slot) return {K, i};
+    const int r = i - per_slot, slot = r / per_slot;
+    return {slot, r - slot * per_slot};
+}
+// Items i = c, c+G, c+2G, ... below total.
+GP_DEVINL int items_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
+
+// Down work: CTA c owns the range [v0, v1) of (row tile, slot order q) pairs,
+// v = tile*(K+1) + q, slot order q = 0 the shared expert, q >= 1 routed slot
+// q-1.  The range is walked from its first tile boundary, the leading partial
+// tile (late slots) last.
+struct DownRange {
+    int v0, v1, b;
+    GP_DEVINL int count() const { return v1 - v0; }
+    GP_DEVINL int at(int i) const { return b + i < v1 ? b + i : v0 + (b + i - v1); }
+};
+GP_DEVINL DownRange down_range(int c, int G, int total, int per_tile) {
+    DownRange r;
+    r.v0 = (int)((int64_t)total * c / G);
+    r.v1 = (int)((int64_t)total * (c + 1) / G);
+    const int b = (r.v0 + per_tile - 1) / per_tile * per_tile;
+    r.b = b < r.v1 ? b : r.v0;
+    return r;
+}
+
+// Quantises the unit of h held one value per lane exactly as a lane quantises
+// its activations for the GEMV (quant_i16<32>, scale * 1/4), into hq: 16
+// int16-pair words at unit*64, the scale at 2*I + unit*4.
+GP_DEVINL void quantise_unit(float v, uint8_t* hq, int I, int unit, int lane) {
+    float amax = fabsf(v);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
+    const int q = __float2int_rn(v * inv);
+    const int qn = __shfl_down_sync(0xffffffffu, q, 1);
+    if (!(lane & 1))
+        reinterpret_cast<uint32_t*>(hq)[unit * (UNIT / 2) + (lane >> 1)] =
+            (static_cast<uint32_t>(q) & 0xFFFFu) | (static_cast<uint32_t>(qn) << 16);
+    if (lane == 0) reinterpret_cast<float*>(hq + 2 * I)[unit] = 0.25f * (amax * (1.0f / 32767.0f));
+}
 
 template <int HH, int II, int PG, int RPWG, int PD, int RPWD>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeLayerArgs a) {
@@ -241,95 +292,130 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
     constexpr int H = HH, I = II;
+    constexpr int TD = H / TRD, NU = I / UNIT;
+    constexpr uint32_t GU_BYTES = TRG * 98u * (H / 256), DN_BYTES = TRD * 98u * (I / 256);
+    constexpr uint32_t HQ_BYTES = I * 2u + NU * 4u;
+    static_assert(NU <= kMaxUnits && TD <= kDecodeSyncWords - kSyncTile, "counter block too small");
+    static_assert(UNIT % TRG == 0 && HQ_BYTES % 16 == 0 && DN_BYTES % 16 == 0 && GU_BYTES % 16 == 0,
+                  "bulk copies need 16-byte sizes and offsets");
     const int E = a.E, K = a.K, S = a.stages;
     const Smem L = decode_smem(H, I, S);
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t full0 = sbase + L.bar_off, empty0 = full0 + 8u * S;
-    const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u;
+    // per stage: full (producer -> compute warps), pdone (compute warps ->
+    // epilogue warp: partial sums written), empty (epilogue -> producer)
+    const uint32_t full0 = sbase + L.bar_off, pdone0 = full0 + 8u * S, empty0 = pdone0 + 8u * S;
+    const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u;
     volatile uint32_t* s_abort = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off);
-    int* s_done = reinterpret_cast<int*>(smem + L.misc_off + 16u);
-    int* s_ids = reinterpret_cast<int*>(smem + L.misc_off + 16u + 4u * S);
-    float* s_w = reinterpret_cast<float*>(s_ids + MAXK);
-    float* s_score = s_w + MAXK;
-    float* s_choice = s_score + kMaxEFused;
-    const uint32_t gu_bytes = TRG * 98u * (H / 256), dn_bytes = TRD * 98u * (I / 256);
-    const int TG = I / TRG, TD = H / TRD;             // tiles per expert
-    // gate/up items per CTA are balanced over shared + routed tiles: CTA c
-    // takes shared tiles c, c+G, ... and as many routed tiles as keeps its total
-    // at floor((c+1)T/G) - floor(cT/G), T = TG * (K+1)
-    const int nA = shared_tiles(c, G, TG);
-    const int sharedA = (TG / G) * c + min(c, TG % G);  // shared tiles taken by CTAs before c
-    const int T = TG * (K + 1), nD_total = (K + 1) * TD;
-    const int rb = (int)((int64_t)T * c / G) - sharedA;
-    const int re = (int)((int64_t)T * (c + 1) / G) - sharedA - nA;
-    const int db = (int)((int64_t)nD_total * c / G), de = (int)((int64_t)nD_total * (c + 1) / G);
-    const int n_gu = nA + (re - rb);
-    const int n_items = n_gu + (de - db);
+    int* s_ids = reinterpret_cast<int*>(smem + L.misc_off + 16u);
+    float* s_w = reinterpret_cast<float*>(s_ids + 32);
+    float* s_slice = s_w + 32;
+    float* partial = reinterpret_cast<float*>(smem + L.partial_off);
+    constexpr uint32_t pstride = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC);
+    const uint32_t stage0 = sbase + L.stages_off;
+    const int n_gu = TPU * items_of(c, G, NU * (K + 1));
+    const int n_shared = TPU * items_of(c, G, NU);  // leading gate/up tiles that need no routing
+    const DownRange R = down_range(c, G, TD * (K + 1), K + 1);
+    const int n_items = n_gu + R.count();
+    const int n_own = items_of(c, G, E);            // router experts c, c+G, ...
+    const int n_tasks = n_own * RSPLIT;
 
+    // the next kernel's CTAs may take each SM as soon as ours leaves it; they
+    // wait for this grid's results before reading any of them
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(full0 + 8u * s, 1);
-            mbar_init(empty0 + 8u * s, NWC);
-            s_done[s] = 0;
+            mbar_init(pdone0 + 8u * s, NWC);
+            mbar_init(empty0 + 8u * s, 1);
         }
         mbar_init(tbar, 1);
         mbar_init(topk_bar, 1);
+        mbar_init(rbar, n_tasks > 0 ? n_tasks : 1);
         *s_abort = gp_tables_at_base(smem) ? 0u : 1u;
         if (*s_abort) atomicOr(a.status, GP_DEV_BAD_SHAPE);
         fence_mbar_init();
     }
     __syncthreads();
 
-    if (warp == NWC) {
-        // ================= producer =================
+    if (warp == PROD) {
+        // ================= producer (lane 0 issues; the warp polls) =================
         if (lane == 0) {
+            GP_STAMP(9);
             mbar_arrive_expect_tx(tbar, GP_IQ3_TABLE_BYTES);
             for (int k4 = 0; k4 < 4; ++k4) bulk_g2s(sbase + k4 * 16384u, a.tables + k4 * 16384, 16384u, tbar);
-            int s = 0, issued = 0;
-            uint32_t ph = 1;
-            bool have_topk = false;
-            for (int it = 0; it < n_items && !*s_abort; ++it, ++issued) {
-                const uint8_t* src0;
-                const uint8_t* src1 = nullptr;
-                uint32_t bytes;
-                if (it < nA) {                            // shared expert gate/up
-                    const int64_t off = (int64_t)E * a.gu_stride + (int64_t)(c + it * G) * gu_bytes;
-                    src0 = a.gate + off;
-                    src1 = a.up + off;
-                    bytes = gu_bytes;
-                } else {
-                    if (!have_topk) {                     // routed tiles need the top-k
-                        if (!mbar_wait(topk_bar, 0)) {
-                            *s_abort = 1;
-                            atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
-                            break;
-                        }
-                        have_topk = true;
+        }
+        int s = 0, issued = 0;
+        uint32_t ph = 1, ready = 0;
+        bool have_topk = false;
+        for (int it = 0; it < n_items; ++it) {
+            if (__shfl_sync(0xffffffffu, *s_abort, 0)) break;
+            int slot;
+            uint32_t off, b0, b1;
+            const uint8_t *src0, *src1;
+            if (it < n_gu) {
+                const Item u = item_of(c + (it / TPU) * G, NU, K);
+                slot = u.slot;
+                off = (uint32_t)(u.idx * TPU + it % TPU) * GU_BYTES;
+                b0 = b1 = GU_BYTES;
+            } else {
+                const int v = R.at(it - n_gu), q = v % (K + 1);
+                slot = q == 0 ? K : q - 1;
+                off = (uint32_t)(v / (K + 1)) * DN_BYTES;
+                b0 = DN_BYTES;
+                b1 = HQ_BYTES;
+                // the tile travels with its slot's quantised h: wait (warp-wide
+                // poll of every slot's counter) until all its units are counted
+                if (!((ready >> slot) & 1u)) {
+                    uint32_t n = 0;
+                    for (; n < GP_SPIN_LIMIT; ++n) {
+                        const unsigned cnt = lane <= K ? ld_relaxed(a.sync + kSyncSlot + lane) : 0u;
+                        ready = __ballot_sync(0xffffffffu, lane <= K && cnt >= (unsigned)NU);
+                        if ((ready >> slot) & 1u) break;
+                        __nanosleep(64);
                     }
-                    if (it < n_gu) {                      // routed gate/up
-                        const int r = rb + (it - nA), k = r / TG, t = r - k * TG;
-                        const int64_t off = (int64_t)s_ids[k] * a.gu_stride + (int64_t)t * gu_bytes;
-                        src0 = a.gate + off;
-                        src1 = a.up + off;
-                        bytes = gu_bytes;
-                    } else {                              // down
-                        const int r = db + (it - n_gu), slot = r / TD, t = r - slot * TD;
-                        const int e = slot < K ? s_ids[slot] : E;
-                        src0 = a.down + (int64_t)e * a.d_stride + (int64_t)t * dn_bytes;
-                        bytes = dn_bytes;
+                    if (n == GP_SPIN_LIMIT) {
+                        if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                        break;
                     }
+                    fence_acq_rel_gpu();
+                    if (lane == 0 && it == n_gu) GP_STAMP(12);
                 }
-                if (!mbar_wait(empty0 + 8u * s, ph)) {
-                    *s_abort = 1;
-                    atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
-                    break;
-                }
-                const uint32_t dst = sbase + L.stages_off + s * L.stage_bytes;
-                mbar_arrive_expect_tx(full0 + 8u * s, src1 ? 2u * bytes : bytes);
-                bulk_g2s(dst, src0, bytes, full0 + 8u * s);
-                if (src1) bulk_g2s(dst + bytes, src1, bytes, full0 + 8u * s);
-                if (++s == S) { s = 0; ph ^= 1u; }
             }
+            if (lane == 0) {
+                bool ok = true;
+                if (it >= n_shared && !have_topk) {  // routed tiles need the top-k
+                    ok = have_topk = mbar_wait(topk_bar, 0);
+                    if (ok) GP_STAMP(10);
+                    else { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                }
+                if (ok) {
+                    const int e = slot < K ? s_ids[slot] : E;
+                    if (it < n_gu) {
+                        const int64_t eo = (int64_t)e * a.gu_stride + off;
+                        src0 = a.gate + eo;
+                        src1 = a.up + eo;
+                    } else {
+                        fence_proxy_async_global();
+                        src0 = a.down + (int64_t)e * a.d_stride + off;
+                        src1 = a.hq + (int64_t)slot * HQ_BYTES;
+                    }
+                    if (!mbar_wait(empty0 + 8u * s, ph)) {
+                        *s_abort = 1;
+                        atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
+                    } else {
+                        const uint32_t dst = stage0 + s * L.stage_bytes;
+                        mbar_arrive_expect_tx(full0 + 8u * s, b0 + b1);
+                        bulk_g2s(dst, src0, b0, full0 + 8u * s);
+                        bulk_g2s(dst + b0, src1, b1, full0 + 8u * s);
+                        ++issued;
+                        if (++s == S) { s = 0; ph ^= 1u; }
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        if (lane == 0) {
+            // no copy may still be in flight when the CTA exits
             for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
                 mbar_wait(full0 + 8u * (i % S), (uint32_t)(i / S) & 1u);
             mbar_wait(tbar, 0);
@@ -337,179 +423,207 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         return;
     }
 
-    // ================= consumers =================
-    pdl_wait();
-    const uint32_t stage0 = sbase + L.stages_off;
-    float* partial = reinterpret_cast<float*>(smem + L.partial_off);
-    const uint32_t pstride = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC);
-
-    // ---- router slices: warp task = (expert e, slice) ----
-    {
-        const int slice = H / RSPLIT;          // multiple of 128 (host-checked), <= 1024
-        for (int task = c * NWC + warp; task < E * RSPLIT; task += G * NWC) {
-            const int e = task % E, sl = task / E;
-            const float* w = a.router + (int64_t)e * H + sl * slice + lane * 4;
-            float acc = 0.f;
+    if (warp == EPI) {
+        // ================= routing, then the epilogues =================
+        constexpr int EJ = kMaxEFused / 32;
+        float bias[EJ];
 #pragma unroll
-            for (int i0 = 0; i0 < 8; i0 += 4) {  // 4 weight + 4 activation float4s in flight
-                float4 wv[4], xv[4];
+        for (int j = 0; j < EJ; ++j) bias[j] = a.corr && lane + 32 * j < E ? __ldg(a.corr + lane + 32 * j) : 0.f;
+        pdl_wait();
+        if (n_tasks > 0) {  // this CTA's experts: slices added in order
+            if (!mbar_wait(rbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (lane < n_own) {
+                float lg = 0.f;
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    if ((i0 + i) * 128 < slice) wv[i] = *reinterpret_cast<const float4*>(w + (i0 + i) * 128);
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    if ((i0 + i) * 128 < slice) {
-                        const int k0 = sl * slice + lane * 4 + (i0 + i) * 128;
-                        if (a.x_bf16) {
-                            const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + k0);
-                            xv[i] = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
-                                                __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
-                        } else {
-                            xv[i] = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + k0);
-                        }
-                    }
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    if ((i0 + i) * 128 < slice) {
-                        acc = fmaf(wv[i].x, xv[i].x, acc);
-                        acc = fmaf(wv[i].y, xv[i].y, acc);
-                        acc = fmaf(wv[i].z, xv[i].z, acc);
-                        acc = fmaf(wv[i].w, xv[i].w, acc);
-                    }
+                for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[lane * RSPLIT + sl];
+                a.rpart[c + lane * G] = lg;
             }
-            acc = warp_sum(acc);
-            if (lane == 0) a.rpart[(int64_t)sl * E + e] = acc;
+            __syncwarp();
+            if (lane == 0) red_release_add(a.sync + kSyncRouter, (unsigned)n_own);
         }
-        named_bar_sync(1, NWC * 32);
-        if (tid == 0) {
-            __threadfence();
-            red_release_add(a.sync + 0, 1);
-            if (!*s_abort && !wait_geq(a.sync + 0, (unsigned)G)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+        if (lane == 0) {
+            GP_STAMP(1);
+            if (!wait_geq(a.sync + kSyncRouter, (unsigned)E)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            GP_STAMP(11);
         }
-        named_bar_sync(1, NWC * 32);
-        __threadfence();
-    }
+        __syncwarp();
+        fence_acq_rel_gpu();
+        topk_warp(a, bias, lane, c, s_ids, s_w, topk_bar);
+        if (lane == 0) GP_STAMP(2);
 
-    // ---- logits -> scores (one thread per expert, slices added in order) ----
-    for (int e = tid; e < E; e += NWC * 32) {
-        float lg = 0.f;
-        float v[RSPLIT];
-#pragma unroll
-        for (int sl = 0; sl < RSPLIT; ++sl) v[sl] = a.rpart[(int64_t)sl * E + e];
-#pragma unroll
-        for (int sl = 0; sl < RSPLIT; ++sl) lg += v[sl];
-        const float sc = 1.0f / (1.0f + expf(-lg));
-        s_score[e] = sc;
-        s_choice[e] = sc + (a.corr ? a.corr[e] : 0.f);
-    }
-    named_bar_sync(1, NWC * 32);
-    // ---- top-k (warp NWG: idle in the gate/up phase) ----
-    if (warp == NWG) topk_warp(a, lane, c, s_score, s_choice, s_ids, s_w, topk_bar);
-
-    if (!mbar_wait(tbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-    int s = 0;
-    uint32_t ph = 0;
-
-    // ---- gate/up items: the shared expert's tiles, then the routed ones ----
-    {
-        const auto mg = lane_map<HH, NWG, PG>(warp < NWG ? warp : 0, lane, stage0);
-        uint32_t xq[16];
-        float sx4 = 0.f;
-        if (warp < NWG) sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
-        const int rs = 32 * NWG / (H / 32);
-        for (int it = 0; it < n_gu; ++it) {
-            int slot, tile;
-            if (it < nA) { slot = K; tile = c + it * G; }
-            else { const int r = rb + (it - nA); slot = r / TG; tile = r - slot * TG; }
-            if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            float* pbuf = partial + (size_t)s * pstride;
-            if (!*s_abort && warp < NWG) consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, pbuf, warp, lane);
-            if (stage_done(s_done + s, lane) && !*s_abort) {
-                for (int row = lane; row < TRG; row += 32) {
-                    const int ur = TRG + row;
-                    const int g0 = (row % rs) * (H / 32) / 32, g1 = ((row % rs + 1) * (H / 32) - 1) / 32;
-                    const int u0 = (ur % rs) * (H / 32) / 32, u1 = ((ur % rs + 1) * (H / 32) - 1) / 32;
+        int s = 0;
+        uint32_t ph = 0;
+        constexpr int rsg = 32 * NWG / (H / 32), rsd = 32 * NWC / (I / 32);
+        float hv = 0.f, acc = 0.f, d_sh = 0.f;
+        for (int it = 0; it < n_items; ++it) {
+            const bool gu = it < n_gu;
+            if (!*s_abort && !mbar_wait(pdone0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            const float* pbuf = partial + (size_t)s * pstride;
+            float val = 0.f;
+            if (gu) {
+                if (lane < TRG) {
+                    const int row = lane, ur = TRG + row;
+                    const int g0 = (row % rsg) * (H / 32) / 32, g1 = ((row % rsg + 1) * (H / 32) - 1) / 32;
+                    const int u0 = (ur % rsg) * (H / 32) / 32, u1 = ((ur % rsg + 1) * (H / 32) - 1) / 32;
                     float gs = 0.f, us = 0.f;
                     for (int w = g0; w <= g1; ++w) gs += pbuf[row * NWG + w];
                     for (int w = u0; w <= u1; ++w) us += pbuf[ur * NWG + w];
-                    a.h[(int64_t)slot * I + tile * TRG + row] = silu_clamped(gs, us, a.limit);
+                    val = silu_clamped(gs, us, a.limit);
                 }
-                __syncwarp();
+            } else {
+                const int r0 = lane % rsd;
+                const int w0 = r0 * (I / 32) / 32, w1 = ((r0 + 1) * (I / 32) - 1) / 32;
+                for (int w = w0; w <= w1; ++w) val += pbuf[lane * NWC + w];
             }
-            if (lane == 0) mbar_arrive(empty0 + 8u * s);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8u * s);  // partials read: the stage may refill
             if (++s == S) { s = 0; ph ^= 1u; }
-        }
-    }
-
-    // every h written grid-wide before any down tile is consumed
-    named_bar_sync(1, NWC * 32);
-    if (tid == 0) {
-        __threadfence();
-        red_release_add(a.sync + 1, 1);
-        if (!*s_abort && !wait_geq(a.sync + 1, (unsigned)G)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-    }
-    named_bar_sync(1, NWC * 32);
-    __threadfence();
-
-    // ---- down items ----
-    {
-        const auto md = lane_map<II, NWC, PD>(warp, lane, stage0);
-        uint32_t xq[16];
-        float sx4 = 0.f;
-        int cur_slot = -1;
-        const int rs = 32 * NWC / (I / 32);
-        for (int it = n_gu; it < n_items; ++it) {
-            const int r = db + (it - n_gu), slot = r / TD, tile = r - slot * TD;
-            if (slot != cur_slot) {
-                cur_slot = slot;
-                sx4 = load_quant(a.h, 0, slot, I, md.sb, xq);
-            }
-            if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            float* pbuf = partial + (size_t)s * pstride;
-            if (!*s_abort) consume<II, NWC, PD, RPWD>(md, s * L.stage_bytes, xq, sx4, pbuf, warp, lane);
-            if (stage_done(s_done + s, lane) && !*s_abort) {
-                for (int row = lane; row < TRD; row += 32) {
-                    const int r0 = row % rs;
-                    const int w0 = r0 * (I / 32) / 32, w1 = ((r0 + 1) * (I / 32) - 1) / 32;
-                    float dsum = 0.f;
-                    for (int w = w0; w <= w1; ++w) dsum += pbuf[row * NWC + w];
-                    a.D[(int64_t)slot * H + tile * TRD + row] = dsum;
+            if (gu) {
+                // rows j*8 .. j*8+7 of the unit land on lanes j*8 .. j*8+7
+                const int j = it % TPU;
+                const float v = __shfl_sync(0xffffffffu, val, lane & (TRG - 1));
+                if ((lane / TRG) == j) hv = v;
+                if (j == TPU - 1 && !*s_abort) {
+                    const Item u = item_of(c + (it / TPU) * G, NU, K);
+                    quantise_unit(hv, a.hq + (int64_t)u.slot * HQ_BYTES, I, u.idx, lane);
+                    __syncwarp();
+                    if (lane == 0) red_release_add(a.sync + kSyncSlot + u.slot, 1);
                 }
-                __syncwarp();
+            } else if (!*s_abort) {
+                const int v = R.at(it - n_gu), t = v / (K + 1), q = v % (K + 1);
+                const int slot = q == 0 ? K : q - 1;
+                const int j = t * TRD + lane;
+                const int tb = t * (K + 1), te = tb + K + 1;
+                if (tb >= R.v0 && te <= R.v1) {
+                    // whole row tile in this CTA, slots in order: y directly
+                    if (q == 0) { d_sh = val; acc = 0.f; }
+                    else acc = fmaf(s_w[q - 1], val, acc);
+                    if (q == K) a.y[j] = acc + d_sh;
+                } else {
+                    // tile split between CTAs: D in global memory, the last adder writes y
+                    a.D[(int64_t)slot * H + j] = val;
+                    const int mine_end = te < R.v1 ? te : R.v1;
+                    if (v == mine_end - 1) {
+                        const int mine = mine_end - (tb > R.v0 ? tb : R.v0);
+                        unsigned* dcnt = a.sync + kSyncTile + t;
+                        __syncwarp();
+                        unsigned done = 0;
+                        if (lane == 0) done = atom_add_acq_rel(dcnt, (unsigned)mine) + mine == (unsigned)(K + 1);
+                        if (__shfl_sync(0xffffffffu, done, 0)) {
+                            fence_acq_rel_gpu();
+                            float y = 0.f;
+                            for (int k = 0; k < K; ++k) y = fmaf(s_w[k], __ldcg(a.D + (int64_t)k * H + j), y);
+                            a.y[j] = y + __ldcg(a.D + (int64_t)K * H + j);
+                            if (lane == 0) *dcnt = 0;
+                        }
+                    }
+                }
             }
-            if (lane == 0) mbar_arrive(empty0 + 8u * s);
-            if (++s == S) { s = 0; ph ^= 1u; }
         }
-    }
+        if (lane == 0) GP_STAMP(7);
+    } else {
+        // ================= compute warps =================
+        // router weights of this warp's first slice: independent of the
+        // previous kernel, so loaded before waiting for it
+        constexpr int RSL = H / RSPLIT, RV = RSL / 128;
+        static_assert(H % (RSPLIT * 128) == 0 && RV <= 8, "router slices are whole float4 columns");
+        float4 wv[RV];
+        auto load_router = [&](int task) {
+            const float* w = a.router + (int64_t)(c + (task / RSPLIT) * G) * H + (task % RSPLIT) * RSL + lane * 4;
+#pragma unroll
+            for (int i = 0; i < RV; ++i) wv[i] = __ldg(reinterpret_cast<const float4*>(w + i * 128));
+        };
+        if (warp < n_tasks) load_router(warp);
+        pdl_wait();
+        if (tid == 0) GP_STAMP(0);
 
-    // ---- combine: this CTA's slice of rows ----
-    named_bar_sync(1, NWC * 32);
-    if (tid == 0) {
-        __threadfence();
-        red_release_add(a.sync + 2, 1);
-        if (!*s_abort && !wait_geq(a.sync + 2, (unsigned)G)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-    }
-    named_bar_sync(1, NWC * 32);
-    __threadfence();
-    {
-        const int j0 = (int)((int64_t)H * c / G), j1 = (int)((int64_t)H * (c + 1) / G);
-        for (int j = j0 + tid; j < j1; j += NWC * 32) {
+        // ---- router slices of this CTA's experts: warp task = (expert, slice) ----
+        for (int task = warp; task < n_tasks; task += NWC) {
+            if (task != warp) load_router(task);
+            const int sl = task % RSPLIT;
             float acc = 0.f;
-            for (int k = 0; k < K; ++k) acc = fmaf(s_w[k], a.D[(int64_t)k * H + j], acc);
-            if (a.with_shared) acc += a.D[(int64_t)K * H + j];
-            a.y[j] = acc;
+#pragma unroll
+            for (int i = 0; i < RV; ++i) {
+                const int k0 = sl * RSL + lane * 4 + i * 128;
+                float4 xv;
+                if (a.x_bf16) {
+                    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + k0);
+                    xv = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                                     __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+                } else {
+                    xv = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + k0);
+                }
+                acc = fmaf(wv[i].x, xv.x, acc);
+                acc = fmaf(wv[i].y, xv.y, acc);
+                acc = fmaf(wv[i].z, xv.z, acc);
+                acc = fmaf(wv[i].w, xv.w, acc);
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) {
+                s_slice[task] = acc;
+                mbar_arrive(rbar);
+            }
         }
+
+        if (!mbar_wait(tbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+        int s = 0;
+        uint32_t ph = 0;
+        // ---- gate/up tiles (warps >= NWG only keep the stage protocol) ----
+        {
+            const auto mg = lane_map<HH, NWG, PG>(warp < NWG ? warp : 0, lane, stage0);
+            uint32_t xq[16];
+            float sx4 = 0.f;
+            if (warp < NWG) sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
+            for (int it = 0; it < n_gu; ++it) {
+                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (tid == 0 && it == n_shared) GP_STAMP(3);
+                if (!*s_abort && warp < NWG)
+                    consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pdone0 + 8u * s);
+                if (++s == S) { s = 0; ph ^= 1u; }
+            }
+        }
+        if (tid == 0) GP_STAMP(4);
+        // ---- down tiles: the activations come with the tile ----
+        {
+            const auto md = lane_map<II, NWC, PD>(warp, lane, stage0);
+            for (int it = n_gu; it < n_items; ++it) {
+                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (tid == 0 && it == n_gu) GP_STAMP(5);
+                if (!*s_abort) {
+                    const uint32_t xb = stage0 + s * L.stage_bytes + DN_BYTES;
+                    uint32_t xq[16];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const uint4 v = lds128(xb + md.sb * 64u + 16u * i);
+                        xq[4 * i] = v.x;
+                        xq[4 * i + 1] = v.y;
+                        xq[4 * i + 2] = v.z;
+                        xq[4 * i + 3] = v.w;
+                    }
+                    const float sx4 = ldsf(xb + 2u * I + md.sb * 4u);
+                    consume<II, NWC, PD, RPWD>(md, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp,
+                                               lane);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pdone0 + 8u * s);
+                if (++s == S) { s = 0; ph ^= 1u; }
+            }
+        }
+        if (tid == 0) GP_STAMP(6);
     }
-    // the last CTA out resets the counters for the next launch
-    named_bar_sync(1, NWC * 32);
+
+    // the last CTA out clears the counters that are waited on
+    named_bar_sync(1, (NWC + 1) * 32);
     if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(a.sync + 3, 1u) == (unsigned)G - 1) {
-            a.sync[0] = 0;
-            a.sync[1] = 0;
-            a.sync[2] = 0;
-            __threadfence();
-            a.sync[3] = 0;
+        GP_STAMP(8);
+        fence_acq_rel_gpu();
+        if (atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1) {
+            a.sync[kSyncRouter] = 0;
+            for (int k = 0; k <= K; ++k) a.sync[kSyncSlot + k] = 0;
+            fence_acq_rel_gpu();
+            a.sync[kSyncEnd] = 0;
         }
     }
 }
@@ -528,10 +642,12 @@ size_t decode_layer_smem(int H, int I, int stages) { return decode_smem(H, I, st
 
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st) {
     if (!decode_layer_supported(a.H, a.I, a.E, a.K, a.with_shared)) return cudaErrorInvalidValue;
+    if (grid * kMaxOwned < a.E) return cudaErrorInvalidValue;  // router experts per CTA
     const Smem L = decode_smem(a.H, a.I, a.stages);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
     auto kern = decode_layer_kernel<5120, 1536, 4, 1, 2, 2>;
     static int configured = 0;
+    static bool pdl_ok = true;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
@@ -542,12 +658,22 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kern, a);
+    cfg.numAttrs = pdl_ok ? 2 : 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+    if (e != cudaSuccess && pdl_ok) {
+        // a driver that refuses the pair: launch without the early start
+        (void)cudaGetLastError();
+        pdl_ok = false;
+        cfg.numAttrs = 1;
+        e = cudaLaunchKernelEx(&cfg, kern, a);
+    }
+    return e;
 }
 
 }  // namespace gp

@@ -132,12 +132,23 @@ struct DecodeLayerArgs {
     float* topk_w;             // [K] or nullptr
     float* rpart;              // [8][E] router slice sums
     float* h;                  // [K+1][I]
+    uint8_t* hq;               // [K+1][decode_layer_hq_bytes(I)] h quantised per 32-unit
     float* D;                  // [K+1][H]
-    unsigned* sync;            // [4] grid counters, zero between launches
+    unsigned* sync;            // [kDecodeSyncWords] counters, zero between launches
     const uint8_t* tables;
     uint32_t* status;
     int stages;
 };
+// Counter words of the persistent kernel (all zero between launches; the host
+// clears them after a launch that reported an error).
+constexpr int kSyncRouter = 0;                  // CTAs done with their router slices
+constexpr int kSyncEnd = 1;                     // CTAs finished
+constexpr int kSyncSlot = 8;                    // [K+1] h units quantised per slot
+constexpr int kSyncUnit = 64;                   // [K+1][64] gate/up tiles done per h unit
+constexpr int kSyncTile = kSyncUnit + 33 * 64;  // [H/32] down slots done per row tile
+constexpr int kDecodeSyncWords = 4096;
+// h[slot] as int16 pairs (I*2 bytes) followed by one fp32 scale per 32-unit.
+inline size_t decode_layer_hq_bytes(int I) { return (size_t)I * 2 + (size_t)(I / 32) * 4; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
 size_t decode_layer_smem(int H, int I, int stages);
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st);
