@@ -195,7 +195,7 @@ def run_gpu(args, rank, local_rank, world):
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
 
-    # one static token per layer copy; graphs of one forward each
+    # one static token per layer copy
     xs = [tokens(1, 100 + l).cuda() for l in range(L)]
     ys = [torch.empty(1, H, device="cuda") for _ in range(L)]
     with torch.cuda.stream(stream):
@@ -203,21 +203,35 @@ def run_gpu(args, rank, local_rank, world):
             layers[l].forward(xs[l], ys[l], stream=stream)
     stream.synchronize()
     ctx.check(stream)
-    graphs = []
-    for l in range(L):
+    # graphs of consecutive layer forwards, as a model runs its MoE layers: a
+    # step is one layer forward; chains[n] runs layers 0..n-1 back to back, so
+    # each layer's kernel can start while the previous one drains
+    def chain(n):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
-            layers[l].forward(xs[l], ys[l], stream=stream)
-        graphs.append(g)
+            for l in range(n):
+                layers[l].forward(xs[l], ys[l], stream=stream)
+        return g
+
+    chains = {L: chain(L)}
+
+    def run_steps(n):
+        for _ in range(n // L):
+            chains[L].replay()
+        if n % L:
+            if n % L not in chains:
+                chains[n % L] = chain(n % L)
+            chains[n % L].replay()
 
     def barrier():
         if world > 1:
             dist.barrier()
 
     # ---- device-resident throughput (value) ----
+    if args.steps % L and args.steps % L not in chains:
+        chains[args.steps % L] = chain(args.steps % L)
     with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            graphs[i % L].replay()
+        run_steps(args.warmup)
     stream.synchronize()
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -225,8 +239,7 @@ def run_gpu(args, rank, local_rank, world):
         torch.cuda.synchronize()
         with torch.cuda.stream(stream):
             ev0.record(stream)
-            for i in range(args.steps):
-                graphs[i % L].replay()
+            run_steps(args.steps)
             ev1.record(stream)
         stream.synchronize()
         ms_total = ev0.elapsed_time(ev1)
@@ -234,8 +247,7 @@ def run_gpu(args, rank, local_rank, world):
         soak_t0 = time.perf_counter()
         with torch.cuda.stream(stream):
             while time.perf_counter() - soak_t0 < 1.5:
-                for i in range(200):
-                    graphs[i % L].replay()
+                run_steps(25 * L)
                 stream.synchronize()
     barrier()
     ctx.check(stream)
@@ -336,7 +348,7 @@ def run_gpu(args, rank, local_rank, world):
             "gpu_launches": (1 if fused else 5) * args.steps,
             "clocks": clk.summary(),
         }
-    del graphs, e2e_graphs
+    del chains, e2e_graphs
     ctx.close()
     return line
 

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "lib", "libgpeed_moe.so")
 OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_UNSUPPORTED, ERR_NCCL = range(6)
 DTYPE_F32, DTYPE_IQ3_XXS, DTYPE_BF16 = 0, 18, 30
 OPT_FUSED_DECODE = 1
+OPT_FUSED_COOPERATIVE = 2
 
 
 class GpeedError(RuntimeError):

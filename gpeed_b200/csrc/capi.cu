@@ -91,7 +91,8 @@ struct gpeed_ctx {
     DevBuf<gp::SlotDesc> slots;
     // batch-1 forward in one persistent kernel when the shape has a variant
     bool fused_decode = true;
-    DevBuf<float> rpart;
+    bool fused_cooperative = false;
+    DevBuf<unsigned long long> logits;
     DevBuf<uint8_t> hq;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
@@ -311,7 +312,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     c->slots.release();
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
-    c->rpart.release();
+    c->logits.release();
     c->hq.release();
     cudaFree(c->sync);
     cudaFree(c->tables);
@@ -329,7 +330,10 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
     GP_CUDA(cudaMemcpy(&st, c->status, sizeof(st), cudaMemcpyDeviceToHost));
     if (st) {
         GP_CUDA(cudaMemset(c->status, 0, sizeof(uint32_t)));
-        GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));  // a kernel that gave up may leave them set
+        // a kernel that gave up may leave counters set; generation and logit
+        // tags restart together
+        GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));
+        if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape)", st);
     }
@@ -340,6 +344,7 @@ int gpeed_ctx_set_option(gpeed_ctx* c, int option, int value) {
     if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
     switch (option) {
         case GPEED_OPT_FUSED_DECODE: c->fused_decode = value != 0; return GPEED_OK;
+        case GPEED_OPT_FUSED_COOPERATIVE: c->fused_cooperative = value != 0; return GPEED_OK;
         default: return fail(GPEED_ERR_INVALID, "unknown option %d", option);
     }
 }
@@ -540,7 +545,10 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         if (c->prof) cudaEventRecord(c->ev[i], st);
     };
     if (n == 1 && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
-        if ((rc = c->rpart.ensure((size_t)8 * E))) return rc;
+        const size_t had = c->logits.n;
+        if ((rc = c->logits.ensure((size_t)E))) return rc;
+        if (c->logits.n != had)  // tags must start below the first launch's
+            GP_CUDA(cudaMemsetAsync(c->logits.p, 0, c->logits.n * sizeof(unsigned long long), st));
         if ((rc = c->hq.ensure((size_t)(K + 1) * gp::decode_layer_hq_bytes(I)))) return rc;
         gp::DecodeLayerArgs da{};
         da.router = L.router;
@@ -564,7 +572,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         da.forced = forced;
         da.topk_ids = topk_ids;
         da.topk_w = topk_w;
-        da.rpart = c->rpart.p;
+        da.logits = c->logits.p;
         da.h = c->h.p;
         da.hq = c->hq.p;
         da.D = c->D.p;
@@ -572,6 +580,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         da.tables = c->tables;
         da.status = c->status;
         da.stages = 4;
+        da.cooperative = c->fused_cooperative;
         // profiling: the one kernel's time goes to the gate/up slot, the other
         // stages read 0
         mark(2);

@@ -81,11 +81,20 @@ __host__ __device__ inline Smem decode_smem(int H, int I, int S) {
     const uint32_t pb = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC) * 4u;
     L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
     L.misc_off = L.bar_off + (3u * S + 3u) * 8u;
-    // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT]
-    L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT;
+    // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT],
+    // one down row tile's per-slot values [MAXK + 1][32]
+    L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT + 4u * (MAXK + 1) * 32u;
     return L;
 }
 
+GP_DEVINL unsigned long long ld_relaxed64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+GP_DEVINL void st_relaxed64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 GP_DEVINL unsigned ld_relaxed(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -184,49 +193,91 @@ GP_DEVINL float load_quant(const void* x, int x_bf16, int64_t row, int in_dim, i
 
 // Epilogue warp: sigmoid scores from the gathered logits, top-K by score +
 // bias (ties to the lower id), weights score/(1e-20 + sum)*scale
-// (model.cpp:704-725); publishes them to the CTA.  Each round takes the lanes'
-// best remaining key to a warp maximum (redux), then the lowest id holding it.
-GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float (&bias)[kMaxEFused / 32], int lane, int c,
-                         int* s_ids, float* s_w, uint32_t topk_bar) {
+// (model.cpp:704-725); publishes them to the CTA.  Each lane sorts its EJ
+// candidates (expert ids lane + 32j) by (key desc, id asc); a round then takes
+// the warp maximum of the lanes' head keys (redux), the lowest id holding it,
+// and that lane pops its head.
+template <int EJ>
+GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t tag, int lane, int c, int* s_ids,
+                         float* s_w, uint32_t topk_bar, volatile uint32_t* s_abort) {
     const int E = a.E, K = a.K;
-    constexpr int EJ = kMaxEFused / 32;
-    float lg[EJ];
+    // every CTA's logits, each word tagged by its writer with this launch's
+    // tag: the data is its own flag, so one poll round trip suffices
+    unsigned long long w[EJ];
+    uint32_t n = 0;
+    for (; n < GP_SPIN_LIMIT; ++n) {
 #pragma unroll
-    for (int j = 0; j < EJ; ++j) lg[j] = lane + 32 * j < E ? __ldcg(a.rpart + lane + 32 * j) : 0.f;
+        for (int j = 0; j < EJ; ++j) w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + lane + 32 * j) : 0ull;
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < EJ; ++j) ok &= lane + 32 * j >= E || (uint32_t)(w[j] >> 32) == tag;
+        if (__all_sync(0xffffffffu, ok)) break;
+        __nanosleep(32);
+    }
+    if (n == GP_SPIN_LIMIT && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+    if (lane == 0) GP_STAMP(11);
     float score[EJ];
-    uint32_t key[EJ];
+    uint32_t key[EJ], id[EJ];
 #pragma unroll
     for (int j = 0; j < EJ; ++j) {
-        score[j] = 1.0f / (1.0f + expf(-lg[j]));
-        key[j] = lane + 32 * j < E ? order_key(score[j] + bias[j]) : 0u;  // 0: below every float's key
+        const int e = lane + 32 * j;
+        const float lg = e < E ? __uint_as_float((uint32_t)w[j]) : 0.f;
+        score[j] = 1.0f / (1.0f + expf(-lg));
+        key[j] = e < E ? order_key(score[j] + bias[j]) : 0u;  // 0: below every float's key
+        id[j] = e < E ? (uint32_t)e : 0xffffffffu;
     }
     if (lane == 0) GP_STAMP(13);
     float denom = 1e-20f, my_s = 0.f;
     int my_e = 0;
-    for (int k = 0; k < K; ++k) {
-        int eb;
-        if (a.forced) {
-            eb = a.forced[k];
+    if (a.forced) {
+        for (int k = 0; k < K; ++k) {
+            int eb = a.forced[k];
             if (eb < 0 || eb >= E) {
                 if (lane == 0) atomicOr(a.status, GP_DEV_BAD_EXPERT);
                 eb = 0;
             }
-        } else {
-            uint32_t bk = 0;
-            int bj = 0;
+            float sc = 0.f;
 #pragma unroll
             for (int j = 0; j < EJ; ++j)
-                if (key[j] > bk) { bk = key[j]; bj = j; }  // strict: the lowest id of the lane on ties
-            const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
-            eb = (int)__reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
+                if (lane + 32 * j == eb) sc = score[j];
+            sc = __shfl_sync(0xffffffffu, sc, eb & 31);
+            denom += sc;  // model.cpp:718-721 order
+            if (lane == k) { my_s = sc; my_e = eb; }
         }
-        float sc = 0.f;
+    } else {
+        // odd-even transposition sort of the lane's candidates (EJ passes)
 #pragma unroll
-        for (int j = 0; j < EJ; ++j)
-            if (lane + 32 * j == eb) { sc = score[j]; key[j] = 0u; }
-        sc = __shfl_sync(0xffffffffu, sc, eb & 31);
-        denom += sc;  // model.cpp:718-721 order
-        if (lane == k) { my_s = sc; my_e = eb; }
+        for (int pass = 0; pass < EJ; ++pass) {
+#pragma unroll
+            for (int j = pass & 1; j + 1 < EJ; j += 2) {
+                const bool sw = key[j + 1] > key[j] || (key[j + 1] == key[j] && id[j + 1] < id[j]);
+                const uint32_t k0 = key[j], i0 = id[j];
+                const float s0 = score[j];
+                key[j] = sw ? key[j + 1] : k0;
+                key[j + 1] = sw ? k0 : key[j + 1];
+                id[j] = sw ? id[j + 1] : i0;
+                id[j + 1] = sw ? i0 : id[j + 1];
+                score[j] = sw ? score[j + 1] : s0;
+                score[j + 1] = sw ? s0 : score[j + 1];
+            }
+        }
+        for (int k = 0; k < K; ++k) {
+            const uint32_t m = __reduce_max_sync(0xffffffffu, key[0]);
+            const uint32_t eb = __reduce_min_sync(0xffffffffu, key[0] == m ? id[0] : 0xffffffffu);
+            const float sc = __shfl_sync(0xffffffffu, score[0], eb & 31);
+            if (id[0] == eb) {  // pop the head
+#pragma unroll
+                for (int j = 0; j + 1 < EJ; ++j) {
+                    key[j] = key[j + 1];
+                    id[j] = id[j + 1];
+                    score[j] = score[j + 1];
+                }
+                key[EJ - 1] = 0u;
+                id[EJ - 1] = 0xffffffffu;
+            }
+            denom += sc;  // model.cpp:718-721 order
+            if (lane == k) { my_s = sc; my_e = (int)eb; }
+        }
     }
     if (lane < K) {
         const float w = a.norm_topk ? (my_s / denom) * a.routed_scale : my_s * a.routed_scale;
@@ -252,21 +303,59 @@ GP_DEVINL Item item_of(int i, int per_slot, int K) {
 // Items i = c, c+G, c+2G, ... below total.
 GP_DEVINL int items_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
 
-// Down work: CTA c owns the range [v0, v1) of (row tile, slot order q) pairs,
-// v = tile*(K+1) + q, slot order q = 0 the shared expert, q >= 1 routed slot
-// q-1.  The range is walked from its first tile boundary, the leading partial
-// tile (late slots) last.
+// Down work: positions v = tile*(K+1) + q over (row tile, slot position q);
+// position q = K is the shared expert (ready first), q < K routed slot K-1-q
+// (slot 0 at q = K-1 is ready next, slot K-1 at q = 0 last).  CTA c owns the
+// range [v0, v1), sized so that its down work plus its routed gate/up units
+// is the same for every CTA (weights: one unit ~ wu, one down tile ~ wd).
+// The range is walked as: the leading partial tile, the first whole tile,
+// the trailing partial tile, the other whole tiles; each tile in descending
+// q.  Partial tiles thus meet the early-ready slots first, the tiles shared
+// with a neighbour CTA are settled early, and the CTA ends on a whole tile
+// it combines by itself.
+GP_DEVINL int down_slot(int q, int K) { return q == K ? K : K - 1 - q; }
 struct DownRange {
-    int v0, v1, b;
+    int v0, v1, b, e, P;  // range, first / last tile boundary inside it, K+1
     GP_DEVINL int count() const { return v1 - v0; }
-    GP_DEVINL int at(int i) const { return b + i < v1 ? b + i : v0 + (b + i - v1); }
+    GP_DEVINL int at(int i) const {
+        const int lead_end = b < v1 ? b : v1;
+        if (i < lead_end - v0) return lead_end - 1 - i;
+        i -= lead_end - v0;
+        const int nf = e > b ? (e - b) / P : 0;
+        if (nf > 0) {
+            if (i < P) return b + P - 1 - i;
+            i -= P;
+        }
+        const int n_trail = (e >= b && e < v1) ? v1 - e : 0;
+        if (i < n_trail) return v1 - 1 - i;
+        i -= n_trail;
+        const int f = 1 + i / P;
+        return b + f * P + P - 1 - (i - (f - 1) * P);
+    }
 };
-GP_DEVINL DownRange down_range(int c, int G, int total, int per_tile) {
+GP_DEVINL int prefix_rr(int c, int G, int total) {  // sum of items_of(c', G, total) over c' < c
+    return (total / G) * c + (c < total % G ? c : total % G);
+}
+GP_DEVINL DownRange down_range(int c, int G, int n_tiles, int P, int units, int shared_units) {
+    // 32-bit arithmetic: G * W < 2^31 for the supported shapes (host-checked)
+    constexpr int wu = 42, wd = 10;  // measured cost: a gate/up unit ~ 4.2 down tiles
+    const int routed = units - shared_units, total = n_tiles * P;
+    const int W = routed * wu + total * wd;
+    const int max_units = (units + G - 1) / G;
+    const bool weighted = max_units * wu * G <= W;  // every CTA still gets >= 0 down tiles
+    auto start = [&](int cc) -> int {
+        if (!weighted) return total * cc / G;
+        const int eff = prefix_rr(cc, G, units) - prefix_rr(cc, G, shared_units);
+        return (cc * W - G * eff * wu) / (G * wd);
+    };
     DownRange r;
-    r.v0 = (int)((int64_t)total * c / G);
-    r.v1 = (int)((int64_t)total * (c + 1) / G);
-    const int b = (r.v0 + per_tile - 1) / per_tile * per_tile;
-    r.b = b < r.v1 ? b : r.v0;
+    r.P = P;
+    r.v0 = start(c);
+    r.v1 = c + 1 == G ? (int)total : start(c + 1);
+    r.b = (r.v0 + P - 1) / P * P;
+    r.e = r.v1 / P * P;
+    if (r.b > r.v1) r.b = r.v1;
+    if (r.e < r.b) r.e = r.b;
     return r;
 }
 
@@ -309,12 +398,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     int* s_ids = reinterpret_cast<int*>(smem + L.misc_off + 16u);
     float* s_w = reinterpret_cast<float*>(s_ids + 32);
     float* s_slice = s_w + 32;
+    float* s_dv = s_slice + kMaxOwned * RSPLIT;
     float* partial = reinterpret_cast<float*>(smem + L.partial_off);
     constexpr uint32_t pstride = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC);
     const uint32_t stage0 = sbase + L.stages_off;
     const int n_gu = TPU * items_of(c, G, NU * (K + 1));
     const int n_shared = TPU * items_of(c, G, NU);  // leading gate/up tiles that need no routing
-    const DownRange R = down_range(c, G, TD * (K + 1), K + 1);
+    const DownRange R = down_range(c, G, TD, K + 1, NU * (K + 1), NU);
     const int n_items = n_gu + R.count();
     const int n_own = items_of(c, G, E);            // router experts c, c+G, ...
     const int n_tasks = n_own * RSPLIT;
@@ -358,8 +448,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 off = (uint32_t)(u.idx * TPU + it % TPU) * GU_BYTES;
                 b0 = b1 = GU_BYTES;
             } else {
-                const int v = R.at(it - n_gu), q = v % (K + 1);
-                slot = q == 0 ? K : q - 1;
+                const int v = R.at(it - n_gu);
+                slot = down_slot(v % (K + 1), K);
                 off = (uint32_t)(v / (K + 1)) * DN_BYTES;
                 b0 = DN_BYTES;
                 b1 = HQ_BYTES;
@@ -430,31 +520,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
 #pragma unroll
         for (int j = 0; j < EJ; ++j) bias[j] = a.corr && lane + 32 * j < E ? __ldg(a.corr + lane + 32 * j) : 0.f;
         pdl_wait();
+        const uint32_t tag = ld_relaxed(a.sync + kSyncGen) + 1u;
         if (n_tasks > 0) {  // this CTA's experts: slices added in order
             if (!mbar_wait(rbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (lane < n_own) {
                 float lg = 0.f;
 #pragma unroll
                 for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[lane * RSPLIT + sl];
-                a.rpart[c + lane * G] = lg;
+                st_relaxed64(a.logits + c + lane * G, ((unsigned long long)tag << 32) | __float_as_uint(lg));
             }
-            __syncwarp();
-            if (lane == 0) red_release_add(a.sync + kSyncRouter, (unsigned)n_own);
         }
-        if (lane == 0) {
-            GP_STAMP(1);
-            if (!wait_geq(a.sync + kSyncRouter, (unsigned)E)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            GP_STAMP(11);
-        }
-        __syncwarp();
-        fence_acq_rel_gpu();
-        topk_warp(a, bias, lane, c, s_ids, s_w, topk_bar);
+        if (lane == 0) GP_STAMP(1);
+        if (E <= 160) topk_warp<5>(a, bias, tag, lane, c, s_ids, s_w, topk_bar, s_abort);
+        else topk_warp<kMaxEFused / 32>(a, bias, tag, lane, c, s_ids, s_w, topk_bar, s_abort);
         if (lane == 0) GP_STAMP(2);
 
         int s = 0;
         uint32_t ph = 0;
         constexpr int rsg = 32 * NWG / (H / 32), rsd = 32 * NWC / (I / 32);
-        float hv = 0.f, acc = 0.f, d_sh = 0.f;
+        float hv = 0.f;
         for (int it = 0; it < n_items; ++it) {
             const bool gu = it < n_gu;
             if (!*s_abort && !mbar_wait(pdone0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
@@ -490,21 +574,26 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     if (lane == 0) red_release_add(a.sync + kSyncSlot + u.slot, 1);
                 }
             } else if (!*s_abort) {
-                const int v = R.at(it - n_gu), t = v / (K + 1), q = v % (K + 1);
-                const int slot = q == 0 ? K : q - 1;
+                const int v = R.at(it - n_gu), t = v / (K + 1);
+                const int slot = down_slot(v % (K + 1), K);
                 const int j = t * TRD + lane;
                 const int tb = t * (K + 1), te = tb + K + 1;
+                const int mine_lo = tb > R.v0 ? tb : R.v0, mine_hi = te < R.v1 ? te : R.v1;
                 if (tb >= R.v0 && te <= R.v1) {
-                    // whole row tile in this CTA, slots in order: y directly
-                    if (q == 0) { d_sh = val; acc = 0.f; }
-                    else acc = fmaf(s_w[q - 1], val, acc);
-                    if (q == K) a.y[j] = acc + d_sh;
+                    // whole row tile in this CTA: y once its last position (q = 0) is in
+                    s_dv[slot * 32 + lane] = val;
+                    if (v == tb) {
+                        __syncwarp();
+                        float y = 0.f;
+                        for (int k = 0; k < K; ++k) y = fmaf(s_w[k], s_dv[k * 32 + lane], y);
+                        a.y[j] = y + s_dv[K * 32 + lane];
+                        __syncwarp();
+                    }
                 } else {
-                    // tile split between CTAs: D in global memory, the last adder writes y
+                    // tile shared with a neighbour: D in global memory, the last adder writes y
                     a.D[(int64_t)slot * H + j] = val;
-                    const int mine_end = te < R.v1 ? te : R.v1;
-                    if (v == mine_end - 1) {
-                        const int mine = mine_end - (tb > R.v0 ? tb : R.v0);
+                    if (v == mine_lo) {
+                        const int mine = mine_hi - mine_lo;
                         unsigned* dcnt = a.sync + kSyncTile + t;
                         __syncwarp();
                         unsigned done = 0;
@@ -620,7 +709,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         GP_STAMP(8);
         fence_acq_rel_gpu();
         if (atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1) {
-            a.sync[kSyncRouter] = 0;
+            a.sync[kSyncGen] += 1u;
             for (int k = 0; k <= K; ++k) a.sync[kSyncSlot + k] = 0;
             fence_acq_rel_gpu();
             a.sync[kSyncEnd] = 0;
@@ -643,11 +732,13 @@ size_t decode_layer_smem(int H, int I, int stages) { return decode_smem(H, I, st
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st) {
     if (!decode_layer_supported(a.H, a.I, a.E, a.K, a.with_shared)) return cudaErrorInvalidValue;
     if (grid * kMaxOwned < a.E) return cudaErrorInvalidValue;  // router experts per CTA
+    // down-range weights in 32-bit: grid * (units * 42 + tiles * 10) < 2^31
+    if ((int64_t)grid * ((int64_t)(a.I / UNIT) * (a.K + 1) * 42 + (int64_t)(a.H / TRD) * (a.K + 1) * 10) >= (1ll << 31))
+        return cudaErrorInvalidValue;
     const Smem L = decode_smem(a.H, a.I, a.stages);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
     auto kern = decode_layer_kernel<5120, 1536, 4, 1, 2, 2>;
     static int configured = 0;
-    static bool pdl_ok = true;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
@@ -658,21 +749,24 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
     cfg.blockDim = dim3(NTHREADS);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl_ok ? 2 : 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
-    if (e != cudaSuccess && pdl_ok) {
-        // a driver that refuses the pair: launch without the early start
-        (void)cudaGetLastError();
-        pdl_ok = false;
-        cfg.numAttrs = 1;
-        e = cudaLaunchKernelEx(&cfg, kern, a);
+    // One CTA per SM, all resident at once.  The default launch lets this
+    // grid's CTAs take SMs as the previous kernel's leave (programmatic
+    // dependent launch), which hides the launch gap between layers; it relies
+    // on no other kernel holding SMs meanwhile (a concurrent kernel only
+    // delays the waits, which are bounded).  A cooperative launch guarantees
+    // co-residency instead, but the driver then starts the grid only after
+    // the previous kernel has finished.
+    cudaLaunchAttribute attr[1];
+    if (a.cooperative) {
+        attr[0].id = cudaLaunchAttributeCooperative;
+        attr[0].val.cooperative = 1;
+    } else {
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
     }
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
     return e;
 }
 

@@ -111,7 +111,7 @@ struct CombineArgs {
 };
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl);
 
-// One MoE layer at batch 1 in one cooperative persistent kernel (decode_layer.cu).
+// One MoE layer at batch 1 in one persistent kernel, one CTA per SM (decode_layer.cu).
 struct DecodeLayerArgs {
     const float* router;       // [E][H] fp32
     const float* corr;         // [E] or nullptr
@@ -130,7 +130,7 @@ struct DecodeLayerArgs {
     const int* forced;         // [K] or nullptr
     int* topk_ids;             // [K] or nullptr
     float* topk_w;             // [K] or nullptr
-    float* rpart;              // [8][E] router slice sums
+    unsigned long long* logits;  // [E] router logits tagged with the launch generation
     float* h;                  // [K+1][I]
     uint8_t* hq;               // [K+1][decode_layer_hq_bytes(I)] h quantised per 32-unit
     float* D;                  // [K+1][H]
@@ -138,10 +138,11 @@ struct DecodeLayerArgs {
     const uint8_t* tables;
     uint32_t* status;
     int stages;
+    int cooperative;           // 1: cooperative launch instead of programmatic dependent launch
 };
 // Counter words of the persistent kernel (all zero between launches; the host
 // clears them after a launch that reported an error).
-constexpr int kSyncRouter = 0;                  // CTAs done with their router slices
+constexpr int kSyncGen = 0;                     // launch generation (tags the exchanged logits)
 constexpr int kSyncEnd = 1;                     // CTAs finished
 constexpr int kSyncSlot = 8;                    // [K+1] h units quantised per slot
 constexpr int kSyncUnit = 64;                   // [K+1][64] gate/up tiles done per h unit

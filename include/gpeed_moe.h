@@ -87,6 +87,13 @@ GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
  * compiled variant; 0 forces the multi-kernel path (same results within
  * rounding).  No counterpart in the reference. */
 #define GPEED_OPT_FUSED_DECODE 1
+/* GPEED_OPT_FUSED_COOPERATIVE (default 0): launch that persistent kernel
+ * cooperatively.  By default its CTAs start as the previous kernel's CTAs
+ * leave the SMs (programmatic dependent launch), which assumes no other
+ * kernel occupies SMs at the same time; a cooperative launch guarantees
+ * co-residency at the cost of the launch gap.  Either way every wait inside
+ * is bounded and a timeout is reported by gpeed_ctx_check. */
+#define GPEED_OPT_FUSED_COOPERATIVE 2
 GPEED_API int gpeed_ctx_set_option(gpeed_ctx* ctx, int option, int value);
 
 /* Per-stage timing of gpeed_moe_forward (no counterpart in the reference;
