@@ -92,7 +92,7 @@ struct gpeed_ctx {
     // batch-1 forward in one persistent kernel when the shape has a variant
     bool fused_decode = true;
     bool fused_cooperative = false;
-    DevBuf<unsigned long long> logits;
+    DevBuf<unsigned long long> logits, dx;
     DevBuf<uint8_t> hq;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
@@ -313,6 +313,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
     c->logits.release();
+    c->dx.release();
     c->hq.release();
     cudaFree(c->sync);
     cudaFree(c->tables);
@@ -334,6 +335,7 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
         // tags restart together
         GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));
         if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
+        if (c->dx.p) GP_CUDA(cudaMemset(c->dx.p, 0, c->dx.n * sizeof(unsigned long long)));
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape)", st);
     }
@@ -549,6 +551,9 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         if ((rc = c->logits.ensure((size_t)E))) return rc;
         if (c->logits.n != had)  // tags must start below the first launch's
             GP_CUDA(cudaMemsetAsync(c->logits.p, 0, c->logits.n * sizeof(unsigned long long), st));
+        const size_t had_dx = c->dx.n;
+        if ((rc = c->dx.ensure((size_t)(K + 1) * H))) return rc;
+        if (c->dx.n != had_dx) GP_CUDA(cudaMemsetAsync(c->dx.p, 0, c->dx.n * sizeof(unsigned long long), st));
         if ((rc = c->hq.ensure((size_t)(K + 1) * gp::decode_layer_hq_bytes(I)))) return rc;
         gp::DecodeLayerArgs da{};
         da.router = L.router;
@@ -573,6 +578,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         da.topk_ids = topk_ids;
         da.topk_w = topk_w;
         da.logits = c->logits.p;
+        da.dx = c->dx.p;
         da.h = c->h.p;
         da.hq = c->hq.p;
         da.D = c->D.p;

@@ -1,4 +1,4 @@
-// One MoE layer at batch 1 in a single persistent, cooperative kernel
+// One MoE layer at batch 1 in a single persistent kernel
 // (reference Model::moe_forward, cpp/core/src/model.cpp:692-756).
 //
 // Separate kernels for router, routing, gate/up, down and combine each pay a
@@ -7,16 +7,19 @@
 // SM runs the whole layer.  Warp roles: 24 compute warps, one TMA producer
 // warp streaming weight tiles through a ring of shared-memory stages, and one
 // epilogue warp that does the routing and turns each stage's partial sums
-// into results.  Under full HBM load a round trip to L2 costs microseconds,
-// so the layout keeps those out of the per-tile path:
+// into results.  Under full HBM load a round trip to L2 costs microseconds
+// (more from the other die), so the design keeps those out of the per-tile
+// path: no atomics are read back, and values other CTAs produced are read as
+// words tagged with the launch generation (the data is its own flag).
 //
 //   router   CTA c owns experts c, c+G, ...; 8 warps each compute one 1/8
 //            slice of an owned expert's fp32 logit (weights prefetched before
-//            the wait on the previous kernel), the epilogue warp adds the
-//            slices in order, stores the logit and bumps one counter per CTA
-//   top-k    every CTA's epilogue warp loads the E logits, applies sigmoid +
-//            bias and picks top-K by warp reductions (ties to the lower id),
-//            weights score/(1e-20 + sum)*scale (model.cpp:704-725)
+//            the wait on the previous kernel); the epilogue warp adds the
+//            slices in order and stores the logit tagged with the launch
+//            generation, so readers poll the data itself
+//   top-k    every CTA's epilogue warp polls the E tagged logits, applies
+//            sigmoid + bias and picks top-K by warp reductions (ties to the
+//            lower id), weights score/(1e-20 + sum)*scale (model.cpp:704-725)
 //   gate/up  units of 32 rows of h, dealt round-robin in slot order (the
 //            shared expert, storage slot K, first: it needs no routing; then
 //            routed slots 0..K-1); a unit is 4 consecutive tiles of 8 rows of
@@ -24,19 +27,19 @@
 //            (model.cpp:733-739), quantises the finished unit to int16 (hq)
 //            and counts it for its slot: no value of h leaves the CTA
 //            unquantised and no counter is read back
-//   down     tiles of 32 rows x (K+1) slots in tile-major order (shared slot
-//            first), a contiguous range per CTA; the producer copies each tile
-//            with its slot's hq once all units of that slot are counted
-//            (model.cpp:740).  The epilogue accumulates y = sum_k w_k D[k] +
-//            D[shared] for a whole row tile in top-k order (model.cpp:741-755);
-//            only tiles split between CTAs go through D in global memory and a
-//            counter whose last adder writes y
+//   down     tiles of 32 rows x (K+1) slots, a contiguous range of (tile,
+//            slot) positions per CTA sized to even out the total work; the
+//            producer copies each tile with its slot's hq once all units of
+//            that slot are counted (model.cpp:740).  The epilogue keeps a row
+//            tile's slot results in shared memory and writes y = sum_k w_k
+//            D[k] + D[shared] in top-k order (model.cpp:741-755); for a tile
+//            shared with the next CTAs it reads their slots as tagged words
 //
-// Counters are reset by their last user, so they are zero between launches.
-// Waits on other CTAs need every CTA resident: the kernel is launched
-// cooperatively with one CTA per SM.  Every wait is bounded; a timeout sets a
-// status bit, the CTA stops waiting and finishes (results then invalid, the
-// host reports the status and clears the counters).
+// Waits on other CTAs need every CTA resident: one CTA per SM, launched either
+// with programmatic dependent launch (default) or cooperatively.  Every wait
+// is bounded; a timeout sets a status bit, the CTA stops waiting and finishes
+// (results then invalid, the host reports the status and clears the
+// counters and tags).
 #include <cuda_fp16.h>
 
 #include "expert_common.cuh"
@@ -64,7 +67,6 @@ constexpr int RSPLIT = 8;        // router slices per expert
 constexpr int MAXK = 31;         // K+1 slots fit one warp
 constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
 constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
-constexpr int kMaxUnits = 64;
 static_assert(TRD == 32, "the combine maps one row of a down tile to each epilogue lane");
 
 struct Smem {
@@ -337,16 +339,18 @@ GP_DEVINL int prefix_rr(int c, int G, int total) {  // sum of items_of(c', G, to
     return (total / G) * c + (c < total % G ? c : total % G);
 }
 GP_DEVINL DownRange down_range(int c, int G, int n_tiles, int P, int units, int shared_units) {
-    // 32-bit arithmetic: G * W < 2^31 for the supported shapes (host-checked)
-    constexpr int wu = 42, wd = 10;  // measured cost: a gate/up unit ~ 4.2 down tiles
+    // measured costs: a routed gate/up unit ~ 4.4 down positions; a shared
+    // unit mostly overlaps the routing, ~0.4 of a routed one.  32-bit
+    // arithmetic: G * W < 2^31 for the supported shapes (host-checked).
+    constexpr int wu = 44, ws = 17, wd = 10;
     const int routed = units - shared_units, total = n_tiles * P;
-    const int W = routed * wu + total * wd;
+    const int W = routed * wu + shared_units * ws + total * wd;
     const int max_units = (units + G - 1) / G;
-    const bool weighted = max_units * wu * G <= W;  // every CTA still gets >= 0 down tiles
+    const bool weighted = max_units * wu * G <= W;  // every CTA still gets >= 0 down positions
     auto start = [&](int cc) -> int {
         if (!weighted) return total * cc / G;
-        const int eff = prefix_rr(cc, G, units) - prefix_rr(cc, G, shared_units);
-        return (cc * W - G * eff * wu) / (G * wd);
+        const int sh = prefix_rr(cc, G, shared_units), all = prefix_rr(cc, G, units);
+        return (cc * W - G * ((all - sh) * wu + sh * ws)) / (G * wd);
     };
     DownRange r;
     r.P = P;
@@ -384,7 +388,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     constexpr int TD = H / TRD, NU = I / UNIT;
     constexpr uint32_t GU_BYTES = TRG * 98u * (H / 256), DN_BYTES = TRD * 98u * (I / 256);
     constexpr uint32_t HQ_BYTES = I * 2u + NU * 4u;
-    static_assert(NU <= kMaxUnits && TD <= kDecodeSyncWords - kSyncTile, "counter block too small");
+    static_assert(MAXK + 1 <= kDecodeSyncWords - kSyncSlot, "counter block too small");
     static_assert(UNIT % TRG == 0 && HQ_BYTES % 16 == 0 && DN_BYTES % 16 == 0 && GU_BYTES % 16 == 0,
                   "bulk copies need 16-byte sizes and offsets");
     const int E = a.E, K = a.K, S = a.stages;
@@ -578,11 +582,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 const int slot = down_slot(v % (K + 1), K);
                 const int j = t * TRD + lane;
                 const int tb = t * (K + 1), te = tb + K + 1;
-                const int mine_lo = tb > R.v0 ? tb : R.v0, mine_hi = te < R.v1 ? te : R.v1;
-                if (tb >= R.v0 && te <= R.v1) {
-                    // whole row tile in this CTA: y once its last position (q = 0) is in
+                if (tb >= R.v0) {
+                    // this CTA holds the tile's last walked position (q = 0): it
+                    // writes y, with the slots other CTAs computed (positions
+                    // [v1, te), walked early by them) read as tagged words
                     s_dv[slot * 32 + lane] = val;
                     if (v == tb) {
+                        if (te > R.v1) {
+                            uint32_t n = 0;
+                            for (; n < GP_SPIN_LIMIT; ++n) {
+                                bool ok = true;
+                                for (int base = R.v1; base < te; base += 8) {  // 8 loads in flight
+                                    unsigned long long w[8];
+#pragma unroll
+                                    for (int i = 0; i < 8; ++i)
+                                        w[i] = base + i < te ? ld_relaxed64(a.dx + (int64_t)down_slot(base + i - tb, K) * H + j)
+                                                             : (unsigned long long)tag << 32;
+#pragma unroll
+                                    for (int i = 0; i < 8; ++i) {
+                                        ok &= (uint32_t)(w[i] >> 32) == tag;
+                                        if (base + i < te) s_dv[down_slot(base + i - tb, K) * 32 + lane] = __uint_as_float((uint32_t)w[i]);
+                                    }
+                                }
+                                if (__all_sync(0xffffffffu, ok)) break;
+                                __nanosleep(64);
+                            }
+                            if (n == GP_SPIN_LIMIT && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                        }
                         __syncwarp();
                         float y = 0.f;
                         for (int k = 0; k < K; ++k) y = fmaf(s_w[k], s_dv[k * 32 + lane], y);
@@ -590,22 +616,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                         __syncwarp();
                     }
                 } else {
-                    // tile shared with a neighbour: D in global memory, the last adder writes y
-                    a.D[(int64_t)slot * H + j] = val;
-                    if (v == mine_lo) {
-                        const int mine = mine_hi - mine_lo;
-                        unsigned* dcnt = a.sync + kSyncTile + t;
-                        __syncwarp();
-                        unsigned done = 0;
-                        if (lane == 0) done = atom_add_acq_rel(dcnt, (unsigned)mine) + mine == (unsigned)(K + 1);
-                        if (__shfl_sync(0xffffffffu, done, 0)) {
-                            fence_acq_rel_gpu();
-                            float y = 0.f;
-                            for (int k = 0; k < K; ++k) y = fmaf(s_w[k], __ldcg(a.D + (int64_t)k * H + j), y);
-                            a.y[j] = y + __ldcg(a.D + (int64_t)K * H + j);
-                            if (lane == 0) *dcnt = 0;
-                        }
-                    }
+                    // the CTA before this one finishes the tile
+                    st_relaxed64(a.dx + (int64_t)slot * H + j, ((unsigned long long)tag << 32) | __float_as_uint(val));
                 }
             }
         }

@@ -133,21 +133,21 @@ struct DecodeLayerArgs {
     unsigned long long* logits;  // [E] router logits tagged with the launch generation
     float* h;                  // [K+1][I]
     uint8_t* hq;               // [K+1][decode_layer_hq_bytes(I)] h quantised per 32-unit
-    float* D;                  // [K+1][H]
+    float* D;                  // [K+1][H] (multi-kernel path)
+    unsigned long long* dx;    // [K+1][H] down rows of tiles split between CTAs, tagged like logits
     unsigned* sync;            // [kDecodeSyncWords] counters, zero between launches
     const uint8_t* tables;
     uint32_t* status;
     int stages;
     int cooperative;           // 1: cooperative launch instead of programmatic dependent launch
 };
-// Counter words of the persistent kernel (all zero between launches; the host
-// clears them after a launch that reported an error).
-constexpr int kSyncGen = 0;                     // launch generation (tags the exchanged logits)
+// Counter words of the persistent kernel: the generation counts launches, the
+// others are zero between launches; the host clears all of them (and the
+// tagged buffers) after a launch that reported an error.
+constexpr int kSyncGen = 0;                     // launch generation (tags exchanged logits and rows)
 constexpr int kSyncEnd = 1;                     // CTAs finished
 constexpr int kSyncSlot = 8;                    // [K+1] h units quantised per slot
-constexpr int kSyncUnit = 64;                   // [K+1][64] gate/up tiles done per h unit
-constexpr int kSyncTile = kSyncUnit + 33 * 64;  // [H/32] down slots done per row tile
-constexpr int kDecodeSyncWords = 4096;
+constexpr int kDecodeSyncWords = 64;
 // h[slot] as int16 pairs (I*2 bytes) followed by one fp32 scale per 32-unit.
 inline size_t decode_layer_hq_bytes(int I) { return (size_t)I * 2 + (size_t)(I / 32) * 4; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
