@@ -82,6 +82,9 @@ GP_DEVINL void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
 GP_DEVINL void mbar_arrive(uint32_t bar) {
     asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
+GP_DEVINL void mbar_arrive_cnt(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
 GP_DEVINL bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -96,6 +99,16 @@ GP_DEVINL bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 GP_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity) {
     for (uint32_t i = 0; i < GP_SPIN_LIMIT; ++i)
         if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// Bounded wait for a phase expected to take long: sleeps between polls so the
+// waiting warp leaves the issue slots to the others.
+GP_DEVINL bool mbar_wait_sleepy(uint32_t bar, uint32_t parity) {
+    for (uint32_t i = 0; i < GP_SPIN_LIMIT; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        __nanosleep(256);
+    }
     return false;
 }
 

@@ -82,7 +82,7 @@ __host__ __device__ inline Smem decode_smem(int H, int I, int S) {
     L.partial_off = L.stages_off + S * L.stage_bytes;
     const uint32_t pb = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC) * 4u;
     L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
-    L.misc_off = L.bar_off + (3u * S + 3u) * 8u;
+    L.misc_off = L.bar_off + (3u * S + 4u) * 8u;
     // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT],
     // one down row tile's per-slot values [MAXK + 1][32]
     L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT + 4u * (MAXK + 1) * 32u;
@@ -364,8 +364,10 @@ GP_DEVINL DownRange down_range(int c, int G, int n_tiles, int P, int units, int 
 }
 
 // Quantises the unit of h held one value per lane exactly as a lane quantises
-// its activations for the GEMV (quant_i16<32>, scale * 1/4), into hq: 16
-// int16-pair words at unit*64, the scale at 2*I + unit*4.
+// its activations for the GEMV (quant_i16<32>, scale * 1/4), into hq.  hq
+// layout: 4 planes of NU 16-byte chunks (plane i holds words 4i..4i+3 of every
+// unit, so a warp's 16-byte loads of consecutive units are conflict-free),
+// then the NU fp32 scales at 2*I.
 GP_DEVINL void quantise_unit(float v, uint8_t* hq, int I, int unit, int lane) {
     float amax = fabsf(v);
 #pragma unroll
@@ -373,8 +375,9 @@ GP_DEVINL void quantise_unit(float v, uint8_t* hq, int I, int unit, int lane) {
     const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
     const int q = __float2int_rn(v * inv);
     const int qn = __shfl_down_sync(0xffffffffu, q, 1);
+    const int w = lane >> 1;  // word of the unit
     if (!(lane & 1))
-        reinterpret_cast<uint32_t*>(hq)[unit * (UNIT / 2) + (lane >> 1)] =
+        *reinterpret_cast<uint32_t*>(hq + (w >> 2) * (I / UNIT) * 16 + unit * 16 + (w & 3) * 4) =
             (static_cast<uint32_t>(q) & 0xFFFFu) | (static_cast<uint32_t>(qn) << 16);
     if (lane == 0) reinterpret_cast<float*>(hq + 2 * I)[unit] = 0.25f * (amax * (1.0f / 32767.0f));
 }
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     // per stage: full (producer -> compute warps), pdone (compute warps ->
     // epilogue warp: partial sums written), empty (epilogue -> producer)
     const uint32_t full0 = sbase + L.bar_off, pdone0 = full0 + 8u * S, empty0 = pdone0 + 8u * S;
-    const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u;
+    const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u, gbar = rbar + 8u;
     volatile uint32_t* s_abort = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off);
     int* s_ids = reinterpret_cast<int*>(smem + L.misc_off + 16u);
     float* s_w = reinterpret_cast<float*>(s_ids + 32);
@@ -425,6 +428,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         mbar_init(tbar, 1);
         mbar_init(topk_bar, 1);
         mbar_init(rbar, n_tasks > 0 ? n_tasks : 1);
+        mbar_init(gbar, 1);
         *s_abort = gp_tables_at_base(smem) ? 0u : 1u;
         if (*s_abort) atomicOr(a.status, GP_DEV_BAD_SHAPE);
         fence_mbar_init();
@@ -669,21 +673,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         if (!mbar_wait(tbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         int s = 0;
         uint32_t ph = 0;
-        // ---- gate/up tiles (warps >= NWG only keep the stage protocol) ----
-        {
-            const auto mg = lane_map<HH, NWG, PG>(warp < NWG ? warp : 0, lane, stage0);
+        // ---- gate/up tiles: warps 0..NWG-1; warp 0 also arrives for the
+        // others, which sleep until the down phase ----
+        if (warp < NWG) {
+            const auto mg = lane_map<HH, NWG, PG>(warp, lane, stage0);
             uint32_t xq[16];
-            float sx4 = 0.f;
-            if (warp < NWG) sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
+            const float sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
             for (int it = 0; it < n_gu; ++it) {
                 if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 if (tid == 0 && it == n_shared) GP_STAMP(3);
-                if (!*s_abort && warp < NWG)
+                if (!*s_abort)
                     consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
                 __syncwarp();
-                if (lane == 0) mbar_arrive(pdone0 + 8u * s);
+                if (lane == 0) mbar_arrive_cnt(pdone0 + 8u * s, warp == 0 ? 1 + NWC - NWG : 1);
                 if (++s == S) { s = 0; ph ^= 1u; }
             }
+            if (warp == 0 && lane == 0) mbar_arrive(gbar);
+        } else {
+            // once warp 0 has passed every gate/up stage, the first down
+            // stage is at most one phase ahead of its parity wait
+            if (!mbar_wait_sleepy(gbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            s = n_gu % S;
+            ph = (uint32_t)(n_gu / S) & 1u;
         }
         if (tid == 0) GP_STAMP(4);
         // ---- down tiles: the activations come with the tile ----
@@ -697,7 +708,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     uint32_t xq[16];
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        const uint4 v = lds128(xb + md.sb * 64u + 16u * i);
+                        const uint4 v = lds128(xb + i * (NU * 16u) + md.sb * 16u);
                         xq[4 * i] = v.x;
                         xq[4 * i + 1] = v.y;
                         xq[4 * i + 2] = v.z;
