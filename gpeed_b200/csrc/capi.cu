@@ -585,7 +585,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         da.sync = c->sync;
         da.tables = c->tables;
         da.status = c->status;
-        da.stages = 4;
+        da.stages = 4;  // the deepest stage ring that fits next to the tables
+        while (gp::decode_layer_smem(H, I, da.stages + 1) <= 227u * 1024u && da.stages < 8) ++da.stages;
         da.cooperative = c->fused_cooperative;
         // profiling: the one kernel's time goes to the gate/up slot, the other
         // stages read 0

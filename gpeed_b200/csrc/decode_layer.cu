@@ -69,25 +69,6 @@ constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
 constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
 static_assert(TRD == 32, "the combine maps one row of a down tile to each epilogue lane");
 
-struct Smem {
-    uint32_t stage_bytes, stages_off, partial_off, bar_off, misc_off, total;
-};
-
-__host__ __device__ inline Smem decode_smem(int H, int I, int S) {
-    Smem L;
-    const uint32_t gu = 2u * TRG * 98u * (H / 256);
-    const uint32_t dn = TRD * 98u * (I / 256) + (uint32_t)I * 2u + (uint32_t)(I / UNIT) * 4u;
-    L.stage_bytes = ((gu > dn ? gu : dn) + 15u) & ~15u;
-    L.stages_off = GP_IQ3_TABLE_BYTES;
-    L.partial_off = L.stages_off + S * L.stage_bytes;
-    const uint32_t pb = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC) * 4u;
-    L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
-    L.misc_off = L.bar_off + (3u * S + 4u) * 8u;
-    // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT],
-    // one down row tile's per-slot values [MAXK + 1][32]
-    L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT + 4u * (MAXK + 1) * 32u;
-    return L;
-}
 
 GP_DEVINL unsigned long long ld_relaxed64(const unsigned long long* p) {
     unsigned long long v;
@@ -119,6 +100,14 @@ struct LaneMap {
     static_assert((32 * NW) % SB == 0, "lanes must tile whole rows");
     static_assert(ROWSTEP % 8 == 0 || (ROWSTEP < 8 && 8 % ROWSTEP == 0 && (8 / ROWSTEP) * ROWSTEP == 8),
                   "passes must keep a lane inside the same 8-row group pattern");
+    // warps whose lanes cover row r of a pass: first_warp(r) .. first_warp(r) + span - 1
+    static constexpr GP_DEVINL int first_warp(int r) { return r * SB / 32; }
+    static constexpr GP_DEVINL int last_warp(int r) { return (r * SB + SB - 1) / 32; }
+    static constexpr int max_span(int r = 0, int m = 0) {
+        return r == ROWSTEP ? m : max_span(r + 1, last_warp(r) - first_warp(r) + 1 > m ? last_warp(r) - first_warp(r) + 1 : m);
+    }
+    // partial sums per row: one slot per covering warp (row * WPR + warp - first_warp)
+    static constexpr int WPR = max_span();
     uint32_t q0, a0, d0;
     int sb, wrow0, wspan, jrow, row0;
     // byte offset of pass p relative to pass 0 for a stream with `stride` bytes per row in a group
@@ -182,7 +171,8 @@ GP_DEVINL void consume(const LaneMap<IN, NW, P>& m, uint32_t soff, const uint32_
     constexpr int kShift = 5 - ilog2(M);
     if ((lane & ((1 << kShift) - 1)) == 0) {
         const int idx = lane >> kShift, p = idx / RPW, j = idx % RPW;
-        if (j < m.wspan) pbuf[(m.wrow0 + j + p * LM::ROWSTEP) * NW + warp] = red;
+        const int r = m.wrow0 + j;  // row within the pass
+        if (j < m.wspan) pbuf[(r + p * LM::ROWSTEP) * LM::WPR + warp - LM::first_warp(r)] = red;
     }
 }
 
@@ -290,6 +280,31 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t t
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(topk_bar);  // release: the producer reads s_ids
+}
+
+// Per-stage partial sums: one per (row of the tile, covering warp).
+constexpr uint32_t kPartialFloats =
+    2 * TRG * LaneMap<5120, NWG, 4>::WPR > TRD * LaneMap<1536, NWC, 2>::WPR ? 2 * TRG * LaneMap<5120, NWG, 4>::WPR
+                                                                          : TRD * LaneMap<1536, NWC, 2>::WPR;
+
+struct Smem {
+    uint32_t stage_bytes, stages_off, partial_off, bar_off, misc_off, total;
+};
+
+__host__ __device__ inline Smem decode_smem(int H, int I, int S) {
+    Smem L;
+    const uint32_t gu = 2u * TRG * 98u * (H / 256);
+    const uint32_t dn = TRD * 98u * (I / 256) + (uint32_t)I * 2u + (uint32_t)(I / UNIT) * 4u;
+    L.stage_bytes = ((gu > dn ? gu : dn) + 15u) & ~15u;
+    L.stages_off = GP_IQ3_TABLE_BYTES;
+    L.partial_off = L.stages_off + S * L.stage_bytes;
+    const uint32_t pb = kPartialFloats * 4u;
+    L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
+    L.misc_off = L.bar_off + (3u * S + 4u) * 8u;
+    // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT],
+    // one down row tile's per-slot values [MAXK + 1][32]
+    L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT + 4u * (MAXK + 1) * 32u;
+    return L;
 }
 
 // Work item i of a phase in slot order: the shared expert (storage slot K)
@@ -407,7 +422,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     float* s_slice = s_w + 32;
     float* s_dv = s_slice + kMaxOwned * RSPLIT;
     float* partial = reinterpret_cast<float*>(smem + L.partial_off);
-    constexpr uint32_t pstride = (2 * TRG * NWG > TRD * NWC ? 2 * TRG * NWG : TRD * NWC);
+    constexpr uint32_t pstride = kPartialFloats;
     const uint32_t stage0 = sbase + L.stages_off;
     const int n_gu = TPU * items_of(c, G, NU * (K + 1));
     const int n_shared = TPU * items_of(c, G, NU);  // leading gate/up tiles that need no routing
@@ -475,7 +490,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                         if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                         break;
                     }
+                    // order the observed counts (and so the hq words they
+                    // release) before this warp's later bulk-copy reads; a
+                    // slot seen ready stays ready, so one fence per poll
                     fence_acq_rel_gpu();
+                    fence_proxy_async_global();
                     if (lane == 0 && it == n_gu) GP_STAMP(12);
                 }
             }
@@ -493,7 +512,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                         src0 = a.gate + eo;
                         src1 = a.up + eo;
                     } else {
-                        fence_proxy_async_global();
                         src0 = a.down + (int64_t)e * a.d_stride + off;
                         src1 = a.hq + (int64_t)slot * HQ_BYTES;
                     }
@@ -553,19 +571,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             const float* pbuf = partial + (size_t)s * pstride;
             float val = 0.f;
             if (gu) {
-                if (lane < TRG) {
+                if (lane < TRG) {  // partials in warp order (LaneMap layout)
+                    using LG = LaneMap<HH, NWG, PG>;
                     const int row = lane, ur = TRG + row;
-                    const int g0 = (row % rsg) * (H / 32) / 32, g1 = ((row % rsg + 1) * (H / 32) - 1) / 32;
-                    const int u0 = (ur % rsg) * (H / 32) / 32, u1 = ((ur % rsg + 1) * (H / 32) - 1) / 32;
+                    const int ng = LG::last_warp(row % rsg) - LG::first_warp(row % rsg);
+                    const int nu = LG::last_warp(ur % rsg) - LG::first_warp(ur % rsg);
                     float gs = 0.f, us = 0.f;
-                    for (int w = g0; w <= g1; ++w) gs += pbuf[row * NWG + w];
-                    for (int w = u0; w <= u1; ++w) us += pbuf[ur * NWG + w];
+                    for (int w = 0; w <= ng; ++w) gs += pbuf[row * LG::WPR + w];
+                    for (int w = 0; w <= nu; ++w) us += pbuf[ur * LG::WPR + w];
                     val = silu_clamped(gs, us, a.limit);
                 }
             } else {
+                using LD = LaneMap<II, NWC, PD>;
                 const int r0 = lane % rsd;
-                const int w0 = r0 * (I / 32) / 32, w1 = ((r0 + 1) * (I / 32) - 1) / 32;
-                for (int w = w0; w <= w1; ++w) val += pbuf[lane * NWC + w];
+                const int nw = LD::last_warp(r0) - LD::first_warp(r0);
+                for (int w = 0; w <= nw; ++w) val += pbuf[lane * LD::WPR + w];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty0 + 8u * s);  // partials read: the stage may refill

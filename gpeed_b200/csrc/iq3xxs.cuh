@@ -72,9 +72,10 @@ GP_DEVINL uint32_t tbl_grid(uint32_t off) {
 }
 GP_DEVINL uint32_t tbl_sel(uint32_t off) {
     uint32_t v;
-    asm("ld.shared.u32 %0, [%1+1152];" : "=r"(v) : "r"(off));  // words 32..63 of the row
+    asm("ld.shared.u32 %0, [%1+1152];" : "=r"(v) : "r"(off));  // words 32..63 of row k
     return v;
 }
+
 
 // Codebook word for the index in byte `m` of q (selector constant 0x55m4:
 // byte0 <- lane offset, byte1 <- index, bytes 2,3 <- 0 => index*256 + lane*4).
@@ -84,11 +85,17 @@ GP_DEVINL uint32_t iq3_grid(const uint8_t* tbl, uint32_t q, uint32_t lane4) {
     return tbl_grid(prmt(q, lane4, 0x5504u | (M << 4)));
 }
 
-// Selector word for the 7-bit sign field whose bits sit at positions 8..14 of f
-// (the caller shifts aux so the field lands there).
-GP_DEVINL uint32_t iq3_sel(const uint8_t* tbl, uint32_t f, uint32_t lane4) {
-    (void)tbl;
-    return tbl_sel((f & 0x7F00u) | lane4);
+// Table offset of the selectors for the 7-bit sign field at bits 8..14 of f
+// (the caller moves the field there).
+GP_DEVINL uint32_t iq3_sel_off(uint32_t f, uint32_t lane4) { return (f & 0x7F00u) | lane4; }
+
+// x >> n as a multiply-high, which issues on the FMA pipe instead of the
+// integer ALU pipe that the byte permutes and dot products saturate.
+template <int N>
+GP_DEVINL uint32_t shr_fma(uint32_t x) {
+    uint32_t r;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(1u << (32 - N)));
+    return r;
 }
 
 // Signed int8 weights for 4 positions: magnitudes g, selector sel (low 16 bits).
@@ -105,9 +112,9 @@ GP_DEVINL void iq3_group(const uint8_t* tbl, uint32_t q, uint32_t f, uint32_t la
                          uint32_t& s1) {
     const uint32_t g0 = iq3_grid<M>(tbl, q, lane4);
     const uint32_t g1 = iq3_grid<M + 1>(tbl, q, lane4);
-    const uint32_t sel = iq3_sel(tbl, f, lane4);
+    const uint32_t sel = tbl_sel(iq3_sel_off(f, lane4));
     s0 = iq3_apply_sign(g0, sel);
-    s1 = iq3_apply_sign(g1, sel >> 16);
+    s1 = iq3_apply_sign(g1, shr_fma<16>(sel));
 }
 
 // Full 32-weight sub-block: q0/q1 = its 8 index bytes, aux = its scale/sign
@@ -116,8 +123,8 @@ GP_DEVINL void iq3_decode_sub32(const uint8_t* tbl, uint32_t q0, uint32_t q1, ui
                                 uint32_t (&sw)[8]) {
     iq3_group<0>(tbl, q0, aux << 8, lane4, sw[0], sw[1]);
     iq3_group<2>(tbl, q0, aux << 1, lane4, sw[2], sw[3]);
-    iq3_group<0>(tbl, q1, aux >> 6, lane4, sw[4], sw[5]);
-    iq3_group<2>(tbl, q1, aux >> 13, lane4, sw[6], sw[7]);
+    iq3_group<0>(tbl, q1, shr_fma<6>(aux), lane4, sw[4], sw[5]);
+    iq3_group<2>(tbl, q1, shr_fma<13>(aux), lane4, sw[6], sw[7]);
 }
 
 // Half sub-block (16 weights, sign groups 2h and 2h+1): q = the 4 index bytes
@@ -144,7 +151,8 @@ GP_DEVINL float iq3_subscale(float d, uint32_t aux) {
     return d * (float)((aux >> 27) | 1u) * 0.25f;
 }
 // The odd factor 2s+1 of a sub-block; |isum * (2s+1)| < 2^31 for int16 activations.
-GP_DEVINL int iq3_oddscale(uint32_t aux) { return (int)((aux >> 27) | 1u); }
+// (2 * (aux >> 28) + 1, all on the FMA pipe.)
+GP_DEVINL int iq3_oddscale(uint32_t aux) { return (int)(shr_fma<28>(aux) * 2u + 1u); }
 
 // Quantises UNIT activations to int16 pairs; returns the scale sx (x ~= sx*q).
 template <int UNIT>
