@@ -52,6 +52,13 @@ SIGNATURES = {
     "gpeed_moe_synth_layer": [_vp, _i, ctypes.POINTER(MoeShape), _vp, _vp, _i, _u64, _u64],
     "gpeed_synth_iq3xxs": [_vp, _u64, _u64, _u64, _u64, _vp],
     "gpeed_moe_forward": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
+    "gpeed_moe_load_layer_range": [_vp, _i, ctypes.POINTER(MoeShape), _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                   _vp, _i],
+    "gpeed_moe_synth_layer_range": [_vp, _i, ctypes.POINTER(MoeShape), _i, _i, _vp, _vp, _i, _u64, _u64],
+    "gpeed_moe_route": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp],
+    "gpeed_ep_pack": [_vp, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
+    "gpeed_moe_experts": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp],
+    "gpeed_moe_combine": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],
 }
 _RESTYPES = {"gpeed_last_error": ctypes.c_char_p}
 

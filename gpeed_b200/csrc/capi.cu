@@ -51,6 +51,10 @@ struct Layer {
     uint8_t* up = nullptr;
     uint8_t* down = nullptr;  // (E + n_shared) experts x H rows of I
     int64_t gu_stride = 0, d_stride = 0;
+    // experts held here: routed [e_lo, e_lo + e_cnt) at local index e - e_lo,
+    // then the shared expert at local index e_cnt (all of them unless the
+    // layer was loaded for expert parallelism)
+    int e_lo = 0, e_cnt = 0;
 };
 
 template <typename T>
@@ -207,9 +211,9 @@ int check_shape(const gpeed_moe_shape* s) {
     return GPEED_OK;
 }
 
-int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
-                int on_device, Layer** out) {
-    const int H = s->hidden, I = s->inter, E = s->n_experts, NE = E + s->n_shared;
+int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int e_lo, int e_cnt, const float* router_w,
+                const float* corr, int on_device, Layer** out) {
+    const int H = s->hidden, I = s->inter, E = s->n_experts, NE = e_cnt + s->n_shared;
     auto it = c->layers.find(layer);
     if (it != c->layers.end()) {
         Layer& old = it->second;
@@ -218,6 +222,8 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* 
     }
     Layer L;
     L.shape = *s;
+    L.e_lo = e_lo;
+    L.e_cnt = e_cnt;
     L.gu_stride = gp::repacked_bytes(I, H);
     L.d_stride = gp::repacked_bytes(H, I);
     const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -250,6 +256,79 @@ int ensure_scratch(gpeed_ctx* c, int n, int E, int K, int H, int I) {
     if ((rc = c->nslots.ensure(1))) return rc;
     if ((rc = c->h.ensure(na * I))) return rc;
     if ((rc = c->D.ensure(na * H))) return rc;
+    return GPEED_OK;
+}
+
+// The batched path's expert work for n rows: route (or take the given top-k),
+// gate/up with SwiGLU, down, and the weighted combine into y.  `ro` holds the
+// routing inputs; the scratch and slot fields are filled in here.
+template <typename Mark>
+int expert_pass(gpeed_ctx* c, const Layer& L, const void* x, int x_bf16, gp::RouteArgs ro, int combine_shared,
+                const float* d_shared, float* y, cudaStream_t st, Mark&& mark) {
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, n = ro.n, K = ro.K;
+    int rc;
+    Geo ggu, gd;
+    // one slot list serves both expert kernels: its token count must suit both
+    const int nt = nt_for(n);
+    if ((rc = pick_geo(H, 2, nt, I, &ggu))) return rc;
+    if ((rc = pick_geo(I, 1, nt, H, &gd))) return rc;
+    ro.nt = nt;
+    ro.perm_tok = c->perm.p;
+    ro.inv_pos = c->inv_pos.p;
+    ro.counts = c->counts.p;
+    ro.slots = c->slots.p;
+    ro.max_slots = (int)c->slots.n;
+    ro.nslots = c->nslots.p;
+    ro.status = c->status;
+    GP_CUDA(gp::launch_route(ro, st, !c->prof));
+    mark(2);
+
+    gp::GemvArgs a{};
+    a.w0 = L.gate;
+    a.w1 = L.up;
+    a.expert_stride = L.gu_stride;
+    a.in_dim = H;
+    a.rows = I;
+    a.tile_rows = ggu.tile_rows;
+    a.nwarps = ggu.nwarps;
+    a.stages = ggu.stages;
+    a.slots = c->slots.p;
+    a.nslots = c->nslots.p;
+    a.perm_tok = c->perm.p;
+    a.x = x;
+    a.x_bf16 = x_bf16;
+    a.out = c->h.p;
+    a.limit = s.swiglu_limit;
+    a.tables = c->tables;
+    a.status = c->status;
+    if (I % a.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "inter %% %d != 0", a.tile_rows);
+    GP_CUDA(gp::launch_gemv(a, nt, true, ggu.passes, ggu.rpw, c->num_sms, st, !c->prof));
+    mark(3);
+
+    gp::GemvArgs d{};
+    d.w0 = L.down;
+    d.w1 = nullptr;
+    d.expert_stride = L.d_stride;
+    d.in_dim = I;
+    d.rows = H;
+    d.tile_rows = gd.tile_rows;
+    d.nwarps = gd.nwarps;
+    d.stages = gd.stages;
+    d.slots = c->slots.p;
+    d.nslots = c->nslots.p;
+    d.perm_tok = nullptr;
+    d.x = c->h.p;
+    d.x_bf16 = 0;
+    d.out = c->D.p;
+    d.tables = c->tables;
+    d.status = c->status;
+    if (H % d.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "hidden %% %d != 0", d.tile_rows);
+    GP_CUDA(gp::launch_gemv(d, nt, false, gd.passes, gd.rpw, c->num_sms, st, !c->prof));
+    mark(4);
+
+    gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, combine_shared, y, d_shared};
+    GP_CUDA(gp::launch_combine(cb, st, !c->prof));
     return GPEED_OK;
 }
 
@@ -474,55 +553,85 @@ int gpeed_matvec_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int 
     return gpeed_matmul_quant(c, handle, row0, in_dim, out_dim, x, 1, dst, stream);
 }
 
-int gpeed_moe_load_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
-                         const void* gate, const void* up, const void* down, const void* gate_sh, const void* up_sh,
-                         const void* down_sh, int on_device) {
+int gpeed_moe_load_layer_range(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int expert_begin, int expert_count,
+                               const float* router_w, const float* corr, const void* gate, const void* up,
+                               const void* down, const void* gate_sh, const void* up_sh, const void* down_sh,
+                               int on_device) {
     int rc;
     if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
     if ((rc = check_shape(s))) return rc;
-    if (!router_w || !gate || !up || !down) return fail(GPEED_ERR_INVALID, "NULL expert tensor");
+    if (expert_begin < 0 || expert_count < 0 || expert_begin + expert_count > s->n_experts)
+        return fail(GPEED_ERR_INVALID, "expert range [%d, %d) outside [0, %d)", expert_begin,
+                    expert_begin + expert_count, s->n_experts);
+    if (!router_w || (expert_count && (!gate || !up || !down))) return fail(GPEED_ERR_INVALID, "NULL expert tensor");
     if (s->n_shared && (!gate_sh || !up_sh || !down_sh)) return fail(GPEED_ERR_INVALID, "n_shared=1 needs the shared tensors");
     if ((rc = set_device(c))) return rc;
     Layer* L;
-    if ((rc = alloc_layer(c, layer, s, router_w, corr, on_device, &L))) return rc;
-    const int H = s->hidden, I = s->inter, E = s->n_experts;
-    if ((rc = upload_matrix(c, gate, on_device, (int64_t)E * I, H, L->gate, 0))) return rc;
-    if ((rc = upload_matrix(c, up, on_device, (int64_t)E * I, H, L->up, 0))) return rc;
-    if ((rc = upload_matrix(c, down, on_device, (int64_t)E * H, I, L->down, 0))) return rc;
+    if ((rc = alloc_layer(c, layer, s, expert_begin, expert_count, router_w, corr, on_device, &L))) return rc;
+    const int H = s->hidden, I = s->inter, EC = expert_count;
+    if (EC) {
+        if ((rc = upload_matrix(c, gate, on_device, (int64_t)EC * I, H, L->gate, 0))) return rc;
+        if ((rc = upload_matrix(c, up, on_device, (int64_t)EC * I, H, L->up, 0))) return rc;
+        if ((rc = upload_matrix(c, down, on_device, (int64_t)EC * H, I, L->down, 0))) return rc;
+    }
     if (s->n_shared) {
-        if ((rc = upload_matrix(c, gate_sh, on_device, I, H, L->gate + L->gu_stride * E, 0))) return rc;
-        if ((rc = upload_matrix(c, up_sh, on_device, I, H, L->up + L->gu_stride * E, 0))) return rc;
-        if ((rc = upload_matrix(c, down_sh, on_device, H, I, L->down + L->d_stride * E, 0))) return rc;
+        if ((rc = upload_matrix(c, gate_sh, on_device, I, H, L->gate + L->gu_stride * EC, 0))) return rc;
+        if ((rc = upload_matrix(c, up_sh, on_device, I, H, L->up + L->gu_stride * EC, 0))) return rc;
+        if ((rc = upload_matrix(c, down_sh, on_device, H, I, L->down + L->d_stride * EC, 0))) return rc;
     }
     GP_CUDA(cudaDeviceSynchronize());
     return GPEED_OK;
 }
 
-int gpeed_moe_synth_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
-                          int on_device, uint64_t seed, uint64_t stream0) {
+int gpeed_moe_load_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
+                         const void* gate, const void* up, const void* down, const void* gate_sh, const void* up_sh,
+                         const void* down_sh, int on_device) {
+    if (!s) return fail(GPEED_ERR_INVALID, "shape is NULL");
+    return gpeed_moe_load_layer_range(c, layer, s, 0, s->n_experts, router_w, corr, gate, up, down, gate_sh, up_sh,
+                                      down_sh, on_device);
+}
+
+int gpeed_moe_synth_layer_range(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int expert_begin,
+                                int expert_count, const float* router_w, const float* corr, int on_device,
+                                uint64_t seed, uint64_t stream0) {
     int rc;
     if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
     if ((rc = check_shape(s))) return rc;
     if (!router_w) return fail(GPEED_ERR_INVALID, "router_w is NULL");
+    if (expert_begin < 0 || expert_count < 0 || expert_begin + expert_count > s->n_experts)
+        return fail(GPEED_ERR_INVALID, "expert range [%d, %d) outside [0, %d)", expert_begin,
+                    expert_begin + expert_count, s->n_experts);
     if ((rc = set_device(c))) return rc;
     Layer* L;
-    if ((rc = alloc_layer(c, layer, s, router_w, corr, on_device, &L))) return rc;
-    const int H = s->hidden, I = s->inter, E = s->n_experts;
-    const int64_t nb_gu = (int64_t)E * I * (H / 256), nb_d = (int64_t)E * H * (I / 256);
+    if ((rc = alloc_layer(c, layer, s, expert_begin, expert_count, router_w, corr, on_device, &L))) return rc;
+    const int H = s->hidden, I = s->inter, EC = expert_count;
+    // block indices of the full layer's generator streams: a range holds the
+    // same bytes as the matching slice of the whole layer
+    const int64_t bgu = (int64_t)I * (H / 256), bd = (int64_t)H * (I / 256);
+    const int64_t nb_gu = EC * bgu, nb_d = EC * bd;
     uint8_t* tmp = nullptr;
-    GP_CUDA(cudaMalloc(&tmp, (size_t)std::max(nb_gu, nb_d) * 98));
-    struct M { uint8_t* dst; int64_t rows; int in; int64_t nb; };
-    const M mats[6] = {{L->gate, (int64_t)E * I, H, nb_gu}, {L->up, (int64_t)E * I, H, nb_gu},
-                       {L->down, (int64_t)E * H, I, nb_d},  {L->gate + L->gu_stride * E, I, H, (int64_t)I * H / 256},
-                       {L->up + L->gu_stride * E, I, H, (int64_t)I * H / 256},
-                       {L->down + L->d_stride * E, H, I, (int64_t)H * I / 256}};
+    GP_CUDA(cudaMalloc(&tmp, (size_t)std::max<int64_t>(std::max(nb_gu, nb_d), bgu) * 98));
+    struct M { uint8_t* dst; int64_t rows; int in; int64_t block0, nb; };
+    const M mats[6] = {{L->gate, (int64_t)EC * I, H, expert_begin * bgu, nb_gu},
+                       {L->up, (int64_t)EC * I, H, expert_begin * bgu, nb_gu},
+                       {L->down, (int64_t)EC * H, I, expert_begin * bd, nb_d},
+                       {L->gate + L->gu_stride * EC, I, H, 0, bgu},
+                       {L->up + L->gu_stride * EC, I, H, 0, bgu},
+                       {L->down + L->d_stride * EC, H, I, 0, bd}};
     for (int m = 0; m < (s->n_shared ? 6 : 3); ++m) {
-        GP_CUDA(gp::launch_synth(tmp, seed, stream0 + m, 0, mats[m].nb, 0));
+        if (!mats[m].nb) continue;
+        GP_CUDA(gp::launch_synth(tmp, seed, stream0 + m, mats[m].block0, mats[m].nb, 0));
         GP_CUDA(gp::launch_repack(tmp, mats[m].dst, mats[m].rows, mats[m].in, 0));
     }
     GP_CUDA(cudaDeviceSynchronize());
     GP_CUDA(cudaFree(tmp));
     return GPEED_OK;
+}
+
+int gpeed_moe_synth_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, const float* router_w, const float* corr,
+                          int on_device, uint64_t seed, uint64_t stream0) {
+    if (!s) return fail(GPEED_ERR_INVALID, "shape is NULL");
+    return gpeed_moe_synth_layer_range(c, layer, s, 0, s->n_experts, router_w, corr, on_device, seed, stream0);
 }
 
 int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, float* y, const int* forced,
@@ -539,6 +648,9 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     const Layer& L = it->second;
     const gpeed_moe_shape& s = L.shape;
     const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k;
+    if (L.e_cnt != E)
+        return fail(GPEED_ERR_INVALID, "layer %d holds experts [%d, %d) of %d: use the expert-parallel entry points",
+                    layer, L.e_lo, L.e_lo + L.e_cnt, E);
     int rc;
     if ((rc = set_device(c))) return rc;
     if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
@@ -608,14 +720,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     GP_CUDA(gp::launch_router(ra, st, false));
     mark(1);
 
-    Geo ggu, gd;
-    // one slot list serves both expert kernels: its token count must suit both
-    const int nt = nt_for(n);
-    if ((rc = pick_geo(H, 2, nt, I, &ggu))) return rc;
-    if ((rc = pick_geo(I, 1, nt, H, &gd))) return rc;
     gp::RouteArgs ro{};
     ro.logits = c->partial.p;
-    ro.topk_ready = 0;
     ro.corr = L.corr;
     ro.forced = forced;
     ro.n = n;
@@ -623,67 +729,12 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     ro.K = K;
     ro.routed_scale = s.routed_scale;
     ro.norm_topk = s.norm_topk;
-    ro.nt = nt;
     ro.with_shared = s.n_shared;
     ro.expert_lo = 0;
     ro.expert_hi = E;
     ro.topk_ids = topk_ids ? topk_ids : c->topk_ids.p;
     ro.topk_w = topk_w ? topk_w : c->topk_w.p;
-    ro.perm_tok = c->perm.p;
-    ro.inv_pos = c->inv_pos.p;
-    ro.counts = c->counts.p;
-    ro.slots = c->slots.p;
-    ro.max_slots = (int)c->slots.n;
-    ro.nslots = c->nslots.p;
-    ro.status = c->status;
-    GP_CUDA(gp::launch_route(ro, st, !c->prof));
-    mark(2);
-
-    gp::GemvArgs a{};
-    a.w0 = L.gate;
-    a.w1 = L.up;
-    a.expert_stride = L.gu_stride;
-    a.in_dim = H;
-    a.rows = I;
-    a.tile_rows = ggu.tile_rows;
-    a.nwarps = ggu.nwarps;
-    a.stages = ggu.stages;
-    a.slots = c->slots.p;
-    a.nslots = c->nslots.p;
-    a.perm_tok = c->perm.p;
-    a.x = x;
-    a.x_bf16 = x_dtype == GPEED_DTYPE_BF16;
-    a.out = c->h.p;
-    a.limit = s.swiglu_limit;
-    a.tables = c->tables;
-    a.status = c->status;
-    if (I % a.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "inter %% %d != 0", a.tile_rows);
-    GP_CUDA(gp::launch_gemv(a, nt, true, ggu.passes, ggu.rpw, c->num_sms, st, !c->prof));
-    mark(3);
-
-    gp::GemvArgs d{};
-    d.w0 = L.down;
-    d.w1 = nullptr;
-    d.expert_stride = L.d_stride;
-    d.in_dim = I;
-    d.rows = H;
-    d.tile_rows = gd.tile_rows;
-    d.nwarps = gd.nwarps;
-    d.stages = gd.stages;
-    d.slots = c->slots.p;
-    d.nslots = c->nslots.p;
-    d.perm_tok = nullptr;
-    d.x = c->h.p;
-    d.x_bf16 = 0;
-    d.out = c->D.p;
-    d.tables = c->tables;
-    d.status = c->status;
-    if (H % d.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "hidden %% %d != 0", d.tile_rows);
-    GP_CUDA(gp::launch_gemv(d, nt, false, gd.passes, gd.rpw, c->num_sms, st, !c->prof));
-    mark(4);
-
-    gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, s.n_shared, y};
-    GP_CUDA(gp::launch_combine(cb, st, !c->prof));
+    if ((rc = expert_pass(c, L, x, x_dtype == GPEED_DTYPE_BF16, ro, s.n_shared, nullptr, y, st, mark))) return rc;
     mark(5);
     if (c->prof) {
         GP_CUDA(cudaEventSynchronize(c->ev[5]));
@@ -694,6 +745,147 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         }
         ++c->prof_calls;
     }
+    return GPEED_OK;
+}
+
+// ---- expert parallelism (no counterpart in the reference) ----------------
+
+int gpeed_moe_route(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, const int* forced, int* topk_ids,
+                    float* topk_w, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    if (n < 0) return fail(GPEED_ERR_INVALID, "n_tok < 0");
+    if (n == 0) return GPEED_OK;
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (!x || !topk_ids || !topk_w || (reinterpret_cast<uintptr_t>(x) & 15))
+        return fail(GPEED_ERR_INVALID, "x (16-byte aligned), topk_ids and topk_w are required");
+    const Layer& L = it->second;
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k;
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p};
+    GP_CUDA(gp::launch_router(ra, st, false));
+    gp::RouteArgs ro{};
+    ro.logits = c->partial.p;
+    ro.corr = L.corr;
+    ro.forced = forced;
+    ro.n = n;
+    ro.E = E;
+    ro.K = K;
+    ro.routed_scale = s.routed_scale;
+    ro.norm_topk = s.norm_topk;
+    ro.nt = 1;
+    ro.with_shared = 0;
+    ro.expert_lo = ro.expert_hi = 0;  // ids and weights only: no expert slots
+    ro.topk_ids = topk_ids;
+    ro.topk_w = topk_w;
+    ro.perm_tok = c->perm.p;
+    ro.inv_pos = c->inv_pos.p;
+    ro.counts = c->counts.p;
+    ro.slots = c->slots.p;
+    ro.max_slots = (int)c->slots.n;
+    ro.nslots = c->nslots.p;
+    ro.status = c->status;
+    GP_CUDA(gp::launch_route(ro, st, false));
+    return GPEED_OK;
+}
+
+int gpeed_ep_pack(gpeed_ctx* c, int n_experts, int world, int n, int K, const int* topk_ids, const void* x,
+                  int x_dtype, int hidden, void* send_rows, int* send_ids, int* rank_counts, int* slot_of,
+                  void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if (world < 1 || n_experts < world || n_experts % world)
+        return fail(GPEED_ERR_INVALID, "n_experts %d must split evenly over %d ranks", n_experts, world);
+    if (n < 0 || K < 1 || K > 32 || hidden % 256) return fail(GPEED_ERR_INVALID, "bad n/K/hidden");
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (!rank_counts) return fail(GPEED_ERR_INVALID, "rank_counts is NULL");
+    if (n && (!topk_ids || !x || !send_rows || !send_ids || !slot_of || (reinterpret_cast<uintptr_t>(x) & 15) ||
+              (reinterpret_cast<uintptr_t>(send_rows) & 15)))
+        return fail(GPEED_ERR_INVALID, "NULL or unaligned buffer");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (n == 0) {
+        GP_CUDA(cudaMemsetAsync(rank_counts, 0, sizeof(int) * world, st));
+        return GPEED_OK;
+    }
+    if ((rc = ensure_scratch(c, n, n_experts, K, hidden, 256))) return rc;
+    // stable bucket sort of the assignments by expert = by destination rank
+    gp::RouteArgs ro{};
+    ro.topk_ready = 1;
+    ro.n = n;
+    ro.E = n_experts;
+    ro.K = K;
+    ro.nt = 1;
+    ro.expert_lo = ro.expert_hi = 0;
+    ro.topk_ids = const_cast<int*>(topk_ids);
+    ro.topk_w = c->topk_w.p;
+    ro.perm_tok = c->perm.p;
+    ro.inv_pos = slot_of;
+    ro.counts = c->counts.p;
+    ro.slots = c->slots.p;
+    ro.max_slots = (int)c->slots.n;
+    ro.nslots = c->nslots.p;
+    ro.status = c->status;
+    GP_CUDA(gp::launch_route(ro, st, false));
+    GP_CUDA(gp::launch_ep_pack(x, x_dtype == GPEED_DTYPE_BF16, hidden, n, K, topk_ids, slot_of, c->counts.p,
+                               n_experts, world, n_experts / world, send_rows, send_ids, rank_counts, st));
+    return GPEED_OK;
+}
+
+int gpeed_moe_experts(gpeed_ctx* c, int layer, const void* rows, int rows_dtype, int m, const int* expert_ids,
+                      float* out, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    if (m < 0) return fail(GPEED_ERR_INVALID, "m < 0");
+    if (m == 0) return GPEED_OK;
+    if (rows_dtype != GPEED_DTYPE_BF16 && rows_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "rows_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", rows_dtype);
+    if (!rows || !expert_ids || !out || (reinterpret_cast<uintptr_t>(rows) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+        return fail(GPEED_ERR_INVALID, "rows and out must be 16-byte aligned device pointers; expert_ids required");
+    const Layer& L = it->second;
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, El = L.e_cnt + s.n_shared;
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    if ((rc = ensure_scratch(c, m, El, 1, H, I))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    GP_CUDA(gp::launch_local_ids(expert_ids, m, s.n_experts, L.e_lo, L.e_cnt, c->topk_ids.p, c->topk_w.p, c->status,
+                                 st));
+    // one assignment per row, weight 1, no shared add: out = down(SwiGLU(gate x, up x))
+    gp::RouteArgs ro{};
+    ro.topk_ready = 1;
+    ro.n = m;
+    ro.E = El;
+    ro.K = 1;
+    ro.with_shared = 0;
+    ro.expert_lo = 0;
+    ro.expert_hi = El;
+    ro.topk_ids = c->topk_ids.p;
+    ro.topk_w = c->topk_w.p;
+    auto nomark = [](int) {};
+    return expert_pass(c, L, rows, rows_dtype == GPEED_DTYPE_BF16, ro, 0, nullptr, out, st, nomark);
+}
+
+int gpeed_moe_combine(gpeed_ctx* c, int n, int K, int hidden, const float* d_rows, const int* slot_of,
+                      const float* topk_w, const float* d_shared, float* y, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if (n < 0 || K < 1 || K > 32 || hidden % 4) return fail(GPEED_ERR_INVALID, "bad n/K/hidden");
+    if (n == 0) return GPEED_OK;
+    if (!d_rows || !slot_of || !topk_w || !y || (reinterpret_cast<uintptr_t>(d_rows) & 15) ||
+        (reinterpret_cast<uintptr_t>(y) & 15) || (d_shared && (reinterpret_cast<uintptr_t>(d_shared) & 15)))
+        return fail(GPEED_ERR_INVALID, "NULL or unaligned buffer");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    gp::CombineArgs cb{d_rows, slot_of, topk_w, n, K, hidden, d_shared ? 1 : 0, y, d_shared};
+    GP_CUDA(gp::launch_combine(cb, (cudaStream_t)stream, false));
     return GPEED_OK;
 }
 

@@ -108,6 +108,7 @@ struct CombineArgs {
     const float* topk_w;
     int n, K, H, with_shared;
     float* y;
+    const float* D_shared;  // shared-expert rows [n][H]; nullptr: they follow the routed rows in D
 };
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl);
 
@@ -141,6 +142,17 @@ struct DecodeLayerArgs {
     int stages;
     int cooperative;           // 1: cooperative launch instead of programmatic dependent launch
 };
+// Expert parallelism helpers (ep.cu).
+// global expert ids -> this layer's local expert index (routed e -> e - lo,
+// the shared expert E -> cnt); ids outside [lo, lo+cnt) and != E set BAD_EXPERT.
+cudaError_t launch_local_ids(const int* ids, int m, int E, int lo, int cnt, int* local, float* ones,
+                             uint32_t* status, cudaStream_t st);
+// send_rows[pos[i]] = x[i / K] for every assignment i, send_ids[pos[i]] = ids[i];
+// rank_counts[r] = assignments whose expert lies in [r*epr, (r+1)*epr).
+cudaError_t launch_ep_pack(const void* x, int x_bf16, int H, int n, int K, const int* ids, const int* pos,
+                           const int* counts, int E, int world, int epr, void* send_rows, int* send_ids,
+                           int* rank_counts, cudaStream_t st);
+
 // Counter words of the persistent kernel: the generation counts launches, the
 // others are zero between launches; the host clears all of them (and the
 // tagged buffers) after a launch that reported an error.

@@ -303,7 +303,8 @@ __global__ void combine_kernel(const CombineArgs a) {
             acc.w = fmaf(w[k], d[k].w, acc.w);
         }
     if (a.with_shared) {
-        const float4 s = *reinterpret_cast<const float4*>(a.D + ((int64_t)a.n * a.K + t) * a.H + j);
+        const float* sh = a.D_shared ? a.D_shared + (int64_t)t * a.H : a.D + ((int64_t)a.n * a.K + t) * a.H;
+        const float4 s = *reinterpret_cast<const float4*>(sh + j);
         acc.x += s.x;
         acc.y += s.y;
         acc.z += s.z;
@@ -352,7 +353,7 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl) {
     }
     cudaLaunchAttribute attr[1];
     RouteArgs b = a;
-    if (a.n > 64) {  // large batches: top-k on many CTAs first
+    if (a.n > 64 && !a.topk_ready) {  // large batches: top-k on many CTAs first
         cudaLaunchConfig_t cfg = make_cfg(dim3(min(1184, (a.n + 7) / 8)), dim3(256), 0, st, pdl, attr);
         cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel, a);
         if (e != cudaSuccess) return e;

@@ -163,6 +163,57 @@ GPEED_API int gpeed_synth_iq3xxs(void* dst_dev, uint64_t seed, uint64_t stream, 
 GPEED_API int gpeed_moe_forward(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, int n_tok, float* y_dev,
                       const int* forced_topk_dev, int* topk_ids_dev, float* topk_w_dev, void* stream);
 
+/* ---- Expert parallelism (no counterpart in the reference: it runs every
+ * expert on one host).  Experts split into equal contiguous ranges, one per
+ * rank; tokens stay data-parallel; the router and the shared expert are
+ * replicated.  The exchange between ranks (counts, token rows, expert
+ * outputs) is left to the caller's collectives (NCCL all-to-all); these
+ * entry points do the device work on either side of it:
+ *
+ *   gpeed_moe_route     -> top-k ids/weights of this rank's tokens
+ *   gpeed_ep_pack       -> rows grouped by destination rank + per-rank counts
+ *   (all-to-all of rows and ids)
+ *   gpeed_moe_experts   -> down(SwiGLU(gate x, up x)) per received row, its expert
+ *   (all-to-all of the results back)
+ *   gpeed_moe_experts   -> the shared expert on this rank's own tokens (id = E)
+ *   gpeed_moe_combine   -> y = sum_k w_k D_k + D_shared, in top-k order
+ *
+ * With the same weights every rank's y is bit-identical to gpeed_moe_forward
+ * on one GPU for n_tok > 1 (the batched path). */
+
+/* Loads only routed experts [expert_begin, expert_begin + expert_count) (their
+ * GGUF bytes at gate/up/down) plus the shared expert; the router stays whole. */
+GPEED_API int gpeed_moe_load_layer_range(gpeed_ctx* ctx, int layer, const gpeed_moe_shape* shape, int expert_begin,
+                               int expert_count, const float* router_w, const float* corr_bias, const void* gate_exps,
+                               const void* up_exps, const void* down_exps, const void* gate_sh, const void* up_sh,
+                               const void* down_sh, int on_device);
+/* As gpeed_moe_synth_layer, for an expert range: the bytes equal the matching
+ * slice of the whole synthetic layer. */
+GPEED_API int gpeed_moe_synth_layer_range(gpeed_ctx* ctx, int layer, const gpeed_moe_shape* shape, int expert_begin,
+                                int expert_count, const float* router_w, const float* corr_bias, int on_device,
+                                uint64_t seed, uint64_t stream0);
+/* Router + top-k only (model_batch.cpp:171-203): topk_ids/topk_w device [n_tok][K]. */
+GPEED_API int gpeed_moe_route(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, int n_tok,
+                              const int* forced_topk_dev, int* topk_ids_dev, float* topk_w_dev, void* stream);
+/* Groups this rank's n_tok*K assignments by destination rank (expert /
+ * (n_experts/world)), stable in token order within an expert: send_rows
+ * [n_tok*K][hidden] (x's dtype), send_ids [n_tok*K] (global expert ids),
+ * rank_counts [world] (device), slot_of [n_tok][K] = position of (t, k) in
+ * the send buffers. */
+GPEED_API int gpeed_ep_pack(gpeed_ctx* ctx, int n_experts, int world, int n_tok, int K, const int* topk_ids_dev,
+                            const void* x_dev, int x_dtype, int hidden, void* send_rows_dev, int* send_ids_dev,
+                            int* rank_counts_dev, int* slot_of_dev, void* stream);
+/* out[i] = down_e(SwiGLU(gate_e rows[i], up_e rows[i])) for e = expert_ids[i]
+ * (global id; n_experts = the shared expert), fp32 [m][hidden].  The layer
+ * must hold every listed expert. */
+GPEED_API int gpeed_moe_experts(gpeed_ctx* ctx, int layer, const void* rows_dev, int rows_dtype, int m,
+                                const int* expert_ids_dev, float* out_dev, void* stream);
+/* y[t] = sum_k w[t][k] * d_rows[slot_of[t][k]] (+ d_shared[t]), fp32, k in order
+ * (model.cpp:741-755). */
+GPEED_API int gpeed_moe_combine(gpeed_ctx* ctx, int n_tok, int K, int hidden, const float* d_rows_dev,
+                                const int* slot_of_dev, const float* topk_w_dev, const float* d_shared_dev,
+                                float* y_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

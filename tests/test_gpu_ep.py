@@ -1,0 +1,120 @@
+"""Expert parallelism on the GPU.  One GPU: two ranks emulated in one process
+(two expert-range layers, the exchange done by slicing) against the
+single-GPU batched forward.  Two GPUs: the real NCCL exchange."""
+import datetime
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+from gpeed_b200 import Context, MoeConfig, MoeLayer
+from gpeed_b200.ep import CudaExecutor, ExpertParallelLayer
+from tests.helpers import rel_l2
+
+pytestmark = pytest.mark.gpu
+SEED, S0 = 42, 100
+
+
+def _router(cfg):
+    return (np.random.default_rng(1).standard_normal((cfg.n_experts, cfg.hidden)) * 0.02).astype(np.float32)
+
+
+def _tokens(cfg, n):
+    return torch.from_numpy(np.random.default_rng(5).standard_normal((n, cfg.hidden)).astype(np.float32)).to(
+        torch.bfloat16)
+
+
+def test_ep_device_steps_emulated_two_ranks():
+    ctx = Context(0)
+    try:
+        cfg = MoeConfig()
+        router = _router(cfg)
+        full = MoeLayer(ctx, cfg, layer_id=300).synth(router, None, SEED, S0)
+        splits = [10, 6]
+        X = _tokens(cfg, sum(splits)).cuda()
+        y_ref = full.forward(X)
+        ids_ref = torch.empty(sum(splits), cfg.top_k, dtype=torch.int32, device="cuda")
+        full.forward(X, topk_ids=ids_ref)
+        ex = []
+        for r in range(2):
+            lo, cnt = ExpertParallelLayer.expert_range(cfg, r, 2)
+            e = CudaExecutor(ctx, cfg, 301 + r, lo, cnt)
+            e.synth(router, None, SEED, S0)
+            ex.append(e)
+        Xr = list(torch.split(X, splits))
+        routed = [ex[r].route(Xr[r]) for r in range(2)]
+        packed = [ex[r].pack(routed[r][0], Xr[r], 2) for r in range(2)]
+        counts = [p[2].cpu().tolist() for p in packed]
+        off = [np.concatenate([[0], np.cumsum(c)]).tolist() for c in counts]
+        # rank d receives the segments addressed to it, in source order
+        recv_rows = [torch.cat([packed[r][0][off[r][d]:off[r][d + 1]] for r in range(2)]) for d in range(2)]
+        recv_ids = [torch.cat([packed[r][1][off[r][d]:off[r][d + 1]] for r in range(2)]) for d in range(2)]
+        d_recv = [ex[d].experts(recv_rows[d], recv_ids[d]) for d in range(2)]
+        recv_off = [np.concatenate([[0], np.cumsum([counts[r][d] for r in range(2)])]).tolist() for d in range(2)]
+        ys = []
+        for r in range(2):
+            d_back = torch.cat([d_recv[d][recv_off[d][r]:recv_off[d][r + 1]] for d in range(2)])
+            shared = torch.full((splits[r],), cfg.n_experts, dtype=torch.int32, device="cuda")
+            d_sh = ex[r].experts(Xr[r], shared)
+            ys.append(ex[r].combine(d_back, packed[r][3], routed[r][1], d_sh))
+        ctx.check()
+        np.testing.assert_array_equal(torch.cat([routed[0][0], routed[1][0]]).cpu().numpy(), ids_ref.cpu().numpy())
+        assert rel_l2(torch.cat(ys).cpu().numpy(), y_ref.cpu().numpy()) < 1e-6
+        # a range layer refuses the single-GPU forward
+        with pytest.raises(Exception, match="expert-parallel"):
+            MoeLayer(ctx, cfg, layer_id=301).forward(X)
+    finally:
+        ctx.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, splits, out_dir):
+    import torch.distributed as dist
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        ctx = Context(rank)
+        cfg = MoeConfig()
+        lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+        ex = CudaExecutor(ctx, cfg, 0, lo, cnt)
+        ex.synth(_router(cfg), None, SEED, S0)
+        ep = ExpertParallelLayer(cfg, ex)
+        X = _tokens(cfg, sum(splits))
+        b = sum(splits[:rank])
+        y = ep.forward(X[b:b + splits[rank]].cuda())
+        ctx.check()
+        np.save(os.path.join(out_dir, f"y_{rank}.npy"), y.cpu().numpy())
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_nccl_two_gpus(tmp_path):
+    splits = [9, 7]
+    cfg = MoeConfig()
+    ctx = Context(0)
+    try:
+        y_ref = MoeLayer(ctx, cfg, layer_id=400).synth(_router(cfg), None, SEED, S0).forward(
+            _tokens(cfg, sum(splits)).cuda()).cpu().numpy()
+    finally:
+        ctx.close()
+    mpc = mp.get_context("spawn")
+    port = _free_port()
+    procs = [mpc.Process(target=_nccl_worker, args=(r, 2, port, splits, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    y = np.concatenate([np.load(os.path.join(str(tmp_path), f"y_{r}.npy")) for r in range(2)])
+    assert rel_l2(y, y_ref) < 1e-6
