@@ -353,6 +353,134 @@ def run_gpu(args, rank, local_rank, world):
     return line
 
 
+PREFILL_FLOPS_PER_TOKEN = (K_TOP + 1) * 3 * 2 * I * H + 2 * E * H   # experts + router, per token
+
+
+def run_prefill(args, rank, local_rank, world):
+    """one MoE layer over a 4096-token batch (tensor-bound).
+    A step is one forward of the whole batch through one layer; the experts run
+    as grouped GEMMs on the tensor cores (fp16 operands, fp32 accumulation)."""
+    import torch
+    import torch.distributed as dist
+
+    from gpeed_b200 import Context, MoeConfig, MoeLayer
+    from gpeed_b200 import _capi
+
+    n = args.tokens
+    torch.cuda.set_device(local_rank)
+    ctx = Context(local_rank)
+    cfg = MoeConfig()
+    L = max(1, min(args.layers, 2))
+    layers = [MoeLayer(ctx, cfg, layer_id=l).synth(router_for(l), None, seed=1000 + l, stream0=0) for l in range(L)]
+    stream = torch.cuda.Stream()
+    xs = [tokens(n, 300 + l).cuda() for l in range(L)]
+    ys = [torch.empty(n, H, device="cuda") for _ in range(L)]
+    with torch.cuda.stream(stream):
+        for l in range(L):
+            layers[l].forward(xs[l], ys[l], stream=stream)
+    stream.synchronize()
+    ctx.check(stream)
+    graphs = []
+    for l in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            layers[l].forward(xs[l], ys[l], stream=stream)
+        graphs.append(g)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % L].replay()
+    stream.synchronize()
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for i in range(args.steps):
+                graphs[i % L].replay()
+            ev1.record(stream)
+        stream.synchronize()
+        ms_total = ev0.elapsed_time(ev1)
+    barrier()
+    ctx.check(stream)
+    if world > 1:
+        t = torch.tensor([ms_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    value = world * n * args.steps / (ms_total / 1000.0)
+
+    # per-kernel timing (events between the forward's kernels): gate/up and down GEMMs
+    _capi.call("gpeed_ctx_profile", ctx.handle, 1)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.steps, 4)):
+            layers[i % L].forward(xs[i % L], ys[i % L], stream=stream)
+    stage = (ctypes.c_float * 5)()
+    calls = ctypes.c_int()
+    _capi.call("gpeed_ctx_profile_read", ctx.handle, stage, ctypes.byref(calls))
+    _capi.call("gpeed_ctx_profile", ctx.handle, 0)
+    stage_ms = list(stage)
+
+    # end to end with host buffers: x in, y out every step
+    x_host = tokens(n, 555).pin_memory()
+    y_host = torch.empty(n, H, dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_steps = max(3, args.steps // 4)
+    for i in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            xs[0].copy_(x_host, non_blocking=True)
+            layers[0].forward(xs[0], ys[0], stream=stream)
+            y_host.copy_(ys[0], non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    ctx.check(stream)
+
+    _, tf_peak, peak_src = peaks()
+    gu_flops = n * (K_TOP + 1) * 2 * 2 * I * H
+    dn_flops = n * (K_TOP + 1) * 2 * I * H
+    line = None
+    if rank == 0:
+        gu_tf = gu_flops / (stage_ms[2] * 1e-3) / 1e12 if stage_ms[2] > 0 else None
+        dn_tf = dn_flops / (stage_ms[3] * 1e-3) / 1e12 if stage_ms[3] > 0 else None
+        step_tf = PREFILL_FLOPS_PER_TOKEN * n / (ms_total / args.steps * 1e-3) / 1e12
+        cpu = None
+        if not args.no_cpu and world == 1:
+            from oracle import oracle
+            kind = "reference" if oracle.available("reference") else "port"
+            tps, done, dt, cores = cpu_time_layer(kind, args.cpu_seconds, 64)
+            cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
+                   "sample": f"{done} tokens x 1 layer (config 2 shapes, token by token) in {dt:.1f} s"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 x f16 -> f32 (tcgen05), IQ3_XXS weights decoded in-kernel",
+            "data": "synthetic",
+            "config": {"workload": f"prefill{n}: MoE layer over a {n}-token batch (BASELINE config 4)", "hidden": H,
+                       "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
+                       "layer_copies": L, "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "step_tflops": step_tf,
+                       "stage_ms": dict(zip(["router", "route+gather", "gateup_gemm", "down_gemm", "combine"],
+                                            stage_ms))},
+            "roofline": {"bound": "tensor", "achieved": gu_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": (gu_tf / tf_peak) if gu_tf and tf_peak else None, "traffic": None,
+                         "kernel": "tc_moe_kernel<gate/up> (grouped GEMM, 161 expert slots)",
+                         "flops_per_launch": gu_flops, "down_tflops": dn_tf, "peak_source": peak_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": n * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": n * H * 2,
+                    "d2h_bytes_per_step": n * H * 4},
+            "gpu_launches": 7 * args.steps,
+            "clocks": clk.summary(),
+        }
+    del graphs
+    ctx.close()
+    return line
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -362,6 +490,9 @@ def main():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--workload", default="decode1", choices=["decode1", "prefill"],
+                    help="decode1: BASELINE config 2 (default); prefill: config 4")
+    ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = env_rank()
@@ -375,7 +506,7 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    line = run_gpu(args, rank, local_rank, world)
+    line = run_prefill(args, rank, local_rank, world) if args.workload == "prefill" else run_gpu(args, rank, local_rank, world)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -15,6 +15,7 @@ OK, ERR_INVALID, ERR_CUDA, ERR_DEVICE, ERR_UNSUPPORTED, ERR_NCCL = range(6)
 DTYPE_F32, DTYPE_IQ3_XXS, DTYPE_BF16 = 0, 18, 30
 OPT_FUSED_DECODE = 1
 OPT_FUSED_COOPERATIVE = 2
+OPT_TC_MIN_TOKENS = 3
 
 
 class GpeedError(RuntimeError):

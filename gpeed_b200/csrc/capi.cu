@@ -96,6 +96,8 @@ struct gpeed_ctx {
     // batch-1 forward in one persistent kernel when the shape has a variant
     bool fused_decode = true;
     bool fused_cooperative = false;
+    int tc_min_tokens = 1024;          // batches this large run the experts on tensor cores
+    DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<unsigned long long> logits, dx;
     DevBuf<uint8_t> hq;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
@@ -392,6 +394,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
     c->logits.release();
+    c->xp.release();
     c->dx.release();
     c->hq.release();
     cudaFree(c->sync);
@@ -426,6 +429,10 @@ int gpeed_ctx_set_option(gpeed_ctx* c, int option, int value) {
     switch (option) {
         case GPEED_OPT_FUSED_DECODE: c->fused_decode = value != 0; return GPEED_OK;
         case GPEED_OPT_FUSED_COOPERATIVE: c->fused_cooperative = value != 0; return GPEED_OK;
+        case GPEED_OPT_TC_MIN_TOKENS:
+            if (value < 1) return fail(GPEED_ERR_INVALID, "tensor-core threshold must be >= 1");
+            c->tc_min_tokens = value;
+            return GPEED_OK;
         default: return fail(GPEED_ERR_INVALID, "unknown option %d", option);
     }
 }
@@ -719,6 +726,56 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p};
     GP_CUDA(gp::launch_router(ra, st, false));
     mark(1);
+    if (n >= c->tc_min_tokens && s.n_shared && gp::tc_moe_supported(H, I)) {
+        // experts on tensor cores: slots of <= 256 rows per expert, fp16 operands
+        const int npos = n * K + n;
+        if ((rc = c->xp.ensure((size_t)npos * H))) return rc;
+        gp::RouteArgs ro{};
+        ro.logits = c->partial.p;
+        ro.corr = L.corr;
+        ro.forced = forced;
+        ro.n = n;
+        ro.E = E;
+        ro.K = K;
+        ro.routed_scale = s.routed_scale;
+        ro.norm_topk = s.norm_topk;
+        ro.nt = 256;
+        ro.with_shared = 1;
+        ro.expert_lo = 0;
+        ro.expert_hi = E;
+        ro.topk_ids = topk_ids ? topk_ids : c->topk_ids.p;
+        ro.topk_w = topk_w ? topk_w : c->topk_w.p;
+        ro.perm_tok = c->perm.p;
+        ro.inv_pos = c->inv_pos.p;
+        ro.counts = c->counts.p;
+        ro.slots = c->slots.p;
+        ro.max_slots = (int)c->slots.n;
+        ro.nslots = c->nslots.p;
+        ro.status = c->status;
+        GP_CUDA(gp::launch_route(ro, st, false));
+        GP_CUDA(gp::launch_gather_cast(x, x_dtype == GPEED_DTYPE_BF16, c->perm.p, npos, H, c->xp.p, st));
+        mark(2);
+        uint16_t* h16 = reinterpret_cast<uint16_t*>(c->h.p);  // npos x I fp16 fits the fp32 h scratch
+        gp::TcArgs ga{c->slots.p, c->nslots.p, I / 128, H, I, s.swiglu_limit, h16, c->status};
+        GP_CUDA(gp::launch_tc_moe(true, L.gate, L.up, (int64_t)(E + 1) * I, c->xp.p, npos, ga, c->num_sms, st));
+        mark(3);
+        gp::TcArgs da{c->slots.p, c->nslots.p, H / 128, I, H, 0.f, c->D.p, c->status};
+        GP_CUDA(gp::launch_tc_moe(false, L.down, nullptr, (int64_t)(E + 1) * H, h16, npos, da, c->num_sms, st));
+        mark(4);
+        gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, 1, y, nullptr};
+        GP_CUDA(gp::launch_combine(cb, st, false));
+        mark(5);
+        if (c->prof) {
+            GP_CUDA(cudaEventSynchronize(c->ev[5]));
+            for (int i = 0; i < 5; ++i) {
+                float ms = 0.f;
+                GP_CUDA(cudaEventElapsedTime(&ms, c->ev[i], c->ev[i + 1]));
+                c->prof_ms[i] += ms;
+            }
+            ++c->prof_calls;
+        }
+        return GPEED_OK;
+    }
 
     gp::RouteArgs ro{};
     ro.logits = c->partial.p;

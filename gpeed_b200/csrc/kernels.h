@@ -142,6 +142,22 @@ struct DecodeLayerArgs {
     int stages;
     int cooperative;           // 1: cooperative launch instead of programmatic dependent launch
 };
+// Tensor-core experts for large batches (tc_moe.cu).
+struct TcArgs {
+    const SlotDesc* slots;  // expert slots of <= 256 rows (expert-sorted positions)
+    const int* nslots;
+    int mt;                 // 128-row tiles per expert matrix (nout / 128)
+    int kin, nout;          // inputs per row, rows per expert
+    float limit;            // SwiGLU clamp (gate/up pass)
+    void* out;              // gate/up: fp16 h [position][nout]; down: fp32 D [position][nout]
+    uint32_t* status;
+};
+bool tc_moe_supported(int H, int I);
+cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
+                               cudaStream_t st);
+cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t weight_rows, const uint16_t* b,
+                          int npos, const TcArgs& args, int grid, cudaStream_t st);
+
 // Expert parallelism helpers (ep.cu).
 // global expert ids -> this layer's local expert index (routed e -> e - lo,
 // the shared expert E -> cnt); ids outside [lo, lo+cnt) and != E set BAD_EXPERT.

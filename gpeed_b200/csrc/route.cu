@@ -83,6 +83,73 @@ __global__ void __launch_bounds__(32 * kRouterWarps) router_kernel(const RouterA
     pdl_launch_dependents();
 }
 
+// Large batches: logits as a register-blocked fp32 GEMM.  CTA tile = 128
+// tokens x 32 experts, K in slices of 32 staged in shared memory; each thread
+// accumulates 4 tokens x 4 experts over K in order (deterministic).
+constexpr int kRgTok = 128, kRgExp = 32, kRgK = 32;
+__global__ void __launch_bounds__(256) router_gemm_kernel(const RouterArgs a) {
+    __shared__ __align__(16) float xs[kRgK][kRgTok + 4];
+    __shared__ __align__(16) float ws[kRgK][kRgExp + 4];
+    pdl_wait();
+    const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
+    const int t0 = blockIdx.y * kRgTok, e0 = blockIdx.x * kRgExp;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < a.H; k0 += kRgK) {
+        // x tile: 128 tokens x 32 k (4 consecutive k per load)
+        for (int i = tid; i < kRgTok * kRgK / 4; i += 256) {
+            const int t = i / (kRgK / 4), kq = (i % (kRgK / 4)) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (t0 + t < a.n) {
+                const int64_t off = (int64_t)(t0 + t) * a.H + k0 + kq;
+                if (a.x_bf16) {
+                    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + off);
+                    v = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                                    __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+                } else {
+                    v = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + off);
+                }
+            }
+            xs[kq][t] = v.x;
+            xs[kq + 1][t] = v.y;
+            xs[kq + 2][t] = v.z;
+            xs[kq + 3][t] = v.w;
+        }
+        // w tile: 32 experts x 32 k
+        {
+            const int e = tid / (kRgK / 4), kq = (tid % (kRgK / 4)) * 4;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e0 + e < a.E) v = *reinterpret_cast<const float4*>(a.w + (int64_t)(e0 + e) * a.H + k0 + kq);
+            ws[kq][e] = v.x;
+            ws[kq + 1][e] = v.y;
+            ws[kq + 2][e] = v.z;
+            ws[kq + 3][e] = v.w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int k = 0; k < kRgK; ++k) {
+            const float4 xv = *reinterpret_cast<const float4*>(&xs[k][ty * 4]);
+            const float4 wv = *reinterpret_cast<const float4*>(&ws[k][tx * 4]);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(xa[i], wa[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + ty * 4 + i;
+        if (t >= a.n) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int e = e0 + tx * 4 + j;
+            if (e < a.E) a.logits[(int64_t)t * a.E + e] = acc[i][j];
+        }
+    }
+    pdl_launch_dependents();
+}
+
 constexpr int kRouteThreads = 1024;
 constexpr int kMaxE = 512;
 
@@ -335,6 +402,12 @@ size_t route_smem_bytes(int n, int E, int K) {
 
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl) {
     if (a.H % 4 || a.H > 4 * 256 * kRouterMaxVec) return cudaErrorInvalidValue;
+    if (a.n >= 64 && a.H % kRgK == 0) {
+        cudaLaunchAttribute attr[1];
+        cudaLaunchConfig_t cfg = make_cfg(dim3((a.E + kRgExp - 1) / kRgExp, (a.n + kRgTok - 1) / kRgTok), dim3(256), 0,
+                                          st, pdl, attr);
+        return cudaLaunchKernelEx(&cfg, router_gemm_kernel, a);
+    }
     const int ntc = (a.n + kRouterTok - 1) / kRouterTok;
     cudaLaunchAttribute attr[1];
     cudaLaunchConfig_t cfg = make_cfg(dim3(a.E, ntc), dim3(32 * kRouterWarps), 0, st, pdl, attr);

@@ -1,0 +1,89 @@
+// tcgen05 / TMEM / tensor-map helpers for the sm_100a tensor-core kernels.
+// Descriptor layouts follow the PTX ISA (tcgen05 "Matrix descriptors" and
+// "Instruction descriptor"): K-major operands in the 128-byte swizzled
+// canonical layout (8-row x 128-byte atoms, atoms stacked 1024 bytes apart).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+
+namespace gp {
+
+// ---- shared-memory matrix descriptor, K-major, SWIZZLE_128B -----------------
+// start address >> 4 in [0,14), leading-dimension byte offset >> 4 in [16,30)
+// (unused for swizzled K-major: 1), stride byte offset >> 4 in [32,46) (1024 B
+// between 8-row groups), version 1 in [46,48), base offset 0, layout type 2
+// (128-byte swizzle) in [61,64).  The tile base must be 1024-byte aligned; a
+// K step inside the 128-byte row advances the start address by the bytes
+// skipped (the hardware applies the swizzle to the final address).
+GP_DEVINL uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// ---- instruction descriptor, kind::f16, f32 accumulate, both K-major -------
+// c_format [4,6) = 1 (f32); a_format [7,10) / b_format [10,13) = 0 (f16) or 1
+// (bf16); n_dim [17,23) = N >> 3; m_dim [24,29) = M >> 4.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N, bool bf16) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
+}
+
+GP_DEVINL void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+// Arrives on the mbarrier once every MMA this thread issued before it has completed.
+GP_DEVINL void umma_commit(uint32_t mbar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)
+                 : "memory");
+}
+GP_DEVINL void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+GP_DEVINL void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// ---- TMEM ------------------------------------------------------------------
+// Whole warp: allocates ncols columns (power of 2, >= 32); the TMEM address
+// lands in shared memory at dst.
+GP_DEVINL void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem), "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+GP_DEVINL void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// 32 lanes x 32 consecutive columns starting at taddr (lane field = this warp's
+// quadrant): thread l gets row (quadrant*32 + l), columns col..col+31.
+GP_DEVINL void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ---- TMA tiled loads (no multicast) ----------------------------------------
+GP_DEVINL void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(mbar)
+        : "memory");
+}
+
+// Byte offset of element (row, k) (2-byte elements) inside a K-major,
+// 128-byte-swizzled tile whose rows hold 64 elements: 16-byte chunk index
+// XOR (row % 8).
+__host__ __device__ inline uint32_t sw128_offset(uint32_t row, uint32_t k) {
+    const uint32_t chunk = (k >> 3) ^ (row & 7u);
+    return row * 128u + chunk * 16u + (k & 7u) * 2u;
+}
+
+}  // namespace gp

@@ -1,0 +1,418 @@
+// Large-batch (prefill) MoE experts on the 5th-generation tensor cores.
+//
+// For each expert slot (expert e, up to 256 token rows in expert-sorted
+// order) and each 128-row tile of an expert matrix, one CTA computes
+//   D[row][tok] = sum_k W[row][k] * X[tok][k]
+// with tcgen05.mma (kind::f16, fp16 operands, fp32 accumulators in TMEM).
+// The weights stay IQ3_XXS in HBM: decode warps turn each 128 x 64 slice into
+// fp16 (the reference's fp32 weight d*(0.5+s)*0.5*g*sign, rounded once to
+// fp16) straight into the 128-byte-swizzled operand layout in shared memory.
+//
+//   gate/up pass  A = gate and up tiles (two accumulators), B = the tokens'
+//                 rows (fp16); epilogue SwiGLU with the reference clamp
+//                 (model_batch.cpp:249-253) -> h [position][I] fp16
+//   down pass     A = down tile, B = h rows; epilogue -> D [position][H] fp32,
+//                 then the batched path's combine (model_batch.cpp:257-280)
+//
+// Warp roles (448 threads, one CTA per SM, persistent over the tile list):
+//   warp 0     TMA producer: token tile (2-D, 128-byte swizzle) and the raw
+//              IQ3_XXS bytes of the tile (3-D maps over the row-group layout:
+//              index bytes, sign/scale words, per-tile fp16 scales)
+//   warp 1     TMEM allocation; one thread issues the MMAs and commits
+//   warps 2-5  epilogue: TMEM -> registers -> global (one lane quadrant each)
+//   warps 6-13 decode: 2 sub-blocks per thread per matrix per K slice
+// No cluster, no multicast.  Every wait is bounded; a timeout sets a status bit.
+#include <cuda_fp16.h>
+
+#include "expert_common.cuh"
+#include "iq3xxs.cuh"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace gp {
+namespace {
+
+constexpr int TBM = 128;  // weight rows per tile (MMA M = TMEM lanes)
+constexpr int TBN = 256;  // token rows per tile (MMA N)
+constexpr int TBK = 64;   // K per slice (one 128-byte swizzled fp16 row)
+constexpr int TST = 3;    // token/raw stages
+constexpr int TAS = 2;    // decoded weight stages
+constexpr int NDEC = 8;   // decode warps
+constexpr int NEPI = 4;   // epilogue warps
+constexpr int WEPI0 = 2, WDEC0 = 6;
+constexpr int TC_THREADS = 32 * (WDEC0 + NDEC);
+constexpr uint32_t B_TILE = TBN * TBK * 2;  // 32 KB
+constexpr uint32_t A_TILE = TBM * TBK * 2;  // 16 KB
+constexpr uint32_t RAW_QS = TBM * 16;       // 2 sub-blocks x 8 index bytes per row
+constexpr uint32_t RAW_AUX = TBM * 16;      // 4 sign/scale words per row (2 used)
+
+struct TcSmem {
+    uint32_t stage, stages_off, a_off, d_off, dbytes, grid_off, bar_off, total;
+};
+
+__host__ __device__ inline TcSmem tc_smem(int nm, int kin) {
+    TcSmem L;
+    L.stage = B_TILE + nm * (RAW_QS + RAW_AUX);
+    L.stages_off = 0;
+    L.a_off = TST * L.stage;
+    L.dbytes = (uint32_t)(256 * (kin / 256) + 127) & ~127u;  // 16 groups x 16 * NBLK bytes
+    L.d_off = L.a_off + TAS * nm * A_TILE;
+    L.grid_off = L.d_off + 2 * nm * L.dbytes;
+    L.bar_off = L.grid_off + 1024;
+    L.total = L.bar_off + 256 + 1024;  // barriers + TMEM slot; 1 KB alignment slack
+    return L;
+}
+
+struct TcMaps {
+    CUtensorMap b;         // token rows, fp16 [positions][kin], box {64, 256}, 128-byte swizzle
+    CUtensorMap qs[2];     // per matrix: index bytes {64*NBLK, 8, groups}, box {16, 8, 16}
+    CUtensorMap aux[2];    // sign/scale words {32*NBLK, 8, groups}, box {16, 8, 16}
+    CUtensorMap dsc[2];    // fp16 scales {8*NBLK, 2, groups}, box {8*NBLK, 2, 16}
+};
+
+// One K slice of one weight matrix: thread (r, hf) decodes sub-block 2*(c%4)+hf
+// of block c/4 in row r into the swizzled fp16 tile.
+GP_DEVINL void decode_slice(uint32_t a_tile, const uint8_t* qs, const uint8_t* aux, const uint8_t* dsc,
+                            const uint32_t* grid, int nblk, int c, int r, int hf) {
+    const uint2 q = *reinterpret_cast<const uint2*>(qs + r * 16 + hf * 8);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(aux + r * 16 + (c & 1) * 8 + hf * 4);
+    const uint16_t dh = *reinterpret_cast<const uint16_t*>(dsc + (r >> 3) * 16 * nblk + (r & 7) * 2 * nblk + 2 * (c >> 2));
+    const float db = iq3_db(__half2float(__ushort_as_half(dh)), w);
+    const uint32_t idx[2] = {q.x, q.y};
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const uint32_t k7 = (w >> (7 * l)) & 127u;
+        const uint32_t sg = k7 | ((uint32_t)(__popc(k7) & 1) << 7);
+        const uint32_t g0 = grid[(idx[l >> 1] >> (16 * (l & 1))) & 0xFF];
+        const uint32_t g1 = grid[(idx[l >> 1] >> (16 * (l & 1) + 8)) & 0xFF];
+        uint32_t h[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+            const uint32_t ga = ((j < 4 ? g0 : g1) >> (8 * (j & 3))) & 0xFF;
+            const uint32_t gb = ((j + 1 < 4 ? g0 : g1) >> (8 * ((j + 1) & 3))) & 0xFF;
+            const float wa = iq3_weight_f32(db, ga, (sg >> j) & 1u);
+            const float wb = iq3_weight_f32(db, gb, (sg >> (j + 1)) & 1u);
+            const __half2 p = __floats2half2_rn(wa, wb);
+            h[j >> 1] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        const uint32_t chunk = (uint32_t)(4 * hf + l) ^ (uint32_t)(r & 7);
+        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a_tile + r * 128 + chunk * 16), "r"(h[0]),
+                     "r"(h[1]), "r"(h[2]), "r"(h[3])
+                     : "memory");
+    }
+}
+
+GP_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+GP_DEVINL void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+            "r"(dst),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(mbar)
+        : "memory");
+}
+
+template <bool GU>
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
+    constexpr int NM = GU ? 2 : 1;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw0 = smem_u32(smem_raw);
+    const uint32_t base = (raw0 + 1023u) & ~1023u;
+    uint8_t* gbase = smem_raw + (base - raw0);
+    const TcSmem L = tc_smem(NM, a.kin);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nblk = a.kin / 256, nk = a.kin / TBK;
+    const uint32_t bar = base + L.bar_off;
+    const uint32_t st_full = bar, st_empty = bar + 8 * TST, a_full = st_empty + 8 * TST, a_empty = a_full + 8 * TAS;
+    const uint32_t d_full = a_empty + 8 * TAS, d_empty = d_full + 16, acc_full = d_empty + 16, acc_empty = acc_full + 16;
+    const uint32_t tslot = acc_empty + 16;
+    uint32_t* s_grid = reinterpret_cast<uint32_t*>(gbase + L.grid_off);
+    const int nslots = *a.nslots;
+    const int ntiles = nslots * a.mt;
+
+    if (tid == 0) {
+        for (int s = 0; s < TST; ++s) { mbar_init(st_full + 8 * s, 1); mbar_init(st_empty + 8 * s, NDEC + 1); }
+        for (int s = 0; s < TAS; ++s) { mbar_init(a_full + 8 * s, NDEC); mbar_init(a_empty + 8 * s, 1); }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(d_full + 8 * s, 1);
+            mbar_init(d_empty + 8 * s, NDEC);
+            mbar_init(acc_full + 8 * s, 1);
+            mbar_init(acc_empty + 8 * s, NEPI);
+        }
+        fence_mbar_init();
+    }
+    for (int i = tid; i < 256; i += TC_THREADS) s_grid[i] = gp_iq3xxs_grid_dev[i];
+    if (warp == 1) tmem_alloc(tslot, 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tbase = *reinterpret_cast<volatile uint32_t*>(gbase + (tslot - base));
+
+    if (warp == 0) {
+        // ================= producer =================
+        if (lane == 0) {
+            const uint32_t tx = B_TILE + NM * (RAW_QS + RAW_AUX);
+            int gc = 0;
+            for (int t = blockIdx.x, lt = 0; t < ntiles; t += gridDim.x, ++lt) {
+                const SlotDesc sd = a.slots[t / a.mt];
+                const int z0 = (sd.expert * a.nout + (t % a.mt) * TBM) / 8;
+                const int db = lt & 1;
+                if (!mbar_wait(d_empty + 8 * db, ((lt >> 1) & 1) ^ 1)) { atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY); break; }
+                mbar_arrive_expect_tx(d_full + 8 * db, NM * 16 * 16 * nblk);
+                for (int mi = 0; mi < NM; ++mi)
+                    tma_load_3d(base + L.d_off + (db * NM + mi) * L.dbytes, &maps.dsc[mi], 0, 0, z0, d_full + 8 * db);
+                bool ok = true;
+                for (int c = 0; c < nk; ++c, ++gc) {
+                    const int s = gc % TST;
+                    if (!mbar_wait(st_empty + 8 * s, ((gc / TST) & 1) ^ 1)) { ok = false; break; }
+                    const uint32_t sb = base + L.stages_off + s * L.stage;
+                    mbar_arrive_expect_tx(st_full + 8 * s, tx);
+                    tma_load_2d(sb, &maps.b, c * TBK, sd.begin, st_full + 8 * s);
+                    for (int mi = 0; mi < NM; ++mi) {
+                        const uint32_t rq = sb + B_TILE + mi * (RAW_QS + RAW_AUX);
+                        tma_load_3d(rq, &maps.qs[mi], 64 * (c >> 2) + 16 * (c & 3), 0, z0, st_full + 8 * s);
+                        tma_load_3d(rq + RAW_QS, &maps.aux[mi], 32 * (c >> 2) + 16 * ((c & 3) >> 1), 0, z0,
+                                    st_full + 8 * s);
+                    }
+                }
+                if (!ok) { atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY); break; }
+            }
+        }
+    } else if (warp == 1) {
+        // ================= MMA issue =================
+        if (lane == 0) {
+            int gc = 0;
+            bool ok = true;
+            for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
+                // N follows the slot's rows (multiple of 16, as M = 128 requires)
+                const int ntok = a.slots[t / a.mt].ntok;
+                const uint32_t idesc = umma_idesc_f16(TBM, ntok >= TBN ? TBN : (ntok + 15) & ~15, false);
+                const int ab = GU ? 0 : (lt & 1);
+                const uint32_t ph_e = GU ? ((lt & 1) ^ 1) : (((lt >> 1) & 1) ^ 1);
+                if (!mbar_wait(acc_empty + 8 * ab, ph_e)) { ok = false; break; }
+                tc_fence_after();
+                for (int c = 0; c < nk; ++c, ++gc) {
+                    const int s = gc % TST, as = gc % TAS;
+                    if (!mbar_wait(a_full + 8 * as, (gc / TAS) & 1) || !mbar_wait(st_full + 8 * s, (gc / TST) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sb = base + L.stages_off + s * L.stage;
+#pragma unroll
+                    for (int kk = 0; kk < TBK / 16; ++kk) {
+                        const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
+#pragma unroll
+                        for (int mi = 0; mi < NM; ++mi) {
+                            const uint32_t at = base + L.a_off + (as * NM + mi) * A_TILE;
+                            const uint32_t dt = tbase + (GU ? mi * TBN : ab * TBN);
+                            umma_f16(dt, umma_desc_sw128(at + kk * 32), bdesc, idesc, (c | kk) != 0);
+                        }
+                    }
+                    umma_commit(a_empty + 8 * as);
+                    umma_commit(st_empty + 8 * s);
+                }
+                if (ok) umma_commit(acc_full + 8 * ab);
+            }
+            if (!ok) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+        }
+    } else if (warp < WDEC0) {
+        // ================= epilogue =================
+        const int q = warp & 3;
+        bool ok = true;
+        for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
+            const SlotDesc sd = a.slots[t / a.mt];
+            const int row = (t % a.mt) * TBM + 32 * q + lane;
+            const int ab = GU ? 0 : (lt & 1);
+            const uint32_t ph = GU ? (lt & 1) : ((lt >> 1) & 1);
+            if (!mbar_wait(acc_full + 8 * ab, ph)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t lanebase = tbase + ((uint32_t)(32 * q) << 16);
+            for (int j0 = 0; j0 < TBN && j0 < sd.ntok; j0 += 32) {
+                uint32_t v0[32];
+                tmem_ld32(lanebase + (GU ? 0 : ab * TBN) + j0, v0);
+                if (GU) {
+                    uint32_t v1[32];
+                    tmem_ld32(lanebase + TBN + j0, v1);
+                    __half* h = static_cast<__half*>(a.out);
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj)
+                        if (j0 + jj < sd.ntok)
+                            h[(int64_t)(sd.begin + j0 + jj) * a.nout + row] =
+                                __float2half_rn(silu_clamped(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit));
+                } else {
+                    float* d = static_cast<float*>(a.out);
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj)
+                        if (j0 + jj < sd.ntok) d[(int64_t)(sd.begin + j0 + jj) * a.nout + row] = __uint_as_float(v0[jj]);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+        }
+        if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+    } else {
+        // ================= decode =================
+        const int td = tid - 32 * WDEC0, r = td >> 1, hf = td & 1;
+        int gc = 0;
+        bool ok = true;
+        for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
+            const int db = lt & 1;
+            if (!mbar_wait(d_full + 8 * db, (lt >> 1) & 1)) { ok = false; break; }
+            for (int c = 0; c < nk; ++c, ++gc) {
+                const int s = gc % TST, as = gc % TAS;
+                if (!mbar_wait(st_full + 8 * s, (gc / TST) & 1) || !mbar_wait(a_empty + 8 * as, ((gc / TAS) & 1) ^ 1)) {
+                    ok = false;
+                    break;
+                }
+                const uint8_t* sb = gbase + L.stages_off + s * L.stage;
+#pragma unroll
+                for (int mi = 0; mi < NM; ++mi) {
+                    const uint8_t* rq = sb + B_TILE + mi * (RAW_QS + RAW_AUX);
+                    decode_slice(base + L.a_off + (as * NM + mi) * A_TILE, rq, rq + RAW_QS,
+                                 gbase + L.d_off + (db * NM + mi) * L.dbytes, s_grid, nblk, c, r, hf);
+                }
+                fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(a_full + 8 * as);
+                    mbar_arrive(st_empty + 8 * s);
+                }
+            }
+            __syncwarp();
+            if (ok && lane == 0) mbar_arrive(d_empty + 8 * db);
+        }
+        if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tbase, 512);
+    }
+}
+
+// Casts token rows to fp16 in expert-sorted order: xp[p] = x[perm[p]].
+__global__ void gather_cast_kernel(const void* x, int x_bf16, const int* perm, int npos, int H, __half* xp) {
+    const int qpr = H / 8;  // 8 elements per thread step
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)npos * qpr;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i / qpr), q = (int)(i % qpr);
+        const int64_t src = (int64_t)perm[p] * H + q * 8;
+        float v[8];
+        if (x_bf16) {
+            const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + src);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[2 * j] = __uint_as_float(w[j] << 16);
+                v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+            }
+        } else {
+            const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src);
+            const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src + 4);
+            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+        }
+        uint4 o;
+        __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+        __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
+        o.x = *reinterpret_cast<uint32_t*>(&h0);
+        o.y = *reinterpret_cast<uint32_t*>(&h1);
+        o.z = *reinterpret_cast<uint32_t*>(&h2);
+        o.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(xp + (int64_t)p * H + q * 8) = o;
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encoder() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+bool encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = encoder();
+    if (!fn) return false;
+    const cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Maps for one repacked IQ3_XXS matrix of `groups` 8-row groups, kin inputs.
+bool encode_weight_maps(TcMaps& m, int mi, const uint8_t* w, int64_t groups, int kin) {
+    const int nblk = kin / 256;
+    const cuuint64_t gstride = 784ull * nblk;
+    {
+        const cuuint64_t dims[3] = {64ull * nblk, 8, (cuuint64_t)groups};
+        const cuuint64_t str[2] = {64ull * nblk, gstride};
+        const cuuint32_t box[3] = {16, 8, 16};
+        if (!encode(&m.qs[mi], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    {
+        const cuuint64_t dims[3] = {32ull * nblk, 8, (cuuint64_t)groups};
+        const cuuint64_t str[2] = {32ull * nblk, gstride};
+        const cuuint32_t box[3] = {16, 8, 16};
+        if (!encode(&m.aux[mi], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w + 512ull * nblk, dims, str, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    {
+        const cuuint64_t dims[3] = {8ull * nblk, 2, (cuuint64_t)groups};
+        const cuuint64_t str[2] = {8ull * nblk, gstride};
+        const cuuint32_t box[3] = {(cuuint32_t)(8 * nblk), 2, 16};
+        if (!encode(&m.dsc[mi], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w + 768ull * nblk, dims, str, box,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+            return false;
+    }
+    return true;
+}
+
+}  // namespace
+
+bool tc_moe_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0 && H % TBM == 0 && I % TBM == 0 && H <= 8192 && I <= 8192; }
+
+cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
+                               cudaStream_t st) {
+    if (npos <= 0) return cudaSuccess;
+    gather_cast_kernel<<<148 * 8, 256, 0, st>>>(x, x_bf16, perm, npos, H, reinterpret_cast<__half*>(xp));
+    return cudaGetLastError();
+}
+
+// gate/up (gu = true: w0 gate, w1 up, B = xp [npos][kin]) or down (w0, B = h).
+cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t weight_rows, const uint16_t* b,
+                          int npos, const TcArgs& args, int grid, cudaStream_t st) {
+    TcMaps m{};
+    const int kin = args.kin;
+    if (!tc_moe_supported(kin, args.nout) || npos <= 0 || weight_rows % 8) return cudaErrorInvalidValue;
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)kin, (cuuint64_t)npos};
+        const cuuint64_t str[1] = {(cuuint64_t)kin * 2};
+        const cuuint32_t box[2] = {TBK, TBN};
+        if (!encode(&m.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
+            return cudaErrorInvalidValue;
+    }
+    if (!encode_weight_maps(m, 0, w0, weight_rows / 8, kin)) return cudaErrorInvalidValue;
+    if (gu && !encode_weight_maps(m, 1, w1, weight_rows / 8, kin)) return cudaErrorInvalidValue;
+    const TcSmem L = tc_smem(gu ? 2 : 1, kin);
+    if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
+    auto kern = gu ? tc_moe_kernel<true> : tc_moe_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    if (e != cudaSuccess) return e;
+    kern<<<grid, TC_THREADS, L.total, st>>>(m, args);
+    return cudaGetLastError();
+}
+
+}  // namespace gp

@@ -94,6 +94,11 @@ GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
  * co-residency at the cost of the launch gap.  Either way every wait inside
  * is bounded and a timeout is reported by gpeed_ctx_check. */
 #define GPEED_OPT_FUSED_COOPERATIVE 2
+/* GPEED_OPT_TC_MIN_TOKENS (default 1024): batches of at least this many
+ * tokens run the expert matrices as grouped GEMMs on the tensor cores (fp16
+ * operands, fp32 accumulation; weights decoded from IQ3_XXS on the fly);
+ * smaller batches use the quantised GEMV path (int8 x int16 dot products). */
+#define GPEED_OPT_TC_MIN_TOKENS 3
 GPEED_API int gpeed_ctx_set_option(gpeed_ctx* ctx, int option, int value);
 
 /* Per-stage timing of gpeed_moe_forward (no counterpart in the reference;
