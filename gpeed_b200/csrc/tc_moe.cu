@@ -37,10 +37,11 @@ constexpr int TBN = 256;  // token rows per tile (MMA N)
 constexpr int TBK = 64;   // K per slice (one 128-byte swizzled fp16 row)
 constexpr int TST = 3;    // token/raw stages
 constexpr int TAS = 2;    // decoded weight stages
-constexpr int NDEC = 8;   // decode warps
 constexpr int NEPI = 4;   // epilogue warps
 constexpr int WEPI0 = 2, WDEC0 = 6;
-constexpr int TC_THREADS = 32 * (WDEC0 + NDEC);
+// decode warps: one sub-block per thread per K slice (NM matrices x 128 rows x 2)
+__host__ __device__ constexpr int tc_ndec(int nm) { return 8 * nm; }
+__host__ __device__ constexpr int tc_threads(int nm) { return 32 * (WDEC0 + tc_ndec(nm)); }
 constexpr uint32_t B_TILE = TBN * TBK * 2;  // 32 KB
 constexpr uint32_t A_TILE = TBM * TBK * 2;  // 16 KB
 constexpr uint32_t RAW_QS = TBM * 16;       // 2 sub-blocks x 8 index bytes per row
@@ -58,7 +59,7 @@ __host__ __device__ inline TcSmem tc_smem(int nm, int kin) {
     L.dbytes = (uint32_t)(256 * (kin / 256) + 127) & ~127u;  // 16 groups x 16 * NBLK bytes
     L.d_off = L.a_off + TAS * nm * A_TILE;
     L.grid_off = L.d_off + 2 * nm * L.dbytes;
-    L.bar_off = L.grid_off + 1024;
+    L.bar_off = L.grid_off + 1024 + 4096;  // codebook, then the sign-mask table
     L.total = L.bar_off + 256 + 1024;  // barriers + TMEM slot; 1 KB alignment slack
     return L;
 }
@@ -71,29 +72,34 @@ struct TcMaps {
 };
 
 // One K slice of one weight matrix: thread (r, hf) decodes sub-block 2*(c%4)+hf
-// of block c/4 in row r into the swizzled fp16 tile.
+// of block c/4 in row r into the swizzled fp16 tile.  Per weight pair: the
+// index bytes become floats 2^23 + g by one byte permute each; the weight
+// db*g = fma(db, 2^23 + g, -db*2^23) rounds exactly like the reference's
+// product; the pair is rounded to fp16 together and its signs applied by one
+// XOR with a mask from `sgn` (sign byte -> four fp16-pair masks).
 GP_DEVINL void decode_slice(uint32_t a_tile, const uint8_t* qs, const uint8_t* aux, const uint8_t* dsc,
-                            const uint32_t* grid, int nblk, int c, int r, int hf) {
+                            const uint32_t* grid, const uint4* sgn, int nblk, int c, int r, int hf) {
     const uint2 q = *reinterpret_cast<const uint2*>(qs + r * 16 + hf * 8);
     const uint32_t w = *reinterpret_cast<const uint32_t*>(aux + r * 16 + (c & 1) * 8 + hf * 4);
     const uint16_t dh = *reinterpret_cast<const uint16_t*>(dsc + (r >> 3) * 16 * nblk + (r & 7) * 2 * nblk + 2 * (c >> 2));
     const float db = iq3_db(__half2float(__ushort_as_half(dh)), w);
+    const float ndb = -db * 8388608.0f;  // exact: a power-of-two scaling
     const uint32_t idx[2] = {q.x, q.y};
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
         const uint32_t k7 = (w >> (7 * l)) & 127u;
-        const uint32_t sg = k7 | ((uint32_t)(__popc(k7) & 1) << 7);
+        const uint4 sm = sgn[k7];
         const uint32_t g0 = grid[(idx[l >> 1] >> (16 * (l & 1))) & 0xFF];
         const uint32_t g1 = grid[(idx[l >> 1] >> (16 * (l & 1) + 8)) & 0xFF];
+        const uint32_t msk[4] = {sm.x, sm.y, sm.z, sm.w};
         uint32_t h[4];
 #pragma unroll
-        for (int j = 0; j < 8; j += 2) {
-            const uint32_t ga = ((j < 4 ? g0 : g1) >> (8 * (j & 3))) & 0xFF;
-            const uint32_t gb = ((j + 1 < 4 ? g0 : g1) >> (8 * ((j + 1) & 3))) & 0xFF;
-            const float wa = iq3_weight_f32(db, ga, (sg >> j) & 1u);
-            const float wb = iq3_weight_f32(db, gb, (sg >> (j + 1)) & 1u);
-            const __half2 p = __floats2half2_rn(wa, wb);
-            h[j >> 1] = *reinterpret_cast<const uint32_t*>(&p);
+        for (int p = 0; p < 4; ++p) {
+            const uint32_t gw = p < 2 ? g0 : g1;
+            const float fa = __uint_as_float(prmt(gw, 0x4B000000u, 0x7540u | ((2 * p) & 3)));
+            const float fb = __uint_as_float(prmt(gw, 0x4B000000u, 0x7540u | ((2 * p + 1) & 3)));
+            const __half2 hp = __floats2half2_rn(__fmaf_rn(db, fa, ndb), __fmaf_rn(db, fb, ndb));
+            h[p] = *reinterpret_cast<const uint32_t*>(&hp) ^ msk[p];
         }
         const uint32_t chunk = (uint32_t)(4 * hf + l) ^ (uint32_t)(r & 7);
         asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a_tile + r * 128 + chunk * 16), "r"(h[0]),
@@ -113,8 +119,9 @@ GP_DEVINL void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, i
 }
 
 template <bool GU>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
-    constexpr int NM = GU ? 2 : 1;
+__global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
+    tc_moe_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
+    constexpr int NM = GU ? 2 : 1, NDEC = tc_ndec(NM), TC_THREADS = tc_threads(NM);
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw0 = smem_u32(smem_raw);
     const uint32_t base = (raw0 + 1023u) & ~1023u;
@@ -127,6 +134,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_cons
     const uint32_t d_full = a_empty + 8 * TAS, d_empty = d_full + 16, acc_full = d_empty + 16, acc_empty = acc_full + 16;
     const uint32_t tslot = acc_empty + 16;
     uint32_t* s_grid = reinterpret_cast<uint32_t*>(gbase + L.grid_off);
+    uint4* s_sgn = reinterpret_cast<uint4*>(gbase + L.grid_off + 1024);
     const int nslots = *a.nslots;
     const int ntiles = nslots * a.mt;
 
@@ -142,6 +150,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_cons
         fence_mbar_init();
     }
     for (int i = tid; i < 256; i += TC_THREADS) s_grid[i] = gp_iq3xxs_grid_dev[i];
+    for (int k = tid; k < 128; k += TC_THREADS) {  // 7-bit sign field -> fp16 sign masks per weight pair
+        const uint32_t sg = (uint32_t)k | ((uint32_t)(__popc(k) & 1) << 7);
+        uint32_t m[4];
+        for (int p = 0; p < 4; ++p) m[p] = (((sg >> (2 * p)) & 1u) << 15) | (((sg >> (2 * p + 1)) & 1u) << 31);
+        s_sgn[k] = make_uint4(m[0], m[1], m[2], m[3]);
+    }
     if (warp == 1) tmem_alloc(tslot, 512);
     tc_fence_before();
     __syncthreads();
@@ -225,22 +239,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_cons
             const int row = (t % a.mt) * TBM + 32 * q + lane;
             const int ab = GU ? 0 : (lt & 1);
             const uint32_t ph = GU ? (lt & 1) : ((lt >> 1) & 1);
-            if (!mbar_wait(acc_full + 8 * ab, ph)) { ok = false; break; }
+            if (!mbar_wait_sleepy(acc_full + 8 * ab, ph)) { ok = false; break; }  // a tile takes ~40 us
             tc_fence_after();
             const uint32_t lanebase = tbase + ((uint32_t)(32 * q) << 16);
-            for (int j0 = 0; j0 < TBN && j0 < sd.ntok; j0 += 32) {
-                uint32_t v0[32];
-                tmem_ld32(lanebase + (GU ? 0 : ab * TBN) + j0, v0);
-                if (GU) {
-                    uint32_t v1[32];
-                    tmem_ld32(lanebase + TBN + j0, v1);
+            if (GU) {
+                for (int j0 = 0; j0 < TBN && j0 < sd.ntok; j0 += 16) {
+                    uint32_t v0[16], v1[16];
+                    tmem_ld16(lanebase + j0, v0);
+                    tmem_ld16(lanebase + TBN + j0, v1);
                     __half* h = static_cast<__half*>(a.out);
 #pragma unroll
-                    for (int jj = 0; jj < 32; ++jj)
+                    for (int jj = 0; jj < 16; ++jj)
                         if (j0 + jj < sd.ntok)
                             h[(int64_t)(sd.begin + j0 + jj) * a.nout + row] =
                                 __float2half_rn(silu_clamped(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit));
-                } else {
+                }
+            } else {
+                for (int j0 = 0; j0 < TBN && j0 < sd.ntok; j0 += 32) {
+                    uint32_t v0[32];
+                    tmem_ld32(lanebase + ab * TBN + j0, v0);
                     float* d = static_cast<float*>(a.out);
 #pragma unroll
                     for (int jj = 0; jj < 32; ++jj)
@@ -254,7 +271,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_cons
         if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
     } else {
         // ================= decode =================
-        const int td = tid - 32 * WDEC0, r = td >> 1, hf = td & 1;
+        const int td = tid - 32 * WDEC0, mi = td >> 8, r = (td >> 1) & 127, hf = td & 1;
         int gc = 0;
         bool ok = true;
         for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
@@ -266,13 +283,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_moe_kernel(const __grid_cons
                     ok = false;
                     break;
                 }
-                const uint8_t* sb = gbase + L.stages_off + s * L.stage;
-#pragma unroll
-                for (int mi = 0; mi < NM; ++mi) {
-                    const uint8_t* rq = sb + B_TILE + mi * (RAW_QS + RAW_AUX);
-                    decode_slice(base + L.a_off + (as * NM + mi) * A_TILE, rq, rq + RAW_QS,
-                                 gbase + L.d_off + (db * NM + mi) * L.dbytes, s_grid, nblk, c, r, hf);
-                }
+                const uint8_t* rq = gbase + L.stages_off + s * L.stage + B_TILE + mi * (RAW_QS + RAW_AUX);
+                decode_slice(base + L.a_off + (as * NM + mi) * A_TILE, rq, rq + RAW_QS,
+                             gbase + L.d_off + (db * NM + mi) * L.dbytes, s_grid, s_sgn, nblk, c, r, hf);
                 fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
                 __syncwarp();
                 if (lane == 0) {
@@ -411,7 +424,7 @@ cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t
     auto kern = gu ? tc_moe_kernel<true> : tc_moe_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
-    kern<<<grid, TC_THREADS, L.total, st>>>(m, args);
+    kern<<<grid, tc_threads(gu ? 2 : 1), L.total, st>>>(m, args);
     return cudaGetLastError();
 }
 
