@@ -14,13 +14,16 @@
 //   down pass     A = down tile, B = h rows; epilogue -> D [position][H] fp32,
 //                 then the batched path's combine (model_batch.cpp:257-280)
 //
-// Warp roles (448 threads, one CTA per SM, persistent over the tile list):
+// Warp roles (one CTA per SM, persistent over the tile list):
 //   warp 0     TMA producer: token tile (2-D, 128-byte swizzle) and the raw
 //              IQ3_XXS bytes of the tile (3-D maps over the row-group layout:
 //              index bytes, sign/scale words, per-tile fp16 scales)
 //   warp 1     TMEM allocation; one thread issues the MMAs and commits
 //   warps 2-5  epilogue: TMEM -> registers -> global (one lane quadrant each)
-//   warps 6-13 decode: 2 sub-blocks per thread per matrix per K slice
+//   warps 6+   decode: one sub-block per thread per matrix per K slice
+//              (8 warps per matrix); in the gate/up pass they then join the
+//              epilogue, which splits each lane quadrant's columns
+// 704 threads for gate/up, 448 for down.
 // No cluster, no multicast.  Every wait is bounded; a timeout sets a status bit.
 #include <cuda_fp16.h>
 
@@ -48,8 +51,9 @@ constexpr uint32_t RAW_QS = TBM * 16;       // 2 sub-blocks x 8 index bytes per 
 constexpr uint32_t RAW_AUX = TBM * 16;      // 4 sign/scale words per row (2 used)
 
 struct TcSmem {
-    uint32_t stage, stages_off, a_off, d_off, dbytes, grid_off, bar_off, total;
+    uint32_t stage, stages_off, a_off, d_off, dbytes, grid_off, gcopy_shift, bar_off, total;
 };
+constexpr uint32_t TC_SMEM_MAX = 227u * 1024u;
 
 __host__ __device__ inline TcSmem tc_smem(int nm, int kin) {
     TcSmem L;
@@ -59,7 +63,9 @@ __host__ __device__ inline TcSmem tc_smem(int nm, int kin) {
     L.dbytes = (uint32_t)(256 * (kin / 256) + 127) & ~127u;  // 16 groups x 16 * NBLK bytes
     L.d_off = L.a_off + TAS * nm * A_TILE;
     L.grid_off = L.d_off + 2 * nm * L.dbytes;
-    L.bar_off = L.grid_off + 1024 + 4096;  // codebook, then the sign-mask table
+    // interleaved codebook copies: 16 where they fit, else 8 (1 KB each)
+    L.gcopy_shift = L.grid_off + 16 * 1024 + 256 + 1024 <= TC_SMEM_MAX ? 4 : 3;
+    L.bar_off = L.grid_off + (1024u << L.gcopy_shift);
     L.total = L.bar_off + 256 + 1024;  // barriers + TMEM slot; 1 KB alignment slack
     return L;
 }
@@ -76,9 +82,16 @@ struct TcMaps {
 // index bytes become floats 2^23 + g by one byte permute each; the weight
 // db*g = fma(db, 2^23 + g, -db*2^23) rounds exactly like the reference's
 // product; the pair is rounded to fp16 together and its signs applied by one
-// XOR with a mask from `sgn` (sign byte -> four fp16-pair masks).
+// XOR.
+//
+// Shared-memory bandwidth bounds this decode, not arithmetic: the tensor core
+// reads its operands from the same shared memory.  So the sign masks are
+// built in registers (a multiply spreads the 8 sign bits onto byte msbs, a
+// sign-replicating byte permute widens each onto an fp16 sign bit), and the
+// codebook is read from one of 2^gsh interleaved copies (copy = lane mod
+// 2^gsh), so a warp's random lookups cost at most 32 >> gsh wavefronts.
 GP_DEVINL void decode_slice(uint32_t a_tile, const uint8_t* qs, const uint8_t* aux, const uint8_t* dsc,
-                            const uint32_t* grid, const uint4* sgn, int nblk, int c, int r, int hf) {
+                            const uint32_t* grid, uint32_t gsh, uint32_t gcopy, int nblk, int c, int r, int hf) {
     const uint2 q = *reinterpret_cast<const uint2*>(qs + r * 16 + hf * 8);
     const uint32_t w = *reinterpret_cast<const uint32_t*>(aux + r * 16 + (c & 1) * 8 + hf * 4);
     const uint16_t dh = *reinterpret_cast<const uint16_t*>(dsc + (r >> 3) * 16 * nblk + (r & 7) * 2 * nblk + 2 * (c >> 2));
@@ -87,11 +100,14 @@ GP_DEVINL void decode_slice(uint32_t a_tile, const uint8_t* qs, const uint8_t* a
     const uint32_t idx[2] = {q.x, q.y};
 #pragma unroll
     for (int l = 0; l < 4; ++l) {
+        // 8 sign bits: the 7-bit field and its parity (the reference's ksigns table)
         const uint32_t k7 = (w >> (7 * l)) & 127u;
-        const uint4 sm = sgn[k7];
-        const uint32_t g0 = grid[(idx[l >> 1] >> (16 * (l & 1))) & 0xFF];
-        const uint32_t g1 = grid[(idx[l >> 1] >> (16 * (l & 1) + 8)) & 0xFF];
-        const uint32_t msk[4] = {sm.x, sm.y, sm.z, sm.w};
+        const uint32_t s8 = k7 | ((uint32_t)(__popc(k7) & 1) << 7);
+        // bit j < 4 of the multiplicand lands on bit 8j+7 (no carries)
+        const uint32_t sl = (s8 & 15u) * 0x10204080u, sh = (s8 >> 4) * 0x10204080u;
+        const uint32_t wd = idx[l >> 1] >> (16 * (l & 1));
+        const uint32_t g0 = grid[((wd & 0xFFu) << gsh) | gcopy];
+        const uint32_t g1 = grid[(((wd >> 8) & 0xFFu) << gsh) | gcopy];
         uint32_t h[4];
 #pragma unroll
         for (int p = 0; p < 4; ++p) {
@@ -99,7 +115,9 @@ GP_DEVINL void decode_slice(uint32_t a_tile, const uint8_t* qs, const uint8_t* a
             const float fa = __uint_as_float(prmt(gw, 0x4B000000u, 0x7540u | ((2 * p) & 3)));
             const float fb = __uint_as_float(prmt(gw, 0x4B000000u, 0x7540u | ((2 * p + 1) & 3)));
             const __half2 hp = __floats2half2_rn(__fmaf_rn(db, fa, ndb), __fmaf_rn(db, fb, ndb));
-            h[p] = *reinterpret_cast<const uint32_t*>(&hp) ^ msk[p];
+            // bytes 1 and 3 <- sign-replicated bytes (2p)%4 and (2p+1)%4 of the spread word
+            const uint32_t m = prmt(p < 2 ? sl : sh, 0u, (p & 1) ? 0xB4A4u : 0x9484u);
+            h[p] = *reinterpret_cast<const uint32_t*>(&hp) ^ (m & 0x80008000u);
         }
         const uint32_t chunk = (uint32_t)(4 * hf + l) ^ (uint32_t)(r & 7);
         asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(a_tile + r * 128 + chunk * 16), "r"(h[0]),
@@ -134,7 +152,6 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
     const uint32_t d_full = a_empty + 8 * TAS, d_empty = d_full + 16, acc_full = d_empty + 16, acc_empty = acc_full + 16;
     const uint32_t tslot = acc_empty + 16;
     uint32_t* s_grid = reinterpret_cast<uint32_t*>(gbase + L.grid_off);
-    uint4* s_sgn = reinterpret_cast<uint4*>(gbase + L.grid_off + 1024);
     const int nslots = *a.nslots;
     const int ntiles = nslots * a.mt;
 
@@ -145,17 +162,11 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
             mbar_init(d_full + 8 * s, 1);
             mbar_init(d_empty + 8 * s, NDEC);
             mbar_init(acc_full + 8 * s, 1);
-            mbar_init(acc_empty + 8 * s, NEPI);
+            mbar_init(acc_empty + 8 * s, GU ? NEPI + NDEC : NEPI);  // the epilogue warps
         }
         fence_mbar_init();
     }
-    for (int i = tid; i < 256; i += TC_THREADS) s_grid[i] = gp_iq3xxs_grid_dev[i];
-    for (int k = tid; k < 128; k += TC_THREADS) {  // 7-bit sign field -> fp16 sign masks per weight pair
-        const uint32_t sg = (uint32_t)k | ((uint32_t)(__popc(k) & 1) << 7);
-        uint32_t m[4];
-        for (int p = 0; p < 4; ++p) m[p] = (((sg >> (2 * p)) & 1u) << 15) | (((sg >> (2 * p + 1)) & 1u) << 31);
-        s_sgn[k] = make_uint4(m[0], m[1], m[2], m[3]);
-    }
+    for (int i = tid; i < (256 << L.gcopy_shift); i += TC_THREADS) s_grid[i] = gp_iq3xxs_grid_dev[i >> L.gcopy_shift];
     if (warp == 1) tmem_alloc(tslot, 512);
     tc_fence_before();
     __syncthreads();
@@ -230,11 +241,46 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
             }
             if (!ok) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
         }
-    } else if (warp < WDEC0) {
-        // ================= epilogue =================
-        const int q = warp & 3;
+    } else {
+        // ================= workers: decode (warps >= WDEC0), then the epilogue =================
+        // The epilogue of a tile is shared by every worker warp of the same TMEM
+        // lane quadrant (warp % 4).  In the gate/up pass the decode warps join
+        // it: that pass has a single accumulator (gate and up fill all 512
+        // TMEM columns), so the MMA waits until the epilogue has read it.
+        constexpr int NEP = GU ? NEPI + NDEC : NEPI;  // epilogue warps
+        constexpr int PER_Q = NEP / 4;                // of them per lane quadrant
+        const int wk = warp - WEPI0, q = warp & 3, kq = wk / 4;
+        const bool decoder = warp >= WDEC0, epi = wk < NEP;
+        const int td = tid - 32 * WDEC0, mi = td >> 8, r = (td >> 1) & 127, hf = td & 1;
+        const uint32_t gsh = L.gcopy_shift, gcopy = (uint32_t)lane & ((1u << gsh) - 1u);
+        int gc = 0;
         bool ok = true;
         for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
+            if (decoder) {
+                const int db = lt & 1;
+                if (!mbar_wait(d_full + 8 * db, (lt >> 1) & 1)) { ok = false; break; }
+                for (int c = 0; c < nk; ++c, ++gc) {
+                    const int s = gc % TST, as = gc % TAS;
+                    if (!mbar_wait(st_full + 8 * s, (gc / TST) & 1) ||
+                        !mbar_wait(a_empty + 8 * as, ((gc / TAS) & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* rq = gbase + L.stages_off + s * L.stage + B_TILE + mi * (RAW_QS + RAW_AUX);
+                    decode_slice(base + L.a_off + (as * NM + mi) * A_TILE, rq, rq + RAW_QS,
+                                 gbase + L.d_off + (db * NM + mi) * L.dbytes, s_grid, gsh, gcopy, nblk, c, r, hf);
+                    fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(a_full + 8 * as);
+                        mbar_arrive(st_empty + 8 * s);
+                    }
+                }
+                __syncwarp();
+                if (!ok) break;
+                if (lane == 0) mbar_arrive(d_empty + 8 * db);
+            }
+            if (!epi) continue;
             const SlotDesc sd = a.slots[t / a.mt];
             const int row = (t % a.mt) * TBM + 32 * q + lane;
             const int ab = GU ? 0 : (lt & 1);
@@ -243,7 +289,7 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
             tc_fence_after();
             const uint32_t lanebase = tbase + ((uint32_t)(32 * q) << 16);
             if (GU) {
-                for (int j0 = 0; j0 < TBN && j0 < sd.ntok; j0 += 16) {
+                for (int j0 = 16 * kq; j0 < TBN && j0 < sd.ntok; j0 += 16 * PER_Q) {
                     uint32_t v0[16], v1[16];
                     tmem_ld16(lanebase + j0, v0);
                     tmem_ld16(lanebase + TBN + j0, v1);
@@ -255,7 +301,7 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                                 __float2half_rn(silu_clamped(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit));
                 }
             } else {
-                for (int j0 = 0; j0 < TBN && j0 < sd.ntok; j0 += 32) {
+                for (int j0 = 32 * kq; j0 < TBN && j0 < sd.ntok; j0 += 32 * PER_Q) {
                     uint32_t v0[32];
                     tmem_ld32(lanebase + ab * TBN + j0, v0);
                     float* d = static_cast<float*>(a.out);
@@ -267,34 +313,6 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
-        }
-        if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
-    } else {
-        // ================= decode =================
-        const int td = tid - 32 * WDEC0, mi = td >> 8, r = (td >> 1) & 127, hf = td & 1;
-        int gc = 0;
-        bool ok = true;
-        for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
-            const int db = lt & 1;
-            if (!mbar_wait(d_full + 8 * db, (lt >> 1) & 1)) { ok = false; break; }
-            for (int c = 0; c < nk; ++c, ++gc) {
-                const int s = gc % TST, as = gc % TAS;
-                if (!mbar_wait(st_full + 8 * s, (gc / TST) & 1) || !mbar_wait(a_empty + 8 * as, ((gc / TAS) & 1) ^ 1)) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t* rq = gbase + L.stages_off + s * L.stage + B_TILE + mi * (RAW_QS + RAW_AUX);
-                decode_slice(base + L.a_off + (as * NM + mi) * A_TILE, rq, rq + RAW_QS,
-                             gbase + L.d_off + (db * NM + mi) * L.dbytes, s_grid, s_sgn, nblk, c, r, hf);
-                fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(a_full + 8 * as);
-                    mbar_arrive(st_empty + 8 * s);
-                }
-            }
-            __syncwarp();
-            if (ok && lane == 0) mbar_arrive(d_empty + 8 * db);
         }
         if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
     }
@@ -420,7 +438,7 @@ cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t
     if (!encode_weight_maps(m, 0, w0, weight_rows / 8, kin)) return cudaErrorInvalidValue;
     if (gu && !encode_weight_maps(m, 1, w1, weight_rows / 8, kin)) return cudaErrorInvalidValue;
     const TcSmem L = tc_smem(gu ? 2 : 1, kin);
-    if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
+    if (L.total > TC_SMEM_MAX) return cudaErrorInvalidValue;
     auto kern = gu ? tc_moe_kernel<true> : tc_moe_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
