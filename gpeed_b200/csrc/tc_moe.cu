@@ -34,6 +34,15 @@
 #include "kernels.h"
 #include "tc_common.cuh"
 
+// Timing hooks: no-ops here; a profiling build may define them to accumulate
+// per-role wait and work cycles.
+#ifndef TC_MARK
+#define TC_DECL() ((void)0)
+#define TC_MARK(v) ((void)0)
+#define TC_ACC(i, v) ((void)0)
+#define TC_DUMP(gu, role) ((void)0)
+#endif
+
 namespace gp {
 namespace {
 
@@ -98,9 +107,16 @@ GP_DEVINL uint32_t pair_sign(uint32_t s8) {
 //   fp32  byte permutes build floats 2^23+g; fma(db, 2^23+g, -db*2^23) is the
 //         reference's fp32 product db*g, rounded once to fp16
 // then one LOP3 applies the signs.
+// Codebook word at shared address a (read-only after the kernel's set-up barrier).
+GP_DEVINL uint32_t lds_grid(uint32_t a) {
+    uint32_t v;
+    asm("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+
 template <bool F16>
-GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, float db, const uint32_t* gp,
-                          uint32_t gmul) {
+GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, float db, uint32_t gaddr,
+                          uint32_t gstride) {
     const __half2 dbh = __float2half2_rn(db);
     const __half2 ndbh = __float2half2_rn(-1024.0f * db);
     const float ndb = -db * 8388608.0f;
@@ -111,8 +127,8 @@ GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, f
         const uint32_t k7 = (l == 0 ? w : __umulhi(w, 1u << ((32 - 7 * l) & 31))) & 127u;
         const uint32_t s8 = (uint32_t)__popc(k7) * 128u + k7;
         const uint32_t wd = l < 2 ? q.x : q.y;
-        const uint32_t g0 = gp[prmt(wd, 0u, 0x4440u | (2u * (l & 1))) * gmul];
-        const uint32_t g1 = gp[prmt(wd, 0u, 0x4440u | (2u * (l & 1) + 1u)) * gmul];
+        const uint32_t g0 = lds_grid(prmt(wd, 0u, 0x4440u | (2u * (l & 1))) * gstride + gaddr);
+        const uint32_t g1 = lds_grid(prmt(wd, 0u, 0x4440u | (2u * (l & 1) + 1u)) * gstride + gaddr);
         const uint32_t m[4] = {pair_sign<0>(s8), pair_sign<1>(s8), pair_sign<2>(s8), pair_sign<3>(s8)};
         uint32_t h[4];
 #pragma unroll
@@ -137,26 +153,26 @@ GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, f
 }
 
 // One K slice of one weight matrix: thread (r, hf) decodes sub-block 2*(c%4)+hf
-// of block c/4 in row r into the 128-byte-swizzled fp16 tile.
+// of block c/4 in row r into the 128-byte-swizzled fp16 tile (row_addr = the
+// row in the tile, c0 = its swizzle phase; qp, wp, dp = the thread's index
+// bytes, sign/scale word and fp16 block scale).
 //
-// Shared-memory bandwidth and the integer ALU pipe bound this decode: the
-// tensor core reads its operands from the same shared memory, and the ALU pipe
+// Shared-memory bandwidth and instruction issue bound this decode: the tensor
+// core reads its operands from the same shared memory, and the ALU pipe
 // issues at half the rate of the FMA pipe.  So the sign masks come from
 // multiplies rather than a table, and the codebook is read from one of
-// `gmul` interleaved copies (`gp` = copy lane mod gmul), so that a warp's
-// random lookups cost at most 32 / gmul wavefronts.
-GP_DEVINL void decode_slice(uint32_t a_tile, const uint8_t* qs, const uint8_t* aux, const uint8_t* dsc,
-                            const uint32_t* gp, uint32_t gmul, int nblk, int c, int r, int hf) {
-    const uint2 q = *reinterpret_cast<const uint2*>(qs + r * 16 + hf * 8);
-    const uint32_t w = *reinterpret_cast<const uint32_t*>(aux + r * 16 + (c & 1) * 8 + hf * 4);
-    const uint16_t dh = *reinterpret_cast<const uint16_t*>(dsc + (r >> 3) * 16 * nblk + (r & 7) * 2 * nblk + 2 * (c >> 2));
-    const float db = iq3_db(__half2float(__ushort_as_half(dh)), w);
-    const uint32_t row_addr = a_tile + r * 128, c0 = (uint32_t)(4 * hf) ^ (uint32_t)(r & 7);
+// several interleaved copies (gaddr = this lane's copy, gstride = bytes per
+// entry across copies), so that a warp's random lookups cost few wavefronts.
+GP_DEVINL void decode_slice(uint32_t row_addr, uint32_t c0, const uint8_t* qp, const uint8_t* wp, const uint8_t* dp,
+                            uint32_t gaddr, uint32_t gstride) {
+    const uint2 q = *reinterpret_cast<const uint2*>(qp);
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(wp);
+    const float db = iq3_db(__half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(dp))), w);
     // fp16 intermediates reach 1086*|db|: below 65504 with margin
     if (__builtin_expect(fabsf(db) < 32.0f, 1))
-        decode_sub<true>(row_addr, c0, q, w, db, gp, gmul);
+        decode_sub<true>(row_addr, c0, q, w, db, gaddr, gstride);
     else
-        decode_sub<false>(row_addr, c0, q, w, db, gp, gmul);
+        decode_sub<false>(row_addr, c0, q, w, db, gaddr, gstride);
 }
 
 GP_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -187,6 +203,7 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
     uint32_t* s_grid = reinterpret_cast<uint32_t*>(gbase + L.grid_off);
     const int nslots = *a.nslots;
     const int ntiles = nslots * a.mt;
+    TC_DECL();
 
     if (tid == 0) {
         for (int s = 0; s < TST; ++s) { mbar_init(st_full + 8 * s, 1); mbar_init(st_empty + 8 * s, NDEC + 1); }
@@ -210,19 +227,24 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
         // ================= producer =================
         if (lane == 0) {
             const uint32_t tx = B_TILE + NM * (RAW_QS + RAW_AUX);
+            TC_MARK(t_all);
             int gc = 0;
             for (int t = blockIdx.x, lt = 0; t < ntiles; t += gridDim.x, ++lt) {
                 const SlotDesc sd = a.slots[t / a.mt];
                 const int z0 = (sd.expert * a.nout + (t % a.mt) * TBM) / 8;
                 const int db = lt & 1;
+                TC_MARK(t_de);
                 if (!mbar_wait(d_empty + 8 * db, ((lt >> 1) & 1) ^ 1)) { atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY); break; }
+                TC_ACC(1, t_de);
                 mbar_arrive_expect_tx(d_full + 8 * db, NM * 16 * 16 * nblk);
                 for (int mi = 0; mi < NM; ++mi)
                     tma_load_3d(base + L.d_off + (db * NM + mi) * L.dbytes, &maps.dsc[mi], 0, 0, z0, d_full + 8 * db);
                 bool ok = true;
                 for (int c = 0; c < nk; ++c, ++gc) {
                     const int s = gc % TST;
+                    TC_MARK(t_se);
                     if (!mbar_wait(st_empty + 8 * s, ((gc / TST) & 1) ^ 1)) { ok = false; break; }
+                    TC_ACC(0, t_se);
                     const uint32_t sb = base + L.stages_off + s * L.stage;
                     mbar_arrive_expect_tx(st_full + 8 * s, tx);
                     tma_load_2d(sb, &maps.b, c * TBK, sd.begin, st_full + 8 * s);
@@ -235,10 +257,13 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                 }
                 if (!ok) { atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY); break; }
             }
+            TC_ACC(7, t_all);
+            TC_DUMP(GU, 0);
         }
     } else if (warp == 1) {
         // ================= MMA issue =================
         if (lane == 0) {
+            TC_MARK(t_all);
             int gc = 0;
             bool ok = true;
             for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
@@ -247,14 +272,18 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                 const uint32_t idesc = umma_idesc_f16(TBM, ntok >= TBN ? TBN : (ntok + 15) & ~15, false);
                 const int ab = GU ? 0 : (lt & 1);
                 const uint32_t ph_e = GU ? ((lt & 1) ^ 1) : (((lt >> 1) & 1) ^ 1);
+                TC_MARK(t_ae);
                 if (!mbar_wait(acc_empty + 8 * ab, ph_e)) { ok = false; break; }
+                TC_ACC(0, t_ae);
                 tc_fence_after();
                 for (int c = 0; c < nk; ++c, ++gc) {
                     const int s = gc % TST, as = gc % TAS;
-                    if (!mbar_wait(a_full + 8 * as, (gc / TAS) & 1) || !mbar_wait(st_full + 8 * s, (gc / TST) & 1)) {
-                        ok = false;
-                        break;
-                    }
+                    TC_MARK(t_af);
+                    if (!mbar_wait(a_full + 8 * as, (gc / TAS) & 1)) { ok = false; break; }
+                    TC_ACC(1, t_af);
+                    TC_MARK(t_sf);
+                    if (!mbar_wait(st_full + 8 * s, (gc / TST) & 1)) { ok = false; break; }
+                    TC_ACC(2, t_sf);
                     tc_fence_after();
                     const uint32_t sb = base + L.stages_off + s * L.stage;
 #pragma unroll
@@ -273,6 +302,8 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                 if (ok) umma_commit(acc_full + 8 * ab);
             }
             if (!ok) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+            TC_ACC(7, t_all);
+            TC_DUMP(GU, 1);
         }
     } else {
         // ================= workers: decode (warps >= WDEC0), then the epilogue =================
@@ -285,30 +316,46 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
         const int wk = warp - WEPI0, q = warp & 3, kq = wk / 4;
         const bool decoder = warp >= WDEC0, epi = wk < NEP;
         const int td = tid - 32 * WDEC0, mi = td >> 8, r = (td >> 1) & 127, hf = td & 1;
-        const uint32_t gmul = 1u << L.gcopy_shift;
-        const uint32_t* gp = s_grid + ((uint32_t)lane & (gmul - 1u));
-        int gc = 0;
+        // the decode thread's fixed offsets: its row in the A tile, its bytes in a raw stage
+        const uint32_t gstride = 4u << L.gcopy_shift;
+        const uint32_t gaddr = base + L.grid_off + 4u * ((uint32_t)lane & ((1u << L.gcopy_shift) - 1u));
+        const uint32_t a_row = base + L.a_off + mi * A_TILE + (uint32_t)r * 128u;
+        const uint32_t c0 = (uint32_t)(4 * hf) ^ (uint32_t)(r & 7);
+        const uint8_t* raw_t = gbase + L.stages_off + B_TILE + mi * (RAW_QS + RAW_AUX) + r * 16;
+        const uint8_t* d_t = gbase + L.d_off + mi * L.dbytes + (r >> 3) * 16 * nblk + (r & 7) * 2 * nblk;
+        int s = 0, as = 0;         // stage of the token/raw ring and of the A ring
+        uint32_t sph = 0, aph = 0;  // their phase parities
         bool ok = true;
+        TC_MARK(t_all);
         for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
             if (decoder) {
                 const int db = lt & 1;
+                TC_MARK(t_df);
                 if (!mbar_wait(d_full + 8 * db, (lt >> 1) & 1)) { ok = false; break; }
-                for (int c = 0; c < nk; ++c, ++gc) {
-                    const int s = gc % TST, as = gc % TAS;
-                    if (!mbar_wait(st_full + 8 * s, (gc / TST) & 1) ||
-                        !mbar_wait(a_empty + 8 * as, ((gc / TAS) & 1) ^ 1)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint8_t* rq = gbase + L.stages_off + s * L.stage + B_TILE + mi * (RAW_QS + RAW_AUX);
-                    decode_slice(base + L.a_off + (as * NM + mi) * A_TILE, rq, rq + RAW_QS,
-                                 gbase + L.d_off + (db * NM + mi) * L.dbytes, gp, gmul, nblk, c, r, hf);
+                TC_ACC(0, t_df);
+                const uint8_t* dsc = d_t + db * NM * L.dbytes;
+                for (int c = 0; c < nk; ++c) {
+                    TC_MARK(t_sf);
+                    if (!mbar_wait(st_full + 8 * s, sph)) { ok = false; break; }
+                    TC_ACC(1, t_sf);
+                    TC_MARK(t_ae);
+                    if (!mbar_wait(a_empty + 8 * as, aph ^ 1u)) { ok = false; break; }
+                    TC_ACC(2, t_ae);
+                    TC_MARK(t_dec);
+                    const uint8_t* rq = raw_t + s * L.stage;
+                    decode_slice(a_row + as * (NM * A_TILE), c0, rq + hf * 8, rq + RAW_QS + (c & 1) * 8 + hf * 4,
+                                 dsc + 2 * (c >> 2), gaddr, gstride);
+                    TC_ACC(3, t_dec);
+                    TC_MARK(t_fa);
                     fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(a_full + 8 * as);
                         mbar_arrive(st_empty + 8 * s);
                     }
+                    if (++s == TST) { s = 0; sph ^= 1u; }
+                    if (++as == TAS) { as = 0; aph ^= 1u; }
+                    TC_ACC(4, t_fa);
                 }
                 __syncwarp();
                 if (!ok) break;
@@ -319,7 +366,10 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
             const int row = (t % a.mt) * TBM + 32 * q + lane;
             const int ab = GU ? 0 : (lt & 1);
             const uint32_t ph = GU ? (lt & 1) : ((lt >> 1) & 1);
+            TC_MARK(t_af);
             if (!mbar_wait_sleepy(acc_full + 8 * ab, ph)) { ok = false; break; }  // a tile takes ~40 us
+            TC_ACC(5, t_af);
+            TC_MARK(t_ep);
             tc_fence_after();
             const uint32_t lanebase = tbase + ((uint32_t)(32 * q) << 16);
             if (GU) {
@@ -347,8 +397,11 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(acc_empty + 8 * ab);
+            TC_ACC(6, t_ep);
         }
         if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+        TC_ACC(7, t_all);
+        if (lane == 0 && (warp == WDEC0 || warp == WEPI0)) TC_DUMP(GU, warp == WDEC0 ? 2 : 3);
     }
     tc_fence_before();
     __syncthreads();
