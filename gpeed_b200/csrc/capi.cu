@@ -248,7 +248,8 @@ int ensure_scratch(gpeed_ctx* c, int n, int E, int K, int H, int I) {
     const size_t nk = (size_t)n * K, na = nk + n;
     const size_t max_slots = nk + E + n + 4;  // nt >= 1
     int rc;
-    if ((rc = c->partial.ensure((size_t)n * E))) return rc;
+    const int rs = gp::router_splits(n, H, E);  // logits, then the router's split partial sums
+    if ((rc = c->partial.ensure((size_t)n * E * (rs > 1 ? 1 + rs : 1)))) return rc;
     if ((rc = c->topk_w.ensure(nk))) return rc;
     if ((rc = c->topk_ids.ensure(nk))) return rc;
     if ((rc = c->perm.ensure(na))) return rc;
@@ -723,7 +724,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     }
     mark(0);
 
-    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p};
+    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p,
+                      c->partial.p + (size_t)n * E, c->partial.n - (size_t)n * E};
     GP_CUDA(gp::launch_router(ra, st, false));
     mark(1);
     if (n >= c->tc_min_tokens && s.n_shared && gp::tc_moe_supported(H, I)) {
@@ -825,7 +827,8 @@ int gpeed_moe_route(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, 
     if ((rc = set_device(c))) return rc;
     if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p};
+    gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p,
+                      c->partial.p + (size_t)n * E, c->partial.n - (size_t)n * E};
     GP_CUDA(gp::launch_router(ra, st, false));
     gp::RouteArgs ro{};
     ro.logits = c->partial.p;

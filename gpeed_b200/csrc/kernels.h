@@ -73,8 +73,14 @@ struct RouterArgs {
     int x_bf16;
     int n, H, E;
     float* logits;        // [n][E]
+    // Large batches split K across CTAs: partial sums [split][n][E] go here and
+    // are added in split order.  nullptr (or too small): no split.
+    float* split_scratch;
+    size_t split_floats;
 };
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl);
+// Splits the router GEMM would use for n tokens (scratch = splits * n * E floats when > 1).
+int router_splits(int n, int H, int E);
 
 // Top-k, histogram, stable expert-major permutation and slot list.
 struct RouteArgs {

@@ -85,7 +85,11 @@ __global__ void __launch_bounds__(32 * kRouterWarps) router_kernel(const RouterA
 
 // Large batches: logits as a register-blocked fp32 GEMM.  CTA tile = 128
 // tokens x 32 experts, K in slices of 32 staged in shared memory; each thread
-// accumulates 4 tokens x 4 experts over K in order (deterministic).
+// accumulates 4 tokens x 4 experts over its K range in order.  With
+// gridDim.z = S > 1 CTA z covers K range z of S and writes partial sums to
+// split_scratch[z]; router_split_sum_kernel adds them in order z = 0..S-1
+// (deterministic).  The split gives each SM several CTAs, whose loads hide
+// one another's global-memory latency.
 constexpr int kRgTok = 128, kRgExp = 32, kRgK = 32;
 __global__ void __launch_bounds__(256) router_gemm_kernel(const RouterArgs a) {
     __shared__ __align__(16) float xs[kRgK][kRgTok + 4];
@@ -93,8 +97,10 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const RouterArgs a) {
     pdl_wait();
     const int tid = threadIdx.x, ty = tid >> 3, tx = tid & 7;
     const int t0 = blockIdx.y * kRgTok, e0 = blockIdx.x * kRgExp;
+    const int klen = a.H / (int)gridDim.z, kbeg = (int)blockIdx.z * klen;
+    float* out = gridDim.z == 1 ? a.logits : a.split_scratch + (size_t)blockIdx.z * a.n * a.E;
     float acc[4][4] = {};
-    for (int k0 = 0; k0 < a.H; k0 += kRgK) {
+    for (int k0 = kbeg; k0 < kbeg + klen; k0 += kRgK) {
         // x tile: 128 tokens x 32 k (4 consecutive k per load)
         for (int i = tid; i < kRgTok * kRgK / 4; i += 256) {
             const int t = i / (kRgK / 4), kq = (i % (kRgK / 4)) * 4;
@@ -144,8 +150,19 @@ __global__ void __launch_bounds__(256) router_gemm_kernel(const RouterArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
             const int e = e0 + tx * 4 + j;
-            if (e < a.E) a.logits[(int64_t)t * a.E + e] = acc[i][j];
+            if (e < a.E) out[(int64_t)t * a.E + e] = acc[i][j];
         }
+    }
+    pdl_launch_dependents();
+}
+
+__global__ void router_split_sum_kernel(const RouterArgs a, int S) {
+    pdl_wait();
+    const size_t ne = (size_t)a.n * a.E;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < ne; i += (size_t)gridDim.x * blockDim.x) {
+        float v = a.split_scratch[i];
+        for (int z = 1; z < S; ++z) v += a.split_scratch[z * ne + i];
+        a.logits[i] = v;
     }
     pdl_launch_dependents();
 }
@@ -342,36 +359,43 @@ __global__ void __launch_bounds__(256) topk_kernel(const RouteArgs a) {
 }
 
 constexpr int kCombineMaxK = 32;
+constexpr int kCombineThreads = 256;  // one float4 column of one token per thread
+constexpr int kCombineGroup = 8;      // expert rows loaded together (16 B each per thread)
 
-__global__ void combine_kernel(const CombineArgs a) {
+// y[t] = sum_k w[t][k] * D[pos(t,k)] (k in order, fp32 fma) + the shared-expert
+// row.  The K rows are read in groups of 8 independent 16-byte loads per
+// thread, so each SM keeps enough bytes in flight to stream D at HBM rate.
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(const CombineArgs a) {
+    __shared__ int s_pos[kCombineMaxK];
+    __shared__ float s_w[kCombineMaxK];
     pdl_wait();
     const int t = blockIdx.y;
-    const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (threadIdx.x < a.K) {
+        s_pos[threadIdx.x] = a.inv_pos[(int64_t)t * a.K + threadIdx.x];
+        s_w[threadIdx.x] = a.topk_w[(int64_t)t * a.K + threadIdx.x];
+    }
+    __syncthreads();
+    const int j = (blockIdx.x * kCombineThreads + threadIdx.x) * 4;
     if (j >= a.H) return;
-    int pos[kCombineMaxK];
-    float w[kCombineMaxK];
-#pragma unroll
-    for (int k = 0; k < kCombineMaxK; ++k)
-        if (k < a.K) {
-            pos[k] = a.inv_pos[(int64_t)t * a.K + k];
-            w[k] = a.topk_w[(int64_t)t * a.K + k];
-        }
-    float4 d[kCombineMaxK];
-#pragma unroll
-    for (int k = 0; k < kCombineMaxK; ++k)
-        if (k < a.K) d[k] = *reinterpret_cast<const float4*>(a.D + (int64_t)pos[k] * a.H + j);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < a.K; k0 += kCombineGroup) {
+        float4 d[kCombineGroup];
 #pragma unroll
-    for (int k = 0; k < kCombineMaxK; ++k)
-        if (k < a.K) {
-            acc.x = fmaf(w[k], d[k].x, acc.x);
-            acc.y = fmaf(w[k], d[k].y, acc.y);
-            acc.z = fmaf(w[k], d[k].z, acc.z);
-            acc.w = fmaf(w[k], d[k].w, acc.w);
-        }
+        for (int g = 0; g < kCombineGroup; ++g)
+            if (k0 + g < a.K) d[g] = __ldcs(reinterpret_cast<const float4*>(a.D + (int64_t)s_pos[k0 + g] * a.H + j));
+#pragma unroll
+        for (int g = 0; g < kCombineGroup; ++g)
+            if (k0 + g < a.K) {
+                const float w = s_w[k0 + g];
+                acc.x = fmaf(w, d[g].x, acc.x);
+                acc.y = fmaf(w, d[g].y, acc.y);
+                acc.z = fmaf(w, d[g].z, acc.z);
+                acc.w = fmaf(w, d[g].w, acc.w);
+            }
+    }
     if (a.with_shared) {
         const float* sh = a.D_shared ? a.D_shared + (int64_t)t * a.H : a.D + ((int64_t)a.n * a.K + t) * a.H;
-        const float4 s = *reinterpret_cast<const float4*>(sh + j);
+        const float4 s = __ldcs(reinterpret_cast<const float4*>(sh + j));
         acc.x += s.x;
         acc.y += s.y;
         acc.z += s.z;
@@ -400,13 +424,26 @@ size_t route_smem_bytes(int n, int E, int K) {
     return (2 * E * nw + ((size_t)n * K <= kCacheIds ? (size_t)n * K : 0)) * sizeof(uint32_t);
 }
 
+int router_splits(int n, int H, int E) {
+    if (n < 64 || H % kRgK) return 1;
+    const int tiles = ((E + kRgExp - 1) / kRgExp) * ((n + kRgTok - 1) / kRgTok);
+    int S = 1;  // about four CTAs per SM of 148, each K range a whole number of slices
+    while (S < 8 && tiles * S * 2 <= 148 * 5 && H % (2 * S * kRgK) == 0) S *= 2;
+    return S;
+}
+
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl) {
     if (a.H % 4 || a.H > 4 * 256 * kRouterMaxVec) return cudaErrorInvalidValue;
     if (a.n >= 64 && a.H % kRgK == 0) {
+        int S = router_splits(a.n, a.H, a.E);
+        if (S > 1 && (!a.split_scratch || a.split_floats < (size_t)S * a.n * a.E)) S = 1;
         cudaLaunchAttribute attr[1];
-        cudaLaunchConfig_t cfg = make_cfg(dim3((a.E + kRgExp - 1) / kRgExp, (a.n + kRgTok - 1) / kRgTok), dim3(256), 0,
-                                          st, pdl, attr);
-        return cudaLaunchKernelEx(&cfg, router_gemm_kernel, a);
+        cudaLaunchConfig_t cfg = make_cfg(dim3((a.E + kRgExp - 1) / kRgExp, (a.n + kRgTok - 1) / kRgTok, S),
+                                          dim3(256), 0, st, pdl, attr);
+        cudaError_t e = cudaLaunchKernelEx(&cfg, router_gemm_kernel, a);
+        if (e != cudaSuccess || S == 1) return e;
+        cudaLaunchConfig_t cfg2 = make_cfg(dim3(148 * 4), dim3(256), 0, st, pdl, attr);
+        return cudaLaunchKernelEx(&cfg2, router_split_sum_kernel, a, S);
     }
     const int ntc = (a.n + kRouterTok - 1) / kRouterTok;
     cudaLaunchAttribute attr[1];
@@ -439,7 +476,8 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl) {
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl) {
     if (a.H % 4 || a.K > kCombineMaxK) return cudaErrorInvalidValue;
     cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg = make_cfg(dim3((a.H / 4 + 127) / 128, a.n), dim3(128), 0, st, pdl, attr);
+    cudaLaunchConfig_t cfg = make_cfg(dim3((a.H / 4 + kCombineThreads - 1) / kCombineThreads, a.n),
+                                      dim3(kCombineThreads), 0, st, pdl, attr);
     return cudaLaunchKernelEx(&cfg, combine_kernel, a);
 }
 
