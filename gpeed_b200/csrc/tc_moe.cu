@@ -17,15 +17,18 @@
 //                 then the batched path's combine (model_batch.cpp:257-280)
 //
 // Warp roles (one CTA per SM, persistent over the tile list):
-//   warp 0     TMA producer: token tile (2-D, 128-byte swizzle) and the raw
-//              IQ3_XXS bytes of the tile (3-D maps over the row-group layout:
-//              index bytes, sign/scale words, per-tile fp16 scales)
+//   warp 0     TMA producer of the token tiles (2-D, 128-byte swizzle), a ring
+//              freed by the MMA
 //   warp 1     TMEM allocation; one thread issues the MMAs and commits
-//   warps 2-5  epilogue: TMEM -> registers -> global (one lane quadrant each)
-//   warps 6+   decode: one sub-block per thread per matrix per K slice
+//   warp 2     TMA producer of the raw IQ3_XXS bytes (3-D maps over the
+//              row-group layout: index bytes, sign/scale words, per-tile fp16
+//              scales), a deeper ring freed by the decoders, so that weight
+//              loads run several K slices ahead of the decode
+//   warps 3-6  epilogue: TMEM -> registers -> global (one lane quadrant each)
+//   warps 7+   decode: one sub-block per thread per matrix per K slice
 //              (8 warps per matrix); in the gate/up pass they then join the
 //              epilogue, which splits each lane quadrant's columns
-// 704 threads for gate/up, 448 for down.
+// 736 threads for gate/up, 480 for down.
 // No cluster, no multicast.  Every wait is bounded; a timeout sets a status bit.
 #include <cuda_fp16.h>
 
@@ -49,35 +52,45 @@ namespace {
 constexpr int TBM = 128;  // weight rows per tile (MMA M = TMEM lanes)
 constexpr int TBN = 256;  // token rows per tile (MMA N)
 constexpr int TBK = 64;   // K per slice (one 128-byte swizzled fp16 row)
-constexpr int TST = 3;    // token/raw stages
 constexpr int TAS = 2;    // decoded weight stages
 constexpr int NEPI = 4;   // epilogue warps
-constexpr int WEPI0 = 2, WDEC0 = 6;
-// decode warps: one sub-block per thread per K slice (NM matrices x 128 rows x 2)
-__host__ __device__ constexpr int tc_ndec(int nm) { return 8 * nm; }
-__host__ __device__ constexpr int tc_threads(int nm) { return 32 * (WDEC0 + tc_ndec(nm)); }
+// warp roles: token-tile producer, MMA issue, raw-weight producer, epilogue, decode
+constexpr int WPB = 0, WMMA = 1, WPR = 2, WEPI0 = 3, WDEC0 = 7;
 constexpr uint32_t B_TILE = TBN * TBK * 2;  // 32 KB
 constexpr uint32_t A_TILE = TBM * TBK * 2;  // 16 KB
 constexpr uint32_t RAW_QS = TBM * 16;       // 2 sub-blocks x 8 index bytes per row
 constexpr uint32_t RAW_AUX = TBM * 16;      // 4 sign/scale words per row (2 used)
-
-struct TcSmem {
-    uint32_t stage, stages_off, a_off, d_off, dbytes, grid_off, gcopy_shift, bar_off, total;
-};
 constexpr uint32_t TC_SMEM_MAX = 227u * 1024u;
 
-__host__ __device__ inline TcSmem tc_smem(int nm, int kin) {
+// Per pass: the token ring is freed by the MMA, the raw-weight ring by the
+// decoders as soon as they have decoded a slice, so raw loads run several
+// slices ahead of the decode.  Depths and codebook copies fill shared memory.
+template <bool GU>
+struct TcCfg {
+    static constexpr int NM = GU ? 2 : 1;   // weight matrices (gate and up, or down)
+    static constexpr int TSB = GU ? 3 : 4;  // token-tile stages
+    static constexpr int TSR = GU ? 4 : 6;  // raw-weight stages
+    static constexpr int GSH = GU ? 3 : 4;  // log2 of the interleaved codebook copies
+    static constexpr int NDEC = 8 * NM;     // decode warps: one sub-block per thread per slice
+    static constexpr int THREADS = 32 * (WDEC0 + NDEC);
+};
+
+struct TcSmem {
+    uint32_t raw_stage, raw_off, a_off, d_off, dbytes, grid_off, bar_off, total;
+};
+
+template <bool GU>
+__host__ __device__ inline TcSmem tc_smem(int kin) {
+    using C = TcCfg<GU>;
     TcSmem L;
-    L.stage = B_TILE + nm * (RAW_QS + RAW_AUX);
-    L.stages_off = 0;
-    L.a_off = TST * L.stage;
+    L.raw_stage = C::NM * (RAW_QS + RAW_AUX);
+    L.raw_off = C::TSB * B_TILE;  // token tiles first (1024-byte aligned for the swizzle)
+    L.a_off = L.raw_off + C::TSR * L.raw_stage;
     L.dbytes = (uint32_t)(256 * (kin / 256) + 127) & ~127u;  // 16 groups x 16 * NBLK bytes
-    L.d_off = L.a_off + TAS * nm * A_TILE;
-    L.grid_off = L.d_off + 2 * nm * L.dbytes;
-    // interleaved codebook copies: 16 where they fit, else 8 (1 KB each)
-    L.gcopy_shift = L.grid_off + 16 * 1024 + 256 + 1024 <= TC_SMEM_MAX ? 4 : 3;
-    L.bar_off = L.grid_off + (1024u << L.gcopy_shift);
-    L.total = L.bar_off + 256 + 1024;  // barriers + TMEM slot; 1 KB alignment slack
+    L.d_off = L.a_off + TAS * C::NM * A_TILE;
+    L.grid_off = L.d_off + 2 * C::NM * L.dbytes;
+    L.bar_off = L.grid_off + (1024u << C::GSH);
+    L.total = L.bar_off + 512 + 1024;  // barriers + TMEM slot; 1 KB alignment slack
     return L;
 }
 
@@ -186,27 +199,29 @@ GP_DEVINL void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, i
 }
 
 template <bool GU>
-__global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
+__global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
     tc_moe_kernel(const __grid_constant__ TcMaps maps, const TcArgs a) {
-    constexpr int NM = GU ? 2 : 1, NDEC = tc_ndec(NM), TC_THREADS = tc_threads(NM);
+    using C = TcCfg<GU>;
+    constexpr int NM = C::NM, NDEC = C::NDEC, TSB = C::TSB, TSR = C::TSR;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw0 = smem_u32(smem_raw);
     const uint32_t base = (raw0 + 1023u) & ~1023u;
     uint8_t* gbase = smem_raw + (base - raw0);
-    const TcSmem L = tc_smem(NM, a.kin);
+    const TcSmem L = tc_smem<GU>(a.kin);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nblk = a.kin / 256, nk = a.kin / TBK;
     const uint32_t bar = base + L.bar_off;
-    const uint32_t st_full = bar, st_empty = bar + 8 * TST, a_full = st_empty + 8 * TST, a_empty = a_full + 8 * TAS;
+    const uint32_t sb_full = bar, sb_empty = sb_full + 8 * TSB, sr_full = sb_empty + 8 * TSB;
+    const uint32_t sr_empty = sr_full + 8 * TSR, a_full = sr_empty + 8 * TSR, a_empty = a_full + 8 * TAS;
     const uint32_t d_full = a_empty + 8 * TAS, d_empty = d_full + 16, acc_full = d_empty + 16, acc_empty = acc_full + 16;
     const uint32_t tslot = acc_empty + 16;
-    uint32_t* s_grid = reinterpret_cast<uint32_t*>(gbase + L.grid_off);
     const int nslots = *a.nslots;
     const int ntiles = nslots * a.mt;
     TC_DECL();
 
     if (tid == 0) {
-        for (int s = 0; s < TST; ++s) { mbar_init(st_full + 8 * s, 1); mbar_init(st_empty + 8 * s, NDEC + 1); }
+        for (int s = 0; s < TSB; ++s) { mbar_init(sb_full + 8 * s, 1); mbar_init(sb_empty + 8 * s, 1); }
+        for (int s = 0; s < TSR; ++s) { mbar_init(sr_full + 8 * s, 1); mbar_init(sr_empty + 8 * s, NDEC); }
         for (int s = 0; s < TAS; ++s) { mbar_init(a_full + 8 * s, NDEC); mbar_init(a_empty + 8 * s, 1); }
         for (int s = 0; s < 2; ++s) {
             mbar_init(d_full + 8 * s, 1);
@@ -216,55 +231,80 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
         }
         fence_mbar_init();
     }
-    for (int i = tid; i < (256 << L.gcopy_shift); i += TC_THREADS) s_grid[i] = gp_iq3xxs_grid_dev[i >> L.gcopy_shift];
-    if (warp == 1) tmem_alloc(tslot, 512);
+    {
+        uint32_t* s_grid = reinterpret_cast<uint32_t*>(gbase + L.grid_off);
+        for (int i = tid; i < (256 << C::GSH); i += C::THREADS) s_grid[i] = gp_iq3xxs_grid_dev[i >> C::GSH];
+    }
+    if (warp == WMMA) tmem_alloc(tslot, 512);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tbase = *reinterpret_cast<volatile uint32_t*>(gbase + (tslot - base));
 
-    if (warp == 0) {
-        // ================= producer =================
+    if (warp == WPB) {
+        // ================= token-tile producer =================
         if (lane == 0) {
-            const uint32_t tx = B_TILE + NM * (RAW_QS + RAW_AUX);
             TC_MARK(t_all);
-            int gc = 0;
-            for (int t = blockIdx.x, lt = 0; t < ntiles; t += gridDim.x, ++lt) {
+            int sb = 0;
+            uint32_t bph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                const int row0 = a.slots[t / a.mt].begin;
+                for (int c = 0; c < nk; ++c) {
+                    TC_MARK(t_se);
+                    if (!mbar_wait(sb_empty + 8 * sb, bph ^ 1u)) { ok = false; break; }
+                    TC_ACC(0, t_se);
+                    mbar_arrive_expect_tx(sb_full + 8 * sb, B_TILE);
+                    tma_load_2d(base + sb * B_TILE, &maps.b, c * TBK, row0, sb_full + 8 * sb);
+                    if (++sb == TSB) { sb = 0; bph ^= 1u; }
+                }
+            }
+            if (!ok) atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
+            TC_ACC(7, t_all);
+            TC_DUMP(GU, 0);
+        }
+    } else if (warp == WPR) {
+        // ================= raw-weight producer: per-tile scales, then per-slice bytes =================
+        if (lane == 0) {
+            TC_MARK(t_all);
+            int sr = 0;
+            uint32_t rph = 0;
+            bool ok = true;
+            for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
                 const SlotDesc sd = a.slots[t / a.mt];
                 const int z0 = (sd.expert * a.nout + (t % a.mt) * TBM) / 8;
                 const int db = lt & 1;
                 TC_MARK(t_de);
-                if (!mbar_wait(d_empty + 8 * db, ((lt >> 1) & 1) ^ 1)) { atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY); break; }
+                if (!mbar_wait(d_empty + 8 * db, ((lt >> 1) & 1) ^ 1)) { ok = false; break; }
                 TC_ACC(1, t_de);
                 mbar_arrive_expect_tx(d_full + 8 * db, NM * 16 * 16 * nblk);
                 for (int mi = 0; mi < NM; ++mi)
                     tma_load_3d(base + L.d_off + (db * NM + mi) * L.dbytes, &maps.dsc[mi], 0, 0, z0, d_full + 8 * db);
-                bool ok = true;
-                for (int c = 0; c < nk; ++c, ++gc) {
-                    const int s = gc % TST;
-                    TC_MARK(t_se);
-                    if (!mbar_wait(st_empty + 8 * s, ((gc / TST) & 1) ^ 1)) { ok = false; break; }
-                    TC_ACC(0, t_se);
-                    const uint32_t sb = base + L.stages_off + s * L.stage;
-                    mbar_arrive_expect_tx(st_full + 8 * s, tx);
-                    tma_load_2d(sb, &maps.b, c * TBK, sd.begin, st_full + 8 * s);
+                for (int c = 0; c < nk; ++c) {
+                    TC_MARK(t_re);
+                    if (!mbar_wait(sr_empty + 8 * sr, rph ^ 1u)) { ok = false; break; }
+                    TC_ACC(2, t_re);
+                    const uint32_t rb = base + L.raw_off + sr * L.raw_stage;
+                    mbar_arrive_expect_tx(sr_full + 8 * sr, L.raw_stage);
                     for (int mi = 0; mi < NM; ++mi) {
-                        const uint32_t rq = sb + B_TILE + mi * (RAW_QS + RAW_AUX);
-                        tma_load_3d(rq, &maps.qs[mi], 64 * (c >> 2) + 16 * (c & 3), 0, z0, st_full + 8 * s);
+                        const uint32_t rq = rb + mi * (RAW_QS + RAW_AUX);
+                        tma_load_3d(rq, &maps.qs[mi], 64 * (c >> 2) + 16 * (c & 3), 0, z0, sr_full + 8 * sr);
                         tma_load_3d(rq + RAW_QS, &maps.aux[mi], 32 * (c >> 2) + 16 * ((c & 3) >> 1), 0, z0,
-                                    st_full + 8 * s);
+                                    sr_full + 8 * sr);
                     }
+                    if (++sr == TSR) { sr = 0; rph ^= 1u; }
                 }
-                if (!ok) { atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY); break; }
             }
-            TC_ACC(7, t_all);
+            if (!ok) atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
+            TC_ACC(6, t_all);
             TC_DUMP(GU, 0);
         }
-    } else if (warp == 1) {
+    } else if (warp == WMMA) {
         // ================= MMA issue =================
         if (lane == 0) {
             TC_MARK(t_all);
-            int gc = 0;
+            int sb = 0, as = 0;
+            uint32_t bph = 0, aph = 0;
             bool ok = true;
             for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
                 // N follows the slot's rows (multiple of 16, as M = 128 requires)
@@ -276,19 +316,18 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                 if (!mbar_wait(acc_empty + 8 * ab, ph_e)) { ok = false; break; }
                 TC_ACC(0, t_ae);
                 tc_fence_after();
-                for (int c = 0; c < nk; ++c, ++gc) {
-                    const int s = gc % TST, as = gc % TAS;
+                for (int c = 0; c < nk; ++c) {
                     TC_MARK(t_af);
-                    if (!mbar_wait(a_full + 8 * as, (gc / TAS) & 1)) { ok = false; break; }
+                    if (!mbar_wait(a_full + 8 * as, aph)) { ok = false; break; }
                     TC_ACC(1, t_af);
                     TC_MARK(t_sf);
-                    if (!mbar_wait(st_full + 8 * s, (gc / TST) & 1)) { ok = false; break; }
+                    if (!mbar_wait(sb_full + 8 * sb, bph)) { ok = false; break; }
                     TC_ACC(2, t_sf);
                     tc_fence_after();
-                    const uint32_t sb = base + L.stages_off + s * L.stage;
+                    const uint32_t bt = base + sb * B_TILE;
 #pragma unroll
                     for (int kk = 0; kk < TBK / 16; ++kk) {
-                        const uint64_t bdesc = umma_desc_sw128(sb + kk * 32);
+                        const uint64_t bdesc = umma_desc_sw128(bt + kk * 32);
 #pragma unroll
                         for (int mi = 0; mi < NM; ++mi) {
                             const uint32_t at = base + L.a_off + (as * NM + mi) * A_TILE;
@@ -297,7 +336,9 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                         }
                     }
                     umma_commit(a_empty + 8 * as);
-                    umma_commit(st_empty + 8 * s);
+                    umma_commit(sb_empty + 8 * sb);
+                    if (++sb == TSB) { sb = 0; bph ^= 1u; }
+                    if (++as == TAS) { as = 0; aph ^= 1u; }
                 }
                 if (ok) umma_commit(acc_full + 8 * ab);
             }
@@ -317,14 +358,14 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
         const bool decoder = warp >= WDEC0, epi = wk < NEP;
         const int td = tid - 32 * WDEC0, mi = td >> 8, r = (td >> 1) & 127, hf = td & 1;
         // the decode thread's fixed offsets: its row in the A tile, its bytes in a raw stage
-        const uint32_t gstride = 4u << L.gcopy_shift;
-        const uint32_t gaddr = base + L.grid_off + 4u * ((uint32_t)lane & ((1u << L.gcopy_shift) - 1u));
+        const uint32_t gstride = 4u << C::GSH;
+        const uint32_t gaddr = base + L.grid_off + 4u * ((uint32_t)lane & ((1u << C::GSH) - 1u));
         const uint32_t a_row = base + L.a_off + mi * A_TILE + (uint32_t)r * 128u;
         const uint32_t c0 = (uint32_t)(4 * hf) ^ (uint32_t)(r & 7);
-        const uint8_t* raw_t = gbase + L.stages_off + B_TILE + mi * (RAW_QS + RAW_AUX) + r * 16;
+        const uint8_t* raw_t = gbase + L.raw_off + mi * (RAW_QS + RAW_AUX) + r * 16;
         const uint8_t* d_t = gbase + L.d_off + mi * L.dbytes + (r >> 3) * 16 * nblk + (r & 7) * 2 * nblk;
-        int s = 0, as = 0;         // stage of the token/raw ring and of the A ring
-        uint32_t sph = 0, aph = 0;  // their phase parities
+        int sr = 0, as = 0;         // stage of the raw ring and of the A ring
+        uint32_t rph = 0, aph = 0;  // their phase parities
         bool ok = true;
         TC_MARK(t_all);
         for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
@@ -336,13 +377,13 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                 const uint8_t* dsc = d_t + db * NM * L.dbytes;
                 for (int c = 0; c < nk; ++c) {
                     TC_MARK(t_sf);
-                    if (!mbar_wait(st_full + 8 * s, sph)) { ok = false; break; }
+                    if (!mbar_wait(sr_full + 8 * sr, rph)) { ok = false; break; }
                     TC_ACC(1, t_sf);
                     TC_MARK(t_ae);
                     if (!mbar_wait(a_empty + 8 * as, aph ^ 1u)) { ok = false; break; }
                     TC_ACC(2, t_ae);
                     TC_MARK(t_dec);
-                    const uint8_t* rq = raw_t + s * L.stage;
+                    const uint8_t* rq = raw_t + sr * L.raw_stage;
                     decode_slice(a_row + as * (NM * A_TILE), c0, rq + hf * 8, rq + RAW_QS + (c & 1) * 8 + hf * 4,
                                  dsc + 2 * (c >> 2), gaddr, gstride);
                     TC_ACC(3, t_dec);
@@ -351,9 +392,9 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(a_full + 8 * as);
-                        mbar_arrive(st_empty + 8 * s);
+                        mbar_arrive(sr_empty + 8 * sr);
                     }
-                    if (++s == TST) { s = 0; sph ^= 1u; }
+                    if (++sr == TSR) { sr = 0; rph ^= 1u; }
                     if (++as == TAS) { as = 0; aph ^= 1u; }
                     TC_ACC(4, t_fa);
                 }
@@ -405,7 +446,7 @@ __global__ void __launch_bounds__(tc_threads(GU ? 2 : 1), 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == WMMA) {
         tc_fence_after();
         tmem_dealloc(tbase, 512);
     }
@@ -500,7 +541,10 @@ bool encode_weight_maps(TcMaps& m, int mi, const uint8_t* w, int64_t groups, int
 
 }  // namespace
 
-bool tc_moe_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0 && H % TBM == 0 && I % TBM == 0 && H <= 8192 && I <= 8192; }
+bool tc_moe_supported(int H, int I) {
+    return H % 256 == 0 && I % 256 == 0 && H % TBM == 0 && I % TBM == 0 && tc_smem<true>(H).total <= TC_SMEM_MAX &&
+           tc_smem<false>(I).total <= TC_SMEM_MAX;
+}
 
 cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
                                cudaStream_t st) {
@@ -524,12 +568,12 @@ cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t
     }
     if (!encode_weight_maps(m, 0, w0, weight_rows / 8, kin)) return cudaErrorInvalidValue;
     if (gu && !encode_weight_maps(m, 1, w1, weight_rows / 8, kin)) return cudaErrorInvalidValue;
-    const TcSmem L = tc_smem(gu ? 2 : 1, kin);
+    const TcSmem L = gu ? tc_smem<true>(kin) : tc_smem<false>(kin);
     if (L.total > TC_SMEM_MAX) return cudaErrorInvalidValue;
     auto kern = gu ? tc_moe_kernel<true> : tc_moe_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
-    kern<<<grid, tc_threads(gu ? 2 : 1), L.total, st>>>(m, args);
+    kern<<<grid, gu ? TcCfg<true>::THREADS : TcCfg<false>::THREADS, L.total, st>>>(m, args);
     return cudaGetLastError();
 }
 
