@@ -55,6 +55,9 @@ struct Layer {
     // then the shared expert at local index e_cnt (all of them unless the
     // layer was loaded for expert parallelism)
     int e_lo = 0, e_cnt = 0;
+    // the router weights split into bf16 hi/lo/lo2 rows for the tensor-core router (or nullptr)
+    uint16_t* router_split = nullptr;
+    int router_nb = 0;
 };
 
 template <typename T>
@@ -220,6 +223,7 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int e_lo, int
     if (it != c->layers.end()) {
         Layer& old = it->second;
         cudaFree(old.router); cudaFree(old.corr); cudaFree(old.gate); cudaFree(old.up); cudaFree(old.down);
+        cudaFree(old.router_split);
         c->layers.erase(it);
     }
     Layer L;
@@ -231,6 +235,12 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int e_lo, int
     const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
     GP_CUDA(cudaMalloc(&L.router, sizeof(float) * E * H));
     GP_CUDA(cudaMemcpy(L.router, router_w, sizeof(float) * E * H, kind));
+    L.router_nb = gp::router_tc_nb(E, H);
+    if (L.router_nb) {
+        GP_CUDA(cudaMalloc(&L.router_split, sizeof(uint16_t) * 2 * L.router_nb * H));
+        GP_CUDA(gp::launch_router_split(L.router, E, H, L.router_nb, L.router_split, 0));
+        GP_CUDA(cudaStreamSynchronize(0));
+    }
     if (corr) {
         GP_CUDA(cudaMalloc(&L.corr, sizeof(float) * E));
         GP_CUDA(cudaMemcpy(L.corr, corr, sizeof(float) * E, kind));
@@ -388,6 +398,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& kv : c->layers) {
         Layer& L = kv.second;
         cudaFree(L.router); cudaFree(L.corr); cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down);
+        cudaFree(L.router_split);
     }
     c->partial.release(); c->topk_w.release(); c->h.release(); c->D.release(); c->mvout.release();
     c->topk_ids.release(); c->perm.release(); c->inv_pos.release(); c->counts.release(); c->nslots.release();
@@ -725,7 +736,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     mark(0);
 
     gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p,
-                      c->partial.p + (size_t)n * E, c->partial.n - (size_t)n * E};
+                      c->partial.p + (size_t)n * E, c->partial.n - (size_t)n * E, L.router_split, L.router_nb, c->status};
     GP_CUDA(gp::launch_router(ra, st, false));
     mark(1);
     if (n >= c->tc_min_tokens && s.n_shared && gp::tc_moe_supported(H, I)) {
@@ -828,7 +839,7 @@ int gpeed_moe_route(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, 
     if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
     gp::RouterArgs ra{L.router, x, x_dtype == GPEED_DTYPE_BF16, n, H, E, c->partial.p,
-                      c->partial.p + (size_t)n * E, c->partial.n - (size_t)n * E};
+                      c->partial.p + (size_t)n * E, c->partial.n - (size_t)n * E, L.router_split, L.router_nb, c->status};
     GP_CUDA(gp::launch_router(ra, st, false));
     gp::RouteArgs ro{};
     ro.logits = c->partial.p;

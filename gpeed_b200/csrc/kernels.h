@@ -77,10 +77,20 @@ struct RouterArgs {
     // are added in split order.  nullptr (or too small): no split.
     float* split_scratch;
     size_t split_floats;
+    // bf16 x and these split weights (router_tc.cu): tensor-core logits.
+    const uint16_t* wsplit;  // [hi; lo; lo2; 0] bf16 rows, 2 * wsplit_nb rows of H, or nullptr
+    int wsplit_nb;
+    uint32_t* status;        // device status word (the tensor-core kernel's wait timeouts)
 };
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl);
-// Splits the router GEMM would use for n tokens (scratch = splits * n * E floats when > 1).
+// Largest K split the router may use for n tokens (scratch = splits * n * E floats when > 1).
 int router_splits(int n, int H, int E);
+// Tensor-core router (router_tc.cu): rows per MMA half for E experts (0: unsupported),
+// K splits for n tokens, the load-time weight split, and the launch.
+int router_tc_nb(int E, int H);
+int router_tc_splits(int n, int H);
+cudaError_t launch_router_split(const float* R, int E, int H, int nb, uint16_t* out, cudaStream_t st);
+cudaError_t launch_router_tc(const RouterArgs& a, int S, float* out, cudaStream_t st, bool pdl);
 
 // Top-k, histogram, stable expert-major permutation and slot list.
 struct RouteArgs {

@@ -424,7 +424,7 @@ size_t route_smem_bytes(int n, int E, int K) {
     return (2 * E * nw + ((size_t)n * K <= kCacheIds ? (size_t)n * K : 0)) * sizeof(uint32_t);
 }
 
-int router_splits(int n, int H, int E) {
+int router_gemm_splits(int n, int H, int E) {
     if (n < 64 || H % kRgK) return 1;
     const int tiles = ((E + kRgExp - 1) / kRgExp) * ((n + kRgTok - 1) / kRgTok);
     int S = 1;  // about four CTAs per SM of 148, each K range a whole number of slices
@@ -432,10 +432,28 @@ int router_splits(int n, int H, int E) {
     return S;
 }
 
+int router_splits(int n, int H, int E) {
+    const int tc = router_tc_nb(E, H) ? router_tc_splits(n, H) : 1;
+    return max(router_gemm_splits(n, H, E), tc);
+}
+
+constexpr int kRouterTcMinTokens = 256;
+
 cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl) {
     if (a.H % 4 || a.H > 4 * 256 * kRouterMaxVec) return cudaErrorInvalidValue;
+    if (a.n >= kRouterTcMinTokens && a.x_bf16 && a.wsplit && a.wsplit_nb > 0 && a.status &&
+        reinterpret_cast<uintptr_t>(a.x) % 16 == 0) {
+        // bf16 activations: tensor cores on the exactly split weights
+        int S = router_tc_splits(a.n, a.H);
+        if (S > 1 && (!a.split_scratch || a.split_floats < (size_t)S * a.n * a.E)) S = 1;
+        cudaError_t e = launch_router_tc(a, S, S > 1 ? a.split_scratch : a.logits, st, pdl);
+        if (e != cudaSuccess || S == 1) return e;
+        cudaLaunchAttribute attr[1];
+        cudaLaunchConfig_t cfg2 = make_cfg(dim3(148 * 4), dim3(256), 0, st, pdl, attr);
+        return cudaLaunchKernelEx(&cfg2, router_split_sum_kernel, a, S);
+    }
     if (a.n >= 64 && a.H % kRgK == 0) {
-        int S = router_splits(a.n, a.H, a.E);
+        int S = router_gemm_splits(a.n, a.H, a.E);
         if (S > 1 && (!a.split_scratch || a.split_floats < (size_t)S * a.n * a.E)) S = 1;
         cudaLaunchAttribute attr[1];
         cudaLaunchConfig_t cfg = make_cfg(dim3((a.E + kRgExp - 1) / kRgExp, (a.n + kRgTok - 1) / kRgTok, S),

@@ -87,6 +87,33 @@ GP_DEVINL void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, u
         : "memory");
 }
 
+// ---- tensor maps (host) -----------------------------------------------------
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn tmap_encoder() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+inline bool encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+    EncodeTiledFn fn = tmap_encoder();
+    if (!fn) return false;
+    const cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Byte offset of element (row, k) (2-byte elements) inside a K-major,
 // 128-byte-swizzled tile whose rows hold 64 elements: 16-byte chunk index
 // XOR (row % 8).

@@ -484,31 +484,6 @@ __global__ void gather_cast_kernel(const void* x, int x_bf16, const int* perm, i
     }
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encoder() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<EncodeTiledFn>(p);
-    }
-    return fn;
-}
-
-bool encode(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
-            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
-    EncodeTiledFn fn = encoder();
-    if (!fn) return false;
-    const cuuint32_t es[3] = {1, 1, 1};
-    return fn(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // Maps for one repacked IQ3_XXS matrix of `groups` 8-row groups, kin inputs.
 bool encode_weight_maps(TcMaps& m, int mi, const uint8_t* w, int64_t groups, int kin) {
     const int nblk = kin / 256;
