@@ -229,7 +229,7 @@ GP_DEVINL void topk_token(const RouteArgs& a, int t, int lane, int* s_ids) {
     }
 }
 
-// Dynamic shared memory: bitmap [E][nw] + word prefix [E][nw] (nw = ceil(n/32))
+// Dynamic shared memory: bitmap [E][ns] + word prefix [E][ns] (ns = ceil(n/32) rounded up to odd)
 // + cached top-k ids [n*K] when n*K <= kCacheIds.
 constexpr int kCacheIds = 8192;
 
@@ -245,11 +245,13 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
         if (tid == 0) { atomicOr(a.status, GP_DEV_BAD_SHAPE); *a.nslots = 0; }
         return;
     }
-    const int nw = (n + 31) / 32;
+    // per-expert token bitmaps, rows padded to an odd word count so that one
+    // token word of different experts falls in different banks
+    const int nw = (n + 31) / 32, ns = nw | 1;
     uint32_t* bitmap = dsm;
-    uint32_t* wpref = dsm + E * nw;
-    int* s_ids = (!a.topk_ready && n * K <= kCacheIds) ? reinterpret_cast<int*>(dsm + 2 * E * nw) : nullptr;
-    for (int i = tid; i < E * nw; i += kRouteThreads) bitmap[i] = 0;
+    uint32_t* wpref = dsm + E * ns;
+    int* s_ids = (!a.topk_ready && n * K <= kCacheIds) ? reinterpret_cast<int*>(dsm + 2 * E * ns) : nullptr;
+    for (int i = tid; i < E * ns; i += kRouteThreads) bitmap[i] = 0;
     for (int e = tid; e < E; e += kRouteThreads) s_cnt[e] = 0;
     __syncthreads();
 
@@ -264,7 +266,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
         const int t = i / K;
         const int e = s_ids ? s_ids[i] : a.topk_ids[i];
         atomicAdd(&s_cnt[e], 1);
-        atomicOr(&bitmap[e * nw + (t >> 5)], 1u << (t & 31));
+        atomicOr(&bitmap[e * ns + (t >> 5)], 1u << (t & 31));
     }
     __syncthreads();
 
@@ -292,8 +294,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
     for (int e = tid; e < E; e += kRouteThreads) {
         uint32_t acc = 0;
         for (int w = 0; w < nw; ++w) {
-            wpref[e * nw + w] = acc;
-            acc += __popc(bitmap[e * nw + w]);
+            wpref[e * ns + w] = acc;
+            acc += __popc(bitmap[e * ns + w]);
         }
     }
     __syncthreads();
@@ -303,8 +305,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const RouteArgs a)
     for (int i = tid; i < nk; i += kRouteThreads) {
         const int t = i / K;
         const int e = s_ids ? s_ids[i] : a.topk_ids[i];
-        const uint32_t below = bitmap[e * nw + (t >> 5)] & ((1u << (t & 31)) - 1u);
-        const int p = s_ptr[e] + (int)wpref[e * nw + (t >> 5)] + __popc(below);
+        const uint32_t below = bitmap[e * ns + (t >> 5)] & ((1u << (t & 31)) - 1u);
+        const int p = s_ptr[e] + (int)wpref[e * ns + (t >> 5)] + __popc(below);
         a.perm_tok[p] = t;
         a.inv_pos[i] = p;
     }
@@ -420,8 +422,8 @@ cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st,
 }  // namespace
 
 size_t route_smem_bytes(int n, int E, int K) {
-    const size_t nw = (n + 31) / 32;
-    return (2 * E * nw + ((size_t)n * K <= kCacheIds ? (size_t)n * K : 0)) * sizeof(uint32_t);
+    const size_t ns = ((n + 31) / 32) | 1;  // bitmap row stride (odd)
+    return (2 * E * ns + ((size_t)n * K <= kCacheIds ? (size_t)n * K : 0)) * sizeof(uint32_t);
 }
 
 int router_gemm_splits(int n, int H, int E) {

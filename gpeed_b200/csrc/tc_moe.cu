@@ -452,35 +452,38 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
     }
 }
 
-// Casts token rows to fp16 in expert-sorted order: xp[p] = x[perm[p]].
-__global__ void gather_cast_kernel(const void* x, int x_bf16, const int* perm, int npos, int H, __half* xp) {
+// Casts token rows to fp16 in expert-sorted order: xp[p] = x[perm[p]].  One
+// CTA per row at a time, 16-byte loads and stores.
+__global__ void __launch_bounds__(128) gather_cast_kernel(const void* x, int x_bf16, const int* perm, int npos, int H,
+                                                          __half* xp) {
     const int qpr = H / 8;  // 8 elements per thread step
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < (int64_t)npos * qpr;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int p = (int)(i / qpr), q = (int)(i % qpr);
-        const int64_t src = (int64_t)perm[p] * H + q * 8;
-        float v[8];
-        if (x_bf16) {
-            const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + src);
-            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    for (int p = blockIdx.x; p < npos; p += gridDim.x) {
+        const int64_t src = (int64_t)perm[p] * H;
+        uint4* dst = reinterpret_cast<uint4*>(xp + (int64_t)p * H);
+        for (int q = threadIdx.x; q < qpr; q += blockDim.x) {
+            float v[8];
+            if (x_bf16) {
+                const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + src + q * 8);
+                const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                v[2 * j] = __uint_as_float(w[j] << 16);
-                v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+                for (int j = 0; j < 4; ++j) {
+                    v[2 * j] = __uint_as_float(w[j] << 16);
+                    v[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+                }
+            } else {
+                const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src + q * 8);
+                const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src + q * 8 + 4);
+                v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
             }
-        } else {
-            const float4 a = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src);
-            const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src + 4);
-            v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+            uint4 o;
+            __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
+            __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
+            o.x = *reinterpret_cast<uint32_t*>(&h0);
+            o.y = *reinterpret_cast<uint32_t*>(&h1);
+            o.z = *reinterpret_cast<uint32_t*>(&h2);
+            o.w = *reinterpret_cast<uint32_t*>(&h3);
+            dst[q] = o;
         }
-        uint4 o;
-        __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
-        __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
-        o.x = *reinterpret_cast<uint32_t*>(&h0);
-        o.y = *reinterpret_cast<uint32_t*>(&h1);
-        o.z = *reinterpret_cast<uint32_t*>(&h2);
-        o.w = *reinterpret_cast<uint32_t*>(&h3);
-        *reinterpret_cast<uint4*>(xp + (int64_t)p * H + q * 8) = o;
     }
 }
 
@@ -524,7 +527,7 @@ bool tc_moe_supported(int H, int I) {
 cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
                                cudaStream_t st) {
     if (npos <= 0) return cudaSuccess;
-    gather_cast_kernel<<<148 * 8, 256, 0, st>>>(x, x_bf16, perm, npos, H, reinterpret_cast<__half*>(xp));
+    gather_cast_kernel<<<148 * 16, 128, 0, st>>>(x, x_bf16, perm, npos, H, reinterpret_cast<__half*>(xp));
     return cudaGetLastError();
 }
 
