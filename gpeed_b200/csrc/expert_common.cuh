@@ -42,6 +42,15 @@ GP_DEVINL float silu_clamped(float g, float u, float lim) {
     return gi / (1.0f + expf(-gi)) * ui;
 }
 
+// The same, for results rounded to fp16 right after (the tensor-core path's h):
+// hardware exp2 and reciprocal approximations, a few fp32 ulps, far below the
+// fp16 rounding that follows.
+GP_DEVINL __half silu_clamped_h(float g, float u, float lim) {
+    const float gi = fminf(g, lim);
+    const float ui = fminf(fmaxf(u, -lim), lim);
+    return __float2half_rn(__fdividef(gi, 1.0f + __expf(-gi)) * ui);
+}
+
 // Sum of M per-lane values across the warp, sharing shuffles between values:
 // each butterfly level keeps half of the remaining values (the half picked by
 // the lane bit) and adds the partner's other half.  Afterwards lane l holds

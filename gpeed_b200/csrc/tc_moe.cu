@@ -69,8 +69,8 @@ template <bool GU>
 struct TcCfg {
     static constexpr int NM = GU ? 2 : 1;   // weight matrices (gate and up, or down)
     static constexpr int TSB = GU ? 3 : 4;  // token-tile stages
-    static constexpr int TSR = GU ? 4 : 6;  // raw-weight stages
-    static constexpr int GSH = GU ? 3 : 4;  // log2 of the interleaved codebook copies
+    static constexpr int TSR = GU ? 3 : 6;  // raw-weight stages
+    static constexpr int GSH = 4;           // log2 of the interleaved codebook copies
     static constexpr int NDEC = 8 * NM;     // decode warps: one sub-block per thread per slice
     static constexpr int THREADS = 32 * (WDEC0 + NDEC);
 };
@@ -423,7 +423,7 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
                     for (int jj = 0; jj < 16; ++jj)
                         if (j0 + jj < sd.ntok)
                             h[(int64_t)(sd.begin + j0 + jj) * a.nout + row] =
-                                __float2half_rn(silu_clamped(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit));
+                                silu_clamped_h(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit);
                 }
             } else {
                 for (int j0 = 32 * kq; j0 < TBN && j0 < sd.ntok; j0 += 32 * PER_Q) {
