@@ -740,7 +740,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     GP_CUDA(gp::launch_router(ra, st, false));
     mark(1);
     if (n >= c->tc_min_tokens && s.n_shared && gp::tc_moe_supported(H, I)) {
-        // experts on tensor cores: slots of <= 256 rows per expert, fp16 operands
+        // experts on tensor cores: slots of <= 224 rows per expert, fp16 operands
         const int npos = n * K + n;
         if ((rc = c->xp.ensure((size_t)npos * H))) return rc;
         gp::RouteArgs ro{};
@@ -752,7 +752,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         ro.K = K;
         ro.routed_scale = s.routed_scale;
         ro.norm_topk = s.norm_topk;
-        ro.nt = 256;
+        ro.nt = gp::tc_moe_slot_tokens();
         ro.with_shared = 1;
         ro.expert_lo = 0;
         ro.expert_hi = E;

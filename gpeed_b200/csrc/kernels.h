@@ -168,6 +168,8 @@ struct TcArgs {
     void* out;              // gate/up: fp16 h [position][nout]; down: fp32 D [position][nout]
     uint32_t* status;
 };
+// Tokens per expert slot of the tensor-core path (the MMA N bound).
+int tc_moe_slot_tokens();
 bool tc_moe_supported(int H, int I);
 cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
                                cudaStream_t st);

@@ -50,13 +50,13 @@ namespace gp {
 namespace {
 
 constexpr int TBM = 128;  // weight rows per tile (MMA M = TMEM lanes)
-constexpr int TBN = 256;  // token rows per tile (MMA N)
+constexpr int TBN = 224;  // token rows per slot (MMA N <= 224: two accumulators + A stages fit TMEM)
 constexpr int TBK = 64;   // K per slice (one 128-byte swizzled fp16 row)
 constexpr int TAS = 2;    // decoded weight stages
 constexpr int NEPI = 4;   // epilogue warps
 // warp roles: token-tile producer, MMA issue, raw-weight producer, epilogue, decode
 constexpr int WPB = 0, WMMA = 1, WPR = 2, WEPI0 = 3, WDEC0 = 7;
-constexpr uint32_t B_TILE = TBN * TBK * 2;  // 32 KB
+constexpr uint32_t B_TILE = TBN * TBK * 2;  // 28 KB
 constexpr uint32_t A_TILE = TBM * TBK * 2;  // 16 KB
 constexpr uint32_t RAW_QS = TBM * 16;       // 2 sub-blocks x 8 index bytes per row
 constexpr uint32_t RAW_AUX = TBM * 16;      // 4 sign/scale words per row (2 used)
@@ -65,15 +65,22 @@ constexpr uint32_t TC_SMEM_MAX = 227u * 1024u;
 // Per pass: the token ring is freed by the MMA, the raw-weight ring by the
 // decoders as soon as they have decoded a slice, so raw loads run several
 // slices ahead of the decode.  Depths and codebook copies fill shared memory.
+// The down pass keeps its decoded weights in tensor memory (TA): its two
+// accumulators take 2 x 224 columns and the two A stages the last 64, so the
+// decoded tile never passes through shared memory.  The gate/up pass needs
+// 2 x 224 columns for one gate and one up accumulator and stages A in shared
+// memory.
 template <bool GU>
 struct TcCfg {
     static constexpr int NM = GU ? 2 : 1;   // weight matrices (gate and up, or down)
-    static constexpr int TSB = GU ? 3 : 4;  // token-tile stages
-    static constexpr int TSR = GU ? 3 : 6;  // raw-weight stages
+    static constexpr bool TA = !GU;         // A operand in tensor memory
+    static constexpr int TSB = GU ? 3 : 5;  // token-tile stages
+    static constexpr int TSR = GU ? 4 : 8;  // raw-weight stages
     static constexpr int GSH = 4;           // log2 of the interleaved codebook copies
     static constexpr int NDEC = 8 * NM;     // decode warps: one sub-block per thread per slice
     static constexpr int THREADS = 32 * (WDEC0 + NDEC);
 };
+constexpr uint32_t TMEM_A_COL = 2 * TBN;  // first column of the A stages (down pass)
 
 struct TcSmem {
     uint32_t raw_stage, raw_off, a_off, d_off, dbytes, grid_off, bar_off, total;
@@ -87,7 +94,7 @@ __host__ __device__ inline TcSmem tc_smem(int kin) {
     L.raw_off = C::TSB * B_TILE;  // token tiles first (1024-byte aligned for the swizzle)
     L.a_off = L.raw_off + C::TSR * L.raw_stage;
     L.dbytes = (uint32_t)(256 * (kin / 256) + 127) & ~127u;  // 16 groups x 16 * NBLK bytes
-    L.d_off = L.a_off + TAS * C::NM * A_TILE;
+    L.d_off = L.a_off + (C::TA ? 0 : TAS * C::NM * A_TILE);
     L.grid_off = L.d_off + 2 * C::NM * L.dbytes;
     L.bar_off = L.grid_off + (1024u << C::GSH);
     L.total = L.bar_off + 512 + 1024;  // barriers + TMEM slot; 1 KB alignment slack
@@ -127,9 +134,11 @@ GP_DEVINL uint32_t lds_grid(uint32_t a) {
     return v;
 }
 
-template <bool F16>
+// TM: the 16 words (weight pairs in K order) go to o[] for a tensor-memory
+// store; otherwise to the swizzled shared-memory row (row_addr, phase c0).
+template <bool F16, bool TM>
 GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, float db, uint32_t gaddr,
-                          uint32_t gstride) {
+                          uint32_t gstride, uint32_t (&o)[16]) {
     const __half2 dbh = __float2half2_rn(db);
     const __half2 ndbh = __float2half2_rn(-1024.0f * db);
     const float ndb = -db * 8388608.0f;
@@ -159,16 +168,19 @@ GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, f
                 v = *reinterpret_cast<const uint32_t*>(&hp);
             }
             h[p] = v ^ (m[p] & 0x80008000u);
+            if (TM) o[4 * l + p] = h[p];
         }
-        asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + ((c0 ^ (uint32_t)l) << 4)),
-                     "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]));
+        if (!TM)
+            asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(row_addr + ((c0 ^ (uint32_t)l) << 4)),
+                         "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3]));
     }
 }
 
 // One K slice of one weight matrix: thread (r, hf) decodes sub-block 2*(c%4)+hf
-// of block c/4 in row r into the 128-byte-swizzled fp16 tile (row_addr = the
-// row in the tile, c0 = its swizzle phase; qp, wp, dp = the thread's index
-// bytes, sign/scale word and fp16 block scale).
+// of block c/4 in row r, into the 128-byte-swizzled fp16 tile (row_addr = the
+// row in the tile, c0 = its swizzle phase) or, with TM, into o[] for tensor
+// memory (qp, wp, dp = the thread's index bytes, sign/scale word and fp16
+// block scale).
 //
 // Shared-memory bandwidth and instruction issue bound this decode: the tensor
 // core reads its operands from the same shared memory, and the ALU pipe
@@ -176,16 +188,17 @@ GP_DEVINL void decode_sub(uint32_t row_addr, uint32_t c0, uint2 q, uint32_t w, f
 // multiplies rather than a table, and the codebook is read from one of
 // several interleaved copies (gaddr = this lane's copy, gstride = bytes per
 // entry across copies), so that a warp's random lookups cost few wavefronts.
+template <bool TM>
 GP_DEVINL void decode_slice(uint32_t row_addr, uint32_t c0, const uint8_t* qp, const uint8_t* wp, const uint8_t* dp,
-                            uint32_t gaddr, uint32_t gstride) {
+                            uint32_t gaddr, uint32_t gstride, uint32_t (&o)[16]) {
     const uint2 q = *reinterpret_cast<const uint2*>(qp);
     const uint32_t w = *reinterpret_cast<const uint32_t*>(wp);
     const float db = iq3_db(__half2float(__ushort_as_half(*reinterpret_cast<const uint16_t*>(dp))), w);
     // fp16 intermediates reach 1086*|db|: below 65504 with margin
     if (__builtin_expect(fabsf(db) < 32.0f, 1))
-        decode_sub<true>(row_addr, c0, q, w, db, gaddr, gstride);
+        decode_sub<true, TM>(row_addr, c0, q, w, db, gaddr, gstride, o);
     else
-        decode_sub<false>(row_addr, c0, q, w, db, gaddr, gstride);
+        decode_sub<false, TM>(row_addr, c0, q, w, db, gaddr, gstride, o);
 }
 
 GP_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
@@ -330,9 +343,13 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
                         const uint64_t bdesc = umma_desc_sw128(bt + kk * 32);
 #pragma unroll
                         for (int mi = 0; mi < NM; ++mi) {
-                            const uint32_t at = base + L.a_off + (as * NM + mi) * A_TILE;
                             const uint32_t dt = tbase + (GU ? mi * TBN : ab * TBN);
-                            umma_f16(dt, umma_desc_sw128(at + kk * 32), bdesc, idesc, (c | kk) != 0);
+                            if (C::TA) {  // K = 16 per MMA: 8 columns of the A stage
+                                umma_f16_ts(dt, tbase + TMEM_A_COL + 32 * as + 8 * kk, bdesc, idesc, (c | kk) != 0);
+                            } else {
+                                const uint32_t at = base + L.a_off + (as * NM + mi) * A_TILE;
+                                umma_f16(dt, umma_desc_sw128(at + kk * 32), bdesc, idesc, (c | kk) != 0);
+                            }
                         }
                     }
                     umma_commit(a_empty + 8 * as);
@@ -356,7 +373,13 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
         constexpr int PER_Q = NEP / 4;                // of them per lane quadrant
         const int wk = warp - WEPI0, q = warp & 3, kq = wk / 4;
         const bool decoder = warp >= WDEC0, epi = wk < NEP;
-        const int td = tid - 32 * WDEC0, mi = td >> 8, r = (td >> 1) & 127, hf = td & 1;
+        // decode thread -> (matrix, row, half).  Tensor-memory A: lane = row, so a
+        // warp takes the 32 rows of its TMEM lane quadrant (warp % 4) and one half.
+        const int td = tid - 32 * WDEC0;
+        const int mi = C::TA ? 0 : td >> 8;
+        const int r = C::TA ? 32 * q + lane : (td >> 1) & 127;
+        const int hf = C::TA ? (td >> 7) & 1 : td & 1;
+        const uint32_t a_tm = tbase + ((uint32_t)(32 * q) << 16) + TMEM_A_COL + 16 * hf;
         // the decode thread's fixed offsets: its row in the A tile, its bytes in a raw stage
         const uint32_t gstride = 4u << C::GSH;
         const uint32_t gaddr = base + L.grid_off + 4u * ((uint32_t)lane & ((1u << C::GSH) - 1u));
@@ -384,11 +407,19 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
                     TC_ACC(2, t_ae);
                     TC_MARK(t_dec);
                     const uint8_t* rq = raw_t + sr * L.raw_stage;
-                    decode_slice(a_row + as * (NM * A_TILE), c0, rq + hf * 8, rq + RAW_QS + (c & 1) * 8 + hf * 4,
-                                 dsc + 2 * (c >> 2), gaddr, gstride);
+                    uint32_t o[16];
+                    if (C::TA) tc_fence_after();  // the MMA that read this stage has completed
+                    decode_slice<C::TA>(a_row + as * (NM * A_TILE), c0, rq + hf * 8,
+                                        rq + RAW_QS + (c & 1) * 8 + hf * 4, dsc + 2 * (c >> 2), gaddr, gstride, o);
                     TC_ACC(3, t_dec);
                     TC_MARK(t_fa);
-                    fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+                    if (C::TA) {
+                        tmem_st16(a_tm + 32 * as, o);
+                        tmem_wait_st();
+                        tc_fence_before();
+                    } else {
+                        fence_proxy_async_smem();  // the tensor core reads these writes through the async proxy
+                    }
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(a_full + 8 * as);
@@ -518,6 +549,8 @@ bool encode_weight_maps(TcMaps& m, int mi, const uint8_t* w, int64_t groups, int
 }
 
 }  // namespace
+
+int tc_moe_slot_tokens() { return TBN; }
 
 bool tc_moe_supported(int H, int I) {
     return H % 256 == 0 && I % 256 == 0 && H % TBM == 0 && I % TBM == 0 && tc_smem<true>(H).total <= TC_SMEM_MAX &&
