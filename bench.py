@@ -468,7 +468,7 @@ def run_prefill(args, rank, local_rank, world):
                                             stage_ms))},
             "roofline": {"bound": "tensor", "achieved": gu_tf, "peak": tf_peak, "unit": "TFLOP/s",
                          "frac": (gu_tf / tf_peak) if gu_tf and tf_peak else None, "traffic": None,
-                         "kernel": "tc_moe_kernel<gate/up> (grouped GEMM, 161 expert slots)",
+                         "kernel": "tc_moe_kernel<gate/up> (grouped GEMM over the expert slot list)",
                          "flops_per_launch": gu_flops, "down_tflops": dn_tf, "peak_source": peak_src},
             "cpu_baseline": cpu,
             "e2e": {"value": n * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": n * H * 2,
@@ -477,6 +477,97 @@ def run_prefill(args, rank, local_rank, world):
             "clocks": clk.summary(),
         }
     del graphs
+    ctx.close()
+    return line
+
+
+def run_prefill_ep(args, rank, local_rank, world):
+    """BASELINE config 4, expert-parallel over the GPUs of one box: each rank
+    holds E/world routed experts (a contiguous range) plus the shared expert and
+    its own 4096-token batch; every step routes the batch, sends each (token,
+    expert) row to its expert's rank and the results back with NCCL all-to-all,
+    runs the received rows and the shared expert through the tensor-core GEMMs
+    and combines.  Weak scaling: tokens per GPU are fixed as N grows."""
+    import torch
+    import torch.distributed as dist
+
+    from gpeed_b200 import Context, MoeConfig
+    from gpeed_b200.ep import CudaExecutor, ExpertParallelLayer
+
+    n = args.tokens
+    torch.cuda.set_device(local_rank)
+    ctx = Context(local_rank)
+    cfg = MoeConfig()
+    L = max(1, min(args.layers, 2))
+    lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+    layers = []
+    for l in range(L):
+        ex = CudaExecutor(ctx, cfg, 500 + l, lo, cnt)
+        ex.synth(router_for(l), None, 1000 + l, 0)
+        layers.append(ExpertParallelLayer(cfg, ex))
+    xs = [tokens(n, 300 + 17 * rank + l).cuda() for l in range(L)]
+
+    for i in range(args.warmup):
+        layers[i % L].forward(xs[i % L])
+    torch.cuda.synchronize()
+    ctx.check()
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        ev0.record()
+        for i in range(args.steps):
+            layers[i % L].forward(xs[i % L])
+        ev1.record()
+        torch.cuda.synchronize()
+        ms_total = ev0.elapsed_time(ev1)
+    dist.barrier()
+    ctx.check()
+    t = torch.tensor([ms_total], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_total = float(t.item())
+    value = world * n * args.steps / (ms_total / 1000.0)
+
+    # end to end: this rank's batch from pinned host memory, y back to the host, every step
+    x_host = tokens(n, 555 + rank).pin_memory()
+    y_host = torch.empty(n, H, dtype=torch.float32).pin_memory()
+    e2e_steps = max(3, args.steps // 4)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        xs[0].copy_(x_host, non_blocking=True)
+        y = layers[0].forward(xs[0])
+        y_host.copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_s = torch.tensor([time.perf_counter() - t0], device="cuda")
+    dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
+    ctx.check()
+
+    _, tf_peak, peak_src = peaks()
+    line = None
+    if rank == 0:
+        gpu_tf = PREFILL_FLOPS_PER_TOKEN * n / (ms_total / args.steps * 1e-3) / 1e12  # per GPU, whole step
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 x f16 -> f32 (tcgen05), IQ3_XXS weights decoded in-kernel",
+            "data": "synthetic",
+            "config": {"workload": f"prefill{n}-ep: MoE layer over {n} tokens per GPU, experts split over the GPUs "
+                                   "(BASELINE config 4)", "hidden": H, "n_experts": E, "top_k": K_TOP, "inter": I,
+                       "n_shared": 1, "quant": "IQ3_XXS", "layer_copies": L, "experts_per_gpu": cnt,
+                       "parallelism": f"ep{world}: NCCL all-to-all dispatch and combine, shared expert replicated"},
+            "roofline": {"bound": "tensor", "achieved": gpu_tf, "peak": tf_peak, "unit": "TFLOP/s",
+                         "frac": gpu_tf / tf_peak if tf_peak else None, "traffic": None,
+                         "kernel": "whole expert-parallel step per GPU (routing, two all-to-alls, grouped GEMMs, "
+                                   "combine)", "flops_per_token": PREFILL_FLOPS_PER_TOKEN, "peak_source": peak_src},
+            "cpu_baseline": None,
+            "e2e": {"value": world * n * e2e_steps / float(e2e_s.item()), "unit": "tokens/s",
+                    "h2d_bytes_per_step": n * H * 2, "d2h_bytes_per_step": n * H * 4},
+            # per step: route 4 (router, split sum, top-k, route), pack 3, experts 2 x 6, combine 1
+            "gpu_launches": 20 * args.steps,
+            "clocks": clk.summary(),
+        }
     ctx.close()
     return line
 
@@ -493,6 +584,8 @@ def main():
     ap.add_argument("--workload", default="decode1", choices=["decode1", "prefill"],
                     help="decode1: BASELINE config 2 (default); prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
+    ap.add_argument("--ep", action="store_true",
+                    help="prefill with the experts split over the GPUs (NCCL all-to-all); needs --gpus >= 2")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local_rank, world = env_rank()
@@ -506,7 +599,12 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local_rank))
-    line = run_prefill(args, rank, local_rank, world) if args.workload == "prefill" else run_gpu(args, rank, local_rank, world)
+    if args.workload == "prefill" and args.ep and world > 1:
+        line = run_prefill_ep(args, rank, local_rank, world)
+    elif args.workload == "prefill":
+        line = run_prefill(args, rank, local_rank, world)
+    else:
+        line = run_gpu(args, rank, local_rank, world)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -101,6 +101,7 @@ struct gpeed_ctx {
     bool fused_cooperative = false;
     int tc_min_tokens = 1024;          // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
+    DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
     DevBuf<unsigned long long> logits, dx;
     DevBuf<uint8_t> hq;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
@@ -261,6 +262,7 @@ int ensure_scratch(gpeed_ctx* c, int n, int E, int K, int H, int I) {
     const int rs = gp::router_splits(n, H, E);  // logits, then the router's split partial sums
     if ((rc = c->partial.ensure((size_t)n * E * (rs > 1 ? 1 + rs : 1)))) return rc;
     if ((rc = c->topk_w.ensure(nk))) return rc;
+    if ((rc = c->route_chunks.ensure(gp::route_chunk_ints(n, K, E) + 1))) return rc;
     if ((rc = c->topk_ids.ensure(nk))) return rc;
     if ((rc = c->perm.ensure(na))) return rc;
     if ((rc = c->inv_pos.ensure(nk))) return rc;
@@ -281,12 +283,6 @@ int expert_pass(gpeed_ctx* c, const Layer& L, const void* x, int x_bf16, gp::Rou
     const gpeed_moe_shape& s = L.shape;
     const int H = s.hidden, I = s.inter, n = ro.n, K = ro.K;
     int rc;
-    Geo ggu, gd;
-    // one slot list serves both expert kernels: its token count must suit both
-    const int nt = nt_for(n);
-    if ((rc = pick_geo(H, 2, nt, I, &ggu))) return rc;
-    if ((rc = pick_geo(I, 1, nt, H, &gd))) return rc;
-    ro.nt = nt;
     ro.perm_tok = c->perm.p;
     ro.inv_pos = c->inv_pos.p;
     ro.counts = c->counts.p;
@@ -294,6 +290,35 @@ int expert_pass(gpeed_ctx* c, const Layer& L, const void* x, int x_bf16, gp::Rou
     ro.max_slots = (int)c->slots.n;
     ro.nslots = c->nslots.p;
     ro.status = c->status;
+    ro.chunk_counts = c->route_chunks.p;
+    ro.chunk_cap = c->route_chunks.n;
+    const int npos = n * K;
+    if (npos >= c->tc_min_tokens && !ro.with_shared && gp::tc_moe_supported(H, I)) {
+        // large batches: grouped GEMMs on the tensor cores over slots of <= 224 rows
+        // (the same kernels as the whole-layer forward; here without the shared expert)
+        ro.nt = gp::tc_moe_slot_tokens();
+        GP_CUDA(gp::launch_route(ro, st, false));
+        if ((rc = c->xp.ensure((size_t)npos * H))) return rc;
+        GP_CUDA(gp::launch_gather_cast(x, x_bf16, c->perm.p, npos, H, c->xp.p, st));
+        mark(2);
+        const int El = L.e_cnt + s.n_shared;
+        uint16_t* h16 = reinterpret_cast<uint16_t*>(c->h.p);  // npos x I fp16 fits the fp32 h scratch
+        gp::TcArgs ga{c->slots.p, c->nslots.p, I / 128, H, I, s.swiglu_limit, h16, c->status};
+        GP_CUDA(gp::launch_tc_moe(true, L.gate, L.up, (int64_t)El * I, c->xp.p, npos, ga, c->num_sms, st));
+        mark(3);
+        gp::TcArgs da{c->slots.p, c->nslots.p, H / 128, I, H, 0.f, c->D.p, c->status};
+        GP_CUDA(gp::launch_tc_moe(false, L.down, nullptr, (int64_t)El * H, h16, npos, da, c->num_sms, st));
+        mark(4);
+        gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, combine_shared, y, d_shared};
+        GP_CUDA(gp::launch_combine(cb, st, false));
+        return GPEED_OK;
+    }
+    Geo ggu, gd;
+    // one slot list serves both expert kernels: its token count must suit both
+    const int nt = nt_for(n);
+    if ((rc = pick_geo(H, 2, nt, I, &ggu))) return rc;
+    if ((rc = pick_geo(I, 1, nt, H, &gd))) return rc;
+    ro.nt = nt;
     GP_CUDA(gp::launch_route(ro, st, !c->prof));
     mark(2);
 
@@ -407,6 +432,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
         if (e) cudaEventDestroy(e);
     c->logits.release();
     c->xp.release();
+    c->route_chunks.release();
     c->dx.release();
     c->hq.release();
     cudaFree(c->sync);
@@ -765,6 +791,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         ro.max_slots = (int)c->slots.n;
         ro.nslots = c->nslots.p;
         ro.status = c->status;
+        ro.chunk_counts = c->route_chunks.p;
+        ro.chunk_cap = c->route_chunks.n;
         GP_CUDA(gp::launch_route(ro, st, false));
         GP_CUDA(gp::launch_gather_cast(x, x_dtype == GPEED_DTYPE_BF16, c->perm.p, npos, H, c->xp.p, st));
         mark(2);
@@ -862,6 +890,8 @@ int gpeed_moe_route(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, 
     ro.max_slots = (int)c->slots.n;
     ro.nslots = c->nslots.p;
     ro.status = c->status;
+    ro.chunk_counts = c->route_chunks.p;
+    ro.chunk_cap = c->route_chunks.n;
     GP_CUDA(gp::launch_route(ro, st, false));
     return GPEED_OK;
 }
@@ -904,6 +934,8 @@ int gpeed_ep_pack(gpeed_ctx* c, int n_experts, int world, int n, int K, const in
     ro.max_slots = (int)c->slots.n;
     ro.nslots = c->nslots.p;
     ro.status = c->status;
+    ro.chunk_counts = c->route_chunks.p;
+    ro.chunk_cap = c->route_chunks.n;
     GP_CUDA(gp::launch_route(ro, st, false));
     GP_CUDA(gp::launch_ep_pack(x, x_dtype == GPEED_DTYPE_BF16, hidden, n, K, topk_ids, slot_of, c->counts.p,
                                n_experts, world, n_experts / world, send_rows, send_ids, rank_counts, st));

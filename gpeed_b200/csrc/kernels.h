@@ -113,8 +113,13 @@ struct RouteArgs {
     int max_slots;
     int* nslots;
     uint32_t* status;
+    // large batches (see route_chunked_floats): per-chunk expert counts, or nullptr
+    int* chunk_counts;
+    size_t chunk_cap;
 };
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl);
+// Ints of RouteArgs::chunk_counts a batch of n tokens x K picks needs (0: not chunked).
+size_t route_chunk_ints(int n, int K, int E);
 size_t route_smem_bytes(int n, int E, int K);
 
 // Y[t] = sum_k w[t][k] * D[inv_pos[t][k]] (+ D[n*K + t] when with_shared).

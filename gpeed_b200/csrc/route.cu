@@ -360,6 +360,156 @@ __global__ void __launch_bounds__(256) topk_kernel(const RouteArgs a) {
     pdl_launch_dependents();
 }
 
+// ---- large batches: stable counting sort over many CTAs ---------------------
+// The single-CTA route_kernel keeps per-expert token bitmaps in shared memory,
+// which stops fitting (and stops being fast) past a few thousand assignments.
+// For those: (1) per-chunk expert histograms, (2) one CTA scans them over
+// chunks and experts into every chunk's starting position per expert and
+// writes counts and the slot list, (3) one warp per chunk walks its
+// assignments in order and places each one after the earlier ones of its
+// expert (ranks within 32 assignments from a warp match), so the permutation
+// is the same stable expert-major order as route_kernel's.
+constexpr int kChunk = 256;          // assignments per chunk (one warp)
+constexpr int kChunkThreshold = 8192;  // assignments from which the chunked sort runs
+
+GP_DEVINL int assignment_expert(const RouteArgs& a, int i) { return a.topk_ids[i]; }
+
+__global__ void __launch_bounds__(256) route_hist_kernel(const RouteArgs a, int nchunks) {
+    __shared__ int hist[kMaxE];
+    pdl_wait();
+    const int nk = a.n * a.K;
+    for (int c = blockIdx.x; c < nchunks; c += gridDim.x) {
+        for (int e = threadIdx.x; e < a.E; e += blockDim.x) hist[e] = 0;
+        __syncthreads();
+        for (int i = c * kChunk + threadIdx.x; i < min(nk, (c + 1) * kChunk); i += blockDim.x) {
+            const int e = assignment_expert(a, i);
+            if (e >= 0 && e < a.E) atomicAdd(&hist[e], 1);
+            else atomicOr(a.status, GP_DEV_BAD_EXPERT);
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < a.E; e += blockDim.x) a.chunk_counts[(size_t)c * a.E + e] = hist[e];
+        __syncthreads();
+    }
+}
+
+// One CTA: chunk_counts[c][e] becomes the position of chunk c's first
+// assignment to expert e; counts, slots and the shared-expert rows as in route_kernel.
+__global__ void __launch_bounds__(kRouteThreads) route_scan_kernel(const RouteArgs a, int nchunks) {
+    __shared__ int s_cnt[kMaxE];
+    __shared__ int s_ptr[kMaxE + 1];
+    __shared__ int s_slot0[kMaxE + 1];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarp = kRouteThreads / 32;
+    const int E = a.E, n = a.n, nk = n * a.K;
+    for (int e = tid; e < E; e += kRouteThreads) {
+        int run = 0;
+        for (int c = 0; c < nchunks; ++c) {
+            const int v = a.chunk_counts[(size_t)c * E + e];
+            a.chunk_counts[(size_t)c * E + e] = run;
+            run += v;
+        }
+        s_cnt[e] = run;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int run = 0, srun = 0;
+        for (int base = 0; base < E; base += 32) {
+            const int e = base + lane;
+            const int c = e < E ? s_cnt[e] : 0;
+            const bool own = e >= a.expert_lo && e < a.expert_hi;
+            const int ns = own ? (c + a.nt - 1) / a.nt : 0;
+            int inc = c, sinc = ns;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, inc, o);
+                const int sv = __shfl_up_sync(0xffffffffu, sinc, o);
+                if (lane >= o) { inc += v; sinc += sv; }
+            }
+            if (e < E) { s_ptr[e] = run + inc - c; s_slot0[e] = srun + sinc - ns; }
+            run += __shfl_sync(0xffffffffu, inc, 31);
+            srun += __shfl_sync(0xffffffffu, sinc, 31);
+        }
+        if (lane == 0) { s_ptr[E] = run; s_slot0[E] = srun; }
+    }
+    __syncthreads();
+    for (int e = tid; e < E; e += kRouteThreads) {
+        a.counts[e] = s_cnt[e];
+        for (int c = 0; c < nchunks; ++c) a.chunk_counts[(size_t)c * E + e] += s_ptr[e];
+    }
+    for (int e = warp; e < E; e += nwarp) {
+        if (e < a.expert_lo || e >= a.expert_hi) continue;
+        const int c = s_cnt[e];
+        for (int i = lane; i * a.nt < c; i += 32) {
+            const int sidx = s_slot0[e] + i;
+            if (sidx < a.max_slots) {
+                SlotDesc sd;
+                sd.expert = e;
+                sd.begin = s_ptr[e] + i * a.nt;
+                sd.ntok = min(a.nt, c - i * a.nt);
+                sd.pad = 0;
+                a.slots[sidx] = sd;
+            }
+        }
+    }
+    int total = s_slot0[E];
+    if (a.with_shared) {
+        for (int t = tid; t < n; t += kRouteThreads) a.perm_tok[nk + t] = t;
+        const int ns = (n + a.nt - 1) / a.nt;
+        for (int i = tid; i < ns; i += kRouteThreads) {
+            const int sidx = total + i;
+            if (sidx < a.max_slots) {
+                SlotDesc sd;
+                sd.expert = E;  // the shared expert is stored after the routed ones
+                sd.begin = nk + i * a.nt;
+                sd.ntok = min(a.nt, n - i * a.nt);
+                sd.pad = 0;
+                a.slots[sidx] = sd;
+            }
+        }
+        total += ns;
+    }
+    if (tid == 0) {
+        if (total > a.max_slots) { atomicOr(a.status, GP_DEV_BAD_SHAPE); total = a.max_slots; }
+        *a.nslots = total;
+    }
+}
+
+// One warp per chunk, its assignments in order: stable positions.
+__global__ void __launch_bounds__(256) route_scatter_kernel(const RouteArgs a, int nchunks) {
+    __shared__ int cnt[8][kMaxE];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = blockIdx.x * 8 + warp;
+    const int E = a.E, nk = a.n * a.K;
+    if (c >= nchunks) return;
+    for (int e = lane; e < E; e += 32) cnt[warp][e] = a.chunk_counts[(size_t)c * E + e];
+    __syncwarp();
+    for (int i0 = c * kChunk; i0 < min(nk, (c + 1) * kChunk); i0 += 32) {
+        const int i = i0 + lane;
+        const bool live = i < min(nk, (c + 1) * kChunk);
+        int e = live ? assignment_expert(a, i) : -1;
+        if (e >= E) e = -1;
+        const unsigned same = __match_any_sync(0xffffffffu, e);
+        const int leader = __ffs(same) - 1;
+        int b = (lane == leader && e >= 0) ? cnt[warp][e] : 0;
+        b = __shfl_sync(0xffffffffu, b, leader);
+        const int p = b + __popc(same & ((1u << lane) - 1u));
+        __syncwarp();
+        if (lane == leader && e >= 0) cnt[warp][e] = b + __popc(same);
+        __syncwarp();
+        if (live && e >= 0) {
+            a.perm_tok[p] = i / a.K;
+            a.inv_pos[i] = p;
+        } else if (live) {
+            a.inv_pos[i] = 0;  // a bad id (status already set): keep later reads in bounds
+        }
+    }
+}
+
+size_t route_chunk_ints_impl(int n, int K, int E) {
+    const int nk = n * K;
+    if (nk < kChunkThreshold) return 0;
+    return (size_t)((nk + kChunk - 1) / kChunk) * E;
+}
+
 constexpr int kCombineMaxK = 32;
 constexpr int kCombineThreads = 256;  // one float4 column of one token per thread
 constexpr int kCombineGroup = 8;      // expert rows loaded together (16 B each per thread)
@@ -471,8 +621,29 @@ cudaError_t launch_router(const RouterArgs& a, cudaStream_t st, bool pdl) {
     return cudaLaunchKernelEx(&cfg, router_kernel, a);
 }
 
+size_t route_chunk_ints(int n, int K, int E) { return route_chunk_ints_impl(n, K, E); }
+
 cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl) {
     if (a.E > kMaxE || a.K > 32 || a.K > a.E || a.nt < 1) return cudaErrorInvalidValue;
+    const size_t need = route_chunk_ints_impl(a.n, a.K, a.E);
+    if (need && a.chunk_counts && a.chunk_cap >= need) {
+        // large batches: top-k on many CTAs (unless given), then the chunked stable sort
+        cudaLaunchAttribute attr[1];
+        RouteArgs b = a;
+        if (!a.topk_ready) {
+            cudaLaunchConfig_t cfg = make_cfg(dim3(min(1184, (a.n + 7) / 8)), dim3(256), 0, st, pdl, attr);
+            cudaError_t e = cudaLaunchKernelEx(&cfg, topk_kernel, a);
+            if (e != cudaSuccess) return e;
+            b.topk_ready = 1;
+        }
+        const int nchunks = (a.n * a.K + kChunk - 1) / kChunk;
+        cudaLaunchConfig_t c1 = make_cfg(dim3(min(nchunks, 148 * 4)), dim3(256), 0, st, pdl, attr);
+        cudaError_t e = cudaLaunchKernelEx(&c1, route_hist_kernel, b, nchunks);
+        if (e != cudaSuccess) return e;
+        route_scan_kernel<<<1, kRouteThreads, 0, st>>>(b, nchunks);
+        route_scatter_kernel<<<(nchunks + 7) / 8, 256, 0, st>>>(b, nchunks);
+        return cudaGetLastError();
+    }
     const size_t smem = route_smem_bytes(a.n, a.E, a.K);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
     static size_t configured = 0;

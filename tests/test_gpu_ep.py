@@ -70,6 +70,38 @@ def test_ep_device_steps_emulated_two_ranks():
         ctx.close()
 
 
+def test_ep_experts_step_tensor_core_path():
+    """The experts step of an expert-range layer at prefill sizes (2048 rows for
+    its 80 experts, then 1024 rows of the shared expert) runs the tensor-core
+    GEMMs; it must agree with the same step on the GEMV path within the layer
+    tolerance."""
+    from gpeed_b200 import _capi
+    ctx = Context(0)
+    try:
+        cfg = MoeConfig()
+        lo, cnt = ExpertParallelLayer.expert_range(cfg, 1, 2)
+        ex = CudaExecutor(ctx, cfg, 320, lo, cnt)
+        ex.synth(_router(cfg), None, SEED, S0)
+        rng = np.random.default_rng(11)
+        outs = {}
+        for name, m, ids in (("routed", 2048, rng.integers(lo, lo + cnt, 2048)),
+                             ("shared", 1024, np.full(1024, cfg.n_experts))):
+            rows = _tokens(cfg, m).cuda()
+            idt = torch.from_numpy(ids.astype(np.int32)).cuda()
+            y_tc = ex.experts(rows, idt)
+            ctx.check()
+            ctx.set_option(_capi.OPT_TC_MIN_TOKENS, 1 << 30)
+            try:
+                y_gemv = ex.experts(rows, idt)
+                ctx.check()
+            finally:
+                ctx.set_option(_capi.OPT_TC_MIN_TOKENS, 1024)
+            outs[name] = rel_l2(y_tc.cpu().numpy(), y_gemv.cpu().numpy())
+        assert outs["routed"] < 1e-3 and outs["shared"] < 1e-3, outs
+    finally:
+        ctx.close()
+
+
 def _free_port():
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
