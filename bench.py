@@ -11,6 +11,11 @@ steps never find their 85 MB of weights in the 126 MB L2.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl gpeed|reference]
 
+Other workloads: --workload ragged64 (config 3: 64 tokens, Zipf-skewed expert
+loads, quantised GEMV path), --workload prefill (config 4: 4096 tokens,
+tensor-core grouped GEMMs; with --ep and N >= 2 GPUs the experts are split over
+the GPUs with NCCL all-to-all dispatch and combine).
+
 N > 1 (launched by torchrun): every rank runs its own replica of the layer
 stack on its GPU (weak scaling, no data-path collective); value sums tokens
 over ranks and divides by the slowest rank's time.
@@ -481,6 +486,135 @@ def run_prefill(args, rank, local_rank, world):
     return line
 
 
+def zipf_bias(seed):
+    """Selection bias that skews expert loads toward Zipf(s=1.1):
+    b_e = 0.25 * (-1.1 * ln(rank_e + 1)) over a seeded random ranking."""
+    rank = np.random.default_rng(seed).permutation(E)
+    return (0.25 * (-1.1 * np.log(rank + 1.0))).astype(np.float32)
+
+
+def run_ragged(args, rank, local_rank, world):
+    """a ragged continuous-batching decode step, 64 tokens
+    through one MoE layer with Zipf-skewed expert loads (quantised GEMV path).
+    Steps cycle over the layer copies (each step's weights come from HBM)."""
+    import torch
+
+    from gpeed_b200 import Context, MoeConfig, MoeLayer
+    from gpeed_b200 import _capi
+
+    n = args.batch
+    torch.cuda.set_device(local_rank)
+    ctx = Context(local_rank)
+    cfg = MoeConfig()
+    L = max(1, args.layers)
+    layers = [MoeLayer(ctx, cfg, layer_id=l).synth(router_for(l), zipf_bias(50 + l), seed=1000 + l, stream0=0)
+              for l in range(L)]
+    stream = torch.cuda.Stream()
+    xs = [tokens(n, 700 + l).cuda() for l in range(L)]
+    ys = [torch.empty(n, H, device="cuda") for _ in range(L)]
+    ids = [torch.empty(n, K_TOP, dtype=torch.int32, device="cuda") for _ in range(L)]
+    with torch.cuda.stream(stream):
+        for l in range(L):
+            layers[l].forward(xs[l], ys[l], topk_ids=ids[l], stream=stream)
+    stream.synchronize()
+    ctx.check(stream)
+    # algorithmic bytes per step: router, every touched routed expert once, the shared expert
+    touched = [len(np.unique(t.cpu().numpy())) for t in ids]
+    step_bytes = [E * H * 4 + (k + 1) * EXPERT_BYTES + n * H * 2 + n * H * 4 for k in touched]
+    graphs = []
+    for l in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            layers[l].forward(xs[l], ys[l], stream=stream)
+        graphs.append(g)
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % L].replay()
+    stream.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for i in range(args.steps):
+                graphs[i % L].replay()
+            ev1.record(stream)
+        stream.synchronize()
+        ms_total = ev0.elapsed_time(ev1)
+    ctx.check(stream)
+    value = world * n * args.steps / (ms_total / 1000.0)
+    mean_bytes = sum(step_bytes[i % L] for i in range(args.steps)) / args.steps
+
+    _capi.call("gpeed_ctx_profile", ctx.handle, 1)
+    with torch.cuda.stream(stream):
+        for i in range(max(args.steps, 4)):
+            layers[i % L].forward(xs[i % L], ys[i % L], stream=stream)
+    stage = (ctypes.c_float * 5)()
+    calls = ctypes.c_int()
+    _capi.call("gpeed_ctx_profile_read", ctx.handle, stage, ctypes.byref(calls))
+    _capi.call("gpeed_ctx_profile", ctx.handle, 0)
+    stage_ms = list(stage)
+
+    x_host = tokens(n, 555).pin_memory()
+    y_host = torch.empty(n, H, dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e2e_steps = max(3, args.steps // 4)
+    for i in range(e2e_steps):
+        with torch.cuda.stream(stream):
+            xs[i % L].copy_(x_host, non_blocking=True)
+            layers[i % L].forward(xs[i % L], ys[i % L], stream=stream)
+            y_host.copy_(ys[i % L], non_blocking=True)
+        stream.synchronize()
+    e2e_s = time.perf_counter() - t0
+    ctx.check(stream)
+
+    hbm_peak, _, peak_src = peaks()
+    tc = n >= _capi.TC_MIN_TOKENS_DEFAULT
+    tc_dtype = "f16 x f16 -> f32 (tcgen05), IQ3_XXS weights decoded in-kernel"
+    line = None
+    if rank == 0:
+        achieved = mean_bytes / (ms_total / args.steps * 1e-3) / 1e9
+        expert_ms = stage_ms[2] + stage_ms[3]
+        expert_bytes = sum((k + 1) * EXPERT_BYTES for k in touched) / L
+        cpu = None
+        if not args.no_cpu and world == 1:
+            from oracle import oracle
+            kind = "reference" if oracle.available("reference") else "port"
+            tps, done, dt, cores = cpu_time_layer(kind, args.cpu_seconds, 64)
+            cpu = {"value": tps, "unit": "tokens/s", "cores": cores, "kind": kind,
+                   "sample": f"{done} tokens x 1 layer (config 2 shapes, token by token) in {dt:.1f} s"}
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_total / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": tc_dtype if tc else "iq3_xxs(int8)xint16->f32", "data": "synthetic",
+            "config": {"workload": f"ragged{n}: {n}-token decode step, Zipf(1.1)-skewed expert loads (BASELINE config 3)",
+                       "hidden": H, "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
+                       "layer_copies": L, "touched_experts_per_layer": touched,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                       "l2": "each step's layer copy (>1 GB of experts) exceeds L2",
+                       "expert_path": "tensor-core grouped GEMMs" if tc else "quantised GEMV",
+                       "stage_ms": dict(zip(["router", "route+gather" if tc else "route", "gateup", "down", "combine"],
+                                            stage_ms))},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak if hbm_peak else None, "traffic": None,
+                         "kernel": "whole layer step (router, route, expert gate/up and down, combine): algorithmic "
+                                   "bytes of the touched experts / step time",
+                         "bytes_per_step": mean_bytes,
+                         "expert_stage_gbs": expert_bytes / (expert_ms * 1e-3) / 1e9 if expert_ms > 0 else None,
+                         "peak_source": peak_src},
+            "cpu_baseline": cpu,
+            "e2e": {"value": n * e2e_steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": n * H * 2,
+                    "d2h_bytes_per_step": n * H * 4},
+            # per step: router 2 (GEMM, split sum), top-k, route, gather, gate/up, down, combine; GEMV path: 6
+            "gpu_launches": (8 if tc else 6) * args.steps,
+            "clocks": clk.summary(),
+        }
+    del graphs
+    ctx.close()
+    return line
+
+
 def run_prefill_ep(args, rank, local_rank, world):
     """BASELINE config 4, expert-parallel over the GPUs of one box: each rank
     holds E/world routed experts (a contiguous range) plus the shared expert and
@@ -581,9 +715,10 @@ def main():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="decode1", choices=["decode1", "prefill"],
-                    help="decode1: BASELINE config 2 (default); prefill: config 4")
+    ap.add_argument("--workload", default="decode1", choices=["decode1", "ragged64", "prefill"],
+                    help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
+    ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
     ap.add_argument("--ep", action="store_true",
                     help="prefill with the experts split over the GPUs (NCCL all-to-all); needs --gpus >= 2")
     args = ap.parse_args()
@@ -603,6 +738,8 @@ def main():
         line = run_prefill_ep(args, rank, local_rank, world)
     elif args.workload == "prefill":
         line = run_prefill(args, rank, local_rank, world)
+    elif args.workload == "ragged64":
+        line = run_ragged(args, rank, local_rank, world)
     else:
         line = run_gpu(args, rank, local_rank, world)
     if world > 1:

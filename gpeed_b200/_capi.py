@@ -16,6 +16,7 @@ DTYPE_F32, DTYPE_IQ3_XXS, DTYPE_BF16 = 0, 18, 30
 OPT_FUSED_DECODE = 1
 OPT_FUSED_COOPERATIVE = 2
 OPT_TC_MIN_TOKENS = 3
+TC_MIN_TOKENS_DEFAULT = 8  # the library's default for OPT_TC_MIN_TOKENS
 
 
 class GpeedError(RuntimeError):

@@ -99,7 +99,7 @@ struct gpeed_ctx {
     // batch-1 forward in one persistent kernel when the shape has a variant
     bool fused_decode = true;
     bool fused_cooperative = false;
-    int tc_min_tokens = 1024;          // batches this large run the experts on tensor cores
+    int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
     DevBuf<unsigned long long> logits, dx;

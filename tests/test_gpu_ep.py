@@ -28,7 +28,12 @@ def _tokens(cfg, n):
 
 
 def test_ep_device_steps_emulated_two_ranks():
+    """The orchestration, bit for bit: every step on the quantised GEMV path so
+    the split layer must reproduce the single-GPU layer exactly (the
+    tensor-core experts step has its own test)."""
+    from gpeed_b200 import _capi
     ctx = Context(0)
+    ctx.set_option(_capi.OPT_TC_MIN_TOKENS, 1 << 30)
     try:
         cfg = MoeConfig()
         router = _router(cfg)
@@ -95,7 +100,7 @@ def test_ep_experts_step_tensor_core_path():
                 y_gemv = ex.experts(rows, idt)
                 ctx.check()
             finally:
-                ctx.set_option(_capi.OPT_TC_MIN_TOKENS, 1024)
+                ctx.set_option(_capi.OPT_TC_MIN_TOKENS, _capi.TC_MIN_TOKENS_DEFAULT)
             outs[name] = rel_l2(y_tc.cpu().numpy(), y_gemv.cpu().numpy())
         assert outs["routed"] < 1e-3 and outs["shared"] < 1e-3, outs
     finally:
@@ -114,7 +119,9 @@ def _nccl_worker(rank, world, port, splits, out_dir):
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
+        from gpeed_b200 import _capi
         ctx = Context(rank)
+        ctx.set_option(_capi.OPT_TC_MIN_TOKENS, 1 << 30)  # GEMV path on both sides: exact comparison
         cfg = MoeConfig()
         lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
         ex = CudaExecutor(ctx, cfg, 0, lo, cnt)
@@ -132,9 +139,11 @@ def _nccl_worker(rank, world, port, splits, out_dir):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_ep_nccl_two_gpus(tmp_path):
+    from gpeed_b200 import _capi
     splits = [9, 7]
     cfg = MoeConfig()
     ctx = Context(0)
+    ctx.set_option(_capi.OPT_TC_MIN_TOKENS, 1 << 30)
     try:
         y_ref = MoeLayer(ctx, cfg, layer_id=400).synth(_router(cfg), None, SEED, S0).forward(
             _tokens(cfg, sum(splits)).cuda()).cpu().numpy()
