@@ -14,7 +14,8 @@ steps never find their 85 MB of weights in the 126 MB L2.
 Other workloads: --workload ragged64 (config 3: 64 tokens, Zipf-skewed expert
 loads, quantised GEMV path), --workload prefill (config 4: 4096 tokens,
 tensor-core grouped GEMMs; with --ep and N >= 2 GPUs the experts are split over
-the GPUs with NCCL all-to-all dispatch and combine).
+the GPUs with NCCL all-to-all dispatch and combine), --workload stack40 (config
+5 on one GPU: 40 layers, decode batches 1 to 256).
 
 N > 1 (launched by torchrun): every rank runs its own replica of the layer
 stack on its GPU (weak scaling, no data-path collective); value sums tokens
@@ -615,6 +616,84 @@ def run_ragged(args, rank, local_rank, world):
     return line
 
 
+def run_stack(args, rank, local_rank, world):
+    """BASELINE config 5 on one GPU: a 40-layer MoE decode stack (160 experts +
+    shared each, IQ3_XXS, ~58 GB), swept over decode batches of 1, 8, 32, 128
+    and 256 tokens with uniform-random router logits.  A step is one batch
+    through all 40 layers, the 40 forwards captured back to back in one CUDA
+    graph (batch 1: the fused decode kernel; 2-7: the quantised GEMV path; 8
+    and up: the tensor-core grouped GEMMs).  Each layer reads its own static
+    input (the timing does not depend on the values, and chaining unnormalised
+    MoE outputs through 40 layers would overflow)."""
+    import torch
+
+    from gpeed_b200 import Context, MoeConfig, MoeLayer
+
+    torch.cuda.set_device(local_rank)
+    ctx = Context(local_rank)
+    cfg = MoeConfig()
+    NL = 40
+    layers = [MoeLayer(ctx, cfg, layer_id=l).synth(router_for(2000 + l), None, seed=5000 + l, stream0=0)
+              for l in range(NL)]
+    stream = torch.cuda.Stream()
+    sweep = []
+    with ClockSampler(local_rank) as clk:
+        for B in (1, 8, 32, 128, 256):
+            xs = [tokens(B, 9000 + 7 * l + B).cuda() for l in range(NL)]
+            ys = [torch.empty(B, H, device="cuda") for _ in range(NL)]
+            with torch.cuda.stream(stream):
+                for l in range(NL):
+                    layers[l].forward(xs[l], ys[l], stream=stream)
+            stream.synchronize()
+            ctx.check(stream)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for l in range(NL):
+                    layers[l].forward(xs[l], ys[l], stream=stream)
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    g.replay()
+            stream.synchronize()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                ev0.record(stream)
+                for _ in range(args.steps):
+                    g.replay()
+                ev1.record(stream)
+            stream.synchronize()
+            ctx.check(stream)
+            ms = ev0.elapsed_time(ev1) / args.steps
+            sweep.append({"batch": B, "ms_per_stack": ms, "ms_per_layer": ms / NL, "tokens_per_s": B / (ms * 1e-3)})
+            del g
+    hbm_peak, _, peak_src = peaks()
+    line = None
+    if rank == 0:
+        b1 = sweep[0]
+        achieved = LAYER_TOKEN_BYTES / (b1["ms_per_layer"] * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": world * sweep[-1]["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": sweep[-1]["ms_per_stack"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "batch 1: iq3_xxs(int8)xint16->f32; 8+: f16 x f16 -> f32 (tcgen05)", "data": "synthetic",
+            "config": {"workload": "stack40: 40 MoE layers, decode batch sweep 1/8/32/128/256 (BASELINE config 5, "
+                                   "one GPU; value = batch 256 through the stack)",
+                       "hidden": H, "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
+                       "layers": NL, "expert_bytes_per_layer": E * EXPERT_BYTES + EXPERT_BYTES,
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU (all 40 layers resident)",
+                       "sweep": sweep},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak if hbm_peak else None, "traffic": None,
+                         "kernel": "batch 1: decode_layer_kernel per layer inside the 40-layer graph",
+                         "bytes_per_launch": LAYER_TOKEN_BYTES, "peak_source": peak_src},
+            "cpu_baseline": None,
+            "e2e": None,
+            "gpu_launches": NL * args.steps,
+            "clocks": clk.summary(),
+        }
+    ctx.close()
+    return line
+
+
 def run_prefill_ep(args, rank, local_rank, world):
     """BASELINE config 4, expert-parallel over the GPUs of one box: each rank
     holds E/world routed experts (a contiguous range) plus the shared expert and
@@ -715,7 +794,7 @@ def main():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="decode1", choices=["decode1", "ragged64", "prefill"],
+    ap.add_argument("--workload", default="decode1", choices=["decode1", "ragged64", "prefill", "stack40"],
                     help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
     ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
@@ -740,6 +819,8 @@ def main():
         line = run_prefill(args, rank, local_rank, world)
     elif args.workload == "ragged64":
         line = run_ragged(args, rank, local_rank, world)
+    elif args.workload == "stack40":
+        line = run_stack(args, rank, local_rank, world)
     else:
         line = run_gpu(args, rank, local_rank, world)
     if world > 1:
