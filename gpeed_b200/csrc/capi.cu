@@ -705,7 +705,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     };
     if (n == 1 && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
         const size_t had = c->logits.n;
-        if ((rc = c->logits.ensure((size_t)E))) return rc;
+        if ((rc = c->logits.ensure(gp::decode_layer_logit_words(E)))) return rc;
         if (c->logits.n != had)  // tags must start below the first launch's
             GP_CUDA(cudaMemsetAsync(c->logits.p, 0, c->logits.n * sizeof(unsigned long long), st));
         const size_t had_dx = c->dx.n;

@@ -17,7 +17,8 @@
 //            the wait on the previous kernel); the epilogue warp adds the
 //            slices in order and stores the logit tagged with the launch
 //            generation, so readers poll the data itself
-//   top-k    every CTA's epilogue warp polls the E tagged logits, applies
+//   top-k    every CTA's epilogue warp polls the E tagged logits (one of 8
+//            replicas, spread over L2 lines), applies
 //            sigmoid + bias and picks top-K by warp reductions (ties to the
 //            lower id), weights score/(1e-20 + sum)*scale (model.cpp:704-725)
 //   gate/up  units of 32 rows of h, dealt round-robin in slot order (the
@@ -46,6 +47,9 @@
 #include "iq3xxs.cuh"
 #include "kernels.h"
 
+#ifndef TOPK_POLL_NS
+#define TOPK_POLL_NS 32
+#endif
 // Optional instrumentation hook (timestamps per CTA); compiled out here.
 #ifndef GP_STAMP
 #define GP_STAMP(i) ((void)0)
@@ -67,6 +71,14 @@ constexpr int RSPLIT = 8;        // router slices per expert
 constexpr int MAXK = 31;         // K+1 slots fit one warp
 constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
 constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
+// Tagged logits: every CTA polls all E of them, so one array would send every
+// poll of every CTA to the few L2 slices holding it.  Each logit is stored in
+// kLogitCopies replicas, one word per 256-byte line; CTA c polls replica
+// c % kLogitCopies.
+constexpr int kLogitCopies = 8;
+constexpr int kLogitStride = 32;  // words
+static_assert(kLogitCopies * kLogitStride == 256, "decode_layer_logit_words (kernels.h) assumes 8 x 32");
+GP_DEVINL int logit_word(int copy, int e, int E) { return (copy * E + e) * kLogitStride; }
 static_assert(TRD == 32, "the combine maps one row of a down tile to each epilogue lane");
 
 
@@ -199,12 +211,13 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t t
     uint32_t n = 0;
     for (; n < GP_SPIN_LIMIT; ++n) {
 #pragma unroll
-        for (int j = 0; j < EJ; ++j) w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + lane + 32 * j) : 0ull;
+        for (int j = 0; j < EJ; ++j)
+            w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + logit_word(c % kLogitCopies, lane + 32 * j, E)) : 0ull;
         bool ok = true;
 #pragma unroll
         for (int j = 0; j < EJ; ++j) ok &= lane + 32 * j >= E || (uint32_t)(w[j] >> 32) == tag;
         if (__all_sync(0xffffffffu, ok)) break;
-        __nanosleep(32);
+        __nanosleep(TOPK_POLL_NS);
     }
     if (n == GP_SPIN_LIMIT && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
     if (lane == 0) GP_STAMP(11);
@@ -553,7 +566,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 float lg = 0.f;
 #pragma unroll
                 for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[lane * RSPLIT + sl];
-                st_relaxed64(a.logits + c + lane * G, ((unsigned long long)tag << 32) | __float_as_uint(lg));
+                const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(lg);
+#pragma unroll
+                for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.logits + logit_word(cp, c + lane * G, E), v);
             }
         }
         if (lane == 0) GP_STAMP(1);

@@ -152,7 +152,7 @@ struct DecodeLayerArgs {
     const int* forced;         // [K] or nullptr
     int* topk_ids;             // [K] or nullptr
     float* topk_w;             // [K] or nullptr
-    unsigned long long* logits;  // [E] router logits tagged with the launch generation
+    unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
     float* h;                  // [K+1][I]
     uint8_t* hq;               // [K+1][decode_layer_hq_bytes(I)] h quantised per 32-unit
     float* D;                  // [K+1][H] (multi-kernel path)
@@ -201,6 +201,8 @@ constexpr int kSyncSlot = 8;                    // [K+1] h units quantised per s
 constexpr int kDecodeSyncWords = 64;
 // h[slot] as int16 pairs (I*2 bytes) followed by one fp32 scale per 32-unit.
 inline size_t decode_layer_hq_bytes(int I) { return (size_t)I * 2 + (size_t)(I / 32) * 4; }
+// Words of DecodeLayerArgs::logits: 8 replicas of E tagged logits, one word per 256-byte line.
+inline size_t decode_layer_logit_words(int E) { return (size_t)8 * E * 32; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
 size_t decode_layer_smem(int H, int I, int stages);
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st);
