@@ -17,6 +17,8 @@ OPT_FUSED_DECODE = 1
 OPT_FUSED_COOPERATIVE = 2
 OPT_TC_MIN_TOKENS = 3
 TC_MIN_TOKENS_DEFAULT = 8  # the library's default for OPT_TC_MIN_TOKENS
+OPT_FUSED_MAX_TOKENS = 4
+FUSED_MAX_TOKENS_DEFAULT = 12
 
 
 class GpeedError(RuntimeError):

@@ -98,6 +98,7 @@ struct gpeed_ctx {
     DevBuf<gp::SlotDesc> slots;
     // batch-1 forward in one persistent kernel when the shape has a variant
     bool fused_decode = true;
+    int fused_max_tokens = 12;         // batches up to this size: the fused kernel once per token
     bool fused_cooperative = false;
     int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
@@ -466,6 +467,10 @@ int gpeed_ctx_set_option(gpeed_ctx* c, int option, int value) {
     if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
     switch (option) {
         case GPEED_OPT_FUSED_DECODE: c->fused_decode = value != 0; return GPEED_OK;
+        case GPEED_OPT_FUSED_MAX_TOKENS:
+            if (value < 1) return fail(GPEED_ERR_INVALID, "GPEED_OPT_FUSED_MAX_TOKENS must be >= 1");
+            c->fused_max_tokens = value;
+            return GPEED_OK;
         case GPEED_OPT_FUSED_COOPERATIVE: c->fused_cooperative = value != 0; return GPEED_OK;
         case GPEED_OPT_TC_MIN_TOKENS:
             if (value < 1) return fail(GPEED_ERR_INVALID, "tensor-core threshold must be >= 1");
@@ -703,7 +708,9 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     auto mark = [&](int i) {
         if (c->prof) cudaEventRecord(c->ev[i], st);
     };
-    if (n == 1 && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
+    if (n <= c->fused_max_tokens && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
+        // batch 1, and small batches one token at a time: each launch streams
+        // only its token's experts, and consecutive launches overlap (PDL)
         const size_t had = c->logits.n;
         if ((rc = c->logits.ensure(gp::decode_layer_logit_words(E)))) return rc;
         if (c->logits.n != had)  // tags must start below the first launch's
@@ -748,7 +755,15 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         // profiling: the one kernel's time goes to the gate/up slot, the other
         // stages read 0
         mark(2);
-        GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
+        const size_t xrow = (size_t)H * (x_dtype == GPEED_DTYPE_BF16 ? 2 : 4);
+        for (int t = 0; t < n; ++t) {
+            da.x = static_cast<const uint8_t*>(x) + t * xrow;
+            da.y = y + (size_t)t * H;
+            da.forced = forced ? forced + (size_t)t * K : nullptr;
+            da.topk_ids = topk_ids ? topk_ids + (size_t)t * K : nullptr;
+            da.topk_w = topk_w ? topk_w + (size_t)t * K : nullptr;
+            GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
+        }
         mark(3);
         if (c->prof) {
             GP_CUDA(cudaEventSynchronize(c->ev[3]));

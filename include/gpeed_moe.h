@@ -103,6 +103,13 @@ GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
  * Zipf-skewed routing 8 tokens 0.26 vs 0.34 ms, 64 tokens 0.42 vs 1.70 ms;
  * uniform routing 8 tokens 0.52 vs 0.62 ms, 32 tokens 1.11 vs 1.49 ms. */
 #define GPEED_OPT_TC_MIN_TOKENS 3
+/* GPEED_OPT_FUSED_MAX_TOKENS (default 12): batches of up to this many tokens
+ * run the fused decode kernel once per token (each launch streams only that
+ * token's nine experts; launches overlap through programmatic dependent
+ * launch).  Larger batches take the tensor-core or GEMV paths above.
+ * Measured with uniform routing: 8 tokens 0.30 ms per layer this way against
+ * 0.52 ms on the tensor cores. */
+#define GPEED_OPT_FUSED_MAX_TOKENS 4
 GPEED_API int gpeed_ctx_set_option(gpeed_ctx* ctx, int option, int value);
 
 /* Per-stage timing of gpeed_moe_forward (no counterpart in the reference;
