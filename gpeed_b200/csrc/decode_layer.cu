@@ -337,7 +337,7 @@ GP_DEVINL int items_of(int c, int G, int total) { return c < total ? (total - 1 
 // position q = K is the shared expert (ready first), q < K routed slot K-1-q
 // (slot 0 at q = K-1 is ready next, slot K-1 at q = 0 last).  CTA c owns the
 // range [v0, v1), sized so that its down work plus its routed gate/up units
-// is the same for every CTA (weights: one unit ~ wu, one down tile ~ wd).
+// is the same for every CTA (weights: one unit ~ wu, one down position ~ wd).
 // The range is walked as: the leading partial tile, the first whole tile,
 // the trailing partial tile, the other whole tiles; each tile in descending
 // q.  Partial tiles thus meet the early-ready slots first, the tiles shared
@@ -367,10 +367,13 @@ GP_DEVINL int prefix_rr(int c, int G, int total) {  // sum of items_of(c', G, to
     return (total / G) * c + (c < total % G ? c : total % G);
 }
 GP_DEVINL DownRange down_range(int c, int G, int n_tiles, int P, int units, int shared_units) {
-    // measured costs: a routed gate/up unit ~ 4.4 down positions; a shared
-    // unit mostly overlaps the routing, ~0.4 of a routed one.  32-bit
-    // arithmetic: G * W < 2^31 for the supported shapes (host-checked).
-    constexpr int wu = 44, ws = 17, wd = 10;
+    // weights set by measurement of the whole layer (not of the units alone):
+    // a routed gate/up unit counts as 3 down positions, although it takes
+    // about 5.7, because a CTA that finishes its units early cannot start the
+    // down tiles of the slots still being computed elsewhere; a shared unit
+    // mostly overlaps the routing.  32-bit arithmetic: G * W < 2^31 for the
+    // supported shapes (host-checked).
+    constexpr int wu = 30, ws = 17, wd = 10;
     const int routed = units - shared_units, total = n_tiles * P;
     const int W = routed * wu + shared_units * ws + total * wd;
     const int max_units = (units + G - 1) / G;
