@@ -8,9 +8,10 @@ expert.  One forward on each rank:
   1. route its own tokens (router + top-k)                       device
   2. group the (token, k) assignments by destination rank         device
   3. all-to-all: per-rank counts, then token rows and expert ids  collective
-  4. gate/up -> SwiGLU -> down for every received row             device
+  4. gate/up -> SwiGLU -> down for every received row and, in the
+     same pass, the shared expert on this rank's own tokens        device
   5. all-to-all: the expert outputs back to their token's rank    collective
-  6. the shared expert on its own tokens; y = sum_k w_k D_k + D_sh device
+  6. y = sum_k w_k D_k + D_shared                                  device
 
 The collectives are torch.distributed all_to_all_single (NCCL between GPUs,
 gloo on CPU); the device steps go through an executor.  The product executor
@@ -119,7 +120,11 @@ class ExpertParallelLayer:
         return recv
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
-        """x [n, H] (this rank's tokens) -> y [n, H] fp32."""
+        """x [n, H] (this rank's tokens) -> y [n, H] fp32.
+
+        The received rows and this rank's own rows for the shared expert go
+        through one experts pass: the exchange lands in the head of one row
+        buffer whose tail holds the own tokens."""
         ex, cfg = self.ex, self.cfg
         n, K = x.shape[0], cfg.top_k
         if n:
@@ -136,12 +141,18 @@ class ExpertParallelLayer:
         dist.all_to_all_single(recv_counts, send_counts, group=self.group)
         send_splits = send_counts.cpu().tolist()
         recv_splits = recv_counts.cpu().tolist()
-        recv_rows = self._a2a(send_rows, send_splits, recv_splits)
-        recv_ids = self._a2a(send_ids, send_splits, recv_splits)
-        d_recv = ex.experts(recv_rows, recv_ids) if recv_rows.shape[0] else ex.empty((0, cfg.hidden), torch.float32)
-        d_back = self._a2a(d_recv, recv_splits, send_splits)
+        r = sum(recv_splits)
+        m = r + (n if cfg.n_shared else 0)
+        rows = ex.empty((m, cfg.hidden), x.dtype)
+        row_ids = ex.empty((m,), torch.int32)
+        dist.all_to_all_single(rows[:r], send_rows.contiguous(), recv_splits, send_splits, group=self.group)
+        dist.all_to_all_single(row_ids[:r], send_ids.contiguous(), recv_splits, send_splits, group=self.group)
+        if m > r:  # the shared expert on this rank's own tokens
+            rows[r:].copy_(x)
+            row_ids[r:].fill_(cfg.n_experts)
+        d_all = ex.experts(rows, row_ids) if m else ex.empty((0, cfg.hidden), torch.float32)
+        d_back = self._a2a(d_all[:r], recv_splits, send_splits)
         if not n:
             return ex.empty((0, cfg.hidden), torch.float32)
-        shared_ids = torch.full((n,), cfg.n_experts, dtype=torch.int32, device=x.device)
-        d_shared = ex.experts(x, shared_ids) if cfg.n_shared else None
+        d_shared = d_all[r:] if cfg.n_shared else None
         return ex.combine(d_back, slot_of, w, d_shared)
