@@ -6,5 +6,7 @@ engine's expert-op interface on top of it.
 """
 from ._capi import GpeedError, load as load_library  # noqa: F401
 from .moe import Context, MoeConfig, MoeLayer, WeightStore, dequantize  # noqa: F401
+from .gguf import GgufModel  # noqa: F401
 
-__all__ = ["Context", "MoeConfig", "MoeLayer", "WeightStore", "dequantize", "GpeedError", "load_library"]
+__all__ = ["Context", "MoeConfig", "MoeLayer", "WeightStore", "dequantize", "GpeedError", "load_library",
+           "GgufModel"]

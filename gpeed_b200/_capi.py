@@ -35,7 +35,13 @@ class MoeShape(ctypes.Structure):
                 ("norm_topk", ctypes.c_int), ("swiglu_limit", ctypes.c_float)]
 
 
+class GgufTensor(ctypes.Structure):
+    _fields_ = [("dtype", ctypes.c_int), ("n_dims", ctypes.c_int), ("dims", ctypes.c_uint64 * 4),
+                ("offset", ctypes.c_uint64), ("nbytes", ctypes.c_uint64), ("shard", ctypes.c_int)]
+
+
 _vp, _i, _u64, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint64, ctypes.c_float
+_i64, _cs = ctypes.c_int64, ctypes.c_char_p
 # name -> argtypes (every function returns int status unless listed in _RESTYPES)
 SIGNATURES = {
     "gpeed_last_error": [],
@@ -63,6 +69,21 @@ SIGNATURES = {
     "gpeed_ep_pack": [_vp, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "gpeed_moe_experts": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp],
     "gpeed_moe_combine": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],
+    "gpeed_dense_mlp_forward": [_vp, _i, _i, _i, _f, _vp, _i, _i, _vp, _vp],
+    "gpeed_gguf_open": [_cs, ctypes.POINTER(_vp)],
+    "gpeed_gguf_close": [_vp],
+    "gpeed_gguf_counts": [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i64), ctypes.POINTER(_i64)],
+    "gpeed_gguf_tensor_name": [_vp, _i64, ctypes.POINTER(_cs)],
+    "gpeed_gguf_key_name": [_vp, _i64, ctypes.POINTER(_cs)],
+    "gpeed_gguf_tensor_info": [_vp, _cs, ctypes.POINTER(GgufTensor)],
+    "gpeed_gguf_read": [_vp, _cs, _u64, _u64, _vp],
+    "gpeed_gguf_meta_type": [_vp, _cs, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_u64)],
+    "gpeed_gguf_meta_f64": [_vp, _cs, _u64, ctypes.POINTER(ctypes.c_double)],
+    "gpeed_gguf_meta_u64": [_vp, _cs, ctypes.POINTER(_u64)],
+    "gpeed_gguf_meta_str": [_vp, _cs, ctypes.POINTER(_cs)],
+    "gpeed_gguf_moe_shape": [_vp, _i, ctypes.POINTER(MoeShape)],
+    "gpeed_moe_load_layer_gguf": [_vp, _vp, _i, _i, _i, _i, ctypes.POINTER(MoeShape)],
+    "gpeed_tensor_upload_gguf": [_vp, _vp, _cs, ctypes.POINTER(_i)],
 }
 _RESTYPES = {"gpeed_last_error": ctypes.c_char_p}
 

@@ -12,9 +12,11 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/gpeed_moe.h"
+#include "host_error.h"
 #include "kernels.h"
 
 namespace {
@@ -111,7 +113,15 @@ struct gpeed_ctx {
     cudaEvent_t ev[6] = {};
     double prof_ms[5] = {0, 0, 0, 0, 0};
     long prof_calls = 0;
+    // pinned staging ring for weight uploads from pageable host memory
+    uint8_t* stage[4] = {};
+    cudaEvent_t stage_ev[4] = {};
 };
+
+int gp::set_error(int code, const std::string& msg) {
+    g_err = msg;
+    return code;
+}
 
 namespace {
 
@@ -119,6 +129,14 @@ int set_device(const gpeed_ctx* c) {
     int cur = -1;
     if (cudaGetDevice(&cur) != cudaSuccess || cur != c->device) GP_CUDA(cudaSetDevice(c->device));
     return GPEED_OK;
+}
+
+// every row to local expert 0 with weight 1 (the dense MLP as a one-expert pass)
+__global__ void fill_unit_kernel(int* ids, float* w, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        ids[i] = 0;
+        w[i] = 1.f;
+    }
 }
 
 __global__ void make_slots_kernel(gp::SlotDesc* slots, int* nslots, int n_tok, int nt) {
@@ -187,6 +205,54 @@ int nt_for(int ntok) {
     return 4;
 }
 
+constexpr size_t kStageBytes = size_t(32) << 20;
+constexpr int kStages = 4;
+
+// memcpy split over up to `nthr` host threads (page-cache reads of a mapped
+// file fault in page by page; several threads keep the H2D link busy)
+void parallel_copy(uint8_t* dst, const uint8_t* src, size_t n, unsigned nthr) {
+    if (n < (size_t(2) << 20) || nthr <= 1) {
+        std::memcpy(dst, src, n);
+        return;
+    }
+    std::vector<std::thread> th;
+    const size_t part = (n / nthr + 4095) & ~size_t(4095);
+    size_t done = 0;
+    try {
+        for (unsigned i = 0; i + 1 < nthr && done + part < n; ++i, done += part)
+            th.emplace_back([=] { std::memcpy(dst + done, src + done, part); });
+    } catch (...) {  // no thread to be had: the calling thread copies the rest
+    }
+    std::memcpy(dst + done, src + done, n - done);
+    for (auto& t : th) t.join();
+}
+
+// Pageable host bytes (a file mapping or a caller's array) -> device through
+// kStages pinned buffers: host threads fill one while the copy engine drains
+// the others, so an upload runs at the slower of the host reads and the H2D
+// link rather than through the driver's synchronous pageable staging.
+int h2d_staged(gpeed_ctx* c, void* dst, const void* src, size_t bytes, cudaStream_t st) {
+    if (!c->stage[0]) {
+        for (int i = 0; i < kStages; ++i) {
+            GP_CUDA(cudaHostAlloc(&c->stage[i], kStageBytes, cudaHostAllocDefault));
+            GP_CUDA(cudaEventCreateWithFlags(&c->stage_ev[i], cudaEventDisableTiming));
+        }
+    }
+    const unsigned nthr = std::max(1u, std::min(8u, std::thread::hardware_concurrency()));
+    const uint8_t* s = static_cast<const uint8_t*>(src);
+    uint8_t* d = static_cast<uint8_t*>(dst);
+    size_t k = 0;
+    for (size_t off = 0; off < bytes; off += kStageBytes, ++k) {
+        const int b = (int)(k % kStages);
+        const size_t n = std::min(kStageBytes, bytes - off);
+        GP_CUDA(cudaEventSynchronize(c->stage_ev[b]));  // the copy that last read this buffer has ended
+        parallel_copy(c->stage[b], s + off, n, nthr);
+        GP_CUDA(cudaMemcpyAsync(d + off, c->stage[b], n, cudaMemcpyHostToDevice, st));
+        GP_CUDA(cudaEventRecord(c->stage_ev[b], st));
+    }
+    return GPEED_OK;
+}
+
 int upload_matrix(gpeed_ctx* c, const void* raw, int on_device, int64_t rows, int in_dim, uint8_t* dst,
                   cudaStream_t st) {
     const size_t raw_bytes = (size_t)rows * (in_dim / 256) * 98;
@@ -194,7 +260,12 @@ int upload_matrix(gpeed_ctx* c, const void* raw, int on_device, int64_t rows, in
     uint8_t* tmp = nullptr;
     if (!on_device) {
         GP_CUDA(cudaMalloc(&tmp, raw_bytes));
-        GP_CUDA(cudaMemcpyAsync(tmp, raw, raw_bytes, cudaMemcpyHostToDevice, st));
+        int rc = h2d_staged(c, tmp, raw, raw_bytes, st);
+        if (rc) {
+            cudaStreamSynchronize(st);
+            cudaFree(tmp);
+            return rc;
+        }
         src = tmp;
     }
     GP_CUDA(gp::launch_repack(src, dst, rows, in_dim, st));
@@ -439,6 +510,10 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     cudaFree(c->sync);
     cudaFree(c->tables);
     cudaFree(c->status);
+    for (int i = 0; i < 4; ++i) {
+        if (c->stage[i]) cudaFreeHost(c->stage[i]);
+        if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
+    }
     delete c;
     return GPEED_OK;
 }
@@ -990,6 +1065,53 @@ int gpeed_moe_experts(gpeed_ctx* c, int layer, const void* rows, int rows_dtype,
     ro.topk_w = c->topk_w.p;
     auto nomark = [](int) {};
     return expert_pass(c, L, rows, rows_dtype == GPEED_DTYPE_BF16, ro, 0, nullptr, out, st, nomark);
+}
+
+int gpeed_dense_mlp_forward(gpeed_ctx* c, int gate, int up, int down, float swiglu_limit, const void* X, int x_dtype,
+                            int n, float* Y, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    const int nt = (int)c->tensors.size();
+    if (gate < 0 || gate >= nt || up < 0 || up >= nt || down < 0 || down >= nt)
+        return fail(GPEED_ERR_INVALID, "bad tensor handle");
+    const Tensor &G = c->tensors[gate], &U = c->tensors[up], &D = c->tensors[down];
+    const int H = G.in_dim;
+    const int64_t I = G.rows;
+    if (U.in_dim != H || U.rows != I || D.in_dim != I || D.rows != H)
+        return fail(GPEED_ERR_INVALID, "gate/up must be inter x hidden and down hidden x inter (got %lld x %d, %lld x %d, "
+                    "%lld x %d)", (long long)G.rows, G.in_dim, (long long)U.rows, U.in_dim, (long long)D.rows, D.in_dim);
+    if (n < 0) return fail(GPEED_ERR_INVALID, "n_tok < 0");
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (n && (!X || !Y || (reinterpret_cast<uintptr_t>(X) & 15) || (reinterpret_cast<uintptr_t>(Y) & 15)))
+        return fail(GPEED_ERR_INVALID, "X and Y must be 16-byte aligned device pointers");
+    Layer L;
+    L.shape = gpeed_moe_shape{H, (int)I, 1, 1, 0, 1.f, 0, swiglu_limit};
+    int rc;
+    if ((rc = check_shape(&L.shape))) return rc;
+    if (n == 0) return GPEED_OK;
+    L.e_cnt = 1;
+    L.gate = G.packed;
+    L.up = U.packed;
+    L.down = D.packed;
+    L.gu_stride = gp::repacked_bytes(I, H);
+    L.d_stride = gp::repacked_bytes(H, (int)I);
+    if ((rc = set_device(c))) return rc;
+    if ((rc = ensure_scratch(c, n, 1, 1, H, (int)I))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    fill_unit_kernel<<<std::min((n + 255) / 256, 148), 256, 0, st>>>(c->topk_ids.p, c->topk_w.p, n);
+    GP_CUDA(cudaGetLastError());
+    gp::RouteArgs ro{};
+    ro.topk_ready = 1;
+    ro.n = n;
+    ro.E = 1;
+    ro.K = 1;
+    ro.with_shared = 0;
+    ro.expert_lo = 0;
+    ro.expert_hi = 1;
+    ro.topk_ids = c->topk_ids.p;
+    ro.topk_w = c->topk_w.p;
+    auto nomark = [](int) {};
+    return expert_pass(c, L, X, x_dtype == GPEED_DTYPE_BF16, ro, 0, nullptr, Y, st, nomark);
 }
 
 int gpeed_moe_combine(gpeed_ctx* c, int n, int K, int hidden, const float* d_rows, const int* slot_of,

@@ -6,6 +6,11 @@
 // become std::runtime_error carrying gpeed_last_error(), as the reference
 // throws (weights.cpp:170-174, quant.cpp:523-554).  Header-only; link
 // libgpeed_moe.so.
+//
+// gpeed::GgufModel opens a (sharded) GGUF model like glm5::GgufModel
+// (gguf.h:122-150); a WeightStore built on one resolves tensor names in it on
+// first use, as glm5::WeightStore(const GgufModel&, bool) does (weights.h:15-20),
+// and keeps the device copy for later calls.
 #pragma once
 #include <stdexcept>
 #include <string>
@@ -19,9 +24,34 @@ inline void check(int rc) {
     if (rc != GPEED_OK) throw std::runtime_error(std::string("gpeed: ") + gpeed_last_error());
 }
 
+class GgufModel {
+public:
+    // any one shard path; the others are found by name (gguf.cpp:298-326)
+    explicit GgufModel(const std::string& path) { check(gpeed_gguf_open(path.c_str(), &g_)); }
+    ~GgufModel() { gpeed_gguf_close(g_); }
+    GgufModel(const GgufModel&) = delete;
+    GgufModel& operator=(const GgufModel&) = delete;
+
+    gpeed_gguf* handle() const { return g_; }
+    // nullptr-like false when absent (GgufModel::find_tensor)
+    bool find_tensor(const std::string& name, gpeed_gguf_tensor* out) const {
+        return gpeed_gguf_tensor_info(g_, name.c_str(), out) == GPEED_OK;
+    }
+    // GgufFile::read_at, inside one tensor
+    void read_at(const std::string& name, uint64_t offset, size_t bytes, void* dst) const {
+        check(gpeed_gguf_read(g_, name.c_str(), offset, bytes, dst));
+    }
+
+private:
+    gpeed_gguf* g_ = nullptr;
+};
+
 class WeightStore {
 public:
     explicit WeightStore(int device = 0) { check(gpeed_ctx_create(device, &ctx_)); }
+    explicit WeightStore(const GgufModel& model, int device = 0) : model_(&model) {
+        check(gpeed_ctx_create(device, &ctx_));
+    }
     ~WeightStore() { gpeed_ctx_destroy(ctx_); }
     WeightStore(const WeightStore&) = delete;
     WeightStore& operator=(const WeightStore&) = delete;
@@ -49,11 +79,16 @@ public:
     }
 
 private:
-    int handle(const std::string& name) const {
+    int handle(const std::string& name) {
         auto it = handles_.find(name);
-        if (it == handles_.end()) throw std::runtime_error("weights: missing tensor " + name);  // weights.cpp:170
-        return it->second;
+        if (it != handles_.end()) return it->second;
+        if (!model_) throw std::runtime_error("weights: missing tensor " + name);  // weights.cpp:170
+        int h = -1;
+        check(gpeed_tensor_upload_gguf(ctx_, model_->handle(), name.c_str(), &h));
+        handles_[name] = h;
+        return h;
     }
+    const GgufModel* model_ = nullptr;
     gpeed_ctx* ctx_ = nullptr;
     std::unordered_map<std::string, int> handles_;
 };

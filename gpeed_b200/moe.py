@@ -121,6 +121,19 @@ class WeightStore:
         call("gpeed_matmul_quant", self.ctx.handle, self._h(name), ctypes.c_uint64(row0), in_dim, out_dim,
              _ptr(X), n_tok, _ptr(Y), _stream(stream))
 
+    def dense_mlp(self, gate: str, up: str, down: str, X: torch.Tensor, Y: torch.Tensor | None = None,
+                  swiglu_limit: float = 10.0, stream=None) -> torch.Tensor:
+        """Y = down(silu(min(gate X, L)) * clamp(up X, -L, L)) for the dense layers
+        (Model::dense_mlp / dense_mlp_batch, model.cpp:677-690, model_batch.cpp:145-163)."""
+        if X.dim() == 1:
+            X = X.unsqueeze(0)
+        dt = _capi.DTYPE_BF16 if X.dtype == torch.bfloat16 else _capi.DTYPE_F32
+        if Y is None:
+            Y = torch.empty(X.shape[0], X.shape[1], dtype=torch.float32, device=X.device)
+        call("gpeed_dense_mlp_forward", self.ctx.handle, self._h(gate), self._h(up), self._h(down),
+             ctypes.c_float(swiglu_limit), _ptr(X.contiguous()), dt, X.shape[0], _ptr(Y), _stream(stream))
+        return Y
+
 
 @dataclass
 class MoeConfig:
@@ -163,6 +176,13 @@ class MoeLayer:
         call("gpeed_moe_load_layer", self.ctx.handle, self.layer_id, ctypes.byref(self._shape), _ptr(router),
              _ptr(corr_c), *[_ptr(t) for t in keep], int(on_dev))
         return self
+
+    @classmethod
+    def from_gguf(cls, ctx: Context, model, blk: int, layer_id: int | None = None, expert_begin: int = 0,
+                  expert_count: int | None = None) -> "MoeLayer":
+        """Block `blk` of a GGUF model (``gpeed_b200.gguf.GgufModel``), read by tensor name."""
+        from .gguf import load_moe_layer
+        return load_moe_layer(ctx, model, blk, layer_id, expert_begin, expert_count)
 
     def synth(self, router: np.ndarray, corr: np.ndarray | None, seed: int, stream0: int) -> "MoeLayer":
         """Expert bytes from the device generator (seed, streams stream0..stream0+5)."""

@@ -230,6 +230,87 @@ GPEED_API int gpeed_moe_combine(gpeed_ctx* ctx, int n_tok, int K, int hidden, co
                                 const int* slot_of_dev, const float* topk_w_dev, const float* d_shared_dev,
                                 float* y_dev, void* stream);
 
+/* Dense SwiGLU MLP of the leading dense layers (Model::dense_mlp,
+ * model.cpp:677-690, and dense_mlp_batch, model_batch.cpp:145-163):
+ *   Y[t] = down(silu(min(gate X[t], L)) * clamp(up X[t], -L, L))
+ * over three IQ3_XXS tensors registered with gpeed_tensor_upload[_gguf]
+ * (gate/up: inter rows of hidden weights; down: hidden rows of inter), run by
+ * the expert kernels as a one-expert pass.  X bf16 or fp32 [n_tok][hidden],
+ * Y fp32 [n_tok][hidden], device. */
+GPEED_API int gpeed_dense_mlp_forward(gpeed_ctx* ctx, int gate, int up, int down, float swiglu_limit, const void* X_dev,
+                                      int x_dtype, int n_tok, float* Y_dev, void* stream);
+
+/* ---- GGUF model files (cpp/core/include/glm5/gguf.h; gguf.cpp).
+ *
+ *   gpeed_gguf_open           <- GgufModel::load(GgufModel::discover_shards(path))
+ *                                (gguf.cpp:255-326, parse at gguf.cpp:133-188):
+ *                                versions 2 and 3, "<stem>-NNNNN-of-MMMMM.gguf"
+ *                                shards found from any one of them; a tensor
+ *                                name resolves to its first shard, a metadata
+ *                                key to the first shard that has it.  The
+ *                                files are mapped read-only (the reference
+ *                                maps them on Windows and reads them with an
+ *                                ifstream elsewhere, weights.cpp:62-68).
+ *   gpeed_gguf_tensor_info    <- GgufModel::find_tensor + TensorInfo
+ *   gpeed_gguf_read           <- GgufFile::read_at (gguf.cpp:236-248)
+ *   gpeed_gguf_meta_*         <- GgufModel::find + GgufValue::as_* (permissive
+ *                                numeric coercion as gguf.cpp:85-117)
+ *   gpeed_gguf_moe_shape      <- ModelConfig::from_gguf, MoE fields
+ *                                (model_config.cpp:80-95) for block `blk`
+ *   gpeed_tensor_upload_gguf  <- WeightStore's payload of one tensor by name
+ *                                (weights.cpp:62-68)
+ *   gpeed_moe_load_layer_gguf <- the tensors Model::moe_forward reads by name
+ *                                (model.cpp:702-754) for block `blk`, straight
+ *                                from the mapping into the library's layout;
+ *                                an expert range for expert parallelism.
+ * Handles are not thread-safe; the mapping lives until gpeed_gguf_close. */
+typedef struct gpeed_gguf gpeed_gguf;
+
+typedef struct gpeed_gguf_tensor {
+    int dtype;           /* ggml type id (reference common.h:10-44) */
+    int n_dims;          /* 1..4 */
+    uint64_t dims[4];    /* ggml ne order: dims[0] is the contiguous one */
+    uint64_t offset;     /* byte offset inside its shard's tensor-data section */
+    uint64_t nbytes;     /* payload bytes (0 for a type without a known block size) */
+    int shard;           /* index of the shard file holding it */
+} gpeed_gguf_tensor;
+
+#define GPEED_GGUF_UINT8 0      /* metadata value types (gguf.h:15-29) */
+#define GPEED_GGUF_STRING 8
+#define GPEED_GGUF_ARRAY 9
+
+GPEED_API int gpeed_gguf_open(const char* path, gpeed_gguf** out);
+GPEED_API int gpeed_gguf_close(gpeed_gguf* g);
+GPEED_API int gpeed_gguf_counts(gpeed_gguf* g, int* n_shards, int64_t* n_tensors, int64_t* n_keys);
+/* i-th tensor name in shard order (GgufModel::tensor_names); valid until close. */
+GPEED_API int gpeed_gguf_tensor_name(gpeed_gguf* g, int64_t i, const char** name);
+/* i-th metadata key (union over shards, first-seen order); valid until close. */
+GPEED_API int gpeed_gguf_key_name(gpeed_gguf* g, int64_t i, const char** name);
+GPEED_API int gpeed_gguf_tensor_info(gpeed_gguf* g, const char* name, gpeed_gguf_tensor* out);
+/* Copies `bytes` bytes at `byte_off` inside tensor `name` to host memory. */
+GPEED_API int gpeed_gguf_read(gpeed_gguf* g, const char* name, uint64_t byte_off, uint64_t bytes, void* dst_host);
+/* Value type of `key` (GPEED_GGUF_*; for arrays also the element type and length). */
+GPEED_API int gpeed_gguf_meta_type(gpeed_gguf* g, const char* key, int* type, int* elem_type, uint64_t* n);
+/* Numeric scalar (index 0) or element `index` of a numeric array. */
+GPEED_API int gpeed_gguf_meta_f64(gpeed_gguf* g, const char* key, uint64_t index, double* out);
+GPEED_API int gpeed_gguf_meta_u64(gpeed_gguf* g, const char* key, uint64_t* out);
+GPEED_API int gpeed_gguf_meta_str(gpeed_gguf* g, const char* key, const char** out);
+/* MoE shape of block `blk`: H, I, E from the expert tensors' dims, the rest
+ * from "<general.architecture>.<key>" metadata with the reference's defaults
+ * (top_k 8, n_shared 1, scale 2.5, norm 1, swiglu limit 10); fails
+ * GPEED_ERR_UNSUPPORTED unless the gating function is sigmoid (2). */
+GPEED_API int gpeed_gguf_moe_shape(gpeed_gguf* g, int blk, gpeed_moe_shape* out);
+/* gpeed_tensor_upload of the IQ3_XXS tensor `name` straight from the file
+ * mapping (rows = product of dims[1..], in_dim = dims[0]): the payload the
+ * reference's WeightStore reads by name (weights.cpp:62-68, 167-203). */
+GPEED_API int gpeed_tensor_upload_gguf(gpeed_ctx* ctx, gpeed_gguf* g, const char* name, int* handle);
+/* Registers block `blk`'s MoE tensors as layer `layer` of ctx: the router
+ * (ffn_gate_inp, F32/F16/BF16), the bias (exp_probs_b, optional), routed
+ * experts [expert_begin, expert_begin + expert_count) of ffn_{gate,up,down}_exps
+ * (IQ3_XXS) and the shared expert (ffn_*_shexp).  expert_count < 0 = all. */
+GPEED_API int gpeed_moe_load_layer_gguf(gpeed_ctx* ctx, gpeed_gguf* g, int blk, int layer, int expert_begin,
+                                        int expert_count, gpeed_moe_shape* shape_out);
+
 #ifdef __cplusplus
 }
 #endif

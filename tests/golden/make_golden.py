@@ -17,6 +17,11 @@ Fixtures written (all small, committed):
   (zero, negative, subnormal and largest-normal fp16 scales; all-zero and
   all-one scale/sign words) and their decode by the reference's compiled
   dequantize() - bit patterns, for bit-exact comparison.
+* ref_selftest.gguf      the GGUF file that script writes (5 tensors: F32, F16,
+  BF16, Q8_0, IQ3_XXS; 7 metadata keys), and
+  ref_selftest_gguf.json what the reference's python/reference/gguf_reader.py
+  reads from it (version, data offset, metadata, tensor table in file order).
+  ``--only gguf`` rewrites just these two.
 * moe_tiny.npz           a tiny MoE layer (H=512, I=512, E=8, K=2, 1 shared
   expert; expert bytes from the counter-based generator, seed 7, streams
   gate..down_sh = 1..6) run through the reference harness: matvec_quant outputs, the
@@ -73,6 +78,31 @@ def selftest_vector(ref_root: str) -> dict:
     }
 
 
+def selftest_gguf(ref_root: str) -> None:
+    import shutil
+    with tempfile.TemporaryDirectory() as tmp:
+        subprocess.run([sys.executable, os.path.join(ref_root, "python", "tools", "make_test_gguf.py"),
+                        "--out", tmp], check=True, capture_output=True)
+        sys.path.insert(0, os.path.join(ref_root, "python", "reference"))
+        from gguf_reader import GgufReader  # the reference's reader
+
+        path = os.path.join(tmp, "test.gguf")
+        r = GgufReader.open(path)
+        table = {
+            "source": "reference python/tools/make_test_gguf.py (seed 1234), read by "
+                      "python/reference/gguf_reader.py",
+            "version": r.version,
+            "data_offset": r.data_offset,
+            "metadata": r.metadata,
+            "tensors": [{"name": n, "dims": list(r.tensors[n].dims), "type": r.tensors[n].ggml_type,
+                         "offset": r.tensors[n].offset} for n in r.tensor_order],
+        }
+        r._fh.close()
+        shutil.copyfile(path, os.path.join(HERE, "ref_selftest.gguf"))
+    with open(os.path.join(HERE, "ref_selftest_gguf.json"), "w") as fh:
+        json.dump(table, fh, indent=1)
+
+
 def edge_blocks(rng: np.random.Generator) -> np.ndarray:
     blocks = []
     for dbits in (0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x7BFF, 0xFBFF, 0x2C00, 0xAC00):
@@ -92,7 +122,11 @@ def edge_blocks(rng: np.random.Generator) -> np.ndarray:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("GPEED_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--only", choices=["gguf"], default=None)
     args = ap.parse_args()
+    selftest_gguf(args.ref)
+    if args.only == "gguf":
+        return 0
     ref = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libgpeed_ref.so"))
     rng = np.random.default_rng(20240601)
 
