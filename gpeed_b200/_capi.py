@@ -53,6 +53,7 @@ SIGNATURES = {
     "gpeed_ctx_profile": [_vp, _i],
     "gpeed_ctx_profile_read": [_vp, _vp, ctypes.POINTER(_i)],
     "gpeed_iq3xxs_dequantize": [_vp, _vp, _u64, _vp],
+    "gpeed_dequantize": [_i, _vp, _vp, _u64, _vp],
     "gpeed_tensor_upload": [_vp, _vp, _i, _i, _u64, _i, ctypes.POINTER(_i)],
     "gpeed_tensor_download": [_vp, _i, _vp],
     "gpeed_matvec_quant": [_vp, _i, _u64, _i, _i, _vp, _vp, _vp],

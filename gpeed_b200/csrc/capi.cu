@@ -588,6 +588,17 @@ int gpeed_synth_iq3xxs(void* dst, uint64_t seed, uint64_t stream, uint64_t block
     return GPEED_OK;
 }
 
+int gpeed_dequantize(int dtype, const void* src, float* dst, uint64_t n, void* stream) {
+    const int bv = gp::codec_block_values(dtype);
+    if (!bv) return fail(GPEED_ERR_UNSUPPORTED, "dequantize: type %d not implemented", dtype);
+    if (n % (uint64_t)bv) return fail(GPEED_ERR_INVALID, "dequantize: element count not a multiple of block size");
+    if (n == 0) return GPEED_OK;
+    if (!src || !dst || (reinterpret_cast<uintptr_t>(dst) & 15) || (bv == 1 && (reinterpret_cast<uintptr_t>(src) & 3)))
+        return fail(GPEED_ERR_INVALID, "dequantize: NULL or unaligned buffer (dst 16-byte, element-wise src 4-byte)");
+    GP_CUDA(gp::launch_codec_dequantize(dtype, src, dst, (int64_t)n, (cudaStream_t)stream));
+    return GPEED_OK;
+}
+
 int gpeed_tensor_upload(gpeed_ctx* c, const void* raw, int on_device, int dtype, uint64_t rows, int in_dim, int* handle) {
     if (!c || !raw || !handle) return fail(GPEED_ERR_INVALID, "NULL argument");
     if (dtype != GPEED_DTYPE_IQ3_XXS) return fail(GPEED_ERR_UNSUPPORTED, "dtype %d: only IQ3_XXS (18) is supported", dtype);

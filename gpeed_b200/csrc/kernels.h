@@ -207,4 +207,10 @@ bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
 size_t decode_layer_smem(int H, int I, int stages);
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st);
 
+// ---- codecs.cu: the other GGUF codecs (quant.cpp:130-573), bit-exact ----
+// values per block of a ggml type the reference decodes (1 for F32/F16/BF16), 0 if it decodes none
+int codec_block_values(int dtype);
+// dst[0, n) fp32 from src (device, GGUF bytes of `dtype`); n a whole number of blocks
+cudaError_t launch_codec_dequantize(int dtype, const void* src, float* dst, int64_t n, cudaStream_t st);
+
 }  // namespace gp

@@ -125,6 +125,13 @@ GPEED_API int gpeed_ctx_profile_read(gpeed_ctx* ctx, float* stage_ms /* [5] */, 
  * 256; the reference throws otherwise, quant.cpp:523-524). */
 GPEED_API int gpeed_iq3xxs_dequantize(const void* src_dev, float* dst_dev, uint64_t n, void* stream);
 
+/* Any codec the reference decodes, bit-exact (glm5::dequantize,
+ * quant.cpp:521-573 with the block decoders at quant.cpp:165-503): dtype =
+ * ggml id F32 0, F16 1, Q8_0 8, Q2_K 10, Q3_K 11, Q6_K 14, IQ3_XXS 18,
+ * IQ3_S 21, IQ2_S 22, IQ4_XS 23, BF16 30; n a whole number of blocks (the
+ * reference throws otherwise).  Device pointers; dst 16-byte aligned. */
+GPEED_API int gpeed_dequantize(int dtype, const void* src_dev, float* dst_dev, uint64_t n, void* stream);
+
 /* Uploads (or copies from device memory) an IQ3_XXS tensor of `rows` rows of
  * `in_dim` weights in GGUF row-major block order; the library keeps its own
  * device copy in a layout of its choosing.  Returns a handle (>= 0). */

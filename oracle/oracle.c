@@ -17,6 +17,7 @@
 #endif
 
 #include "../gpeed_b200/csrc/iq3xxs_grid.h"
+#include "../gpeed_b200/csrc/quant_grids.h"
 #include "../gpeed_b200/csrc/synth.h"
 
 #define QK_K 256
@@ -114,6 +115,208 @@ float orc_dot_f32(const float* a, const float* b, int n) {
     float acc = h0 + h1;
     for (; i < n; ++i) acc += a[i] * b[i];
     return acc;
+}
+
+/* ---- the other GGUF codecs the reference decodes (quant.cpp:165-519) ------
+ * One restated block decoder per type, writing the block's values in order.
+ * Arithmetic follows the reference's products term by term, without
+ * contraction (-ffp-contract=off here; the reference's -O3 -mavx2 -mfma build
+ * of quant.cpp does not contract Q2_K's dl * q - ml either: the two agree bit
+ * for bit on every type). */
+
+static const uint64_t kOrcIq2sGrid[1024] = {GPEED_IQ2S_GRID_VALUES};
+static const uint32_t kOrcIq3sGrid[512] = {GPEED_IQ3S_GRID_VALUES};
+static const int8_t kOrcIq4nl[16] = {GPEED_IQ4NL_VALUES};
+
+static inline float h2f_at(const uint8_t* p) {
+    uint16_t h;
+    memcpy(&h, p, 2);
+    return orc_f16_to_f32(h);
+}
+
+/* quant.cpp:165-184: y = d * q */
+static void blk_q8_0_(const uint8_t* b, float* y) {
+    const float d = h2f_at(b);
+    for (int i = 0; i < 32; ++i) y[i] = d * (float)(int8_t)b[2 + i];
+}
+
+/* quant.cpp:212-307 (the scalar branch; the AVX2 branch forms the same products) */
+static void blk_q6_k_(const uint8_t* b, float* y) {
+    const float d = h2f_at(b + 208);
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t* ql = b + 64 * h;
+        const uint8_t* qh = b + 128 + 32 * h;
+        const int8_t* sc = (const int8_t*)(b + 192 + 8 * h);
+        float* o = y + 128 * h;
+        for (int l = 0; l < 32; ++l) {
+            const int is = l / 16;
+            const int q1 = (int)((ql[l] & 0xF) | ((qh[l] & 3) << 4)) - 32;
+            const int q2 = (int)((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+            const int q3 = (int)((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+            const int q4 = (int)((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+            o[l] = d * (float)sc[is] * (float)q1;
+            o[l + 32] = d * (float)sc[is + 2] * (float)q2;
+            o[l + 64] = d * (float)sc[is + 4] * (float)q3;
+            o[l + 96] = d * (float)sc[is + 6] * (float)q4;
+        }
+    }
+}
+
+/* quant.cpp:309-335: y = dl * q - ml, 16 values per scale */
+static void blk_q2_k_(const uint8_t* b, float* y) {
+    const float d = h2f_at(b + 80), mn = h2f_at(b + 82);
+    int is = 0;
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t* q = b + 16 + 32 * h;
+        for (int j = 0; j < 4; ++j) {
+            const int shift = 2 * j;
+            for (int half = 0; half < 2; ++half) {
+                const uint8_t sc = b[is++];
+                const float dl = d * (float)(sc & 0xF), ml = mn * (float)(sc >> 4);
+                for (int l = 0; l < 16; ++l)
+                    *y++ = dl * (float)((q[l + 16 * half] >> shift) & 3) - ml;
+            }
+        }
+    }
+}
+
+/* quant.cpp:337-371: 6-bit scales unpacked from 12 bytes; high bit from hmask */
+static void blk_q3_k_(const uint8_t* b, float* y) {
+    const uint8_t* hm = b;
+    uint32_t aux[4];
+    memcpy(aux, b + 96, 12);
+    const uint32_t m1 = 0x03030303u, m2 = 0x0f0f0f0fu, t = aux[2];
+    aux[2] = ((aux[0] >> 4) & m2) | (((t >> 4) & m1) << 4);
+    aux[3] = ((aux[1] >> 4) & m2) | (((t >> 6) & m1) << 4);
+    aux[0] = (aux[0] & m2) | ((t & m1) << 4);
+    aux[1] = (aux[1] & m2) | (((t >> 2) & m1) << 4);
+    const int8_t* scales = (const int8_t*)aux;
+    const float d_all = h2f_at(b + 108);
+    int is = 0;
+    uint8_t m = 1;
+    for (int h = 0; h < 2; ++h) {
+        const uint8_t* q = b + 32 + 32 * h;
+        for (int j = 0; j < 4; ++j, m <<= 1) {
+            const int shift = 2 * j;
+            for (int half = 0; half < 2; ++half) {
+                const float dl = d_all * (float)(scales[is++] - 32);
+                for (int l = 16 * half; l < 16 * half + 16; ++l)
+                    *y++ = dl * (float)((int)((q[l] >> shift) & 3) - ((hm[l] & m) ? 0 : 4));
+            }
+        }
+    }
+}
+
+/* quant.cpp:373-419: 10-bit grid index (qs + 2 bits of qh), explicit sign bytes.
+ * As the AVX2 branch the reference builds with: the sign negates the grid byte
+ * before the product (dl * -g; the scalar branch's (dl * g) * -1 differs only
+ * in the sign of a NaN). */
+static void blk_iq2_s_(const uint8_t* b, float* y) {
+    const float d = h2f_at(b);
+    const uint8_t* qs = b + 2;
+    const uint8_t* qh = b + 66;
+    const uint8_t* scales = b + 74;
+    const uint8_t* signs = b + 2 + 32;
+    for (int ib = 0; ib < 8; ++ib) {
+        const float db0 = d * (0.5f + (float)(scales[ib] & 0xf)) * 0.25f;
+        const float db1 = d * (0.5f + (float)(scales[ib] >> 4)) * 0.25f;
+        for (int l = 0; l < 4; ++l) {
+            const float dl = l < 2 ? db0 : db1;
+            const uint32_t idx = (uint32_t)qs[l] | (((uint32_t)qh[ib] << (8 - 2 * l)) & 0x300u);
+            const uint64_t g = kOrcIq2sGrid[idx];
+            for (int j = 0; j < 8; ++j)
+                y[j] = dl * (float)((signs[l] >> j) & 1 ? -(int)(uint8_t)(g >> (8 * j)) : (int)(uint8_t)(g >> (8 * j)));
+            y += 8;
+        }
+        qs += 4;
+        signs += 4;
+    }
+}
+
+/* quant.cpp:421-483: 9-bit grid index (qs + 1 bit of qh), explicit sign bytes;
+ * signed grid byte times db, as the AVX2 branch */
+static void blk_iq3_s_(const uint8_t* b, float* y) {
+    const float d = h2f_at(b);
+    const uint8_t* qs = b + 2;
+    const uint8_t* qh = b + 66;
+    const uint8_t* signs = b + 74;
+    const uint8_t* scales = b + 106;
+    for (int ib = 0; ib < 8; ib += 2) {
+        const float db1 = d * (1.0f + 2.0f * (float)(scales[ib / 2] & 0xf));
+        const float db2 = d * (1.0f + 2.0f * (float)(scales[ib / 2] >> 4));
+        for (int pass = 0; pass < 2; ++pass) {
+            const float db = pass == 0 ? db1 : db2;
+            for (int l = 0; l < 4; ++l) {
+                const uint32_t i1 = (uint32_t)qs[2 * l] | (((uint32_t)qh[pass] << (8 - 2 * l)) & 256u);
+                const uint32_t i2 = (uint32_t)qs[2 * l + 1] | (((uint32_t)qh[pass] << (7 - 2 * l)) & 256u);
+                const uint32_t g1 = kOrcIq3sGrid[i1], g2 = kOrcIq3sGrid[i2];
+                for (int j = 0; j < 4; ++j) {
+                    const int a1 = (uint8_t)(g1 >> (8 * j)), a2 = (uint8_t)(g2 >> (8 * j));
+                    y[j] = db * (float)((signs[l] >> j) & 1 ? -a1 : a1);
+                    y[j + 4] = db * (float)((signs[l] >> (j + 4)) & 1 ? -a2 : a2);
+                }
+                y += 8;
+            }
+            qs += 8;
+            signs += 4;
+        }
+        qh += 2;
+    }
+}
+
+/* quant.cpp:485-503: 6-bit block scales, non-linear 4-bit values */
+static void blk_iq4_xs_(const uint8_t* b, float* y) {
+    const float d = h2f_at(b);
+    uint16_t sh;
+    memcpy(&sh, b + 2, 2);
+    const uint8_t* sl = b + 4;
+    const uint8_t* qs = b + 8;
+    for (int ib = 0; ib < 8; ++ib) {
+        const int ls = ((sl[ib / 2] >> (4 * (ib % 2))) & 0xf) | (((sh >> (2 * ib)) & 3) << 4);
+        const float dl = d * (float)(ls - 32);
+        for (int j = 0; j < 16; ++j) {
+            y[j] = dl * (float)kOrcIq4nl[qs[j] & 0xf];
+            y[j + 16] = dl * (float)kOrcIq4nl[qs[j] >> 4];
+        }
+        y += 32;
+        qs += 16;
+    }
+}
+
+/* quant.cpp:521-573: F32 / F16 / BF16 element-wise, block types per block;
+ * -1 for a count that is not a whole number of blocks, -2 for a type the
+ * reference does not decode (it throws in both cases). */
+int orc_dequantize(int type, const uint8_t* src, float* dst, uint64_t n) {
+    void (*fn)(const uint8_t*, float*) = NULL;
+    int bytes = 0, vals = 256;
+    switch (type) {
+        case 0: memcpy(dst, src, (size_t)n * 4); return 0;
+        case 1:
+            for (uint64_t i = 0; i < n; ++i) dst[i] = h2f_at(src + 2 * i);
+            return 0;
+        case 30:
+            for (uint64_t i = 0; i < n; ++i) {
+                uint16_t h;
+                memcpy(&h, src + 2 * i, 2);
+                const uint32_t bits = (uint32_t)h << 16;
+                memcpy(dst + i, &bits, 4);
+            }
+            return 0;
+        case 8: fn = blk_q8_0_; bytes = 34; vals = 32; break;
+        case 10: fn = blk_q2_k_; bytes = 84; break;
+        case 11: fn = blk_q3_k_; bytes = 110; break;
+        case 14: fn = blk_q6_k_; bytes = 210; break;
+        case 18: return orc_dequantize_iq3xxs(src, dst, n);
+        case 21: fn = blk_iq3_s_; bytes = 110; break;
+        case 22: fn = blk_iq2_s_; bytes = 82; break;
+        case 23: fn = blk_iq4_xs_; bytes = 136; break;
+        default: return -2;
+    }
+    if (n % (uint64_t)vals) return -1;
+    const int64_t nb = (int64_t)(n / (uint64_t)vals);
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < nb; ++i) fn(src + (size_t)i * bytes, dst + (size_t)i * vals);
+    return 0;
 }
 
 static size_t row_bytes(int in_dim) { return (size_t)(in_dim / QK_K) * IQ3XXS_BLOCK_BYTES; }

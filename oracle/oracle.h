@@ -28,6 +28,11 @@ float orc_f16_to_f32(uint16_t h);
 /* quant.cpp:521-573 (dequantize / dequantize_row for IQ3_XXS); returns -1 when
  * n is not a multiple of 256 (the reference throws, quant.cpp:523-524). */
 int orc_dequantize_iq3xxs(const uint8_t* src, float* dst, uint64_t n);
+/* quant.cpp:521-573 for every type the reference decodes: F32 (0), F16 (1),
+ * Q8_0 (8), Q2_K (10), Q3_K (11), Q6_K (14), IQ3_XXS (18), IQ3_S (21),
+ * IQ2_S (22), IQ4_XS (23), BF16 (30).  -1: n not a whole number of blocks;
+ * -2: type not decoded by the reference. */
+int orc_dequantize(int type, const uint8_t* src, float* dst, uint64_t n);
 /* simd.h:12-37: AVX2 dot_f32 summation order, emulated with fmaf. */
 float orc_dot_f32(const float* a, const float* b, int n);
 /* weights.cpp:167-203: dst[j] = dot(decode(row row0+j), x). */

@@ -67,6 +67,17 @@ class Checker:
             raise ValueError("dequantize failed")
         return out
 
+    def dequantize_type(self, dtype: int, raw: np.ndarray, n: int) -> np.ndarray:
+        """Any codec the reference decodes (ggml type id), n values."""
+        raw = np.ascontiguousarray(raw, np.uint8).reshape(-1)
+        out = np.empty(n, np.float32)
+        fn = self._f("dequantize")
+        fn.argtypes = [ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64]
+        rc = fn(dtype, _p(raw), _p(out), ctypes.c_uint64(n))
+        if rc:
+            raise ValueError(f"dequantize of type {dtype} failed ({rc})")
+        return out
+
     def matvec_quant(self, w, row0, in_dim, out_dim, x):
         x = np.ascontiguousarray(x, np.float32)
         y = np.empty(out_dim, np.float32)

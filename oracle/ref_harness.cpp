@@ -101,6 +101,16 @@ int ref_dequantize_iq3xxs(const uint8_t* src, float* dst, uint64_t n) {
     return 0;
 }
 
+// any codec the reference decodes (quant.cpp:521-573 dispatch): type = ggml id
+int ref_dequantize(int type, const uint8_t* src, float* dst, uint64_t n) {
+    try {
+        dequantize(static_cast<DType>(type), src, dst, n);
+    } catch (const std::exception&) {
+        return -1;
+    }
+    return 0;
+}
+
 float ref_dot_f32(const float* a, const float* b, int n) { return dot_f32(a, b, n); }
 
 int ref_matvec_quant(const uint8_t* w, uint64_t row0, int in_dim, int out_dim, const float* x,

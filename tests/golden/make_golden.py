@@ -22,6 +22,11 @@ Fixtures written (all small, committed):
   ref_selftest_gguf.json what the reference's python/reference/gguf_reader.py
   reads from it (version, data offset, metadata, tensor table in file order).
   ``--only gguf`` rewrites just these two.
+* codec_blocks.npz       for every codec the reference decodes (F16, BF16,
+  Q8_0, Q2_K, Q3_K, Q6_K, IQ3_XXS, IQ3_S, IQ2_S, IQ4_XS): 12 seeded and 24
+  edge blocks with the reference's compiled decode (bit patterns), and
+  codec_digests.json     the SHA-256 of its decode of 4096 seeded blocks per
+  type (2^20 values for F16/BF16); ``--only codecs``.
 * moe_tiny.npz           a tiny MoE layer (H=512, I=512, E=8, K=2, 1 shared
   expert; expert bytes from the counter-based generator, seed 7, streams
   gate..down_sh = 1..6) run through the reference harness: matvec_quant outputs, the
@@ -103,6 +108,33 @@ def selftest_gguf(ref_root: str) -> None:
         json.dump(table, fh, indent=1)
 
 
+def codec_fixture(ref) -> None:
+    """Every codec the reference decodes: seeded + edge blocks and the
+    reference's compiled decode of them (bit patterns), plus the SHA-256 of its
+    decode of a larger seeded set that tests regenerate (tests.helpers)."""
+    import hashlib
+    sys.path.insert(0, REPO)
+    from tests.helpers import CODECS, codec_blocks, codec_edge_blocks
+    arrays, digests = {}, {}
+    for t, (bb, vals, _) in CODECS.items():
+        small = np.concatenate([codec_blocks(t, 12, 500 + t), codec_edge_blocks(t)])
+        n = small.size // bb * vals
+        out = np.zeros(n, np.float32)
+        assert ref.ref_dequantize(t, ptr(small), ptr(out), ctypes.c_uint64(n)) == 0
+        arrays[f"blocks_{t}"] = small
+        arrays[f"bits_{t}"] = out.view(np.uint32)
+        big = codec_blocks(t, 4096 if vals > 1 else 1 << 20, 900 + t)
+        n = big.size // bb * vals
+        out = np.zeros(n, np.float32)
+        assert ref.ref_dequantize(t, ptr(big), ptr(out), ctypes.c_uint64(n)) == 0
+        digests[str(t)] = hashlib.sha256(out.tobytes()).hexdigest()
+    np.savez_compressed(os.path.join(HERE, "codec_blocks.npz"), **arrays)
+    with open(os.path.join(HERE, "codec_digests.json"), "w") as fh:
+        json.dump({"source": "reference cpp/core/src/quant.cpp dequantize (compiled), blocks from "
+                             "tests.helpers.codec_blocks(type, 4096 blocks or 2^20 halves, seed 900 + type)",
+                   "sha256": digests}, fh, indent=1)
+
+
 def edge_blocks(rng: np.random.Generator) -> np.ndarray:
     blocks = []
     for dbits in (0x0000, 0x8000, 0x0001, 0x03FF, 0x0400, 0x7BFF, 0xFBFF, 0x2C00, 0xAC00):
@@ -122,12 +154,15 @@ def edge_blocks(rng: np.random.Generator) -> np.ndarray:
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("GPEED_REFERENCE_ROOT", "/root/reference"))
-    ap.add_argument("--only", choices=["gguf"], default=None)
+    ap.add_argument("--only", choices=["gguf", "codecs"], default=None)
     args = ap.parse_args()
-    selftest_gguf(args.ref)
-    if args.only == "gguf":
-        return 0
     ref = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libgpeed_ref.so"))
+    if args.only in (None, "gguf"):
+        selftest_gguf(args.ref)
+    if args.only in (None, "codecs"):
+        codec_fixture(ref)
+    if args.only:
+        return 0
     rng = np.random.default_rng(20240601)
 
     with open(os.path.join(HERE, "iq3xxs_selftest.json"), "w") as fh:

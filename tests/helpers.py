@@ -34,3 +34,40 @@ def rel_l2(a, b):
     a = np.asarray(a, np.float64)
     b = np.asarray(b, np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# ggml type id -> (bytes per block, values per block, byte offsets of fp16 scales)
+CODECS = {8: (34, 32, (0,)), 10: (84, 256, (80, 82)), 11: (110, 256, (108,)), 14: (210, 256, (208,)),
+          18: (98, 256, (0,)), 21: (110, 256, (0,)), 22: (82, 256, (0,)), 23: (136, 256, (0,)),
+          1: (2, 1, ()), 30: (2, 1, ())}
+CODEC_NAMES = {8: "Q8_0", 10: "Q2_K", 11: "Q3_K", 14: "Q6_K", 18: "IQ3_XXS", 21: "IQ3_S", 22: "IQ2_S",
+               23: "IQ4_XS", 1: "F16", 30: "BF16"}
+
+
+def codec_blocks(dtype: int, nblocks: int, seed: int) -> np.ndarray:
+    """Seeded random GGUF blocks of `dtype` (uint8 [nblocks * bytes]): random
+    payload bytes, fp16 scales drawn from [1e-4, 2e-3) (element-wise types:
+    random finite halves / bf16 values)."""
+    bb, vals, dofs = CODECS[dtype]
+    rng = np.random.default_rng(seed)
+    blk = np.frombuffer(rng.bytes(bb * nblocks), np.uint8).reshape(nblocks, bb).copy()
+    for o in dofs:
+        d = (1e-4 + 1.9e-3 * rng.random(nblocks)).astype(np.float16)
+        blk[:, o:o + 2] = np.frombuffer(d.tobytes(), np.uint8).reshape(nblocks, 2)
+    return blk.reshape(-1)
+
+
+def codec_edge_blocks(dtype: int) -> np.ndarray:
+    """Edge cases: zero, negative, subnormal, largest, infinite and NaN fp16
+    scales, all-zero and all-one payloads."""
+    bb, vals, dofs = CODECS[dtype]
+    rng = np.random.default_rng(dtype)
+    out = []
+    for dbits in (0x0000, 0x8000, 0x0001, 0x03FF, 0x7BFF, 0xFBFF, 0x7C00, 0x7E01):
+        for fill in (None, 0x00, 0xFF):
+            b = np.frombuffer(rng.bytes(bb), np.uint8).copy() if fill is None else np.full(bb, fill, np.uint8)
+            for o in dofs:
+                b[o] = dbits & 0xFF
+                b[o + 1] = dbits >> 8
+            out.append(b)
+    return np.concatenate(out)
