@@ -785,6 +785,120 @@ def run_prefill_ep(args, rank, local_rank, world):
     return line
 
 
+CODEC_TYPES = {8: ("Q8_0", 34, 32, (0,)), 10: ("Q2_K", 84, 256, (80, 82)), 11: ("Q3_K", 110, 256, (108,)),
+               14: ("Q6_K", 210, 256, (208,)), 18: ("IQ3_XXS", 98, 256, (0,)), 21: ("IQ3_S", 110, 256, (0,)),
+               22: ("IQ2_S", 82, 256, (0,)), 23: ("IQ4_XS", 136, 256, (0,)), 1: ("F16", 2, 1, ()),
+               30: ("BF16", 2, 1, ())}
+
+
+def run_codecs(args):
+    """gpeed_dequantize over 2^26 values per codec (fp32 output 256 MiB, past L2):
+    achieved (read + write) GB/s per codec against the measured HBM copy peak."""
+    import ctypes
+    import numpy as np
+    import torch
+    from gpeed_b200 import _capi
+    hbm_peak, _, peak_src = peaks()
+    n = 1 << 26
+    rng = np.random.default_rng(0)
+    per = {}
+    tot_bytes = tot_ms = 0.0
+    launches = 0
+    with ClockSampler(0) as clk:
+        for t, (name, bb, vals, dofs) in CODEC_TYPES.items():
+            nb = n // vals
+            raw = np.frombuffer(rng.bytes(bb * nb), np.uint8).reshape(nb, bb).copy()
+            for o in dofs:
+                raw[:, o:o + 2] = np.frombuffer((1e-4 + 1.9e-3 * rng.random(nb)).astype(np.float16).tobytes(),
+                                                np.uint8).reshape(nb, 2)
+            if vals == 1:  # finite values for the element-wise types
+                raw = np.frombuffer((rng.standard_normal(n)).astype(np.float16 if t == 1 else np.float32)
+                                    .tobytes(), np.uint8).copy()
+                if t == 30:
+                    raw = raw.view(np.uint32) >> 16
+                    raw = raw.astype(np.uint16).view(np.uint8)
+            src = torch.from_numpy(raw).cuda()
+            dst = torch.empty(n, dtype=torch.float32, device="cuda")
+            call = lambda: _capi.call("gpeed_dequantize", t, ctypes.c_void_p(src.data_ptr()),
+                                      ctypes.c_void_p(dst.data_ptr()), ctypes.c_uint64(n), None)
+            for _ in range(args.warmup):
+                call()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                call()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            byt = raw.size + 4 * n
+            per[name] = {"ms": ms, "gb_s": byt / ms / 1e6, "frac": byt / ms / 1e6 / hbm_peak,
+                         "bytes_read_per_value": raw.size / n}
+            tot_bytes += byt * args.steps
+            tot_ms += ms * args.steps
+            launches += args.steps
+            del src, dst
+    gbs = tot_bytes / tot_ms / 1e6
+    return {"metric": "GGUF dequantisation throughput (read + write bytes)", "value": gbs, "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": tot_ms / launches,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "codecs: gpeed_dequantize, 2^26 values per codec (output 256 MiB, past L2)",
+                       "codecs": per},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "traffic": None, "peak_source": peak_src},
+            "gpu_launches": launches, "clocks": clk.summary()}
+
+
+def run_dense(args):
+    """Dense SwiGLU MLP of the leading layers (H 5120, intermediate 12288, IQ3_XXS)
+    through gpeed_dense_mlp_forward: batch 1 (GEMV, HBM-bound) and --tokens
+    (tensor cores)."""
+    import ctypes
+    import torch
+    from gpeed_b200 import Context, WeightStore, _capi
+    hbm_peak, tf_peak, peak_src = peaks()
+    Hd, Id = H, 12288
+    ctx = Context(0)
+    ws = WeightStore(ctx)
+    L = 4  # weight copies rotated so the batch-1 reads come from HBM (4 x 3 x 22.6 MB)
+    for c in range(L):
+        for m, (nm, rows, inn) in enumerate([("gate", Id, Hd), ("up", Id, Hd), ("down", Hd, Id)]):
+            raw = torch.empty(rows * inn // 256 * 98, dtype=torch.uint8, device="cuda")
+            _capi.call("gpeed_synth_iq3xxs", ctypes.c_void_p(raw.data_ptr()), ctypes.c_uint64(5),
+                       ctypes.c_uint64(10 * c + m), ctypes.c_uint64(0), ctypes.c_uint64(rows * inn // 256), None)
+            ws.add(f"{c}.{nm}", raw, rows, inn)
+    wbytes = 3 * Hd * Id // 256 * 98
+    res = {}
+    with ClockSampler(0) as clk:
+        for n in (1, args.tokens):
+            X = torch.randn(n, Hd, device="cuda").to(torch.bfloat16)
+            Y = torch.empty(n, Hd, dtype=torch.float32, device="cuda")
+            step = lambda c: ws.dense_mlp(f"{c}.gate", f"{c}.up", f"{c}.down", X, Y)
+            for i in range(args.warmup):
+                step(i % L)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(args.steps):
+                step(i % L)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            res[n] = {"ms": ms, "tokens_s": n / ms * 1e3, "weight_gb_s": wbytes / ms / 1e6,
+                      "hbm_frac": wbytes / ms / 1e6 / hbm_peak,
+                      "tflops": 2 * 3 * Hd * Id * n / ms / 1e9, "tensor_frac": 2 * 3 * Hd * Id * n / ms / 1e9 / tf_peak}
+    ctx.check()
+    ctx.close()
+    return {"metric": "dense SwiGLU MLP tokens/s (IQ3_XXS, H 5120, intermediate 12288)", "value": res[1]["tokens_s"],
+            "unit": "tokens/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": res[1]["ms"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8xint16 / fp16",
+            "data": "synthetic", "config": {"workload": f"dense: batch 1 and {args.tokens} tokens, {L} weight copies rotated",
+                                            "batches": res},
+            "roofline": {"bound": "hbm", "achieved": res[1]["weight_gb_s"], "peak": hbm_peak, "unit": "GB/s",
+                         "frac": res[1]["hbm_frac"], "traffic": None, "peak_source": peak_src},
+            "gpu_launches": None, "clocks": clk.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -794,7 +908,8 @@ def main():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--workload", default="decode1", choices=["decode1", "ragged64", "prefill", "stack40"],
+    ap.add_argument("--workload", default="decode1",
+                    choices=["decode1", "ragged64", "prefill", "stack40", "codecs", "dense"],
                     help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
     ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
@@ -821,6 +936,8 @@ def main():
         line = run_ragged(args, rank, local_rank, world)
     elif args.workload == "stack40":
         line = run_stack(args, rank, local_rank, world)
+    elif args.workload in ("codecs", "dense"):
+        line = (run_codecs if args.workload == "codecs" else run_dense)(args) if rank == 0 else None
     else:
         line = run_gpu(args, rank, local_rank, world)
     if world > 1:
