@@ -899,6 +899,77 @@ def run_dense(args):
             "gpu_launches": None, "clocks": clk.summary()}
 
 
+def run_mhc(args):
+    """mHC mixing + RMSNorm before the MoE layer and the stream update after it
+    (N = 4 streams of H = 5120): batch 1 and --tokens.  Each measurement replays
+    a CUDA graph of R calls over R different stream buffers (and, at batch 1,
+    R different fn matrices, as successive layers would read), so launch
+    overhead and L2 residency do not flatter the numbers."""
+    import torch
+    from gpeed_b200 import Context
+    from gpeed_b200.moe import mhc_post, mhc_pre
+    hbm_peak, _, peak_src = peaks()
+    Nh, W = 4, 24
+    ctx = Context(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    base, scale, nw = torch.randn(W, device="cuda"), torch.ones(3, device="cuda"), torch.ones(H, device="cuda")
+    res = {}
+    launches = 0
+    with ClockSampler(0) as clk:
+        for n in (1, args.tokens):
+            R = 64 if n == 1 else 2
+            S = [torch.randn(n, Nh, H, device="cuda", generator=g) for _ in range(R)]
+            F = [torch.randn(W, Nh * H, device="cuda", generator=g) * 0.02 for _ in range(R if n == 1 else 1)]
+            mlp = torch.randn(n, H, device="cuda", generator=g)
+            outs = []
+            for i in range(max(args.warmup, 3)):
+                outs = [mhc_pre(ctx, S[r], F[r % len(F)], base, scale, nw) for r in range(R)]
+                for r in range(R):
+                    mhc_post(ctx, S[r], mlp, outs[r][1], outs[r][2], out=S[r])
+            torch.cuda.synchronize()
+            gp_ = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gp_):
+                outs = [mhc_pre(ctx, S[r], F[r % len(F)], base, scale, nw) for r in range(R)]
+            gq = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gq):
+                for r in range(R):
+                    mhc_post(ctx, S[r], mlp, outs[r][1], outs[r][2], out=S[r])
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+            reps = max(1, args.steps // R)
+            gp_.replay()
+            gq.replay()
+            torch.cuda.synchronize()
+            ev[0].record()
+            for _ in range(reps):
+                gp_.replay()
+            ev[1].record()
+            for _ in range(reps):
+                gq.replay()
+            ev[2].record()
+            torch.cuda.synchronize()
+            t_pre = ev[0].elapsed_time(ev[1]) / (reps * R)
+            t_post = ev[1].elapsed_time(ev[2]) / (reps * R)
+            launches += reps * R * 3
+            pre_bytes = 2 * n * Nh * H * 4 + W * Nh * H * 4 + n * H * 2   # streams twice, fn once, bf16 x
+            post_bytes = 2 * n * Nh * H * 4 + n * H * 4
+            res[n] = {"pre_us": t_pre * 1e3, "post_us": t_post * 1e3, "pre_gb_s": pre_bytes / t_pre / 1e6,
+                      "pre_frac": pre_bytes / t_pre / 1e6 / hbm_peak, "post_gb_s": post_bytes / t_post / 1e6,
+                      "post_frac": post_bytes / t_post / 1e6 / hbm_peak}
+            del gp_, gq
+    ctx.check()
+    ctx.close()
+    big = res[args.tokens]
+    return {"metric": "mHC mixing + RMSNorm around the MoE layer, tokens/s (pre + post)",
+            "value": args.tokens / ((big["pre_us"] + big["post_us"]) * 1e-6), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": (big["pre_us"] + big["post_us"]) / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"mhc: N=4 streams of {H}, batch 1 and {args.tokens}", "batches": res},
+            "roofline": {"bound": "hbm", "achieved": big["pre_gb_s"], "peak": hbm_peak, "unit": "GB/s",
+                         "frac": big["pre_frac"], "traffic": None, "peak_source": peak_src,
+                         "kernel": "mhc_dot_kernel + mhc_finish_kernel"},
+            "gpu_launches": launches, "clocks": clk.summary()}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -909,7 +980,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="decode1",
-                    choices=["decode1", "ragged64", "prefill", "stack40", "codecs", "dense"],
+                    choices=["decode1", "ragged64", "prefill", "stack40", "codecs", "dense", "mhc"],
                     help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
     ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
@@ -936,8 +1007,9 @@ def main():
         line = run_ragged(args, rank, local_rank, world)
     elif args.workload == "stack40":
         line = run_stack(args, rank, local_rank, world)
-    elif args.workload in ("codecs", "dense"):
-        line = (run_codecs if args.workload == "codecs" else run_dense)(args) if rank == 0 else None
+    elif args.workload in ("codecs", "dense", "mhc"):
+        fn = {"codecs": run_codecs, "dense": run_dense, "mhc": run_mhc}[args.workload]
+        line = fn(args) if rank == 0 else None
     else:
         line = run_gpu(args, rank, local_rank, world)
     if world > 1:

@@ -35,6 +35,11 @@ class MoeShape(ctypes.Structure):
                 ("norm_topk", ctypes.c_int), ("swiglu_limit", ctypes.c_float)]
 
 
+class MhcParams(ctypes.Structure):
+    _fields_ = [("hc_mult", ctypes.c_int), ("sinkhorn_iters", ctypes.c_int), ("hc_eps", ctypes.c_float),
+                ("rms_eps", ctypes.c_float)]
+
+
 class GgufTensor(ctypes.Structure):
     _fields_ = [("dtype", ctypes.c_int), ("n_dims", ctypes.c_int), ("dims", ctypes.c_uint64 * 4),
                 ("offset", ctypes.c_uint64), ("nbytes", ctypes.c_uint64), ("shard", ctypes.c_int)]
@@ -71,6 +76,8 @@ SIGNATURES = {
     "gpeed_moe_experts": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp],
     "gpeed_moe_combine": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],
     "gpeed_dense_mlp_forward": [_vp, _i, _i, _i, _f, _vp, _i, _i, _vp, _vp],
+    "gpeed_mhc_pre": [_vp, _vp, _i, _i, ctypes.POINTER(MhcParams), _vp, _vp, _vp, _vp, _vp, _i, _vp, _vp, _vp],
+    "gpeed_mhc_post": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp, _vp],
     "gpeed_gguf_open": [_cs, ctypes.POINTER(_vp)],
     "gpeed_gguf_close": [_vp],
     "gpeed_gguf_counts": [_vp, ctypes.POINTER(_i), ctypes.POINTER(_i64), ctypes.POINTER(_i64)],

@@ -113,6 +113,7 @@ struct gpeed_ctx {
     cudaEvent_t ev[6] = {};
     double prof_ms[5] = {0, 0, 0, 0, 0};
     long prof_calls = 0;
+    DevBuf<float> mhc_partial;         // per-slice partial sums of the mHC dot products
     // pinned staging ring for weight uploads from pageable host memory
     uint8_t* stage[4] = {};
     cudaEvent_t stage_ev[4] = {};
@@ -505,6 +506,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     c->logits.release();
     c->xp.release();
     c->route_chunks.release();
+    c->mhc_partial.release();
     c->dx.release();
     c->hq.release();
     cudaFree(c->sync);
@@ -1123,6 +1125,46 @@ int gpeed_dense_mlp_forward(gpeed_ctx* c, int gate, int up, int down, float swig
     ro.topk_w = c->topk_w.p;
     auto nomark = [](int) {};
     return expert_pass(c, L, X, x_dtype == GPEED_DTYPE_BF16, ro, 0, nullptr, Y, st, nomark);
+}
+
+int gpeed_mhc_pre(gpeed_ctx* c, const float* streams, int n, int hidden, const gpeed_mhc_params* p, const float* fn,
+                  const float* base, const float* scale, const float* norm_w, void* x_out, int x_dtype, float* post,
+                  float* comb, void* stream) {
+    if (!c || !p) return fail(GPEED_ERR_INVALID, "ctx or params is NULL");
+    if (p->hc_mult < 1 || p->hc_mult > 4) return fail(GPEED_ERR_UNSUPPORTED, "hc_mult %d not in [1, 4]", p->hc_mult);
+    if (p->sinkhorn_iters < 1) return fail(GPEED_ERR_INVALID, "sinkhorn_iters must be >= 1");
+    if (hidden <= 0 || hidden % 4) return fail(GPEED_ERR_INVALID, "hidden %d must be a positive multiple of 4", hidden);
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (n < 0) return fail(GPEED_ERR_INVALID, "n_tok < 0");
+    if (n == 0) return GPEED_OK;
+    if (!streams || !fn || !base || !scale || !norm_w || !x_out || !post || !comb ||
+        (reinterpret_cast<uintptr_t>(streams) & 15) || (reinterpret_cast<uintptr_t>(fn) & 15))
+        return fail(GPEED_ERR_INVALID, "NULL buffer, or streams / fn not 16-byte aligned");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    if ((rc = c->mhc_partial.ensure((size_t)gp::mhc_partial_floats(n, p->hc_mult, hidden)))) return rc;
+    gp::MhcArgs a{p->hc_mult, hidden, p->sinkhorn_iters, p->hc_eps, p->rms_eps, fn, base, scale, norm_w, x_out,
+                  x_dtype == GPEED_DTYPE_BF16, post, comb};
+    GP_CUDA(gp::launch_mhc_pre(streams, n, a, c->mhc_partial.p, (cudaStream_t)stream));
+    return GPEED_OK;
+}
+
+int gpeed_mhc_post(gpeed_ctx* c, const float* streams_in, const float* mlp_out, const float* post, const float* comb,
+                   int n, int hidden, int hc_mult, float* streams_out, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if (hc_mult < 1 || hc_mult > 4) return fail(GPEED_ERR_UNSUPPORTED, "hc_mult %d not in [1, 4]", hc_mult);
+    if (hidden <= 0 || hidden % 4) return fail(GPEED_ERR_INVALID, "hidden %d must be a positive multiple of 4", hidden);
+    if (n < 0) return fail(GPEED_ERR_INVALID, "n_tok < 0");
+    if (n == 0) return GPEED_OK;
+    if (!streams_in || !mlp_out || !post || !comb || !streams_out ||
+        ((reinterpret_cast<uintptr_t>(streams_in) | reinterpret_cast<uintptr_t>(mlp_out) |
+          reinterpret_cast<uintptr_t>(streams_out)) & 15))
+        return fail(GPEED_ERR_INVALID, "NULL buffer, or streams / mlp_out not 16-byte aligned");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    GP_CUDA(gp::launch_mhc_post(streams_in, mlp_out, post, comb, n, hc_mult, hidden, streams_out, (cudaStream_t)stream));
+    return GPEED_OK;
 }
 
 int gpeed_moe_combine(gpeed_ctx* c, int n, int K, int hidden, const float* d_rows, const int* slot_of,

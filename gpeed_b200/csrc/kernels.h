@@ -213,4 +213,23 @@ int codec_block_values(int dtype);
 // dst[0, n) fp32 from src (device, GGUF bytes of `dtype`); n a whole number of blocks
 cudaError_t launch_codec_dequantize(int dtype, const void* src, float* dst, int64_t n, cudaStream_t st);
 
+// ---- mhc.cu: mHC residual mixing + RMSNorm around the MoE layer ----------
+struct MhcArgs {
+    int N, H;                 // hc_mult streams of H
+    int iters;                // Sinkhorn iterations (hc_sinkhorn_iters)
+    float hc_eps, rms_eps;
+    const float* fn;          // [(2+N)N][N*H]
+    const float* base;        // [(2+N)N]
+    const float* scale;       // [3]
+    const float* norm_w;      // [H] (ffn_norm)
+    void* x_out;              // [n][H] fp32 or bf16
+    int x_bf16;
+    float* post_out;          // [n][N]
+    float* comb_out;          // [n][N][N]
+};
+int mhc_partial_floats(int n, int N, int H);
+cudaError_t launch_mhc_pre(const float* streams, int n, const MhcArgs& a, float* partial, cudaStream_t st);
+cudaError_t launch_mhc_post(const float* in, const float* mlp, const float* post, const float* comb, int n, int N,
+                            int H, float* out, cudaStream_t st);
+
 }  // namespace gp

@@ -105,7 +105,7 @@ struct TcMaps {
     CUtensorMap b;         // token rows, fp16 [positions][kin], box {64, 256}, 128-byte swizzle
     CUtensorMap qs[2];     // per matrix: index bytes {64*NBLK, 8, groups}, box {16, 8, 16}
     CUtensorMap aux[2];    // sign/scale words {32*NBLK, 8, groups}, box {16, 8, 16}
-    CUtensorMap dsc[2];    // fp16 scales {8*NBLK, 2, groups}, box {8*NBLK, 2, 16}
+    CUtensorMap dsc[2];    // fp16 scales {16*NBLK/q, q, groups}, box {16*NBLK/q, q, 16}
 };
 
 // Sign mask of weight pair p (weights 2p, 2p+1) of a sign group: s8 = the 8
@@ -538,9 +538,13 @@ bool encode_weight_maps(TcMaps& m, int mi, const uint8_t* w, int64_t groups, int
             return false;
     }
     {
-        const cuuint64_t dims[3] = {8ull * nblk, 2, (cuuint64_t)groups};
-        const cuuint64_t str[2] = {8ull * nblk, gstride};
-        const cuuint32_t box[3] = {(cuuint32_t)(8 * nblk), 2, 16};
+        // a group's 16 * NBLK scale bytes as q rows of 16 * NBLK / q (one box row at most 256 bytes,
+        // a whole number of 16-byte units): q = the smallest divisor of NBLK leaving <= 16 blocks
+        int q = 1;
+        while (nblk / q > 16 || nblk % q) ++q;
+        const cuuint64_t dims[3] = {16ull * nblk / q, (cuuint64_t)q, (cuuint64_t)groups};
+        const cuuint64_t str[2] = {16ull * nblk / q, gstride};
+        const cuuint32_t box[3] = {(cuuint32_t)(16 * nblk / q), (cuuint32_t)q, 16};
         if (!encode(&m.dsc[mi], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, w + 768ull * nblk, dims, str, box,
                     CU_TENSOR_MAP_SWIZZLE_NONE))
             return false;
@@ -569,7 +573,8 @@ cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t
                           int npos, const TcArgs& args, int grid, cudaStream_t st) {
     TcMaps m{};
     const int kin = args.kin;
-    if (!tc_moe_supported(kin, args.nout) || npos <= 0 || weight_rows % 8) return cudaErrorInvalidValue;
+    if (kin % 256 || kin % TBM || args.nout % TBM || npos <= 0 || weight_rows % 8)
+        return cudaErrorInvalidValue;
     {
         const cuuint64_t dims[2] = {(cuuint64_t)kin, (cuuint64_t)npos};
         const cuuint64_t str[1] = {(cuuint64_t)kin * 2};

@@ -152,6 +152,42 @@ class MoeConfig:
                         int(self.norm_topk), self.swiglu_limit)
 
 
+@dataclass
+class MhcParams:
+    """mHC constants of glm5::ModelConfig (model_config.h:47-49, 68)."""
+    hc_mult: int = 4
+    sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+    rms_eps: float = 1e-5
+
+
+def mhc_pre(ctx: Context, streams: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: torch.Tensor,
+            norm_w: torch.Tensor, params: MhcParams = MhcParams(), x_dtype=torch.bfloat16, stream=None):
+    """Model::hc_forward + the ffn RMSNorm (model.cpp:205-263, 292-296) for n tokens:
+    streams [n, N, H] fp32 -> (x [n, H] (the MoE input), post [n, N], comb [n, N, N])."""
+    n, N, H = streams.shape
+    x = torch.empty(n, H, dtype=x_dtype, device=streams.device)
+    post = torch.empty(n, N, dtype=torch.float32, device=streams.device)
+    comb = torch.empty(n, N, N, dtype=torch.float32, device=streams.device)
+    p = _capi.MhcParams(N, params.sinkhorn_iters, params.hc_eps, params.rms_eps)
+    dt = _capi.DTYPE_BF16 if x_dtype == torch.bfloat16 else _capi.DTYPE_F32
+    call("gpeed_mhc_pre", ctx.handle, _ptr(streams.contiguous()), n, H, ctypes.byref(p), _ptr(fn.contiguous()),
+         _ptr(base.contiguous()), _ptr(scale.contiguous()), _ptr(norm_w.contiguous()), _ptr(x), dt, _ptr(post),
+         _ptr(comb), _stream(stream))
+    return x, post, comb
+
+
+def mhc_post(ctx: Context, streams_in: torch.Tensor, mlp_out: torch.Tensor, post: torch.Tensor, comb: torch.Tensor,
+             out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+    """Streams after the MLP (model.cpp:309-318): out[t][k] = post[t][k] mlp[t] + sum_m comb[t][m][k] in[t][m]."""
+    n, N, H = streams_in.shape
+    if out is None:
+        out = torch.empty_like(streams_in)
+    call("gpeed_mhc_post", ctx.handle, _ptr(streams_in), _ptr(mlp_out.contiguous()), _ptr(post.contiguous()),
+         _ptr(comb.contiguous()), n, H, N, _ptr(out), _stream(stream))
+    return out
+
+
 class MoeLayer:
     """One routed-expert MoE layer resident on the device."""
 

@@ -247,6 +247,36 @@ GPEED_API int gpeed_moe_combine(gpeed_ctx* ctx, int n_tok, int K, int hidden, co
 GPEED_API int gpeed_dense_mlp_forward(gpeed_ctx* ctx, int gate, int up, int down, float swiglu_limit, const void* X_dev,
                                       int x_dtype, int n_tok, float* Y_dev, void* stream);
 
+/* ---- mHC residual mixing + RMSNorm on either side of the MoE layer
+ * (Model::hc_forward, model.cpp:205-263, the ffn norm at model.cpp:292-296 and
+ * the stream update at model.cpp:309-318; run_chunk passes 4 and 6,
+ * model_batch.cpp:374-410).  Per token t, hc_mult = N residual streams of H:
+ *
+ *   gpeed_mhc_pre:  x[t] = rmsnorm(sum_n pre[n] streams[t][n]) * norm_w, the
+ *                   MoE / dense-MLP input (fp32 or bf16), with pre, post and
+ *                   the Sinkhorn-normalised comb [N][N] formed from the
+ *                   (2+N)N dot products of fn with rmsnorm(streams[t]);
+ *   gpeed_mhc_post: streams_out[t][n] = post[t][n] mlp_out[t]
+ *                   + sum_m comb[t][m][n] streams_in[t][m]  (in place allowed).
+ *
+ * fn [(2+N)N][N*H], base [(2+N)N], scale [3], norm_w [H], streams [n][N][H],
+ * all fp32 device buffers (the reference widens these tensors to fp32 too).
+ * Floating point: sums run in a different order than the reference's
+ * (relative differences ~1e-6). */
+typedef struct gpeed_mhc_params {
+    int hc_mult;         /* N, 1..4 (model_config.h:47, default 4) */
+    int sinkhorn_iters;  /* 20 */
+    float hc_eps;        /* 1e-6 */
+    float rms_eps;       /* 1e-5 */
+} gpeed_mhc_params;
+GPEED_API int gpeed_mhc_pre(gpeed_ctx* ctx, const float* streams_dev, int n_tok, int hidden,
+                            const gpeed_mhc_params* params, const float* fn_dev, const float* base_dev,
+                            const float* scale_dev, const float* norm_w_dev, void* x_dev, int x_dtype, float* post_dev,
+                            float* comb_dev, void* stream);
+GPEED_API int gpeed_mhc_post(gpeed_ctx* ctx, const float* streams_in_dev, const float* mlp_out_dev,
+                             const float* post_dev, const float* comb_dev, int n_tok, int hidden, int hc_mult,
+                             float* streams_out_dev, void* stream);
+
 /* ---- GGUF model files (cpp/core/include/glm5/gguf.h; gguf.cpp).
  *
  *   gpeed_gguf_open           <- GgufModel::load(GgufModel::discover_shards(path))

@@ -557,6 +557,97 @@ int orc_moe_batch(const orc_shape* s, const float* router_w, const float* corr,
     return 0;
 }
 
+/* ---- mHC residual mixing around the MoE layer ----------------------------- */
+
+/* ops.h rmsnorm: y = x * (1 / sqrt(mean(x^2) + eps)) [* w] */
+static void rmsnorm_(float* out, const float* x, const float* w, int n, float eps) {
+    float ss = 0.0f;
+    for (int i = 0; i < n; ++i) ss += x[i] * x[i];
+    const float rstd = 1.0f / sqrtf(ss / (float)n + eps);
+    for (int i = 0; i < n; ++i) out[i] = w ? x[i] * rstd * w[i] : x[i] * rstd;
+}
+
+/* model.cpp:49-59 softmax (max-subtracted) */
+static void softmax_(float* s, int n) {
+    float mx = s[0];
+    for (int i = 1; i < n; ++i) mx = s[i] > mx ? s[i] : mx;
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) {
+        s[i] = expf(s[i] - mx);
+        sum += s[i];
+    }
+    const float inv = 1.0f / sum;
+    for (int i = 0; i < n; ++i) s[i] *= inv;
+}
+
+/* model.cpp:205-263 (Model::hc_forward) then the ffn norm (model.cpp:292-296,
+ * model_batch.cpp:374-384), per token */
+int orc_mhc_pre(const float* streams, int n, int N, int H, int iters, float hc_eps, float rms_eps, const float* fn,
+                const float* base, const float* scale, const float* norm_w, float* x, float* post, float* comb) {
+    if (N < 1 || N > 8 || iters < 1) return -1;
+    const int HN = N * H, W = (2 + N) * N;
+    float* flat = (float*)malloc(sizeof(float) * (size_t)HN);
+    float* mixed = (float*)malloc(sizeof(float) * (size_t)H);
+    float w[80], pre[8], row[8];
+    for (int t = 0; t < n; ++t) {
+        const float* S = streams + (size_t)t * HN;
+        float* po = post + (size_t)t * N;
+        float* cb = comb + (size_t)t * N * N;
+        rmsnorm_(flat, S, NULL, HN, rms_eps);
+        for (int j = 0; j < W; ++j) w[j] = orc_dot_f32(fn + (size_t)j * HN, flat, HN);  /* matvec, model.cpp:41-46 */
+        for (int i = 0; i < N; ++i) {
+            pre[i] = 1.0f / (1.0f + expf(-(w[i] * scale[0] + base[i]))) + hc_eps;
+            po[i] = 2.0f * (1.0f / (1.0f + expf(-(w[N + i] * scale[1] + base[N + i]))));
+        }
+        for (int i = 0; i < N; ++i) {
+            for (int j = 0; j < N; ++j) row[j] = w[2 * N + i * N + j] * scale[2] + base[2 * N + i * N + j];
+            softmax_(row, N);
+            for (int j = 0; j < N; ++j) cb[i * N + j] = row[j] + hc_eps;
+        }
+        for (int j = 0; j < N; ++j) {  /* Sinkhorn: columns, then (iters - 1) x (rows, columns) */
+            float d = 0.0f;
+            for (int i = 0; i < N; ++i) d += cb[i * N + j];
+            d += hc_eps;
+            for (int i = 0; i < N; ++i) cb[i * N + j] /= d;
+        }
+        for (int it = 0; it < iters - 1; ++it) {
+            for (int i = 0; i < N; ++i) {
+                float d = 0.0f;
+                for (int j = 0; j < N; ++j) d += cb[i * N + j];
+                d += hc_eps;
+                for (int j = 0; j < N; ++j) cb[i * N + j] /= d;
+            }
+            for (int j = 0; j < N; ++j) {
+                float d = 0.0f;
+                for (int i = 0; i < N; ++i) d += cb[i * N + j];
+                d += hc_eps;
+                for (int i = 0; i < N; ++i) cb[i * N + j] /= d;
+            }
+        }
+        for (int d = 0; d < H; ++d) mixed[d] = 0.0f;
+        for (int i = 0; i < N; ++i)
+            for (int d = 0; d < H; ++d) mixed[d] += pre[i] * S[(size_t)i * H + d];
+        rmsnorm_(x + (size_t)t * H, mixed, norm_w, H, rms_eps);
+    }
+    free(flat);
+    free(mixed);
+    return 0;
+}
+
+/* model.cpp:309-318 / model_batch.cpp:395-409: streams after the MLP */
+int orc_mhc_post(const float* in, const float* mlp, const float* post, const float* comb, int n, int N, int H,
+                 float* out) {
+    for (int t = 0; t < n; ++t)
+        for (int k = 0; k < N; ++k)
+            for (int d = 0; d < H; ++d) {
+                float acc = post[(size_t)t * N + k] * mlp[(size_t)t * H + d];
+                for (int m = 0; m < N; ++m)
+                    acc += comb[(size_t)t * N * N + m * N + k] * in[((size_t)t * N + m) * H + d];
+                out[((size_t)t * N + k) * H + d] = acc;
+            }
+    return 0;
+}
+
 void orc_synth_iq3xxs(uint64_t seed, uint64_t stream, uint64_t block0, uint64_t nblocks, uint8_t* dst) {
 #pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < (int64_t)nblocks; ++b)

@@ -33,6 +33,13 @@ int orc_dequantize_iq3xxs(const uint8_t* src, float* dst, uint64_t n);
  * IQ2_S (22), IQ4_XS (23), BF16 (30).  -1: n not a whole number of blocks;
  * -2: type not decoded by the reference. */
 int orc_dequantize(int type, const uint8_t* src, float* dst, uint64_t n);
+/* model.cpp:205-263 (Model::hc_forward) + the ffn RMSNorm, per token:
+ * streams [n][N][H] -> x [n][H], post [n][N], comb [n][N][N]. */
+int orc_mhc_pre(const float* streams, int n, int N, int H, int iters, float hc_eps, float rms_eps, const float* fn,
+                const float* base, const float* scale, const float* norm_w, float* x, float* post, float* comb);
+/* model.cpp:309-318: out[t][k] = post[t][k] mlp[t] + sum_m comb[t][m][k] in[t][m]. */
+int orc_mhc_post(const float* in, const float* mlp, const float* post, const float* comb, int n, int N, int H,
+                 float* out);
 /* simd.h:12-37: AVX2 dot_f32 summation order, emulated with fmaf. */
 float orc_dot_f32(const float* a, const float* b, int n);
 /* weights.cpp:167-203: dst[j] = dot(decode(row row0+j), x). */

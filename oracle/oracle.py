@@ -78,6 +78,32 @@ class Checker:
             raise ValueError(f"dequantize of type {dtype} failed ({rc})")
         return out
 
+    def mhc_pre(self, streams, fn, base, scale, norm_w, N=4, iters=20, hc_eps=1e-6, rms_eps=1e-5):
+        """model.cpp:205-263 + the ffn RMSNorm: streams [n][N][H] -> (x [n][H], post [n][N], comb [n][N][N])."""
+        streams = np.ascontiguousarray(streams, np.float32)
+        n, H = streams.shape[0], streams.shape[-1]
+        x = np.empty((n, H), np.float32)
+        post = np.empty((n, N), np.float32)
+        comb = np.empty((n, N, N), np.float32)
+        fn_, base_, scale_, w_ = (np.ascontiguousarray(a, np.float32) for a in (fn, base, scale, norm_w))
+        f = self._f("mhc_pre")
+        f.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float,
+                      ctypes.c_float] + [ctypes.c_void_p] * 7
+        if f(_p(streams), n, N, H, iters, hc_eps, rms_eps, _p(fn_), _p(base_), _p(scale_), _p(w_), _p(x), _p(post),
+             _p(comb)):
+            raise ValueError("mhc_pre failed")
+        return x, post, comb
+
+    def mhc_post(self, streams_in, mlp, post, comb):
+        streams_in = np.ascontiguousarray(streams_in, np.float32)
+        n, N, H = streams_in.shape
+        out = np.empty_like(streams_in)
+        args = [np.ascontiguousarray(a, np.float32) for a in (mlp, post, comb)]
+        f = self._f("mhc_post")
+        f.argtypes = [ctypes.c_void_p] * 4 + [ctypes.c_int] * 3 + [ctypes.c_void_p]
+        f(_p(streams_in), _p(args[0]), _p(args[1]), _p(args[2]), n, N, H, _p(out))
+        return out
+
     def matvec_quant(self, w, row0, in_dim, out_dim, x):
         x = np.ascontiguousarray(x, np.float32)
         y = np.empty(out_dim, np.float32)
