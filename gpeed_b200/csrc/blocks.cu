@@ -1,7 +1,7 @@
-// Block-level IQ3_XXS kernels: the bit-exact fp32 dequantizer (reference
-// cpp/core/src/quant.cpp:186-210 blk_iq3_xxs, :521-573 dequantize), the
-// lossless raw <-> repacked layout conversion used for library-owned weights,
-// the decode-table image, and the device side of the synthetic generator.
+// Block-level IQ3_XXS kernels: the lossless raw <-> repacked layout
+// conversion used for library-owned weights, the decode-table image, and the
+// device side of the synthetic generator.  (The bit-exact fp32 dequantizer,
+// quant.cpp:186-210 / :521-573, is the IQ3_XXS case of codecs.cu.)
 #include <cuda_fp16.h>
 
 #include "iq3xxs.cuh"
@@ -10,57 +10,6 @@
 
 namespace gp {
 namespace {
-
-// One warp per 4 blocks: the 392 contiguous bytes are read as 98 aligned
-// 32-bit words (the group of 4 blocks starts 8-byte aligned whenever the
-// tensor is 16-byte aligned), staged in shared memory, then each lane decodes
-// one 32-weight sub-block and writes 32 floats with 16-byte stores.
-constexpr int kDqWarps = 8;
-
-__global__ void __launch_bounds__(32 * kDqWarps) dequant_kernel(const uint8_t* __restrict__ raw, float* __restrict__ dst,
-                                                                int64_t nblocks) {
-    __shared__ uint32_t s_grid[256];
-    __shared__ __align__(16) uint8_t s_blk[kDqWarps][4 * 98 + 8];
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) s_grid[i] = gp_iq3xxs_grid_dev[i];
-    __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t ngroups = (nblocks + 3) / 4;
-    for (int64_t grp = (int64_t)blockIdx.x * kDqWarps + warp; grp < ngroups; grp += (int64_t)gridDim.x * kDqWarps) {
-        const int64_t b0 = grp * 4;
-        const int nb = (int)gp_min64(4, nblocks - b0);
-        const uint8_t* src = raw + b0 * 98;
-        // byte-granular staging (keeps any source alignment legal)
-        for (int i = lane; i < nb * 98; i += 32) s_blk[warp][i] = src[i];
-        __syncwarp();
-        const int blk = lane >> 3, ib = lane & 7;
-        if (blk < nb) {
-            const uint8_t* p = s_blk[warp] + blk * 98;
-            const uint16_t dh = (uint16_t)(p[0] | (p[1] << 8));
-            const float d = __half2float(__ushort_as_half(dh));  // exact, incl. subnormals
-            const uint8_t* qs = p + 2 + 8 * ib;
-            const uint8_t* sa = p + 66 + 4 * ib;
-            const uint32_t aux = (uint32_t)sa[0] | ((uint32_t)sa[1] << 8) | ((uint32_t)sa[2] << 16) |
-                                 ((uint32_t)sa[3] << 24);
-            const float db = iq3_db(d, aux);
-            float out[32];
-#pragma unroll
-            for (int l = 0; l < 4; ++l) {
-                const uint32_t k7 = (aux >> (7 * l)) & 127u;
-                const uint32_t signs = k7 | ((uint32_t)(__popc(k7) & 1) << 7);
-                const uint32_t g1 = s_grid[qs[2 * l]], g2 = s_grid[qs[2 * l + 1]];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    out[8 * l + j] = iq3_weight_f32(db, (g1 >> (8 * j)) & 0xFF, (signs >> j) & 1);
-                    out[8 * l + j + 4] = iq3_weight_f32(db, (g2 >> (8 * j)) & 0xFF, (signs >> (j + 4)) & 1);
-                }
-            }
-            float4* o = reinterpret_cast<float4*>(dst + (b0 + blk) * 256 + 32 * ib);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = make_float4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
-        }
-        __syncwarp();
-    }
-}
 
 // raw row-major blocks -> row groups of 8: [qs 8 x nblk x 64][aux 8 x nblk x 32][d 8 x nblk x 2]
 // One thread per (row, block); rows past `rows` in the last group are zero-filled.
@@ -127,11 +76,7 @@ __global__ void synth_kernel(uint8_t* __restrict__ dst, uint64_t seed, uint64_t 
 }  // namespace
 
 cudaError_t launch_dequantize(const uint8_t* raw, float* dst, int64_t nblocks, cudaStream_t st) {
-    if (nblocks <= 0) return cudaSuccess;
-    const int64_t groups = (nblocks + 3) / 4;
-    const int grid = (int)gp_min64((groups + kDqWarps - 1) / kDqWarps, 148 * 16);
-    dequant_kernel<<<grid, 32 * kDqWarps, 0, st>>>(raw, dst, nblocks);
-    return cudaGetLastError();
+    return launch_codec_dequantize(18, raw, dst, nblocks * 256, st);  // codecs.cu
 }
 
 cudaError_t launch_repack(const uint8_t* raw, uint8_t* packed, int64_t rows, int in_dim, cudaStream_t st) {

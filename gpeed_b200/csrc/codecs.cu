@@ -1,6 +1,6 @@
-// Dequantisation of the other GGUF codecs the reference decodes (quant.cpp:
-// 130-573): F16, BF16, Q8_0, Q2_K, Q3_K, Q6_K, IQ2_S, IQ3_S, IQ4_XS (IQ3_XXS has
-// its own kernel in blocks.cu, F32 is a copy).  Bit-exact with the reference:
+// Dequantisation of every GGUF codec the reference decodes (quant.cpp:
+// 130-573): F16, BF16, Q8_0, Q2_K, Q3_K, Q6_K, IQ3_XXS, IQ2_S, IQ3_S, IQ4_XS
+// (F32 is a copy).  Bit-exact with the reference:
 // every value is formed with the same fp32 products in the same order
 // (__fmul_rn / __fsub_rn keep the compiler from contracting them), and fp16
 // scales widen with the reference's integer conversion (quant.cpp:130-154),
@@ -18,6 +18,7 @@
 #include <stdint.h>
 
 #include "kernels.h"
+#include "iq3xxs_grid.h"
 #include "quant_grids.h"
 
 namespace gp {
@@ -25,6 +26,7 @@ namespace {
 
 __device__ const uint64_t g_iq2s_grid[1024] = {GPEED_IQ2S_GRID_VALUES};
 __device__ const uint32_t g_iq3s_grid[512] = {GPEED_IQ3S_GRID_VALUES};
+__device__ const uint32_t g_iq3xxs_grid[256] = {GPEED_IQ3XXS_GRID_VALUES};
 __device__ __align__(16) const int8_t g_iq4nl[16] = {GPEED_IQ4NL_VALUES};
 
 constexpr int kCdWarps = 8;
@@ -160,6 +162,28 @@ struct Codec<21> {  // IQ3_S, quant.cpp:421-483
 };
 
 template <>
+struct Codec<18> {  // IQ3_XXS, quant.cpp:186-210: y = (db * grid) * sign, db = d * (0.5 + aux>>28) * 0.5
+    static constexpr int kBytes = 98, kVals = 256;
+    __device__ static void unit(const uint8_t* b, int s, const uint8_t* tab, float* y) {
+        const int ib = s >> 2, l = s & 3;
+        const uint8_t* sa = b + 66 + 4 * ib;
+        const uint32_t aux = (uint32_t)sa[0] | ((uint32_t)sa[1] << 8) | ((uint32_t)sa[2] << 16) | ((uint32_t)sa[3] << 24);
+        const float db = __fmul_rn(__fmul_rn(ld_f16(b), __fadd_rn(0.5f, (float)(aux >> 28))), 0.5f);
+        const uint32_t k7 = (aux >> (7 * l)) & 127u;
+        const uint32_t sg = k7 | ((uint32_t)(__popc(k7) & 1) << 7);  // the sign table entry: k | parity(k) << 7
+        const uint32_t* grid = reinterpret_cast<const uint32_t*>(tab);
+        const uint32_t g1 = grid[b[2 + 8 * ib + 2 * l]], g2 = grid[b[2 + 8 * ib + 2 * l + 1]];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float w1 = __fmul_rn(db, (float)((g1 >> (8 * j)) & 0xFF));
+            const float w2 = __fmul_rn(db, (float)((g2 >> (8 * j)) & 0xFF));
+            y[j] = ((sg >> j) & 1) ? -w1 : w1;
+            y[j + 4] = ((sg >> (j + 4)) & 1) ? -w2 : w2;
+        }
+    }
+};
+
+template <>
 struct Codec<23> {  // IQ4_XS, quant.cpp:485-503: y = d * (ls - 32) * v[nibble]
     static constexpr int kBytes = 136, kVals = 256;
     __device__ static void unit(const uint8_t* b, int s, const uint8_t* tab, float* y) {
@@ -176,7 +200,7 @@ struct Codec<23> {  // IQ4_XS, quant.cpp:485-503: y = d * (ls - 32) * v[nibble]
 
 template <int T>
 __device__ __forceinline__ int table_bytes() {
-    return T == 22 ? 8192 : T == 21 ? 2048 : T == 23 ? 16 : 0;
+    return T == 22 ? 8192 : T == 21 ? 2048 : T == 18 ? 1024 : T == 23 ? 16 : 0;
 }
 
 template <int T>
@@ -185,11 +209,12 @@ __global__ void __launch_bounds__(32 * kCdWarps) codec_kernel(const uint8_t* __r
     using C = Codec<T>;
     constexpr int kPer = 256 / C::kVals;           // blocks per warp step
     constexpr int kStage = (kPer * C::kBytes + 15) & ~15;
-    __shared__ __align__(16) uint8_t s_tab[T == 22 ? 8192 : T == 21 ? 2048 : 16];
+    __shared__ __align__(16) uint8_t s_tab[T == 22 ? 8192 : T == 21 ? 2048 : T == 18 ? 1024 : 16];
     __shared__ __align__(16) uint8_t s_blk[kCdWarps][kStage];
     if (table_bytes<T>()) {
         const uint8_t* t = T == 22 ? reinterpret_cast<const uint8_t*>(g_iq2s_grid)
                          : T == 21 ? reinterpret_cast<const uint8_t*>(g_iq3s_grid)
+                         : T == 18 ? reinterpret_cast<const uint8_t*>(g_iq3xxs_grid)
                                    : reinterpret_cast<const uint8_t*>(g_iq4nl);
         for (int i = threadIdx.x; i < table_bytes<T>() / 4; i += blockDim.x)
             reinterpret_cast<uint32_t*>(s_tab)[i] = reinterpret_cast<const uint32_t*>(t)[i];
@@ -215,8 +240,30 @@ __global__ void __launch_bounds__(32 * kCdWarps) codec_kernel(const uint8_t* __r
     }
 }
 
+// 8 values per thread per step (one 16-byte load, two float4 stores) when the
+// source is 16-byte aligned; the remainder (and unaligned sources) one by one
 __global__ void f16_kernel(const uint16_t* __restrict__ src, float* __restrict__ dst, int64_t n, int bf16) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x, tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    int64_t done = 0;
+    if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+        const int64_t n8 = n / 8;
+        for (int64_t i = tid; i < n8; i += stride) {
+            const uint4 v = reinterpret_cast<const uint4*>(src)[i];
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            float y[8];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t lo = w[q] & 0xffffu, hi = w[q] >> 16;
+                y[2 * q] = bf16 ? __uint_as_float(lo << 16) : f16_ref(lo);
+                y[2 * q + 1] = bf16 ? __uint_as_float(hi << 16) : f16_ref(hi);
+            }
+            float4* o = reinterpret_cast<float4*>(dst + 8 * i);
+            o[0] = make_float4(y[0], y[1], y[2], y[3]);
+            o[1] = make_float4(y[4], y[5], y[6], y[7]);
+        }
+        done = n8 * 8;
+    }
+    for (int64_t i = done + tid; i < n; i += stride) {
         const uint32_t h = src[i];
         dst[i] = bf16 ? __uint_as_float(h << 16) : f16_ref(h);
     }
@@ -252,8 +299,9 @@ cudaError_t launch_codec_dequantize(int dtype, const void* src, float* dst, int6
         case 0: return cudaMemcpyAsync(dst, src, (size_t)n * 4, cudaMemcpyDeviceToDevice, st);
         case 1:
         case 30: {
-            int64_t grid = (n + 255) / 256;
+            int64_t grid = (n / 8 + 255) / 256;
             if (grid > 148 * 16) grid = 148 * 16;
+            if (grid < 1) grid = 1;
             f16_kernel<<<(int)grid, 256, 0, st>>>(static_cast<const uint16_t*>(src), dst, n, dtype == 30);
             return cudaGetLastError();
         }
@@ -261,7 +309,7 @@ cudaError_t launch_codec_dequantize(int dtype, const void* src, float* dst, int6
         case 10: return launch_codec<10>(s, dst, n, st);
         case 11: return launch_codec<11>(s, dst, n, st);
         case 14: return launch_codec<14>(s, dst, n, st);
-        case 18: return launch_dequantize(s, dst, n / 256, st);
+        case 18: return launch_codec<18>(s, dst, n, st);
         case 21: return launch_codec<21>(s, dst, n, st);
         case 22: return launch_codec<22>(s, dst, n, st);
         case 23: return launch_codec<23>(s, dst, n, st);

@@ -13,14 +13,15 @@
 //         mix  = sum_n pre[n] streams[n];  x = mix * rsqrt(mean(mix^2) + eps) * norm_w
 //   post: streams'[n] = post[n] mlp + sum_m comb[m][n] streams[m]
 //
-// Kernels: mhc_dot_kernel<N> computes the W dot products of fn with the raw
-// streams as a small SGEMM over token tiles and K slices (fn is read once per
-// 64-token tile); mhc_finish_kernel (one CTA per token) adds the slices in
-// order, scales by the RMS factor (r * (fn . x) = fn . (r x)), forms the
-// coefficients with one warp, mixes the streams into shared memory and
-// normalises; mhc_post_kernel updates the streams element-wise (one thread per
-// (token, 4 elements) writes all N streams, so it may run in place).  fp32
-// throughout; expf / sqrtf are CUDA's.
+// Kernels: the sum of squares and the W dot products of fn with the raw
+// streams per K slice (mhc_dot_vec_kernel, a CTA per token and slice, below 32
+// tokens; mhc_dot_kernel, a small SGEMM over 64-token tiles that reads fn once
+// per tile, above); mhc_coef_kernel (a warp per token) adds the slices,
+// scales by the RMS factor (r * (fn . x) = fn . (r x)) and forms pre, post
+// and comb; mhc_mix_kernel (a CTA per token) mixes the streams into shared
+// memory and normalises; mhc_post_kernel updates the streams element-wise
+// (one thread per (token, 4 elements) writes all N streams, so it may run in
+// place).  fp32 throughout; expf / sqrtf are CUDA's.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -33,162 +34,242 @@ namespace {
 constexpr int kMhcMaxW = 24;          // (2 + N) N for N <= 4
 constexpr int kMhcThreads = 256;
 
-// Dot products as a small SGEMM: a CTA takes a tile of 64 tokens x all W
-// outputs over one K slice, staging 64 x 32 stream values and W x 32 fn values
-// per step in shared memory; 128 threads, each 4 tokens x (W / 8) outputs.
-constexpr int kDotM = 64, kDotK = 32, kDotThreads = 128;
+// Dot products as a small SGEMM: a CTA takes a tile of 128 tokens x all W
+// outputs over one K slice; per 32-element step it stages 128 x 32 stream
+// values and W x 32 fn values in shared memory (the next step's global loads
+// are issued before the current step's arithmetic), and each of its 128
+// threads accumulates 8 tokens x W/8 outputs.  The sum of squares comes from
+// the staging loads (each thread's 8 rows), reduced over the 8 threads that
+// share a row.
+constexpr int kDotM = 128, kDotK = 32, kDotThreads = 128;
 
 template <int N>
 __global__ void __launch_bounds__(kDotThreads) mhc_dot_kernel(const float* __restrict__ streams,
                                                              const float* __restrict__ fn, int n, int HN, int klen,
                                                              float* __restrict__ partial) {
-    constexpr int W = (2 + N) * N, WT = (W + 7) / 8;  // outputs per thread
+    constexpr int W = (2 + N) * N, WT = (W + 7) / 8, FR = 8 * WT;  // FR fn rows staged (zero past W)
     __shared__ __align__(16) float xs[kDotK][kDotM + 4];
-    __shared__ __align__(16) float fs[kDotK][8 * WT + 1];
-    const int tid = threadIdx.x, tm = tid & 15, tn = tid >> 4;  // 16 x 8 threads
+    __shared__ __align__(16) float fs[kDotK][FR + 1];
+    const int tid = threadIdx.x, tm = tid & 15, tn = tid >> 4;
     const int t0 = blockIdx.y * kDotM, slice = blockIdx.x;
     const int kb = slice * klen, ke = min(HN, kb + klen);
-    float acc[4][WT];
+    const int srow = tid >> 3, c4 = (tid & 7) * 4;  // staging: rows srow + 16 q, columns c4..c4+3
+    float acc[8][WT], sq[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i) {
+        sq[i] = 0.f;
 #pragma unroll
         for (int j = 0; j < WT; ++j) acc[i][j] = 0.f;
-    for (int k0 = kb; k0 < ke; k0 += kDotK) {
-        // stage: 64 tokens x 32 k (512 float4, 4 per thread), W x 32 fn
-        for (int i = tid; i < kDotM * kDotK / 4; i += kDotThreads) {
-            const int r = i >> 3, c4 = (i & 7) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (t0 + r < n && k0 + c4 < ke) v = *reinterpret_cast<const float4*>(streams + (size_t)(t0 + r) * HN + k0 + c4);
-            xs[c4][r] = v.x;
-            xs[c4 + 1][r] = v.y;
-            xs[c4 + 2][r] = v.z;
-            xs[c4 + 3][r] = v.w;
+    }
+    float4 xr[8], fr[2];
+    auto load = [&](int k0) {
+        const bool kin = k0 + c4 < ke;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int r = srow + 16 * q;
+            xr[q] = (kin && t0 + r < n) ? *reinterpret_cast<const float4*>(streams + (size_t)(t0 + r) * HN + k0 + c4)
+                                        : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        for (int i = tid; i < 8 * WT * kDotK / 4; i += kDotThreads) {
-            const int r = i >> 3, c4 = (i & 7) * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (r < W && k0 + c4 < ke) v = __ldg(reinterpret_cast<const float4*>(fn + (size_t)r * HN + k0 + c4));
-            fs[c4][r] = v.x;
-            fs[c4 + 1][r] = v.y;
-            fs[c4 + 2][r] = v.z;
-            fs[c4 + 3][r] = v.w;
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int row = srow + 16 * q;
+            fr[q] = (kin && row < W) ? __ldg(reinterpret_cast<const float4*>(fn + (size_t)row * HN + k0 + c4))
+                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    if (kb < ke) load(kb);
+    for (int k0 = kb; k0 < ke; k0 += kDotK) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int r = srow + 16 * q;
+            xs[c4][r] = xr[q].x;
+            xs[c4 + 1][r] = xr[q].y;
+            xs[c4 + 2][r] = xr[q].z;
+            xs[c4 + 3][r] = xr[q].w;
+            sq[q] += xr[q].x * xr[q].x + xr[q].y * xr[q].y + xr[q].z * xr[q].z + xr[q].w * xr[q].w;
+        }
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+            const int row = srow + 16 * q;
+            if (row < FR) {
+                fs[c4][row] = fr[q].x;
+                fs[c4 + 1][row] = fr[q].y;
+                fs[c4 + 2][row] = fr[q].z;
+                fs[c4 + 3][row] = fr[q].w;
+            }
         }
         __syncthreads();
-#pragma unroll 8
+        if (k0 + kDotK < ke) load(k0 + kDotK);
+#pragma unroll 4
         for (int k = 0; k < kDotK; ++k) {
-            const float4 xv = *reinterpret_cast<const float4*>(&xs[k][4 * tm]);
-            const float xa[4] = {xv.x, xv.y, xv.z, xv.w};
+            const float4 xa = *reinterpret_cast<const float4*>(&xs[k][8 * tm]);
+            const float4 xb = *reinterpret_cast<const float4*>(&xs[k][8 * tm + 4]);
+            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
             for (int j = 0; j < WT; ++j) {
                 const float f = fs[k][tn * WT + j];
 #pragma unroll
-                for (int i = 0; i < 4; ++i) acc[i][j] += xa[i] * f;
+                for (int i = 0; i < 8; ++i) acc[i][j] += xv[i] * f;
             }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int t = t0 + 4 * tm + i;
+    for (int q = 0; q < 8; ++q) {  // the 8 threads of a staging row are 8 consecutive lanes
+#pragma unroll
+        for (int o = 4; o; o >>= 1) sq[q] += __shfl_xor_sync(0xffffffffu, sq[q], o);
+        const int t = t0 + srow + 16 * q;
+        if ((tid & 7) == 0 && t < n) partial[((size_t)t * gridDim.x + slice) * (W + 1)] = sq[q];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int t = t0 + 8 * tm + i;
         if (t >= n) continue;
+        float* pp = partial + ((size_t)t * gridDim.x + slice) * (W + 1);
 #pragma unroll
         for (int j = 0; j < WT; ++j) {
             const int o = tn * WT + j;
-            if (o < W) partial[((size_t)t * gridDim.x + slice) * W + o] = acc[i][j];
+            if (o < W) pp[1 + o] = acc[i][j];
         }
     }
 }
 
-// One CTA per token: sum of squares of the streams, coefficients (one warp,
-// N*N lanes for the Sinkhorn steps), mixed streams kept in shared memory, then
-// the weighted RMSNorm.
-__global__ void __launch_bounds__(kMhcThreads) mhc_finish_kernel(const float* __restrict__ streams,
-                                                               const float* __restrict__ partial, int S,
-                                                               MhcArgs a) {
-    extern __shared__ __align__(16) float mixed[];  // [H]
-    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int N = a.N, H = a.H, HN = N * H, W = (2 + N) * N;
-    __shared__ float wv[kMhcMaxW];
-    __shared__ float coef[4];  // pre[N]
-    __shared__ float red[kMhcThreads / 32];
-    const float4* S4 = reinterpret_cast<const float4*>(streams + (size_t)t * HN);
-    float ss = 0.f;
-    for (int i = tid; i < HN / 4; i += kMhcThreads) {
-        const float4 v = S4[i];
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+// Small batches: a CTA per (token, slice of 1024 elements), a float4 per
+// thread, the W + 1 sums reduced across the CTA; all fn loads of a thread are
+// independent, so a slice costs about one memory latency.
+template <int N>
+__global__ void __launch_bounds__(kMhcThreads) mhc_dot_vec_kernel(const float* __restrict__ streams,
+                                                                 const float* __restrict__ fn, int HN,
+                                                                 float* __restrict__ partial) {
+    constexpr int W = (2 + N) * N;
+    const int slice = blockIdx.x, t = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int k = slice * 4 * kMhcThreads + 4 * tid;
+    float v[W + 1];
+#pragma unroll
+    for (int j = 0; j <= W; ++j) v[j] = 0.f;
+    if (k < HN) {
+        const float4 x = *reinterpret_cast<const float4*>(streams + (size_t)t * HN + k);
+        float4 f[W];
+#pragma unroll
+        for (int j = 0; j < W; ++j) f[j] = __ldg(reinterpret_cast<const float4*>(fn + (size_t)j * HN + k));
+        v[0] = x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
+#pragma unroll
+        for (int j = 0; j < W; ++j) v[1 + j] = f[j].x * x.x + f[j].y * x.y + f[j].z * x.z + f[j].w * x.w;
     }
-    for (int j = warp; j < W; j += kMhcThreads / 32) {  // slice partials: lanes stride, then a fixed tree
-        float s = 0.f;
-        for (int i = lane; i < S; i += 32) s += partial[((size_t)t * S + i) * W + j];
+    __shared__ float red[kMhcThreads / 32][W + 1];
+#pragma unroll
+    for (int j = 0; j <= W; ++j) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v[j] += __shfl_xor_sync(0xffffffffu, v[j], o);
+        if (lane == 0) red[warp][j] = v[j];
+    }
+    __syncthreads();
+    if (tid <= W) {
+        float s2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMhcThreads / 32; ++w) s2 += red[w][tid];
+        partial[((size_t)t * gridDim.x + slice) * (W + 1) + tid] = s2;
+    }
+}
+
+// Coefficients, one warp per token: the slice partials (lanes stride, then a
+// fixed tree), the RMS factor of the streams, pre / post, the row softmax and
+// the Sinkhorn steps on N*N lanes (comb[i][j] on lane i*N + j).
+__global__ void __launch_bounds__(kMhcThreads) mhc_coef_kernel(const float* __restrict__ partial, int S, int n,
+                                                             float* __restrict__ pre_out, MhcArgs a) {
+    const int lane = threadIdx.x & 31, t = blockIdx.x * (kMhcThreads / 32) + (threadIdx.x >> 5);
+    if (t >= n) return;
+    const int N = a.N, HN = N * a.H, W = (2 + N) * N;
+    // lane i loads slice i's W + 1 sums (all loads issued together), then a fixed
+    // shuffle tree per sum; lane j keeps sum j (W + 1 <= 32)
+    float part[kMhcMaxW + 1];
+#pragma unroll
+    for (int j = 0; j <= kMhcMaxW; ++j) part[j] = 0.f;
+    for (int i0 = 0; i0 < S; i0 += 32) {
+        const float* pp = partial + ((size_t)t * S + i0 + lane) * (W + 1);
+        const bool have = i0 + lane < S;
+#pragma unroll
+        for (int j = 0; j <= kMhcMaxW; ++j)
+            if (j <= W && have) part[j] += pp[j];
+    }
+    float wv = 0.f;
+#pragma unroll
+    for (int j = 0; j <= kMhcMaxW; ++j) {
+        float s = part[j];
 #pragma unroll
         for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) wv[j] = s;
+        if (lane == j) wv = s;
     }
+    const float r = 1.0f / sqrtf(__shfl_sync(0xffffffffu, wv, 0) / (float)HN + a.rms_eps);
+    const float w_pre = __shfl_sync(0xffffffffu, wv, (1 + lane) & 31);
+    const float w_post = __shfl_sync(0xffffffffu, wv, (1 + N + lane) & 31);
+    const float w_comb = __shfl_sync(0xffffffffu, wv, (1 + 2 * N + lane) & 31);
+    if (lane < N) {
+        pre_out[(size_t)t * N + lane] = 1.0f / (1.0f + expf(-(w_pre * r * a.scale[0] + a.base[lane]))) + a.hc_eps;
+        a.post_out[(size_t)t * N + lane] = 2.0f / (1.0f + expf(-(w_post * r * a.scale[1] + a.base[N + lane])));
+    }
+    const int i = lane / N, j = lane % N;
+    const bool on = lane < N * N;
+    float c = 0.f;
+    {
+        const float z = on ? w_comb * r * a.scale[2] + a.base[2 * N + lane] : 0.f;
+        float mx = z;
+        for (int q = 0; q < N; ++q) mx = fmaxf(mx, __shfl_sync(0xffffffffu, z, (i * N + q) & 31));
+        const float e = on ? expf(z - mx) : 0.f;
+        float sum = 0.f;
+        for (int q = 0; q < N; ++q) sum += __shfl_sync(0xffffffffu, e, (i * N + q) & 31);
+        if (on) c = e * (1.0f / sum) + a.hc_eps;
+    }
+    // Sinkhorn: columns, then (iters - 1) x (rows, columns); sums in index order + eps
+    for (int it = 0; it < a.iters; ++it) {
+        if (it > 0) {
+            float rs = 0.f;
+            for (int q = 0; q < N; ++q) rs += __shfl_sync(0xffffffffu, c, (i * N + q) & 31);
+            if (on) c = c / (rs + a.hc_eps);
+        }
+        float cs = 0.f;
+        for (int q = 0; q < N; ++q) cs += __shfl_sync(0xffffffffu, c, (q * N + j) & 31);
+        if (on) c = c / (cs + a.hc_eps);
+    }
+    if (on) a.comb_out[(size_t)t * N * N + lane] = c;
+}
+
+// One CTA per token: mixed = sum_n pre[n] streams[n] (kept in shared memory),
+// then the weighted RMSNorm.
+__global__ void __launch_bounds__(kMhcThreads) mhc_mix_kernel(const float* __restrict__ streams,
+                                                            const float* __restrict__ pre, MhcArgs a) {
+    extern __shared__ __align__(16) float mixed[];  // [H]
+    const int t = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int N = a.N, H = a.H;
+    __shared__ float red[kMhcThreads / 32];
+    const float4* S4 = reinterpret_cast<const float4*>(streams + (size_t)t * N * H);
+    float p[4];
 #pragma unroll
-    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[warp] = ss;
-    __syncthreads();
-    if (warp == 0) {
-        float tot = 0.f;
-        for (int w = 0; w < kMhcThreads / 32; ++w) tot += red[w];
-        const float r = 1.0f / sqrtf(tot / (float)HN + a.rms_eps);
-        if (lane < N) {
-            coef[lane] = 1.0f / (1.0f + expf(-(wv[lane] * r * a.scale[0] + a.base[lane]))) + a.hc_eps;
-            a.post_out[(size_t)t * N + lane] = 2.0f / (1.0f + expf(-(wv[N + lane] * r * a.scale[1] + a.base[N + lane])));
-        }
-        // comb[i][j] on lane i * N + j; row groups of N lanes
-        const int i = lane / N, j = lane % N;
-        const bool on = lane < N * N;
-        const unsigned grp = on ? (((1u << N) - 1u) << (i * N)) : 0u;
-        float c = 0.f;
-        if (on) {
-            const float z = wv[2 * N + lane] * r * a.scale[2] + a.base[2 * N + lane];
-            float mx = z;
-            for (int q = 0; q < N; ++q) mx = fmaxf(mx, __shfl_sync(grp, z, i * N + q));
-            const float e = expf(z - mx);
-            float sum = 0.f;
-            for (int q = 0; q < N; ++q) sum += __shfl_sync(grp, e, i * N + q);
-            c = e * (1.0f / sum) + a.hc_eps;
-        }
-        // Sinkhorn: columns, then (iters - 1) x (rows, columns); sums in index order + eps
-        const unsigned all = (N * N == 32) ? 0xffffffffu : ((1u << (N * N)) - 1u);
-        for (int it = 0; it < a.iters; ++it) {
-            if (it > 0) {
-                float rs = 0.f;
-                for (int q = 0; q < N; ++q) rs += __shfl_sync(0xffffffffu, c, (i * N + q) & 31);
-                if (on) c = c / (rs + a.hc_eps);
-            }
-            float cs = 0.f;
-            for (int q = 0; q < N; ++q) cs += __shfl_sync(0xffffffffu, c, (q * N + j) & 31);
-            if (on) c = c / (cs + a.hc_eps);
-        }
-        (void)all;
-        if (on) a.comb_out[(size_t)t * N * N + lane] = c;
-    }
-    __syncthreads();
-    // mixed = sum_n pre[n] streams[n] (kept in shared memory), then the weighted RMSNorm
+    for (int q = 0; q < 4; ++q) p[q] = q < N ? pre[(size_t)t * N + q] : 0.f;
     float ss2 = 0.f;
+#pragma unroll 2
     for (int d4 = tid; d4 < H / 4; d4 += kMhcThreads) {
         float4 m = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int q = 0; q < N; ++q) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            if (q >= N) break;
             const float4 v = S4[q * (H / 4) + d4];
-            const float p = coef[q];
-            m.x += p * v.x;
-            m.y += p * v.y;
-            m.z += p * v.z;
-            m.w += p * v.w;
+            m.x += p[q] * v.x;
+            m.y += p[q] * v.y;
+            m.z += p[q] * v.z;
+            m.w += p[q] * v.w;
         }
         reinterpret_cast<float4*>(mixed)[d4] = m;
         ss2 += m.x * m.x + m.y * m.y + m.z * m.z + m.w * m.w;
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) ss2 += __shfl_xor_sync(0xffffffffu, ss2, o);
-    __syncthreads();  // red reuse
     if (lane == 0) red[warp] = ss2;
     __syncthreads();
     float tot = 0.f;
     for (int w = 0; w < kMhcThreads / 32; ++w) tot += red[w];
     const float r2 = 1.0f / sqrtf(tot / (float)H + a.rms_eps);
+#pragma unroll 4
     for (int d = tid; d < H; d += kMhcThreads) {
         const float v = mixed[d] * r2 * a.norm_w[d];
         if (a.x_bf16)
@@ -233,18 +314,36 @@ __global__ void mhc_post_kernel(const float* in, const float* __restrict__ mlp, 
 int mhc_slices(int n, int HN) {
     const int tiles = (n + kDotM - 1) / kDotM, steps = (HN + kDotK - 1) / kDotK;
     int S = (8 * 148 + tiles - 1) / tiles;
+    if (S > 64) S = 64;  // the coefficient kernel reads a token's slices in two rounds of 32 lanes at most
     if (S > steps) S = steps;
     if (S < 1) S = 1;
     return S;
 }
 
-int mhc_partial_floats(int n, int N, int H) { return n * mhc_slices(n, N * H) * (2 + N) * N; }
+constexpr int kVecMaxTokens = 32;  // below this the vector kernel (one token per CTA) is used
+
+int mhc_slices_for(int n, int HN) {
+    return n < kVecMaxTokens ? (HN + 4 * kMhcThreads - 1) / (4 * kMhcThreads) : mhc_slices(n, HN);
+}
+
+// slice partials, then pre[n][N]
+int mhc_partial_floats(int n, int N, int H) { return n * mhc_slices_for(n, N * H) * ((2 + N) * N + 1) + n * N; }
 
 cudaError_t launch_mhc_pre(const float* streams, int n, const MhcArgs& a, float* partial, cudaStream_t st) {
     if (n <= 0) return cudaSuccess;
     const int HN = a.N * a.H;
     if (a.H % 4) return cudaErrorInvalidValue;
-    const int S = mhc_slices(n, HN);
+    const int S = mhc_slices_for(n, HN);
+    if (n < kVecMaxTokens) {
+        const dim3 grid(S, n);
+        switch (a.N) {
+            case 1: mhc_dot_vec_kernel<1><<<grid, kMhcThreads, 0, st>>>(streams, a.fn, HN, partial); break;
+            case 2: mhc_dot_vec_kernel<2><<<grid, kMhcThreads, 0, st>>>(streams, a.fn, HN, partial); break;
+            case 3: mhc_dot_vec_kernel<3><<<grid, kMhcThreads, 0, st>>>(streams, a.fn, HN, partial); break;
+            case 4: mhc_dot_vec_kernel<4><<<grid, kMhcThreads, 0, st>>>(streams, a.fn, HN, partial); break;
+            default: return cudaErrorInvalidValue;
+        }
+    } else {
     const int steps = (HN + kDotK - 1) / kDotK, klen = (steps + S - 1) / S * kDotK;
     const dim3 grid(S, (n + kDotM - 1) / kDotM);
     switch (a.N) {
@@ -254,14 +353,19 @@ cudaError_t launch_mhc_pre(const float* streams, int n, const MhcArgs& a, float*
         case 4: mhc_dot_kernel<4><<<grid, kDotThreads, 0, st>>>(streams, a.fn, n, HN, klen, partial); break;
         default: return cudaErrorInvalidValue;
     }
+    }
     cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    float* pre = partial + (size_t)n * S * ((2 + a.N) * a.N + 1);
+    mhc_coef_kernel<<<(n + kMhcThreads / 32 - 1) / (kMhcThreads / 32), kMhcThreads, 0, st>>>(partial, S, n, pre, a);
+    e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const size_t smem = sizeof(float) * (size_t)a.H;
     if (smem > 48 * 1024) {
-        e = cudaFuncSetAttribute(mhc_finish_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        e = cudaFuncSetAttribute(mhc_mix_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
-    mhc_finish_kernel<<<n, kMhcThreads, smem, st>>>(streams, partial, S, a);
+    mhc_mix_kernel<<<n, kMhcThreads, smem, st>>>(streams, pre, a);
     return cudaGetLastError();
 }
 
