@@ -34,96 +34,93 @@ namespace {
 constexpr int kMhcMaxW = 24;          // (2 + N) N for N <= 4
 constexpr int kMhcThreads = 256;
 
-// Dot products as a small SGEMM: a CTA takes a tile of 128 tokens x all W
-// outputs over one K slice; per 32-element step it stages 128 x 32 stream
-// values and W x 32 fn values in shared memory (the next step's global loads
-// are issued before the current step's arithmetic), and each of its 128
-// threads accumulates 8 tokens x W/8 outputs.  The sum of squares comes from
-// the staging loads (each thread's 8 rows), reduced over the 8 threads that
-// share a row.
-constexpr int kDotM = 128, kDotK = 32, kDotThreads = 128;
+// Dot products as a small SGEMM: a CTA takes a tile of 64 tokens x all W
+// outputs over one K slice.  Per 128-element step it stages the tile's 64 row
+// pieces of 512 contiguous bytes each (a warp reads one piece per load, so
+// HBM sees half-kilobyte runs of each token's rows) and the W fn pieces in
+// shared memory, natural layout; the next step's global loads are issued
+// before the current step's arithmetic.  Each of the 128 threads accumulates
+// 4 tokens (tm + 16 i) x W/8 outputs, reading 4 elements along K at a time.
+// The sum of squares comes from the staging loads, reduced over the warp that
+// staged a row.
+constexpr int kDotM = 64, kDotK = 128, kDotThreads = 128;
 
 template <int N>
 __global__ void __launch_bounds__(kDotThreads) mhc_dot_kernel(const float* __restrict__ streams,
                                                              const float* __restrict__ fn, int n, int HN, int klen,
                                                              float* __restrict__ partial) {
     constexpr int W = (2 + N) * N, WT = (W + 7) / 8, FR = 8 * WT;  // FR fn rows staged (zero past W)
-    __shared__ __align__(16) float xs[kDotK][kDotM + 4];
-    __shared__ __align__(16) float fs[kDotK][FR + 1];
-    const int tid = threadIdx.x, tm = tid & 15, tn = tid >> 4;
+    constexpr int XQ = kDotM * kDotK / 4 / kDotThreads;             // staged x float4 per thread (16)
+    constexpr int FQ = (FR * kDotK / 4 + kDotThreads - 1) / kDotThreads;
+    __shared__ __align__(16) float xs[kDotM][kDotK + 4];
+    __shared__ __align__(16) float fs[FR][kDotK + 4];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, tm = tid & 15, tn = tid >> 4;
     const int t0 = blockIdx.y * kDotM, slice = blockIdx.x;
     const int kb = slice * klen, ke = min(HN, kb + klen);
-    const int srow = tid >> 3, c4 = (tid & 7) * 4;  // staging: rows srow + 16 q, columns c4..c4+3
-    float acc[8][WT], sq[8];
+    float acc[4][WT], sq[XQ];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        sq[i] = 0.f;
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < WT; ++j) acc[i][j] = 0.f;
-    }
-    float4 xr[8], fr[2];
-    auto load = [&](int k0) {
-        const bool kin = k0 + c4 < ke;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int r = srow + 16 * q;
-            xr[q] = (kin && t0 + r < n) ? *reinterpret_cast<const float4*>(streams + (size_t)(t0 + r) * HN + k0 + c4)
+    for (int q = 0; q < XQ; ++q) sq[q] = 0.f;
+    float4 xr[XQ], fr[FQ];
+    auto load = [&](int k0) {
+        const int col = k0 + 4 * lane;
+        const bool kin = col < ke;
+#pragma unroll
+        for (int q = 0; q < XQ; ++q) {  // row warp + 4 q
+            const int r = warp + 4 * q;
+            xr[q] = (kin && t0 + r < n) ? *reinterpret_cast<const float4*>(streams + (size_t)(t0 + r) * HN + col)
                                         : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int row = srow + 16 * q;
-            fr[q] = (kin && row < W) ? __ldg(reinterpret_cast<const float4*>(fn + (size_t)row * HN + k0 + c4))
+        for (int q = 0; q < FQ; ++q) {
+            const int row = (tid + kDotThreads * q) >> 5;
+            fr[q] = (kin && row < W) ? __ldg(reinterpret_cast<const float4*>(fn + (size_t)row * HN + col))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
         }
     };
     if (kb < ke) load(kb);
     for (int k0 = kb; k0 < ke; k0 += kDotK) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int r = srow + 16 * q;
-            xs[c4][r] = xr[q].x;
-            xs[c4 + 1][r] = xr[q].y;
-            xs[c4 + 2][r] = xr[q].z;
-            xs[c4 + 3][r] = xr[q].w;
+        for (int q = 0; q < XQ; ++q) {
+            *reinterpret_cast<float4*>(&xs[warp + 4 * q][4 * lane]) = xr[q];
             sq[q] += xr[q].x * xr[q].x + xr[q].y * xr[q].y + xr[q].z * xr[q].z + xr[q].w * xr[q].w;
         }
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-            const int row = srow + 16 * q;
-            if (row < FR) {
-                fs[c4][row] = fr[q].x;
-                fs[c4 + 1][row] = fr[q].y;
-                fs[c4 + 2][row] = fr[q].z;
-                fs[c4 + 3][row] = fr[q].w;
-            }
+        for (int q = 0; q < FQ; ++q) {
+            const int row = (tid + kDotThreads * q) >> 5;
+            if (row < FR) *reinterpret_cast<float4*>(&fs[row][4 * lane]) = fr[q];
         }
         __syncthreads();
         if (k0 + kDotK < ke) load(k0 + kDotK);
-#pragma unroll 4
-        for (int k = 0; k < kDotK; ++k) {
-            const float4 xa = *reinterpret_cast<const float4*>(&xs[k][8 * tm]);
-            const float4 xb = *reinterpret_cast<const float4*>(&xs[k][8 * tm + 4]);
-            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll 2
+        for (int k = 0; k < kDotK; k += 4) {
+            float4 xv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tm + 16 * i][k]);
 #pragma unroll
             for (int j = 0; j < WT; ++j) {
-                const float f = fs[k][tn * WT + j];
+                const float4 f = *reinterpret_cast<const float4*>(&fs[tn * WT + j][k]);
 #pragma unroll
-                for (int i = 0; i < 8; ++i) acc[i][j] += xv[i] * f;
+                for (int i = 0; i < 4; ++i)
+                    acc[i][j] += xv[i].x * f.x + xv[i].y * f.y + xv[i].z * f.z + xv[i].w * f.w;
             }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {  // the 8 threads of a staging row are 8 consecutive lanes
+    for (int q = 0; q < XQ; ++q) {  // a staged row's 32 pieces are the 32 lanes of one warp
+        float v = sq[q];
 #pragma unroll
-        for (int o = 4; o; o >>= 1) sq[q] += __shfl_xor_sync(0xffffffffu, sq[q], o);
-        const int t = t0 + srow + 16 * q;
-        if ((tid & 7) == 0 && t < n) partial[((size_t)t * gridDim.x + slice) * (W + 1)] = sq[q];
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const int t = t0 + warp + 4 * q;
+        if (lane == 0 && t < n) partial[((size_t)t * gridDim.x + slice) * (W + 1)] = v;
     }
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const int t = t0 + 8 * tm + i;
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + tm + 16 * i;
         if (t >= n) continue;
         float* pp = partial + ((size_t)t * gridDim.x + slice) * (W + 1);
 #pragma unroll
