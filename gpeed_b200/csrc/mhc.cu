@@ -34,92 +34,83 @@ namespace {
 constexpr int kMhcMaxW = 24;          // (2 + N) N for N <= 4
 constexpr int kMhcThreads = 256;
 
-// Dot products as a small SGEMM: a CTA takes a tile of 64 tokens x all W
-// outputs over one K slice.  Per 128-element step it stages the tile's 64 row
-// pieces of 512 contiguous bytes each (a warp reads one piece per load, so
-// HBM sees half-kilobyte runs of each token's rows) and the W fn pieces in
-// shared memory, natural layout; the next step's global loads are issued
-// before the current step's arithmetic.  Each of the 128 threads accumulates
-// 4 tokens (tm + 16 i) x W/8 outputs, reading 4 elements along K at a time.
-// The sum of squares comes from the staging loads, reduced over the warp that
-// staged a row.
-constexpr int kDotM = 64, kDotK = 128, kDotThreads = 128;
+// Dot products as a small SGEMM: a CTA of 64 threads takes a tile of 128
+// tokens x all W outputs over one K slice.  Per 64-element step it copies the
+// tile's 128 row pieces (256 contiguous bytes each; a warp copies one piece
+// per two loads) and the W fn pieces to shared memory, natural layout.  Each
+// thread accumulates 8 tokens (tm + 16 i) x W/4 outputs, reading 4 elements
+// along K at a time, so a shared-memory read feeds 8 (x) or 12 (fn)
+// multiply-adds per element.  The sum of squares comes from the copies,
+// reduced over the 16 lanes that copied a row.
+constexpr int kDotM = 128, kDotK = 64, kDotThreads = 64;
 
 template <int N>
 __global__ void __launch_bounds__(kDotThreads) mhc_dot_kernel(const float* __restrict__ streams,
                                                              const float* __restrict__ fn, int n, int HN, int klen,
                                                              float* __restrict__ partial) {
-    constexpr int W = (2 + N) * N, WT = (W + 7) / 8, FR = 8 * WT;  // FR fn rows staged (zero past W)
-    constexpr int XQ = kDotM * kDotK / 4 / kDotThreads;             // staged x float4 per thread (16)
+    constexpr int W = (2 + N) * N, WT = (W + 3) / 4, FR = 4 * WT;  // FR fn rows staged (zero past W)
+    constexpr int XQ = kDotM * kDotK / 4 / kDotThreads;             // x float4 copied per thread (32)
     constexpr int FQ = (FR * kDotK / 4 + kDotThreads - 1) / kDotThreads;
     __shared__ __align__(16) float xs[kDotM][kDotK + 4];
     __shared__ __align__(16) float fs[FR][kDotK + 4];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, tm = tid & 15, tn = tid >> 4;
+    const int tid = threadIdx.x, tm = tid & 15, tn = tid >> 4;
     const int t0 = blockIdx.y * kDotM, slice = blockIdx.x;
     const int kb = slice * klen, ke = min(HN, kb + klen);
-    float acc[4][WT], sq[XQ];
+    // copy mapping: float4 i = tid + 64 q -> row i >> 4, column 4 * (i & 15)
+    const int crow = tid >> 4, ccol = 4 * (tid & 15);
+    float acc[8][WT], sq[XQ];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
         for (int j = 0; j < WT; ++j) acc[i][j] = 0.f;
 #pragma unroll
     for (int q = 0; q < XQ; ++q) sq[q] = 0.f;
-    float4 xr[XQ], fr[FQ];
-    auto load = [&](int k0) {
-        const int col = k0 + 4 * lane;
+    for (int k0 = kb; k0 < ke; k0 += kDotK) {
+        const int col = k0 + ccol;
         const bool kin = col < ke;
 #pragma unroll
-        for (int q = 0; q < XQ; ++q) {  // row warp + 4 q
-            const int r = warp + 4 * q;
-            xr[q] = (kin && t0 + r < n) ? *reinterpret_cast<const float4*>(streams + (size_t)(t0 + r) * HN + col)
-                                        : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < XQ; ++q) {
+            const int r = crow + 4 * q;
+            const float4 v = (kin && t0 + r < n)
+                                 ? *reinterpret_cast<const float4*>(streams + (size_t)(t0 + r) * HN + col)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(&xs[r][ccol]) = v;
+            sq[q] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         }
 #pragma unroll
         for (int q = 0; q < FQ; ++q) {
-            const int row = (tid + kDotThreads * q) >> 5;
-            fr[q] = (kin && row < W) ? __ldg(reinterpret_cast<const float4*>(fn + (size_t)row * HN + col))
+            const int row = crow + 4 * q;
+            if (row < FR)
+                *reinterpret_cast<float4*>(&fs[row][ccol]) =
+                    (kin && row < W) ? __ldg(reinterpret_cast<const float4*>(fn + (size_t)row * HN + col))
                                      : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-    };
-    if (kb < ke) load(kb);
-    for (int k0 = kb; k0 < ke; k0 += kDotK) {
-#pragma unroll
-        for (int q = 0; q < XQ; ++q) {
-            *reinterpret_cast<float4*>(&xs[warp + 4 * q][4 * lane]) = xr[q];
-            sq[q] += xr[q].x * xr[q].x + xr[q].y * xr[q].y + xr[q].z * xr[q].z + xr[q].w * xr[q].w;
-        }
-#pragma unroll
-        for (int q = 0; q < FQ; ++q) {
-            const int row = (tid + kDotThreads * q) >> 5;
-            if (row < FR) *reinterpret_cast<float4*>(&fs[row][4 * lane]) = fr[q];
-        }
         __syncthreads();
-        if (k0 + kDotK < ke) load(k0 + kDotK);
 #pragma unroll 2
         for (int k = 0; k < kDotK; k += 4) {
-            float4 xv[4];
+            float4 f[WT];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = *reinterpret_cast<const float4*>(&xs[tm + 16 * i][k]);
+            for (int j = 0; j < WT; ++j) f[j] = *reinterpret_cast<const float4*>(&fs[tn * WT + j][k]);
 #pragma unroll
-            for (int j = 0; j < WT; ++j) {
-                const float4 f = *reinterpret_cast<const float4*>(&fs[tn * WT + j][k]);
+            for (int i = 0; i < 8; ++i) {
+                const float4 xv = *reinterpret_cast<const float4*>(&xs[tm + 16 * i][k]);
 #pragma unroll
-                for (int i = 0; i < 4; ++i)
-                    acc[i][j] += xv[i].x * f.x + xv[i].y * f.y + xv[i].z * f.z + xv[i].w * f.w;
+                for (int j = 0; j < WT; ++j)
+                    acc[i][j] += xv.x * f[j].x + xv.y * f[j].y + xv.z * f[j].z + xv.w * f[j].w;
             }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int q = 0; q < XQ; ++q) {  // a staged row's 32 pieces are the 32 lanes of one warp
+    for (int q = 0; q < XQ; ++q) {  // a copied row's 16 pieces are 16 consecutive lanes
         float v = sq[q];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        const int t = t0 + warp + 4 * q;
-        if (lane == 0 && t < n) partial[((size_t)t * gridDim.x + slice) * (W + 1)] = v;
+        for (int o = 8; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        const int t = t0 + crow + 4 * q;
+        if ((tid & 15) == 0 && t < n) partial[((size_t)t * gridDim.x + slice) * (W + 1)] = v;
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
+    for (int i = 0; i < 8; ++i) {
         const int t = t0 + tm + 16 * i;
         if (t >= n) continue;
         float* pp = partial + ((size_t)t * gridDim.x + slice) * (W + 1);
