@@ -1111,6 +1111,54 @@ int gpeed_dense_mlp_forward(gpeed_ctx* c, int gate, int up, int down, float swig
     if ((rc = set_device(c))) return rc;
     if ((rc = ensure_scratch(c, n, 1, 1, H, (int)I))) return rc;
     cudaStream_t st = (cudaStream_t)stream;
+    if (n < c->tc_min_tokens || !gp::tc_moe_supported(H, (int)I)) {
+        // GEMV path with nothing to route: slots over the tokens in order, gate/up + SwiGLU reading x
+        // rows directly, down writing Y rows directly (no permutation, no weighted combine)
+        const int nt = nt_for(n);
+        Geo ggu, gd;
+        if ((rc = pick_geo(H, 2, nt, (int)I, &ggu))) return rc;
+        if ((rc = pick_geo((int)I, 1, nt, H, &gd))) return rc;
+        if (I % ggu.tile_rows || H % gd.tile_rows) return fail(GPEED_ERR_UNSUPPORTED, "row tiling of the dense MLP");
+        make_slots_kernel<<<1, 256, 0, st>>>(c->slots.p, c->nslots.p, n, nt);
+        GP_CUDA(cudaGetLastError());
+        gp::GemvArgs g{};
+        g.w0 = G.packed;
+        g.w1 = U.packed;
+        g.expert_stride = L.gu_stride;
+        g.in_dim = H;
+        g.rows = (int)I;
+        g.tile_rows = ggu.tile_rows;
+        g.nwarps = ggu.nwarps;
+        g.stages = ggu.stages;
+        g.slots = c->slots.p;
+        g.nslots = c->nslots.p;
+        g.perm_tok = nullptr;
+        g.x = X;
+        g.x_bf16 = x_dtype == GPEED_DTYPE_BF16;
+        g.out = c->h.p;
+        g.limit = swiglu_limit;
+        g.tables = c->tables;
+        g.status = c->status;
+        GP_CUDA(gp::launch_gemv(g, nt, true, ggu.passes, ggu.rpw, c->num_sms, st, true));
+        gp::GemvArgs d{};
+        d.w0 = D.packed;
+        d.expert_stride = L.d_stride;
+        d.in_dim = (int)I;
+        d.rows = H;
+        d.tile_rows = gd.tile_rows;
+        d.nwarps = gd.nwarps;
+        d.stages = gd.stages;
+        d.slots = c->slots.p;
+        d.nslots = c->nslots.p;
+        d.perm_tok = nullptr;
+        d.x = c->h.p;
+        d.x_bf16 = 0;
+        d.out = Y;
+        d.tables = c->tables;
+        d.status = c->status;
+        GP_CUDA(gp::launch_gemv(d, nt, false, gd.passes, gd.rpw, c->num_sms, st, true));
+        return GPEED_OK;
+    }
     fill_unit_kernel<<<std::min((n + 255) / 256, 148), 256, 0, st>>>(c->topk_ids.p, c->topk_w.p, n);
     GP_CUDA(cudaGetLastError());
     gp::RouteArgs ro{};
