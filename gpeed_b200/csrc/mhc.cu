@@ -257,6 +257,24 @@ __global__ void __launch_bounds__(kMhcThreads) mhc_mix_kernel(const float* __res
     float tot = 0.f;
     for (int w = 0; w < kMhcThreads / 32; ++w) tot += red[w];
     const float r2 = 1.0f / sqrtf(tot / (float)H + a.rms_eps);
+    const bool vec = ((reinterpret_cast<uintptr_t>(a.norm_w) | reinterpret_cast<uintptr_t>(a.x_out)) & 15) == 0;
+    if (vec) {  // 4 elements per thread per step: 16-byte loads, 8-byte (bf16) or 16-byte (fp32) stores
+        for (int d4 = tid; d4 < H / 4; d4 += kMhcThreads) {
+            const float4 m = reinterpret_cast<const float4*>(mixed)[d4];
+            const float4 w = reinterpret_cast<const float4*>(a.norm_w)[d4];
+            const float4 v = make_float4(m.x * r2 * w.x, m.y * r2 * w.y, m.z * r2 * w.z, m.w * r2 * w.w);
+            if (a.x_bf16) {
+                __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y), hi = __floats2bfloat162_rn(v.z, v.w);
+                uint2 u;
+                u.x = *reinterpret_cast<uint32_t*>(&lo);
+                u.y = *reinterpret_cast<uint32_t*>(&hi);
+                reinterpret_cast<uint2*>(a.x_out)[(size_t)t * (H / 4) + d4] = u;
+            } else {
+                reinterpret_cast<float4*>(a.x_out)[(size_t)t * (H / 4) + d4] = v;
+            }
+        }
+        return;
+    }
 #pragma unroll 4
     for (int d = tid; d < H; d += kMhcThreads) {
         const float v = mixed[d] * r2 * a.norm_w[d];
