@@ -19,6 +19,10 @@ OPT_TC_MIN_TOKENS = 3
 TC_MIN_TOKENS_DEFAULT = 8  # the library's default for OPT_TC_MIN_TOKENS
 OPT_FUSED_MAX_TOKENS = 4
 FUSED_MAX_TOKENS_DEFAULT = 12
+OPT_SPIN_LIMIT = 5
+SPIN_LIMIT_DEFAULT = 1 << 22
+OPT_TEST_WITHHOLD_LOGIT = 6
+TC_SLOT_TOKENS = 224  # rows per expert slot of the tensor-core path (tc_moe.cu, the MMA's N)
 
 
 class GpeedError(RuntimeError):

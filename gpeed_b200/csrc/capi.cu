@@ -102,6 +102,8 @@ struct gpeed_ctx {
     bool fused_decode = true;
     int fused_max_tokens = 12;         // batches up to this size: the fused kernel once per token
     bool fused_cooperative = false;
+    uint32_t spin_limit = GPEED_SPIN_LIMIT_DEFAULT;  // polls before a wait of the fused kernel gives up
+    int withhold_logit = -1;           // test hook (GPEED_OPT_TEST_WITHHOLD_LOGIT)
     int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
@@ -372,7 +374,7 @@ int expert_pass(gpeed_ctx* c, const Layer& L, const void* x, int x_bf16, gp::Rou
         ro.nt = gp::tc_moe_slot_tokens();
         GP_CUDA(gp::launch_route(ro, st, false));
         if ((rc = c->xp.ensure((size_t)npos * H))) return rc;
-        GP_CUDA(gp::launch_gather_cast(x, x_bf16, c->perm.p, npos, H, c->xp.p, st));
+        GP_CUDA(gp::launch_gather_cast(x, x_bf16, c->perm.p, npos, H, c->xp.p, c->status, st));
         mark(2);
         const int El = L.e_cnt + s.n_shared;
         uint16_t* h16 = reinterpret_cast<uint16_t*>(c->h.p);  // npos x I fp16 fits the fp32 h scratch
@@ -440,6 +442,86 @@ int expert_pass(gpeed_ctx* c, const Layer& L, const void* x, int x_bf16, gp::Rou
 
     gp::CombineArgs cb{c->D.p, c->inv_pos.p, ro.topk_w, n, K, H, combine_shared, y, d_shared};
     GP_CUDA(gp::launch_combine(cb, st, !c->prof));
+    return GPEED_OK;
+}
+
+// One gpeed_matmul_quant call (WeightStore::matmul_quant, weights.cpp:86-165):
+// the validated arguments and the GEMV geometry.  Both the allocating entry
+// point and gpeed_matmul_quant_noalloc run exactly this plan; they differ only
+// in where the work list and the staged output live (MatmulScratch).
+struct MatmulPlan {
+    bool empty = false;         // n_tok or out_dim <= 0: nothing to do (weights.cpp:88)
+    const Tensor* t = nullptr;
+    Geo g{};
+    int nt = 1, ns = 0, n_tok = 0, in_dim = 0, out_dim = 0;
+    int64_t g0 = 0, skip = 0, ntile = 0, rows_eff = 0;
+    bool direct = true;         // output rows land in Y as they are (no staging)
+    size_t staged_floats() const { return direct ? 0 : (size_t)n_tok * rows_eff; }
+};
+
+struct MatmulScratch {
+    gp::SlotDesc* slots;        // >= plan.ns descriptors
+    int* nslots;
+    float* staged;              // >= plan.staged_floats(), or nullptr when direct
+};
+
+int plan_matmul(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* X, int n_tok,
+                const float* Y, MatmulPlan* p) {
+    if (!c || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
+    if (n_tok <= 0 || out_dim <= 0) {
+        p->empty = true;
+        return GPEED_OK;
+    }
+    const Tensor& t = c->tensors[handle];
+    if (in_dim != t.in_dim) return fail(GPEED_ERR_INVALID, "in_dim %d != tensor in_dim %d", in_dim, t.in_dim);
+    if ((int64_t)row0 + out_dim > t.rows)
+        return fail(GPEED_ERR_INVALID, "rows [%llu, %llu) past the tensor's %lld rows", (unsigned long long)row0,
+                    (unsigned long long)row0 + out_dim, (long long)t.rows);
+    if (!X || !Y || (reinterpret_cast<uintptr_t>(X) & 15)) return fail(GPEED_ERR_INVALID, "X must be a 16-byte aligned device pointer");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    p->t = &t;
+    p->nt = nt_for(n_tok);
+    if ((rc = pick_geo(in_dim, 1, p->nt, 0, &p->g))) return rc;
+    p->n_tok = n_tok;
+    p->in_dim = in_dim;
+    p->out_dim = out_dim;
+    p->g0 = (int64_t)row0 / 8 * 8;
+    p->skip = (int64_t)row0 - p->g0;
+    p->ntile = (p->skip + out_dim + p->g.tile_rows - 1) / p->g.tile_rows;
+    p->rows_eff = p->ntile * p->g.tile_rows;
+    p->ns = (n_tok + p->nt - 1) / p->nt;
+    p->direct = p->skip == 0 && p->rows_eff == out_dim;
+    return GPEED_OK;
+}
+
+int run_matmul(gpeed_ctx* c, const MatmulPlan& p, const float* X, float* Y, const MatmulScratch& sc,
+               cudaStream_t st) {
+    make_slots_kernel<<<1, 256, 0, st>>>(sc.slots, sc.nslots, p.n_tok, p.nt);
+    GP_CUDA(cudaGetLastError());
+    gp::GemvArgs a{};
+    a.w0 = p.t->packed + (p.g0 / 8) * 784 * (p.in_dim / 256);
+    a.w1 = nullptr;
+    a.expert_stride = 0;
+    a.in_dim = p.in_dim;
+    a.rows = (int)p.rows_eff;
+    a.tile_rows = p.g.tile_rows;
+    a.nwarps = p.g.nwarps;
+    a.stages = p.g.stages;
+    a.slots = sc.slots;
+    a.nslots = sc.nslots;
+    a.perm_tok = nullptr;
+    a.x = X;
+    a.x_bf16 = 0;
+    a.out = p.direct ? Y : sc.staged;
+    a.limit = 0.f;
+    a.tables = c->tables;
+    a.status = c->status;
+    const int grid = (int)std::min<int64_t>(c->num_sms, p.ntile * p.ns);
+    GP_CUDA(gp::launch_gemv(a, p.nt, false, p.g.passes, p.g.rpw, grid, st, false));
+    if (!p.direct)
+        GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * p.out_dim, sc.staged + p.skip, sizeof(float) * p.rows_eff,
+                                  sizeof(float) * p.out_dim, p.n_tok, cudaMemcpyDeviceToDevice, st));
     return GPEED_OK;
 }
 
@@ -535,7 +617,8 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
         if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
         if (c->dx.p) GP_CUDA(cudaMemset(c->dx.p, 0, c->dx.n * sizeof(unsigned long long)));
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
-                                      "4: expert id out of range, 8: bad shape)", st);
+                                      "4: expert id out of range, 8: bad shape, 16: a token or h value past the fp16 range "
+                                      "on the tensor-core path)", st);
     }
     return GPEED_OK;
 }
@@ -549,6 +632,11 @@ int gpeed_ctx_set_option(gpeed_ctx* c, int option, int value) {
             c->fused_max_tokens = value;
             return GPEED_OK;
         case GPEED_OPT_FUSED_COOPERATIVE: c->fused_cooperative = value != 0; return GPEED_OK;
+        case GPEED_OPT_SPIN_LIMIT:
+            if (value < 1) return fail(GPEED_ERR_INVALID, "GPEED_OPT_SPIN_LIMIT must be >= 1");
+            c->spin_limit = (uint32_t)value;
+            return GPEED_OK;
+        case GPEED_OPT_TEST_WITHHOLD_LOGIT: c->withhold_logit = value < 0 ? -1 : value; return GPEED_OK;
         case GPEED_OPT_TC_MIN_TOKENS:
             if (value < 1) return fail(GPEED_ERR_INVALID, "tensor-core threshold must be >= 1");
             c->tc_min_tokens = value;
@@ -636,54 +724,17 @@ int gpeed_tensor_download(gpeed_ctx* c, int handle, void* raw_host) {
 
 int gpeed_matmul_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* X, int n_tok,
                        float* Y, void* stream) {
-    if (!c || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
-    if (n_tok <= 0 || out_dim <= 0) return GPEED_OK;  // weights.cpp:88
-    const Tensor& t = c->tensors[handle];
-    if (in_dim != t.in_dim) return fail(GPEED_ERR_INVALID, "in_dim %d != tensor in_dim %d", in_dim, t.in_dim);
-    if ((int64_t)row0 + out_dim > t.rows)
-        return fail(GPEED_ERR_INVALID, "rows [%llu, %llu) past the tensor's %lld rows", (unsigned long long)row0,
-                    (unsigned long long)row0 + out_dim, (long long)t.rows);
-    if (!X || !Y || (reinterpret_cast<uintptr_t>(X) & 15)) return fail(GPEED_ERR_INVALID, "X must be a 16-byte aligned device pointer");
+    MatmulPlan p;
     int rc;
-    if ((rc = set_device(c))) return rc;
-    Geo g;
-    const int nt = nt_for(n_tok);
-    if ((rc = pick_geo(in_dim, 1, nt, 0, &g))) return rc;
-    cudaStream_t st = (cudaStream_t)stream;
-    const int64_t g0 = (int64_t)row0 / 8 * 8, skip = (int64_t)row0 - g0;
-    const int64_t ntile = (skip + out_dim + g.tile_rows - 1) / g.tile_rows;
-    const int64_t rows_eff = ntile * g.tile_rows;
-    const int ns = (n_tok + nt - 1) / nt;
-    if ((rc = c->slots.ensure(ns))) return rc;
+    if ((rc = plan_matmul(c, handle, row0, in_dim, out_dim, X, n_tok, Y, &p)) || p.empty) return rc;
+    MatmulScratch sc;
+    if ((rc = c->slots.ensure(p.ns))) return rc;
     if ((rc = c->nslots.ensure(1))) return rc;
-    const bool direct = skip == 0 && rows_eff == out_dim;
-    if (!direct && (rc = c->mvout.ensure((size_t)n_tok * rows_eff))) return rc;
-    make_slots_kernel<<<1, 256, 0, st>>>(c->slots.p, c->nslots.p, n_tok, nt);
-    GP_CUDA(cudaGetLastError());
-    gp::GemvArgs a{};
-    a.w0 = t.packed + (g0 / 8) * 784 * (in_dim / 256);
-    a.w1 = nullptr;
-    a.expert_stride = 0;
-    a.in_dim = in_dim;
-    a.rows = (int)rows_eff;
-    a.tile_rows = g.tile_rows;
-    a.nwarps = g.nwarps;
-    a.stages = g.stages;
-    a.slots = c->slots.p;
-    a.nslots = c->nslots.p;
-    a.perm_tok = nullptr;
-    a.x = X;
-    a.x_bf16 = 0;
-    a.out = direct ? Y : c->mvout.p;
-    a.limit = 0.f;
-    a.tables = c->tables;
-    a.status = c->status;
-    const int grid = (int)std::min<int64_t>(c->num_sms, ntile * ns);
-    GP_CUDA(gp::launch_gemv(a, nt, false, g.passes, g.rpw, grid, st, false));
-    if (!direct)
-        GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * out_dim, c->mvout.p + skip, sizeof(float) * rows_eff,
-                                  sizeof(float) * out_dim, n_tok, cudaMemcpyDeviceToDevice, st));
-    return GPEED_OK;
+    if (!p.direct && (rc = c->mvout.ensure((size_t)n_tok * p.rows_eff))) return rc;
+    sc.slots = c->slots.p;
+    sc.nslots = c->nslots.p;
+    sc.staged = p.direct ? nullptr : c->mvout.p;
+    return run_matmul(c, p, X, Y, sc, (cudaStream_t)stream);
 }
 
 int gpeed_matvec_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* x, float* dst,
@@ -840,6 +891,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         da.stages = 4;  // the deepest stage ring that fits next to the tables
         while (gp::decode_layer_smem(H, I, da.stages + 1) <= 227u * 1024u && da.stages < 8) ++da.stages;
         da.cooperative = c->fused_cooperative;
+        da.spin_limit = c->spin_limit;
+        da.withhold_logit = c->withhold_logit;
         // profiling: the one kernel's time goes to the gate/up slot, the other
         // stages read 0
         mark(2);
@@ -897,7 +950,7 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
         ro.chunk_counts = c->route_chunks.p;
         ro.chunk_cap = c->route_chunks.n;
         GP_CUDA(gp::launch_route(ro, st, false));
-        GP_CUDA(gp::launch_gather_cast(x, x_dtype == GPEED_DTYPE_BF16, c->perm.p, npos, H, c->xp.p, st));
+        GP_CUDA(gp::launch_gather_cast(x, x_dtype == GPEED_DTYPE_BF16, c->perm.p, npos, H, c->xp.p, c->status, st));
         mark(2);
         uint16_t* h16 = reinterpret_cast<uint16_t*>(c->h.p);  // npos x I fp16 fits the fp32 h scratch
         gp::TcArgs ga{c->slots.p, c->nslots.p, I / 128, H, I, s.swiglu_limit, h16, c->status};
@@ -1233,11 +1286,13 @@ int gpeed_moe_combine(gpeed_ctx* c, int n, int K, int hidden, const float* d_row
 }  // extern "C"
 
 // ---- allocation-free variant of gpeed_matmul_quant -------------------------
-// For callers that must not allocate device memory once they are serving: a
-// process inside CUDA graph capture, under a fixed memory budget, or embedded
-// in a host engine whose allocator owns the GPU.  The GEMV's work list and its
-// output staging live in this file-scope device array instead of ctx scratch.
-// Every GPU that loads the library holds the array until the process exits.
+// Some callers cannot call cudaMalloc once they are serving: an engine that
+// owns the GPU's memory through its own allocator or memory pool, a process
+// held to a fixed device-memory budget decided at start-up, or a host whose
+// allocations must not fail or stall in the middle of a step.  For them the
+// GEMV's work list and its output staging live in this file-scope device array
+// instead of context scratch.  Every GPU that loads the library holds the
+// array (GPEED_NOALLOC_SCRATCH_BYTES) until the process exits.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[GPEED_NOALLOC_SCRATCH_BYTES];
 
 namespace {
@@ -1246,8 +1301,10 @@ std::mutex g_noalloc_mu;
 constexpr int kMaxDevices = 64;
 unsigned char* g_noalloc_ptr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on `device` (which must be current):
-// looked up once per device, on that device's first call.
+// Device address of g_noalloc_scratch on `device`, which must be current: in
+// host code the array's name is only a host-side stand-in, so the address is
+// looked up with cudaGetSymbolAddress, once per device, on that device's first
+// call.
 int noalloc_scratch(int device, unsigned char** out) {
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
     if (device < 0 || device >= kMaxDevices) return fail(GPEED_ERR_INVALID, "device %d out of range", device);
@@ -1262,19 +1319,6 @@ int noalloc_scratch(int device, unsigned char** out) {
     return GPEED_OK;
 }
 
-__global__ void noalloc_slots_kernel(gp::SlotDesc* slots, int* nslots, int n_tok, int nt) {
-    const int ns = (n_tok + nt - 1) / nt;
-    for (int i = threadIdx.x; i < ns; i += blockDim.x) {
-        gp::SlotDesc sd;
-        sd.expert = 0;
-        sd.begin = i * nt;
-        sd.ntok = min(nt, n_tok - i * nt);
-        sd.pad = 0;
-        slots[i] = sd;
-    }
-    if (threadIdx.x == 0) *nslots = ns;
-}
-
 size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
 }  // namespace
@@ -1283,64 +1327,25 @@ extern "C" {
 
 int gpeed_matmul_quant_noalloc(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* X,
                                int n_tok, float* Y, void* stream) {
-    if (!c || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
-    if (n_tok <= 0 || out_dim <= 0) return GPEED_OK;
-    const Tensor& t = c->tensors[handle];
-    if (in_dim != t.in_dim) return fail(GPEED_ERR_INVALID, "in_dim %d != tensor in_dim %d", in_dim, t.in_dim);
-    if ((int64_t)row0 + out_dim > t.rows)
-        return fail(GPEED_ERR_INVALID, "rows [%llu, %llu) past the tensor's %lld rows", (unsigned long long)row0,
-                    (unsigned long long)row0 + out_dim, (long long)t.rows);
-    if (!X || !Y || (reinterpret_cast<uintptr_t>(X) & 15)) return fail(GPEED_ERR_INVALID, "X must be a 16-byte aligned device pointer");
+    MatmulPlan p;
     int rc;
-    if ((rc = set_device(c))) return rc;
-    Geo g;
-    const int nt = nt_for(n_tok);
-    if ((rc = pick_geo(in_dim, 1, nt, 0, &g))) return rc;
-    const int64_t g0 = (int64_t)row0 / 8 * 8, skip = (int64_t)row0 - g0;
-    const int64_t ntile = (skip + out_dim + g.tile_rows - 1) / g.tile_rows;
-    const int64_t rows_eff = ntile * g.tile_rows;
-    const int ns = (n_tok + nt - 1) / nt;
-    const bool direct = skip == 0 && rows_eff == out_dim;
-    // scratch layout: [slots][nslots][staged output]
-    const size_t off_n = align256((size_t)ns * sizeof(gp::SlotDesc));
+    if ((rc = plan_matmul(c, handle, row0, in_dim, out_dim, X, n_tok, Y, &p)) || p.empty) return rc;
+    // scratch layout: [slots][nslots][staged output]; the slot kernel rewrites
+    // the work list on every call, so nothing left by a previous call is read
+    const size_t off_n = align256((size_t)p.ns * sizeof(gp::SlotDesc));
     const size_t off_y = off_n + 256;
-    const size_t need = off_y + (direct ? 0 : (size_t)n_tok * rows_eff * sizeof(float));
+    const size_t need = off_y + p.staged_floats() * sizeof(float);
     if (need > GPEED_NOALLOC_SCRATCH_BYTES)
         return fail(GPEED_ERR_INVALID, "matmul_quant_noalloc: %zu bytes of scratch needed, the static limit is %u "
                     "(n_tok * ceil(out_dim + row0 %% 8, %d) * 4 bytes of staging when row0 %% 8 != 0 or out_dim %% %d "
-                    "!= 0, plus the work list)", need, GPEED_NOALLOC_SCRATCH_BYTES, g.tile_rows, g.tile_rows);
+                    "!= 0, plus the work list)", need, GPEED_NOALLOC_SCRATCH_BYTES, p.g.tile_rows, p.g.tile_rows);
     unsigned char* scratch = nullptr;
     if ((rc = noalloc_scratch(c->device, &scratch))) return rc;
-    gp::SlotDesc* slots = reinterpret_cast<gp::SlotDesc*>(scratch);
-    int* nslots = reinterpret_cast<int*>(scratch + off_n);
-    float* staged = reinterpret_cast<float*>(scratch + off_y);
-    cudaStream_t st = (cudaStream_t)stream;
-    noalloc_slots_kernel<<<1, 256, 0, st>>>(slots, nslots, n_tok, nt);
-    GP_CUDA(cudaGetLastError());
-    gp::GemvArgs a{};
-    a.w0 = t.packed + (g0 / 8) * 784 * (in_dim / 256);
-    a.w1 = nullptr;
-    a.expert_stride = 0;
-    a.in_dim = in_dim;
-    a.rows = (int)rows_eff;
-    a.tile_rows = g.tile_rows;
-    a.nwarps = g.nwarps;
-    a.stages = g.stages;
-    a.slots = slots;
-    a.nslots = nslots;
-    a.perm_tok = nullptr;
-    a.x = X;
-    a.x_bf16 = 0;
-    a.out = direct ? Y : staged;
-    a.limit = 0.f;
-    a.tables = c->tables;
-    a.status = c->status;
-    const int grid = (int)std::min<int64_t>(c->num_sms, ntile * ns);
-    GP_CUDA(gp::launch_gemv(a, nt, false, g.passes, g.rpw, grid, st, false));
-    if (!direct)
-        GP_CUDA(cudaMemcpy2DAsync(Y, sizeof(float) * out_dim, staged + skip, sizeof(float) * rows_eff,
-                                  sizeof(float) * out_dim, n_tok, cudaMemcpyDeviceToDevice, st));
-    return GPEED_OK;
+    MatmulScratch sc;
+    sc.slots = reinterpret_cast<gp::SlotDesc*>(scratch);
+    sc.nslots = reinterpret_cast<int*>(scratch + off_n);
+    sc.staged = p.direct ? nullptr : reinterpret_cast<float*>(scratch + off_y);
+    return run_matmul(c, p, X, Y, sc, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -23,6 +23,7 @@ enum gp_dev_status : uint32_t {
     GP_DEV_TIMEOUT_EMPTY = 2,    // producer gave up waiting for a stage to drain
     GP_DEV_BAD_EXPERT = 4,       // an expert id outside [0, E)
     GP_DEV_BAD_SHAPE = 8,
+    GP_DEV_FP16_RANGE = 16,      // a token value or an h value past the fp16 range (tensor-core path)
 };
 
 GP_DEVINL uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -95,17 +96,18 @@ GP_DEVINL bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and leaves the barrier alone) after GP_SPIN_LIMIT polls.
-GP_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < GP_SPIN_LIMIT; ++i)
+// Bounded wait: returns false (and leaves the barrier alone) after `limit`
+// polls (GP_SPIN_LIMIT unless the kernel takes its limit at run time).
+GP_DEVINL bool mbar_wait(uint32_t bar, uint32_t parity, uint32_t limit = GP_SPIN_LIMIT) {
+    for (uint32_t i = 0; i < limit; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
 
 // Bounded wait for a phase expected to take long: sleeps between polls so the
 // waiting warp leaves the issue slots to the others.
-GP_DEVINL bool mbar_wait_sleepy(uint32_t bar, uint32_t parity) {
-    for (uint32_t i = 0; i < GP_SPIN_LIMIT; ++i) {
+GP_DEVINL bool mbar_wait_sleepy(uint32_t bar, uint32_t parity, uint32_t limit = GP_SPIN_LIMIT) {
+    for (uint32_t i = 0; i < limit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         __nanosleep(256);
     }

@@ -209,7 +209,7 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t t
     // tag: the data is its own flag, so one poll round trip suffices
     unsigned long long w[EJ];
     uint32_t n = 0;
-    for (; n < GP_SPIN_LIMIT; ++n) {
+    for (; n < a.spin_limit; ++n) {
 #pragma unroll
         for (int j = 0; j < EJ; ++j)
             w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + logit_word(c % kLogitCopies, lane + 32 * j, E)) : 0ull;
@@ -219,7 +219,7 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t t
         if (__all_sync(0xffffffffu, ok)) break;
         __nanosleep(TOPK_POLL_NS);
     }
-    if (n == GP_SPIN_LIMIT && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+    if (n == a.spin_limit && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
     if (lane == 0) GP_STAMP(11);
     float score[EJ];
     uint32_t key[EJ], id[EJ];
@@ -496,13 +496,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 // poll of every slot's counter) until all its units are counted
                 if (!((ready >> slot) & 1u)) {
                     uint32_t n = 0;
-                    for (; n < GP_SPIN_LIMIT; ++n) {
+                    for (; n < a.spin_limit; ++n) {
                         const unsigned cnt = lane <= K ? ld_relaxed(a.sync + kSyncSlot + lane) : 0u;
                         ready = __ballot_sync(0xffffffffu, lane <= K && cnt >= (unsigned)NU);
                         if ((ready >> slot) & 1u) break;
                         __nanosleep(64);
                     }
-                    if (n == GP_SPIN_LIMIT) {
+                    if (n == a.spin_limit) {
                         if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                         break;
                     }
@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             if (lane == 0) {
                 bool ok = true;
                 if (it >= n_shared && !have_topk) {  // routed tiles need the top-k
-                    ok = have_topk = mbar_wait(topk_bar, 0);
+                    ok = have_topk = mbar_wait(topk_bar, 0, a.spin_limit);
                     if (ok) GP_STAMP(10);
                     else { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 }
@@ -531,7 +531,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                         src0 = a.down + (int64_t)e * a.d_stride + off;
                         src1 = a.hq + (int64_t)slot * HQ_BYTES;
                     }
-                    if (!mbar_wait(empty0 + 8u * s, ph)) {
+                    if (!mbar_wait(empty0 + 8u * s, ph, a.spin_limit)) {
                         *s_abort = 1;
                         atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
                     } else {
@@ -549,8 +549,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         if (lane == 0) {
             // no copy may still be in flight when the CTA exits
             for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
-                mbar_wait(full0 + 8u * (i % S), (uint32_t)(i / S) & 1u);
-            mbar_wait(tbar, 0);
+                mbar_wait(full0 + 8u * (i % S), (uint32_t)(i / S) & 1u);  // the compile-time limit,
+            mbar_wait(tbar, 0);                                           // whatever the run-time one
         }
         return;
     }
@@ -564,14 +564,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         pdl_wait();
         const uint32_t tag = ld_relaxed(a.sync + kSyncGen) + 1u;
         if (n_tasks > 0) {  // this CTA's experts: slices added in order
-            if (!mbar_wait(rbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (!mbar_wait(rbar, 0, a.spin_limit) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (lane < n_own) {
                 float lg = 0.f;
 #pragma unroll
                 for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[lane * RSPLIT + sl];
                 const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(lg);
+                if (c + lane * G != a.withhold_logit) {  // (a test withholds one to make the top-k wait run out)
 #pragma unroll
-                for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.logits + logit_word(cp, c + lane * G, E), v);
+                    for (int cp = 0; cp < kLogitCopies; ++cp)
+                        st_relaxed64(a.logits + logit_word(cp, c + lane * G, E), v);
+                }
             }
         }
         if (lane == 0) GP_STAMP(1);
@@ -585,7 +588,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         float hv = 0.f;
         for (int it = 0; it < n_items; ++it) {
             const bool gu = it < n_gu;
-            if (!*s_abort && !mbar_wait(pdone0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (!*s_abort && !mbar_wait(pdone0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             const float* pbuf = partial + (size_t)s * pstride;
             float val = 0.f;
             if (gu) {
@@ -632,7 +635,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     if (v == tb) {
                         if (te > R.v1) {
                             uint32_t n = 0;
-                            for (; n < GP_SPIN_LIMIT; ++n) {
+                            for (; n < a.spin_limit; ++n) {
                                 bool ok = true;
                                 for (int base = R.v1; base < te; base += 8) {  // 8 loads in flight
                                     unsigned long long w[8];
@@ -649,7 +652,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                                 if (__all_sync(0xffffffffu, ok)) break;
                                 __nanosleep(64);
                             }
-                            if (n == GP_SPIN_LIMIT && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                            if (n == a.spin_limit && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                         }
                         __syncwarp();
                         float y = 0.f;
@@ -708,7 +711,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             }
         }
 
-        if (!mbar_wait(tbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+        if (!mbar_wait(tbar, 0, a.spin_limit) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         int s = 0;
         uint32_t ph = 0;
         // ---- gate/up tiles: warps 0..NWG-1; warp 0 also arrives for the
@@ -718,7 +721,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             uint32_t xq[16];
             const float sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
             for (int it = 0; it < n_gu; ++it) {
-                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 if (tid == 0 && it == n_shared) GP_STAMP(3);
                 if (!*s_abort)
                     consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
@@ -730,7 +733,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         } else {
             // once warp 0 has passed every gate/up stage, the first down
             // stage is at most one phase ahead of its parity wait
-            if (!mbar_wait_sleepy(gbar, 0) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (!mbar_wait_sleepy(gbar, 0, a.spin_limit) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             s = n_gu % S;
             ph = (uint32_t)(n_gu / S) & 1u;
         }
@@ -739,7 +742,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         {
             const auto md = lane_map<II, NWC, PD>(warp, lane, stage0);
             for (int it = n_gu; it < n_items; ++it) {
-                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 if (tid == 0 && it == n_gu) GP_STAMP(5);
                 if (!*s_abort) {
                     const uint32_t xb = stage0 + s * L.stage_bytes + DN_BYTES;
@@ -799,11 +802,23 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
     const Smem L = decode_smem(a.H, a.I, a.stages);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
     auto kern = decode_layer_kernel<5120, 1536, 4, 1, 2, 2>;
-    static int configured = 0;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        configured = 1;
+    static std::atomic<unsigned long long> configured{0};  // per device
+    if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured)) return e0;
+    // Co-residency: every CTA waits on data the others publish, so the grid
+    // must fit the GPU at one CTA per SM.  Checked against the kernel's real
+    // resource use (registers, shared memory) once per device; a grid larger
+    // than the SMs that can hold a CTA is refused rather than left to time out.
+    static std::atomic<unsigned long long> fits{0};
+    int dev = 0;
+    if (cudaError_t e1 = cudaGetDevice(&dev)) return e1;
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (!bit || !(fits.load(std::memory_order_acquire) & bit)) {
+        int per_sm = 0, sms = 0;
+        if (cudaError_t e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NTHREADS, 227 * 1024))
+            return e2;
+        if (cudaError_t e3 = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) return e3;
+        if (per_sm < 1 || grid > sms * per_sm) return cudaErrorCooperativeLaunchTooLarge;
+        if (bit) fits.fetch_or(bit, std::memory_order_acq_rel);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

@@ -45,10 +45,12 @@ GP_DEVINL float silu_clamped(float g, float u, float lim) {
 // The same, for results rounded to fp16 right after (the tensor-core path's h):
 // hardware exp2 and reciprocal approximations, a few fp32 ulps, far below the
 // fp16 rounding that follows.
-GP_DEVINL __half silu_clamped_h(float g, float u, float lim) {
+GP_DEVINL __half silu_clamped_h(float g, float u, float lim, bool& over) {
     const float gi = fminf(g, lim);
     const float ui = fminf(fmaxf(u, -lim), lim);
-    return __float2half_rn(__fdividef(gi, 1.0f + __expf(-gi)) * ui);
+    const float h = __fdividef(gi, 1.0f + __expf(-gi)) * ui;
+    over |= fabsf(h) >= 65520.0f;  // rounds to an fp16 infinity
+    return __float2half_rn(h);
 }
 
 // Sum of M per-lane values across the warp, sharing shuffles between values:

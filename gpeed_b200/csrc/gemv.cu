@@ -303,12 +303,9 @@ cudaError_t launch_t(const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
     const int nthreads = 32 * (a.nwarps + 1);
     if (nthreads > threads_cap(NT, GATEUP) || L.total > 227u * 1024u) return cudaErrorInvalidValue;
     auto kern = gemv_kernel<NT, GATEUP, P, RPW>;
-    static int configured = 0;  // opt-in shared memory is raised once per instantiation
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        configured = 1;
-    }
+    static std::atomic<unsigned long long> configured{0};  // per device, per instantiation
+    cudaError_t e = raise_smem_limit(kern, 227 * 1024, configured);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(nthreads);

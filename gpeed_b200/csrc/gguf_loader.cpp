@@ -86,7 +86,9 @@ TypeSize type_size(int t) {
 uint64_t payload_bytes(int type, uint64_t n_elements) {
     const TypeSize ts = type_size(type);
     if (!ts.bytes || n_elements % (uint64_t)ts.block) return 0;
-    return n_elements / (uint64_t)ts.block * (uint64_t)ts.bytes;
+    uint64_t bytes = 0;
+    if (__builtin_mul_overflow(n_elements / (uint64_t)ts.block, (uint64_t)ts.bytes, &bytes)) return 0;
+    return bytes;
 }
 
 enum VType : int { U8 = 0, I8 = 1, U16 = 2, I16 = 3, U32 = 4, I32 = 5, F32 = 6, BOOL = 7, STR = 8, ARR = 9,
@@ -298,14 +300,22 @@ int open_shard(gpeed_gguf* g, const std::string& path, int index) {
         if (nd == 0 || nd > 4) return err(GPEED_ERR_UNSUPPORTED, "GGUF: tensor '%s' has %u dims", t.name.c_str(), nd);
         t.n_dims = (int)nd;
         uint64_t ne = 1;
+        bool wrapped = false;
         for (uint32_t d = 0; d < nd; ++d) {
             t.dims[d] = c.get<uint64_t>();
-            ne *= t.dims[d];
+            wrapped |= __builtin_mul_overflow(ne, t.dims[d], &ne);
         }
         t.type = (int)c.get<uint32_t>();
         t.offset = c.get<uint64_t>();
         t.shard = index;
+        if (!c.ok) break;
+        if (wrapped) return err(GPEED_ERR_INVALID, "GGUF: tensor '%s': element count overflows 64 bits", t.name.c_str());
         t.nbytes = payload_bytes(t.type, ne);
+        // a known type whose element count is not a whole number of blocks, or
+        // whose byte count overflows, describes no payload this reader can map
+        if (type_size(t.type).bytes && ne && !t.nbytes)
+            return err(GPEED_ERR_INVALID, "GGUF: tensor '%s': %llu elements do not form whole blocks of type %d",
+                       t.name.c_str(), (unsigned long long)ne, t.type);
         g->tensors.push_back(std::move(t));
     }
     if (!c.ok) return err(GPEED_ERR_INVALID, "GGUF: unexpected end of tensor table in %s", path.c_str());

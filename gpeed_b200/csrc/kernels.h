@@ -3,7 +3,27 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace gp {
+
+// Raises `kern`'s opt-in dynamic shared-memory limit to `bytes` on the current
+// device.  The attribute belongs to each device's context, so it is recorded
+// per device (bit d of `done`, one word per kernel instantiation): a process
+// that drives several GPUs sets it on each of them.  Two host threads racing
+// here both set the same value, which is harmless.  Devices past 63 set it on
+// every launch.
+template <typename F>
+inline cudaError_t raise_smem_limit(F kern, int bytes, std::atomic<unsigned long long>& done) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
+    if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+    return e;
+}
 
 // One unit of expert work: `ntok` consecutive assignments starting at `begin`
 // (positions in the expert-sorted assignment list) that all use `expert`.
@@ -162,6 +182,8 @@ struct DecodeLayerArgs {
     uint32_t* status;
     int stages;
     int cooperative;           // 1: cooperative launch instead of programmatic dependent launch
+    uint32_t spin_limit;       // polls before any wait gives up (sets a GP_DEV_TIMEOUT_* bit)
+    int withhold_logit;        // test hook: the router logit of this expert is never published (-1: none)
 };
 // Tensor-core experts for large batches (tc_moe.cu).
 struct TcArgs {
@@ -176,8 +198,10 @@ struct TcArgs {
 // Tokens per expert slot of the tensor-core path (the MMA N bound).
 int tc_moe_slot_tokens();
 bool tc_moe_supported(int H, int I);
+// Token rows to fp16 in expert-sorted order; a value past the fp16 range sets
+// GP_DEV_FP16_RANGE in *status.
 cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
-                               cudaStream_t st);
+                               uint32_t* status, cudaStream_t st);
 cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t weight_rows, const uint16_t* b,
                           int npos, const TcArgs& args, int grid, cudaStream_t st);
 

@@ -646,11 +646,10 @@ cudaError_t launch_route(const RouteArgs& a, cudaStream_t st, bool pdl) {
     }
     const size_t smem = route_smem_bytes(a.n, a.E, a.K);
     if (smem > 200 * 1024) return cudaErrorInvalidValue;
-    static size_t configured = 0;
-    if (smem > 48 * 1024 && configured < smem) {
-        cudaError_t e = cudaFuncSetAttribute(route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    static std::atomic<unsigned long long> configured{0};  // per device: the limit is always 200 KB
+    if (smem > 48 * 1024) {
+        cudaError_t e = raise_smem_limit(route_kernel, 200 * 1024, configured);
         if (e != cudaSuccess) return e;
-        configured = 200 * 1024;
     }
     cudaLaunchAttribute attr[1];
     RouteArgs b = a;

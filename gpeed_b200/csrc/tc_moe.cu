@@ -390,6 +390,7 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
         int sr = 0, as = 0;         // stage of the raw ring and of the A ring
         uint32_t rph = 0, aph = 0;  // their phase parities
         bool ok = true;
+        bool h_over = false;  // an h value past the fp16 range (gate/up epilogue)
         TC_MARK(t_all);
         for (int t = blockIdx.x, lt = 0; t < ntiles && ok; t += gridDim.x, ++lt) {
             if (decoder) {
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
                     for (int jj = 0; jj < 16; ++jj)
                         if (j0 + jj < sd.ntok)
                             h[(int64_t)(sd.begin + j0 + jj) * a.nout + row] =
-                                silu_clamped_h(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit);
+                                silu_clamped_h(__uint_as_float(v0[jj]), __uint_as_float(v1[jj]), a.limit, h_over);
                 }
             } else {
                 for (int j0 = 32 * kq; j0 < TBN && j0 < sd.ntok; j0 += 32 * PER_Q) {
@@ -472,6 +473,7 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
             TC_ACC(6, t_ep);
         }
         if (!ok && lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+        if (__any_sync(0xffffffffu, h_over) && lane == 0) atomicOr(a.status, GP_DEV_FP16_RANGE);
         TC_ACC(7, t_all);
         if (lane == 0 && (warp == WDEC0 || warp == WEPI0)) TC_DUMP(GU, warp == WDEC0 ? 2 : 3);
     }
@@ -486,8 +488,9 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
 // Casts token rows to fp16 in expert-sorted order: xp[p] = x[perm[p]].  One
 // CTA per row at a time, 16-byte loads and stores.
 __global__ void __launch_bounds__(128) gather_cast_kernel(const void* x, int x_bf16, const int* perm, int npos, int H,
-                                                          __half* xp) {
+                                                          __half* xp, uint32_t* status) {
     const int qpr = H / 8;  // 8 elements per thread step
+    bool over = false;      // a value that rounds to an fp16 infinity (|v| >= 65520)
     for (int p = blockIdx.x; p < npos; p += gridDim.x) {
         const int64_t src = (int64_t)perm[p] * H;
         uint4* dst = reinterpret_cast<uint4*>(xp + (int64_t)p * H);
@@ -506,6 +509,8 @@ __global__ void __launch_bounds__(128) gather_cast_kernel(const void* x, int x_b
                 const float4 b = *reinterpret_cast<const float4*>(static_cast<const float*>(x) + src + q * 8 + 4);
                 v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
             }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) over |= fabsf(v[j]) >= 65520.0f;
             uint4 o;
             __half2 h0 = __floats2half2_rn(v[0], v[1]), h1 = __floats2half2_rn(v[2], v[3]);
             __half2 h2 = __floats2half2_rn(v[4], v[5]), h3 = __floats2half2_rn(v[6], v[7]);
@@ -516,6 +521,7 @@ __global__ void __launch_bounds__(128) gather_cast_kernel(const void* x, int x_b
             dst[q] = o;
         }
     }
+    if (__any_sync(0xffffffffu, over) && (threadIdx.x & 31) == 0) atomicOr(status, GP_DEV_FP16_RANGE);
 }
 
 // Maps for one repacked IQ3_XXS matrix of `groups` 8-row groups, kin inputs.
@@ -562,9 +568,9 @@ bool tc_moe_supported(int H, int I) {
 }
 
 cudaError_t launch_gather_cast(const void* x, int x_bf16, const int* perm, int npos, int H, uint16_t* xp,
-                               cudaStream_t st) {
+                               uint32_t* status, cudaStream_t st) {
     if (npos <= 0) return cudaSuccess;
-    gather_cast_kernel<<<148 * 16, 128, 0, st>>>(x, x_bf16, perm, npos, H, reinterpret_cast<__half*>(xp));
+    gather_cast_kernel<<<148 * 16, 128, 0, st>>>(x, x_bf16, perm, npos, H, reinterpret_cast<__half*>(xp), status);
     return cudaGetLastError();
 }
 

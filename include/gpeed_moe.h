@@ -110,6 +110,19 @@ GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
  * Measured with uniform routing: 8 tokens 0.30 ms per layer this way against
  * 0.52 ms on the tensor cores. */
 #define GPEED_OPT_FUSED_MAX_TOKENS 4
+/* GPEED_OPT_SPIN_LIMIT (default GPEED_SPIN_LIMIT_DEFAULT polls, a few seconds
+ * under load): how long a wait inside the fused batch-1 kernel (on a pipeline
+ * stage, or on data other CTAs publish) polls before it gives up, sets a
+ * timeout bit that gpeed_ctx_check reports, and lets the kernel finish with
+ * invalid results instead of hanging the GPU.  No counterpart in the
+ * reference (it only throws, weights.cpp:21,25). */
+#define GPEED_OPT_SPIN_LIMIT 5
+#define GPEED_SPIN_LIMIT_DEFAULT (1 << 22)
+/* GPEED_OPT_TEST_WITHHOLD_LOGIT (default -1): FOR TESTS ONLY.  The fused
+ * kernel never publishes the router logit of this expert id, so every CTA's
+ * wait for the full set of logits runs out (after GPEED_OPT_SPIN_LIMIT polls)
+ * and the timeout path can be exercised without any fault; -1 turns it off. */
+#define GPEED_OPT_TEST_WITHHOLD_LOGIT 6
 GPEED_API int gpeed_ctx_set_option(gpeed_ctx* ctx, int option, int value);
 
 /* Per-stage timing of gpeed_moe_forward (no counterpart in the reference;
@@ -147,17 +160,22 @@ GPEED_API int gpeed_matvec_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int 
 GPEED_API int gpeed_matmul_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim, const float* X_dev,
                        int n_tok, float* Y_dev, void* stream);
 
-/* Same result as gpeed_matmul_quant, for callers that cannot allocate device
- * memory while they run (inside CUDA graph capture, under a fixed memory
- * budget, or behind a host engine's own allocator).  No counterpart in the
- * reference.  It allocates nothing: its work list and output staging use one
- * static 4 MiB device array (GPEED_NOALLOC_SCRATCH_BYTES) that every GPU
- * loading the library keeps until exit.  Calls needing more scratch than that
- * fail with GPEED_ERR_INVALID: the staging is n_tok * (out_dim + row0 % 8
- * rounded up to the row tile) * 4 bytes and is only used when row0 % 8 != 0
- * or out_dim is not a multiple of the row tile.  The first call on a device
- * looks the array's address up (make it before any stream capture).  All calls
- * share the array, so calls that overlap on the GPU race; serialise them. */
+/* Same result as gpeed_matmul_quant (bit for bit: the same kernels on the same
+ * work list), for callers that cannot call cudaMalloc once they are serving:
+ * an engine whose own allocator or memory pool owns the GPU's memory, a
+ * process held to a device-memory budget fixed at start-up, or a host whose
+ * allocations must not fail or stall in the middle of a step.  No counterpart
+ * in the reference.  It allocates nothing (no cudaMalloc, cudaFree or
+ * allocating library call): its work list and output staging use one static
+ * 4 MiB device array (GPEED_NOALLOC_SCRATCH_BYTES) that every GPU loading the
+ * library keeps until exit.  Calls needing more scratch than that fail with
+ * GPEED_ERR_INVALID: the staging is n_tok * (out_dim + row0 % 8 rounded up to
+ * the row tile) * 4 bytes and is only used when row0 % 8 != 0 or out_dim is
+ * not a multiple of the row tile.  The first call on a device looks the
+ * array's device address up (cudaGetSymbolAddress), so make that first call
+ * before any stream capture.  All calls share the array and it keeps the last
+ * call's contents (each call rewrites what it reads), so calls that overlap on
+ * the GPU race; serialise them. */
 #define GPEED_NOALLOC_SCRATCH_BYTES (4u << 20)
 GPEED_API int gpeed_matmul_quant_noalloc(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim,
                                          const float* X_dev, int n_tok, float* Y_dev, void* stream);

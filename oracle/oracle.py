@@ -9,6 +9,7 @@ sources.  Both expose the same functions, wrapped here for numpy arrays.
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 import subprocess
 
@@ -29,9 +30,24 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
 
+def reference_root() -> str | None:
+    """The reference project's source tree, or None when it is not on this
+    machine (it never is on a GPU box).  Taken from GPEED_REFERENCE_ROOT, else
+    from the `reference_path` BASELINE.json records for this build."""
+    root = os.environ.get("GPEED_REFERENCE_ROOT")
+    if not root:
+        try:
+            with open(os.path.join(HERE, "..", "BASELINE.json")) as fh:
+                root = json.load(fh).get("reference_path")
+        except (OSError, ValueError):
+            root = None
+    return root if root and os.path.isdir(os.path.join(root, "cpp")) else None
+
+
 def build() -> None:
     """Compiles liboracle.so (and oracle/_ref when the reference tree exists)."""
-    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    ref = reference_root()
+    subprocess.run(["make", "-s", "-C", HERE] + ([f"REF={ref}"] if ref else []), check=True)
 
 
 def available(kind: str) -> bool:

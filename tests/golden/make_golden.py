@@ -47,6 +47,8 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.abspath(os.path.join(HERE, "..", ".."))
+sys.path.insert(0, REPO)
+from oracle import oracle  # noqa: E402  (the repo root is not a package path when run as a script)
 
 
 class Shape(ctypes.Structure):
@@ -153,9 +155,13 @@ def edge_blocks(rng: np.random.Generator) -> np.ndarray:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("GPEED_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=None, help="reference source tree (default: GPEED_REFERENCE_ROOT, else "
+                    "BASELINE.json's reference_path)")
     ap.add_argument("--only", choices=["gguf", "codecs"], default=None)
     args = ap.parse_args()
+    args.ref = args.ref or oracle.reference_root()
+    if not args.ref:
+        ap.error("the reference source tree is required: pass --ref or set GPEED_REFERENCE_ROOT")
     ref = ctypes.CDLL(os.path.join(REPO, "oracle", "_ref", "libgpeed_ref.so"))
     if args.only in (None, "gguf"):
         selftest_gguf(args.ref)

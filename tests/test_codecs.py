@@ -21,6 +21,7 @@ import numpy as np
 import pytest
 
 from gpeed_b200 import _capi
+from oracle import oracle
 from tests.helpers import CODEC_NAMES, CODECS, codec_blocks
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
@@ -51,8 +52,8 @@ def test_codebooks_are_pinned():
     assert hashlib.sha256(struct.pack("<1024Q", *g2)).hexdigest() == pins["GPEED_IQ2S_GRID_SHA256"]
     assert hashlib.sha256(struct.pack("<512I", *g3)).hexdigest() == pins["GPEED_IQ3S_GRID_SHA256"]
     assert hashlib.sha256(struct.pack("<16b", *v4)).hexdigest() == pins["GPEED_IQ4NL_VALUES_SHA256"]
-    ref = os.environ.get("GPEED_REFERENCE_ROOT", "/root/reference")
-    hdr = os.path.join(ref, "cpp", "core", "include", "glm5", "quant_tables.h")
+    ref = oracle.reference_root()
+    hdr = os.path.join(ref or "", "cpp", "core", "include", "glm5", "quant_tables.h")
     if os.path.exists(hdr):
         rt = open(hdr).read()
         for name, mine in (("kIq2sGrid", g2), ("kIq3sGrid", g3), ("kValuesIq4nl", v4)):

@@ -125,6 +125,24 @@ def test_malformed_files_fail_cleanly(tmp_path):
         GgufModel(str(tmp_path / "absent.gguf"))
 
 
+def test_tensor_dims_that_overflow_or_split_a_block_are_refused(tmp_path):
+    """A tensor table whose dims multiply past 64 bits, or whose element count
+    is not a whole number of blocks of a known type, is rejected by name
+    instead of being accepted with a wrapped byte count."""
+    p = tmp_path / "wrap.gguf"
+    write_gguf(str(p), [], [("big", [1 << 33, 1 << 33], 0, b"")])
+    with pytest.raises(GpeedError, match="big.*overflows"):
+        GgufModel(str(p))
+    p = tmp_path / "partial.gguf"
+    write_gguf(str(p), [], [("half_block", [300], 18, b"\0" * 98)])  # IQ3_XXS blocks hold 256 values
+    with pytest.raises(GpeedError, match="half_block.*whole blocks"):
+        GgufModel(str(p))
+    p = tmp_path / "unknown.gguf"  # a type without a known block size still opens (nbytes 0)
+    write_gguf(str(p), [], [("odd", [7], 99, b"\0" * 16)])
+    with GgufModel(str(p)) as m:
+        assert m.find_tensor("odd").nbytes == 0
+
+
 def _tiny_bytes(z):
     from oracle import oracle
     H, I, E = (int(z[k]) for k in ("H", "I", "E"))

@@ -11,7 +11,7 @@ import pytest
 from oracle import oracle
 
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-REF_ROOT = os.environ.get("GPEED_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = oracle.reference_root() or ""
 GRID_H = os.path.join(os.path.dirname(__file__), "..", "gpeed_b200", "csrc", "iq3xxs_grid.h")
 
 
