@@ -96,6 +96,12 @@ GP_DEVINL unsigned ld_relaxed(const unsigned* p) {
     return v;
 }
 
+// Warp-uniform view of the CTA's abort flag.  Lanes read the volatile word
+// separately and may see it change between reads; every branch that contains
+// warp-collective operations (shuffles, votes) must use one value for the
+// whole warp.
+GP_DEVINL bool warp_aborted(const volatile uint32_t* s_abort) { return __any_sync(0xffffffffu, *s_abort != 0u); }
+
 // Monotonic map of a float onto u32 (for redux max); -0 is folded onto +0 first.
 GP_DEVINL uint32_t order_key(float f) {
     const uint32_t u = __float_as_uint(f + 0.0f);
@@ -564,7 +570,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         pdl_wait();
         const uint32_t tag = ld_relaxed(a.sync + kSyncGen) + 1u;
         if (n_tasks > 0) {  // this CTA's experts: slices added in order
-            if (!mbar_wait(rbar, 0, a.spin_limit) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (!mbar_wait(rbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (lane < n_own) {
                 float lg = 0.f;
 #pragma unroll
@@ -586,9 +592,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         uint32_t ph = 0;
         constexpr int rsg = 32 * NWG / (H / 32), rsd = 32 * NWC / (I / 32);
         float hv = 0.f;
+        // After an abort every warp leaves its loop at once (and arrives on no
+        // further barrier), so no barrier phase sees arrivals from two
+        // iterations; every wait left behind in another warp is bounded.
         for (int it = 0; it < n_items; ++it) {
             const bool gu = it < n_gu;
-            if (!*s_abort && !mbar_wait(pdone0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (warp_aborted(s_abort)) break;
+            if (!mbar_wait(pdone0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (warp_aborted(s_abort)) break;
             const float* pbuf = partial + (size_t)s * pstride;
             float val = 0.f;
             if (gu) {
@@ -616,13 +627,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 const int j = it % TPU;
                 const float v = __shfl_sync(0xffffffffu, val, lane & (TRG - 1));
                 if ((lane / TRG) == j) hv = v;
-                if (j == TPU - 1 && !*s_abort) {
+                if (j == TPU - 1) {
                     const Item u = item_of(c + (it / TPU) * G, NU, K);
                     quantise_unit(hv, a.hq + (int64_t)u.slot * HQ_BYTES, I, u.idx, lane);
                     __syncwarp();
                     if (lane == 0) red_release_add(a.sync + kSyncSlot + u.slot, 1);
                 }
-            } else if (!*s_abort) {
+            } else {
                 const int v = R.at(it - n_gu), t = v / (K + 1);
                 const int slot = down_slot(v % (K + 1), K);
                 const int j = t * TRD + lane;
@@ -711,7 +722,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             }
         }
 
-        if (!mbar_wait(tbar, 0, a.spin_limit) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+        if (!mbar_wait(tbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         int s = 0;
         uint32_t ph = 0;
         // ---- gate/up tiles: warps 0..NWG-1; warp 0 also arrives for the
@@ -721,10 +732,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             uint32_t xq[16];
             const float sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
             for (int it = 0; it < n_gu; ++it) {
-                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (warp_aborted(s_abort)) break;
+                if (!mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (warp_aborted(s_abort)) break;
                 if (tid == 0 && it == n_shared) GP_STAMP(3);
-                if (!*s_abort)
-                    consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
+                consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cnt(pdone0 + 8u * s, warp == 0 ? 1 + NWC - NWG : 1);
                 if (++s == S) { s = 0; ph ^= 1u; }
@@ -733,7 +745,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         } else {
             // once warp 0 has passed every gate/up stage, the first down
             // stage is at most one phase ahead of its parity wait
-            if (!mbar_wait_sleepy(gbar, 0, a.spin_limit) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (!mbar_wait_sleepy(gbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             s = n_gu % S;
             ph = (uint32_t)(n_gu / S) & 1u;
         }
@@ -742,9 +754,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         {
             const auto md = lane_map<II, NWC, PD>(warp, lane, stage0);
             for (int it = n_gu; it < n_items; ++it) {
-                if (!*s_abort && !mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (warp_aborted(s_abort)) break;
+                if (!mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (warp_aborted(s_abort)) break;
                 if (tid == 0 && it == n_gu) GP_STAMP(5);
-                if (!*s_abort) {
+                {
                     const uint32_t xb = stage0 + s * L.stage_bytes + DN_BYTES;
                     uint32_t xq[16];
 #pragma unroll
