@@ -17,9 +17,15 @@ tensor-core grouped GEMMs; with --ep and N >= 2 GPUs the experts are split over
 the GPUs with NCCL all-to-all dispatch and combine), --workload stack40 (config
 5 on one GPU: 40 layers, decode batches 1 to 256).
 
-N > 1 (launched by torchrun): every rank runs its own replica of the layer
-stack on its GPU (weak scaling, no data-path collective); value sums tokens
-over ranks and divides by the slowest rank's time.
+N > 1 (launched by torchrun): expert parallelism.  The same layer's 160
+routed experts are split 160/N per GPU (plus the shared expert on every GPU);
+each rank brings one token per step (weak scaling).  A step is an NCCL
+all-gather of the N tokens, one persistent kernel per rank that routes all N
+tokens and runs its experts' share of each plus its own token's shared expert
+(gpeed_moe_decode_partial), and an NCCL reduce-scatter that sums the partial
+outputs; all captured in CUDA graphs.  value = tokens over all ranks / the
+slowest rank's time.  The reference arm runs on rank 0 only, on every host
+core.
 """
 from __future__ import annotations
 
@@ -133,10 +139,18 @@ def tokens(n, seed):
     return torch.from_numpy(np.random.default_rng(seed).standard_normal((n, H)).astype(np.float32)).to(torch.bfloat16)
 
 
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_time_layer(kind: str, budget_s: float, max_tokens: int):
     """The reference CPU expert path (oracle/_ref, or the oracle port) on this host."""
     from oracle import oracle
     chk = oracle.Checker(kind)
+    chk.set_num_threads(host_cores())
     layer = host_layer(1000, 0, 0)
     shape = oracle.Shape(H, I, E, K_TOP, 2.5, 1, 10.0)
     X = tokens(max_tokens + 1, 7).float().numpy()
@@ -158,6 +172,7 @@ def run_reference(args, world):
     # capped at ~120 s of timed work
     budget = float(os.environ.get("GPEED_REF_BUDGET_S", "120"))
     chk = oracle.Checker(kind)
+    chk.set_num_threads(host_cores())  # torchrun starts ranks with OMP_NUM_THREADS=1
     layer = host_layer(1000, 0, 0)
     shape = oracle.Shape(H, I, E, K_TOP, 2.5, 1, 10.0)
     X = tokens(args.warmup + steps, 7).float().numpy()
@@ -352,6 +367,181 @@ def run_gpu(args, rank, local_rank, world):
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 4},
             "gpu_launches": (1 if fused else 5) * args.steps,
+            "clocks": clk.summary(),
+        }
+    del chains, e2e_graphs
+    ctx.close()
+    return line
+
+
+def run_gpu_ep(args, rank, local_rank, world):
+    """BASELINE config 2's layer, expert-parallel over `world` GPUs (the N > 1
+    default).  Rank r holds routed experts [r*E/N, (r+1)*E/N) of every layer
+    copy plus the shared expert and brings its own token each step.  A step
+    (one token per rank through one layer): NCCL all-gather of the N tokens,
+    gpeed_moe_decode_partial (one persistent kernel: routing of all N tokens,
+    this rank's experts' share of each, its own token's shared expert), NCCL
+    reduce-scatter of the partial outputs.  Layer copies rotate so each step's
+    weights come from HBM, and the steps are captured back to back in CUDA
+    graphs (collectives included)."""
+    import torch
+    import torch.distributed as dist
+
+    from gpeed_b200 import Context, MoeConfig, MoeLayer
+    from gpeed_b200.ep import ExpertParallelLayer
+
+    torch.cuda.set_device(local_rank)
+    ctx = Context(local_rank)
+    cfg = MoeConfig()
+    L = args.layers
+    lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+    layers = [MoeLayer(ctx, cfg, layer_id=l).synth_range(router_for(l), None, 1000 + l, 0, lo, cnt)
+              for l in range(L)]
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    xs = [tokens(1, 100 + l + 7919 * rank).cuda() for l in range(L)]  # this rank's token per layer copy
+    x_all = [torch.empty(world, H, dtype=torch.bfloat16, device="cuda") for _ in range(L)]
+    y_part = [torch.empty(world, H, device="cuda") for _ in range(L)]
+    ys = [torch.empty(1, H, device="cuda") for _ in range(L)]
+
+    def step(l, ev=None):
+        if ev:
+            ev[0].record(stream)
+        dist.all_gather_into_tensor(x_all[l], xs[l])
+        if ev:
+            ev[1].record(stream)
+        layers[l].decode_partial(x_all[l], rank, y_part[l], stream=stream)
+        if ev:
+            ev[2].record(stream)
+        dist.reduce_scatter_tensor(ys[l], y_part[l], op=dist.ReduceOp.SUM)
+        if ev:
+            ev[3].record(stream)
+
+    with torch.cuda.stream(stream):
+        for l in range(L):  # communicators, scratch and kernel attributes set up outside capture
+            step(l)
+    stream.synchronize()
+    ctx.check(stream)
+
+    def chain(n):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for l in range(n):
+                step(l)
+        return g
+
+    chains = {L: chain(L)}
+    if args.steps % L:
+        chains[args.steps % L] = chain(args.steps % L)
+
+    def run_steps(n):
+        for _ in range(n // L):
+            chains[L].replay()
+        if n % L:
+            if n % L not in chains:
+                chains[n % L] = chain(n % L)
+            chains[n % L].replay()
+
+    with torch.cuda.stream(stream):
+        run_steps(args.warmup)
+    stream.synchronize()
+    dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            run_steps(args.steps)
+            ev1.record(stream)
+        stream.synchronize()
+        ms_total = ev0.elapsed_time(ev1)
+        # the same work ~1.5 s more, so the sampler sees the clocks under load:
+        # the round count is agreed first (every rank runs the same collectives)
+        t = torch.tensor([ms_total], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+        n_soak = max(1, min(400, int(1500.0 / max(ms_max / args.steps * 25 * L, 1e-3))))
+        with torch.cuda.stream(stream):
+            for _ in range(n_soak):
+                run_steps(25 * L)
+        stream.synchronize()
+    dist.barrier()
+    ctx.check(stream)
+    value = world * args.steps / (ms_max / 1000.0)
+
+    # ---- per-phase split (events between the phases, eager launches) ----
+    n_prof = max(4 * L, 32)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n_prof)]
+    with torch.cuda.stream(stream):
+        for i in range(n_prof):
+            step(i % L, evs[i])
+    stream.synchronize()
+    ph = [sum(evs[i][k].elapsed_time(evs[i][k + 1]) for i in range(n_prof)) / n_prof for k in range(3)]
+    # routed slots this rank ran per layer copy (picks of all tokens in its range): the kernel's bytes
+    slots = []
+    for l in range(L):
+        ids = torch.empty(world, K_TOP, dtype=torch.int32, device="cuda")
+        layers[l].decode_partial(x_all[l], rank, torch.empty(world, H, device="cuda"), topk_ids=ids)
+        g = ids.cpu().numpy()
+        slots.append(int(((g >= lo) & (g < lo + cnt)).sum()))
+    torch.cuda.synchronize()
+    mean_slots = sum(slots) / L
+    kern_bytes = (mean_slots + 1) * EXPERT_BYTES + ROUTER_BYTES + world * H * (2 + 4)
+    achieved = kern_bytes / (ph[1] * 1e-3) / 1e9
+
+    # ---- end to end through the public API with host buffers ----
+    x_host = tokens(args.steps, 555 + rank).pin_memory()
+    y_host = torch.empty(H, dtype=torch.float32).pin_memory()
+    x_slot = x_host[0:1].clone().pin_memory()
+    e2e_graphs = []
+    for l in range(L):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            xs[l].copy_(x_slot, non_blocking=True)
+            step(l)
+            y_host.copy_(ys[l][0], non_blocking=True)
+        e2e_graphs.append(g)
+    for i in range(args.warmup):
+        with torch.cuda.stream(stream):
+            e2e_graphs[i % L].replay()
+        stream.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        x_slot.copy_(x_host[i:i + 1])       # the step's input lands in the pinned staging buffer
+        with torch.cuda.stream(stream):
+            e2e_graphs[i % L].replay()
+        stream.synchronize()                # the step's result is on the host
+    e2e_s = time.perf_counter() - t0
+    t = torch.tensor([e2e_s], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = world * args.steps / float(t.item())
+    ctx.check(stream)
+
+    hbm_peak, _, peak_src = peaks()
+    line = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "iq3_xxs(int8)xint16->f32", "data": "synthetic",
+            "config": {"workload": "decode1: MoE layer decode, batch 1 (BASELINE config 2)", "hidden": H,
+                       "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
+                       "layer_copies": L, "l2": f"inputs larger than L2: steps rotate over {L} layer copies",
+                       "parallelism": f"ep{world}: {cnt} routed experts per GPU + the shared expert; one token "
+                                      f"per GPU per step; NCCL all-gather of tokens, one persistent kernel per "
+                                      f"GPU, NCCL reduce-scatter of partial outputs",
+                       "phase_ms": {"all_gather": ph[0], "experts_kernel": ph[1], "reduce_scatter": ph[2]},
+                       "routed_slots_per_gpu_rank0": mean_slots,
+                       "per_gpu_kernel_hbm_gbs": achieved},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "traffic": None,
+                         "kernel": "decode_layer_kernel, expert-parallel share (rank 0): routing of all tokens, "
+                                   "its routed picks + own shared expert",
+                         "bytes_per_launch": kern_bytes, "peak_source": peak_src},
+            "cpu_baseline": None,
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 4},
+            "gpu_launches": args.steps,
             "clocks": clk.summary(),
         }
     del chains, e2e_graphs
@@ -1010,6 +1200,8 @@ def main():
     elif args.workload in ("codecs", "dense", "mhc"):
         fn = {"codecs": run_codecs, "dense": run_dense, "mhc": run_mhc}[args.workload]
         line = fn(args) if rank == 0 else None
+    elif world > 1:
+        line = run_gpu_ep(args, rank, local_rank, world)
     else:
         line = run_gpu(args, rank, local_rank, world)
     if world > 1:

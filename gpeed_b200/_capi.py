@@ -76,6 +76,7 @@ SIGNATURES = {
                                    _vp, _i],
     "gpeed_moe_synth_layer_range": [_vp, _i, ctypes.POINTER(MoeShape), _i, _i, _vp, _vp, _i, _u64, _u64],
     "gpeed_moe_route": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp],
+    "gpeed_moe_decode_partial": [_vp, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "gpeed_ep_pack": [_vp, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "gpeed_moe_experts": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp],
     "gpeed_moe_combine": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],

@@ -107,7 +107,7 @@ struct gpeed_ctx {
     int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
-    DevBuf<unsigned long long> logits, dx;
+    DevBuf<unsigned long long> logits, picks, dx;
     DevBuf<uint8_t> hq;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
@@ -445,6 +445,69 @@ int expert_pass(gpeed_ctx* c, const Layer& L, const void* x, int x_bf16, gp::Rou
     return GPEED_OK;
 }
 
+// Arguments of the persistent decode kernel (decode_layer.cu) for n_tok
+// tokens of layer L, with the context's exchange buffers sized (and their
+// tags zeroed) on first use.  Outside stream capture on first use.
+int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_tok, int own_tok, float* y,
+               const int* forced, int* topk_ids, float* topk_w, cudaStream_t st, gp::DecodeLayerArgs* out) {
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k;
+    int rc;
+    const size_t had = c->logits.n;
+    if ((rc = c->logits.ensure(gp::decode_layer_logit_words(E)))) return rc;
+    if (c->logits.n != had)  // tags must start below the first launch's
+        GP_CUDA(cudaMemsetAsync(c->logits.p, 0, c->logits.n * sizeof(unsigned long long), st));
+    const size_t had_p = c->picks.n;
+    if ((rc = c->picks.ensure(gp::decode_layer_pick_words()))) return rc;
+    if (c->picks.n != had_p) GP_CUDA(cudaMemsetAsync(c->picks.p, 0, c->picks.n * sizeof(unsigned long long), st));
+    const size_t had_dx = c->dx.n;
+    if ((rc = c->dx.ensure((size_t)gp::kDecodeSlots * H))) return rc;
+    if (c->dx.n != had_dx) GP_CUDA(cudaMemsetAsync(c->dx.p, 0, c->dx.n * sizeof(unsigned long long), st));
+    if ((rc = c->hq.ensure((size_t)gp::kDecodeSlots * gp::decode_layer_hq_bytes(I)))) return rc;
+    gp::DecodeLayerArgs& da = *out;
+    da = gp::DecodeLayerArgs{};
+    da.router = L.router;
+    da.corr = L.corr;
+    da.gate = L.gate;
+    da.up = L.up;
+    da.down = L.down;
+    da.gu_stride = L.gu_stride;
+    da.d_stride = L.d_stride;
+    da.H = H;
+    da.I = I;
+    da.E = E;
+    da.K = K;
+    da.routed_scale = s.routed_scale;
+    da.norm_topk = s.norm_topk;
+    da.limit = s.swiglu_limit;
+    da.with_shared = s.n_shared;
+    da.x = x;
+    da.x_bf16 = x_dtype == GPEED_DTYPE_BF16;
+    da.y = y;
+    da.forced = forced;
+    da.topk_ids = topk_ids;
+    da.topk_w = topk_w;
+    da.n_tok = n_tok;
+    da.e_lo = L.e_lo;
+    da.e_cnt = L.e_cnt;
+    da.own_tok = own_tok;
+    da.logits = c->logits.p;
+    da.picks = c->picks.p;
+    da.dx = c->dx.p;
+    da.h = c->h.p;
+    da.hq = c->hq.p;
+    da.D = c->D.p;
+    da.sync = c->sync;
+    da.tables = c->tables;
+    da.status = c->status;
+    da.stages = 3;  // the deepest stage ring that fits next to the tables
+    while (gp::decode_layer_smem(H, I, da.stages + 1, n_tok, n_tok * K) <= 227u * 1024u && da.stages < 8) ++da.stages;
+    da.cooperative = c->fused_cooperative;
+    da.spin_limit = c->spin_limit;
+    da.withhold_logit = c->withhold_logit;
+    return GPEED_OK;
+}
+
 // One gpeed_matmul_quant call (WeightStore::matmul_quant, weights.cpp:86-165):
 // the validated arguments and the GEMV geometry.  Both the allocating entry
 // point and gpeed_matmul_quant_noalloc run exactly this plan; they differ only
@@ -586,6 +649,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
     c->logits.release();
+    c->picks.release();
     c->xp.release();
     c->route_chunks.release();
     c->mhc_partial.release();
@@ -615,6 +679,7 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
         // tags restart together
         GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));
         if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
+        if (c->picks.p) GP_CUDA(cudaMemset(c->picks.p, 0, c->picks.n * sizeof(unsigned long long)));
         if (c->dx.p) GP_CUDA(cudaMemset(c->dx.p, 0, c->dx.n * sizeof(unsigned long long)));
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape, 16: a token or h value past the fp16 range "
@@ -850,49 +915,8 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     if (n <= c->fused_max_tokens && c->fused_decode && gp::decode_layer_supported(H, I, E, K, s.n_shared)) {
         // batch 1, and small batches one token at a time: each launch streams
         // only its token's experts, and consecutive launches overlap (PDL)
-        const size_t had = c->logits.n;
-        if ((rc = c->logits.ensure(gp::decode_layer_logit_words(E)))) return rc;
-        if (c->logits.n != had)  // tags must start below the first launch's
-            GP_CUDA(cudaMemsetAsync(c->logits.p, 0, c->logits.n * sizeof(unsigned long long), st));
-        const size_t had_dx = c->dx.n;
-        if ((rc = c->dx.ensure((size_t)(K + 1) * H))) return rc;
-        if (c->dx.n != had_dx) GP_CUDA(cudaMemsetAsync(c->dx.p, 0, c->dx.n * sizeof(unsigned long long), st));
-        if ((rc = c->hq.ensure((size_t)(K + 1) * gp::decode_layer_hq_bytes(I)))) return rc;
         gp::DecodeLayerArgs da{};
-        da.router = L.router;
-        da.corr = L.corr;
-        da.gate = L.gate;
-        da.up = L.up;
-        da.down = L.down;
-        da.gu_stride = L.gu_stride;
-        da.d_stride = L.d_stride;
-        da.H = H;
-        da.I = I;
-        da.E = E;
-        da.K = K;
-        da.routed_scale = s.routed_scale;
-        da.norm_topk = s.norm_topk;
-        da.limit = s.swiglu_limit;
-        da.with_shared = s.n_shared;
-        da.x = x;
-        da.x_bf16 = x_dtype == GPEED_DTYPE_BF16;
-        da.y = y;
-        da.forced = forced;
-        da.topk_ids = topk_ids;
-        da.topk_w = topk_w;
-        da.logits = c->logits.p;
-        da.dx = c->dx.p;
-        da.h = c->h.p;
-        da.hq = c->hq.p;
-        da.D = c->D.p;
-        da.sync = c->sync;
-        da.tables = c->tables;
-        da.status = c->status;
-        da.stages = 4;  // the deepest stage ring that fits next to the tables
-        while (gp::decode_layer_smem(H, I, da.stages + 1) <= 227u * 1024u && da.stages < 8) ++da.stages;
-        da.cooperative = c->fused_cooperative;
-        da.spin_limit = c->spin_limit;
-        da.withhold_logit = c->withhold_logit;
+        if ((rc = fused_args(c, L, x, x_dtype, 1, 0, y, forced, topk_ids, topk_w, st, &da))) return rc;
         // profiling: the one kernel's time goes to the gate/up slot, the other
         // stages read 0
         mark(2);
@@ -1003,6 +1027,37 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
 }
 
 // ---- expert parallelism (no counterpart in the reference) ----------------
+
+int gpeed_moe_decode_partial(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, int own_tok, float* y_part,
+                             const int* forced, int* topk_ids, float* topk_w, void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    const Layer& L = it->second;
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k;
+    if (n < 1 || n > gp::kDecodeMaxTokens || n * K > gp::kDecodeMaxRouted)
+        return fail(GPEED_ERR_INVALID, "n_tok %d: 1 .. %d tokens with n_tok * top_k <= %d", n, gp::kDecodeMaxTokens,
+                    gp::kDecodeMaxRouted);
+    if (own_tok < 0 || own_tok >= n) return fail(GPEED_ERR_INVALID, "own_tok %d not in [0, %d)", own_tok, n);
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (!x || !y_part || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y_part) & 15))
+        return fail(GPEED_ERR_INVALID, "x and y_part must be 16-byte aligned device pointers");
+    if (!gp::decode_layer_supported(H, I, E, K, s.n_shared))
+        return fail(GPEED_ERR_UNSUPPORTED, "no persistent decode kernel for hidden %d, inter %d, %d experts, top-%d, "
+                    "%d shared", H, I, E, K, s.n_shared);
+    if (n == 1 && L.e_cnt != E)
+        return fail(GPEED_ERR_INVALID, "one token needs every expert in the layer (use gpeed_moe_forward)");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    gp::DecodeLayerArgs da{};
+    if ((rc = fused_args(c, L, x, x_dtype, n, own_tok, y_part, forced, topk_ids, topk_w, st, &da))) return rc;
+    GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
+    return GPEED_OK;
+}
+
 
 int gpeed_moe_route(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, const int* forced, int* topk_ids,
                     float* topk_w, void* stream) {

@@ -12,28 +12,38 @@
 // path: no atomics are read back, and values other CTAs produced are read as
 // words tagged with the launch generation (the data is its own flag).
 //
+// The same kernel runs one rank's share of an expert-parallel decode step:
+// n_tok tokens (one per rank), the routed experts of one range, the shared
+// expert of the rank's own token.  Its slots are then the (token, expert)
+// picks that fall in the range, and it writes each token's partial output
+// (the ranks' parts sum to the layer).  One token with every expert is the
+// batch-1 layer, with the same arithmetic in the same order.
+//
 //   router   CTA c owns experts c, c+G, ...; 8 warps each compute one 1/8
-//            slice of an owned expert's fp32 logit (weights prefetched before
-//            the wait on the previous kernel); the epilogue warp adds the
-//            slices in order and stores the logit tagged with the launch
-//            generation, so readers poll the data itself
-//   top-k    every CTA's epilogue warp polls the E tagged logits (one of 8
-//            replicas, spread over L2 lines), applies
+//            slice of an owned expert's fp32 logit for every token (weights
+//            prefetched before the wait on the previous kernel); the
+//            epilogue warp adds the slices in order and stores the logit
+//            tagged with the launch generation, so readers poll the data itself
+//   top-k    one token: every CTA's epilogue warp polls the E tagged logits
+//            (one of 8 replicas, spread over L2 lines), applies
 //            sigmoid + bias and picks top-K by warp reductions (ties to the
-//            lower id), weights score/(1e-20 + sum)*scale (model.cpp:704-725)
+//            lower id), weights score/(1e-20 + sum)*scale (model.cpp:704-725).
+//            Several tokens: CTA t picks token t's experts and publishes the
+//            picks as tagged words that every CTA then reads.  The picks in
+//            the launch's expert range become its slots
 //   gate/up  units of 32 rows of h, dealt round-robin in slot order (the
-//            shared expert, storage slot K, first: it needs no routing; then
-//            routed slots 0..K-1); a unit is 4 consecutive tiles of 8 rows of
+//            shared expert first: it needs no routing; then the routed slots
+//            in pick order); a unit is 4 consecutive tiles of 8 rows of
 //            gate and up.  The epilogue applies SwiGLU with the reference clamp
 //            (model.cpp:733-739), quantises the finished unit to int16 (hq)
 //            and counts it for its slot: no value of h leaves the CTA
 //            unquantised and no counter is read back
-//   down     tiles of 32 rows x (K+1) slots, a contiguous range of (tile,
+//   down     tiles of 32 rows x all slots, a contiguous range of (tile,
 //            slot) positions per CTA sized to even out the total work; the
 //            producer copies each tile with its slot's hq once all units of
 //            that slot are counted (model.cpp:740).  The epilogue keeps a row
 //            tile's slot results in shared memory and writes y = sum_k w_k
-//            D[k] + D[shared] in top-k order (model.cpp:741-755); for a tile
+//            D[k] + D[shared] in top-k order per token (model.cpp:741-755); for a tile
 //            shared with the next CTAs it reads their slots as tagged words
 //
 // Waits on other CTAs need every CTA resident: one CTA per SM, launched either
@@ -78,7 +88,6 @@ constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
 constexpr int kLogitCopies = 8;
 constexpr int kLogitStride = 32;  // words
 static_assert(kLogitCopies * kLogitStride == 256, "decode_layer_logit_words (kernels.h) assumes 8 x 32");
-GP_DEVINL int logit_word(int copy, int e, int E) { return (copy * E + e) * kLogitStride; }
 static_assert(TRD == 32, "the combine maps one row of a down tile to each epilogue lane");
 
 
@@ -201,31 +210,47 @@ GP_DEVINL float load_quant(const void* x, int x_bf16, int64_t row, int in_dim, i
     return 0.25f * quant_i16<32>(v, xq);
 }
 
-// Epilogue warp: sigmoid scores from the gathered logits, top-K by score +
-// bias (ties to the lower id), weights score/(1e-20 + sum)*scale
-// (model.cpp:704-725); publishes them to the CTA.  Each lane sorts its EJ
-// candidates (expert ids lane + 32j) by (key desc, id asc); a round then takes
-// the warp maximum of the lanes' head keys (redux), the lowest id holding it,
-// and that lane pops its head.
+// Sentinel slot id of the shared expert in work items (its storage index is
+// kSharedStore; its position among a down tile's values is the routed count).
+constexpr int kShared = -1;
+constexpr int kSharedStore = kDecodeMaxRouted;
+GP_DEVINL int slot_store(int slot) { return slot < 0 ? kSharedStore : slot; }
+
+// Tagged logit of token `tok`, expert e: one token is read by every CTA and
+// kept in kLogitCopies replicas (copy = reader's CTA % kLogitCopies); with
+// several tokens only CTA t reads token t's, one copy (copy 0).
+GP_DEVINL int64_t logit_word(int copy, int tok, int e, int E) {
+    return ((int64_t)(copy + tok) * E + e) * kLogitStride;
+}
+// Tagged top-k pick k of token t (several tokens), kLogitCopies replicas.
+GP_DEVINL int64_t pick_word(int copy, int tok, int k) {
+    return ((int64_t)(copy * kDecodeMaxTokens + tok) * 32 + k) * kLogitStride;
+}
+
+// One token's top-K by score + bias (ties to the lower id), weights
+// score/(1e-20 + sum)*scale (model.cpp:704-725), or the forced ids with their
+// weights.  The E logits are polled as words tagged by their writers with this
+// launch's tag: the data is its own flag, so one poll round trip suffices.
+// Each lane sorts its EJ candidates (expert ids lane + 32j) by (key desc, id
+// asc); a round then takes the warp maximum of the lanes' head keys (redux),
+// the lowest id holding it, and that lane pops its head.  Lane k < K returns
+// pick k in (my_e, my_w).  Returns false when the wait for the logits ran out.
 template <int EJ>
-GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t tag, int lane, int c, int* s_ids,
-                         float* s_w, uint32_t topk_bar, volatile uint32_t* s_abort) {
+GP_DEVINL bool topk_token(const DecodeLayerArgs& a, const float* bias, uint32_t tag, int lane, int copy, int tok,
+                          bool write_out, int& my_e, float& my_w) {
     const int E = a.E, K = a.K;
-    // every CTA's logits, each word tagged by its writer with this launch's
-    // tag: the data is its own flag, so one poll round trip suffices
     unsigned long long w[EJ];
     uint32_t n = 0;
     for (; n < a.spin_limit; ++n) {
 #pragma unroll
         for (int j = 0; j < EJ; ++j)
-            w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + logit_word(c % kLogitCopies, lane + 32 * j, E)) : 0ull;
+            w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + logit_word(copy, tok, lane + 32 * j, E)) : 0ull;
         bool ok = true;
 #pragma unroll
         for (int j = 0; j < EJ; ++j) ok &= lane + 32 * j >= E || (uint32_t)(w[j] >> 32) == tag;
         if (__all_sync(0xffffffffu, ok)) break;
         __nanosleep(TOPK_POLL_NS);
     }
-    if (n == a.spin_limit && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
     if (lane == 0) GP_STAMP(11);
     float score[EJ];
     uint32_t key[EJ], id[EJ];
@@ -239,10 +264,11 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t t
     }
     if (lane == 0) GP_STAMP(13);
     float denom = 1e-20f, my_s = 0.f;
-    int my_e = 0;
+    my_e = 0;
     if (a.forced) {
+        const int* forced = a.forced + (int64_t)tok * K;
         for (int k = 0; k < K; ++k) {
-            int eb = a.forced[k];
+            int eb = forced[k];
             if (eb < 0 || eb >= E) {
                 if (lane == 0) atomicOr(a.status, GP_DEV_BAD_EXPERT);
                 eb = 0;
@@ -290,15 +316,43 @@ GP_DEVINL void topk_warp(const DecodeLayerArgs& a, const float* bias, uint32_t t
             if (lane == k) { my_s = sc; my_e = (int)eb; }
         }
     }
-    if (lane < K) {
-        const float w = a.norm_topk ? (my_s / denom) * a.routed_scale : my_s * a.routed_scale;
-        s_ids[lane] = my_e;
-        s_w[lane] = w;
-        if (c == 0 && a.topk_ids) a.topk_ids[lane] = my_e;
-        if (c == 0 && a.topk_w) a.topk_w[lane] = w;
+    my_w = a.norm_topk ? (my_s / denom) * a.routed_scale : my_s * a.routed_scale;
+    if (write_out && a.topk_ids && lane < K) a.topk_ids[(int64_t)tok * K + lane] = my_e;
+    if (write_out && a.topk_w && lane < K) a.topk_w[(int64_t)tok * K + lane] = my_w;
+    return n < a.spin_limit;
+}
+
+// Slot list of a launch from the picks of its tokens: pair p = t*K + k (lane
+// p, and lane p - 32 for p >= 32) holds pick (e, w) of token t.  The picks
+// whose expert lies in [e_lo, e_lo + e_cnt) become routed slots in p order:
+// s_se = local expert, s_st = token, s_sw = weight; s_first[t] = first slot
+// of token t (s_first[n_tok] = routed slot count, also in s_nsr).
+GP_DEVINL void build_slots(const DecodeLayerArgs& a, int lane, int e0, float w0, int e1, float w1, int* s_nsr,
+                           int* s_first, int* s_se, int* s_st, float* s_sw) {
+    const int np = a.n_tok * a.K;
+    const bool in0 = lane < np && e0 >= a.e_lo && e0 < a.e_lo + a.e_cnt;
+    const bool in1 = lane + 32 < np && e1 >= a.e_lo && e1 < a.e_lo + a.e_cnt;
+    const uint32_t b0 = __ballot_sync(0xffffffffu, in0), b1 = __ballot_sync(0xffffffffu, in1);
+    const uint32_t below = (1u << lane) - 1u;
+    if (in0) {
+        const int p = __popc(b0 & below);
+        s_se[p] = e0 - a.e_lo;
+        s_st[p] = lane / a.K;
+        s_sw[p] = w0;
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(topk_bar);  // release: the producer reads s_ids
+    if (in1) {
+        const int p = __popc(b0) + __popc(b1 & below);
+        s_se[p] = e1 - a.e_lo;
+        s_st[p] = (lane + 32) / a.K;
+        s_sw[p] = w1;
+    }
+    if (lane <= a.n_tok) {  // slots before token `lane`: in-range pairs p < lane*K
+        const int lim = lane * a.K;
+        const int c0 = lim >= 32 ? __popc(b0) : __popc(b0 & ((1u << lim) - 1u));
+        const int c1 = lim >= 64 ? __popc(b1) : lim > 32 ? __popc(b1 & ((1u << (lim - 32)) - 1u)) : 0;
+        s_first[lane] = c0 + c1;
+    }
+    if (lane == 0) *s_nsr = __popc(b0) + __popc(b1);
 }
 
 // Per-stage partial sums: one per (row of the tile, covering warp).
@@ -310,7 +364,11 @@ struct Smem {
     uint32_t stage_bytes, stages_off, partial_off, bar_off, misc_off, total;
 };
 
-__host__ __device__ inline Smem decode_smem(int H, int I, int S) {
+// misc block: abort flag (16 B), routed-slot count + first slot per token (16
+// ints), slot -> local expert / token / weight (3 x kDecodeMaxRouted words),
+// router slices [kMaxOwned * RSPLIT][n_tok], one down row tile's values per
+// slot [max_routed + 1][32].
+__host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok, int max_routed) {
     Smem L;
     const uint32_t gu = 2u * TRG * 98u * (H / 256);
     const uint32_t dn = TRD * 98u * (I / 256) + (uint32_t)I * 2u + (uint32_t)(I / UNIT) * 4u;
@@ -320,38 +378,37 @@ __host__ __device__ inline Smem decode_smem(int H, int I, int S) {
     const uint32_t pb = kPartialFloats * 4u;
     L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
     L.misc_off = L.bar_off + (3u * S + 4u) * 8u;
-    // abort flag, s_ids[32], s_w[32], router slices[kMaxOwned * RSPLIT],
-    // one down row tile's per-slot values [MAXK + 1][32]
-    L.total = L.misc_off + 16u + 8u * 32u + 4u * kMaxOwned * RSPLIT + 4u * (MAXK + 1) * 32u;
+    L.total = L.misc_off + 16u + 64u + 12u * kDecodeMaxRouted + 4u * kMaxOwned * RSPLIT * n_tok +
+              128u * (uint32_t)(max_routed + 1);
     return L;
 }
 
-// Work item i of a phase in slot order: the shared expert (storage slot K)
-// first, then routed slots 0..K-1; `per_slot` items each.
+// Work item i of a phase in slot order: the shared expert first (it needs no
+// routing), then routed slots 0..nsr-1; `per_slot` items each.
 struct Item {
-    int slot, idx;
+    int slot, idx;  // slot kShared: the shared expert
 };
-GP_DEVINL Item item_of(int i, int per_slot, int K) {
-    if (i < per_slot) return {K, i};
+GP_DEVINL Item item_of(int i, int per_slot) {
+    if (i < per_slot) return {kShared, i};
     const int r = i - per_slot, slot = r / per_slot;
     return {slot, r - slot * per_slot};
 }
 // Items i = c, c+G, c+2G, ... below total.
 GP_DEVINL int items_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
 
-// Down work: positions v = tile*(K+1) + q over (row tile, slot position q);
-// position q = K is the shared expert (ready first), q < K routed slot K-1-q
-// (slot 0 at q = K-1 is ready next, slot K-1 at q = 0 last).  CTA c owns the
-// range [v0, v1), sized so that its down work plus its routed gate/up units
-// is the same for every CTA (weights: one unit ~ wu, one down position ~ wd).
-// The range is walked as: the leading partial tile, the first whole tile,
-// the trailing partial tile, the other whole tiles; each tile in descending
-// q.  Partial tiles thus meet the early-ready slots first, the tiles shared
-// with a neighbour CTA are settled early, and the CTA ends on a whole tile
-// it combines by itself.
-GP_DEVINL int down_slot(int q, int K) { return q == K ? K : K - 1 - q; }
+// Down work: positions v = tile*(nsr+1) + q over (row tile, slot position q);
+// position q = nsr is the shared expert (ready first), q < nsr routed slot
+// nsr-1-q (slot 0 at q = nsr-1 is ready next, slot nsr-1 at q = 0 last).  CTA
+// c owns the range [v0, v1), sized so that its down work plus its routed
+// gate/up units is the same for every CTA (weights: one unit ~ wu, one down
+// position ~ wd).  The range is walked as: the leading partial tile, the
+// first whole tile, the trailing partial tile, the other whole tiles; each
+// tile in descending q.  Partial tiles thus meet the early-ready slots first,
+// the tiles shared with a neighbour CTA are settled early, and the CTA ends
+// on a whole tile it combines by itself.
+GP_DEVINL int down_slot(int q, int nsr) { return q == nsr ? kShared : nsr - 1 - q; }
 struct DownRange {
-    int v0, v1, b, e, P;  // range, first / last tile boundary inside it, K+1
+    int v0, v1, b, e, P;  // range, first / last tile boundary inside it, nsr+1
     GP_DEVINL int count() const { return v1 - v0; }
     GP_DEVINL int at(int i) const {
         const int lead_end = b < v1 ? b : v1;
@@ -400,6 +457,21 @@ GP_DEVINL DownRange down_range(int c, int G, int n_tiles, int P, int units, int 
     return r;
 }
 
+// A CTA's share of the work once the routed slot count nsr is known.
+struct Work {
+    int nsr, n_gu, n_items;
+    DownRange R;
+};
+GP_DEVINL Work work_of(int c, int G, int nsr, int NU, int TD) {
+    Work w;
+    w.nsr = nsr < 0 ? 0 : nsr > kDecodeMaxRouted ? kDecodeMaxRouted : nsr;
+    const int nsl = w.nsr + 1;
+    w.n_gu = TPU * items_of(c, G, NU * nsl);
+    w.R = down_range(c, G, TD, nsl, NU * nsl, NU);
+    w.n_items = w.n_gu + w.R.count();
+    return w;
+}
+
 // Quantises the unit of h held one value per lane exactly as a lane quantises
 // its activations for the GEMV (quant_i16<32>, scale * 1/4), into hq.  hq
 // layout: 4 planes of NU 16-byte chunks (plane i holds words 4i..4i+3 of every
@@ -428,28 +500,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     constexpr int TD = H / TRD, NU = I / UNIT;
     constexpr uint32_t GU_BYTES = TRG * 98u * (H / 256), DN_BYTES = TRD * 98u * (I / 256);
     constexpr uint32_t HQ_BYTES = I * 2u + NU * 4u;
-    static_assert(MAXK + 1 <= kDecodeSyncWords - kSyncSlot, "counter block too small");
     static_assert(UNIT % TRG == 0 && HQ_BYTES % 16 == 0 && DN_BYTES % 16 == 0 && GU_BYTES % 16 == 0,
                   "bulk copies need 16-byte sizes and offsets");
-    const int E = a.E, K = a.K, S = a.stages;
-    const Smem L = decode_smem(H, I, S);
+    const int E = a.E, K = a.K, S = a.stages, NT = a.n_tok;
+    const Smem L = decode_smem(H, I, S, NT, NT * K);
     const uint32_t sbase = smem_u32(smem);
     // per stage: full (producer -> compute warps), pdone (compute warps ->
     // epilogue warp: partial sums written), empty (epilogue -> producer)
     const uint32_t full0 = sbase + L.bar_off, pdone0 = full0 + 8u * S, empty0 = pdone0 + 8u * S;
     const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u, gbar = rbar + 8u;
     volatile uint32_t* s_abort = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off);
-    int* s_ids = reinterpret_cast<int*>(smem + L.misc_off + 16u);
-    float* s_w = reinterpret_cast<float*>(s_ids + 32);
-    float* s_slice = s_w + 32;
-    float* s_dv = s_slice + kMaxOwned * RSPLIT;
+    int* s_nsr = reinterpret_cast<int*>(smem + L.misc_off + 16u);
+    int* s_first = s_nsr + 1;                       // [n_tok + 1]
+    int* s_se = s_nsr + 16;                         // [kDecodeMaxRouted] local expert of a slot
+    int* s_st = s_se + kDecodeMaxRouted;            // token of a slot
+    float* s_sw = reinterpret_cast<float*>(s_st + kDecodeMaxRouted);  // weight of a slot
+    float* s_slice = s_sw + kDecodeMaxRouted;       // [task][n_tok] router slices
+    float* s_dv = s_slice + kMaxOwned * RSPLIT * NT;  // [slot position][32] one down row tile
     float* partial = reinterpret_cast<float*>(smem + L.partial_off);
     constexpr uint32_t pstride = kPartialFloats;
     const uint32_t stage0 = sbase + L.stages_off;
-    const int n_gu = TPU * items_of(c, G, NU * (K + 1));
     const int n_shared = TPU * items_of(c, G, NU);  // leading gate/up tiles that need no routing
-    const DownRange R = down_range(c, G, TD, K + 1, NU * (K + 1), NU);
-    const int n_items = n_gu + R.count();
     const int n_own = items_of(c, G, E);            // router experts c, c+G, ...
     const int n_tasks = n_own * RSPLIT;
 
@@ -480,32 +551,53 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             for (int k4 = 0; k4 < 4; ++k4) bulk_g2s(sbase + k4 * 16384u, a.tables + k4 * 16384, 16384u, tbar);
         }
         int s = 0, issued = 0;
-        uint32_t ph = 1, ready = 0;
-        bool have_topk = false;
-        for (int it = 0; it < n_items; ++it) {
+        uint32_t ph = 1;
+        uint32_t ready[3] = {0u, 0u, 0u};  // storage slots whose h units are all counted
+        bool have = false;
+        Work w{};
+        for (int it = 0;; ++it) {
             if (__shfl_sync(0xffffffffu, *s_abort, 0)) break;
+            if (!have && it >= n_shared) {  // routed tiles need the slot list (every lane reads it)
+                const bool ok = mbar_wait(topk_bar, 0, a.spin_limit);
+                if (!ok) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                if (!__all_sync(0xffffffffu, ok)) break;
+                if (lane == 0) GP_STAMP(10);
+                w = work_of(c, G, *s_nsr, NU, TD);
+                have = true;
+            }
+            if (have && it >= w.n_items) break;
             int slot;
             uint32_t off, b0, b1;
-            const uint8_t *src0, *src1;
-            if (it < n_gu) {
-                const Item u = item_of(c + (it / TPU) * G, NU, K);
+            const bool gu = it < (have ? w.n_gu : n_shared);
+            if (gu) {
+                const Item u = item_of(c + (it / TPU) * G, NU);
                 slot = u.slot;
                 off = (uint32_t)(u.idx * TPU + it % TPU) * GU_BYTES;
                 b0 = b1 = GU_BYTES;
             } else {
-                const int v = R.at(it - n_gu);
-                slot = down_slot(v % (K + 1), K);
-                off = (uint32_t)(v / (K + 1)) * DN_BYTES;
+                const int v = w.R.at(it - w.n_gu), nsl = w.nsr + 1;
+                slot = down_slot(v % nsl, w.nsr);
+                off = (uint32_t)(v / nsl) * DN_BYTES;
                 b0 = DN_BYTES;
                 b1 = HQ_BYTES;
                 // the tile travels with its slot's quantised h: wait (warp-wide
-                // poll of every slot's counter) until all its units are counted
-                if (!((ready >> slot) & 1u)) {
+                // poll of the slots' counters) until all its units are counted
+                const int st = slot_store(slot);
+                auto is_ready = [&]() {  // bit st of the three ready words (no dynamic register index)
+                    const uint32_t rw = st < 32 ? ready[0] : st < 64 ? ready[1] : ready[2];
+                    return ((rw >> (st & 31)) & 1u) != 0u;
+                };
+                if (!is_ready()) {
                     uint32_t n = 0;
                     for (; n < a.spin_limit; ++n) {
-                        const unsigned cnt = lane <= K ? ld_relaxed(a.sync + kSyncSlot + lane) : 0u;
-                        ready = __ballot_sync(0xffffffffu, lane <= K && cnt >= (unsigned)NU);
-                        if ((ready >> slot) & 1u) break;
+#pragma unroll
+                        for (int j = 0; j < 3; ++j) {
+                            const int q = lane + 32 * j;
+                            const bool valid = q < w.nsr || q == kSharedStore;
+                            const unsigned cnt = valid ? ld_relaxed(a.sync + kSyncSlot + q) : 0u;
+                            ready[j] = __ballot_sync(0xffffffffu, valid && cnt >= (unsigned)NU);
+                        }
+                        if (is_ready()) break;
                         __nanosleep(64);
                     }
                     if (n == a.spin_limit) {
@@ -517,46 +609,40 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     // slot seen ready stays ready, so one fence per poll
                     fence_acq_rel_gpu();
                     fence_proxy_async_global();
-                    if (lane == 0 && it == n_gu) GP_STAMP(12);
+                    if (lane == 0 && it == w.n_gu) GP_STAMP(12);
                 }
             }
             if (lane == 0) {
-                bool ok = true;
-                if (it >= n_shared && !have_topk) {  // routed tiles need the top-k
-                    ok = have_topk = mbar_wait(topk_bar, 0, a.spin_limit);
-                    if (ok) GP_STAMP(10);
-                    else { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                const int e = slot < 0 ? a.e_cnt : s_se[slot];  // local expert index
+                const uint8_t *src0, *src1;
+                if (gu) {
+                    const int64_t eo = (int64_t)e * a.gu_stride + off;
+                    src0 = a.gate + eo;
+                    src1 = a.up + eo;
+                } else {
+                    src0 = a.down + (int64_t)e * a.d_stride + off;
+                    src1 = a.hq + (int64_t)slot_store(slot) * HQ_BYTES;
                 }
-                if (ok) {
-                    const int e = slot < K ? s_ids[slot] : E;
-                    if (it < n_gu) {
-                        const int64_t eo = (int64_t)e * a.gu_stride + off;
-                        src0 = a.gate + eo;
-                        src1 = a.up + eo;
-                    } else {
-                        src0 = a.down + (int64_t)e * a.d_stride + off;
-                        src1 = a.hq + (int64_t)slot * HQ_BYTES;
-                    }
-                    if (!mbar_wait(empty0 + 8u * s, ph, a.spin_limit)) {
-                        *s_abort = 1;
-                        atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
-                    } else {
-                        const uint32_t dst = stage0 + s * L.stage_bytes;
-                        mbar_arrive_expect_tx(full0 + 8u * s, b0 + b1);
-                        bulk_g2s(dst, src0, b0, full0 + 8u * s);
-                        bulk_g2s(dst + b0, src1, b1, full0 + 8u * s);
-                        ++issued;
-                        if (++s == S) { s = 0; ph ^= 1u; }
-                    }
+                if (!mbar_wait(empty0 + 8u * s, ph, a.spin_limit)) {
+                    *s_abort = 1;
+                    atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
+                } else {
+                    const uint32_t dst = stage0 + s * L.stage_bytes;
+                    mbar_arrive_expect_tx(full0 + 8u * s, b0 + b1);
+                    bulk_g2s(dst, src0, b0, full0 + 8u * s);
+                    bulk_g2s(dst + b0, src1, b1, full0 + 8u * s);
+                    ++issued;
+                    if (++s == S) { s = 0; ph ^= 1u; }
                 }
             }
             __syncwarp();
         }
         if (lane == 0) {
-            // no copy may still be in flight when the CTA exits
+            // no copy may still be in flight when the CTA exits (the
+            // compile-time limit, whatever the run-time one)
             for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
-                mbar_wait(full0 + 8u * (i % S), (uint32_t)(i / S) & 1u);  // the compile-time limit,
-            mbar_wait(tbar, 0);                                           // whatever the run-time one
+                mbar_wait(full0 + 8u * (i % S), (uint32_t)(i / S) & 1u);
+            mbar_wait(tbar, 0);
         }
         return;
     }
@@ -572,22 +658,73 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         if (n_tasks > 0) {  // this CTA's experts: slices added in order
             if (!mbar_wait(rbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (lane < n_own) {
-                float lg = 0.f;
+                const int e = c + lane * G;
+                for (int t = 0; t < NT; ++t) {
+                    float lg = 0.f;
 #pragma unroll
-                for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[lane * RSPLIT + sl];
-                const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(lg);
-                if (c + lane * G != a.withhold_logit) {  // (a test withholds one to make the top-k wait run out)
+                    for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[(lane * RSPLIT + sl) * NT + t];
+                    const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(lg);
+                    if (e == a.withhold_logit) continue;  // (a test withholds one to make the top-k wait run out)
+                    if (NT == 1) {
 #pragma unroll
-                    for (int cp = 0; cp < kLogitCopies; ++cp)
-                        st_relaxed64(a.logits + logit_word(cp, c + lane * G, E), v);
+                        for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.logits + logit_word(cp, 0, e, E), v);
+                    } else {
+                        st_relaxed64(a.logits + logit_word(0, t, e, E), v);
+                    }
                 }
             }
         }
         if (lane == 0) GP_STAMP(1);
-        if (E <= 160) topk_warp<5>(a, bias, tag, lane, c, s_ids, s_w, topk_bar, s_abort);
-        else topk_warp<kMaxEFused / 32>(a, bias, tag, lane, c, s_ids, s_w, topk_bar, s_abort);
+        int e0 = 0, e1 = 0;
+        float w0 = 0.f, w1 = 0.f;
+        bool ok = true;
+        if (NT == 1) {  // every CTA picks the token's experts itself
+            ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0)
+                          : topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0);
+        } else {
+            // CTA t picks token t's experts and publishes them; every CTA
+            // then reads all tokens' picks (one more exchange, no CTA sorts
+            // n_tok tokens in turn)
+            if (c < NT) {
+                int me = 0;
+                float mw = 0.f;
+                ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, 0, c, true, me, mw)
+                              : topk_token<EJ>(a, bias, tag, lane, 0, c, true, me, mw);
+                if (lane < K) {
+                    const unsigned long long v = ((unsigned long long)(tag & 0xFFFFu) << 48) |
+                                                 ((unsigned long long)(me & 0xFFFF) << 32) | __float_as_uint(mw);
+#pragma unroll
+                    for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.picks + pick_word(cp, c, lane), v);
+                }
+            }
+            const int np = NT * K;
+            unsigned long long p0 = 0ull, p1 = 0ull;
+            uint32_t n = 0;
+            for (; n < a.spin_limit && ok; ++n) {
+                p0 = lane < np ? ld_relaxed64(a.picks + pick_word(c % kLogitCopies, lane / K, lane % K)) : 0ull;
+                p1 = lane + 32 < np ? ld_relaxed64(a.picks + pick_word(c % kLogitCopies, (lane + 32) / K, (lane + 32) % K))
+                                    : 0ull;
+                const bool got = (lane >= np || (uint32_t)(p0 >> 48) == (tag & 0xFFFFu)) &&
+                                 (lane + 32 >= np || (uint32_t)(p1 >> 48) == (tag & 0xFFFFu));
+                if (__all_sync(0xffffffffu, got)) break;
+                __nanosleep(TOPK_POLL_NS);
+            }
+            if (n == a.spin_limit) ok = false;
+            e0 = (int)((p0 >> 32) & 0xFFFFu);
+            w0 = __uint_as_float((uint32_t)p0);
+            e1 = (int)((p1 >> 32) & 0xFFFFu);
+            w1 = __uint_as_float((uint32_t)p1);
+        }
+        if (!ok && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+        // (after a timeout the slot list is built from whatever was read: the
+        // ids stay in range, the results are invalid and the status says so)
+        build_slots(a, lane, e0, w0, e1, w1, s_nsr, s_first, s_se, s_st, s_sw);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(topk_bar);  // release: the other roles read the slot list
         if (lane == 0) GP_STAMP(2);
 
+        const Work w = work_of(c, G, *s_nsr, NU, TD);
+        const int nsr = w.nsr;
         int s = 0;
         uint32_t ph = 0;
         constexpr int rsg = 32 * NWG / (H / 32), rsd = 32 * NWC / (I / 32);
@@ -595,8 +732,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         // After an abort every warp leaves its loop at once (and arrives on no
         // further barrier), so no barrier phase sees arrivals from two
         // iterations; every wait left behind in another warp is bounded.
-        for (int it = 0; it < n_items; ++it) {
-            const bool gu = it < n_gu;
+        for (int it = 0; it < w.n_items; ++it) {
+            const bool gu = it < w.n_gu;
             if (warp_aborted(s_abort)) break;
             if (!mbar_wait(pdone0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (warp_aborted(s_abort)) break;
@@ -609,15 +746,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     const int ng = LG::last_warp(row % rsg) - LG::first_warp(row % rsg);
                     const int nu = LG::last_warp(ur % rsg) - LG::first_warp(ur % rsg);
                     float gs = 0.f, us = 0.f;
-                    for (int w = 0; w <= ng; ++w) gs += pbuf[row * LG::WPR + w];
-                    for (int w = 0; w <= nu; ++w) us += pbuf[ur * LG::WPR + w];
+                    for (int ww = 0; ww <= ng; ++ww) gs += pbuf[row * LG::WPR + ww];
+                    for (int ww = 0; ww <= nu; ++ww) us += pbuf[ur * LG::WPR + ww];
                     val = silu_clamped(gs, us, a.limit);
                 }
             } else {
                 using LD = LaneMap<II, NWC, PD>;
                 const int r0 = lane % rsd;
                 const int nw = LD::last_warp(r0) - LD::first_warp(r0);
-                for (int w = 0; w <= nw; ++w) val += pbuf[lane * LD::WPR + w];
+                for (int ww = 0; ww <= nw; ++ww) val += pbuf[lane * LD::WPR + ww];
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(empty0 + 8u * s);  // partials read: the stage may refill
@@ -628,52 +765,63 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 const float v = __shfl_sync(0xffffffffu, val, lane & (TRG - 1));
                 if ((lane / TRG) == j) hv = v;
                 if (j == TPU - 1) {
-                    const Item u = item_of(c + (it / TPU) * G, NU, K);
-                    quantise_unit(hv, a.hq + (int64_t)u.slot * HQ_BYTES, I, u.idx, lane);
+                    const Item u = item_of(c + (it / TPU) * G, NU);
+                    const int st = slot_store(u.slot);
+                    quantise_unit(hv, a.hq + (int64_t)st * HQ_BYTES, I, u.idx, lane);
                     __syncwarp();
-                    if (lane == 0) red_release_add(a.sync + kSyncSlot + u.slot, 1);
+                    if (lane == 0) red_release_add(a.sync + kSyncSlot + st, 1);
                 }
             } else {
-                const int v = R.at(it - n_gu), t = v / (K + 1);
-                const int slot = down_slot(v % (K + 1), K);
-                const int j = t * TRD + lane;
-                const int tb = t * (K + 1), te = tb + K + 1;
-                if (tb >= R.v0) {
+                const int nsl = nsr + 1;
+                const int v = w.R.at(it - w.n_gu), rt = v / nsl;
+                const int slot = down_slot(v % nsl, nsr);
+                const int j = rt * TRD + lane;
+                const int tb = rt * nsl, te = tb + nsl;
+                if (tb >= w.R.v0) {
                     // this CTA holds the tile's last walked position (q = 0): it
                     // writes y, with the slots other CTAs computed (positions
                     // [v1, te), walked early by them) read as tagged words
-                    s_dv[slot * 32 + lane] = val;
+                    s_dv[(slot < 0 ? nsr : slot) * 32 + lane] = val;
                     if (v == tb) {
-                        if (te > R.v1) {
+                        if (te > w.R.v1) {
                             uint32_t n = 0;
                             for (; n < a.spin_limit; ++n) {
-                                bool ok = true;
-                                for (int base = R.v1; base < te; base += 8) {  // 8 loads in flight
-                                    unsigned long long w[8];
+                                bool got = true;
+                                for (int base = w.R.v1; base < te; base += 8) {  // 8 loads in flight
+                                    unsigned long long wd[8];
 #pragma unroll
                                     for (int i = 0; i < 8; ++i)
-                                        w[i] = base + i < te ? ld_relaxed64(a.dx + (int64_t)down_slot(base + i - tb, K) * H + j)
-                                                             : (unsigned long long)tag << 32;
+                                        wd[i] = base + i < te ? ld_relaxed64(a.dx + (int64_t)slot_store(down_slot(base + i - tb, nsr)) * H + j)
+                                                              : (unsigned long long)tag << 32;
 #pragma unroll
                                     for (int i = 0; i < 8; ++i) {
-                                        ok &= (uint32_t)(w[i] >> 32) == tag;
-                                        if (base + i < te) s_dv[down_slot(base + i - tb, K) * 32 + lane] = __uint_as_float((uint32_t)w[i]);
+                                        got &= (uint32_t)(wd[i] >> 32) == tag;
+                                        if (base + i < te) {
+                                            const int sl = down_slot(base + i - tb, nsr);
+                                            s_dv[(sl < 0 ? nsr : sl) * 32 + lane] = __uint_as_float((uint32_t)wd[i]);
+                                        }
                                     }
                                 }
-                                if (__all_sync(0xffffffffu, ok)) break;
+                                if (__all_sync(0xffffffffu, got)) break;
                                 __nanosleep(64);
                             }
                             if (n == a.spin_limit && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                         }
                         __syncwarp();
-                        float y = 0.f;
-                        for (int k = 0; k < K; ++k) y = fmaf(s_w[k], s_dv[k * 32 + lane], y);
-                        a.y[j] = y + s_dv[K * 32 + lane];
+                        // y[t] = sum over t's slots of w * D in pick order
+                        // (+ the shared expert for own_tok), model.cpp:741-755
+                        for (int t = 0; t < NT; ++t) {
+                            float y = 0.f;
+                            for (int k = s_first[t]; k < s_first[t + 1]; ++k) y = fmaf(s_sw[k], s_dv[k * 32 + lane], y);
+                            if (t == a.own_tok) y += s_dv[nsr * 32 + lane];
+                            a.y[(int64_t)t * H + j] = y;
+                        }
                         __syncwarp();
                     }
                 } else {
                     // the CTA before this one finishes the tile
-                    st_relaxed64(a.dx + (int64_t)slot * H + j, ((unsigned long long)tag << 32) | __float_as_uint(val));
+                    st_relaxed64(a.dx + (int64_t)slot_store(slot) * H + j,
+                                 ((unsigned long long)tag << 32) | __float_as_uint(val));
                 }
             }
         }
@@ -686,52 +834,74 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         static_assert(H % (RSPLIT * 128) == 0 && RV <= 8, "router slices are whole float4 columns");
         float4 wv[RV];
         auto load_router = [&](int task) {
-            const float* w = a.router + (int64_t)(c + (task / RSPLIT) * G) * H + (task % RSPLIT) * RSL + lane * 4;
+            const float* wr = a.router + (int64_t)(c + (task / RSPLIT) * G) * H + (task % RSPLIT) * RSL + lane * 4;
 #pragma unroll
-            for (int i = 0; i < RV; ++i) wv[i] = __ldg(reinterpret_cast<const float4*>(w + i * 128));
+            for (int i = 0; i < RV; ++i) wv[i] = __ldg(reinterpret_cast<const float4*>(wr + i * 128));
         };
         if (warp < n_tasks) load_router(warp);
         pdl_wait();
         if (tid == 0) GP_STAMP(0);
 
-        // ---- router slices of this CTA's experts: warp task = (expert, slice) ----
+        // ---- router slices of this CTA's experts: warp task = (expert, slice),
+        // one dot product per token ----
         for (int task = warp; task < n_tasks; task += NWC) {
             if (task != warp) load_router(task);
             const int sl = task % RSPLIT;
-            float acc = 0.f;
+            for (int t = 0; t < NT; ++t) {
+                float acc = 0.f;
 #pragma unroll
-            for (int i = 0; i < RV; ++i) {
-                const int k0 = sl * RSL + lane * 4 + i * 128;
-                float4 xv;
-                if (a.x_bf16) {
-                    const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + k0);
-                    xv = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
-                                     __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
-                } else {
-                    xv = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + k0);
+                for (int i = 0; i < RV; ++i) {
+                    const int64_t k0 = (int64_t)t * H + sl * RSL + lane * 4 + i * 128;
+                    float4 xv;
+                    if (a.x_bf16) {
+                        const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + k0);
+                        xv = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
+                                         __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
+                    } else {
+                        xv = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + k0);
+                    }
+                    acc = fmaf(wv[i].x, xv.x, acc);
+                    acc = fmaf(wv[i].y, xv.y, acc);
+                    acc = fmaf(wv[i].z, xv.z, acc);
+                    acc = fmaf(wv[i].w, xv.w, acc);
                 }
-                acc = fmaf(wv[i].x, xv.x, acc);
-                acc = fmaf(wv[i].y, xv.y, acc);
-                acc = fmaf(wv[i].z, xv.z, acc);
-                acc = fmaf(wv[i].w, xv.w, acc);
+                acc = warp_sum(acc);
+                if (lane == 0) s_slice[task * NT + t] = acc;
             }
-            acc = warp_sum(acc);
-            if (lane == 0) {
-                s_slice[task] = acc;
-                mbar_arrive(rbar);
-            }
+            if (lane == 0) mbar_arrive(rbar);
         }
 
         if (!mbar_wait(tbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         int s = 0;
         uint32_t ph = 0;
+        bool have = false;
+        Work w{};
+        // the slot list (routed slot count, slot tokens) once the top-k is in
+        auto wait_slots = [&]() -> bool {
+            if (!mbar_wait(topk_bar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+            if (warp_aborted(s_abort)) return false;
+            w = work_of(c, G, *s_nsr, NU, TD);
+            have = true;
+            return true;
+        };
         // ---- gate/up tiles: warps 0..NWG-1; warp 0 also arrives for the
         // others, which sleep until the down phase ----
         if (warp < NWG) {
             const auto mg = lane_map<HH, NWG, PG>(warp, lane, stage0);
             uint32_t xq[16];
-            const float sx4 = load_quant(a.x, a.x_bf16, 0, H, mg.sb, xq);
-            for (int it = 0; it < n_gu; ++it) {
+            int cur = a.own_tok;  // the token whose activations xq holds (the shared expert's first)
+            float sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
+            for (int it = 0;; ++it) {
+                if (!have && it >= n_shared && !wait_slots()) break;
+                if (have && it >= w.n_gu) break;
+                if (it % TPU == 0 && NT > 1) {  // a new unit: its slot's token
+                    const Item u = item_of(c + (it / TPU) * G, NU);
+                    const int tk = u.slot < 0 ? a.own_tok : s_st[u.slot];
+                    if (tk != cur) {
+                        cur = tk;
+                        sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
+                    }
+                }
                 if (warp_aborted(s_abort)) break;
                 if (!mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 if (warp_aborted(s_abort)) break;
@@ -746,33 +916,32 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             // once warp 0 has passed every gate/up stage, the first down
             // stage is at most one phase ahead of its parity wait
             if (!mbar_wait_sleepy(gbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            s = n_gu % S;
-            ph = (uint32_t)(n_gu / S) & 1u;
+            if (wait_slots()) {
+                s = w.n_gu % S;
+                ph = (uint32_t)(w.n_gu / S) & 1u;
+            }
         }
         if (tid == 0) GP_STAMP(4);
         // ---- down tiles: the activations come with the tile ----
-        {
+        if (have) {
             const auto md = lane_map<II, NWC, PD>(warp, lane, stage0);
-            for (int it = n_gu; it < n_items; ++it) {
+            for (int it = w.n_gu; it < w.n_items; ++it) {
                 if (warp_aborted(s_abort)) break;
                 if (!mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 if (warp_aborted(s_abort)) break;
-                if (tid == 0 && it == n_gu) GP_STAMP(5);
-                {
-                    const uint32_t xb = stage0 + s * L.stage_bytes + DN_BYTES;
-                    uint32_t xq[16];
+                if (tid == 0 && it == w.n_gu) GP_STAMP(5);
+                const uint32_t xb = stage0 + s * L.stage_bytes + DN_BYTES;
+                uint32_t xq[16];
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const uint4 v = lds128(xb + i * (NU * 16u) + md.sb * 16u);
-                        xq[4 * i] = v.x;
-                        xq[4 * i + 1] = v.y;
-                        xq[4 * i + 2] = v.z;
-                        xq[4 * i + 3] = v.w;
-                    }
-                    const float sx4 = ldsf(xb + 2u * I + md.sb * 4u);
-                    consume<II, NWC, PD, RPWD>(md, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp,
-                                               lane);
+                for (int i = 0; i < 4; ++i) {
+                    const uint4 v = lds128(xb + i * (NU * 16u) + md.sb * 16u);
+                    xq[4 * i] = v.x;
+                    xq[4 * i + 1] = v.y;
+                    xq[4 * i + 2] = v.z;
+                    xq[4 * i + 3] = v.w;
                 }
+                const float sx4 = ldsf(xb + 2u * I + md.sb * 4u);
+                consume<II, NWC, PD, RPWD>(md, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(pdone0 + 8u * s);
                 if (++s == S) { s = 0; ph ^= 1u; }
@@ -788,7 +957,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         fence_acq_rel_gpu();
         if (atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1) {
             a.sync[kSyncGen] += 1u;
-            for (int k = 0; k <= K; ++k) a.sync[kSyncSlot + k] = 0;
+            const int nsr = min(max(*s_nsr, 0), kDecodeMaxRouted);
+            for (int k = 0; k < nsr; ++k) a.sync[kSyncSlot + k] = 0;
+            a.sync[kSyncSlot + kSharedStore] = 0;
             fence_acq_rel_gpu();
             a.sync[kSyncEnd] = 0;
         }
@@ -805,15 +976,23 @@ bool decode_layer_supported(int H, int I, int E, int K, int with_shared) {
     return H == 5120 && I == 1536 && K >= 1 && K <= MAXK && with_shared == 1;
 }
 
-size_t decode_layer_smem(int H, int I, int stages) { return decode_smem(H, I, stages).total; }
+size_t decode_layer_smem(int H, int I, int stages, int n_tok, int max_routed) {
+    return decode_smem(H, I, stages, n_tok, max_routed).total;
+}
 
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st) {
     if (!decode_layer_supported(a.H, a.I, a.E, a.K, a.with_shared)) return cudaErrorInvalidValue;
     if (grid * kMaxOwned < a.E) return cudaErrorInvalidValue;  // router experts per CTA
-    // down-range weights in 32-bit: grid * (units * 42 + tiles * 10) < 2^31
-    if ((int64_t)grid * ((int64_t)(a.I / UNIT) * (a.K + 1) * 42 + (int64_t)(a.H / TRD) * (a.K + 1) * 10) >= (1ll << 31))
+    if (a.n_tok < 1 || a.n_tok > kDecodeMaxTokens || a.n_tok * a.K > kDecodeMaxRouted || a.own_tok < 0 ||
+        a.own_tok >= a.n_tok || a.e_lo < 0 || a.e_cnt < 0 || a.e_lo + a.e_cnt > a.E || a.E >= 65536 ||
+        (a.n_tok > 1 && !a.picks))
         return cudaErrorInvalidValue;
-    const Smem L = decode_smem(a.H, a.I, a.stages);
+    if (a.n_tok == 1 && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // one token: every expert
+    // down-range weights in 32-bit: grid * (units * 42 + tiles * 10) < 2^31
+    const int64_t slots = (int64_t)a.n_tok * a.K + 1;
+    if ((int64_t)grid * ((int64_t)(a.I / UNIT) * slots * 42 + (int64_t)(a.H / TRD) * slots * 10) >= (1ll << 31))
+        return cudaErrorInvalidValue;
+    const Smem L = decode_smem(a.H, a.I, a.stages, a.n_tok, a.n_tok * a.K);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
     auto kern = decode_layer_kernel<5120, 1536, 4, 1, 2, 2>;
     static std::atomic<unsigned long long> configured{0};  // per device

@@ -166,17 +166,27 @@ struct DecodeLayerArgs {
     int norm_topk;
     float limit;
     int with_shared;
-    const void* x;             // [H] bf16 or fp32
+    const void* x;             // [n_tok][H] bf16 or fp32
     int x_bf16;
-    float* y;                  // [H]
-    const int* forced;         // [K] or nullptr
-    int* topk_ids;             // [K] or nullptr
-    float* topk_w;             // [K] or nullptr
+    float* y;                  // [n_tok][H]: the layer output (all experts held), else this range's part
+    const int* forced;         // [n_tok][K] or nullptr
+    int* topk_ids;             // [n_tok][K] or nullptr
+    float* topk_w;             // [n_tok][K] or nullptr
+    // Tokens and experts of one launch.  One token with every expert is the
+    // batch-1 layer (Model::moe_forward).  Several tokens with an expert range
+    // is one rank's share of an expert-parallel decode step: the (token, k)
+    // picks whose expert lies in [e_lo, e_lo + e_cnt) plus the shared expert
+    // of token own_tok, y[t] = that part of token t's output (zero rows for
+    // tokens with nothing here); the ranks' parts sum to the layer output.
+    int n_tok;                 // 1 .. kDecodeMaxTokens
+    int e_lo, e_cnt;           // routed experts held (gate/up/down index e - e_lo; the shared expert at e_cnt)
+    int own_tok;               // token whose shared expert runs in this launch
     unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
-    float* h;                  // [K+1][I]
-    uint8_t* hq;               // [K+1][decode_layer_hq_bytes(I)] h quantised per 32-unit
-    float* D;                  // [K+1][H] (multi-kernel path)
-    unsigned long long* dx;    // [K+1][H] down rows of tiles split between CTAs, tagged like logits
+    unsigned long long* picks;   // [decode_layer_pick_words()] top-k picks of each token, tagged (n_tok > 1)
+    float* h;                  // unused (multi-kernel path scratch)
+    uint8_t* hq;               // [kDecodeSlots][decode_layer_hq_bytes(I)] h quantised per 32-unit
+    float* D;                  // unused (multi-kernel path scratch)
+    unsigned long long* dx;    // [kDecodeSlots][H] down rows of tiles split between CTAs, tagged like logits
     unsigned* sync;            // [kDecodeSyncWords] counters, zero between launches
     const uint8_t* tables;
     uint32_t* status;
@@ -221,14 +231,24 @@ cudaError_t launch_ep_pack(const void* x, int x_bf16, int H, int n, int K, const
 // tagged buffers) after a launch that reported an error.
 constexpr int kSyncGen = 0;                     // launch generation (tags exchanged logits and rows)
 constexpr int kSyncEnd = 1;                     // CTAs finished
-constexpr int kSyncSlot = 8;                    // [K+1] h units quantised per slot
-constexpr int kDecodeSyncWords = 64;
+constexpr int kSyncSlot = 8;                    // [kDecodeSlots] h units quantised per slot
+constexpr int kDecodeMaxTokens = 8;             // tokens per launch of the persistent kernel
+constexpr int kDecodeMaxRouted = 64;            // routed (token, expert) slots per launch
+constexpr int kDecodeSlots = kDecodeMaxRouted + 1;  // + the shared expert's, stored last
+constexpr int kDecodeSyncWords = 128;
+static_assert(kSyncSlot + kDecodeSlots <= kDecodeSyncWords, "slot counters past the counter block");
 // h[slot] as int16 pairs (I*2 bytes) followed by one fp32 scale per 32-unit.
 inline size_t decode_layer_hq_bytes(int I) { return (size_t)I * 2 + (size_t)(I / 32) * 4; }
-// Words of DecodeLayerArgs::logits: 8 replicas of E tagged logits, one word per 256-byte line.
+// Words of DecodeLayerArgs::logits, one word per 256-byte line: 8 replicas of
+// E tagged logits (one token: every CTA reads them), or one copy per token
+// (several tokens: one CTA reads each token's).
 inline size_t decode_layer_logit_words(int E) { return (size_t)8 * E * 32; }
+// Words of DecodeLayerArgs::picks: 8 replicas x kDecodeMaxTokens x 32 picks, one per 256-byte line.
+inline size_t decode_layer_pick_words() { return (size_t)8 * kDecodeMaxTokens * 32 * 32; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
-size_t decode_layer_smem(int H, int I, int stages);
+// Dynamic shared memory of a launch: `stages` pipeline stages, n_tok tokens
+// and at most max_routed routed slots.
+size_t decode_layer_smem(int H, int I, int stages, int n_tok, int max_routed);
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st);
 
 // ---- codecs.cu: the other GGUF codecs (quant.cpp:130-573), bit-exact ----

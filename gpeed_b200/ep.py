@@ -26,15 +26,9 @@ import torch.distributed as dist
 
 from . import _capi
 from ._capi import GpeedError, call
-from .moe import Context, MoeConfig, _ptr, _stream
+from .moe import Context, MoeConfig, MoeLayer, _dtype_code, _ptr, _stream
 
 
-def _dtype_code(t: torch.Tensor) -> int:
-    if t.dtype == torch.bfloat16:
-        return _capi.DTYPE_BF16
-    if t.dtype == torch.float32:
-        return _capi.DTYPE_F32
-    raise GpeedError(_capi.ERR_UNSUPPORTED, f"dtype {t.dtype}")
 
 
 class CudaExecutor:
@@ -90,6 +84,14 @@ class CudaExecutor:
         call("gpeed_moe_experts", self.ctx.handle, self.layer_id, _ptr(rows), _dtype_code(rows), rows.shape[0],
              _ptr(ids), _ptr(out), _stream(None))
         return out
+
+    def decode_partial(self, x_all: torch.Tensor, own_tok: int, y_part: torch.Tensor | None = None,
+                       stream=None) -> torch.Tensor:
+        if y_part is None:
+            y_part = self.empty((x_all.shape[0], self.cfg.hidden), torch.float32)
+        call("gpeed_moe_decode_partial", self.ctx.handle, self.layer_id, _ptr(x_all), _dtype_code(x_all),
+             x_all.shape[0], own_tok, _ptr(y_part), None, None, None, _stream(stream))
+        return y_part
 
     def combine(self, d_rows, slot_of, w, d_shared) -> torch.Tensor:
         n, K = slot_of.shape
@@ -156,3 +158,91 @@ class ExpertParallelLayer:
             return ex.empty((0, cfg.hidden), torch.float32)
         d_shared = d_all[r:] if cfg.n_shared else None
         return ex.combine(d_back, slot_of, w, d_shared)
+
+
+class StepGuard:
+    """Host-side check that every rank reached the same step before any of its
+    device work is launched.  Each rank posts "step i" to a shared key-value
+    store (torch.distributed's TCPStore) and waits up to `timeout_s` for the
+    others' posts; a rank that left between steps (or never joined) turns the
+    next step into a GpeedError on the others instead of a collective that
+    waits on a missing peer.  Off the device's critical path: use it between
+    graph replays in a serving loop, not inside a captured graph."""
+
+    def __init__(self, store, rank: int, world: int, timeout_s: float = 10.0, prefix: str = "gpeed/ep"):
+        self.store, self.rank, self.world = store, rank, world
+        self.timeout_s, self.prefix = timeout_s, prefix
+        self.step = 0
+
+    def __call__(self) -> None:
+        import datetime
+        key = lambda r: f"{self.prefix}/{self.step}/{r}"
+        self.store.set(key(self.rank), "1")
+        try:
+            self.store.wait([key(r) for r in range(self.world)], datetime.timedelta(seconds=self.timeout_s))
+        except Exception as e:  # the store raises on timeout (RuntimeError / DistStoreError)
+            missing = [r for r in range(self.world) if not self.store.check([key(r)])]
+            raise GpeedError(_capi.ERR_NCCL, f"expert parallelism: rank(s) {missing} did not reach step "
+                                             f"{self.step} within {self.timeout_s:.1f} s ({e})") from None
+        self.step += 1
+
+
+class ExpertParallelDecode:
+    """Expert-parallel decode of one MoE layer, one token per rank per step.
+
+    The layer's routed experts are split over the ranks (each executor holds
+    one contiguous range plus the shared expert).  A step:
+      1. all-gather the ranks' tokens                       collective (10 KB each)
+      2. every rank runs gpeed_moe_decode_partial: routing of all tokens, its
+         experts' share of each token and its own token's shared expert, in
+         one persistent kernel                                device
+      3. reduce-scatter the partial outputs (sum over ranks)  collective
+    No step reads anything back to the host, so steps can be captured in a
+    CUDA graph.  With NCCL the collectives are all_gather_into_tensor and
+    reduce_scatter_tensor; gloo (CPU tests) has no reduce-scatter and uses
+    all_reduce plus the own row.  An optional StepGuard checks on the host,
+    before a step's work is launched, that every rank is still there."""
+
+    def __init__(self, cfg: MoeConfig, executor, group=None, guard: StepGuard | None = None):
+        self.cfg, self.ex, self.group, self.guard = cfg, executor, group, guard
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if cfg.n_experts % self.world:
+            raise GpeedError(_capi.ERR_INVALID, f"{cfg.n_experts} experts do not split over {self.world} ranks")
+        if self.world * cfg.top_k > 64 or self.world > 8:
+            raise GpeedError(_capi.ERR_UNSUPPORTED, f"{self.world} ranks x top-{cfg.top_k}: at most 8 ranks and 64 "
+                                                    f"picks per step")
+        self._nccl = dist.get_backend(group) == "nccl"
+        self._bufs = {}
+
+    def _buf(self, name, shape, dtype):
+        b = self._bufs.get(name)
+        if b is None or b.shape != shape or b.dtype != dtype:
+            b = self.ex.empty(shape, dtype)
+            self._bufs[name] = b
+        return b
+
+    def forward(self, x: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
+        """x [1, H] (this rank's token) -> y [1, H] fp32."""
+        H, P = self.cfg.hidden, self.world
+        if self.guard is not None:
+            self.guard()
+        x = x.reshape(1, H)
+        x_all = self._buf("x_all", (P, H), x.dtype)
+        y_part = self._buf("y_part", (P, H), torch.float32)
+        if y is None:
+            y = self.ex.empty((1, H), torch.float32)
+        try:
+            if self._nccl:
+                dist.all_gather_into_tensor(x_all, x.contiguous(), group=self.group)
+            else:
+                dist.all_gather(list(x_all.unbind(0)), x.reshape(H).contiguous(), group=self.group)
+            self.ex.decode_partial(x_all, self.rank, y_part)
+            if self._nccl:
+                dist.reduce_scatter_tensor(y, y_part, op=dist.ReduceOp.SUM, group=self.group)
+            else:
+                dist.all_reduce(y_part, op=dist.ReduceOp.SUM, group=self.group)
+                y.copy_(y_part[self.rank:self.rank + 1])
+        except RuntimeError as e:  # a collective that failed or timed out (a peer left)
+            raise GpeedError(_capi.ERR_NCCL, f"expert-parallel decode step failed: {e}") from e
+        return y

@@ -33,6 +33,14 @@ def _ptr(t) -> ctypes.c_void_p | None:
     return ctypes.c_void_p(t.data_ptr())
 
 
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _capi.DTYPE_BF16
+    if t.dtype == torch.float32:
+        return _capi.DTYPE_F32
+    raise GpeedError(_capi.ERR_UNSUPPORTED, f"dtype {t.dtype}")
+
+
 def _stream(stream) -> ctypes.c_void_p:
     s = stream if stream is not None else torch.cuda.current_stream()
     return ctypes.c_void_p(s.cuda_stream)
@@ -227,6 +235,31 @@ class MoeLayer:
         call("gpeed_moe_synth_layer", self.ctx.handle, self.layer_id, ctypes.byref(self._shape), _ptr(router),
              _ptr(corr_c), 0, ctypes.c_uint64(seed), ctypes.c_uint64(stream0))
         return self
+
+    def synth_range(self, router: np.ndarray, corr: np.ndarray | None, seed: int, stream0: int, expert_begin: int,
+                    expert_count: int) -> "MoeLayer":
+        """Only routed experts [expert_begin, expert_begin + expert_count) plus the
+        shared expert, with the bytes of that slice of the whole synthetic layer
+        (expert parallelism: one rank's share)."""
+        router = np.ascontiguousarray(router, np.float32)
+        corr_c = None if corr is None else np.ascontiguousarray(corr, np.float32)
+        call("gpeed_moe_synth_layer_range", self.ctx.handle, self.layer_id, ctypes.byref(self._shape), expert_begin,
+             expert_count, _ptr(router), _ptr(corr_c), 0, ctypes.c_uint64(seed), ctypes.c_uint64(stream0))
+        return self
+
+    def decode_partial(self, x_all: torch.Tensor, own_tok: int, y_part: torch.Tensor | None = None,
+                       forced_topk: torch.Tensor | None = None, topk_ids: torch.Tensor | None = None,
+                       topk_w: torch.Tensor | None = None, stream=None) -> torch.Tensor:
+        """One rank's share of an expert-parallel decode step (gpeed_moe_decode_partial):
+        x_all [n, H] every rank's token -> y_part [n, H] fp32, the part of each
+        token's output that this layer's experts (plus own_tok's shared expert)
+        contribute.  The ranks' parts sum to MoeLayer.forward of the whole layer."""
+        n = x_all.shape[0]
+        if y_part is None:
+            y_part = torch.empty(n, self.cfg.hidden, dtype=torch.float32, device=x_all.device)
+        call("gpeed_moe_decode_partial", self.ctx.handle, self.layer_id, _ptr(x_all), _dtype_code(x_all), n, own_tok,
+             _ptr(y_part), _ptr(forced_topk), _ptr(topk_ids), _ptr(topk_w), _stream(stream))
+        return y_part
 
     def forward(self, x: torch.Tensor, y: torch.Tensor | None = None, forced_topk: torch.Tensor | None = None,
                 topk_ids: torch.Tensor | None = None, topk_w: torch.Tensor | None = None, stream=None):

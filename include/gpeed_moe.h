@@ -222,6 +222,23 @@ GPEED_API int gpeed_moe_forward(gpeed_ctx* ctx, int layer, const void* x_dev, in
  * With the same weights every rank's y is bit-identical to gpeed_moe_forward
  * on one GPU for n_tok > 1 (the batched path). */
 
+/* Expert-parallel decode, one rank's share in one persistent kernel (the
+ * batch-1 kernel of gpeed_moe_forward generalised): x holds every rank's token
+ * ([n_tok][H], n_tok <= 8 and n_tok * top_k <= 64, identical on all ranks,
+ * e.g. from an all-gather), own_tok is this rank's.  The kernel routes all
+ * n_tok tokens, runs gate/up -> SwiGLU -> down for the (token, k) picks whose
+ * expert the layer holds (gpeed_moe_load_layer_range) plus the shared expert
+ * of own_tok, and writes y_part[t] = sum of w_k D_k over those picks of token
+ * t, in pick order, (+ D_shared for own_tok): zero rows for tokens with
+ * nothing here.  Summed over the ranks (a reduce-scatter), y_part gives
+ * gpeed_moe_forward's y up to the order of that sum.  forced_topk / topk_ids /
+ * topk_w are [n_tok][K] as in gpeed_moe_forward.  No counterpart in the
+ * reference (Model::moe_forward, model.cpp:692-756, runs every expert on one
+ * host). */
+GPEED_API int gpeed_moe_decode_partial(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, int n_tok,
+                                       int own_tok, float* y_part_dev, const int* forced_topk_dev, int* topk_ids_dev,
+                                       float* topk_w_dev, void* stream);
+
 /* Loads only routed experts [expert_begin, expert_begin + expert_count) (their
  * GGUF bytes at gate/up/down) plus the shared expert; the router stays whole. */
 GPEED_API int gpeed_moe_load_layer_range(gpeed_ctx* ctx, int layer, const gpeed_moe_shape* shape, int expert_begin,

@@ -31,6 +31,12 @@ int orc_num_threads(void) {
 #endif
 }
 
+/* Host threads the OpenMP loops use from here on (torchrun starts its ranks
+ * with OMP_NUM_THREADS=1; the CPU baseline wants every core). */
+void orc_set_num_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+
 /* quant.cpp:130-154: IEEE half -> float including subnormals. */
 float orc_f16_to_f32(uint16_t h) {
     const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;

@@ -65,6 +65,7 @@ int orc_moe_batch(const orc_shape* s, const float* router_w, const float* corr,
 /* Host twin of the device synthetic generator (gpeed_b200/csrc/synth.h). */
 void orc_synth_iq3xxs(uint64_t seed, uint64_t stream, uint64_t block0, uint64_t nblocks, uint8_t* dst);
 int orc_num_threads(void);
+void orc_set_num_threads(int n);
 
 #ifdef __cplusplus
 }

@@ -74,6 +74,10 @@ class Checker:
     def num_threads(self) -> int:
         return self._f("num_threads")()
 
+    def set_num_threads(self, n: int) -> None:
+        """OpenMP threads of the checker's loops from now on."""
+        self._f("set_num_threads")(int(n))
+
     def dequantize(self, blocks: np.ndarray) -> np.ndarray:
         blocks = np.ascontiguousarray(blocks, np.uint8).reshape(-1)
         n = blocks.size // 98 * 256

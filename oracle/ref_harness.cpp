@@ -92,6 +92,11 @@ int ref_num_threads(void) {
 #endif
 }
 
+// Host threads the reference's OpenMP loops use from here on (see oracle.c).
+void ref_set_num_threads(int n) {
+    if (n > 0) omp_set_num_threads(n);
+}
+
 int ref_dequantize_iq3xxs(const uint8_t* src, float* dst, uint64_t n) {
     try {
         dequantize(DType::IQ3_XXS, src, dst, n);

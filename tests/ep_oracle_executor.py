@@ -64,3 +64,26 @@ class OracleExecutor:
         if d_shared is not None:
             y = (y + d_shared.numpy()).astype(np.float32)
         return torch.from_numpy(y)
+
+    def decode_partial(self, x_all, own_tok, y_part=None):
+        """gpeed_moe_decode_partial on the oracle: every token's routing, then
+        this rank's share: w_k * D_k over the picks whose expert it holds, in
+        pick order, plus the shared expert of own_tok."""
+        ids, w = self.route(x_all)
+        ids, w = ids.numpy(), w.numpy()
+        n, K = ids.shape
+        out = np.zeros((n, self.cfg.hidden), np.float32)
+        for t in range(n):
+            for k in range(K):
+                e = int(ids[t, k])
+                if self.lo <= e < self.lo + self.cnt:
+                    d = self.experts(x_all[t:t + 1], torch.tensor([e], dtype=torch.int32)).numpy()[0]
+                    out[t] = (out[t] + np.float32(w[t, k]) * d).astype(np.float32)
+            if t == own_tok:
+                d = self.experts(x_all[t:t + 1], torch.tensor([self.cfg.n_experts], dtype=torch.int32)).numpy()[0]
+                out[t] = (out[t] + d).astype(np.float32)
+        y = torch.from_numpy(out)
+        if y_part is not None:
+            y_part.copy_(y)
+            return y_part
+        return y

@@ -159,3 +159,146 @@ def test_ep_nccl_two_gpus(tmp_path):
         assert p.exitcode == 0
     y = np.concatenate([np.load(os.path.join(str(tmp_path), f"y_{r}.npy")) for r in range(2)])
     assert rel_l2(y, y_ref) < 1e-6
+
+
+# ---- expert-parallel decode: one token per rank, one persistent kernel per rank ----
+
+def _ep_layers(ctx, cfg, world, base_id):
+    router = _router(cfg)
+    full = MoeLayer(ctx, cfg, layer_id=base_id).synth(router, None, SEED, S0)
+    parts = []
+    for r in range(world):
+        lo, cnt = ExpertParallelLayer.expert_range(cfg, r, world)
+        parts.append(MoeLayer(ctx, cfg, layer_id=base_id + 1 + r).synth_range(router, None, SEED, S0, lo, cnt))
+    return full, parts
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decode_partial_emulated_ranks(port, world):
+    """gpeed_moe_decode_partial for each rank of an emulated `world`-rank step
+    (the ranks' launches run one after another on one GPU: nothing waits across
+    launches).  Routing is bit-identical to the batch-1 forward of each token;
+    the sum of the ranks' parts matches it up to the order of that sum, and the
+    oracle at the layer bar; tokens with no pick on a rank get exact zeros."""
+    from oracle import oracle
+    ctx = Context(0)
+    try:
+        cfg = MoeConfig()
+        full, parts = _ep_layers(ctx, cfg, world, 500 + 20 * world)
+        X = torch.from_numpy(np.random.default_rng(world).standard_normal((world, cfg.hidden)).astype(np.float32)).to(
+            torch.bfloat16).cuda()
+        K = cfg.top_k
+        y_ref = torch.empty(world, cfg.hidden, device="cuda")
+        ids_ref = torch.empty(world, K, dtype=torch.int32, device="cuda")
+        w_ref = torch.empty(world, K, dtype=torch.float32, device="cuda")
+        for t in range(world):
+            full.forward(X[t:t + 1], y_ref[t:t + 1], topk_ids=ids_ref[t:t + 1], topk_w=w_ref[t:t + 1])
+        y_parts = []
+        for r in range(world):
+            ids = torch.full((world, K), -1, dtype=torch.int32, device="cuda")
+            w = torch.zeros(world, K, device="cuda")
+            y_parts.append(parts[r].decode_partial(X, r, topk_ids=ids, topk_w=w))
+            ctx.check()
+            np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref.cpu().numpy())
+            np.testing.assert_array_equal(w.cpu().numpy(), w_ref.cpu().numpy())
+        y_ep = torch.stack(y_parts).sum(0).cpu().numpy()
+        g = ids_ref.cpu().numpy()
+        epr = cfg.n_experts // world
+        for r in range(world):
+            yp = y_parts[r].cpu().numpy()
+            for t in range(world):
+                if t != r and not ((g[t] >= r * epr) & (g[t] < (r + 1) * epr)).any():
+                    assert not yp[t].any()
+        for t in range(world):
+            assert rel_l2(y_ep[t], y_ref.cpu().numpy()[t]) < 1e-5
+        host = {**{n: oracle.synth_iq3xxs(SEED, S0 + m, c) for m, (n, c) in enumerate(
+            [("gate", cfg.n_experts * cfg.inter * cfg.hidden // 256), ("up", cfg.n_experts * cfg.inter * cfg.hidden // 256),
+             ("down", cfg.n_experts * cfg.hidden * cfg.inter // 256), ("gate_sh", cfg.inter * cfg.hidden // 256),
+             ("up_sh", cfg.inter * cfg.hidden // 256), ("down_sh", cfg.hidden * cfg.inter // 256)])},
+                "router": _router(cfg), "corr": np.zeros(cfg.n_experts, np.float32)}
+        shape = oracle.Shape(cfg.hidden, cfg.inter, cfg.n_experts, K, cfg.routed_scale, int(cfg.norm_topk),
+                             cfg.swiglu_limit)
+        for t in (0, world - 1):
+            y_o, _, _ = port.moe_forward(shape, host, X[t].float().cpu().numpy(), forced=g[t])
+            assert rel_l2(y_ep[t], y_o) < 1e-3
+    finally:
+        ctx.close()
+
+
+def test_decode_partial_crowded_rank_and_limits():
+    """Every pick of 8 tokens forced onto one rank's experts: that rank runs the
+    most slots a launch takes (64 routed + its shared expert), the others only
+    their shared expert.  Also the single-token form (every expert held) equals
+    gpeed_moe_forward bit for bit, and out-of-range arguments are refused."""
+    from gpeed_b200 import GpeedError
+    ctx = Context(0)
+    try:
+        cfg = MoeConfig()
+        world, K = 8, cfg.top_k
+        full, parts = _ep_layers(ctx, cfg, world, 700)
+        X = torch.from_numpy(np.random.default_rng(3).standard_normal((world, cfg.hidden)).astype(np.float32)).to(
+            torch.bfloat16).cuda()
+        forced = torch.tensor([[(t + k) % 20 + 40 for k in range(K)] for t in range(world)], dtype=torch.int32,
+                              device="cuda")  # experts 40..59: rank 2 of 8
+        y_ref = torch.empty(world, cfg.hidden, device="cuda")
+        for t in range(world):
+            full.forward(X[t:t + 1], y_ref[t:t + 1], forced_topk=forced[t:t + 1])
+        y_ep = sum(parts[r].decode_partial(X, r, forced_topk=forced) for r in range(world))
+        ctx.check()
+        assert rel_l2(y_ep.cpu().numpy(), y_ref.cpu().numpy()) < 1e-5
+        one = full.decode_partial(X[:1], 0)
+        ctx.check()
+        np.testing.assert_array_equal(one.cpu().numpy(), full.forward(X[:1]).cpu().numpy())
+        with pytest.raises(GpeedError):
+            parts[0].decode_partial(torch.zeros(9, cfg.hidden, dtype=torch.bfloat16, device="cuda"), 0)
+        with pytest.raises(GpeedError):
+            parts[0].decode_partial(X, world)
+        with pytest.raises(GpeedError):
+            parts[0].decode_partial(X[:1], 0)  # one token needs every expert
+    finally:
+        ctx.close()
+
+
+def _nccl_decode_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from gpeed_b200.ep import ExpertParallelDecode
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        ctx = Context(rank)
+        cfg = MoeConfig()
+        lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+        ex = CudaExecutor(ctx, cfg, 0, lo, cnt)
+        ex.synth(_router(cfg), None, SEED, S0)
+        ep = ExpertParallelDecode(cfg, ex)
+        X = _tokens(cfg, 2 * world).reshape(2, world, cfg.hidden)
+        ys = [ep.forward(X[s, rank:rank + 1].cuda()).cpu().numpy() for s in range(2)]
+        ctx.check()
+        np.save(os.path.join(out_dir, f"yd_{rank}.npy"), np.concatenate(ys))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_decode_nccl_two_gpus(tmp_path):
+    cfg = MoeConfig()
+    ctx = Context(0)
+    try:
+        full = MoeLayer(ctx, cfg, layer_id=800).synth(_router(cfg), None, SEED, S0)
+        X = _tokens(cfg, 4).reshape(2, 2, cfg.hidden)
+        y_ref = np.stack([np.concatenate([full.forward(X[s, r:r + 1].cuda()).cpu().numpy() for s in range(2)])
+                          for r in range(2)])
+    finally:
+        ctx.close()
+    mpc = mp.get_context("spawn")
+    port = _free_port()
+    procs = [mpc.Process(target=_nccl_decode_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    for r in range(2):
+        assert rel_l2(np.load(os.path.join(str(tmp_path), f"yd_{r}.npy")), y_ref[r]) < 1e-5
