@@ -48,6 +48,30 @@ __global__ void repack_kernel(uint8_t* __restrict__ raw, uint8_t* __restrict__ o
     }
 }
 
+// raw row-major blocks of n_mat matrices (rows x nblk blocks each) -> the
+// column-slab layout the persistent decode kernel streams the down projection
+// from (kernels.h, repacked_cols).  One thread per (matrix, row, block).
+__global__ void repack_cols_kernel(const uint8_t* __restrict__ raw, uint8_t* __restrict__ out, int64_t n_mat,
+                                   int rows, int nblk) {
+    const int64_t total = n_mat * rows * nblk;
+    const int64_t unit = (int64_t)rows * 12, mat = (int64_t)rows * nblk * 98;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t m = i / ((int64_t)rows * nblk);
+        const int r = (int)((i / nblk) % rows);
+        const int b = (int)(i % nblk);
+        const uint8_t* s = raw + i * 98;
+        uint8_t* base = out + m * mat;
+        for (int ib = 0; ib < 8; ++ib) {
+            uint8_t* u = base + (int64_t)(8 * b + ib) * unit;
+            for (int j = 0; j < 8; ++j) u[(int64_t)r * 8 + j] = s[2 + 8 * ib + j];
+            for (int j = 0; j < 4; ++j) u[(int64_t)rows * 8 + (int64_t)r * 4 + j] = s[66 + 4 * ib + j];
+        }
+        uint8_t* d = base + (int64_t)8 * nblk * unit + (int64_t)b * rows * 2 + (int64_t)r * 2;
+        d[0] = s[0];
+        d[1] = s[1];
+    }
+}
+
 __global__ void tables_kernel(uint8_t* dst) {
     iq3_build_tables(dst, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
@@ -94,6 +118,16 @@ cudaError_t launch_unpack(const uint8_t* packed, uint8_t* raw, int64_t rows, int
     if (total == 0) return cudaSuccess;
     const int grid = (int)gp_min64((total + 255) / 256, 148 * 32);
     repack_kernel<<<grid, 256, 0, st>>>(raw, const_cast<uint8_t*>(packed), rows, nblk, true);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_repack_cols(const uint8_t* raw, uint8_t* cols, int64_t n_mat, int rows, int in_dim,
+                               cudaStream_t st) {
+    const int nblk = in_dim / 256;
+    const int64_t total = n_mat * rows * nblk;
+    if (total == 0) return cudaSuccess;
+    const int grid = (int)gp_min64((total + 255) / 256, 148 * 32);
+    repack_cols_kernel<<<grid, 256, 0, st>>>(raw, cols, n_mat, rows, nblk);
     return cudaGetLastError();
 }
 

@@ -53,6 +53,10 @@ struct Layer {
     uint8_t* up = nullptr;
     uint8_t* down = nullptr;  // (E + n_shared) experts x H rows of I
     int64_t gu_stride = 0, d_stride = 0;
+    // the down projections again in the column-slab layout the persistent
+    // decode kernel streams (launch_repack_cols), for shapes it serves
+    uint8_t* down_col = nullptr;
+    int64_t dc_stride = 0;
     // experts held here: routed [e_lo, e_lo + e_cnt) at local index e - e_lo,
     // then the shared expert at local index e_cnt (all of them unless the
     // layer was loaded for expert parallelism)
@@ -107,8 +111,7 @@ struct gpeed_ctx {
     int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
-    DevBuf<unsigned long long> logits, picks, dx;
-    DevBuf<uint8_t> hq;
+    DevBuf<unsigned long long> logits, picks;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
     bool prof = false;
@@ -256,8 +259,11 @@ int h2d_staged(gpeed_ctx* c, void* dst, const void* src, size_t bytes, cudaStrea
     return GPEED_OK;
 }
 
+// Raw GGUF IQ3_XXS rows (host or device) -> the row-group layout at dst and,
+// when dst_cols is given, also the column-slab layout of n_mat stacked down
+// projections of rows / n_mat rows each.
 int upload_matrix(gpeed_ctx* c, const void* raw, int on_device, int64_t rows, int in_dim, uint8_t* dst,
-                  cudaStream_t st) {
+                  cudaStream_t st, uint8_t* dst_cols = nullptr, int64_t n_mat = 1) {
     const size_t raw_bytes = (size_t)rows * (in_dim / 256) * 98;
     const uint8_t* src = static_cast<const uint8_t*>(raw);
     uint8_t* tmp = nullptr;
@@ -272,6 +278,7 @@ int upload_matrix(gpeed_ctx* c, const void* raw, int on_device, int64_t rows, in
         src = tmp;
     }
     GP_CUDA(gp::launch_repack(src, dst, rows, in_dim, st));
+    if (dst_cols) GP_CUDA(gp::launch_repack_cols(src, dst_cols, n_mat, (int)(rows / n_mat), in_dim, st));
     if (tmp) {
         GP_CUDA(cudaStreamSynchronize(st));
         GP_CUDA(cudaFree(tmp));
@@ -299,6 +306,7 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int e_lo, int
     if (it != c->layers.end()) {
         Layer& old = it->second;
         cudaFree(old.router); cudaFree(old.corr); cudaFree(old.gate); cudaFree(old.up); cudaFree(old.down);
+        cudaFree(old.down_col);
         cudaFree(old.router_split);
         c->layers.erase(it);
     }
@@ -325,6 +333,10 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int e_lo, int
     GP_CUDA(cudaMalloc(&L.gate, L.gu_stride * NE + gp::repacked_bytes(32, H)));
     GP_CUDA(cudaMalloc(&L.up, L.gu_stride * NE + gp::repacked_bytes(32, H)));
     GP_CUDA(cudaMalloc(&L.down, L.d_stride * NE + gp::repacked_bytes(32, I)));
+    if (gp::decode_layer_supported(H, I, E, s->top_k, s->n_shared)) {
+        L.dc_stride = (int64_t)H * (I / 256) * 98;
+        GP_CUDA(cudaMalloc(&L.down_col, L.dc_stride * NE));
+    }
     c->layers[layer] = L;
     *out = &c->layers[layer];
     return GPEED_OK;
@@ -460,19 +472,16 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     const size_t had_p = c->picks.n;
     if ((rc = c->picks.ensure(gp::decode_layer_pick_words()))) return rc;
     if (c->picks.n != had_p) GP_CUDA(cudaMemsetAsync(c->picks.p, 0, c->picks.n * sizeof(unsigned long long), st));
-    const size_t had_dx = c->dx.n;
-    if ((rc = c->dx.ensure((size_t)gp::kDecodeSlots * H))) return rc;
-    if (c->dx.n != had_dx) GP_CUDA(cudaMemsetAsync(c->dx.p, 0, c->dx.n * sizeof(unsigned long long), st));
-    if ((rc = c->hq.ensure((size_t)gp::kDecodeSlots * gp::decode_layer_hq_bytes(I)))) return rc;
     gp::DecodeLayerArgs& da = *out;
     da = gp::DecodeLayerArgs{};
     da.router = L.router;
     da.corr = L.corr;
+    if (!L.down_col) return fail(GPEED_ERR_UNSUPPORTED, "layer holds no column-slab copy of its down projections");
     da.gate = L.gate;
     da.up = L.up;
-    da.down = L.down;
+    da.down_col = L.down_col;
     da.gu_stride = L.gu_stride;
-    da.d_stride = L.d_stride;
+    da.dc_stride = L.dc_stride;
     da.H = H;
     da.I = I;
     da.E = E;
@@ -493,15 +502,11 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     da.own_tok = own_tok;
     da.logits = c->logits.p;
     da.picks = c->picks.p;
-    da.dx = c->dx.p;
-    da.h = c->h.p;
-    da.hq = c->hq.p;
-    da.D = c->D.p;
     da.sync = c->sync;
     da.tables = c->tables;
     da.status = c->status;
     da.stages = 3;  // the deepest stage ring that fits next to the tables
-    while (gp::decode_layer_smem(H, I, da.stages + 1, n_tok, n_tok * K) <= 227u * 1024u && da.stages < 8) ++da.stages;
+    while (gp::decode_layer_smem(H, I, da.stages + 1, n_tok) <= 227u * 1024u && da.stages < 8) ++da.stages;
     da.cooperative = c->fused_cooperative;
     da.spin_limit = c->spin_limit;
     da.withhold_logit = c->withhold_logit;
@@ -641,6 +646,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& kv : c->layers) {
         Layer& L = kv.second;
         cudaFree(L.router); cudaFree(L.corr); cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down);
+        cudaFree(L.down_col);
         cudaFree(L.router_split);
     }
     c->partial.release(); c->topk_w.release(); c->h.release(); c->D.release(); c->mvout.release();
@@ -653,8 +659,6 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     c->xp.release();
     c->route_chunks.release();
     c->mhc_partial.release();
-    c->dx.release();
-    c->hq.release();
     cudaFree(c->sync);
     cudaFree(c->tables);
     cudaFree(c->status);
@@ -680,7 +684,6 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
         GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));
         if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
         if (c->picks.p) GP_CUDA(cudaMemset(c->picks.p, 0, c->picks.n * sizeof(unsigned long long)));
-        if (c->dx.p) GP_CUDA(cudaMemset(c->dx.p, 0, c->dx.n * sizeof(unsigned long long)));
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape, 16: a token or h value past the fp16 range "
                                       "on the tensor-core path)", st);
@@ -826,12 +829,14 @@ int gpeed_moe_load_layer_range(gpeed_ctx* c, int layer, const gpeed_moe_shape* s
     if (EC) {
         if ((rc = upload_matrix(c, gate, on_device, (int64_t)EC * I, H, L->gate, 0))) return rc;
         if ((rc = upload_matrix(c, up, on_device, (int64_t)EC * I, H, L->up, 0))) return rc;
-        if ((rc = upload_matrix(c, down, on_device, (int64_t)EC * H, I, L->down, 0))) return rc;
+        if ((rc = upload_matrix(c, down, on_device, (int64_t)EC * H, I, L->down, 0, L->down_col, EC))) return rc;
     }
     if (s->n_shared) {
         if ((rc = upload_matrix(c, gate_sh, on_device, I, H, L->gate + L->gu_stride * EC, 0))) return rc;
         if ((rc = upload_matrix(c, up_sh, on_device, I, H, L->up + L->gu_stride * EC, 0))) return rc;
-        if ((rc = upload_matrix(c, down_sh, on_device, H, I, L->down + L->d_stride * EC, 0))) return rc;
+        if ((rc = upload_matrix(c, down_sh, on_device, H, I, L->down + L->d_stride * EC, 0,
+                                L->down_col ? L->down_col + L->dc_stride * EC : nullptr, 1)))
+            return rc;
     }
     GP_CUDA(cudaDeviceSynchronize());
     return GPEED_OK;
@@ -876,6 +881,9 @@ int gpeed_moe_synth_layer_range(gpeed_ctx* c, int layer, const gpeed_moe_shape* 
         if (!mats[m].nb) continue;
         GP_CUDA(gp::launch_synth(tmp, seed, stream0 + m, mats[m].block0, mats[m].nb, 0));
         GP_CUDA(gp::launch_repack(tmp, mats[m].dst, mats[m].rows, mats[m].in, 0));
+        if (L->down_col && (m == 2 || m == 5))  // the down projections, also as column slabs
+            GP_CUDA(gp::launch_repack_cols(tmp, L->down_col + (m == 5 ? L->dc_stride * EC : 0), m == 5 ? 1 : EC, H, I,
+                                           0));
     }
     GP_CUDA(cudaDeviceSynchronize());
     GP_CUDA(cudaFree(tmp));

@@ -1,23 +1,28 @@
-// One MoE layer at batch 1 in a single persistent kernel
+// One MoE layer at decode batch sizes in a single persistent kernel
 // (reference Model::moe_forward, cpp/core/src/model.cpp:692-756).
 //
 // Separate kernels for router, routing, gate/up, down and combine each pay a
 // launch, a prologue (decode tables, first bytes in flight) and a tail, which
 // at batch 1 costs more than streaming the 85 MB of weights.  Here one CTA per
-// SM runs the whole layer.  Warp roles: 24 compute warps, one TMA producer
-// warp streaming weight tiles through a ring of shared-memory stages, and one
+// SM runs the whole layer.  Warp roles: 20 compute warps, one TMA producer
+// warp streaming weights through a ring of shared-memory stages, and one
 // epilogue warp that does the routing and turns each stage's partial sums
-// into results.  Under full HBM load a round trip to L2 costs microseconds
-// (more from the other die), so the design keeps those out of the per-tile
-// path: no atomics are read back, and values other CTAs produced are read as
-// words tagged with the launch generation (the data is its own flag).
+// into h.  Under full HBM load a round trip to L2 costs microseconds, so the
+// only exchange between CTAs is the routing: values other CTAs produced are
+// read as words tagged with the launch generation (the data is its own flag).
 //
-// The same kernel runs one rank's share of an expert-parallel decode step:
-// n_tok tokens (one per rank), the routed experts of one range, the shared
-// expert of the rank's own token.  Its slots are then the (token, expert)
-// picks that fall in the range, and it writes each token's partial output
-// (the ranks' parts sum to the layer).  One token with every expert is the
-// batch-1 layer, with the same arithmetic in the same order.
+// Work item = (slot, unit): 32 rows of h of one slot's expert (a slot is a
+// (token, expert) pick, or the shared expert).  An item runs gate/up for its
+// 32 rows (4 tiles of 8 gate + 8 up rows), SwiGLU with the reference clamp
+// (model.cpp:733-739), quantises its 32 h values, and then at once its slice
+// of the down projection: the 32 input columns of W_down that these h values
+// multiply, for every output row (a split-K down, streamed from a column-slab
+// copy of W_down in 4 chunks of 1280 rows).  The item adds w_k * D_slice into
+// y with vector fp32 reductions, so no CTA waits for h computed elsewhere.
+// Items are dealt round-robin, shared expert first (it needs no routing and
+// overlaps it); each CTA interleaves its stages as GU(0) GU(1) DN(0) GU(2)
+// DN(1) ... so the epilogue's SwiGLU + quantisation of item m overlaps the
+// gate/up of item m+1.
 //
 //   router   CTA c owns experts c, c+G, ...; 8 warps each compute one 1/8
 //            slice of an owned expert's fp32 logit for every token (weights
@@ -25,32 +30,27 @@
 //            epilogue warp adds the slices in order and stores the logit
 //            tagged with the launch generation, so readers poll the data itself
 //   top-k    one token: every CTA's epilogue warp polls the E tagged logits
-//            (one of 8 replicas, spread over L2 lines), applies
-//            sigmoid + bias and picks top-K by warp reductions (ties to the
-//            lower id), weights score/(1e-20 + sum)*scale (model.cpp:704-725).
-//            Several tokens: CTA t picks token t's experts and publishes the
-//            picks as tagged words that every CTA then reads.  The picks in
-//            the launch's expert range become its slots
-//   gate/up  units of 32 rows of h, dealt round-robin in slot order (the
-//            shared expert first: it needs no routing; then the routed slots
-//            in pick order); a unit is 4 consecutive tiles of 8 rows of
-//            gate and up.  The epilogue applies SwiGLU with the reference clamp
-//            (model.cpp:733-739), quantises the finished unit to int16 (hq)
-//            and counts it for its slot: no value of h leaves the CTA
-//            unquantised and no counter is read back
-//   down     tiles of 32 rows x all slots, a contiguous range of (tile,
-//            slot) positions per CTA sized to even out the total work; the
-//            producer copies each tile with its slot's hq once all units of
-//            that slot are counted (model.cpp:740).  The epilogue keeps a row
-//            tile's slot results in shared memory and writes y = sum_k w_k
-//            D[k] + D[shared] in top-k order per token (model.cpp:741-755); for a tile
-//            shared with the next CTAs it reads their slots as tagged words
+//            (one of 8 replicas, spread over L2 lines), applies sigmoid + bias
+//            and picks top-K by warp reductions (ties to the lower id),
+//            weights score/(1e-20 + sum)*scale (model.cpp:704-725).  Several
+//            tokens: CTA t picks token t's experts and publishes the picks as
+//            tagged words that every CTA then reads.  The picks in the
+//            launch's expert range become its slots
+//   y        zeroed by the CTAs before they publish their logits; every
+//            reduction into y comes after its CTA has seen the routing, so
+//            after every CTA's zeroing
 //
-// Waits on other CTAs need every CTA resident: one CTA per SM, launched either
-// with programmatic dependent launch (default) or cooperatively.  Every wait
-// is bounded; a timeout sets a status bit, the CTA stops waiting and finishes
-// (results then invalid, the host reports the status and clears the
-// counters and tags).
+// The same kernel runs one rank's share of an expert-parallel decode step:
+// n_tok tokens (one per rank), the routed experts of one range, the shared
+// expert of the rank's own token; y[t] is then this rank's part of token t's
+// output (the ranks' parts sum to the layer).
+//
+// The routing exchange needs every CTA resident: one CTA per SM, launched
+// either with programmatic dependent launch (default) or cooperatively.
+// Every wait is bounded; a timeout sets a status bit, the CTA stops and
+// finishes (results then invalid, the host reports the status and clears the
+// counters and tags).  Sums into y land in a different order from launch to
+// launch (fp32 reductions), so results agree to rounding, not bit for bit.
 #include <cuda_fp16.h>
 
 #include "expert_common.cuh"
@@ -68,28 +68,26 @@
 namespace gp {
 namespace {
 
-constexpr int NWC = 24;          // compute warps
-constexpr int NWG = 20;          // of which compute gate/up (32*20 lanes = 4 rows of 5120)
+constexpr int NWC = 20;          // compute warps (gate/up: 32*20 lanes = 4 rows of 5120 per pass)
 constexpr int EPI = NWC;         // epilogue warp
 constexpr int PROD = NWC + 1;    // TMA producer warp
 constexpr int NTHREADS = 32 * (NWC + 2);
 constexpr int TRG = 8;           // gate/up rows per matrix per tile
-constexpr int TRD = 32;          // down rows per tile (one per epilogue lane)
-constexpr int UNIT = 32;         // activation quantisation unit = rows of h per gate/up unit
-constexpr int TPU = UNIT / TRG;  // gate/up tiles per unit
+constexpr int UNIT = 32;         // rows of h per work item = input columns of its down slice
+constexpr int TPU = UNIT / TRG;  // gate/up tiles per item
+constexpr int RC = 4 * 32 * NWC; // down rows per chunk (four per compute lane)
 constexpr int RSPLIT = 8;        // router slices per expert
-constexpr int MAXK = 31;         // K+1 slots fit one warp
+constexpr int MAXK = 31;         // picks per token
 constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
 constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
-// Tagged logits: every CTA polls all E of them, so one array would send every
-// poll of every CTA to the few L2 slices holding it.  Each logit is stored in
-// kLogitCopies replicas, one word per 256-byte line; CTA c polls replica
-// c % kLogitCopies.
+constexpr int kPrefetch = 4;     // stages prefetched into L2 beyond the shared-memory ring
+// Tagged logits: with one token every CTA polls all E of them, so one array
+// would send every poll of every CTA to the few L2 slices holding it.  Each
+// logit is then stored in kLogitCopies replicas, one word per 256-byte line;
+// CTA c polls replica c % kLogitCopies.
 constexpr int kLogitCopies = 8;
 constexpr int kLogitStride = 32;  // words
 static_assert(kLogitCopies * kLogitStride == 256, "decode_layer_logit_words (kernels.h) assumes 8 x 32");
-static_assert(TRD == 32, "the combine maps one row of a down tile to each epilogue lane");
-
 
 GP_DEVINL unsigned long long ld_relaxed64(const unsigned long long* p) {
     unsigned long long v;
@@ -103,6 +101,18 @@ GP_DEVINL unsigned ld_relaxed(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
+}
+
+// Prefetch `bytes` at p into L2 (no completion to wait for).
+GP_DEVINL void prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// y[0..3] += v as one fire-and-forget vector reduction: no value comes
+// back, so the warp does not wait for the L2 round trip (an atomicAdd on a
+// float4 returns the old values and stalls the registers that receive them).
+GP_DEVINL void red_add_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
 // Warp-uniform view of the CTA's abort flag.  Lanes read the volatile word
@@ -209,12 +219,6 @@ GP_DEVINL float load_quant(const void* x, int x_bf16, int64_t row, int in_dim, i
     load_x_unit<32>(x, x_bf16, row, in_dim, 32 * sb, v);
     return 0.25f * quant_i16<32>(v, xq);
 }
-
-// Sentinel slot id of the shared expert in work items (its storage index is
-// kSharedStore; its position among a down tile's values is the routed count).
-constexpr int kShared = -1;
-constexpr int kSharedStore = kDecodeMaxRouted;
-GP_DEVINL int slot_store(int slot) { return slot < 0 ? kSharedStore : slot; }
 
 // Tagged logit of token `tok`, expert e: one token is read by every CTA and
 // kept in kLogitCopies replicas (copy = reader's CTA % kLogitCopies); with
@@ -355,10 +359,8 @@ GP_DEVINL void build_slots(const DecodeLayerArgs& a, int lane, int e0, float w0,
     if (lane == 0) *s_nsr = __popc(b0) + __popc(b1);
 }
 
-// Per-stage partial sums: one per (row of the tile, covering warp).
-constexpr uint32_t kPartialFloats =
-    2 * TRG * LaneMap<5120, NWG, 4>::WPR > TRD * LaneMap<1536, NWC, 2>::WPR ? 2 * TRG * LaneMap<5120, NWG, 4>::WPR
-                                                                          : TRD * LaneMap<1536, NWC, 2>::WPR;
+// Per-stage partial sums of a gate/up tile: one per (row of the tile, covering warp).
+constexpr uint32_t kPartialFloats = 2 * TRG * LaneMap<5120, NWC, 4>::WPR;
 
 struct Smem {
     uint32_t stage_bytes, stages_off, partial_off, bar_off, misc_off, total;
@@ -366,149 +368,87 @@ struct Smem {
 
 // misc block: abort flag (16 B), routed-slot count + first slot per token (16
 // ints), slot -> local expert / token / weight (3 x kDecodeMaxRouted words),
-// router slices [kMaxOwned * RSPLIT][n_tok], one down row tile's values per
-// slot [max_routed + 1][32].
-__host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok, int max_routed) {
+// router slices [kMaxOwned * RSPLIT][n_tok], two quantised h units (16 words +
+// scale each, padded to 80 B).
+__host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok) {
     Smem L;
     const uint32_t gu = 2u * TRG * 98u * (H / 256);
-    const uint32_t dn = TRD * 98u * (I / 256) + (uint32_t)I * 2u + (uint32_t)(I / UNIT) * 4u;
+    const uint32_t dn = (uint32_t)RC * 14u;
+    (void)I;
     L.stage_bytes = ((gu > dn ? gu : dn) + 15u) & ~15u;
     L.stages_off = GP_IQ3_TABLE_BYTES;
     L.partial_off = L.stages_off + S * L.stage_bytes;
     const uint32_t pb = kPartialFloats * 4u;
     L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
-    L.misc_off = L.bar_off + (3u * S + 4u) * 8u;
-    L.total = L.misc_off + 16u + 64u + 12u * kDecodeMaxRouted + 4u * kMaxOwned * RSPLIT * n_tok +
-              128u * (uint32_t)(max_routed + 1);
+    // 16-byte aligned: the quantised h units are read with 16-byte loads (every
+    // offset inside the block below is a multiple of 16)
+    L.misc_off = (L.bar_off + (3u * S + 6u) * 8u + 15u) & ~15u;
+    L.total = L.misc_off + 16u + 64u + 12u * kDecodeMaxRouted + 4u * kMaxOwned * RSPLIT * n_tok + 160u;
     return L;
 }
 
-// Work item i of a phase in slot order: the shared expert first (it needs no
-// routing), then routed slots 0..nsr-1; `per_slot` items each.
-struct Item {
-    int slot, idx;  // slot kShared: the shared expert
-};
-GP_DEVINL Item item_of(int i, int per_slot) {
-    if (i < per_slot) return {kShared, i};
-    const int r = i - per_slot, slot = r / per_slot;
-    return {slot, r - slot * per_slot};
-}
 // Items i = c, c+G, c+2G, ... below total.
 GP_DEVINL int items_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
 
-// Down work: positions v = tile*(nsr+1) + q over (row tile, slot position q);
-// position q = nsr is the shared expert (ready first), q < nsr routed slot
-// nsr-1-q (slot 0 at q = nsr-1 is ready next, slot nsr-1 at q = 0 last).  CTA
-// c owns the range [v0, v1), sized so that its down work plus its routed
-// gate/up units is the same for every CTA (weights: one unit ~ wu, one down
-// position ~ wd).  The range is walked as: the leading partial tile, the
-// first whole tile, the trailing partial tile, the other whole tiles; each
-// tile in descending q.  Partial tiles thus meet the early-ready slots first,
-// the tiles shared with a neighbour CTA are settled early, and the CTA ends
-// on a whole tile it combines by itself.
-GP_DEVINL int down_slot(int q, int nsr) { return q == nsr ? kShared : nsr - 1 - q; }
-struct DownRange {
-    int v0, v1, b, e, P;  // range, first / last tile boundary inside it, nsr+1
-    GP_DEVINL int count() const { return v1 - v0; }
-    GP_DEVINL int at(int i) const {
-        const int lead_end = b < v1 ? b : v1;
-        if (i < lead_end - v0) return lead_end - 1 - i;
-        i -= lead_end - v0;
-        const int nf = e > b ? (e - b) / P : 0;
-        if (nf > 0) {
-            if (i < P) return b + P - 1 - i;
-            i -= P;
-        }
-        const int n_trail = (e >= b && e < v1) ? v1 - e : 0;
-        if (i < n_trail) return v1 - 1 - i;
-        i -= n_trail;
-        const int f = 1 + i / P;
-        return b + f * P + P - 1 - (i - (f - 1) * P);
-    }
+// Stage t of a CTA with n items, in the order GU(0) GU(1) DN(0) GU(2) DN(1)
+// ... GU(n-1) DN(n-2) DN(n-1): item m, its tile or chunk j, gate/up or down.
+struct Stage {
+    int m, j;
+    bool gu;
 };
-GP_DEVINL int prefix_rr(int c, int G, int total) {  // sum of items_of(c', G, total) over c' < c
-    return (total / G) * c + (c < total % G ? c : total % G);
-}
-GP_DEVINL DownRange down_range(int c, int G, int n_tiles, int P, int units, int shared_units) {
-    // weights set by measurement of the whole layer (not of the units alone):
-    // a routed gate/up unit counts as 3 down positions, although it takes
-    // about 5.7, because a CTA that finishes its units early cannot start the
-    // down tiles of the slots still being computed elsewhere; a shared unit
-    // mostly overlaps the routing.  32-bit arithmetic: G * W < 2^31 for the
-    // supported shapes (host-checked).
-    constexpr int wu = 30, ws = 17, wd = 10;
-    const int routed = units - shared_units, total = n_tiles * P;
-    const int W = routed * wu + shared_units * ws + total * wd;
-    const int max_units = (units + G - 1) / G;
-    const bool weighted = max_units * wu * G <= W;  // every CTA still gets >= 0 down positions
-    auto start = [&](int cc) -> int {
-        if (!weighted) return total * cc / G;
-        const int sh = prefix_rr(cc, G, shared_units), all = prefix_rr(cc, G, units);
-        return (cc * W - G * ((all - sh) * wu + sh * ws)) / (G * wd);
-    };
-    DownRange r;
-    r.P = P;
-    r.v0 = start(c);
-    r.v1 = c + 1 == G ? (int)total : start(c + 1);
-    r.b = (r.v0 + P - 1) / P * P;
-    r.e = r.v1 / P * P;
-    if (r.b > r.v1) r.b = r.v1;
-    if (r.e < r.b) r.e = r.b;
-    return r;
+GP_DEVINL Stage stage_of(int t, int n, int nch) {
+    if (t < TPU) return {0, t, true};
+    const int r = t - TPU, per = TPU + nch, m = r / per + 1;
+    if (m < n) {
+        const int k = r - (m - 1) * per;
+        return k < TPU ? Stage{m, k, true} : Stage{m - 1, k - TPU, false};
+    }
+    return {n - 1, r - (n - 1) * per, false};
 }
 
-// A CTA's share of the work once the routed slot count nsr is known.
-struct Work {
-    int nsr, n_gu, n_items;
-    DownRange R;
+// Global item i -> (slot, unit): the shared expert's NU units first (slot -1),
+// then routed slots 0.. in pick order.
+struct Item {
+    int slot, unit;
 };
-GP_DEVINL Work work_of(int c, int G, int nsr, int NU, int TD) {
-    Work w;
-    w.nsr = nsr < 0 ? 0 : nsr > kDecodeMaxRouted ? kDecodeMaxRouted : nsr;
-    const int nsl = w.nsr + 1;
-    w.n_gu = TPU * items_of(c, G, NU * nsl);
-    w.R = down_range(c, G, TD, nsl, NU * nsl, NU);
-    w.n_items = w.n_gu + w.R.count();
-    return w;
+GP_DEVINL Item item_of(int i, int NU) {
+    if (i < NU) return {-1, i};
+    const int r = i - NU;
+    return {r / NU, r % NU};
 }
 
 // Quantises the unit of h held one value per lane exactly as a lane quantises
-// its activations for the GEMV (quant_i16<32>, scale * 1/4), into hq.  hq
-// layout: 4 planes of NU 16-byte chunks (plane i holds words 4i..4i+3 of every
-// unit, so a warp's 16-byte loads of consecutive units are conflict-free),
-// then the NU fp32 scales at 2*I.
-GP_DEVINL void quantise_unit(float v, uint8_t* hq, int I, int unit, int lane) {
+// its activations for the GEMV (quant_i16<32>, scale * 1/4): words[w] holds
+// rows 2w (low half) and 2w+1 as int16, words[16] the fp32 scale.
+GP_DEVINL void quantise_unit(float v, uint32_t* words, int lane) {
     float amax = fabsf(v);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float inv = amax > 0.f ? 32767.0f / amax : 0.f;
     const int q = __float2int_rn(v * inv);
     const int qn = __shfl_down_sync(0xffffffffu, q, 1);
-    const int w = lane >> 1;  // word of the unit
-    if (!(lane & 1))
-        *reinterpret_cast<uint32_t*>(hq + (w >> 2) * (I / UNIT) * 16 + unit * 16 + (w & 3) * 4) =
-            (static_cast<uint32_t>(q) & 0xFFFFu) | (static_cast<uint32_t>(qn) << 16);
-    if (lane == 0) reinterpret_cast<float*>(hq + 2 * I)[unit] = 0.25f * (amax * (1.0f / 32767.0f));
+    if (!(lane & 1)) words[lane >> 1] = (static_cast<uint32_t>(q) & 0xFFFFu) | (static_cast<uint32_t>(qn) << 16);
+    if (lane == 0) words[16] = __float_as_uint(0.25f * (amax * (1.0f / 32767.0f)));
 }
 
-template <int HH, int II, int PG, int RPWG, int PD, int RPWD>
+template <int HH, int II, int PG, int RPWG>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
     constexpr int H = HH, I = II;
-    constexpr int TD = H / TRD, NU = I / UNIT;
-    constexpr uint32_t GU_BYTES = TRG * 98u * (H / 256), DN_BYTES = TRD * 98u * (I / 256);
-    constexpr uint32_t HQ_BYTES = I * 2u + NU * 4u;
-    static_assert(UNIT % TRG == 0 && HQ_BYTES % 16 == 0 && DN_BYTES % 16 == 0 && GU_BYTES % 16 == 0,
-                  "bulk copies need 16-byte sizes and offsets");
+    constexpr int NU = I / UNIT, NCH = H / RC;
+    constexpr uint32_t GU_BYTES = TRG * 98u * (H / 256);
+    constexpr uint32_t UNIT_BYTES = (uint32_t)H * 12u;  // one column unit of W_down: qs + aux of every row
+    static_assert(H % RC == 0 && GU_BYTES % 16 == 0 && (RC * 2) % 16 == 0, "bulk copies need 16-byte sizes");
     const int E = a.E, K = a.K, S = a.stages, NT = a.n_tok;
-    const Smem L = decode_smem(H, I, S, NT, NT * K);
+    const Smem L = decode_smem(H, I, S, NT);
     const uint32_t sbase = smem_u32(smem);
     // per stage: full (producer -> compute warps), pdone (compute warps ->
-    // epilogue warp: partial sums written), empty (epilogue -> producer)
+    // epilogue warp: partial sums written / chunk read), empty (epilogue ->
+    // producer); hbar[b]: item m's quantised h is in s_h[b], b = m & 1
     const uint32_t full0 = sbase + L.bar_off, pdone0 = full0 + 8u * S, empty0 = pdone0 + 8u * S;
-    const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u, gbar = rbar + 8u;
+    const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u, hbar0 = rbar + 8u;
     volatile uint32_t* s_abort = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off);
     int* s_nsr = reinterpret_cast<int*>(smem + L.misc_off + 16u);
     int* s_first = s_nsr + 1;                       // [n_tok + 1]
@@ -516,11 +456,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     int* s_st = s_se + kDecodeMaxRouted;            // token of a slot
     float* s_sw = reinterpret_cast<float*>(s_st + kDecodeMaxRouted);  // weight of a slot
     float* s_slice = s_sw + kDecodeMaxRouted;       // [task][n_tok] router slices
-    float* s_dv = s_slice + kMaxOwned * RSPLIT * NT;  // [slot position][32] one down row tile
+    uint32_t* s_h = reinterpret_cast<uint32_t*>(s_slice + kMaxOwned * RSPLIT * NT);  // [2][20]
     float* partial = reinterpret_cast<float*>(smem + L.partial_off);
     constexpr uint32_t pstride = kPartialFloats;
     const uint32_t stage0 = sbase + L.stages_off;
-    const int n_shared = TPU * items_of(c, G, NU);  // leading gate/up tiles that need no routing
     const int n_own = items_of(c, G, E);            // router experts c, c+G, ...
     const int n_tasks = n_own * RSPLIT;
 
@@ -536,108 +475,97 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         mbar_init(tbar, 1);
         mbar_init(topk_bar, 1);
         mbar_init(rbar, n_tasks > 0 ? n_tasks : 1);
-        mbar_init(gbar, 1);
+        mbar_init(hbar0, 1);
+        mbar_init(hbar0 + 8u, 1);
         *s_abort = gp_tables_at_base(smem) ? 0u : 1u;
         if (*s_abort) atomicOr(a.status, GP_DEV_BAD_SHAPE);
         fence_mbar_init();
     }
     __syncthreads();
 
+    // item m of this CTA: its slot (-1: shared), unit, local expert, token
+    auto item_at = [&](int m, int& slot, int& unit, int& e, int& tok) {
+        const Item it = item_of(c + m * G, NU);
+        slot = it.slot;
+        unit = it.unit;
+        e = slot < 0 ? a.e_cnt : s_se[slot];
+        tok = slot < 0 ? a.own_tok : s_st[slot];
+    };
+
     if (warp == PROD) {
-        // ================= producer (lane 0 issues; the warp polls) =================
+        // ================= producer (lane 0 issues) =================
         if (lane == 0) {
-            GP_STAMP(9);
             mbar_arrive_expect_tx(tbar, GP_IQ3_TABLE_BYTES);
             for (int k4 = 0; k4 < 4; ++k4) bulk_g2s(sbase + k4 * 16384u, a.tables + k4 * 16384, 16384u, tbar);
-        }
-        int s = 0, issued = 0;
-        uint32_t ph = 1;
-        uint32_t ready[3] = {0u, 0u, 0u};  // storage slots whose h units are all counted
-        bool have = false;
-        Work w{};
-        for (int it = 0;; ++it) {
-            if (__shfl_sync(0xffffffffu, *s_abort, 0)) break;
-            if (!have && it >= n_shared) {  // routed tiles need the slot list (every lane reads it)
-                const bool ok = mbar_wait(topk_bar, 0, a.spin_limit);
-                if (!ok) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-                if (!__all_sync(0xffffffffu, ok)) break;
-                if (lane == 0) GP_STAMP(10);
-                w = work_of(c, G, *s_nsr, NU, TD);
-                have = true;
-            }
-            if (have && it >= w.n_items) break;
-            int slot;
-            uint32_t off, b0, b1;
-            const bool gu = it < (have ? w.n_gu : n_shared);
-            if (gu) {
-                const Item u = item_of(c + (it / TPU) * G, NU);
-                slot = u.slot;
-                off = (uint32_t)(u.idx * TPU + it % TPU) * GU_BYTES;
-                b0 = b1 = GU_BYTES;
-            } else {
-                const int v = w.R.at(it - w.n_gu), nsl = w.nsr + 1;
-                slot = down_slot(v % nsl, w.nsr);
-                off = (uint32_t)(v / nsl) * DN_BYTES;
-                b0 = DN_BYTES;
-                b1 = HQ_BYTES;
-                // the tile travels with its slot's quantised h: wait (warp-wide
-                // poll of the slots' counters) until all its units are counted
-                const int st = slot_store(slot);
-                auto is_ready = [&]() {  // bit st of the three ready words (no dynamic register index)
-                    const uint32_t rw = st < 32 ? ready[0] : st < 64 ? ready[1] : ready[2];
-                    return ((rw >> (st & 31)) & 1u) != 0u;
-                };
-                if (!is_ready()) {
-                    uint32_t n = 0;
-                    for (; n < a.spin_limit; ++n) {
-#pragma unroll
-                        for (int j = 0; j < 3; ++j) {
-                            const int q = lane + 32 * j;
-                            const bool valid = q < w.nsr || q == kSharedStore;
-                            const unsigned cnt = valid ? ld_relaxed(a.sync + kSyncSlot + q) : 0u;
-                            ready[j] = __ballot_sync(0xffffffffu, valid && cnt >= (unsigned)NU);
-                        }
-                        if (is_ready()) break;
-                        __nanosleep(64);
-                    }
-                    if (n == a.spin_limit) {
-                        if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-                        break;
-                    }
-                    // order the observed counts (and so the hq words they
-                    // release) before this warp's later bulk-copy reads; a
-                    // slot seen ready stays ready, so one fence per poll
-                    fence_acq_rel_gpu();
-                    fence_proxy_async_global();
-                    if (lane == 0 && it == w.n_gu) GP_STAMP(12);
-                }
-            }
-            if (lane == 0) {
-                const int e = slot < 0 ? a.e_cnt : s_se[slot];  // local expert index
-                const uint8_t *src0, *src1;
-                if (gu) {
-                    const int64_t eo = (int64_t)e * a.gu_stride + off;
-                    src0 = a.gate + eo;
-                    src1 = a.up + eo;
+            int s = 0, issued = 0, n = 1;
+            uint32_t ph = 1;
+            bool have = false;  // the slot list (and so this CTA's item count) is known
+            // where item m's bytes are: its gate/up rows, its down column slab
+            // and its d block (the two items in flight, by parity m & 1)
+            struct Src {
+                int64_t guo;
+                const uint8_t *dc, *db;
+            };
+            auto item_src = [&](int m) -> Src {
+                int slot, unit, e, tok;
+                item_at(m, slot, unit, e, tok);
+                return {(int64_t)e * a.gu_stride + (int64_t)unit * TPU * GU_BYTES,
+                        a.down_col + (int64_t)e * a.dc_stride + (int64_t)unit * UNIT_BYTES,
+                        a.down_col + (int64_t)e * a.dc_stride + (int64_t)NU * UNIT_BYTES + (int64_t)(unit >> 3) * H * 2};
+            };
+            // stage u's bytes into L2: a sliding window kPrefetch stages beyond
+            // the shared-memory ring keeps more bytes in flight per SM than
+            // the ring holds, so the ring's copies later wait on L2, not DRAM
+            auto prefetch_stage = [&](int u) {
+                const Stage sg = stage_of(u, n, NCH);
+                const Src r = item_src(sg.m);
+                if (sg.gu) {
+                    prefetch_l2(a.gate + r.guo + (int64_t)sg.j * GU_BYTES, GU_BYTES);
+                    prefetch_l2(a.up + r.guo + (int64_t)sg.j * GU_BYTES, GU_BYTES);
                 } else {
-                    src0 = a.down + (int64_t)e * a.d_stride + off;
-                    src1 = a.hq + (int64_t)slot_store(slot) * HQ_BYTES;
+                    prefetch_l2(r.dc + (int64_t)sg.j * RC * 8, RC * 8u);
+                    prefetch_l2(r.dc + (int64_t)H * 8 + (int64_t)sg.j * RC * 4, RC * 4u);
+                    prefetch_l2(r.db + (int64_t)sg.j * RC * 2, RC * 2u);
+                }
+            };
+            int64_t guo0 = 0, guo1 = 0;
+            const uint8_t *dc0 = nullptr, *dc1 = nullptr, *db0 = nullptr, *db1 = nullptr;
+            for (int t = 0;; ++t) {
+                if (!have && (t >= TPU || c >= NU)) {  // routed items need the slot list
+                    if (!mbar_wait(topk_bar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); break; }
+                    GP_STAMP(10);
+                    n = items_of(c, G, NU * (min(max(*s_nsr, 0), kDecodeMaxRouted) + 1));
+                    have = true;
+                }
+                if (have && t >= n * (TPU + NCH)) break;
+                const Stage sg = stage_of(t, n, NCH);
+                const int p = sg.m & 1;
+                if (sg.gu && sg.j == 0) {  // a new item: where its bytes are, and the next one into L2
+                    const Src r = item_src(sg.m);
+                    if (p) { guo1 = r.guo; dc1 = r.dc; db1 = r.db; } else { guo0 = r.guo; dc0 = r.dc; db0 = r.db; }
                 }
                 if (!mbar_wait(empty0 + 8u * s, ph, a.spin_limit)) {
                     *s_abort = 1;
                     atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
-                } else {
-                    const uint32_t dst = stage0 + s * L.stage_bytes;
-                    mbar_arrive_expect_tx(full0 + 8u * s, b0 + b1);
-                    bulk_g2s(dst, src0, b0, full0 + 8u * s);
-                    bulk_g2s(dst + b0, src1, b1, full0 + 8u * s);
-                    ++issued;
-                    if (++s == S) { s = 0; ph ^= 1u; }
+                    break;
                 }
+                const uint32_t dst = stage0 + s * L.stage_bytes, bar = full0 + 8u * s;
+                if (sg.gu) {
+                    const int64_t eo = (p ? guo1 : guo0) + (int64_t)sg.j * GU_BYTES;
+                    mbar_arrive_expect_tx(bar, 2u * GU_BYTES);
+                    bulk_g2s(dst, a.gate + eo, GU_BYTES, bar);
+                    bulk_g2s(dst + GU_BYTES, a.up + eo, GU_BYTES, bar);
+                } else {
+                    const uint8_t* dc = p ? dc1 : dc0;
+                    mbar_arrive_expect_tx(bar, (uint32_t)RC * 14u);
+                    bulk_g2s(dst, dc + (int64_t)sg.j * RC * 8, RC * 8u, bar);
+                    bulk_g2s(dst + RC * 8u, dc + (int64_t)H * 8 + (int64_t)sg.j * RC * 4, RC * 4u, bar);
+                    bulk_g2s(dst + RC * 12u, (p ? db1 : db0) + (int64_t)sg.j * RC * 2, RC * 2u, bar);
+                }
+                ++issued;
+                if (++s == S) { s = 0; ph ^= 1u; }
+                if (have && t + S + kPrefetch < n * (TPU + NCH)) prefetch_stage(t + S + kPrefetch);
             }
-            __syncwarp();
-        }
-        if (lane == 0) {
             // no copy may still be in flight when the CTA exits (the
             // compile-time limit, whatever the run-time one)
             for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
@@ -648,13 +576,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     }
 
     if (warp == EPI) {
-        // ================= routing, then the epilogues =================
+        // ================= routing, then the gate/up epilogues =================
         constexpr int EJ = kMaxEFused / 32;
         float bias[EJ];
 #pragma unroll
         for (int j = 0; j < EJ; ++j) bias[j] = a.corr && lane + 32 * j < E ? __ldg(a.corr + lane + 32 * j) : 0.f;
         pdl_wait();
         const uint32_t tag = ld_relaxed(a.sync + kSyncGen) + 1u;
+        {   // this CTA's share of y = 0, ordered before its logits are published
+            float4* y4 = reinterpret_cast<float4*>(a.y);
+            for (int i = c * 32 + lane; i < NT * H / 4; i += G * 32) y4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            fence_acq_rel_gpu();
+        }
         if (n_tasks > 0) {  // this CTA's experts: slices added in order
             if (!mbar_wait(rbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (lane < n_own) {
@@ -674,13 +607,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 }
             }
         }
-        if (lane == 0) GP_STAMP(1);
         int e0 = 0, e1 = 0;
         float w0 = 0.f, w1 = 0.f;
         bool ok = true;
         if (NT == 1) {  // every CTA picks the token's experts itself
             ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0)
                           : topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0);
+            fence_acq_rel_gpu();  // the other CTAs' zeroing of y is seen before any reduction of this CTA
         } else {
             // CTA t picks token t's experts and publishes them; every CTA
             // then reads all tokens' picks (one more exchange, no CTA sorts
@@ -690,6 +623,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 float mw = 0.f;
                 ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, 0, c, true, me, mw)
                               : topk_token<EJ>(a, bias, tag, lane, 0, c, true, me, mw);
+                fence_acq_rel_gpu();
                 if (lane < K) {
                     const unsigned long long v = ((unsigned long long)(tag & 0xFFFFu) << 48) |
                                                  ((unsigned long long)(me & 0xFFFF) << 32) | __float_as_uint(mw);
@@ -710,6 +644,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 __nanosleep(TOPK_POLL_NS);
             }
             if (n == a.spin_limit) ok = false;
+            fence_acq_rel_gpu();
             e0 = (int)((p0 >> 32) & 0xFFFFu);
             w0 = __uint_as_float((uint32_t)p0);
             e1 = (int)((p1 >> 32) & 0xFFFFu);
@@ -721,111 +656,60 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         build_slots(a, lane, e0, w0, e1, w1, s_nsr, s_first, s_se, s_st, s_sw);
         __syncwarp();
         if (lane == 0) mbar_arrive(topk_bar);  // release: the other roles read the slot list
-        if (lane == 0) GP_STAMP(2);
+        GP_STAMP(2);
 
-        const Work w = work_of(c, G, *s_nsr, NU, TD);
-        const int nsr = w.nsr;
+        const int nsr = min(max(*s_nsr, 0), kDecodeMaxRouted);
+        const int n = items_of(c, G, NU * (nsr + 1));
         int s = 0;
         uint32_t ph = 0;
-        constexpr int rsg = 32 * NWG / (H / 32), rsd = 32 * NWC / (I / 32);
+        constexpr int rsg = 32 * NWC / (H / 32);
         float hv = 0.f;
-        // After an abort every warp leaves its loop at once (and arrives on no
-        // further barrier), so no barrier phase sees arrivals from two
-        // iterations; every wait left behind in another warp is bounded.
-        for (int it = 0; it < w.n_items; ++it) {
-            const bool gu = it < w.n_gu;
-            if (warp_aborted(s_abort)) break;
-            if (!mbar_wait(pdone0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            if (warp_aborted(s_abort)) break;
-            const float* pbuf = partial + (size_t)s * pstride;
+        // A warp whose bounded wait runs out records it and leaves its loop
+        // (arriving on no further barrier, so no barrier phase sees arrivals
+        // from two iterations); the waits it leaves other warps in run out
+        // in turn.  Decisions are warp-uniform (votes over the lanes' waits).
+        for (int t = 0; t < n * (TPU + NCH); ++t) {
+            const Stage sg = stage_of(t, n, NCH);
+            if (!__all_sync(0xffffffffu, mbar_wait(pdone0 + 8u * s, ph, a.spin_limit))) {
+                if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                break;
+            }
             float val = 0.f;
-            if (gu) {
-                if (lane < TRG) {  // partials in warp order (LaneMap layout)
-                    using LG = LaneMap<HH, NWG, PG>;
-                    const int row = lane, ur = TRG + row;
-                    const int ng = LG::last_warp(row % rsg) - LG::first_warp(row % rsg);
-                    const int nu = LG::last_warp(ur % rsg) - LG::first_warp(ur % rsg);
-                    float gs = 0.f, us = 0.f;
-                    for (int ww = 0; ww <= ng; ++ww) gs += pbuf[row * LG::WPR + ww];
-                    for (int ww = 0; ww <= nu; ++ww) us += pbuf[ur * LG::WPR + ww];
-                    val = silu_clamped(gs, us, a.limit);
+            if (sg.gu && lane < TRG) {  // partials in warp order (LaneMap layout)
+                using LG = LaneMap<HH, NWC, PG>;
+                const float* pbuf = partial + (size_t)s * pstride;
+                const int row = lane, ur = TRG + row;
+                const int ng = LG::last_warp(row % rsg) - LG::first_warp(row % rsg);
+                const int nu = LG::last_warp(ur % rsg) - LG::first_warp(ur % rsg);
+                // every partial loaded at once (independent loads), then added in warp order
+                float gp[LG::WPR], up[LG::WPR];
+#pragma unroll
+                for (int ww = 0; ww < LG::WPR; ++ww) {
+                    gp[ww] = ww <= ng ? pbuf[row * LG::WPR + ww] : 0.f;
+                    up[ww] = ww <= nu ? pbuf[ur * LG::WPR + ww] : 0.f;
                 }
-            } else {
-                using LD = LaneMap<II, NWC, PD>;
-                const int r0 = lane % rsd;
-                const int nw = LD::last_warp(r0) - LD::first_warp(r0);
-                for (int ww = 0; ww <= nw; ++ww) val += pbuf[lane * LD::WPR + ww];
+                float gs = 0.f, us = 0.f;
+#pragma unroll
+                for (int ww = 0; ww < LG::WPR; ++ww) {
+                    gs += gp[ww];
+                    us += up[ww];
+                }
+                val = silu_clamped(gs, us, a.limit);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(empty0 + 8u * s);  // partials read: the stage may refill
+            if (lane == 0) mbar_arrive(empty0 + 8u * s);  // stage read: it may refill
             if (++s == S) { s = 0; ph ^= 1u; }
-            if (gu) {
+            if (sg.gu) {
                 // rows j*8 .. j*8+7 of the unit land on lanes j*8 .. j*8+7
-                const int j = it % TPU;
                 const float v = __shfl_sync(0xffffffffu, val, lane & (TRG - 1));
-                if ((lane / TRG) == j) hv = v;
-                if (j == TPU - 1) {
-                    const Item u = item_of(c + (it / TPU) * G, NU);
-                    const int st = slot_store(u.slot);
-                    quantise_unit(hv, a.hq + (int64_t)st * HQ_BYTES, I, u.idx, lane);
+                if ((lane / TRG) == sg.j) hv = v;
+                if (sg.j == TPU - 1) {
+                    quantise_unit(hv, s_h + (sg.m & 1) * 20, lane);
                     __syncwarp();
-                    if (lane == 0) red_release_add(a.sync + kSyncSlot + st, 1);
-                }
-            } else {
-                const int nsl = nsr + 1;
-                const int v = w.R.at(it - w.n_gu), rt = v / nsl;
-                const int slot = down_slot(v % nsl, nsr);
-                const int j = rt * TRD + lane;
-                const int tb = rt * nsl, te = tb + nsl;
-                if (tb >= w.R.v0) {
-                    // this CTA holds the tile's last walked position (q = 0): it
-                    // writes y, with the slots other CTAs computed (positions
-                    // [v1, te), walked early by them) read as tagged words
-                    s_dv[(slot < 0 ? nsr : slot) * 32 + lane] = val;
-                    if (v == tb) {
-                        if (te > w.R.v1) {
-                            uint32_t n = 0;
-                            for (; n < a.spin_limit; ++n) {
-                                bool got = true;
-                                for (int base = w.R.v1; base < te; base += 8) {  // 8 loads in flight
-                                    unsigned long long wd[8];
-#pragma unroll
-                                    for (int i = 0; i < 8; ++i)
-                                        wd[i] = base + i < te ? ld_relaxed64(a.dx + (int64_t)slot_store(down_slot(base + i - tb, nsr)) * H + j)
-                                                              : (unsigned long long)tag << 32;
-#pragma unroll
-                                    for (int i = 0; i < 8; ++i) {
-                                        got &= (uint32_t)(wd[i] >> 32) == tag;
-                                        if (base + i < te) {
-                                            const int sl = down_slot(base + i - tb, nsr);
-                                            s_dv[(sl < 0 ? nsr : sl) * 32 + lane] = __uint_as_float((uint32_t)wd[i]);
-                                        }
-                                    }
-                                }
-                                if (__all_sync(0xffffffffu, got)) break;
-                                __nanosleep(64);
-                            }
-                            if (n == a.spin_limit && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-                        }
-                        __syncwarp();
-                        // y[t] = sum over t's slots of w * D in pick order
-                        // (+ the shared expert for own_tok), model.cpp:741-755
-                        for (int t = 0; t < NT; ++t) {
-                            float y = 0.f;
-                            for (int k = s_first[t]; k < s_first[t + 1]; ++k) y = fmaf(s_sw[k], s_dv[k * 32 + lane], y);
-                            if (t == a.own_tok) y += s_dv[nsr * 32 + lane];
-                            a.y[(int64_t)t * H + j] = y;
-                        }
-                        __syncwarp();
-                    }
-                } else {
-                    // the CTA before this one finishes the tile
-                    st_relaxed64(a.dx + (int64_t)slot_store(slot) * H + j,
-                                 ((unsigned long long)tag << 32) | __float_as_uint(val));
+                    if (lane == 0) mbar_arrive(hbar0 + 8u * (sg.m & 1));
                 }
             }
         }
-        if (lane == 0) GP_STAMP(7);
     } else {
         // ================= compute warps =================
         // router weights of this warp's first slice: independent of the
@@ -840,7 +724,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         };
         if (warp < n_tasks) load_router(warp);
         pdl_wait();
-        if (tid == 0) GP_STAMP(0);
 
         // ---- router slices of this CTA's experts: warp task = (expert, slice),
         // one dot product per token ----
@@ -872,94 +755,93 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         }
 
         if (!mbar_wait(tbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-        int s = 0;
+        const auto mg = lane_map<HH, NWC, PG>(warp, lane, stage0);
+        const int gl = warp * 32 + lane;  // this lane's two rows of a down chunk: 2gl, 2gl+1
+        uint32_t xq[16], hq[16];
+        int cur = -1;  // the token whose activations xq holds for gate/up
+        float sx4 = 0.f, hs = 0.f;
+        int tok0 = 0, tok1 = 0;  // token and weight of the two items in flight (by parity)
+        float wk0 = 1.f, wk1 = 1.f;
+        int s = 0, n = 1;
         uint32_t ph = 0;
         bool have = false;
-        Work w{};
-        // the slot list (routed slot count, slot tokens) once the top-k is in
-        auto wait_slots = [&]() -> bool {
-            if (!mbar_wait(topk_bar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            if (warp_aborted(s_abort)) return false;
-            w = work_of(c, G, *s_nsr, NU, TD);
-            have = true;
-            return true;
+        auto give_up = [&]() {
+            if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         };
-        // ---- gate/up tiles: warps 0..NWG-1; warp 0 also arrives for the
-        // others, which sleep until the down phase ----
-        if (warp < NWG) {
-            const auto mg = lane_map<HH, NWG, PG>(warp, lane, stage0);
-            uint32_t xq[16];
-            int cur = a.own_tok;  // the token whose activations xq holds (the shared expert's first)
-            float sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
-            for (int it = 0;; ++it) {
-                if (!have && it >= n_shared && !wait_slots()) break;
-                if (have && it >= w.n_gu) break;
-                if (it % TPU == 0 && NT > 1) {  // a new unit: its slot's token
-                    const Item u = item_of(c + (it / TPU) * G, NU);
-                    const int tk = u.slot < 0 ? a.own_tok : s_st[u.slot];
-                    if (tk != cur) {
-                        cur = tk;
-                        sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
-                    }
+        for (int t = 0;; ++t) {
+            if (!have && (t >= TPU || c >= NU)) {  // routed items (and every down chunk) come after the routing
+                if (!__all_sync(0xffffffffu, mbar_wait(topk_bar, 0, a.spin_limit))) { give_up(); break; }
+                n = items_of(c, G, NU * (min(max(*s_nsr, 0), kDecodeMaxRouted) + 1));
+                have = true;
+            }
+            if (have && t >= n * (TPU + NCH)) break;
+            const Stage sg = stage_of(t, n, NCH);
+            const int p = sg.m & 1;
+            if (sg.gu && sg.j == 0) {  // a new item: its token and weight; that token's activations
+                int slot, unit, e, tok;
+                item_at(sg.m, slot, unit, e, tok);
+                const float wk = slot < 0 ? 1.0f : s_sw[slot];
+                if (p) { tok1 = tok; wk1 = wk; } else { tok0 = tok; wk0 = wk; }
+                if (tok != cur) {
+                    cur = tok;
+                    sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
                 }
-                if (warp_aborted(s_abort)) break;
-                if (!mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-                if (warp_aborted(s_abort)) break;
-                if (tid == 0 && it == n_shared) GP_STAMP(3);
-                consume<HH, NWG, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
-                __syncwarp();
-                if (lane == 0) mbar_arrive_cnt(pdone0 + 8u * s, warp == 0 ? 1 + NWC - NWG : 1);
-                if (++s == S) { s = 0; ph ^= 1u; }
             }
-            if (warp == 0 && lane == 0) mbar_arrive(gbar);
-        } else {
-            // once warp 0 has passed every gate/up stage, the first down
-            // stage is at most one phase ahead of its parity wait
-            if (!mbar_wait_sleepy(gbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-            if (wait_slots()) {
-                s = w.n_gu % S;
-                ph = (uint32_t)(w.n_gu / S) & 1u;
-            }
-        }
-        if (tid == 0) GP_STAMP(4);
-        // ---- down tiles: the activations come with the tile ----
-        if (have) {
-            const auto md = lane_map<II, NWC, PD>(warp, lane, stage0);
-            for (int it = w.n_gu; it < w.n_items; ++it) {
-                if (warp_aborted(s_abort)) break;
-                if (!mbar_wait(full0 + 8u * s, ph, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
-                if (warp_aborted(s_abort)) break;
-                if (tid == 0 && it == w.n_gu) GP_STAMP(5);
-                const uint32_t xb = stage0 + s * L.stage_bytes + DN_BYTES;
-                uint32_t xq[16];
+            if (!sg.gu && sg.j == 0) {  // the item's quantised h (double-buffered by item parity), once
+                if (!__all_sync(0xffffffffu, mbar_wait(hbar0 + 8u * p, (uint32_t)(sg.m >> 1) & 1u, a.spin_limit))) {
+                    give_up();
+                    break;
+                }
+                const uint32_t hb = smem_u32(s_h + p * 20);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    const uint4 v = lds128(xb + i * (NU * 16u) + md.sb * 16u);
-                    xq[4 * i] = v.x;
-                    xq[4 * i + 1] = v.y;
-                    xq[4 * i + 2] = v.z;
-                    xq[4 * i + 3] = v.w;
+                    const uint4 v = lds128(hb + 16u * i);
+                    hq[4 * i] = v.x;
+                    hq[4 * i + 1] = v.y;
+                    hq[4 * i + 2] = v.z;
+                    hq[4 * i + 3] = v.w;
                 }
-                const float sx4 = ldsf(xb + 2u * I + md.sb * 4u);
-                consume<II, NWC, PD, RPWD>(md, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
+                hs = ldsf(hb + 64u);
+            }
+            if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, ph, a.spin_limit))) { give_up(); break; }
+            if (sg.gu) {
+                consume<HH, NWC, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
                 __syncwarp();
                 if (lane == 0) mbar_arrive(pdone0 + 8u * s);
-                if (++s == S) { s = 0; ph ^= 1u; }
+            } else {
+                // split-K down: rows 4gl .. 4gl+3 of chunk j, this item's 32 input columns
+                const uint32_t sb = stage0 + s * L.stage_bytes;
+                const uint4 q01 = lds128(sb + 32u * gl), q23 = lds128(sb + 32u * gl + 16u);
+                const uint4 ax = lds128(sb + RC * 8u + 16u * gl);
+                const uint2 dd = lds64(sb + RC * 12u + 8u * gl);
+                float v[4];
+                uint32_t sw[8];
+                const uint32_t qa[4] = {q01.x, q01.z, q23.x, q23.z}, qb[4] = {q01.y, q01.w, q23.y, q23.w};
+                const uint32_t aw[4] = {ax.x, ax.y, ax.z, ax.w}, dw[4] = {dd.x & 0xFFFFu, dd.x >> 16, dd.y & 0xFFFFu, dd.y >> 16};
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    iq3_decode_sub32(nullptr, qa[r], qb[r], aw[r], lane * 4u, sw);
+                    const float dr = __half2float(__ushort_as_half((unsigned short)dw[r]));
+                    v[r] = (float)(iq3_idot<8>(sw, hq) * iq3_oddscale(aw[r])) * (dr * hs);
+                }
+                // the stage is read: release it first, then send the sums
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pdone0 + 8u * s);
+                const float wk = p ? wk1 : wk0;
+                red_add_v4(a.y + (int64_t)(p ? tok1 : tok0) * H + sg.j * RC + 4 * gl, wk * v[0], wk * v[1], wk * v[2],
+                           wk * v[3]);
             }
+            if (++s == S) { s = 0; ph ^= 1u; }
         }
-        if (tid == 0) GP_STAMP(6);
     }
 
-    // the last CTA out clears the counters that are waited on
+    // the last CTA out advances the launch generation (the tag of the next
+    // launch's exchanged words)
     named_bar_sync(1, (NWC + 1) * 32);
     if (tid == 0) {
-        GP_STAMP(8);
         fence_acq_rel_gpu();
         if (atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1) {
             a.sync[kSyncGen] += 1u;
-            const int nsr = min(max(*s_nsr, 0), kDecodeMaxRouted);
-            for (int k = 0; k < nsr; ++k) a.sync[kSyncSlot + k] = 0;
-            a.sync[kSyncSlot + kSharedStore] = 0;
             fence_acq_rel_gpu();
             a.sync[kSyncEnd] = 0;
         }
@@ -971,30 +853,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared) {
     if (E > kMaxEFused || E < K) return false;
     // the instantiated work mapping: gate/up 20 warps over 4 rows of H = 5120
-    // (4 passes), down 24 warps over 16 rows of I = 1536 (2 passes, rows
-    // straddle warps)
+    // (4 passes), down chunks of 1280 rows
     return H == 5120 && I == 1536 && K >= 1 && K <= MAXK && with_shared == 1;
 }
 
-size_t decode_layer_smem(int H, int I, int stages, int n_tok, int max_routed) {
-    return decode_smem(H, I, stages, n_tok, max_routed).total;
-}
+size_t decode_layer_smem(int H, int I, int stages, int n_tok) { return decode_smem(H, I, stages, n_tok).total; }
 
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st) {
     if (!decode_layer_supported(a.H, a.I, a.E, a.K, a.with_shared)) return cudaErrorInvalidValue;
     if (grid * kMaxOwned < a.E) return cudaErrorInvalidValue;  // router experts per CTA
     if (a.n_tok < 1 || a.n_tok > kDecodeMaxTokens || a.n_tok * a.K > kDecodeMaxRouted || a.own_tok < 0 ||
         a.own_tok >= a.n_tok || a.e_lo < 0 || a.e_cnt < 0 || a.e_lo + a.e_cnt > a.E || a.E >= 65536 ||
-        (a.n_tok > 1 && !a.picks))
+        (a.n_tok > 1 && !a.picks) || !a.down_col || (reinterpret_cast<uintptr_t>(a.y) & 15))
         return cudaErrorInvalidValue;
     if (a.n_tok == 1 && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // one token: every expert
-    // down-range weights in 32-bit: grid * (units * 42 + tiles * 10) < 2^31
-    const int64_t slots = (int64_t)a.n_tok * a.K + 1;
-    if ((int64_t)grid * ((int64_t)(a.I / UNIT) * slots * 42 + (int64_t)(a.H / TRD) * slots * 10) >= (1ll << 31))
-        return cudaErrorInvalidValue;
-    const Smem L = decode_smem(a.H, a.I, a.stages, a.n_tok, a.n_tok * a.K);
+    const Smem L = decode_smem(a.H, a.I, a.stages, a.n_tok);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
-    auto kern = decode_layer_kernel<5120, 1536, 4, 1, 2, 2>;
+    auto kern = decode_layer_kernel<5120, 1536, 4, 1>;
     static std::atomic<unsigned long long> configured{0};  // per device
     if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured)) return e0;
     // Co-residency: every CTA waits on data the others publish, so the grid

@@ -78,6 +78,14 @@ cudaError_t build_tables(uint8_t* dst, cudaStream_t st);
 // Raw GGUF IQ3_XXS rows -> repacked row groups (and back, for verification).
 cudaError_t launch_repack(const uint8_t* raw, uint8_t* packed, int64_t rows, int in_dim, cudaStream_t st);
 cudaError_t launch_unpack(const uint8_t* packed, uint8_t* raw, int64_t rows, int in_dim, cudaStream_t st);
+// Column-slab layout of a down projection (rows = H outputs, in_dim = I inputs):
+// per matrix, for each 32-input unit u: [qs rows x 8 B][aux rows x 4 B], then
+// for each 256-input block b: [d rows x 2 B].  The same 98 bytes per 256
+// weights as GGUF; a unit's slab of every row is contiguous, so one work item
+// of the persistent decode kernel streams the down columns of its 32 h values
+// in whole runs.  n_mat matrices of raw row-major blocks, stacked.
+cudaError_t launch_repack_cols(const uint8_t* raw, uint8_t* cols, int64_t n_mat, int rows, int in_dim,
+                               cudaStream_t st);
 
 // Bit-exact IQ3_XXS -> fp32 (raw GGUF blocks).
 cudaError_t launch_dequantize(const uint8_t* raw, float* dst, int64_t nblocks, cudaStream_t st);
@@ -157,10 +165,10 @@ cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl);
 struct DecodeLayerArgs {
     const float* router;       // [E][H] fp32
     const float* corr;         // [E] or nullptr
-    const uint8_t* gate;       // repacked, experts 0..E-1 then the shared expert at E
+    const uint8_t* gate;       // repacked row groups, routed experts held then the shared expert
     const uint8_t* up;
-    const uint8_t* down;
-    int64_t gu_stride, d_stride;
+    const uint8_t* down_col;   // the down projections in the column-slab layout (launch_repack_cols)
+    int64_t gu_stride, dc_stride;  // bytes per expert
     int H, I, E, K;
     float routed_scale;
     int norm_topk;
@@ -183,11 +191,7 @@ struct DecodeLayerArgs {
     int own_tok;               // token whose shared expert runs in this launch
     unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
     unsigned long long* picks;   // [decode_layer_pick_words()] top-k picks of each token, tagged (n_tok > 1)
-    float* h;                  // unused (multi-kernel path scratch)
-    uint8_t* hq;               // [kDecodeSlots][decode_layer_hq_bytes(I)] h quantised per 32-unit
-    float* D;                  // unused (multi-kernel path scratch)
-    unsigned long long* dx;    // [kDecodeSlots][H] down rows of tiles split between CTAs, tagged like logits
-    unsigned* sync;            // [kDecodeSyncWords] counters, zero between launches
+    unsigned* sync;            // [kDecodeSyncWords] launch generation and finished-CTA count
     const uint8_t* tables;
     uint32_t* status;
     int stages;
@@ -229,16 +233,11 @@ cudaError_t launch_ep_pack(const void* x, int x_bf16, int H, int n, int K, const
 // Counter words of the persistent kernel: the generation counts launches, the
 // others are zero between launches; the host clears all of them (and the
 // tagged buffers) after a launch that reported an error.
-constexpr int kSyncGen = 0;                     // launch generation (tags exchanged logits and rows)
+constexpr int kSyncGen = 0;                     // launch generation (tags exchanged logits and picks)
 constexpr int kSyncEnd = 1;                     // CTAs finished
-constexpr int kSyncSlot = 8;                    // [kDecodeSlots] h units quantised per slot
 constexpr int kDecodeMaxTokens = 8;             // tokens per launch of the persistent kernel
 constexpr int kDecodeMaxRouted = 64;            // routed (token, expert) slots per launch
-constexpr int kDecodeSlots = kDecodeMaxRouted + 1;  // + the shared expert's, stored last
-constexpr int kDecodeSyncWords = 128;
-static_assert(kSyncSlot + kDecodeSlots <= kDecodeSyncWords, "slot counters past the counter block");
-// h[slot] as int16 pairs (I*2 bytes) followed by one fp32 scale per 32-unit.
-inline size_t decode_layer_hq_bytes(int I) { return (size_t)I * 2 + (size_t)(I / 32) * 4; }
+constexpr int kDecodeSyncWords = 64;
 // Words of DecodeLayerArgs::logits, one word per 256-byte line: 8 replicas of
 // E tagged logits (one token: every CTA reads them), or one copy per token
 // (several tokens: one CTA reads each token's).
@@ -246,9 +245,8 @@ inline size_t decode_layer_logit_words(int E) { return (size_t)8 * E * 32; }
 // Words of DecodeLayerArgs::picks: 8 replicas x kDecodeMaxTokens x 32 picks, one per 256-byte line.
 inline size_t decode_layer_pick_words() { return (size_t)8 * kDecodeMaxTokens * 32 * 32; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
-// Dynamic shared memory of a launch: `stages` pipeline stages, n_tok tokens
-// and at most max_routed routed slots.
-size_t decode_layer_smem(int H, int I, int stages, int n_tok, int max_routed);
+// Dynamic shared memory of a launch: `stages` pipeline stages, n_tok tokens.
+size_t decode_layer_smem(int H, int I, int stages, int n_tok);
 cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t st);
 
 // ---- codecs.cu: the other GGUF codecs (quant.cpp:130-573), bit-exact ----

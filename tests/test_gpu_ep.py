@@ -229,7 +229,8 @@ def test_decode_partial_crowded_rank_and_limits():
     """Every pick of 8 tokens forced onto one rank's experts: that rank runs the
     most slots a launch takes (64 routed + its shared expert), the others only
     their shared expert.  Also the single-token form (every expert held) equals
-    gpeed_moe_forward bit for bit, and out-of-range arguments are refused."""
+    gpeed_moe_forward (to rounding: the sums into y land in launch order), and
+    out-of-range arguments are refused."""
     from gpeed_b200 import GpeedError
     ctx = Context(0)
     try:
@@ -248,7 +249,7 @@ def test_decode_partial_crowded_rank_and_limits():
         assert rel_l2(y_ep.cpu().numpy(), y_ref.cpu().numpy()) < 1e-5
         one = full.decode_partial(X[:1], 0)
         ctx.check()
-        np.testing.assert_array_equal(one.cpu().numpy(), full.forward(X[:1]).cpu().numpy())
+        assert rel_l2(one.cpu().numpy(), full.forward(X[:1]).cpu().numpy()) < 1e-6
         with pytest.raises(GpeedError):
             parts[0].decode_partial(torch.zeros(9, cfg.hidden, dtype=torch.bfloat16, device="cuda"), 0)
         with pytest.raises(GpeedError):

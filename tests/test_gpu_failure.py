@@ -7,7 +7,7 @@ status word and the kernel finishes with invalid results, so the context
 stays usable.  The test makes one such wait run out on purpose with a short
 limit and a flag that nothing sets (the test-only option that withholds one
 router logit), checks that gpeed_ctx_check reports and clears it, and that the
-next forward gives the same bits as before.  The reference has no device and
+next forward gives the same result as before.  The reference has no device and
 only throws (weights.cpp:21,25)."""
 import re
 
@@ -17,7 +17,7 @@ import torch
 
 from gpeed_b200 import Context, GpeedError, MoeConfig, MoeLayer
 from gpeed_b200 import _capi
-from tests.helpers import host_layer
+from tests.helpers import host_layer, rel_l2
 
 pytestmark = pytest.mark.gpu
 
@@ -46,7 +46,7 @@ def test_fused_wait_that_runs_out_is_reported_and_recovered():
     for _ in range(2):
         y = layer.forward(x)
         ctx.check()
-        np.testing.assert_array_equal(y.cpu().numpy(), y_ok.cpu().numpy())
+        assert rel_l2(y.cpu().numpy(), y_ok.cpu().numpy()) < 1e-6  # sums into y in launch order: to rounding
     with pytest.raises(GpeedError):
         ctx.set_option(_capi.OPT_SPIN_LIMIT, 0)
     ctx.close()
