@@ -68,6 +68,8 @@ SIGNATURES = {
     "gpeed_matvec_quant": [_vp, _i, _u64, _i, _i, _vp, _vp, _vp],
     "gpeed_matmul_quant": [_vp, _i, _u64, _i, _i, _vp, _i, _vp, _vp],
     "gpeed_matmul_quant_noalloc": [_vp, _i, _u64, _i, _i, _vp, _i, _vp, _vp],
+    "gpeed_matvec_quant_host": [_vp, _i, _u64, _i, _i, _vp, _vp],
+    "gpeed_matmul_quant_host": [_vp, _i, _u64, _i, _i, _vp, _i, _vp],
     "gpeed_moe_load_layer": [_vp, _i, ctypes.POINTER(MoeShape), _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i],
     "gpeed_moe_synth_layer": [_vp, _i, ctypes.POINTER(MoeShape), _vp, _vp, _i, _u64, _u64],
     "gpeed_synth_iq3xxs": [_vp, _u64, _u64, _u64, _u64, _vp],

@@ -122,6 +122,12 @@ struct gpeed_ctx {
     // pinned staging ring for weight uploads from pageable host memory
     uint8_t* stage[4] = {};
     cudaEvent_t stage_ev[4] = {};
+    // host-pointer matvec/matmul: pinned in/out staging, device buffers, own stream
+    std::mutex host_mu;
+    float* host_pin = nullptr;
+    size_t host_pin_n = 0;
+    DevBuf<float> host_x, host_y;
+    cudaStream_t host_stream = nullptr;
 };
 
 int gp::set_error(int code, const std::string& msg) {
@@ -666,6 +672,10 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
         if (c->stage[i]) cudaFreeHost(c->stage[i]);
         if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
     }
+    if (c->host_pin) cudaFreeHost(c->host_pin);
+    c->host_x.release();
+    c->host_y.release();
+    if (c->host_stream) cudaStreamDestroy(c->host_stream);
     delete c;
     return GPEED_OK;
 }
@@ -808,6 +818,42 @@ int gpeed_matmul_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int 
 int gpeed_matvec_quant(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* x, float* dst,
                        void* stream) {
     return gpeed_matmul_quant(c, handle, row0, in_dim, out_dim, x, 1, dst, stream);
+}
+
+int gpeed_matmul_quant_host(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* X,
+                            int n_tok, float* Y) {
+    if (!c || handle < 0 || handle >= (int)c->tensors.size()) return fail(GPEED_ERR_INVALID, "bad handle");
+    if (n_tok <= 0 || out_dim <= 0) return GPEED_OK;  // weights.cpp:88
+    if (!X || !Y) return fail(GPEED_ERR_INVALID, "X and Y must be host buffers");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    std::lock_guard<std::mutex> lock(c->host_mu);
+    if (!c->host_stream) GP_CUDA(cudaStreamCreateWithFlags(&c->host_stream, cudaStreamNonBlocking));
+    const size_t nx = (size_t)n_tok * in_dim, ny = (size_t)n_tok * out_dim;
+    if (c->host_pin_n < nx + ny) {
+        if (c->host_pin) cudaFreeHost(c->host_pin);
+        c->host_pin = nullptr;
+        c->host_pin_n = 0;
+        GP_CUDA(cudaHostAlloc(&c->host_pin, (nx + ny) * sizeof(float), cudaHostAllocDefault));
+        c->host_pin_n = nx + ny;
+    }
+    if ((rc = c->host_x.ensure(nx)) || (rc = c->host_y.ensure(ny))) return rc;
+    cudaStream_t st = c->host_stream;
+    std::memcpy(c->host_pin, X, nx * sizeof(float));
+    GP_CUDA(cudaMemcpyAsync(c->host_x.p, c->host_pin, nx * sizeof(float), cudaMemcpyHostToDevice, st));
+    if ((rc = gpeed_matmul_quant(c, handle, row0, in_dim, out_dim, c->host_x.p, n_tok, c->host_y.p, st))) return rc;
+    GP_CUDA(cudaMemcpyAsync(c->host_pin + nx, c->host_y.p, ny * sizeof(float), cudaMemcpyDeviceToHost, st));
+    GP_CUDA(cudaStreamSynchronize(st));
+    std::memcpy(Y, c->host_pin + nx, ny * sizeof(float));
+    uint32_t dev_status = 0;
+    GP_CUDA(cudaMemcpy(&dev_status, c->status, sizeof(dev_status), cudaMemcpyDeviceToHost));
+    if (dev_status) return gpeed_ctx_check(c, st);  // reports and clears it
+    return GPEED_OK;
+}
+
+int gpeed_matvec_quant_host(gpeed_ctx* c, int handle, uint64_t row0, int in_dim, int out_dim, const float* x,
+                            float* dst) {
+    return gpeed_matmul_quant_host(c, handle, row0, in_dim, out_dim, x, 1, dst);
 }
 
 int gpeed_moe_load_layer_range(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int expert_begin, int expert_count,

@@ -2,7 +2,8 @@
 // ABI (include/gpeed_moe.h).  A glm5::WeightStore user swaps
 //   store.matvec_quant(name, row0, in_dim, out_dim, x, dst)
 // (reference cpp/core/include/glm5/weights.h:38-48) for the same call on
-// gpeed::WeightStore, with x/dst in device memory.  Non-zero status codes
+// gpeed::WeightStore, with the same host buffers (matvec_quant_device and
+// matmul_quant_device take device buffers and a stream).  Non-zero status codes
 // become std::runtime_error carrying gpeed_last_error(), as the reference
 // throws (weights.cpp:170-174, quant.cpp:523-554).  Header-only; link
 // libgpeed_moe.so.
@@ -67,16 +68,30 @@ public:
     }
     bool has(const std::string& name) const { return handles_.count(name) != 0; }
 
-    // weights.h:38-41
-    void matvec_quant(const std::string& name, uint64_t row0, int in_dim, int out_dim, const float* x, float* dst,
-                      void* stream = nullptr) {
-        check(gpeed_matvec_quant(ctx_, handle(name), row0, in_dim, out_dim, x, dst, stream));
+    // weights.h:38-41 and weights.h:43-48, with the reference's calling
+    // convention: x / X and dst / Y are host buffers (its callers pass
+    // std::vector data, model.cpp:733-754, model_batch.cpp:241-279) and the
+    // call returns with dst / Y filled.  Throws like the reference.
+    void matvec_quant(const std::string& name, uint64_t row0, int in_dim, int out_dim, const float* x, float* dst) {
+        check(gpeed_matvec_quant_host(ctx_, handle(name), row0, in_dim, out_dim, x, dst));
     }
-    // weights.h:43-48
     void matmul_quant(const std::string& name, uint64_t row0, int in_dim, int out_dim, const float* X, int n_tok,
-                      float* Y, void* stream = nullptr) {
-        check(gpeed_matmul_quant(ctx_, handle(name), row0, in_dim, out_dim, X, n_tok, Y, stream));
+                      float* Y) {
+        check(gpeed_matmul_quant_host(ctx_, handle(name), row0, in_dim, out_dim, X, n_tok, Y));
     }
+
+    // The same on device buffers, asynchronous on `stream` (an engine that
+    // keeps its activations on the GPU; device-side faults surface at
+    // check_device()).
+    void matvec_quant_device(const std::string& name, uint64_t row0, int in_dim, int out_dim, const float* x_dev,
+                             float* dst_dev, void* stream = nullptr) {
+        check(gpeed_matvec_quant(ctx_, handle(name), row0, in_dim, out_dim, x_dev, dst_dev, stream));
+    }
+    void matmul_quant_device(const std::string& name, uint64_t row0, int in_dim, int out_dim, const float* X_dev,
+                             int n_tok, float* Y_dev, void* stream = nullptr) {
+        check(gpeed_matmul_quant(ctx_, handle(name), row0, in_dim, out_dim, X_dev, n_tok, Y_dev, stream));
+    }
+    void check_device(void* stream = nullptr) { check(gpeed_ctx_check(ctx_, stream)); }
 
 private:
     int handle(const std::string& name) {

@@ -160,6 +160,18 @@ GPEED_API int gpeed_matvec_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int 
 GPEED_API int gpeed_matmul_quant(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim, const float* X_dev,
                        int n_tok, float* Y_dev, void* stream);
 
+/* The same two calls on HOST buffers, with the reference's calling convention
+ * (WeightStore::matvec_quant / matmul_quant, weights.h:38-48, whose callers
+ * pass std::vector data, model.cpp:733-754 and model_batch.cpp:241-279): x /
+ * X are read and dst / Y written in host memory, and the call returns when
+ * dst / Y hold the result.  Staged through pinned buffers on a stream of the
+ * context (one host thread at a time per context); device-side errors are
+ * reported here, as the reference throws inside the call. */
+GPEED_API int gpeed_matvec_quant_host(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim,
+                                      const float* x_host, float* dst_host);
+GPEED_API int gpeed_matmul_quant_host(gpeed_ctx* ctx, int handle, uint64_t row0, int in_dim, int out_dim,
+                                      const float* X_host, int n_tok, float* Y_host);
+
 /* Same result as gpeed_matmul_quant (bit for bit: the same kernels on the same
  * work list), for callers that cannot call cudaMalloc once they are serving:
  * an engine whose own allocator or memory pool owns the GPU's memory, a

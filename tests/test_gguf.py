@@ -284,13 +284,19 @@ int main(int argc, char** argv) {
     try {
         gpeed::GgufModel model(argv[1]);
         gpeed::WeightStore store(model, 0);
+        // the reference's call on host buffers (model.cpp:733)
+        store.matvec_quant("blk.4.ffn_gate_exps.weight", 3 * I, H, I, x.data(), y.data());
+        // and the device variant gives the same bits
         float *xd, *yd;
+        std::vector<float> y2(I);
         cudaMalloc(&xd, 4 * H); cudaMalloc(&yd, 4 * I);
         cudaMemcpy(xd, x.data(), 4 * H, cudaMemcpyHostToDevice);
-        store.matvec_quant("blk.4.ffn_gate_exps.weight", 3 * I, H, I, xd, yd);   // model.cpp:733
-        cudaMemcpy(y.data(), yd, 4 * I, cudaMemcpyDeviceToHost);
+        store.matvec_quant_device("blk.4.ffn_gate_exps.weight", 3 * I, H, I, xd, yd);
+        cudaMemcpy(y2.data(), yd, 4 * I, cudaMemcpyDeviceToHost);
+        store.check_device();
+        if (y2 != y) return 5;
         try {
-            store.matvec_quant("blk.4.no_such.weight", 0, H, I, xd, yd);
+            store.matvec_quant("blk.4.no_such.weight", 0, H, I, x.data(), y.data());
             return 4;
         } catch (const std::runtime_error&) {
         }

@@ -1,9 +1,10 @@
 """mHC residual mixing + RMSNorm around the MoE layer (gpeed_b200/csrc/mhc.cu)
 against the C oracle's restatement of Model::hc_forward (model.cpp:205-263),
 the ffn RMSNorm (model.cpp:292-296) and the stream update (model.cpp:309-318).
-The reference computes these in private Model methods that need a full GGUF
-model, so the oracle restatement is not pinned to reference outputs; it is
-checked here for the properties the construction guarantees."""
+The oracle restatement is pinned to the reference engine's own
+Model::hc_forward in tests/test_ref_model.py (outputs recorded from the
+engine on GGUF files); here it is also checked for the properties the
+construction guarantees, and the device path against it at more shapes."""
 import numpy as np
 import pytest
 
