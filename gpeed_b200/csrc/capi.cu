@@ -111,7 +111,7 @@ struct gpeed_ctx {
     int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
-    DevBuf<unsigned long long> logits, picks;
+    DevBuf<unsigned long long> logits, picks, hx;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
     bool prof = false;
@@ -478,6 +478,9 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     const size_t had_p = c->picks.n;
     if ((rc = c->picks.ensure(gp::decode_layer_pick_words()))) return rc;
     if (c->picks.n != had_p) GP_CUDA(cudaMemsetAsync(c->picks.p, 0, c->picks.n * sizeof(unsigned long long), st));
+    const size_t had_h = c->hx.n;
+    if ((rc = c->hx.ensure(gp::decode_layer_h_words(I)))) return rc;
+    if (c->hx.n != had_h) GP_CUDA(cudaMemsetAsync(c->hx.p, 0, c->hx.n * sizeof(unsigned long long), st));
     gp::DecodeLayerArgs& da = *out;
     da = gp::DecodeLayerArgs{};
     da.router = L.router;
@@ -508,6 +511,7 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     da.own_tok = own_tok;
     da.logits = c->logits.p;
     da.picks = c->picks.p;
+    da.hx = c->hx.p;
     da.sync = c->sync;
     da.tables = c->tables;
     da.status = c->status;
@@ -662,6 +666,7 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
         if (e) cudaEventDestroy(e);
     c->logits.release();
     c->picks.release();
+    c->hx.release();
     c->xp.release();
     c->route_chunks.release();
     c->mhc_partial.release();
@@ -694,6 +699,7 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
         GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));
         if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
         if (c->picks.p) GP_CUDA(cudaMemset(c->picks.p, 0, c->picks.n * sizeof(unsigned long long)));
+        if (c->hx.p) GP_CUDA(cudaMemset(c->hx.p, 0, c->hx.n * sizeof(unsigned long long)));
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape, 16: a token or h value past the fp16 range "
                                       "on the tensor-core path)", st);

@@ -80,7 +80,6 @@ constexpr int RSPLIT = 8;        // router slices per expert
 constexpr int MAXK = 31;         // picks per token
 constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
 constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
-constexpr int kPrefetch = 4;     // stages prefetched into L2 beyond the shared-memory ring
 // Tagged logits: with one token every CTA polls all E of them, so one array
 // would send every poll of every CTA to the few L2 slices holding it.  Each
 // logit is then stored in kLogitCopies replicas, one word per 256-byte line;
@@ -101,11 +100,6 @@ GP_DEVINL unsigned ld_relaxed(const unsigned* p) {
     unsigned v;
     asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
-}
-
-// Prefetch `bytes` at p into L2 (no completion to wait for).
-GP_DEVINL void prefetch_l2(const void* p, uint32_t bytes) {
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // y[0..3] += v as one fire-and-forget vector reduction: no value comes
@@ -387,34 +381,42 @@ __host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok) {
     return L;
 }
 
-// Items i = c, c+G, c+2G, ... below total.
-GP_DEVINL int items_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
+// Jobs k = c, c+G, c+2G, ... below total: count of CTA c's.
+GP_DEVINL int jobs_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
 
-// Stage t of a CTA with n items, in the order GU(0) GU(1) DN(0) GU(2) DN(1)
-// ... GU(n-1) DN(n-2) DN(n-1): item m, its tile or chunk j, gate/up or down.
-struct Stage {
-    int m, j;
+// One pipeline stage of work.  Job k of a launch, in the order: the shared
+// expert's gate/up tiles (ngs = NU * TPU of them; no routing needed), the
+// routed slots' gate/up tiles (ngr = slots * NU * TPU), the shared expert's
+// down chunks (NU * NCH), the routed slots' down chunks (slots * NU * NCH).  A
+// gate/up tile (slot, unit, j < TPU) gives h rows unit*32 + j*8 .. +7; a down
+// chunk (slot, unit, j < NCH) adds the unit's 32 input columns into output
+// rows j*RC .. +RC-1 and needs the unit's 32 h rows, which tiles earlier in
+// the order (on any CTA) produced.
+struct Job {
     bool gu;
+    int slot, unit, j;  // slot -1: the shared expert
 };
-GP_DEVINL Stage stage_of(int t, int n, int nch) {
-    if (t < TPU) return {0, t, true};
-    const int r = t - TPU, per = TPU + nch, m = r / per + 1;
-    if (m < n) {
-        const int k = r - (m - 1) * per;
-        return k < TPU ? Stage{m, k, true} : Stage{m - 1, k - TPU, false};
+// (Every division is by a compile-time constant: the producer decodes a job on
+// its critical path, sharing issue slots with the compute warps.)
+template <int NU, int NCH>
+GP_DEVINL Job job_of(int k, int nsr) {
+    constexpr int GS = NU * TPU, DS = NU * NCH;  // jobs per slot, each kind
+    const int cyc = GS * (nsr + 1);
+    if (k < cyc) {
+        int slot = -1;
+        if (k >= GS) {
+            slot = (k - GS) / GS;
+            k -= (slot + 1) * GS;
+        }
+        return {true, slot, k / TPU, k % TPU};
     }
-    return {n - 1, r - (n - 1) * per, false};
-}
-
-// Global item i -> (slot, unit): the shared expert's NU units first (slot -1),
-// then routed slots 0.. in pick order.
-struct Item {
-    int slot, unit;
-};
-GP_DEVINL Item item_of(int i, int NU) {
-    if (i < NU) return {-1, i};
-    const int r = i - NU;
-    return {r / NU, r % NU};
+    k -= cyc;
+    int slot = -1;
+    if (k >= DS) {
+        slot = (k - DS) / DS;
+        k -= (slot + 1) * DS;
+    }
+    return {false, slot, k / NCH, k % NCH};
 }
 
 // Quantises the unit of h held one value per lane exactly as a lane quantises
@@ -446,7 +448,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     const uint32_t sbase = smem_u32(smem);
     // per stage: full (producer -> compute warps), pdone (compute warps ->
     // epilogue warp: partial sums written / chunk read), empty (epilogue ->
-    // producer); hbar[b]: item m's quantised h is in s_h[b], b = m & 1
+    // producer); hbar[b]: the quantised h of this CTA's down job d is in
+    // s_h[b], b = d & 1
     const uint32_t full0 = sbase + L.bar_off, pdone0 = full0 + 8u * S, empty0 = pdone0 + 8u * S;
     const uint32_t tbar = empty0 + 8u * S, topk_bar = tbar + 8u, rbar = topk_bar + 8u, hbar0 = rbar + 8u;
     volatile uint32_t* s_abort = reinterpret_cast<volatile uint32_t*>(smem + L.misc_off);
@@ -460,7 +463,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     float* partial = reinterpret_cast<float*>(smem + L.partial_off);
     constexpr uint32_t pstride = kPartialFloats;
     const uint32_t stage0 = sbase + L.stages_off;
-    const int n_own = items_of(c, G, E);            // router experts c, c+G, ...
+    const int n_own = jobs_of(c, G, E);             // router experts c, c+G, ...
     const int n_tasks = n_own * RSPLIT;
 
     // the next kernel's CTAs may take each SM as soon as ours leaves it; they
@@ -483,89 +486,91 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     }
     __syncthreads();
 
-    // item m of this CTA: its slot (-1: shared), unit, local expert, token
-    auto item_at = [&](int m, int& slot, int& unit, int& e, int& tok) {
-        const Item it = item_of(c + m * G, NU);
-        slot = it.slot;
-        unit = it.unit;
-        e = slot < 0 ? a.e_cnt : s_se[slot];
-        tok = slot < 0 ? a.own_tok : s_st[slot];
-    };
+    // Jobs of this CTA: k = c + m*G.  Before the routing is known only the
+    // shared expert's gate/up tiles (k < nsh) can be decoded; the total needs
+    // the routed slot count.
+    const int nsh = NU * TPU;
+    auto routed_slots = [&]() { return min(max(*s_nsr, 0), kDecodeMaxRouted); };
+    auto total_jobs = [&](int nsr) { return (nsr + 1) * NU * (TPU + NCH); };
 
     if (warp == PROD) {
-        // ================= producer (lane 0 issues) =================
+        // ================= producer (lane 0 issues the copies) =================
+        // The producer's latency per job is on the critical path of the ring,
+        // and it shares issue slots with the compute warps: the warp's 32 lanes
+        // decode the sources of the next 32 jobs at once (lane l: job w0 + l),
+        // and lane 0 reads each job's three addresses with shuffles.
         if (lane == 0) {
             mbar_arrive_expect_tx(tbar, GP_IQ3_TABLE_BYTES);
             for (int k4 = 0; k4 < 4; ++k4) bulk_g2s(sbase + k4 * 16384u, a.tables + k4 * 16384, 16384u, tbar);
-            int s = 0, issued = 0, n = 1;
-            uint32_t ph = 1;
-            bool have = false;  // the slot list (and so this CTA's item count) is known
-            // where item m's bytes are: its gate/up rows, its down column slab
-            // and its d block (the two items in flight, by parity m & 1)
-            struct Src {
-                int64_t guo;
-                const uint8_t *dc, *db;
-            };
-            auto item_src = [&](int m) -> Src {
-                int slot, unit, e, tok;
-                item_at(m, slot, unit, e, tok);
-                return {(int64_t)e * a.gu_stride + (int64_t)unit * TPU * GU_BYTES,
-                        a.down_col + (int64_t)e * a.dc_stride + (int64_t)unit * UNIT_BYTES,
-                        a.down_col + (int64_t)e * a.dc_stride + (int64_t)NU * UNIT_BYTES + (int64_t)(unit >> 3) * H * 2};
-            };
-            // stage u's bytes into L2: a sliding window kPrefetch stages beyond
-            // the shared-memory ring keeps more bytes in flight per SM than
-            // the ring holds, so the ring's copies later wait on L2, not DRAM
-            auto prefetch_stage = [&](int u) {
-                const Stage sg = stage_of(u, n, NCH);
-                const Src r = item_src(sg.m);
-                if (sg.gu) {
-                    prefetch_l2(a.gate + r.guo + (int64_t)sg.j * GU_BYTES, GU_BYTES);
-                    prefetch_l2(a.up + r.guo + (int64_t)sg.j * GU_BYTES, GU_BYTES);
-                } else {
-                    prefetch_l2(r.dc + (int64_t)sg.j * RC * 8, RC * 8u);
-                    prefetch_l2(r.dc + (int64_t)H * 8 + (int64_t)sg.j * RC * 4, RC * 4u);
-                    prefetch_l2(r.db + (int64_t)sg.j * RC * 2, RC * 2u);
-                }
-            };
-            int64_t guo0 = 0, guo1 = 0;
-            const uint8_t *dc0 = nullptr, *dc1 = nullptr, *db0 = nullptr, *db1 = nullptr;
-            for (int t = 0;; ++t) {
-                if (!have && (t >= TPU || c >= NU)) {  // routed items need the slot list
-                    if (!mbar_wait(topk_bar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); break; }
-                    GP_STAMP(10);
-                    n = items_of(c, G, NU * (min(max(*s_nsr, 0), kDecodeMaxRouted) + 1));
-                    have = true;
-                }
-                if (have && t >= n * (TPU + NCH)) break;
-                const Stage sg = stage_of(t, n, NCH);
-                const int p = sg.m & 1;
-                if (sg.gu && sg.j == 0) {  // a new item: where its bytes are, and the next one into L2
-                    const Src r = item_src(sg.m);
-                    if (p) { guo1 = r.guo; dc1 = r.dc; db1 = r.db; } else { guo0 = r.guo; dc0 = r.dc; db0 = r.db; }
-                }
-                if (!mbar_wait(empty0 + 8u * s, ph, a.spin_limit)) {
-                    *s_abort = 1;
-                    atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
-                    break;
-                }
-                const uint32_t dst = stage0 + s * L.stage_bytes, bar = full0 + 8u * s;
-                if (sg.gu) {
-                    const int64_t eo = (p ? guo1 : guo0) + (int64_t)sg.j * GU_BYTES;
-                    mbar_arrive_expect_tx(bar, 2u * GU_BYTES);
-                    bulk_g2s(dst, a.gate + eo, GU_BYTES, bar);
-                    bulk_g2s(dst + GU_BYTES, a.up + eo, GU_BYTES, bar);
-                } else {
-                    const uint8_t* dc = p ? dc1 : dc0;
-                    mbar_arrive_expect_tx(bar, (uint32_t)RC * 14u);
-                    bulk_g2s(dst, dc + (int64_t)sg.j * RC * 8, RC * 8u, bar);
-                    bulk_g2s(dst + RC * 8u, dc + (int64_t)H * 8 + (int64_t)sg.j * RC * 4, RC * 4u, bar);
-                    bulk_g2s(dst + RC * 12u, (p ? db1 : db0) + (int64_t)sg.j * RC * 2, RC * 2u, bar);
-                }
-                ++issued;
-                if (++s == S) { s = 0; ph ^= 1u; }
-                if (have && t + S + kPrefetch < n * (TPU + NCH)) prefetch_stage(t + S + kPrefetch);
+        }
+        int s = 0, issued = 0, n = jobs_of(c, G, nsh), nsr = 0;
+        uint32_t ph = 1;
+        bool have = false;   // the slot list (and so this CTA's job count) is known
+        int w0 = -32;        // first job of the decoded window
+        bool w_have = false;  // the window was decoded with the slot list
+        // this lane's job w0 + lane: gate/up tile (p2 null), or down chunk
+        // (qs, aux) of the unit's column slab and its d block
+        const uint8_t *p0 = nullptr, *p1 = nullptr, *p2 = nullptr;
+        bool ok = true;
+        for (int m = 0;; ++m) {
+            if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) need the slot list
+                if (!__all_sync(0xffffffffu, mbar_wait(topk_bar, 0, a.spin_limit))) { ok = false; break; }
+                GP_STAMP(10);
+                nsr = routed_slots();
+                n = jobs_of(c, G, total_jobs(nsr));
+                have = true;
             }
+            if (m >= n) break;
+            if (m >= w0 + 32 || (have && !w_have)) {
+                w0 = m;
+                w_have = have;
+                const int mm = m + lane;
+                p0 = p1 = p2 = nullptr;
+                if (mm < n && (have || c + mm * G < nsh)) {
+                    const Job jb = job_of<NU, NCH>(c + mm * G, nsr);
+                    const int e = jb.slot < 0 ? a.e_cnt : s_se[jb.slot];
+                    if (jb.gu) {
+                        const int64_t o = (int64_t)e * a.gu_stride + (int64_t)(jb.unit * TPU + jb.j) * GU_BYTES;
+                        p0 = a.gate + o;
+                        p1 = a.up + o;
+                    } else {
+                        const uint8_t* dc = a.down_col + (int64_t)e * a.dc_stride;
+                        p0 = dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)jb.j * RC * 8;
+                        p1 = dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)H * 8 + (int64_t)jb.j * RC * 4;
+                        p2 = dc + (int64_t)NU * UNIT_BYTES + (int64_t)(jb.unit >> 3) * H * 2 + (int64_t)jb.j * RC * 2;
+                    }
+                }
+            }
+            const int src = m - w0;
+            const uint8_t* r0 = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(p0), src));
+            const uint8_t* r1 = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(p1), src));
+            const uint8_t* r2 = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(p2), src));
+            if (!__all_sync(0xffffffffu, mbar_wait(empty0 + 8u * s, ph, a.spin_limit))) {
+                if (lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
+                ok = false;
+                break;
+            }
+            if (lane == 0) {
+                const uint32_t dst = stage0 + s * L.stage_bytes, bar = full0 + 8u * s;
+                if (r2 == nullptr) {
+                    mbar_arrive_expect_tx(bar, 2u * GU_BYTES);
+                    bulk_g2s(dst, r0, GU_BYTES, bar);
+                    bulk_g2s(dst + GU_BYTES, r1, GU_BYTES, bar);
+                } else {
+                    mbar_arrive_expect_tx(bar, (uint32_t)RC * 14u);
+                    bulk_g2s(dst, r0, RC * 8u, bar);
+                    bulk_g2s(dst + RC * 8u, r1, RC * 4u, bar);
+                    bulk_g2s(dst + RC * 12u, r2, RC * 2u, bar);
+                }
+            }
+            ++issued;
+            if (++s == S) { s = 0; ph ^= 1u; }
+        }
+        if (!ok && lane == 0) {
+            *s_abort = 1;
+            atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+        }
+        if (lane == 0) {
             // no copy may still be in flight when the CTA exits (the
             // compile-time limit, whatever the run-time one)
             for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
@@ -576,7 +581,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     }
 
     if (warp == EPI) {
-        // ================= routing, then the gate/up epilogues =================
+        // ================= routing, then the gate/up epilogues and h fetches =================
         constexpr int EJ = kMaxEFused / 32;
         float bias[EJ];
 #pragma unroll
@@ -613,7 +618,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         if (NT == 1) {  // every CTA picks the token's experts itself
             ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0)
                           : topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0);
-            fence_acq_rel_gpu();  // the other CTAs' zeroing of y is seen before any reduction of this CTA
         } else {
             // CTA t picks token t's experts and publishes them; every CTA
             // then reads all tokens' picks (one more exchange, no CTA sorts
@@ -623,7 +627,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 float mw = 0.f;
                 ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, 0, c, true, me, mw)
                               : topk_token<EJ>(a, bias, tag, lane, 0, c, true, me, mw);
-                fence_acq_rel_gpu();
                 if (lane < K) {
                     const unsigned long long v = ((unsigned long long)(tag & 0xFFFFu) << 48) |
                                                  ((unsigned long long)(me & 0xFFFF) << 32) | __float_as_uint(mw);
@@ -644,7 +647,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 __nanosleep(TOPK_POLL_NS);
             }
             if (n == a.spin_limit) ok = false;
-            fence_acq_rel_gpu();
             e0 = (int)((p0 >> 32) & 0xFFFFu);
             w0 = __uint_as_float((uint32_t)p0);
             e1 = (int)((p1 >> 32) & 0xFFFFu);
@@ -657,25 +659,64 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         __syncwarp();
         if (lane == 0) mbar_arrive(topk_bar);  // release: the other roles read the slot list
         GP_STAMP(2);
+        // Acquire: the other CTAs zeroed their parts of y before publishing the
+        // logits (or picks) read above.  Every reduction into y comes from a
+        // down job, whose h this warp hands over (hbar) only after this fence;
+        // the slot list above needs no such order.
+        fence_acq_rel_gpu();
 
-        const int nsr = min(max(*s_nsr, 0), kDecodeMaxRouted);
-        const int n = items_of(c, G, NU * (nsr + 1));
-        int s = 0;
+        const int nsr = routed_slots();
+        const int n = jobs_of(c, G, total_jobs(nsr));
+        int s = 0, fm = 0, d = 0;
         uint32_t ph = 0;
         constexpr int rsg = 32 * NWC / (H / 32);
-        float hv = 0.f;
+        // h of down job at position fm into s_h[d & 1]: its 32 tagged rows
+        // (published by the gate/up tiles of that unit), quantised as a lane
+        // quantises its activations.  Fetched one stage ahead of its use.
+        auto fetch_h = [&](const Job& jb) -> bool {
+            const unsigned long long* src =
+                a.hx + (int64_t)(jb.slot < 0 ? kDecodeMaxRouted : jb.slot) * I + jb.unit * UNIT + lane;
+            unsigned long long w = 0ull;
+            uint32_t k = 0;
+            for (; k < a.spin_limit; ++k) {
+                w = ld_relaxed64(src);
+                if (__all_sync(0xffffffffu, (uint32_t)(w >> 32) == tag)) break;
+                __nanosleep(TOPK_POLL_NS);
+            }
+            quantise_unit(__uint_as_float((uint32_t)w), s_h + (d & 1) * 20, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(hbar0 + 8u * (d & 1));
+            ++d;
+            return k < a.spin_limit;
+        };
         // A warp whose bounded wait runs out records it and leaves its loop
         // (arriving on no further barrier, so no barrier phase sees arrivals
         // from two iterations); the waits it leaves other warps in run out
         // in turn.  Decisions are warp-uniform (votes over the lanes' waits).
-        for (int t = 0; t < n * (TPU + NCH); ++t) {
-            const Stage sg = stage_of(t, n, NCH);
+        for (int m = 0; m < n; ++m) {
+            // the h of the down jobs at positions m and m+1, in order: the
+            // buffer of down job d was last read by down job d-2, whose stage
+            // (two down jobs back, so before position m) this warp has seen done
+            bool fetched = true;
+            const Job jb = job_of<NU, NCH>(c + m * G, nsr);
+            for (; fm <= m + 1 && fm < n && fetched; ++fm) {
+                const Job fj = job_of<NU, NCH>(c + fm * G, nsr);
+                if (fj.gu) continue;
+                // (not ahead of this CTA's own tile of the same unit, whose h
+                // this warp publishes only below)
+                if (fm == m + 1 && jb.gu && jb.slot == fj.slot && jb.unit == fj.unit) break;
+                fetched = fetch_h(fj);
+            }
+            if (!fetched) {
+                if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
+                break;
+            }
             if (!__all_sync(0xffffffffu, mbar_wait(pdone0 + 8u * s, ph, a.spin_limit))) {
                 if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
                 break;
             }
             float val = 0.f;
-            if (sg.gu && lane < TRG) {  // partials in warp order (LaneMap layout)
+            if (jb.gu && lane < TRG) {  // partials in warp order (LaneMap layout)
                 using LG = LaneMap<HH, NWC, PG>;
                 const float* pbuf = partial + (size_t)s * pstride;
                 const int row = lane, ur = TRG + row;
@@ -699,15 +740,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             __syncwarp();
             if (lane == 0) mbar_arrive(empty0 + 8u * s);  // stage read: it may refill
             if (++s == S) { s = 0; ph ^= 1u; }
-            if (sg.gu) {
-                // rows j*8 .. j*8+7 of the unit land on lanes j*8 .. j*8+7
-                const float v = __shfl_sync(0xffffffffu, val, lane & (TRG - 1));
-                if ((lane / TRG) == sg.j) hv = v;
-                if (sg.j == TPU - 1) {
-                    quantise_unit(hv, s_h + (sg.m & 1) * 20, lane);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(hbar0 + 8u * (sg.m & 1));
-                }
+            if (jb.gu && lane < TRG) {  // h rows of the tile, tagged: the data is its own flag
+                unsigned long long* dst = a.hx + (int64_t)(jb.slot < 0 ? kDecodeMaxRouted : jb.slot) * I +
+                                          jb.unit * UNIT + jb.j * TRG + lane;
+                st_relaxed64(dst, ((unsigned long long)tag << 32) | __float_as_uint(val));
             }
         }
     } else {
@@ -756,43 +792,42 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
 
         if (!mbar_wait(tbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         const auto mg = lane_map<HH, NWC, PG>(warp, lane, stage0);
-        const int gl = warp * 32 + lane;  // this lane's two rows of a down chunk: 2gl, 2gl+1
+        const int gl = warp * 32 + lane;  // this lane's rows of a down chunk: 4gl .. 4gl+3
         uint32_t xq[16], hq[16];
-        int cur = -1;  // the token whose activations xq holds for gate/up
+        int cur = -1;  // the token whose activations xq holds
         float sx4 = 0.f, hs = 0.f;
-        int tok0 = 0, tok1 = 0;  // token and weight of the two items in flight (by parity)
-        float wk0 = 1.f, wk1 = 1.f;
-        int s = 0, n = 1;
+        int s = 0, n = jobs_of(c, G, nsh), nsr = 0, d = 0;
         uint32_t ph = 0;
         bool have = false;
         auto give_up = [&]() {
             if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         };
-        for (int t = 0;; ++t) {
-            if (!have && (t >= TPU || c >= NU)) {  // routed items (and every down chunk) come after the routing
+        for (int m = 0;; ++m) {
+            if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) come after the routing
                 if (!__all_sync(0xffffffffu, mbar_wait(topk_bar, 0, a.spin_limit))) { give_up(); break; }
-                n = items_of(c, G, NU * (min(max(*s_nsr, 0), kDecodeMaxRouted) + 1));
+                nsr = routed_slots();
+                n = jobs_of(c, G, total_jobs(nsr));
                 have = true;
             }
-            if (have && t >= n * (TPU + NCH)) break;
-            const Stage sg = stage_of(t, n, NCH);
-            const int p = sg.m & 1;
-            if (sg.gu && sg.j == 0) {  // a new item: its token and weight; that token's activations
-                int slot, unit, e, tok;
-                item_at(sg.m, slot, unit, e, tok);
-                const float wk = slot < 0 ? 1.0f : s_sw[slot];
-                if (p) { tok1 = tok; wk1 = wk; } else { tok0 = tok; wk0 = wk; }
-                if (tok != cur) {
+            if (m >= n) break;
+            const Job jb = job_of<NU, NCH>(c + m * G, nsr);
+            const int tok = jb.slot < 0 ? a.own_tok : s_st[jb.slot];
+            if (jb.gu) {
+                if (tok != cur) {  // that token's activations
                     cur = tok;
                     sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
                 }
-            }
-            if (!sg.gu && sg.j == 0) {  // the item's quantised h (double-buffered by item parity), once
-                if (!__all_sync(0xffffffffu, mbar_wait(hbar0 + 8u * p, (uint32_t)(sg.m >> 1) & 1u, a.spin_limit))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, ph, a.spin_limit))) { give_up(); break; }
+                consume<HH, NWC, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(pdone0 + 8u * s);
+            } else {
+                // the unit's quantised h (double-buffered by down-job parity)
+                if (!__all_sync(0xffffffffu, mbar_wait(hbar0 + 8u * (d & 1), (uint32_t)(d >> 1) & 1u, a.spin_limit))) {
                     give_up();
                     break;
                 }
-                const uint32_t hb = smem_u32(s_h + p * 20);
+                const uint32_t hb = smem_u32(s_h + (d & 1) * 20);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     const uint4 v = lds128(hb + 16u * i);
@@ -802,14 +837,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     hq[4 * i + 3] = v.w;
                 }
                 hs = ldsf(hb + 64u);
-            }
-            if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, ph, a.spin_limit))) { give_up(); break; }
-            if (sg.gu) {
-                consume<HH, NWC, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(pdone0 + 8u * s);
-            } else {
-                // split-K down: rows 4gl .. 4gl+3 of chunk j, this item's 32 input columns
+                ++d;
+                if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, ph, a.spin_limit))) { give_up(); break; }
+                // split-K down: rows 4gl .. 4gl+3 of chunk j, this unit's 32 input columns
                 const uint32_t sb = stage0 + s * L.stage_bytes;
                 const uint4 q01 = lds128(sb + 32u * gl), q23 = lds128(sb + 32u * gl + 16u);
                 const uint4 ax = lds128(sb + RC * 8u + 16u * gl);
@@ -827,9 +857,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 // the stage is read: release it first, then send the sums
                 __syncwarp();
                 if (lane == 0) mbar_arrive(pdone0 + 8u * s);
-                const float wk = p ? wk1 : wk0;
-                red_add_v4(a.y + (int64_t)(p ? tok1 : tok0) * H + sg.j * RC + 4 * gl, wk * v[0], wk * v[1], wk * v[2],
-                           wk * v[3]);
+                const float wk = jb.slot < 0 ? 1.0f : s_sw[jb.slot];
+                red_add_v4(a.y + (int64_t)tok * H + jb.j * RC + 4 * gl, wk * v[0], wk * v[1], wk * v[2], wk * v[3]);
             }
             if (++s == S) { s = 0; ph ^= 1u; }
         }

@@ -191,6 +191,8 @@ struct DecodeLayerArgs {
     int own_tok;               // token whose shared expert runs in this launch
     unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
     unsigned long long* picks;   // [decode_layer_pick_words()] top-k picks of each token, tagged (n_tok > 1)
+    unsigned long long* hx;      // [decode_layer_h_words(I)] h of every (slot, unit), tagged: rows of routed slot s
+                                 // at s * I, the shared expert's at kDecodeMaxRouted * I
     unsigned* sync;            // [kDecodeSyncWords] launch generation and finished-CTA count
     const uint8_t* tables;
     uint32_t* status;
@@ -244,6 +246,8 @@ constexpr int kDecodeSyncWords = 64;
 inline size_t decode_layer_logit_words(int E) { return (size_t)8 * E * 32; }
 // Words of DecodeLayerArgs::picks: 8 replicas x kDecodeMaxTokens x 32 picks, one per 256-byte line.
 inline size_t decode_layer_pick_words() { return (size_t)8 * kDecodeMaxTokens * 32 * 32; }
+// Words of DecodeLayerArgs::hx: one tagged h value per row of every slot's expert.
+inline size_t decode_layer_h_words(int I) { return (size_t)(kDecodeMaxRouted + 1) * I; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
 // Dynamic shared memory of a launch: `stages` pipeline stages, n_tok tokens.
 size_t decode_layer_smem(int H, int I, int stages, int n_tok);
