@@ -7,22 +7,21 @@
 // SM runs the whole layer.  Warp roles: 20 compute warps, one TMA producer
 // warp streaming weights through a ring of shared-memory stages, and one
 // epilogue warp that does the routing and turns each stage's partial sums
-// into h.  Under full HBM load a round trip to L2 costs microseconds, so the
-// only exchange between CTAs is the routing: values other CTAs produced are
-// read as words tagged with the launch generation (the data is its own flag).
+// into h.  Values other CTAs produced (router logits, h) are read as words
+// tagged with the launch generation: the data is its own flag.
 //
-// Work item = (slot, unit): 32 rows of h of one slot's expert (a slot is a
-// (token, expert) pick, or the shared expert).  An item runs gate/up for its
-// 32 rows (4 tiles of 8 gate + 8 up rows), SwiGLU with the reference clamp
-// (model.cpp:733-739), quantises its 32 h values, and then at once its slice
-// of the down projection: the 32 input columns of W_down that these h values
-// multiply, for every output row (a split-K down, streamed from a column-slab
-// copy of W_down in 4 chunks of 1280 rows).  The item adds w_k * D_slice into
-// y with vector fp32 reductions, so no CTA waits for h computed elsewhere.
-// Items are dealt round-robin, shared expert first (it needs no routing and
-// overlaps it); each CTA interleaves its stages as GU(0) GU(1) DN(0) GU(2)
-// DN(1) ... so the epilogue's SwiGLU + quantisation of item m overlaps the
-// gate/up of item m+1.
+// Work is dealt to the CTAs one pipeline stage ("job") at a time, round-robin
+// over a global job list, so every CTA gets the same number of stages within
+// one: first the shared expert's gate/up tiles (they need no routing, and run
+// while the routing exchange is in flight), then the routed slots' gate/up
+// tiles, then every slot's down chunks.  A gate/up tile is 8 gate + 8 up rows
+// of one slot's expert; the epilogue applies SwiGLU with the reference clamp
+// (model.cpp:733-739) and publishes the 8 h values as tagged words.  A down
+// chunk is the split-K slice of W_down that one unit of 32 h values
+// multiplies, for 2560 output rows, streamed from a column-slab copy of
+// W_down; the epilogue fetches and quantises the unit's h one stage ahead
+// (tiles of that unit ran about eleven stages earlier, on any CTA), and the
+// compute warps add w_k * D_slice into y with vector fp32 reductions.
 //
 //   router   CTA c owns experts c, c+G, ...; 8 warps each compute one 1/8
 //            slice of an owned expert's fp32 logit for every token (weights
@@ -73,8 +72,8 @@ constexpr int EPI = NWC;         // epilogue warp
 constexpr int PROD = NWC + 1;    // TMA producer warp
 constexpr int NTHREADS = 32 * (NWC + 2);
 constexpr int TRG = 8;           // gate/up rows per matrix per tile
-constexpr int UNIT = 32;         // rows of h per work item = input columns of its down slice
-constexpr int TPU = UNIT / TRG;  // gate/up tiles per item
+constexpr int UNIT = 32;         // rows of h per unit = input columns of its down slice
+constexpr int TPU = UNIT / TRG;  // gate/up tiles per unit
 constexpr int RC = 4 * 32 * NWC; // down rows per chunk (four per compute lane)
 constexpr int RSPLIT = 8;        // router slices per expert
 constexpr int MAXK = 31;         // picks per token
@@ -494,83 +493,62 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     auto total_jobs = [&](int nsr) { return (nsr + 1) * NU * (TPU + NCH); };
 
     if (warp == PROD) {
-        // ================= producer (lane 0 issues the copies) =================
-        // The producer's latency per job is on the critical path of the ring,
-        // and it shares issue slots with the compute warps: the warp's 32 lanes
-        // decode the sources of the next 32 jobs at once (lane l: job w0 + l),
-        // and lane 0 reads each job's three addresses with shuffles.
+        // ================= producer (lane 0 issues) =================
+        // (Its latency per job is on the ring's critical path: it shares issue
+        // slots with the compute warps, so the per-job work stays small: a
+        // constant-divisor job decode, one shared-memory read, the copies.)
         if (lane == 0) {
             mbar_arrive_expect_tx(tbar, GP_IQ3_TABLE_BYTES);
             for (int k4 = 0; k4 < 4; ++k4) bulk_g2s(sbase + k4 * 16384u, a.tables + k4 * 16384, 16384u, tbar);
-        }
-        int s = 0, issued = 0, n = jobs_of(c, G, nsh), nsr = 0;
-        uint32_t ph = 1;
-        bool have = false;   // the slot list (and so this CTA's job count) is known
-        int w0 = -32;        // first job of the decoded window
-        bool w_have = false;  // the window was decoded with the slot list
-        // this lane's job w0 + lane: gate/up tile (p2 null), or down chunk
-        // (qs, aux) of the unit's column slab and its d block
-        const uint8_t *p0 = nullptr, *p1 = nullptr, *p2 = nullptr;
-        bool ok = true;
-        for (int m = 0;; ++m) {
-            if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) need the slot list
-                if (!__all_sync(0xffffffffu, mbar_wait(topk_bar, 0, a.spin_limit))) { ok = false; break; }
-                GP_STAMP(10);
-                nsr = routed_slots();
-                n = jobs_of(c, G, total_jobs(nsr));
-                have = true;
-            }
-            if (m >= n) break;
-            if (m >= w0 + 32 || (have && !w_have)) {
-                w0 = m;
-                w_have = have;
-                const int mm = m + lane;
-                p0 = p1 = p2 = nullptr;
-                if (mm < n && (have || c + mm * G < nsh)) {
-                    const Job jb = job_of<NU, NCH>(c + mm * G, nsr);
-                    const int e = jb.slot < 0 ? a.e_cnt : s_se[jb.slot];
-                    if (jb.gu) {
-                        const int64_t o = (int64_t)e * a.gu_stride + (int64_t)(jb.unit * TPU + jb.j) * GU_BYTES;
-                        p0 = a.gate + o;
-                        p1 = a.up + o;
-                    } else {
-                        const uint8_t* dc = a.down_col + (int64_t)e * a.dc_stride;
-                        p0 = dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)jb.j * RC * 8;
-                        p1 = dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)H * 8 + (int64_t)jb.j * RC * 4;
-                        p2 = dc + (int64_t)NU * UNIT_BYTES + (int64_t)(jb.unit >> 3) * H * 2 + (int64_t)jb.j * RC * 2;
-                    }
+            int s = 0, issued = 0, n = jobs_of(c, G, nsh), nsr = 0;
+            uint32_t ph = 1;
+            bool have = false;  // the slot list (and so this CTA's job count) is known
+            // global addresses of job m's bytes: gate/up tile, or down chunk
+            // (qs, aux) of the unit's column slab and its d block
+            struct Src {
+                const uint8_t *p0, *p1, *p2;
+            };
+            auto job_src = [&](int m) -> Src {
+                const Job jb = job_of<NU, NCH>(c + m * G, nsr);
+                const int e = jb.slot < 0 ? a.e_cnt : s_se[jb.slot];
+                if (jb.gu) {
+                    const int64_t o = (int64_t)e * a.gu_stride + (int64_t)(jb.unit * TPU + jb.j) * GU_BYTES;
+                    return {a.gate + o, a.up + o, nullptr};
                 }
-            }
-            const int src = m - w0;
-            const uint8_t* r0 = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(p0), src));
-            const uint8_t* r1 = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(p1), src));
-            const uint8_t* r2 = reinterpret_cast<const uint8_t*>(__shfl_sync(0xffffffffu, reinterpret_cast<uintptr_t>(p2), src));
-            if (!__all_sync(0xffffffffu, mbar_wait(empty0 + 8u * s, ph, a.spin_limit))) {
-                if (lane == 0) atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
-                ok = false;
-                break;
-            }
-            if (lane == 0) {
+                const uint8_t* dc = a.down_col + (int64_t)e * a.dc_stride;
+                return {dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)jb.j * RC * 8,
+                        dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)H * 8 + (int64_t)jb.j * RC * 4,
+                        dc + (int64_t)NU * UNIT_BYTES + (int64_t)(jb.unit >> 3) * H * 2 + (int64_t)jb.j * RC * 2};
+            };
+            for (int m = 0;; ++m) {
+                if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) need the slot list
+                    if (!mbar_wait(topk_bar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); break; }
+                    GP_STAMP(10);
+                    nsr = routed_slots();
+                    n = jobs_of(c, G, total_jobs(nsr));
+                    have = true;
+                }
+                if (m >= n) break;
+                const Src r = job_src(m);
+                if (!mbar_wait(empty0 + 8u * s, ph, a.spin_limit)) {
+                    *s_abort = 1;
+                    atomicOr(a.status, GP_DEV_TIMEOUT_EMPTY);
+                    break;
+                }
                 const uint32_t dst = stage0 + s * L.stage_bytes, bar = full0 + 8u * s;
-                if (r2 == nullptr) {
+                if (r.p2 == nullptr) {
                     mbar_arrive_expect_tx(bar, 2u * GU_BYTES);
-                    bulk_g2s(dst, r0, GU_BYTES, bar);
-                    bulk_g2s(dst + GU_BYTES, r1, GU_BYTES, bar);
+                    bulk_g2s(dst, r.p0, GU_BYTES, bar);
+                    bulk_g2s(dst + GU_BYTES, r.p1, GU_BYTES, bar);
                 } else {
                     mbar_arrive_expect_tx(bar, (uint32_t)RC * 14u);
-                    bulk_g2s(dst, r0, RC * 8u, bar);
-                    bulk_g2s(dst + RC * 8u, r1, RC * 4u, bar);
-                    bulk_g2s(dst + RC * 12u, r2, RC * 2u, bar);
+                    bulk_g2s(dst, r.p0, RC * 8u, bar);
+                    bulk_g2s(dst + RC * 8u, r.p1, RC * 4u, bar);
+                    bulk_g2s(dst + RC * 12u, r.p2, RC * 2u, bar);
                 }
+                ++issued;
+                if (++s == S) { s = 0; ph ^= 1u; }
             }
-            ++issued;
-            if (++s == S) { s = 0; ph ^= 1u; }
-        }
-        if (!ok && lane == 0) {
-            *s_abort = 1;
-            atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
-        }
-        if (lane == 0) {
             // no copy may still be in flight when the CTA exits (the
             // compile-time limit, whatever the run-time one)
             for (int i = (issued > S ? issued - S : 0); i < issued; ++i)
