@@ -19,13 +19,15 @@ the GPUs with NCCL all-to-all dispatch and combine), --workload stack40 (config
 
 N > 1 (launched by torchrun): expert parallelism.  The same layer's 160
 routed experts are split 160/N per GPU (plus the shared expert on every GPU);
-each rank brings one token per step (weak scaling).  A step is an NCCL
-all-gather of the N tokens, one persistent kernel per rank that routes all N
-tokens and runs its experts' share of each plus its own token's shared expert
-(gpeed_moe_decode_partial), and an NCCL reduce-scatter that sums the partial
-outputs; all captured in CUDA graphs.  value = tokens over all ranks / the
-slowest rank's time.  The reference arm runs on rank 0 only, on every host
-core.
+each rank brings one token per step (weak scaling).  A step is one persistent
+kernel per rank (gpeed_moe_decode_ep): its token goes to every rank over
+NVLink peer memory, all N tokens are routed, the rank runs its experts' share
+of each plus its own token's shared expert and adds the sums straight into
+the owning rank's output; no collective library on the data path.  With
+--ep-nccl the exchanges are an NCCL all-gather and reduce-scatter around
+gpeed_moe_decode_partial instead.  Steps are captured in CUDA graphs.  value =
+tokens over all ranks / the slowest rank's time.  The reference arm runs on
+rank 0 only, on every host core.
 """
 from __future__ import annotations
 
@@ -381,17 +383,20 @@ def run_gpu_ep(args, rank, local_rank, world):
     """BASELINE config 2's layer, expert-parallel over `world` GPUs (the N > 1
     default).  Rank r holds routed experts [r*E/N, (r+1)*E/N) of every layer
     copy plus the shared expert and brings its own token each step.  A step
-    (one token per rank through one layer): NCCL all-gather of the N tokens,
-    gpeed_moe_decode_partial (one persistent kernel: routing of all N tokens,
-    this rank's experts' share of each, its own token's shared expert), NCCL
-    reduce-scatter of the partial outputs.  Layer copies rotate so each step's
-    weights come from HBM, and the steps are captured back to back in CUDA
-    graphs (collectives included)."""
+    (one token per rank through one layer) is one persistent kernel per rank,
+    gpeed_moe_decode_ep: the tokens go to every rank over NVLink peer memory,
+    all N are routed, this rank's picks of each run and add their sums into
+    the owning rank's output, the launch ends when the other ranks' sums into
+    this rank's output are done.  With --ep-nccl the exchanges are NCCL
+    collectives instead (all-gather of the tokens, gpeed_moe_decode_partial,
+    reduce-scatter of the partial outputs).  Layer copies rotate so each
+    step's weights come from HBM, and the steps are captured back to back in
+    CUDA graphs."""
     import torch
     import torch.distributed as dist
 
     from gpeed_b200 import Context, MoeConfig, MoeLayer
-    from gpeed_b200.ep import ExpertParallelLayer
+    from gpeed_b200.ep import ExpertParallelLayer, PeerDecode
 
     torch.cuda.set_device(local_rank)
     ctx = Context(local_rank)
@@ -400,6 +405,8 @@ def run_gpu_ep(args, rank, local_rank, world):
     lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
     layers = [MoeLayer(ctx, cfg, layer_id=l).synth_range(router_for(l), None, 1000 + l, 0, lo, cnt)
               for l in range(L)]
+    peer = not args.ep_nccl
+    pd = PeerDecode(ctx, cfg, layers) if peer else None
     stream = torch.cuda.Stream()
     torch.cuda.synchronize()
     xs = [tokens(1, 100 + l + 7919 * rank).cuda() for l in range(L)]  # this rank's token per layer copy
@@ -407,16 +414,23 @@ def run_gpu_ep(args, rank, local_rank, world):
     y_part = [torch.empty(world, H, device="cuda") for _ in range(L)]
     ys = [torch.empty(1, H, device="cuda") for _ in range(L)]
 
-    def step(l, ev=None):
+    def step(l, ev=None, topk_ids=None):
         if ev:
             ev[0].record(stream)
-        dist.all_gather_into_tensor(x_all[l], xs[l])
-        if ev:
-            ev[1].record(stream)
-        layers[l].decode_partial(x_all[l], rank, y_part[l], stream=stream)
-        if ev:
-            ev[2].record(stream)
-        dist.reduce_scatter_tensor(ys[l], y_part[l], op=dist.ReduceOp.SUM)
+        if peer:
+            if ev:
+                ev[1].record(stream)
+            pd.forward(l, xs[l], ys[l], topk_ids=topk_ids, stream=stream)
+            if ev:
+                ev[2].record(stream)
+        else:
+            dist.all_gather_into_tensor(x_all[l], xs[l])
+            if ev:
+                ev[1].record(stream)
+            layers[l].decode_partial(x_all[l], rank, y_part[l], topk_ids=topk_ids, stream=stream)
+            if ev:
+                ev[2].record(stream)
+            dist.reduce_scatter_tensor(ys[l], y_part[l], op=dist.ReduceOp.SUM)
         if ev:
             ev[3].record(stream)
 
@@ -482,9 +496,11 @@ def run_gpu_ep(args, rank, local_rank, world):
     ph = [sum(evs[i][k].elapsed_time(evs[i][k + 1]) for i in range(n_prof)) / n_prof for k in range(3)]
     # routed slots this rank ran per layer copy (picks of all tokens in its range): the kernel's bytes
     slots = []
-    for l in range(L):
+    for l in range(L):  # (a step on every rank)
         ids = torch.empty(world, K_TOP, dtype=torch.int32, device="cuda")
-        layers[l].decode_partial(x_all[l], rank, torch.empty(world, H, device="cuda"), topk_ids=ids)
+        with torch.cuda.stream(stream):
+            step(l, topk_ids=ids)
+        stream.synchronize()
         g = ids.cpu().numpy()
         slots.append(int(((g >= lo) & (g < lo + cnt)).sum()))
     torch.cuda.synchronize()
@@ -531,16 +547,20 @@ def run_gpu_ep(args, rank, local_rank, world):
             "config": {"workload": "decode1: MoE layer decode, batch 1 (BASELINE config 2)", "hidden": H,
                        "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
                        "layer_copies": L, "l2": f"inputs larger than L2: steps rotate over {L} layer copies",
-                       "parallelism": f"ep{world}: {cnt} routed experts per GPU + the shared expert; one token "
-                                      f"per GPU per step; NCCL all-gather of tokens, one persistent kernel per "
-                                      f"GPU, NCCL reduce-scatter of partial outputs",
-                       "phase_ms": {"all_gather": ph[0], "experts_kernel": ph[1], "reduce_scatter": ph[2]},
+                       "parallelism": (f"ep{world}: {cnt} routed experts per GPU + the shared expert; one token "
+                                       f"per GPU per step; one persistent kernel per GPU exchanging tokens and "
+                                       f"partial outputs over NVLink peer memory (no collective library)" if peer else
+                                       f"ep{world}: {cnt} routed experts per GPU + the shared expert; one token "
+                                       f"per GPU per step; NCCL all-gather of tokens, one persistent kernel per "
+                                       f"GPU, NCCL reduce-scatter of partial outputs"),
+                       "phase_ms": ({"kernel": ph[1]} if peer else
+                                    {"all_gather": ph[0], "experts_kernel": ph[1], "reduce_scatter": ph[2]}),
                        "routed_slots_per_gpu_rank0": mean_slots,
                        "per_gpu_kernel_hbm_gbs": achieved},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None,
                          "kernel": "decode_layer_kernel, expert-parallel share (rank 0): routing of all tokens, "
-                                   "its routed picks + own shared expert",
+                                   "its routed picks + own shared expert" + (", peer exchange" if peer else ""),
                          "bytes_per_launch": kern_bytes, "peak_source": peak_src},
             "cpu_baseline": None,
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 4},
@@ -548,6 +568,8 @@ def run_gpu_ep(args, rank, local_rank, world):
             "clocks": clk.summary(),
         }
     del chains, e2e_graphs
+    if pd is not None:
+        pd.close()
     ctx.close()
     return line
 
@@ -1177,6 +1199,8 @@ def main():
                     help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
     ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
+    ap.add_argument("--ep-nccl", action="store_true",
+                    help="expert-parallel decode (--gpus N > 1) with NCCL collectives instead of the peer-memory exchange")
     ap.add_argument("--ep", action="store_true",
                     help="prefill with the experts split over the GPUs (NCCL all-to-all); needs --gpus >= 2")
     args = ap.parse_args()

@@ -22,6 +22,7 @@ FUSED_MAX_TOKENS_DEFAULT = 12
 OPT_SPIN_LIMIT = 5
 SPIN_LIMIT_DEFAULT = 1 << 22
 OPT_TEST_WITHHOLD_LOGIT = 6
+IPC_HANDLE_BYTES = 64  # GPEED_IPC_HANDLE_BYTES
 TC_SLOT_TOKENS = 224  # rows per expert slot of the tensor-core path (tc_moe.cu, the MMA's N)
 
 
@@ -79,6 +80,10 @@ SIGNATURES = {
     "gpeed_moe_synth_layer_range": [_vp, _i, ctypes.POINTER(MoeShape), _i, _i, _vp, _vp, _i, _u64, _u64],
     "gpeed_moe_route": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp],
     "gpeed_moe_decode_partial": [_vp, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp],
+    "gpeed_ep_setup": [_vp, _i, _i, _i, _vp],
+    "gpeed_ep_connect": [_vp, _vp],
+    "gpeed_moe_decode_ep": [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp],
+    "gpeed_ep_disconnect": [_vp],
     "gpeed_ep_pack": [_vp, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "gpeed_moe_experts": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp],
     "gpeed_moe_combine": [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp],

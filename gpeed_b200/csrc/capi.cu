@@ -111,7 +111,14 @@ struct gpeed_ctx {
     int tc_min_tokens = 8;             // batches this large run the experts on tensor cores
     DevBuf<uint16_t> xp;               // fp16 token rows in expert-sorted order (tensor-core path)
     DevBuf<int> route_chunks;          // per-chunk expert counts of the large-batch stable sort
-    DevBuf<unsigned long long> logits, picks, hx;
+    DevBuf<unsigned long long> logits, hx;
+    // expert-parallel exchange over peer memory (gpeed_ep_setup / _connect)
+    struct Ep {
+        int world = 0, rank = -1, hidden = 0;
+        uint8_t* base = nullptr;                      // this rank's block (cudaMalloc, exported by IPC)
+        uint8_t* peer[gp::kDecodeMaxTokens] = {};     // every rank's block (this rank's = base)
+        bool connected = false;
+    } ep;
     unsigned* sync = nullptr;  // grid counters of the persistent kernel (zero between launches)
     // optional per-stage timing of gpeed_moe_forward (CUDA events on its stream)
     bool prof = false;
@@ -475,9 +482,6 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     if ((rc = c->logits.ensure(gp::decode_layer_logit_words(E)))) return rc;
     if (c->logits.n != had)  // tags must start below the first launch's
         GP_CUDA(cudaMemsetAsync(c->logits.p, 0, c->logits.n * sizeof(unsigned long long), st));
-    const size_t had_p = c->picks.n;
-    if ((rc = c->picks.ensure(gp::decode_layer_pick_words()))) return rc;
-    if (c->picks.n != had_p) GP_CUDA(cudaMemsetAsync(c->picks.p, 0, c->picks.n * sizeof(unsigned long long), st));
     const size_t had_h = c->hx.n;
     if ((rc = c->hx.ensure(gp::decode_layer_h_words(I)))) return rc;
     if (c->hx.n != had_h) GP_CUDA(cudaMemsetAsync(c->hx.p, 0, c->hx.n * sizeof(unsigned long long), st));
@@ -510,7 +514,6 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     da.e_cnt = L.e_cnt;
     da.own_tok = own_tok;
     da.logits = c->logits.p;
-    da.picks = c->picks.p;
     da.hx = c->hx.p;
     da.sync = c->sync;
     da.tables = c->tables;
@@ -648,6 +651,8 @@ int gpeed_ctx_create(int device, gpeed_ctx** out) {
     return GPEED_OK;
 }
 
+void ep_release(gpeed_ctx* c);  // (below, with the expert-parallel entry points)
+
 int gpeed_ctx_destroy(gpeed_ctx* c) {
     if (!c) return GPEED_OK;
     set_device(c);
@@ -665,8 +670,8 @@ int gpeed_ctx_destroy(gpeed_ctx* c) {
     for (auto& e : c->ev)
         if (e) cudaEventDestroy(e);
     c->logits.release();
-    c->picks.release();
     c->hx.release();
+    ep_release(c);
     c->xp.release();
     c->route_chunks.release();
     c->mhc_partial.release();
@@ -698,8 +703,9 @@ int gpeed_ctx_check(gpeed_ctx* c, void* stream) {
         // tags restart together
         GP_CUDA(cudaMemset(c->sync, 0, gp::kDecodeSyncWords * sizeof(unsigned)));
         if (c->logits.p) GP_CUDA(cudaMemset(c->logits.p, 0, c->logits.n * sizeof(unsigned long long)));
-        if (c->picks.p) GP_CUDA(cudaMemset(c->picks.p, 0, c->picks.n * sizeof(unsigned long long)));
         if (c->hx.p) GP_CUDA(cudaMemset(c->hx.p, 0, c->hx.n * sizeof(unsigned long long)));
+        // (an expert-parallel group whose step failed is set up again: its
+        // counters are shared with the other ranks)
         return fail(GPEED_ERR_DEVICE, "device status 0x%x (1: stage wait timed out, 2: drain wait timed out, "
                                       "4: expert id out of range, 8: bad shape, 16: a token or h value past the fp16 range "
                                       "on the tensor-core path)", st);
@@ -1118,6 +1124,125 @@ int gpeed_moe_decode_partial(gpeed_ctx* c, int layer, const void* x, int x_dtype
     return GPEED_OK;
 }
 
+
+// ---- expert-parallel decode over peer memory ----
+// Block of one rank: [kDecodeMaxTokens][H] tagged token words, then its two
+// accumulators [2][H] fp32 (by step parity), its local partial outputs
+// [kDecodeMaxTokens][H] fp32, its done counter (u64) and its EP step
+// generation.
+namespace {
+size_t ep_x_bytes(int H) { return (size_t)gp::kDecodeMaxTokens * H * sizeof(unsigned long long); }
+size_t ep_y_off(int H) { return ep_x_bytes(H); }
+size_t ep_part_off(int H) { return (ep_y_off(H) + (size_t)2 * H * 4 + 255) & ~(size_t)255; }
+size_t ep_done_off(int H) { return (ep_part_off(H) + (size_t)gp::kDecodeMaxTokens * H * 4 + 255) & ~(size_t)255; }
+size_t ep_sync_off(int H) { return ep_done_off(H) + 256; }
+size_t ep_block_bytes(int H) { return ep_sync_off(H) + 256; }
+}  // namespace
+
+void ep_release(gpeed_ctx* c) {
+    for (int r = 0; r < gp::kDecodeMaxTokens; ++r)
+        if (c->ep.peer[r] && c->ep.peer[r] != c->ep.base) cudaIpcCloseMemHandle(c->ep.peer[r]);
+    if (c->ep.base) cudaFree(c->ep.base);
+    c->ep = gpeed_ctx::Ep{};
+}
+
+int gpeed_ep_setup(gpeed_ctx* c, int world, int rank, int hidden, void* handle_out) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if (world < 2 || world > gp::kDecodeMaxTokens || rank < 0 || rank >= world)
+        return fail(GPEED_ERR_INVALID, "world %d, rank %d: 2 .. %d ranks", world, rank, gp::kDecodeMaxTokens);
+    if (hidden <= 0 || hidden % 8 || !handle_out) return fail(GPEED_ERR_INVALID, "hidden %d (multiple of 8), handle_out required", hidden);
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    ep_release(c);
+    void* p = nullptr;
+    if (cudaMalloc(&p, ep_block_bytes(hidden)) != cudaSuccess) return fail(GPEED_ERR_CUDA, "cudaMalloc of the exchange block");
+    c->ep.base = static_cast<uint8_t*>(p);
+    GP_CUDA(cudaMemset(p, 0, ep_block_bytes(hidden)));  // tags, counters and generation start at 0
+    GP_CUDA(cudaDeviceSynchronize());
+    cudaIpcMemHandle_t h;
+    GP_CUDA(cudaIpcGetMemHandle(&h, p));
+    static_assert(sizeof(h) == GPEED_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(handle_out, &h, sizeof(h));
+    c->ep.world = world;
+    c->ep.rank = rank;
+    c->ep.hidden = hidden;
+    return GPEED_OK;
+}
+
+int gpeed_ep_connect(gpeed_ctx* c, const void* handles) {
+    if (!c || !handles) return fail(GPEED_ERR_INVALID, "ctx and handles required");
+    if (!c->ep.base) return fail(GPEED_ERR_INVALID, "gpeed_ep_setup first");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    const uint8_t* hb = static_cast<const uint8_t*>(handles);
+    for (int r = 0; r < c->ep.world; ++r) {
+        if (r == c->ep.rank) {
+            c->ep.peer[r] = c->ep.base;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hb + (size_t)r * GPEED_IPC_HANDLE_BYTES, sizeof(h));
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            ep_release(c);
+            return fail(GPEED_ERR_CUDA, "cudaIpcOpenMemHandle of rank %d: %s", r, cudaGetErrorString(e));
+        }
+        c->ep.peer[r] = static_cast<uint8_t*>(p);
+    }
+    c->ep.connected = true;
+    return GPEED_OK;
+}
+
+int gpeed_ep_disconnect(gpeed_ctx* c) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    for (int r = 0; r < gp::kDecodeMaxTokens; ++r) {
+        if (c->ep.peer[r] && c->ep.peer[r] != c->ep.base) GP_CUDA(cudaIpcCloseMemHandle(c->ep.peer[r]));
+        c->ep.peer[r] = nullptr;
+    }
+    c->ep.connected = false;
+    return GPEED_OK;
+}
+
+int gpeed_moe_decode_ep(gpeed_ctx* c, int layer, const void* x, int x_dtype, float* y, int* topk_ids, float* topk_w,
+                        void* stream) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    if (!c->ep.connected) return fail(GPEED_ERR_INVALID, "gpeed_ep_setup and gpeed_ep_connect first");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    const Layer& L = it->second;
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k, n = c->ep.world;
+    if (H != c->ep.hidden) return fail(GPEED_ERR_INVALID, "hidden %d != the exchange's %d", H, c->ep.hidden);
+    if (n * K > gp::kDecodeMaxRouted) return fail(GPEED_ERR_INVALID, "%d ranks x top-%d > %d picks", n, K, gp::kDecodeMaxRouted);
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (!x || !y || (reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+        return fail(GPEED_ERR_INVALID, "x and y must be 16-byte aligned device pointers");
+    if (!gp::decode_layer_supported(H, I, E, K, s.n_shared))
+        return fail(GPEED_ERR_UNSUPPORTED, "no persistent decode kernel for hidden %d, inter %d, %d experts, top-%d, "
+                    "%d shared", H, I, E, K, s.n_shared);
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    gp::DecodeLayerArgs da{};
+    float* part = reinterpret_cast<float*>(c->ep.base + ep_part_off(H));
+    if ((rc = fused_args(c, L, x, x_dtype, n, c->ep.rank, part, nullptr, topk_ids, topk_w, st, &da))) return rc;
+    da.ep_out = y;
+    da.ep_world = n;
+    da.ep_rank = c->ep.rank;
+    da.ep_x = reinterpret_cast<unsigned long long*>(c->ep.base);
+    for (int r = 0; r < n; ++r) {
+        da.ep_x_peer[r] = reinterpret_cast<unsigned long long*>(c->ep.peer[r]);
+        da.ep_y[r] = reinterpret_cast<float*>(c->ep.peer[r] + ep_y_off(H));
+        da.ep_done[r] = reinterpret_cast<unsigned long long*>(c->ep.peer[r] + ep_done_off(H));
+    }
+    da.ep_sync = reinterpret_cast<unsigned*>(c->ep.base + ep_sync_off(H));
+    GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
+    return GPEED_OK;
+}
 
 int gpeed_moe_route(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, const int* forced, int* topk_ids,
                     float* topk_w, void* stream) {

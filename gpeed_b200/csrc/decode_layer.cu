@@ -28,13 +28,11 @@
 //            prefetched before the wait on the previous kernel); the
 //            epilogue warp adds the slices in order and stores the logit
 //            tagged with the launch generation, so readers poll the data itself
-//   top-k    one token: every CTA's epilogue warp polls the E tagged logits
+//   top-k    every CTA's epilogue warp polls each token's E tagged logits
 //            (one of 8 replicas, spread over L2 lines), applies sigmoid + bias
 //            and picks top-K by warp reductions (ties to the lower id),
-//            weights score/(1e-20 + sum)*scale (model.cpp:704-725).  Several
-//            tokens: CTA t picks token t's experts and publishes the picks as
-//            tagged words that every CTA then reads.  The picks in the
-//            launch's expert range become its slots
+//            weights score/(1e-20 + sum)*scale (model.cpp:704-725).  The picks
+//            in the launch's expert range become its slots
 //   y        zeroed by the CTAs before they publish their logits; every
 //            reduction into y comes after its CTA has seen the routing, so
 //            after every CTA's zeroing
@@ -101,6 +99,25 @@ GP_DEVINL unsigned ld_relaxed(const unsigned* p) {
     return v;
 }
 
+// System-scope forms for the expert-parallel exchange over peer memory.
+GP_DEVINL unsigned long long ld_relaxed_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+GP_DEVINL void st_relaxed_sys64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+GP_DEVINL unsigned long long ld_acquire_sys64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+GP_DEVINL void red_release_sys_add64(unsigned long long* p, unsigned long long v) {
+    asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+GP_DEVINL void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
 // y[0..3] += v as one fire-and-forget vector reduction: no value comes
 // back, so the warp does not wait for the L2 round trip (an atomicAdd on a
 // float4 returns the old values and stalls the registers that receive them).
@@ -118,6 +135,76 @@ GP_DEVINL bool warp_aborted(const volatile uint32_t* s_abort) { return __any_syn
 GP_DEVINL uint32_t order_key(float f) {
     const uint32_t u = __float_as_uint(f + 0.0f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Token words of the expert-parallel exchange: token t's x as 64-bit words
+// {32 bits of payload (a bf16 pair, or one fp32), the step's tag}.  A reader
+// loads every word it needs at once, 16 bytes per load (w[i] even), checks
+// every tag, and loads again until they all match; ok turns false when that
+// runs out.
+template <int NP>
+GP_DEVINL void ep_fetch(const DecodeLayerArgs& a, int t, const int (&w)[NP], uint32_t tag, uint32_t (&out)[2 * NP],
+                        bool& ok) {
+    const unsigned long long* base = a.ep_x + (int64_t)t * a.H;
+    for (uint32_t n = 0;; ++n) {
+        bool all = true;
+#pragma unroll
+        for (int i = 0; i < NP; ++i) {
+            unsigned long long v0, v1;
+            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(base + w[i]) : "memory");
+            all &= (uint32_t)(v0 >> 32) == tag && (uint32_t)(v1 >> 32) == tag;
+            out[2 * i] = (uint32_t)v0;
+            out[2 * i + 1] = (uint32_t)v1;
+        }
+        if (all) return;
+        if (n >= a.spin_limit) {
+            ok = false;
+            return;
+        }
+        __nanosleep(32);
+    }
+}
+
+// 32 consecutive x elements k0 .. k0+31 of token t from the exchange (k0 % 32 == 0),
+// in pieces of 8 (bf16: 16) elements so that few registers are live at once.
+GP_DEVINL void ep_x32(const DecodeLayerArgs& a, int t, int k0, uint32_t tag, float (&v)[32], bool& ok) {
+    if (a.x_bf16) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            int w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = (k0 + 16 * h) / 2 + 2 * i;
+            uint32_t u[8];
+            ep_fetch<4>(a, t, w, tag, u, ok);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[16 * h + 2 * i] = __uint_as_float(u[i] << 16);
+                v[16 * h + 2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            int w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) w[i] = k0 + 8 * h + 2 * i;
+            uint32_t u[8];
+            ep_fetch<4>(a, t, w, tag, u, ok);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[8 * h + i] = __uint_as_float(u[i]);
+        }
+    }
+}
+
+// x elements k .. k+3 of token t.
+GP_DEVINL float4 x4_of(const DecodeLayerArgs& a, int t, int k) {
+    const int64_t k0 = (int64_t)t * a.H + k;
+    if (a.x_bf16) {
+        const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + k0);
+        return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u), __uint_as_float(r.y << 16),
+                           __uint_as_float(r.y & 0xFFFF0000u));
+    }
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + k0);
 }
 
 // Per-lane view of one GEMV phase (in_dim = IN, NW warps, P passes): this
@@ -213,15 +300,10 @@ GP_DEVINL float load_quant(const void* x, int x_bf16, int64_t row, int in_dim, i
     return 0.25f * quant_i16<32>(v, xq);
 }
 
-// Tagged logit of token `tok`, expert e: one token is read by every CTA and
-// kept in kLogitCopies replicas (copy = reader's CTA % kLogitCopies); with
-// several tokens only CTA t reads token t's, one copy (copy 0).
+// Tagged logit of token `tok`, expert e: every CTA reads every token's, so
+// each is kept in kLogitCopies replicas (copy = reader's CTA % kLogitCopies).
 GP_DEVINL int64_t logit_word(int copy, int tok, int e, int E) {
-    return ((int64_t)(copy + tok) * E + e) * kLogitStride;
-}
-// Tagged top-k pick k of token t (several tokens), kLogitCopies replicas.
-GP_DEVINL int64_t pick_word(int copy, int tok, int k) {
-    return ((int64_t)(copy * kDecodeMaxTokens + tok) * 32 + k) * kLogitStride;
+    return (((int64_t)tok * kLogitCopies + copy) * E + e) * kLogitStride;
 }
 
 // One token's top-K by score + bias (ties to the lower id), weights
@@ -432,7 +514,9 @@ GP_DEVINL void quantise_unit(float v, uint32_t* words, int lane) {
     if (lane == 0) words[16] = __float_as_uint(0.25f * (amax * (1.0f / 32767.0f)));
 }
 
-template <int HH, int II, int PG, int RPWG>
+// EP: the expert-parallel exchange over peer memory (a separate instantiation,
+// so the one-GPU kernel carries none of its code).
+template <int HH, int II, int PG, int RPWG, bool EP>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -443,6 +527,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     constexpr uint32_t UNIT_BYTES = (uint32_t)H * 12u;  // one column unit of W_down: qs + aux of every row
     static_assert(H % RC == 0 && GU_BYTES % 16 == 0 && (RC * 2) % 16 == 0, "bulk copies need 16-byte sizes");
     const int E = a.E, K = a.K, S = a.stages, NT = a.n_tok;
+    constexpr bool ep = EP;  // expert-parallel exchange over peer memory
     const Smem L = decode_smem(H, I, S, NT);
     const uint32_t sbase = smem_u32(smem);
     // per stage: full (producer -> compute warps), pdone (compute warps ->
@@ -566,6 +651,22 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         for (int j = 0; j < EJ; ++j) bias[j] = a.corr && lane + 32 * j < E ? __ldg(a.corr + lane + 32 * j) : 0.f;
         pdl_wait();
         const uint32_t tag = ld_relaxed(a.sync + kSyncGen) + 1u;
+        const uint32_t ep_tag = ep ? ld_relaxed(a.ep_sync) + 1u : 0u;
+        // exchange words per token, and per CTA's share (even: 16-byte pairs)
+        const int ep_nw = a.x_bf16 ? H / 2 : H, ep_wpc = (((ep_nw + G - 1) / G) + 1) & ~1;
+        if (ep) {
+            // this CTA's share of this rank's token to every rank (no fence:
+            // the words carry the step's tag)
+            const uint32_t* xw = static_cast<const uint32_t*>(a.x);
+            const int w_end = min(ep_nw, (c + 1) * ep_wpc);
+            for (int w = c * ep_wpc + 2 * lane; w < w_end; w += 64) {  // (ep_nw and ep_wpc are even)
+                const unsigned long long v0 = ((unsigned long long)ep_tag << 32) | xw[w];
+                const unsigned long long v1 = ((unsigned long long)ep_tag << 32) | xw[w + 1];
+                for (int r = 0; r < a.ep_world; ++r)
+                    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};"
+                                 ::"l"(a.ep_x_peer[r] + (int64_t)a.ep_rank * H + w), "l"(v0), "l"(v1) : "memory");
+            }
+        }
         {   // this CTA's share of y = 0, ordered before its logits are published
             float4* y4 = reinterpret_cast<float4*>(a.y);
             for (int i = c * 32 + lane; i < NT * H / 4; i += G * 32) y4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -581,12 +682,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[(lane * RSPLIT + sl) * NT + t];
                     const unsigned long long v = ((unsigned long long)tag << 32) | __float_as_uint(lg);
                     if (e == a.withhold_logit) continue;  // (a test withholds one to make the top-k wait run out)
-                    if (NT == 1) {
 #pragma unroll
-                        for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.logits + logit_word(cp, 0, e, E), v);
-                    } else {
-                        st_relaxed64(a.logits + logit_word(0, t, e, E), v);
-                    }
+                    for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.logits + logit_word(cp, t, e, E), v);
                 }
             }
         }
@@ -597,38 +694,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0)
                           : topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0);
         } else {
-            // CTA t picks token t's experts and publishes them; every CTA
-            // then reads all tokens' picks (one more exchange, no CTA sorts
-            // n_tok tokens in turn)
-            if (c < NT) {
+            // every CTA picks every token's experts itself (no second exchange
+            // of picks); lane k of token t leaves pick k in the free router
+            // slice area, then pair p = t*K + k goes to lane p (p < 32) or p-32
+            int* s_pe = reinterpret_cast<int*>(s_slice);
+            float* s_pw = s_slice + kDecodeMaxRouted;
+            for (int t = 0; t < NT; ++t) {
                 int me = 0;
                 float mw = 0.f;
-                ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, 0, c, true, me, mw)
-                              : topk_token<EJ>(a, bias, tag, lane, 0, c, true, me, mw);
+                ok &= topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, t, c == 0, me, mw);  // (one instantiation: registers)
                 if (lane < K) {
-                    const unsigned long long v = ((unsigned long long)(tag & 0xFFFFu) << 48) |
-                                                 ((unsigned long long)(me & 0xFFFF) << 32) | __float_as_uint(mw);
-#pragma unroll
-                    for (int cp = 0; cp < kLogitCopies; ++cp) st_relaxed64(a.picks + pick_word(cp, c, lane), v);
+                    s_pe[t * K + lane] = me;
+                    s_pw[t * K + lane] = mw;
                 }
             }
+            __syncwarp();
             const int np = NT * K;
-            unsigned long long p0 = 0ull, p1 = 0ull;
-            uint32_t n = 0;
-            for (; n < a.spin_limit && ok; ++n) {
-                p0 = lane < np ? ld_relaxed64(a.picks + pick_word(c % kLogitCopies, lane / K, lane % K)) : 0ull;
-                p1 = lane + 32 < np ? ld_relaxed64(a.picks + pick_word(c % kLogitCopies, (lane + 32) / K, (lane + 32) % K))
-                                    : 0ull;
-                const bool got = (lane >= np || (uint32_t)(p0 >> 48) == (tag & 0xFFFFu)) &&
-                                 (lane + 32 >= np || (uint32_t)(p1 >> 48) == (tag & 0xFFFFu));
-                if (__all_sync(0xffffffffu, got)) break;
-                __nanosleep(TOPK_POLL_NS);
+            if (lane < np) {
+                e0 = s_pe[lane];
+                w0 = s_pw[lane];
             }
-            if (n == a.spin_limit) ok = false;
-            e0 = (int)((p0 >> 32) & 0xFFFFu);
-            w0 = __uint_as_float((uint32_t)p0);
-            e1 = (int)((p1 >> 32) & 0xFFFFu);
-            w1 = __uint_as_float((uint32_t)p1);
+            if (lane + 32 < np) {
+                e1 = s_pe[lane + 32];
+                w1 = s_pw[lane + 32];
+            }
         }
         if (!ok && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         // (after a timeout the slot list is built from whatever was read: the
@@ -738,6 +827,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         };
         if (warp < n_tasks) load_router(warp);
         pdl_wait();
+        const uint32_t ep_tag = ep ? ld_relaxed(a.ep_sync) + 1u : 0u;
+        bool xok = true;  // the exchange's words arrived (expert-parallel)
 
         // ---- router slices of this CTA's experts: warp task = (expert, slice),
         // one dot product per token ----
@@ -746,17 +837,34 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             const int sl = task % RSPLIT;
             for (int t = 0; t < NT; ++t) {
                 float acc = 0.f;
+                float4 xe[RV];  // expert-parallel: the lane's RV float4s of token t, fetched at once
+                if (ep) {
+                    if (a.x_bf16) {
+                        int w[RV];
+                        uint32_t u[2 * RV];
+#pragma unroll
+                        for (int i = 0; i < RV; ++i) w[i] = (sl * RSL + lane * 4 + i * 128) / 2;
+                        ep_fetch<RV>(a, t, w, ep_tag, u, xok);
+#pragma unroll
+                        for (int i = 0; i < RV; ++i)
+                            xe[i] = make_float4(__uint_as_float(u[2 * i] << 16), __uint_as_float(u[2 * i] & 0xFFFF0000u),
+                                                __uint_as_float(u[2 * i + 1] << 16),
+                                                __uint_as_float(u[2 * i + 1] & 0xFFFF0000u));
+                    } else {
+                        int w[2 * RV];
+                        uint32_t u[4 * RV];
+#pragma unroll
+                        for (int i = 0; i < 2 * RV; ++i) w[i] = sl * RSL + lane * 4 + (i / 2) * 128 + 2 * (i % 2);
+                        ep_fetch<2 * RV>(a, t, w, ep_tag, u, xok);
+#pragma unroll
+                        for (int i = 0; i < RV; ++i)
+                            xe[i] = make_float4(__uint_as_float(u[4 * i]), __uint_as_float(u[4 * i + 1]),
+                                                __uint_as_float(u[4 * i + 2]), __uint_as_float(u[4 * i + 3]));
+                    }
+                }
 #pragma unroll
                 for (int i = 0; i < RV; ++i) {
-                    const int64_t k0 = (int64_t)t * H + sl * RSL + lane * 4 + i * 128;
-                    float4 xv;
-                    if (a.x_bf16) {
-                        const uint2 r = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + k0);
-                        xv = make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xFFFF0000u),
-                                         __uint_as_float(r.y << 16), __uint_as_float(r.y & 0xFFFF0000u));
-                    } else {
-                        xv = *reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + k0);
-                    }
+                    const float4 xv = ep ? xe[i] : x4_of(a, t, sl * RSL + lane * 4 + i * 128);
                     acc = fmaf(wv[i].x, xv.x, acc);
                     acc = fmaf(wv[i].y, xv.y, acc);
                     acc = fmaf(wv[i].z, xv.z, acc);
@@ -767,6 +875,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             }
             if (lane == 0) mbar_arrive(rbar);
         }
+        if (ep && !__all_sync(0xffffffffu, xok) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
 
         if (!mbar_wait(tbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         const auto mg = lane_map<HH, NWC, PG>(warp, lane, stage0);
@@ -793,7 +902,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             if (jb.gu) {
                 if (tok != cur) {  // that token's activations
                     cur = tok;
-                    sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
+                    if (ep) {
+                        float v[32];
+                        ep_x32(a, cur, 32 * mg.sb, ep_tag, v, xok);
+                        sx4 = 0.25f * quant_i16<32>(v, xq);
+                        if (!__all_sync(0xffffffffu, xok)) { give_up(); break; }
+                    } else {
+                        sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
+                    }
                 }
                 if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, ph, a.spin_limit))) { give_up(); break; }
                 consume<HH, NWC, PG, RPWG>(mg, s * L.stage_bytes, xq, sx4, partial + (size_t)s * pstride, warp, lane);
@@ -842,15 +958,69 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         }
     }
 
-    // the last CTA out advances the launch generation (the tag of the next
-    // launch's exchanged words)
+    // The last CTA out advances the launch generation (the tag of the next
+    // launch's exchanged words).  Expert-parallel, the last CTA first adds
+    // every token's partial output into that token's owner's accumulator of
+    // this step's parity over NVLink, then (one system-scope fence) tells
+    // every other rank that this rank's sums are in, waits for every other
+    // rank's signal to this one, copies this rank's accumulator to ep_out and
+    // zeroes it: no rank adds into it again before this rank's next signal.
     named_bar_sync(1, (NWC + 1) * 32);
-    if (tid == 0) {
-        fence_acq_rel_gpu();
-        if (atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1) {
-            a.sync[kSyncGen] += 1u;
+    if constexpr (!EP) {
+        if (tid == 0) {
             fence_acq_rel_gpu();
-            a.sync[kSyncEnd] = 0;
+            if (atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1) {
+                a.sync[kSyncGen] += 1u;
+                fence_acq_rel_gpu();
+                a.sync[kSyncEnd] = 0;
+            }
+        }
+        return;
+    } else {
+        volatile uint32_t* s_last = s_abort + 1;
+        if (tid == 0) {
+            fence_acq_rel_gpu();
+            *s_last = atomicAdd(a.sync + kSyncEnd, 1u) == (unsigned)G - 1 ? 1u : 0u;
+            if (*s_last) fence_acq_rel_gpu();  // every CTA's sums into y are in
+        }
+        named_bar_sync(1, (NWC + 1) * 32);
+        if (*s_last) {
+            const uint32_t g = ld_relaxed(a.ep_sync);
+            const int64_t par = (int64_t)(g & 1u) * H;
+            for (int i = tid; i < NT * (H / 4); i += (NWC + 1) * 32) {  // y[t] into owner t's accumulator
+                const int t = i / (H / 4), q = i % (H / 4);
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(a.y + (int64_t)t * H) + q);
+                red_add_v4(a.ep_y[t] + par + 4 * q, v.x, v.y, v.z, v.w);
+            }
+            named_bar_sync(1, (NWC + 1) * 32);
+            if (tid == 0) {
+                fence_acq_rel_sys();
+                for (int r = 0; r < a.ep_world; ++r)
+                    if (r != a.ep_rank) red_release_sys_add64(a.ep_done[r], 1ull);
+                const unsigned long long target = (unsigned long long)(a.ep_world - 1) * (unsigned long long)(g + 1u);
+                for (uint32_t n = 0; ld_acquire_sys64(a.ep_done[a.ep_rank]) < target; ++n) {
+                    if (n >= a.spin_limit) {
+                        atomicOr(a.status, GP_DEV_TIMEOUT_FULL);
+                        break;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            named_bar_sync(1, (NWC + 1) * 32);
+            // this rank's token: out = its accumulator, which then starts step g + 2 at zero
+            float4* ys4 = reinterpret_cast<float4*>(a.ep_y[a.ep_rank] + par);
+            float4* y4 = reinterpret_cast<float4*>(a.ep_out);
+            for (int i = tid; i < H / 4; i += (NWC + 1) * 32) {
+                y4[i] = __ldcg(ys4 + i);
+                ys4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            named_bar_sync(1, (NWC + 1) * 32);
+            if (tid == 0) {
+                a.ep_sync[0] = g + 1u;
+                a.sync[kSyncGen] += 1u;
+                fence_acq_rel_gpu();
+                a.sync[kSyncEnd] = 0;
+            }
         }
     }
 }
@@ -871,19 +1041,30 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
     if (grid * kMaxOwned < a.E) return cudaErrorInvalidValue;  // router experts per CTA
     if (a.n_tok < 1 || a.n_tok > kDecodeMaxTokens || a.n_tok * a.K > kDecodeMaxRouted || a.own_tok < 0 ||
         a.own_tok >= a.n_tok || a.e_lo < 0 || a.e_cnt < 0 || a.e_lo + a.e_cnt > a.E || a.E >= 65536 ||
-        (a.n_tok > 1 && !a.picks) || !a.down_col || (reinterpret_cast<uintptr_t>(a.y) & 15))
+        !a.down_col || (reinterpret_cast<uintptr_t>(a.y) & 15))
         return cudaErrorInvalidValue;
     if (a.n_tok == 1 && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // one token: every expert
+    if (a.ep_world > 1) {  // the peer-memory exchange: one token per rank, every rank's block mapped
+        if (a.ep_world > kDecodeMaxTokens || a.n_tok != a.ep_world || a.ep_rank < 0 || a.ep_rank >= a.ep_world ||
+            a.own_tok != a.ep_rank || !a.ep_x || !a.ep_sync || !a.ep_out || (reinterpret_cast<uintptr_t>(a.ep_out) & 15))
+            return cudaErrorInvalidValue;
+        for (int r = 0; r < a.ep_world; ++r)
+            if (!a.ep_x_peer[r] || !a.ep_y[r] || !a.ep_done[r] || (reinterpret_cast<uintptr_t>(a.ep_y[r]) & 15) ||
+                (reinterpret_cast<uintptr_t>(a.ep_x_peer[r]) & 7) || (reinterpret_cast<uintptr_t>(a.ep_done[r]) & 7))
+                return cudaErrorInvalidValue;
+    }
     const Smem L = decode_smem(a.H, a.I, a.stages, a.n_tok);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
-    auto kern = decode_layer_kernel<5120, 1536, 4, 1>;
-    static std::atomic<unsigned long long> configured{0};  // per device
-    if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured)) return e0;
+    const bool ep = a.ep_world > 1;
+    auto kern = ep ? decode_layer_kernel<5120, 1536, 4, 1, true> : decode_layer_kernel<5120, 1536, 4, 1, false>;
+    static std::atomic<unsigned long long> configured[2] = {{0}, {0}};  // per device, per instantiation
+    if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured[ep])) return e0;
     // Co-residency: every CTA waits on data the others publish, so the grid
     // must fit the GPU at one CTA per SM.  Checked against the kernel's real
     // resource use (registers, shared memory) once per device; a grid larger
     // than the SMs that can hold a CTA is refused rather than left to time out.
-    static std::atomic<unsigned long long> fits{0};
+    static std::atomic<unsigned long long> fits_all[2] = {{0}, {0}};
+    std::atomic<unsigned long long>& fits = fits_all[ep];
     int dev = 0;
     if (cudaError_t e1 = cudaGetDevice(&dev)) return e1;
     const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;

@@ -162,6 +162,11 @@ struct CombineArgs {
 cudaError_t launch_combine(const CombineArgs& a, cudaStream_t st, bool pdl);
 
 // One MoE layer at batch 1 in one persistent kernel, one CTA per SM (decode_layer.cu).
+constexpr int kSyncGen = 0;                     // launch generation (tags exchanged logits and picks)
+constexpr int kSyncEnd = 1;                     // CTAs finished
+constexpr int kDecodeMaxTokens = 8;             // tokens per launch of the persistent kernel
+constexpr int kDecodeMaxRouted = 64;            // routed (token, expert) slots per launch
+constexpr int kDecodeSyncWords = 64;
 struct DecodeLayerArgs {
     const float* router;       // [E][H] fp32
     const float* corr;         // [E] or nullptr
@@ -190,7 +195,6 @@ struct DecodeLayerArgs {
     int e_lo, e_cnt;           // routed experts held (gate/up/down index e - e_lo; the shared expert at e_cnt)
     int own_tok;               // token whose shared expert runs in this launch
     unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
-    unsigned long long* picks;   // [decode_layer_pick_words()] top-k picks of each token, tagged (n_tok > 1)
     unsigned long long* hx;      // [decode_layer_h_words(I)] h of every (slot, unit), tagged: rows of routed slot s
                                  // at s * I, the shared expert's at kDecodeMaxRouted * I
     unsigned* sync;            // [kDecodeSyncWords] launch generation and finished-CTA count
@@ -200,6 +204,23 @@ struct DecodeLayerArgs {
     int cooperative;           // 1: cooperative launch instead of programmatic dependent launch
     uint32_t spin_limit;       // polls before any wait gives up (sets a GP_DEV_TIMEOUT_* bit)
     int withhold_logit;        // test hook: the router logit of this expert is never published (-1: none)
+    // Expert-parallel decode over peer memory (ep_world > 1; no collective
+    // library): n_tok = ep_world tokens, token t owned by rank t.  Each rank
+    // publishes its own token (x, [1][H]) into every rank's ep_x as words
+    // tagged with the EP step generation g + 1, sums its share of every token
+    // into y ([n_tok][H], local, as for several tokens), and at the end adds
+    // y[t] into owner t's accumulator ep_y[t] + (g & 1) * H over NVLink,
+    // signals every owner (ep_done[t]), waits for the other ranks' signals,
+    // copies its own accumulator to ep_out ([1][H]) and zeroes it for step
+    // g + 2 (the next signal orders that before any rank's adds there).
+    int ep_world;
+    int ep_rank;
+    unsigned long long* ep_x;                         // this rank's [kDecodeMaxTokens][H] tagged words
+    unsigned long long* ep_x_peer[kDecodeMaxTokens];  // every rank's ep_x (this rank's included)
+    float* ep_y[kDecodeMaxTokens];                    // every rank's accumulators [2][H] (by step parity)
+    unsigned long long* ep_done[kDecodeMaxTokens];    // every rank's done counter
+    unsigned* ep_sync;                                // this rank's EP step generation
+    float* ep_out;                                    // this rank's token's output [1][H]
 };
 // Tensor-core experts for large batches (tc_moe.cu).
 struct TcArgs {
@@ -235,17 +256,9 @@ cudaError_t launch_ep_pack(const void* x, int x_bf16, int H, int n, int K, const
 // Counter words of the persistent kernel: the generation counts launches, the
 // others are zero between launches; the host clears all of them (and the
 // tagged buffers) after a launch that reported an error.
-constexpr int kSyncGen = 0;                     // launch generation (tags exchanged logits and picks)
-constexpr int kSyncEnd = 1;                     // CTAs finished
-constexpr int kDecodeMaxTokens = 8;             // tokens per launch of the persistent kernel
-constexpr int kDecodeMaxRouted = 64;            // routed (token, expert) slots per launch
-constexpr int kDecodeSyncWords = 64;
-// Words of DecodeLayerArgs::logits, one word per 256-byte line: 8 replicas of
-// E tagged logits (one token: every CTA reads them), or one copy per token
-// (several tokens: one CTA reads each token's).
-inline size_t decode_layer_logit_words(int E) { return (size_t)8 * E * 32; }
-// Words of DecodeLayerArgs::picks: 8 replicas x kDecodeMaxTokens x 32 picks, one per 256-byte line.
-inline size_t decode_layer_pick_words() { return (size_t)8 * kDecodeMaxTokens * 32 * 32; }
+// Words of DecodeLayerArgs::logits, one word per 256-byte line: per token, 8
+// replicas of E tagged logits (every CTA reads every token's).
+inline size_t decode_layer_logit_words(int E) { return (size_t)kDecodeMaxTokens * 8 * E * 32; }
 // Words of DecodeLayerArgs::hx: one tagged h value per row of every slot's expert.
 inline size_t decode_layer_h_words(int I) { return (size_t)(kDecodeMaxRouted + 1) * I; }
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);

@@ -246,3 +246,56 @@ class ExpertParallelDecode:
         except RuntimeError as e:  # a collective that failed or timed out (a peer left)
             raise GpeedError(_capi.ERR_NCCL, f"expert-parallel decode step failed: {e}") from e
         return y
+
+
+class PeerDecode:
+    """Expert-parallel decode of one MoE layer with no collective library: one
+    token per rank per step, the exchanges inside the persistent kernel over
+    NVLink peer memory (gpeed_ep_setup / gpeed_ep_connect / gpeed_moe_decode_ep).
+
+    Setup (once per process group, collective): every rank allocates its
+    exchange block, the CUDA IPC handles are all-gathered on the host through
+    torch.distributed, and every rank maps the others' blocks.  A step is one
+    kernel launch per rank: its token reaches every rank as tagged words, all
+    tokens are routed, this rank's picks of every token add their down sums
+    straight into the owning rank's accumulator, and the launch ends when the
+    other ranks have signalled theirs.  Nothing is read back to the host, so
+    steps can be captured in CUDA graphs.  Every rank must run the same steps;
+    an optional StepGuard checks on the host that every rank is still there
+    before a step is launched."""
+
+    def __init__(self, ctx: Context, cfg: MoeConfig, layers, group=None, guard: StepGuard | None = None):
+        self.ctx, self.cfg, self.group, self.guard = ctx, cfg, group, guard
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if cfg.n_experts % self.world or self.world > 8 or self.world * cfg.top_k > 64:
+            raise GpeedError(_capi.ERR_UNSUPPORTED, f"{self.world} ranks, {cfg.n_experts} experts, top-{cfg.top_k}: "
+                                                    "2 .. 8 ranks splitting the experts evenly, at most 64 picks")
+        self.layers = {l.layer_id: l for l in (layers if isinstance(layers, (list, tuple)) else [layers])}
+        handle = (ctypes.c_uint8 * _capi.IPC_HANDLE_BYTES)()
+        call("gpeed_ep_setup", ctx.handle, self.world, self.rank, cfg.hidden, handle)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        blob = (ctypes.c_uint8 * (_capi.IPC_HANDLE_BYTES * self.world)).from_buffer_copy(b"".join(handles))
+        call("gpeed_ep_connect", ctx.handle, blob)
+        dist.barrier(group=self.group)  # every block zeroed and mapped before any rank writes into it
+
+    def close(self) -> None:
+        """Collective: every rank unmaps the others' blocks, then the group
+        meets, so no block is freed (with its context) while still mapped."""
+        torch.cuda.synchronize()
+        call("gpeed_ep_disconnect", self.ctx.handle)
+        dist.barrier(group=self.group)
+
+    def forward(self, layer_id: int, x: torch.Tensor, y: torch.Tensor | None = None, topk_ids=None, topk_w=None,
+                stream=None) -> torch.Tensor:
+        """x [1, H] (this rank's token, bf16 or fp32) -> y [1, H] fp32, the layer's output for it."""
+        if self.guard is not None:
+            self.guard()
+        H = self.cfg.hidden
+        x = x.reshape(1, H).contiguous()
+        if y is None:
+            y = torch.empty(1, H, dtype=torch.float32, device=x.device)
+        call("gpeed_moe_decode_ep", self.ctx.handle, self.layers[layer_id].layer_id, _ptr(x), _dtype_code(x), _ptr(y),
+             _ptr(topk_ids), _ptr(topk_w), _stream(stream))
+        return y

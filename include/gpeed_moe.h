@@ -251,6 +251,38 @@ GPEED_API int gpeed_moe_decode_partial(gpeed_ctx* ctx, int layer, const void* x_
                                        int own_tok, float* y_part_dev, const int* forced_topk_dev, int* topk_ids_dev,
                                        float* topk_w_dev, void* stream);
 
+/* Expert-parallel decode with no collective library: the step's exchanges
+ * run inside the persistent kernel over NVLink peer memory.  Each rank of a
+ * world of 2 .. 8 GPUs (one process per GPU) calls gpeed_ep_setup (allocates
+ * this rank's exchange block and returns its CUDA IPC handle,
+ * GPEED_IPC_HANDLE_BYTES bytes), hands every rank's handle to every rank (its
+ * own process group does that; gpeed_b200.ep.PeerDecode uses
+ * torch.distributed) and calls gpeed_ep_connect with the world's handles in
+ * rank order; then, every step, every rank calls gpeed_moe_decode_ep with its
+ * own token x ([1][H] bf16 or fp32) and receives that token's layer output y
+ * ([1][H] fp32).  The layer is this rank's expert range plus the shared
+ * expert (gpeed_moe_load_layer_range / _gguf / _synth_layer_range), E/world
+ * routed experts per rank.  Inside one launch: the token goes to every rank as
+ * tagged words, all world tokens are routed, this rank's picks of every token
+ * run, and their down sums are added straight into the owning rank's
+ * accumulator; the kernel ends when every other rank has signalled that its
+ * sums into this rank's accumulator are done.  Every rank must run the same
+ * sequence of steps (waits are bounded: a rank that does not take part makes
+ * the others' step time out, reported by gpeed_ctx_check, after which the
+ * group is set up again).  Plain peer loads, stores and reductions only: no
+ * TMA, multicast or switch reduction on peer memory.  topk_ids / topk_w:
+ * optional [world][K] picks of every token.  No counterpart in the reference
+ * (Model::moe_forward, model.cpp:692-756, runs every expert on one host). */
+#define GPEED_IPC_HANDLE_BYTES 64
+GPEED_API int gpeed_ep_setup(gpeed_ctx* ctx, int world, int rank, int hidden, void* handle_out);
+GPEED_API int gpeed_ep_connect(gpeed_ctx* ctx, const void* handles /* world x GPEED_IPC_HANDLE_BYTES */);
+GPEED_API int gpeed_moe_decode_ep(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, float* y_dev,
+                                  int* topk_ids_dev, float* topk_w_dev, void* stream);
+/* Unmaps the other ranks' blocks (after the group's last step, before any rank
+ * frees its own block with gpeed_ctx_destroy: every rank disconnects, the group
+ * meets at a barrier, then the contexts are destroyed). */
+GPEED_API int gpeed_ep_disconnect(gpeed_ctx* ctx);
+
 /* Loads only routed experts [expert_begin, expert_begin + expert_count) (their
  * GGUF bytes at gate/up/down) plus the shared expert; the router stays whole. */
 GPEED_API int gpeed_moe_load_layer_range(gpeed_ctx* ctx, int layer, const gpeed_moe_shape* shape, int expert_begin,

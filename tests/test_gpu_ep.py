@@ -303,3 +303,89 @@ def test_ep_decode_nccl_two_gpus(tmp_path):
         assert p.exitcode == 0
     for r in range(2):
         assert rel_l2(np.load(os.path.join(str(tmp_path), f"yd_{r}.npy")), y_ref[r]) < 1e-5
+
+
+# ---- expert-parallel decode over peer memory (no collective library on the data path) ----
+
+def _peer_decode_worker(rank, world, port, out_dir):
+    import torch.distributed as dist
+    from gpeed_b200 import GpeedError, _capi
+    from gpeed_b200.ep import PeerDecode
+    torch.cuda.set_device(rank)
+    # gloo, host only: it carries the IPC handles at setup and the final barrier
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        ctx = Context(rank)
+        cfg = MoeConfig()
+        lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+        layer = MoeLayer(ctx, cfg, layer_id=0).synth_range(_router(cfg), None, SEED, S0, lo, cnt)
+        pd = PeerDecode(ctx, cfg, layer)
+        X = _tokens(cfg, 3 * world).reshape(3, world, cfg.hidden)
+        ys, ids = [], []
+        for s in range(3):
+            tk = torch.full((world, cfg.top_k), -1, dtype=torch.int32, device="cuda")
+            y = pd.forward(0, X[s, rank:rank + 1].cuda(), topk_ids=tk)
+            ctx.check()
+            ys.append(y.cpu().numpy())
+            ids.append(tk.cpu().numpy())
+        np.save(os.path.join(out_dir, f"yp_{rank}.npy"), np.concatenate(ys))
+        np.save(os.path.join(out_dir, f"ip_{rank}.npy"), np.stack(ids))
+        # rank 1 takes no part in the next step: rank 0's waits for its token run
+        # out (a short limit) and the status says so; no fault, no hang
+        dist.barrier()
+        if rank == 0:
+            ctx.set_option(_capi.OPT_SPIN_LIMIT, 1 << 10)
+            pd.forward(0, X[0, 0:1].cuda())
+            try:
+                ctx.check()
+                msg = "no error"
+            except GpeedError as e:
+                msg = str(e)
+            with open(os.path.join(out_dir, "timeout.txt"), "w") as fh:
+                fh.write(msg)
+        dist.barrier()
+        pd.close()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_decode_peer_memory_two_gpus(tmp_path):
+    """PeerDecode on two GPUs: three steps, each rank's output equals the
+    one-GPU layer on its token (the two ranks' sums land in another order: to
+    rounding), the picks of both tokens equal the one-GPU routing; then a step
+    that one rank skips times out on the other, reported by gpeed_ctx_check."""
+    cfg = MoeConfig()
+    ctx = Context(0)
+    try:
+        full = MoeLayer(ctx, cfg, layer_id=810).synth(_router(cfg), None, SEED, S0)
+        X = _tokens(cfg, 6).reshape(3, 2, cfg.hidden)
+        y_ref = np.zeros((2, 3, cfg.hidden), np.float32)
+        id_ref = np.zeros((3, 2, cfg.top_k), np.int32)
+        for s in range(3):
+            for r in range(2):
+                tk = torch.empty(1, cfg.top_k, dtype=torch.int32, device="cuda")
+                y_ref[r, s] = full.forward(X[s, r:r + 1].cuda(), topk_ids=tk).cpu().numpy()[0]
+                id_ref[s, r] = tk.cpu().numpy()[0]
+        ctx.check()
+    finally:
+        ctx.close()
+    mpc = mp.get_context("spawn")
+    port = _free_port()
+    procs = [mpc.Process(target=_peer_decode_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    for r in range(2):
+        y = np.load(os.path.join(str(tmp_path), f"yp_{r}.npy"))
+        assert rel_l2(y, y_ref[r]) < 1e-5, rel_l2(y, y_ref[r])
+        ids = np.load(os.path.join(str(tmp_path), f"ip_{r}.npy"))
+        for s in range(3):
+            for t in range(2):
+                assert sorted(ids[s, t]) == sorted(id_ref[s, t])
+    msg = open(os.path.join(str(tmp_path), "timeout.txt")).read()
+    assert "device status" in msg and "no error" not in msg, msg
