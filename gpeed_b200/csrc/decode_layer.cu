@@ -138,14 +138,14 @@ GP_DEVINL uint32_t order_key(float f) {
 }
 
 // Token words of the expert-parallel exchange: token t's x as 64-bit words
-// {32 bits of payload (a bf16 pair, or one fp32), the step's tag}.  A reader
-// loads every word it needs at once, 16 bytes per load (w[i] even), checks
-// every tag, and loads again until they all match; ok turns false when that
-// runs out.
+// {32 bits of payload (a bf16 pair, or one fp32), the step's tag} at
+// ep_x[t * H + word].  A reader loads every word it needs at once, 16 bytes
+// per load (w[i] even), checks every tag, and loads again until they all
+// match (each round is a round trip to memory under load, so a reader asks
+// for all it needs in one round); ok turns false when that runs out.
 template <int NP>
-GP_DEVINL void ep_fetch(const DecodeLayerArgs& a, int t, const int (&w)[NP], uint32_t tag, uint32_t (&out)[2 * NP],
-                        bool& ok) {
-    const unsigned long long* base = a.ep_x + (int64_t)t * a.H;
+GP_DEVINL void ep_fetch(const DecodeLayerArgs& a, const int (&w)[NP], uint32_t tag, uint32_t (&out)[2 * NP], bool& ok) {
+    const unsigned long long* base = a.ep_x;  // w[i]: token * H + word
     for (uint32_t n = 0;; ++n) {
         bool all = true;
 #pragma unroll
@@ -173,9 +173,9 @@ GP_DEVINL void ep_x32(const DecodeLayerArgs& a, int t, int k0, uint32_t tag, flo
         for (int h = 0; h < 2; ++h) {
             int w[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) w[i] = (k0 + 16 * h) / 2 + 2 * i;
+            for (int i = 0; i < 4; ++i) w[i] = t * a.H + (k0 + 16 * h) / 2 + 2 * i;
             uint32_t u[8];
-            ep_fetch<4>(a, t, w, tag, u, ok);
+            ep_fetch<4>(a, w, tag, u, ok);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
                 v[16 * h + 2 * i] = __uint_as_float(u[i] << 16);
@@ -187,9 +187,9 @@ GP_DEVINL void ep_x32(const DecodeLayerArgs& a, int t, int k0, uint32_t tag, flo
         for (int h = 0; h < 4; ++h) {
             int w[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) w[i] = k0 + 8 * h + 2 * i;
+            for (int i = 0; i < 4; ++i) w[i] = t * a.H + k0 + 8 * h + 2 * i;
             uint32_t u[8];
-            ep_fetch<4>(a, t, w, tag, u, ok);
+            ep_fetch<4>(a, w, tag, u, ok);
 #pragma unroll
             for (int i = 0; i < 8; ++i) v[8 * h + i] = __uint_as_float(u[i]);
         }
@@ -314,29 +314,55 @@ GP_DEVINL int64_t logit_word(int copy, int tok, int e, int E) {
 // asc); a round then takes the warp maximum of the lanes' head keys (redux),
 // the lowest id holding it, and that lane pops its head.  Lane k < K returns
 // pick k in (my_e, my_w).  Returns false when the wait for the logits ran out.
+// Loads token tok's (and tok2's, when tok2 >= 0: both in one round of loads)
+// E tagged logits until every tag matches; false when the wait ran out.
+template <int EJ>
+GP_DEVINL bool poll_logits(const DecodeLayerArgs& a, uint32_t tag, int lane, int copy, int tok, int tok2,
+                           uint32_t (&w)[EJ], uint32_t (&w2)[EJ]) {
+    const int E = a.E;
+    for (uint32_t n = 0; n < a.spin_limit; ++n) {
+        bool ok = true;
+#pragma unroll
+        for (int j = 0; j < EJ; ++j) {  // (values kept as 32-bit logits, tags checked as they arrive)
+            const unsigned long long v =
+                lane + 32 * j < E ? ld_relaxed64(a.logits + logit_word(copy, tok, lane + 32 * j, E)) : 0ull;
+            const unsigned long long v2 = tok2 >= 0 && lane + 32 * j < E
+                                              ? ld_relaxed64(a.logits + logit_word(copy, tok2, lane + 32 * j, E)) : 0ull;
+            ok &= lane + 32 * j >= E || (uint32_t)(v >> 32) == tag;
+            ok &= tok2 < 0 || lane + 32 * j >= E || (uint32_t)(v2 >> 32) == tag;
+            w[j] = (uint32_t)v;
+            w2[j] = (uint32_t)v2;
+        }
+        if (__all_sync(0xffffffffu, ok)) return true;
+        __nanosleep(TOPK_POLL_NS);
+    }
+    return false;
+}
+
+template <int EJ>
+GP_DEVINL void select_topk(const DecodeLayerArgs& a, const float* bias, const uint32_t (&w)[EJ], int lane, int tok,
+                           bool write_out, int& my_e, float& my_w);
+
 template <int EJ>
 GP_DEVINL bool topk_token(const DecodeLayerArgs& a, const float* bias, uint32_t tag, int lane, int copy, int tok,
                           bool write_out, int& my_e, float& my_w) {
+    uint32_t w[EJ], w2[EJ];
+    const bool got = poll_logits<EJ>(a, tag, lane, copy, tok, -1, w, w2);
+    select_topk<EJ>(a, bias, w, lane, tok, write_out, my_e, my_w);
+    return got;
+}
+
+// One token's top-K from its E logits (w, one tagged word per expert lane + 32j).
+template <int EJ>
+GP_DEVINL void select_topk(const DecodeLayerArgs& a, const float* bias, const uint32_t (&w)[EJ], int lane, int tok,
+                           bool write_out, int& my_e, float& my_w) {
     const int E = a.E, K = a.K;
-    unsigned long long w[EJ];
-    uint32_t n = 0;
-    for (; n < a.spin_limit; ++n) {
-#pragma unroll
-        for (int j = 0; j < EJ; ++j)
-            w[j] = lane + 32 * j < E ? ld_relaxed64(a.logits + logit_word(copy, tok, lane + 32 * j, E)) : 0ull;
-        bool ok = true;
-#pragma unroll
-        for (int j = 0; j < EJ; ++j) ok &= lane + 32 * j >= E || (uint32_t)(w[j] >> 32) == tag;
-        if (__all_sync(0xffffffffu, ok)) break;
-        __nanosleep(TOPK_POLL_NS);
-    }
-    if (lane == 0) GP_STAMP(11);
     float score[EJ];
     uint32_t key[EJ], id[EJ];
 #pragma unroll
     for (int j = 0; j < EJ; ++j) {
         const int e = lane + 32 * j;
-        const float lg = e < E ? __uint_as_float((uint32_t)w[j]) : 0.f;
+        const float lg = e < E ? __uint_as_float(w[j]) : 0.f;
         score[j] = 1.0f / (1.0f + expf(-lg));
         key[j] = e < E ? order_key(score[j] + bias[j]) : 0u;  // 0: below every float's key
         id[j] = e < E ? (uint32_t)e : 0xffffffffu;
@@ -398,7 +424,6 @@ GP_DEVINL bool topk_token(const DecodeLayerArgs& a, const float* bias, uint32_t 
     my_w = a.norm_topk ? (my_s / denom) * a.routed_scale : my_s * a.routed_scale;
     if (write_out && a.topk_ids && lane < K) a.topk_ids[(int64_t)tok * K + lane] = my_e;
     if (write_out && a.topk_w && lane < K) a.topk_w[(int64_t)tok * K + lane] = my_w;
-    return n < a.spin_limit;
 }
 
 // Slot list of a launch from the picks of its tokens: pair p = t*K + k (lane
@@ -699,13 +724,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             // slice area, then pair p = t*K + k goes to lane p (p < 32) or p-32
             int* s_pe = reinterpret_cast<int*>(s_slice);
             float* s_pw = s_slice + kDecodeMaxRouted;
-            for (int t = 0; t < NT; ++t) {
+            constexpr int TS = EP ? 2 : 1;  // tokens' logits per round of loads (expert-parallel: registers allow two)
+            for (int t = 0; t < NT; t += TS) {
+                uint32_t w[EJ], w2[EJ];
+                ok &= poll_logits<EJ>(a, tag, lane, c % kLogitCopies, t, TS == 2 && t + 1 < NT ? t + 1 : -1, w, w2);
                 int me = 0;
                 float mw = 0.f;
-                ok &= topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, t, c == 0, me, mw);  // (one instantiation: registers)
+                select_topk<EJ>(a, bias, w, lane, t, c == 0, me, mw);
                 if (lane < K) {
                     s_pe[t * K + lane] = me;
                     s_pw[t * K + lane] = mw;
+                }
+                if (TS == 2 && t + 1 < NT) {
+                    select_topk<EJ>(a, bias, w2, lane, t + 1, c == 0, me, mw);
+                    if (lane < K) {
+                        s_pe[(t + 1) * K + lane] = me;
+                        s_pw[(t + 1) * K + lane] = mw;
+                    }
                 }
             }
             __syncwarp();
@@ -835,43 +870,68 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         for (int task = warp; task < n_tasks; task += NWC) {
             if (task != warp) load_router(task);
             const int sl = task % RSPLIT;
-            for (int t = 0; t < NT; ++t) {
-                float acc = 0.f;
-                float4 xe[RV];  // expert-parallel: the lane's RV float4s of token t, fetched at once
-                if (ep) {
+            if constexpr (!EP) {
+                for (int t = 0; t < NT; ++t) {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < RV; ++i) {
+                        const float4 xv = x4_of(a, t, sl * RSL + lane * 4 + i * 128);
+                        acc = fmaf(wv[i].x, xv.x, acc);
+                        acc = fmaf(wv[i].y, xv.y, acc);
+                        acc = fmaf(wv[i].z, xv.z, acc);
+                        acc = fmaf(wv[i].w, xv.w, acc);
+                    }
+                    acc = warp_sum(acc);
+                    if (lane == 0) s_slice[task * NT + t] = acc;
+                }
+            } else {
+                // this rank's own token from x, the others' from the exchange
+                {
+                    float acc = 0.f;
+#pragma unroll
+                    for (int i = 0; i < RV; ++i) {
+                        const float4 xv = x4_of(a, 0, sl * RSL + lane * 4 + i * 128);
+                        acc = fmaf(wv[i].x, xv.x, acc);
+                        acc = fmaf(wv[i].y, xv.y, acc);
+                        acc = fmaf(wv[i].z, xv.z, acc);
+                        acc = fmaf(wv[i].w, xv.w, acc);
+                    }
+                    acc = warp_sum(acc);
+                    if (lane == 0) s_slice[task * NT + a.ep_rank] = acc;
+                }
+                for (int t = 0; t < NT; ++t) {
+                    if (t == a.ep_rank) continue;
+                    float acc = 0.f;
                     if (a.x_bf16) {
                         int w[RV];
                         uint32_t u[2 * RV];
 #pragma unroll
-                        for (int i = 0; i < RV; ++i) w[i] = (sl * RSL + lane * 4 + i * 128) / 2;
-                        ep_fetch<RV>(a, t, w, ep_tag, u, xok);
+                        for (int i = 0; i < RV; ++i) w[i] = t * H + (sl * RSL + lane * 4 + i * 128) / 2;
+                        ep_fetch<RV>(a, w, ep_tag, u, xok);
 #pragma unroll
-                        for (int i = 0; i < RV; ++i)
-                            xe[i] = make_float4(__uint_as_float(u[2 * i] << 16), __uint_as_float(u[2 * i] & 0xFFFF0000u),
-                                                __uint_as_float(u[2 * i + 1] << 16),
-                                                __uint_as_float(u[2 * i + 1] & 0xFFFF0000u));
+                        for (int i = 0; i < RV; ++i) {
+                            acc = fmaf(wv[i].x, __uint_as_float(u[2 * i] << 16), acc);
+                            acc = fmaf(wv[i].y, __uint_as_float(u[2 * i] & 0xFFFF0000u), acc);
+                            acc = fmaf(wv[i].z, __uint_as_float(u[2 * i + 1] << 16), acc);
+                            acc = fmaf(wv[i].w, __uint_as_float(u[2 * i + 1] & 0xFFFF0000u), acc);
+                        }
                     } else {
                         int w[2 * RV];
                         uint32_t u[4 * RV];
 #pragma unroll
-                        for (int i = 0; i < 2 * RV; ++i) w[i] = sl * RSL + lane * 4 + (i / 2) * 128 + 2 * (i % 2);
-                        ep_fetch<2 * RV>(a, t, w, ep_tag, u, xok);
+                        for (int i = 0; i < 2 * RV; ++i) w[i] = t * H + sl * RSL + lane * 4 + (i / 2) * 128 + 2 * (i % 2);
+                        ep_fetch<2 * RV>(a, w, ep_tag, u, xok);
 #pragma unroll
-                        for (int i = 0; i < RV; ++i)
-                            xe[i] = make_float4(__uint_as_float(u[4 * i]), __uint_as_float(u[4 * i + 1]),
-                                                __uint_as_float(u[4 * i + 2]), __uint_as_float(u[4 * i + 3]));
+                        for (int i = 0; i < RV; ++i) {
+                            acc = fmaf(wv[i].x, __uint_as_float(u[4 * i]), acc);
+                            acc = fmaf(wv[i].y, __uint_as_float(u[4 * i + 1]), acc);
+                            acc = fmaf(wv[i].z, __uint_as_float(u[4 * i + 2]), acc);
+                            acc = fmaf(wv[i].w, __uint_as_float(u[4 * i + 3]), acc);
+                        }
                     }
+                    acc = warp_sum(acc);
+                    if (lane == 0) s_slice[task * NT + t] = acc;
                 }
-#pragma unroll
-                for (int i = 0; i < RV; ++i) {
-                    const float4 xv = ep ? xe[i] : x4_of(a, t, sl * RSL + lane * 4 + i * 128);
-                    acc = fmaf(wv[i].x, xv.x, acc);
-                    acc = fmaf(wv[i].y, xv.y, acc);
-                    acc = fmaf(wv[i].z, xv.z, acc);
-                    acc = fmaf(wv[i].w, xv.w, acc);
-                }
-                acc = warp_sum(acc);
-                if (lane == 0) s_slice[task * NT + t] = acc;
             }
             if (lane == 0) mbar_arrive(rbar);
         }
@@ -902,13 +962,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             if (jb.gu) {
                 if (tok != cur) {  // that token's activations
                     cur = tok;
-                    if (ep) {
+                    if (ep && cur != a.ep_rank) {  // another rank's token: from the exchange
                         float v[32];
                         ep_x32(a, cur, 32 * mg.sb, ep_tag, v, xok);
                         sx4 = 0.25f * quant_i16<32>(v, xq);
                         if (!__all_sync(0xffffffffu, xok)) { give_up(); break; }
-                    } else {
-                        sx4 = load_quant(a.x, a.x_bf16, cur, H, mg.sb, xq);
+                    } else {  // (expert-parallel: this rank's own token is row 0 of x)
+                        sx4 = load_quant(a.x, a.x_bf16, ep ? 0 : cur, H, mg.sb, xq);
                     }
                 }
                 if (!__all_sync(0xffffffffu, mbar_wait(full0 + 8u * s, ph, a.spin_limit))) { give_up(); break; }
