@@ -17,13 +17,16 @@ tensor-core grouped GEMMs; with --ep and N >= 2 GPUs the experts are split over
 the GPUs with NCCL all-to-all dispatch and combine), --workload stack40 (config
 5 on one GPU: 40 layers, decode batches 1 to 256).
 
-N > 1 (launched by torchrun): expert parallelism.  The same layer's 160
-routed experts are split 160/N per GPU (plus the shared expert on every GPU);
-each rank brings one token per step (weak scaling).  A step is one persistent
-kernel per rank (gpeed_moe_decode_ep): its token goes to every rank over
-NVLink peer memory, all N tokens are routed, the rank runs its experts' share
-of each plus its own token's shared expert and adds the sums straight into
-the owning rank's output; no collective library on the data path.  With
+N > 1 (launched by torchrun): expert parallelism.  Every GPU holds 1/N of
+every expert's intermediate rows (units of 32 rows, the tensor-parallel split
+of each expert; --ep-split experts instead gives each GPU 160/N whole routed
+experts plus the shared expert); each rank brings one token per step (weak
+scaling).  A step is one persistent kernel per rank (gpeed_moe_decode_ep): its
+token goes to every rank over NVLink peer memory, all N tokens are routed,
+the rank runs its share of every pick (its slice of each expert; or, with
+expert ranges, the picks in its range and its own token's shared expert) and
+adds the sums straight into the owning rank's output; no collective library
+on the data path.  With
 --ep-nccl the exchanges are an NCCL all-gather and reduce-scatter around
 gpeed_moe_decode_partial instead.  Steps are captured in CUDA graphs.  value =
 tokens over all ranks / the slowest rank's time.  The reference arm runs on
@@ -381,13 +384,15 @@ def run_gpu(args, rank, local_rank, world):
 
 def run_gpu_ep(args, rank, local_rank, world):
     """BASELINE config 2's layer, expert-parallel over `world` GPUs (the N > 1
-    default).  Rank r holds routed experts [r*E/N, (r+1)*E/N) of every layer
-    copy plus the shared expert and brings its own token each step.  A step
-    (one token per rank through one layer) is one persistent kernel per rank,
+    default).  Rank r holds units [r*NU/N, (r+1)*NU/N) of every expert of
+    every layer copy (--ep-split units: 1/N of each expert's 1536 intermediate
+    rows), or routed experts [r*E/N, (r+1)*E/N) plus the shared expert
+    (--ep-split experts), and brings its own token each step.  A step (one
+    token per rank through one layer) is one persistent kernel per rank,
     gpeed_moe_decode_ep: the tokens go to every rank over NVLink peer memory,
-    all N are routed, this rank's picks of each run and add their sums into
-    the owning rank's output, the launch ends when the other ranks' sums into
-    this rank's output are done.  With --ep-nccl the exchanges are NCCL
+    all N are routed, this rank's share of each pick runs and adds its sums
+    into the owning rank's output, the launch ends when the other ranks' sums
+    into this rank's output are done.  With --ep-nccl the exchanges are NCCL
     collectives instead (all-gather of the tokens, gpeed_moe_decode_partial,
     reduce-scatter of the partial outputs).  Layer copies rotate so each
     step's weights come from HBM, and the steps are captured back to back in
@@ -402,9 +407,16 @@ def run_gpu_ep(args, rank, local_rank, world):
     ctx = Context(local_rank)
     cfg = MoeConfig()
     L = args.layers
-    lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
-    layers = [MoeLayer(ctx, cfg, layer_id=l).synth_range(router_for(l), None, 1000 + l, 0, lo, cnt)
-              for l in range(L)]
+    sliced = args.ep_split == "units"
+    if sliced:
+        u_lo, u_cnt = MoeLayer.unit_slice(cfg, rank, world)
+        layers = [MoeLayer(ctx, cfg, layer_id=l).synth(router_for(l), None, 1000 + l, 0).slice_units(u_lo, u_cnt)
+                  for l in range(L)]
+        lo, cnt = 0, E
+    else:
+        lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+        layers = [MoeLayer(ctx, cfg, layer_id=l).synth_range(router_for(l), None, 1000 + l, 0, lo, cnt)
+                  for l in range(L)]
     peer = not args.ep_nccl
     pd = PeerDecode(ctx, cfg, layers) if peer else None
     stream = torch.cuda.Stream()
@@ -505,7 +517,10 @@ def run_gpu_ep(args, rank, local_rank, world):
         slots.append(int(((g >= lo) & (g < lo + cnt)).sum()))
     torch.cuda.synchronize()
     mean_slots = sum(slots) / L
-    kern_bytes = (mean_slots + 1) * EXPERT_BYTES + ROUTER_BYTES + world * H * (2 + 4)
+    # expert bytes this rank streams: its slice of every pick and every token's
+    # shared expert, or its range's picks and its own token's shared expert
+    expert_units = (mean_slots + world) / world if sliced else mean_slots + 1
+    kern_bytes = expert_units * EXPERT_BYTES + ROUTER_BYTES + world * H * (2 + 4)
     achieved = kern_bytes / (ph[1] * 1e-3) / 1e9
 
     # ---- end to end through the public API with host buffers ----
@@ -547,15 +562,18 @@ def run_gpu_ep(args, rank, local_rank, world):
             "config": {"workload": "decode1: MoE layer decode, batch 1 (BASELINE config 2)", "hidden": H,
                        "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
                        "layer_copies": L, "l2": f"inputs larger than L2: steps rotate over {L} layer copies",
-                       "parallelism": (f"ep{world}: {cnt} routed experts per GPU + the shared expert; one token "
-                                       f"per GPU per step; one persistent kernel per GPU exchanging tokens and "
-                                       f"partial outputs over NVLink peer memory (no collective library)" if peer else
-                                       f"ep{world}: {cnt} routed experts per GPU + the shared expert; one token "
-                                       f"per GPU per step; NCCL all-gather of tokens, one persistent kernel per "
-                                       f"GPU, NCCL reduce-scatter of partial outputs"),
+                       "parallelism": (f"ep{world}: " + (f"1/{world} of every expert's units per GPU ({u_cnt} of "
+                                                         f"{I // 32} units of 32 rows)" if sliced else
+                                                         f"{cnt} routed experts per GPU + the shared expert") +
+                                       "; one token per GPU per step; " +
+                                       ("one persistent kernel per GPU exchanging tokens and partial outputs over "
+                                        "NVLink peer memory (no collective library)" if peer else
+                                        "NCCL all-gather of tokens, one persistent kernel per GPU, NCCL "
+                                        "reduce-scatter of partial outputs")),
                        "phase_ms": ({"kernel": ph[1]} if peer else
                                     {"all_gather": ph[0], "experts_kernel": ph[1], "reduce_scatter": ph[2]}),
                        "routed_slots_per_gpu_rank0": mean_slots,
+                       "expert_equivalents_streamed_per_gpu": expert_units,
                        "per_gpu_kernel_hbm_gbs": achieved},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None,
@@ -1201,6 +1219,8 @@ def main():
     ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
     ap.add_argument("--ep-nccl", action="store_true",
                     help="expert-parallel decode (--gpus N > 1) with NCCL collectives instead of the peer-memory exchange")
+    ap.add_argument("--ep-split", default="units", choices=["units", "experts"],
+                    help="expert-parallel decode: each GPU holds 1/N of every expert (units, default) or E/N experts")
     ap.add_argument("--ep", action="store_true",
                     help="prefill with the experts split over the GPUs (NCCL all-to-all); needs --gpus >= 2")
     args = ap.parse_args()

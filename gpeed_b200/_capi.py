@@ -83,6 +83,7 @@ SIGNATURES = {
     "gpeed_ep_setup": [_vp, _i, _i, _i, _vp],
     "gpeed_ep_connect": [_vp, _vp],
     "gpeed_moe_decode_ep": [_vp, _i, _vp, _i, _vp, _vp, _vp, _vp],
+    "gpeed_moe_slice_units": [_vp, _i, _i, _i],
     "gpeed_ep_disconnect": [_vp],
     "gpeed_ep_pack": [_vp, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
     "gpeed_moe_experts": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp],

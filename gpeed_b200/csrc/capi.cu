@@ -61,6 +61,12 @@ struct Layer {
     // then the shared expert at local index e_cnt (all of them unless the
     // layer was loaded for expert parallelism)
     int e_lo = 0, e_cnt = 0;
+    // units of 32 intermediate rows of every expert held here: [u_lo, u_lo +
+    // u_cnt) of inter / 32 (gpeed_moe_slice_units; all of them otherwise).  A
+    // sliced layer keeps only the gate/up row groups and down column slabs of
+    // its units, for the persistent decode kernel.
+    int u_lo = 0, u_cnt = 0;
+    bool sliced() const { return u_cnt != shape.inter / 32; }
     // the router weights split into bf16 hi/lo/lo2 rows for the tensor-core router (or nullptr)
     uint16_t* router_split = nullptr;
     int router_nb = 0;
@@ -327,6 +333,7 @@ int alloc_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int e_lo, int
     L.shape = *s;
     L.e_lo = e_lo;
     L.e_cnt = e_cnt;
+    L.u_cnt = I / 32;
     L.gu_stride = gp::repacked_bytes(I, H);
     L.d_stride = gp::repacked_bytes(H, I);
     const cudaMemcpyKind kind = on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
@@ -513,6 +520,9 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     da.e_lo = L.e_lo;
     da.e_cnt = L.e_cnt;
     da.own_tok = own_tok;
+    da.u_lo = L.u_lo;
+    da.u_cnt = L.u_cnt;
+    da.shared_all = L.sliced() ? 1 : 0;  // a slice of every token's shared expert runs on every rank
     da.logits = c->logits.p;
     da.hx = c->hx.p;
     da.sync = c->sync;
@@ -954,6 +964,62 @@ int gpeed_moe_synth_layer(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, con
     return gpeed_moe_synth_layer_range(c, layer, s, 0, s->n_experts, router_w, corr, on_device, seed, stream0);
 }
 
+int gpeed_moe_slice_units(gpeed_ctx* c, int layer, int unit_begin, int unit_count) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    Layer& L = it->second;
+    const gpeed_moe_shape& s = L.shape;
+    const int H = s.hidden, I = s.inter, NU = I / 32, E = s.n_experts;
+    if (L.sliced()) return fail(GPEED_ERR_INVALID, "layer %d is already sliced", layer);
+    if (L.e_cnt != E) return fail(GPEED_ERR_INVALID, "layer %d holds an expert range: slice a whole layer", layer);
+    if (!L.down_col || !gp::decode_layer_slice_supported(I, unit_count))
+        return fail(GPEED_ERR_UNSUPPORTED, "no persistent decode kernel for %d of the %d units of inter %d", unit_count,
+                    NU, I);
+    if (unit_begin < 0 || unit_begin + unit_count > NU || unit_begin % unit_count)
+        return fail(GPEED_ERR_INVALID, "units [%d, %d): a whole slice of the %d, starting at a multiple of its size",
+                    unit_begin, unit_begin + unit_count, NU);
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    const int NE = L.e_cnt + s.n_shared;
+    // gate/up: 4 row groups of 8 rows per unit; down: the units' column slabs,
+    // then the 256-input d blocks they fall in (repacked_bytes, launch_repack_cols)
+    const int64_t tile = gp::repacked_bytes(8, H), unit_col = (int64_t)H * 12;
+    const int blk_lo = unit_begin / 8, nblk = (unit_begin + unit_count - 1) / 8 - blk_lo + 1;
+    const int64_t gu_w = (int64_t)unit_count * 4 * tile;
+    const int64_t dc_w = (int64_t)unit_count * unit_col, dd_w = (int64_t)nblk * H * 2;
+    uint8_t *g = nullptr, *u = nullptr, *dc = nullptr;
+    auto undo = [&]() { cudaFree(g); cudaFree(u); cudaFree(dc); };
+    if (cudaMalloc(&g, gu_w * NE + gp::repacked_bytes(32, H)) != cudaSuccess ||
+        cudaMalloc(&u, gu_w * NE + gp::repacked_bytes(32, H)) != cudaSuccess ||
+        cudaMalloc(&dc, (dc_w + dd_w) * NE) != cudaSuccess) {
+        undo();
+        cudaGetLastError();
+        return fail(GPEED_ERR_CUDA, "out of device memory slicing layer %d", layer);
+    }
+    const cudaMemcpyKind d2d = cudaMemcpyDeviceToDevice;
+    cudaError_t e = cudaMemcpy2D(g, gu_w, L.gate + unit_begin * 4 * tile, L.gu_stride, gu_w, NE, d2d);
+    if (!e) e = cudaMemcpy2D(u, gu_w, L.up + unit_begin * 4 * tile, L.gu_stride, gu_w, NE, d2d);
+    if (!e) e = cudaMemcpy2D(dc, dc_w + dd_w, L.down_col + unit_begin * unit_col, L.dc_stride, dc_w, NE, d2d);
+    if (!e) e = cudaMemcpy2D(dc + dc_w, dc_w + dd_w, L.down_col + NU * unit_col + (int64_t)blk_lo * H * 2, L.dc_stride,
+                             dd_w, NE, d2d);
+    if (e) {
+        undo();
+        return fail(GPEED_ERR_CUDA, "slicing layer %d: %s", layer, cudaGetErrorString(e));
+    }
+    cudaFree(L.gate); cudaFree(L.up); cudaFree(L.down); cudaFree(L.down_col);
+    L.gate = g;
+    L.up = u;
+    L.down = nullptr;
+    L.down_col = dc;
+    L.gu_stride = gu_w;
+    L.d_stride = 0;
+    L.dc_stride = dc_w + dd_w;
+    L.u_lo = unit_begin;
+    L.u_cnt = unit_count;
+    return GPEED_OK;
+}
+
 int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, float* y, const int* forced,
                       int* topk_ids, float* topk_w, void* stream) {
     if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
@@ -968,9 +1034,9 @@ int gpeed_moe_forward(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n
     const Layer& L = it->second;
     const gpeed_moe_shape& s = L.shape;
     const int H = s.hidden, I = s.inter, E = s.n_experts, K = s.top_k;
-    if (L.e_cnt != E)
-        return fail(GPEED_ERR_INVALID, "layer %d holds experts [%d, %d) of %d: use the expert-parallel entry points",
-                    layer, L.e_lo, L.e_lo + L.e_cnt, E);
+    if (L.e_cnt != E || L.sliced())
+        return fail(GPEED_ERR_INVALID, "layer %d holds experts [%d, %d) of %d, units [%d, %d): use the "
+                    "expert-parallel entry points", layer, L.e_lo, L.e_lo + L.e_cnt, E, L.u_lo, L.u_lo + L.u_cnt);
     int rc;
     if ((rc = set_device(c))) return rc;
     if ((rc = ensure_scratch(c, n, E, K, H, I))) return rc;
@@ -1128,15 +1194,16 @@ int gpeed_moe_decode_partial(gpeed_ctx* c, int layer, const void* x, int x_dtype
 // ---- expert-parallel decode over peer memory ----
 // Block of one rank: [kDecodeMaxTokens][H] tagged token words, then its two
 // accumulators [2][H] fp32 (by step parity), its local partial outputs
-// [kDecodeMaxTokens][H] fp32, its done counter (u64) and its EP step
-// generation.
+// [kDecodeMaxTokens][H] fp32, its done counter (u64), its EP step
+// generation and its tagged picks [kDecodeMaxTokens][32][2] u64.
 namespace {
 size_t ep_x_bytes(int H) { return (size_t)gp::kDecodeMaxTokens * H * sizeof(unsigned long long); }
 size_t ep_y_off(int H) { return ep_x_bytes(H); }
 size_t ep_part_off(int H) { return (ep_y_off(H) + (size_t)2 * H * 4 + 255) & ~(size_t)255; }
 size_t ep_done_off(int H) { return (ep_part_off(H) + (size_t)gp::kDecodeMaxTokens * H * 4 + 255) & ~(size_t)255; }
 size_t ep_sync_off(int H) { return ep_done_off(H) + 256; }
-size_t ep_block_bytes(int H) { return ep_sync_off(H) + 256; }
+size_t ep_pk_off(int H) { return ep_sync_off(H) + 256; }
+size_t ep_block_bytes(int H) { return ep_pk_off(H) + (size_t)gp::kDecodeMaxTokens * 32 * 16; }
 }  // namespace
 
 void ep_release(gpeed_ctx* c) {
@@ -1238,8 +1305,10 @@ int gpeed_moe_decode_ep(gpeed_ctx* c, int layer, const void* x, int x_dtype, flo
         da.ep_x_peer[r] = reinterpret_cast<unsigned long long*>(c->ep.peer[r]);
         da.ep_y[r] = reinterpret_cast<float*>(c->ep.peer[r] + ep_y_off(H));
         da.ep_done[r] = reinterpret_cast<unsigned long long*>(c->ep.peer[r] + ep_done_off(H));
+        da.ep_pk_peer[r] = reinterpret_cast<unsigned long long*>(c->ep.peer[r] + ep_pk_off(H));
     }
     da.ep_sync = reinterpret_cast<unsigned*>(c->ep.base + ep_sync_off(H));
+    da.ep_pk = reinterpret_cast<unsigned long long*>(c->ep.base + ep_pk_off(H));
     GP_CUDA(gp::launch_decode_layer(da, c->num_sms, st));
     return GPEED_OK;
 }
@@ -1350,6 +1419,7 @@ int gpeed_moe_experts(gpeed_ctx* c, int layer, const void* rows, int rows_dtype,
     if (!rows || !expert_ids || !out || (reinterpret_cast<uintptr_t>(rows) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
         return fail(GPEED_ERR_INVALID, "rows and out must be 16-byte aligned device pointers; expert_ids required");
     const Layer& L = it->second;
+    if (L.sliced()) return fail(GPEED_ERR_INVALID, "layer %d holds a slice of each expert's units", layer);
     const gpeed_moe_shape& s = L.shape;
     const int H = s.hidden, I = s.inter, El = L.e_cnt + s.n_shared;
     int rc;

@@ -124,6 +124,12 @@ GP_DEVINL void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memo
 GP_DEVINL void red_add_v4(float* p, float a, float b, float c, float d) {
     asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
+// The same at system scope: an owner's accumulator also takes the other
+// GPUs' adds (expert-parallel).
+GP_DEVINL void red_add_sys_v4(float* p, float a, float b, float c, float d) {
+    asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
 
 // Warp-uniform view of the CTA's abort flag.  Lanes read the volatile word
 // separately and may see it change between reads; every branch that contains
@@ -142,7 +148,8 @@ GP_DEVINL uint32_t order_key(float f) {
 // ep_x[t * H + word].  A reader loads every word it needs at once, 16 bytes
 // per load (w[i] even), checks every tag, and loads again until they all
 // match (each round is a round trip to memory under load, so a reader asks
-// for all it needs in one round); ok turns false when that runs out.
+// for all it needs in one round, and waits longer between rounds as it goes
+// on); ok turns false when that runs out.
 template <int NP>
 GP_DEVINL void ep_fetch(const DecodeLayerArgs& a, const int (&w)[NP], uint32_t tag, uint32_t (&out)[2 * NP], bool& ok) {
     const unsigned long long* base = a.ep_x;  // w[i]: token * H + word
@@ -161,7 +168,9 @@ GP_DEVINL void ep_fetch(const DecodeLayerArgs& a, const int (&w)[NP], uint32_t t
             ok = false;
             return;
         }
-        __nanosleep(32);
+        // growing pauses: many lanes poll at once, and their loads must not
+        // crowd out the SM's other memory traffic (router, logits, copies)
+        __nanosleep(n < 3 ? 128u << n : 1024u);
     }
 }
 
@@ -491,38 +500,35 @@ __host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok) {
 GP_DEVINL int jobs_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
 
 // One pipeline stage of work.  Job k of a launch, in the order: the shared
-// expert's gate/up tiles (ngs = NU * TPU of them; no routing needed), the
-// routed slots' gate/up tiles (ngr = slots * NU * TPU), the shared expert's
-// down chunks (NU * NCH), the routed slots' down chunks (slots * NU * NCH).  A
-// gate/up tile (slot, unit, j < TPU) gives h rows unit*32 + j*8 .. +7; a down
-// chunk (slot, unit, j < NCH) adds the unit's 32 input columns into output
-// rows j*RC .. +RC-1 and needs the unit's 32 h rows, which tiles earlier in
-// the order (on any CTA) produced.
+// slots' gate/up tiles (no routing needed), the routed slots' gate/up tiles,
+// the shared slots' down chunks, the routed slots' down chunks; each slot
+// covers the launch's UC units (all NU of an expert, or the rank's slice when
+// every rank holds a slice of every expert).  A gate/up tile (slot, unit,
+// j < TPU) gives h rows unit*32 + j*8 .. +7; a down chunk (slot, unit,
+// j < NCH) adds the unit's 32 input columns into output rows j*RC .. +RC-1
+// and needs the unit's 32 h rows, which tiles earlier in the order (on any
+// CTA) produced.
 struct Job {
     bool gu;
-    int slot, unit, j;  // slot -1: the shared expert
+    int slot, unit, j;  // slot < 0: shared slot -1 - slot; unit: index within the launch's unit range
 };
-// (Every division is by a compile-time constant: the producer decodes a job on
-// its critical path, sharing issue slots with the compute warps.)
-template <int NU, int NCH>
-GP_DEVINL Job job_of(int k, int nsr) {
-    constexpr int GS = NU * TPU, DS = NU * NCH;  // jobs per slot, each kind
-    const int cyc = GS * (nsr + 1);
+// UC units per slot (all NU of an expert, or a slice of them); nss shared
+// slots (one, or one per token) come before the nsr routed ones.  (Every
+// division is by a compile-time constant: the producer decodes a job on its
+// critical path, sharing issue slots with the compute warps.)
+template <int UC, int NCH>
+GP_DEVINL Job job_of(int k, int nss, int nsr) {
+    constexpr int GS = UC * TPU, DS = UC * NCH;  // jobs per slot, each kind
+    const int cyc = GS * (nss + nsr);
     if (k < cyc) {
-        int slot = -1;
-        if (k >= GS) {
-            slot = (k - GS) / GS;
-            k -= (slot + 1) * GS;
-        }
-        return {true, slot, k / TPU, k % TPU};
+        const int si = k / GS;
+        k -= si * GS;
+        return {true, si < nss ? -1 - si : si - nss, k / TPU, k % TPU};
     }
     k -= cyc;
-    int slot = -1;
-    if (k >= DS) {
-        slot = (k - DS) / DS;
-        k -= (slot + 1) * DS;
-    }
-    return {false, slot, k / NCH, k % NCH};
+    const int si = k / DS;
+    k -= si * DS;
+    return {false, si < nss ? -1 - si : si - nss, k / NCH, k % NCH};
 }
 
 // Quantises the unit of h held one value per lane exactly as a lane quantises
@@ -540,8 +546,10 @@ GP_DEVINL void quantise_unit(float v, uint32_t* words, int lane) {
 }
 
 // EP: the expert-parallel exchange over peer memory (a separate instantiation,
-// so the one-GPU kernel carries none of its code).
-template <int HH, int II, int PG, int RPWG, bool EP>
+// so the one-GPU kernel carries none of its code).  UC: units of each slot's
+// expert that this launch runs (NU, or NU / N when each of N ranks holds a
+// slice of every expert).
+template <int HH, int II, int PG, int RPWG, bool EP, int UC>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -596,11 +604,23 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     __syncthreads();
 
     // Jobs of this CTA: k = c + m*G.  Before the routing is known only the
-    // shared expert's gate/up tiles (k < nsh) can be decoded; the total needs
-    // the routed slot count.
-    const int nsh = NU * TPU;
+    // shared slots' gate/up tiles (k < nsh) can be decoded; the total needs
+    // the routed slot count.  Shared slot i is token i's shared expert when
+    // every token's runs here (nss = n_tok, from own_tok on), else own_tok's
+    // (nss = 1).
+    static_assert(NU % UC == 0, "a slice is a whole fraction of the units");
+    const int nss = a.shared_all ? NT : 1;
+    const int nsh = nss * UC * TPU;
     auto routed_slots = [&]() { return min(max(*s_nsr, 0), kDecodeMaxRouted); };
-    auto total_jobs = [&](int nsr) { return (nsr + 1) * NU * (TPU + NCH); };
+    auto total_jobs = [&](int nsr) { return (nsr + nss) * UC * (TPU + NCH); };
+    auto hx_row = [&](int slot) { return slot < 0 ? kDecodeMaxRouted + (-1 - slot) : slot; };
+    // (shared slots from own_tok on: its activations are local in expert-parallel runs)
+    auto tok_of = [&](int slot) {
+        if (slot >= 0) return s_st[slot];
+        if (!a.shared_all) return a.own_tok;
+        const int t = -1 - slot + a.own_tok;
+        return t < NT ? t : t - NT;
+    };
 
     if (warp == PROD) {
         // ================= producer (lane 0 issues) =================
@@ -619,16 +639,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 const uint8_t *p0, *p1, *p2;
             };
             auto job_src = [&](int m) -> Src {
-                const Job jb = job_of<NU, NCH>(c + m * G, nsr);
+                const Job jb = job_of<UC, NCH>(c + m * G, nss, nsr);
                 const int e = jb.slot < 0 ? a.e_cnt : s_se[jb.slot];
                 if (jb.gu) {
                     const int64_t o = (int64_t)e * a.gu_stride + (int64_t)(jb.unit * TPU + jb.j) * GU_BYTES;
                     return {a.gate + o, a.up + o, nullptr};
                 }
+                // the slab holds units u_lo .. u_lo+UC-1, then the d blocks from u_lo / 8 on
                 const uint8_t* dc = a.down_col + (int64_t)e * a.dc_stride;
+                const int dblk = ((a.u_lo + jb.unit) >> 3) - (a.u_lo >> 3);
                 return {dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)jb.j * RC * 8,
                         dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)H * 8 + (int64_t)jb.j * RC * 4,
-                        dc + (int64_t)NU * UNIT_BYTES + (int64_t)(jb.unit >> 3) * H * 2 + (int64_t)jb.j * RC * 2};
+                        dc + (int64_t)UC * UNIT_BYTES + (int64_t)dblk * H * 2 + (int64_t)jb.j * RC * 2};
             };
             for (int m = 0;; ++m) {
                 if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) need the slot list
@@ -701,7 +723,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             if (!mbar_wait(rbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
             if (lane < n_own) {
                 const int e = c + lane * G;
-                for (int t = 0; t < NT; ++t) {
+                for (int t = EP ? a.ep_rank : 0; t < (EP ? a.ep_rank + 1 : NT); ++t) {  // (EP: its own token)
                     float lg = 0.f;
 #pragma unroll
                     for (int sl = 0; sl < RSPLIT; ++sl) lg += s_slice[(lane * RSPLIT + sl) * NT + t];
@@ -715,7 +737,62 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         int e0 = 0, e1 = 0;
         float w0 = 0.f, w1 = 0.f;
         bool ok = true;
-        if (NT == 1) {  // every CTA picks the token's experts itself
+        if constexpr (EP) {
+            // this rank's token only (every CTA picks its experts itself from
+            // the local logits); CTA 0 sends the picks to every rank, and
+            // every CTA reads the other tokens' picks from its rank's ep_pk
+            const int own = a.ep_rank;
+            int me = 0;
+            float mw = 0.f;
+            ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, c % kLogitCopies, own, c == 0, me, mw)
+                          : topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, own, c == 0, me, mw);
+            if (c == 0 && lane < K) {
+                const unsigned long long v0 = ((unsigned long long)ep_tag << 32) | (uint32_t)me;
+                const unsigned long long v1 = ((unsigned long long)ep_tag << 32) | __float_as_uint(mw);
+                for (int r = 0; r < a.ep_world; ++r)
+                    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};"
+                                 ::"l"(a.ep_pk_peer[r] + ((int64_t)own * 32 + lane) * 2), "l"(v0), "l"(v1) : "memory");
+            }
+            // pair p = t*K + k on lane p (and p - 32): this token's by shuffle, the others polled
+            const int np = NT * K;
+            const int t0 = lane / K, k0 = lane - t0 * K, t1 = (lane + 32) / K, k1 = lane + 32 - t1 * K;
+            const int oe0 = __shfl_sync(0xffffffffu, me, k0), oe1 = __shfl_sync(0xffffffffu, me, k1);
+            const float ow0 = __shfl_sync(0xffffffffu, mw, k0), ow1 = __shfl_sync(0xffffffffu, mw, k1);
+            const bool r0 = lane < np && t0 != own, r1 = lane + 32 < np && t1 != own;
+            if (lane < np && !r0) { e0 = oe0; w0 = ow0; }
+            if (lane + 32 < np && !r1) { e1 = oe1; w1 = ow1; }
+            for (uint32_t n = 0;; ++n) {
+                bool got = true;
+                if (r0) {
+                    unsigned long long v0, v1;
+                    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                                 : "=l"(v0), "=l"(v1) : "l"(a.ep_pk + ((int64_t)t0 * 32 + k0) * 2) : "memory");
+                    got &= (uint32_t)(v0 >> 32) == ep_tag && (uint32_t)(v1 >> 32) == ep_tag;
+                    e0 = (int)(uint32_t)v0;
+                    w0 = __uint_as_float((uint32_t)v1);
+                }
+                if (r1) {
+                    unsigned long long v0, v1;
+                    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];"
+                                 : "=l"(v0), "=l"(v1) : "l"(a.ep_pk + ((int64_t)t1 * 32 + k1) * 2) : "memory");
+                    got &= (uint32_t)(v0 >> 32) == ep_tag && (uint32_t)(v1 >> 32) == ep_tag;
+                    e1 = (int)(uint32_t)v0;
+                    w1 = __uint_as_float((uint32_t)v1);
+                }
+                if (__all_sync(0xffffffffu, got)) break;
+                if (n >= a.spin_limit) {
+                    ok = false;
+                    break;
+                }
+                __nanosleep(n < 2 ? 64u << n : 256u);
+            }
+            if (c == 0) {  // (ids outside [0, E) after a timeout are dropped by build_slots)
+                if (r0 && a.topk_ids) a.topk_ids[lane] = e0;
+                if (r0 && a.topk_w) a.topk_w[lane] = w0;
+                if (r1 && a.topk_ids) a.topk_ids[lane + 32] = e1;
+                if (r1 && a.topk_w) a.topk_w[lane + 32] = w1;
+            }
+        } else if (NT == 1) {  // every CTA picks the token's experts itself
             ok = E <= 160 ? topk_token<5>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0)
                           : topk_token<EJ>(a, bias, tag, lane, c % kLogitCopies, 0, c == 0, e0, w0);
         } else {
@@ -724,23 +801,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             // slice area, then pair p = t*K + k goes to lane p (p < 32) or p-32
             int* s_pe = reinterpret_cast<int*>(s_slice);
             float* s_pw = s_slice + kDecodeMaxRouted;
-            constexpr int TS = EP ? 2 : 1;  // tokens' logits per round of loads (expert-parallel: registers allow two)
-            for (int t = 0; t < NT; t += TS) {
+            for (int t = 0; t < NT; ++t) {
                 uint32_t w[EJ], w2[EJ];
-                ok &= poll_logits<EJ>(a, tag, lane, c % kLogitCopies, t, TS == 2 && t + 1 < NT ? t + 1 : -1, w, w2);
+                ok &= poll_logits<EJ>(a, tag, lane, c % kLogitCopies, t, -1, w, w2);
                 int me = 0;
                 float mw = 0.f;
                 select_topk<EJ>(a, bias, w, lane, t, c == 0, me, mw);
                 if (lane < K) {
                     s_pe[t * K + lane] = me;
                     s_pw[t * K + lane] = mw;
-                }
-                if (TS == 2 && t + 1 < NT) {
-                    select_topk<EJ>(a, bias, w2, lane, t + 1, c == 0, me, mw);
-                    if (lane < K) {
-                        s_pe[(t + 1) * K + lane] = me;
-                        s_pw[(t + 1) * K + lane] = mw;
-                    }
                 }
             }
             __syncwarp();
@@ -776,8 +845,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         // (published by the gate/up tiles of that unit), quantised as a lane
         // quantises its activations.  Fetched one stage ahead of its use.
         auto fetch_h = [&](const Job& jb) -> bool {
-            const unsigned long long* src =
-                a.hx + (int64_t)(jb.slot < 0 ? kDecodeMaxRouted : jb.slot) * I + jb.unit * UNIT + lane;
+            const unsigned long long* src = a.hx + (int64_t)hx_row(jb.slot) * I + jb.unit * UNIT + lane;
             unsigned long long w = 0ull;
             uint32_t k = 0;
             for (; k < a.spin_limit; ++k) {
@@ -800,9 +868,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             // buffer of down job d was last read by down job d-2, whose stage
             // (two down jobs back, so before position m) this warp has seen done
             bool fetched = true;
-            const Job jb = job_of<NU, NCH>(c + m * G, nsr);
+            const Job jb = job_of<UC, NCH>(c + m * G, nss, nsr);
             for (; fm <= m + 1 && fm < n && fetched; ++fm) {
-                const Job fj = job_of<NU, NCH>(c + fm * G, nsr);
+                const Job fj = job_of<UC, NCH>(c + fm * G, nss, nsr);
                 if (fj.gu) continue;
                 // (not ahead of this CTA's own tile of the same unit, whose h
                 // this warp publishes only below)
@@ -843,8 +911,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             if (lane == 0) mbar_arrive(empty0 + 8u * s);  // stage read: it may refill
             if (++s == S) { s = 0; ph ^= 1u; }
             if (jb.gu && lane < TRG) {  // h rows of the tile, tagged: the data is its own flag
-                unsigned long long* dst = a.hx + (int64_t)(jb.slot < 0 ? kDecodeMaxRouted : jb.slot) * I +
-                                          jb.unit * UNIT + jb.j * TRG + lane;
+                unsigned long long* dst = a.hx + (int64_t)hx_row(jb.slot) * I + jb.unit * UNIT + jb.j * TRG + lane;
                 st_relaxed64(dst, ((unsigned long long)tag << 32) | __float_as_uint(val));
             }
         }
@@ -884,58 +951,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                     acc = warp_sum(acc);
                     if (lane == 0) s_slice[task * NT + t] = acc;
                 }
-            } else {
-                // this rank's own token from x, the others' from the exchange
-                {
-                    float acc = 0.f;
+            } else {  // this rank's own token (row 0 of x): the others' are routed on their ranks
+                float acc = 0.f;
 #pragma unroll
-                    for (int i = 0; i < RV; ++i) {
-                        const float4 xv = x4_of(a, 0, sl * RSL + lane * 4 + i * 128);
-                        acc = fmaf(wv[i].x, xv.x, acc);
-                        acc = fmaf(wv[i].y, xv.y, acc);
-                        acc = fmaf(wv[i].z, xv.z, acc);
-                        acc = fmaf(wv[i].w, xv.w, acc);
-                    }
-                    acc = warp_sum(acc);
-                    if (lane == 0) s_slice[task * NT + a.ep_rank] = acc;
+                for (int i = 0; i < RV; ++i) {
+                    const float4 xv = x4_of(a, 0, sl * RSL + lane * 4 + i * 128);
+                    acc = fmaf(wv[i].x, xv.x, acc);
+                    acc = fmaf(wv[i].y, xv.y, acc);
+                    acc = fmaf(wv[i].z, xv.z, acc);
+                    acc = fmaf(wv[i].w, xv.w, acc);
                 }
-                for (int t = 0; t < NT; ++t) {
-                    if (t == a.ep_rank) continue;
-                    float acc = 0.f;
-                    if (a.x_bf16) {
-                        int w[RV];
-                        uint32_t u[2 * RV];
-#pragma unroll
-                        for (int i = 0; i < RV; ++i) w[i] = t * H + (sl * RSL + lane * 4 + i * 128) / 2;
-                        ep_fetch<RV>(a, w, ep_tag, u, xok);
-#pragma unroll
-                        for (int i = 0; i < RV; ++i) {
-                            acc = fmaf(wv[i].x, __uint_as_float(u[2 * i] << 16), acc);
-                            acc = fmaf(wv[i].y, __uint_as_float(u[2 * i] & 0xFFFF0000u), acc);
-                            acc = fmaf(wv[i].z, __uint_as_float(u[2 * i + 1] << 16), acc);
-                            acc = fmaf(wv[i].w, __uint_as_float(u[2 * i + 1] & 0xFFFF0000u), acc);
-                        }
-                    } else {
-                        int w[2 * RV];
-                        uint32_t u[4 * RV];
-#pragma unroll
-                        for (int i = 0; i < 2 * RV; ++i) w[i] = t * H + sl * RSL + lane * 4 + (i / 2) * 128 + 2 * (i % 2);
-                        ep_fetch<2 * RV>(a, w, ep_tag, u, xok);
-#pragma unroll
-                        for (int i = 0; i < RV; ++i) {
-                            acc = fmaf(wv[i].x, __uint_as_float(u[4 * i]), acc);
-                            acc = fmaf(wv[i].y, __uint_as_float(u[4 * i + 1]), acc);
-                            acc = fmaf(wv[i].z, __uint_as_float(u[4 * i + 2]), acc);
-                            acc = fmaf(wv[i].w, __uint_as_float(u[4 * i + 3]), acc);
-                        }
-                    }
-                    acc = warp_sum(acc);
-                    if (lane == 0) s_slice[task * NT + t] = acc;
-                }
+                acc = warp_sum(acc);
+                if (lane == 0) s_slice[task * NT + a.ep_rank] = acc;
             }
             if (lane == 0) mbar_arrive(rbar);
         }
-        if (ep && !__all_sync(0xffffffffu, xok) && lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
 
         if (!mbar_wait(tbar, 0, a.spin_limit)) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         const auto mg = lane_map<HH, NWC, PG>(warp, lane, stage0);
@@ -943,22 +973,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         uint32_t xq[16], hq[16];
         int cur = -1;  // the token whose activations xq holds
         float sx4 = 0.f, hs = 0.f;
-        int s = 0, n = jobs_of(c, G, nsh), nsr = 0, d = 0;
+        // Expert-parallel, only own_tok's shared tiles are decoded before the
+        // routing: the other tokens' activations come over NVLink, and lanes
+        // waiting for them slow this SM's router and logit stores, which every
+        // CTA's top-k waits for (their weights are still fetched early).
+        const int nsh_c = EP ? UC * TPU : nsh;
+        int s = 0, n = jobs_of(c, G, nsh_c), nsr = 0, d = 0;
         uint32_t ph = 0;
         bool have = false;
         auto give_up = [&]() {
             if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         };
         for (int m = 0;; ++m) {
-            if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) come after the routing
+            if (!have && c + m * G >= nsh_c) {  // routed jobs (and every down chunk) come after the routing
                 if (!__all_sync(0xffffffffu, mbar_wait(topk_bar, 0, a.spin_limit))) { give_up(); break; }
                 nsr = routed_slots();
                 n = jobs_of(c, G, total_jobs(nsr));
                 have = true;
             }
             if (m >= n) break;
-            const Job jb = job_of<NU, NCH>(c + m * G, nsr);
-            const int tok = jb.slot < 0 ? a.own_tok : s_st[jb.slot];
+            const Job jb = job_of<UC, NCH>(c + m * G, nss, nsr);
+            const int tok = tok_of(jb.slot);
             if (jb.gu) {
                 if (tok != cur) {  // that token's activations
                     cur = tok;
@@ -1021,10 +1056,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     // The last CTA out advances the launch generation (the tag of the next
     // launch's exchanged words).  Expert-parallel, the last CTA first adds
     // every token's partial output into that token's owner's accumulator of
-    // this step's parity over NVLink, then (one system-scope fence) tells
-    // every other rank that this rank's sums are in, waits for every other
-    // rank's signal to this one, copies this rank's accumulator to ep_out and
-    // zeroes it: no rank adds into it again before this rank's next signal.
+    // this step's parity over NVLink (one 16-byte add per 4 values: far less
+    // traffic than sending every down job's sums), then (one system-scope
+    // fence) tells every other rank that this rank's sums are in, waits for
+    // every other rank's signal to this one, copies this rank's accumulator to
+    // ep_out and zeroes it: no rank adds into it again before this rank's next
+    // signal.
     named_bar_sync(1, (NWC + 1) * 32);
     if constexpr (!EP) {
         if (tid == 0) {
@@ -1050,7 +1087,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             for (int i = tid; i < NT * (H / 4); i += (NWC + 1) * 32) {  // y[t] into owner t's accumulator
                 const int t = i / (H / 4), q = i % (H / 4);
                 const float4 v = __ldcg(reinterpret_cast<const float4*>(a.y + (int64_t)t * H) + q);
-                red_add_v4(a.ep_y[t] + par + 4 * q, v.x, v.y, v.z, v.w);
+                red_add_sys_v4(a.ep_y[t] + par + 4 * q, v.x, v.y, v.z, v.w);
             }
             named_bar_sync(1, (NWC + 1) * 32);
             if (tid == 0) {
@@ -1087,6 +1124,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
 
 }  // namespace
 
+bool decode_layer_slice_supported(int I, int u_cnt) {
+    return I == 1536 && (u_cnt == 48 || u_cnt == 24 || u_cnt == 12 || u_cnt == 6);
+}
+
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared) {
     if (E > kMaxEFused || E < K) return false;
     // the instantiated work mapping: gate/up 20 warps over 4 rows of H = 5120
@@ -1104,27 +1145,48 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
         !a.down_col || (reinterpret_cast<uintptr_t>(a.y) & 15))
         return cudaErrorInvalidValue;
     if (a.n_tok == 1 && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // one token: every expert
+    if (a.shared_all && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // a slice of every expert
     if (a.ep_world > 1) {  // the peer-memory exchange: one token per rank, every rank's block mapped
         if (a.ep_world > kDecodeMaxTokens || a.n_tok != a.ep_world || a.ep_rank < 0 || a.ep_rank >= a.ep_world ||
-            a.own_tok != a.ep_rank || !a.ep_x || !a.ep_sync || !a.ep_out || (reinterpret_cast<uintptr_t>(a.ep_out) & 15))
+            a.own_tok != a.ep_rank || !a.ep_x || !a.ep_sync || !a.ep_out || !a.ep_pk || a.K > 32 ||
+            ((reinterpret_cast<uintptr_t>(a.ep_out) | reinterpret_cast<uintptr_t>(a.ep_x) |
+              reinterpret_cast<uintptr_t>(a.ep_pk)) & 15))
             return cudaErrorInvalidValue;
+        // (16-byte pair stores and loads of tagged words, 16-byte adds)
         for (int r = 0; r < a.ep_world; ++r)
-            if (!a.ep_x_peer[r] || !a.ep_y[r] || !a.ep_done[r] || (reinterpret_cast<uintptr_t>(a.ep_y[r]) & 15) ||
-                (reinterpret_cast<uintptr_t>(a.ep_x_peer[r]) & 7) || (reinterpret_cast<uintptr_t>(a.ep_done[r]) & 7))
+            if (!a.ep_x_peer[r] || !a.ep_y[r] || !a.ep_done[r] || !a.ep_pk_peer[r] ||
+                ((reinterpret_cast<uintptr_t>(a.ep_y[r]) | reinterpret_cast<uintptr_t>(a.ep_x_peer[r]) |
+                  reinterpret_cast<uintptr_t>(a.ep_pk_peer[r])) & 15) ||
+                (reinterpret_cast<uintptr_t>(a.ep_done[r]) & 7))
                 return cudaErrorInvalidValue;
     }
     const Smem L = decode_smem(a.H, a.I, a.stages, a.n_tok);
     if (L.total > 227u * 1024u) return cudaErrorInvalidValue;
     const bool ep = a.ep_world > 1;
-    auto kern = ep ? decode_layer_kernel<5120, 1536, 4, 1, true> : decode_layer_kernel<5120, 1536, 4, 1, false>;
-    static std::atomic<unsigned long long> configured[2] = {{0}, {0}};  // per device, per instantiation
-    if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured[ep])) return e0;
+    const int uc = a.u_cnt ? a.u_cnt : a.I / UNIT;
+    if (a.u_lo < 0 || a.u_lo + uc > a.I / UNIT || (a.u_lo % uc)) return cudaErrorInvalidValue;
+    // instantiations: (exchange, units per slot)
+    using Kern = void (*)(const DecodeLayerArgs);
+    Kern kern = nullptr;
+    int ki = -1;
+    constexpr int kH = 5120, kI = 1536;
+    if (!ep && uc == 48) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 48>; ki = 0; }
+    else if (!ep && uc == 24) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 24>; ki = 1; }
+    else if (!ep && uc == 12) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 12>; ki = 2; }
+    else if (!ep && uc == 6) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 6>; ki = 3; }
+    else if (ep && uc == 48) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 48>; ki = 4; }
+    else if (ep && uc == 24) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 24>; ki = 5; }
+    else if (ep && uc == 12) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 12>; ki = 6; }
+    else if (ep && uc == 6) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 6>; ki = 7; }
+    if (!kern) return cudaErrorInvalidValue;
+    static std::atomic<unsigned long long> configured[8] = {};  // per device, per instantiation
+    if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured[ki])) return e0;
     // Co-residency: every CTA waits on data the others publish, so the grid
     // must fit the GPU at one CTA per SM.  Checked against the kernel's real
     // resource use (registers, shared memory) once per device; a grid larger
     // than the SMs that can hold a CTA is refused rather than left to time out.
-    static std::atomic<unsigned long long> fits_all[2] = {{0}, {0}};
-    std::atomic<unsigned long long>& fits = fits_all[ep];
+    static std::atomic<unsigned long long> fits_all[8] = {};
+    std::atomic<unsigned long long>& fits = fits_all[ki];
     int dev = 0;
     if (cudaError_t e1 = cudaGetDevice(&dev)) return e1;
     const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;

@@ -193,10 +193,13 @@ struct DecodeLayerArgs {
     // tokens with nothing here); the ranks' parts sum to the layer output.
     int n_tok;                 // 1 .. kDecodeMaxTokens
     int e_lo, e_cnt;           // routed experts held (gate/up/down index e - e_lo; the shared expert at e_cnt)
-    int own_tok;               // token whose shared expert runs in this launch
+    int own_tok;               // token whose shared expert runs in this launch (shared_all = 0)
+    int shared_all;            // 1: every token's shared expert runs in this launch
+    int u_lo, u_cnt;           // units of 32 rows of each expert that the layer holds and this launch runs
+                               // (0, I/32: whole experts; a slice when each rank holds a slice of every expert)
     unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
     unsigned long long* hx;      // [decode_layer_h_words(I)] h of every (slot, unit), tagged: rows of routed slot s
-                                 // at s * I, the shared expert's at kDecodeMaxRouted * I
+                                 // at s * I, shared slot i's at (kDecodeMaxRouted + i) * I
     unsigned* sync;            // [kDecodeSyncWords] launch generation and finished-CTA count
     const uint8_t* tables;
     uint32_t* status;
@@ -207,16 +210,20 @@ struct DecodeLayerArgs {
     // Expert-parallel decode over peer memory (ep_world > 1; no collective
     // library): n_tok = ep_world tokens, token t owned by rank t.  Each rank
     // publishes its own token (x, [1][H]) into every rank's ep_x as words
-    // tagged with the EP step generation g + 1, sums its share of every token
-    // into y ([n_tok][H], local, as for several tokens), and at the end adds
-    // y[t] into owner t's accumulator ep_y[t] + (g & 1) * H over NVLink,
-    // signals every owner (ep_done[t]), waits for the other ranks' signals,
-    // copies its own accumulator to ep_out ([1][H]) and zeroes it for step
-    // g + 2 (the next signal orders that before any rank's adds there).
+    // tagged with the EP step generation g + 1, routes its own token and
+    // publishes the picks into every rank's ep_pk the same way, reads the
+    // other ranks' picks from its own ep_pk, sums its share of every token
+    // into y ([n_tok][H], local), and at the end adds y[t] into owner t's
+    // accumulator ep_y[t] + (g & 1) * H over NVLink, signals every owner
+    // (ep_done[t]), waits for the other ranks' signals, copies its own
+    // accumulator to ep_out ([1][H]) and zeroes it for step g + 2 (the next
+    // signal orders that before any rank's adds there).
     int ep_world;
     int ep_rank;
     unsigned long long* ep_x;                         // this rank's [kDecodeMaxTokens][H] tagged words
     unsigned long long* ep_x_peer[kDecodeMaxTokens];  // every rank's ep_x (this rank's included)
+    unsigned long long* ep_pk;                        // this rank's [kDecodeMaxTokens][32][2] tagged picks (id, weight)
+    unsigned long long* ep_pk_peer[kDecodeMaxTokens];  // every rank's ep_pk
     float* ep_y[kDecodeMaxTokens];                    // every rank's accumulators [2][H] (by step parity)
     unsigned long long* ep_done[kDecodeMaxTokens];    // every rank's done counter
     unsigned* ep_sync;                                // this rank's EP step generation
@@ -259,8 +266,11 @@ cudaError_t launch_ep_pack(const void* x, int x_bf16, int H, int n, int K, const
 // Words of DecodeLayerArgs::logits, one word per 256-byte line: per token, 8
 // replicas of E tagged logits (every CTA reads every token's).
 inline size_t decode_layer_logit_words(int E) { return (size_t)kDecodeMaxTokens * 8 * E * 32; }
-// Words of DecodeLayerArgs::hx: one tagged h value per row of every slot's expert.
-inline size_t decode_layer_h_words(int I) { return (size_t)(kDecodeMaxRouted + 1) * I; }
+// Words of DecodeLayerArgs::hx: one tagged h value per row of every slot's expert
+// (routed slots, then up to kDecodeMaxTokens shared slots).
+inline size_t decode_layer_h_words(int I) { return (size_t)(kDecodeMaxRouted + kDecodeMaxTokens) * I; }
+// Whether the persistent decode kernel runs a slice of u_cnt of each expert's inter / 32 units.
+bool decode_layer_slice_supported(int I, int u_cnt);
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);
 // Dynamic shared memory of a launch: `stages` pipeline stages, n_tok tokens.
 size_t decode_layer_smem(int H, int I, int stages, int n_tok);

@@ -253,6 +253,12 @@ class PeerDecode:
     token per rank per step, the exchanges inside the persistent kernel over
     NVLink peer memory (gpeed_ep_setup / gpeed_ep_connect / gpeed_moe_decode_ep).
 
+    `layers`: this rank's share of each layer, either its expert range
+    (MoeLayer.synth_range / from_gguf with an expert range) or a whole layer
+    sliced by units (MoeLayer.slice_units(*MoeLayer.unit_slice(cfg, rank,
+    world))), with which every rank runs its slice of every pick: the same
+    work on every rank whatever the routing.
+
     Setup (once per process group, collective): every rank allocates its
     exchange block, the CUDA IPC handles are all-gathered on the host through
     torch.distributed, and every rank maps the others' blocks.  A step is one

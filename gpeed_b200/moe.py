@@ -247,13 +247,31 @@ class MoeLayer:
              expert_count, _ptr(router), _ptr(corr_c), 0, ctypes.c_uint64(seed), ctypes.c_uint64(stream0))
         return self
 
+    def slice_units(self, unit_begin: int, unit_count: int) -> "MoeLayer":
+        """Keep units [unit_begin, unit_begin + unit_count) of every expert, a unit
+        being 32 intermediate rows (gpeed_moe_slice_units): one rank's share
+        of the tensor-parallel split of every expert.  The layer then serves
+        decode_partial and the expert-parallel decode only."""
+        call("gpeed_moe_slice_units", self.ctx.handle, self.layer_id, unit_begin, unit_count)
+        return self
+
+    @staticmethod
+    def unit_slice(cfg: MoeConfig, rank: int, world: int) -> tuple[int, int]:
+        """(unit_begin, unit_count) of rank `rank` of `world` equal slices."""
+        nu = cfg.inter // 32
+        if nu % world:
+            raise GpeedError(_capi.ERR_INVALID, f"{nu} units do not split over {world} ranks")
+        return rank * (nu // world), nu // world
+
     def decode_partial(self, x_all: torch.Tensor, own_tok: int, y_part: torch.Tensor | None = None,
                        forced_topk: torch.Tensor | None = None, topk_ids: torch.Tensor | None = None,
                        topk_w: torch.Tensor | None = None, stream=None) -> torch.Tensor:
         """One rank's share of an expert-parallel decode step (gpeed_moe_decode_partial):
         x_all [n, H] every rank's token -> y_part [n, H] fp32, the part of each
         token's output that this layer's experts (plus own_tok's shared expert)
-        contribute.  The ranks' parts sum to MoeLayer.forward of the whole layer."""
+        contribute.  The ranks' parts sum to MoeLayer.forward of the whole layer.
+        On a sliced layer (slice_units) the part is this slice of every pick
+        and of every token's shared expert, and own_tok is not used."""
         n = x_all.shape[0]
         if y_part is None:
             y_part = torch.empty(n, self.cfg.hidden, dtype=torch.float32, device=x_all.device)

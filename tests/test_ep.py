@@ -89,6 +89,7 @@ def _decode_worker(rank, world, port, out_dir, steps, leave_after):
         ep = ExpertParallelDecode(cfg, OracleExecutor(layer, cfg, lo, cnt), guard=guard)
         X = np.random.default_rng(21).standard_normal((steps, world, H)).astype(np.float32)
         ys = []
+        dist.barrier()  # both ranks set up: the guard's short wait times steps, not process start-up
         for s in range(steps):
             if leave_after is not None and rank == world - 1 and s == leave_after:
                 result = "left"

@@ -225,6 +225,60 @@ def test_decode_partial_emulated_ranks(port, world):
         ctx.close()
 
 
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_decode_partial_sliced_emulated_ranks(world):
+    """Each emulated rank holds units [r*NU/world, (r+1)*NU/world) of every
+    expert (gpeed_moe_slice_units): its gpeed_moe_decode_partial runs that
+    slice of every pick and of every token's shared expert.  Routing is
+    bit-identical to the batch-1 forward; the ranks' parts add up to it (SwiGLU
+    is row-wise, so only the order of the down sums changes), for `world`
+    tokens and for one token; a sliced layer refuses the whole-layer paths."""
+    from gpeed_b200 import GpeedError
+    ctx = Context(0)
+    try:
+        cfg = MoeConfig()
+        K = cfg.top_k
+        router = _router(cfg)
+        full = MoeLayer(ctx, cfg, layer_id=900 + 20 * world).synth(router, None, SEED, S0)
+        parts = []
+        for r in range(world):
+            lo, cnt = MoeLayer.unit_slice(cfg, r, world)
+            layer = MoeLayer(ctx, cfg, layer_id=901 + 20 * world + r).synth(router, None, SEED, S0)
+            parts.append(layer.slice_units(lo, cnt))
+        X = torch.from_numpy(np.random.default_rng(10 + world).standard_normal((world, cfg.hidden)).astype(
+            np.float32)).to(torch.bfloat16).cuda()
+        y_ref = torch.empty(world, cfg.hidden, device="cuda")
+        ids_ref = torch.empty(world, K, dtype=torch.int32, device="cuda")
+        w_ref = torch.empty(world, K, dtype=torch.float32, device="cuda")
+        for t in range(world):
+            full.forward(X[t:t + 1], y_ref[t:t + 1], topk_ids=ids_ref[t:t + 1], topk_w=w_ref[t:t + 1])
+        y_parts = []
+        for r in range(world):
+            ids = torch.full((world, K), -1, dtype=torch.int32, device="cuda")
+            w = torch.zeros(world, K, device="cuda")
+            y_parts.append(parts[r].decode_partial(X, r, topk_ids=ids, topk_w=w))
+            ctx.check()
+            np.testing.assert_array_equal(ids.cpu().numpy(), ids_ref.cpu().numpy())
+            np.testing.assert_array_equal(w.cpu().numpy(), w_ref.cpu().numpy())
+            assert y_parts[-1].abs().sum(1).min().item() > 0  # every token has a part on every rank
+        y_ep = torch.stack(y_parts).sum(0).cpu().numpy()
+        for t in range(world):
+            assert rel_l2(y_ep[t], y_ref.cpu().numpy()[t]) < 1e-5, (t, rel_l2(y_ep[t], y_ref.cpu().numpy()[t]))
+        one = sum(parts[r].decode_partial(X[1:2], 0) for r in range(world))
+        ctx.check()
+        assert rel_l2(one.cpu().numpy(), y_ref[1:2].cpu().numpy()) < 1e-5
+        with pytest.raises(GpeedError):
+            parts[0].forward(X[:1])
+        with pytest.raises(GpeedError):
+            parts[0].slice_units(0, 6)  # already sliced
+        with pytest.raises(GpeedError):
+            full.slice_units(3, 6)  # not on a multiple of the slice
+        with pytest.raises(GpeedError):
+            full.slice_units(0, 16)  # no kernel for a third of the units
+    finally:
+        ctx.close()
+
+
 def test_decode_partial_crowded_rank_and_limits():
     """Every pick of 8 tokens forced onto one rank's experts: that rank runs the
     most slots a launch takes (64 routed + its shared expert), the others only
@@ -307,7 +361,7 @@ def test_ep_decode_nccl_two_gpus(tmp_path):
 
 # ---- expert-parallel decode over peer memory (no collective library on the data path) ----
 
-def _peer_decode_worker(rank, world, port, out_dir):
+def _peer_decode_worker(rank, world, port, out_dir, sliced=False):
     import torch.distributed as dist
     from gpeed_b200 import GpeedError, _capi
     from gpeed_b200.ep import PeerDecode
@@ -318,8 +372,12 @@ def _peer_decode_worker(rank, world, port, out_dir):
     try:
         ctx = Context(rank)
         cfg = MoeConfig()
-        lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
-        layer = MoeLayer(ctx, cfg, layer_id=0).synth_range(_router(cfg), None, SEED, S0, lo, cnt)
+        if sliced:
+            layer = MoeLayer(ctx, cfg, layer_id=0).synth(_router(cfg), None, SEED, S0)
+            layer.slice_units(*MoeLayer.unit_slice(cfg, rank, world))
+        else:
+            lo, cnt = ExpertParallelLayer.expert_range(cfg, rank, world)
+            layer = MoeLayer(ctx, cfg, layer_id=0).synth_range(_router(cfg), None, SEED, S0, lo, cnt)
         pd = PeerDecode(ctx, cfg, layer)
         X = _tokens(cfg, 3 * world).reshape(3, world, cfg.hidden)
         ys, ids = [], []
@@ -352,9 +410,11 @@ def _peer_decode_worker(rank, world, port, out_dir):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_decode_peer_memory_two_gpus(tmp_path):
-    """PeerDecode on two GPUs: three steps, each rank's output equals the
-    one-GPU layer on its token (the two ranks' sums land in another order: to
+@pytest.mark.parametrize("sliced", [False, True], ids=["expert_ranges", "unit_slices"])
+def test_ep_decode_peer_memory_two_gpus(tmp_path, sliced):
+    """PeerDecode on two GPUs, each rank holding half the experts or half of
+    every expert's units: three steps, each rank's output equals the one-GPU
+    layer on its token (the two ranks' sums land in another order: to
     rounding), the picks of both tokens equal the one-GPU routing; then a step
     that one rank skips times out on the other, reported by gpeed_ctx_check."""
     cfg = MoeConfig()
@@ -374,7 +434,7 @@ def test_ep_decode_peer_memory_two_gpus(tmp_path):
         ctx.close()
     mpc = mp.get_context("spawn")
     port = _free_port()
-    procs = [mpc.Process(target=_peer_decode_worker, args=(r, 2, port, str(tmp_path))) for r in range(2)]
+    procs = [mpc.Process(target=_peer_decode_worker, args=(r, 2, port, str(tmp_path), sliced)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:
