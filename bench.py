@@ -18,15 +18,16 @@ the GPUs with NCCL all-to-all dispatch and combine), --workload stack40 (config
 5 on one GPU: 40 layers, decode batches 1 to 256).
 
 N > 1 (launched by torchrun): expert parallelism.  Every GPU holds 1/N of
-every expert's intermediate rows (units of 32 rows, the tensor-parallel split
-of each expert; --ep-split experts instead gives each GPU 160/N whole routed
-experts plus the shared expert); each rank brings one token per step (weak
-scaling).  A step is one persistent kernel per rank (gpeed_moe_decode_ep): its
-token goes to every rank over NVLink peer memory, all N tokens are routed,
-the rank runs its share of every pick (its slice of each expert; or, with
-expert ranges, the picks in its range and its own token's shared expert) and
-adds the sums straight into the owning rank's output; no collective library
-on the data path.  With
+every routed expert's intermediate rows (units of 32 rows, the
+tensor-parallel split of each expert; --ep-split experts instead gives each
+GPU 160/N whole routed experts) plus the whole shared expert; each rank
+brings one token per step (weak scaling).  A step is one persistent kernel
+per rank (gpeed_moe_decode_ep): its token goes to every rank over NVLink peer
+memory, each rank routes its own token and sends its picks to every rank, the
+rank runs its share of every pick (its slice of each expert; or, with expert
+ranges, the picks in its range) and its own token's shared expert and adds
+the sums into the owning rank's output; no collective library on the data
+path.  With
 --ep-nccl the exchanges are an NCCL all-gather and reduce-scatter around
 gpeed_moe_decode_partial instead.  Steps are captured in CUDA graphs.  value =
 tokens over all ranks / the slowest rank's time.  The reference arm runs on
@@ -384,10 +385,10 @@ def run_gpu(args, rank, local_rank, world):
 
 def run_gpu_ep(args, rank, local_rank, world):
     """BASELINE config 2's layer, expert-parallel over `world` GPUs (the N > 1
-    default).  Rank r holds units [r*NU/N, (r+1)*NU/N) of every expert of
-    every layer copy (--ep-split units: 1/N of each expert's 1536 intermediate
-    rows), or routed experts [r*E/N, (r+1)*E/N) plus the shared expert
-    (--ep-split experts), and brings its own token each step.  A step (one
+    default).  Rank r holds units [r*NU/N, (r+1)*NU/N) of every routed expert
+    of every layer copy (--ep-split units: 1/N of each expert's 1536
+    intermediate rows), or routed experts [r*E/N, (r+1)*E/N) (--ep-split
+    experts), plus the shared expert, and brings its own token each step.  A step (one
     token per rank through one layer) is one persistent kernel per rank,
     gpeed_moe_decode_ep: the tokens go to every rank over NVLink peer memory,
     all N are routed, this rank's share of each pick runs and adds its sums
@@ -517,9 +518,9 @@ def run_gpu_ep(args, rank, local_rank, world):
         slots.append(int(((g >= lo) & (g < lo + cnt)).sum()))
     torch.cuda.synchronize()
     mean_slots = sum(slots) / L
-    # expert bytes this rank streams: its slice of every pick and every token's
-    # shared expert, or its range's picks and its own token's shared expert
-    expert_units = (mean_slots + world) / world if sliced else mean_slots + 1
+    # expert bytes this rank streams: its slice of every pick, or its range's
+    # picks, and its own token's shared expert
+    expert_units = (mean_slots / world if sliced else mean_slots) + 1
     kern_bytes = expert_units * EXPERT_BYTES + ROUTER_BYTES + world * H * (2 + 4)
     achieved = kern_bytes / (ph[1] * 1e-3) / 1e9
 
@@ -562,8 +563,9 @@ def run_gpu_ep(args, rank, local_rank, world):
             "config": {"workload": "decode1: MoE layer decode, batch 1 (BASELINE config 2)", "hidden": H,
                        "n_experts": E, "top_k": K_TOP, "inter": I, "n_shared": 1, "quant": "IQ3_XXS",
                        "layer_copies": L, "l2": f"inputs larger than L2: steps rotate over {L} layer copies",
-                       "parallelism": (f"ep{world}: " + (f"1/{world} of every expert's units per GPU ({u_cnt} of "
-                                                         f"{I // 32} units of 32 rows)" if sliced else
+                       "parallelism": (f"ep{world}: " + (f"1/{world} of every routed expert's units per GPU ({u_cnt} "
+                                                         f"of {I // 32} units of 32 rows) + the shared expert"
+                                                         if sliced else
                                                          f"{cnt} routed experts per GPU + the shared expert") +
                                        "; one token per GPU per step; " +
                                        ("one persistent kernel per GPU exchanging tokens and partial outputs over "

@@ -61,10 +61,11 @@ struct Layer {
     // then the shared expert at local index e_cnt (all of them unless the
     // layer was loaded for expert parallelism)
     int e_lo = 0, e_cnt = 0;
-    // units of 32 intermediate rows of every expert held here: [u_lo, u_lo +
-    // u_cnt) of inter / 32 (gpeed_moe_slice_units; all of them otherwise).  A
-    // sliced layer keeps only the gate/up row groups and down column slabs of
-    // its units, for the persistent decode kernel.
+    // units of 32 intermediate rows of every routed expert held here: [u_lo,
+    // u_lo + u_cnt) of inter / 32 (gpeed_moe_slice_units; all of them
+    // otherwise).  A sliced layer keeps only the gate/up row groups and down
+    // column slabs of those units, for the persistent decode kernel, and the
+    // shared expert whole after them.
     int u_lo = 0, u_cnt = 0;
     bool sliced() const { return u_cnt != shape.inter / 32; }
     // the router weights split into bf16 hi/lo/lo2 rows for the tensor-core router (or nullptr)
@@ -522,7 +523,6 @@ int fused_args(gpeed_ctx* c, const Layer& L, const void* x, int x_dtype, int n_t
     da.own_tok = own_tok;
     da.u_lo = L.u_lo;
     da.u_cnt = L.u_cnt;
-    da.shared_all = L.sliced() ? 1 : 0;  // a slice of every token's shared expert runs on every rank
     da.logits = c->logits.p;
     da.hx = c->hx.p;
     da.sync = c->sync;
@@ -981,28 +981,34 @@ int gpeed_moe_slice_units(gpeed_ctx* c, int layer, int unit_begin, int unit_coun
                     unit_begin, unit_begin + unit_count, NU);
     int rc;
     if ((rc = set_device(c))) return rc;
-    const int NE = L.e_cnt + s.n_shared;
+    const int NR = L.e_cnt;
     // gate/up: 4 row groups of 8 rows per unit; down: the units' column slabs,
-    // then the 256-input d blocks they fall in (repacked_bytes, launch_repack_cols)
+    // then the 256-input d blocks they fall in (repacked_bytes,
+    // launch_repack_cols).  The shared expert follows whole, in the same
+    // layouts (it starts at NR times the sliced strides).
     const int64_t tile = gp::repacked_bytes(8, H), unit_col = (int64_t)H * 12;
     const int blk_lo = unit_begin / 8, nblk = (unit_begin + unit_count - 1) / 8 - blk_lo + 1;
     const int64_t gu_w = (int64_t)unit_count * 4 * tile;
     const int64_t dc_w = (int64_t)unit_count * unit_col, dd_w = (int64_t)nblk * H * 2;
+    const int64_t sh_gu = s.n_shared ? L.gu_stride : 0, sh_dc = s.n_shared ? L.dc_stride : 0;
     uint8_t *g = nullptr, *u = nullptr, *dc = nullptr;
     auto undo = [&]() { cudaFree(g); cudaFree(u); cudaFree(dc); };
-    if (cudaMalloc(&g, gu_w * NE + gp::repacked_bytes(32, H)) != cudaSuccess ||
-        cudaMalloc(&u, gu_w * NE + gp::repacked_bytes(32, H)) != cudaSuccess ||
-        cudaMalloc(&dc, (dc_w + dd_w) * NE) != cudaSuccess) {
+    if (cudaMalloc(&g, gu_w * NR + sh_gu + gp::repacked_bytes(32, H)) != cudaSuccess ||
+        cudaMalloc(&u, gu_w * NR + sh_gu + gp::repacked_bytes(32, H)) != cudaSuccess ||
+        cudaMalloc(&dc, (dc_w + dd_w) * NR + sh_dc) != cudaSuccess) {
         undo();
         cudaGetLastError();
         return fail(GPEED_ERR_CUDA, "out of device memory slicing layer %d", layer);
     }
     const cudaMemcpyKind d2d = cudaMemcpyDeviceToDevice;
-    cudaError_t e = cudaMemcpy2D(g, gu_w, L.gate + unit_begin * 4 * tile, L.gu_stride, gu_w, NE, d2d);
-    if (!e) e = cudaMemcpy2D(u, gu_w, L.up + unit_begin * 4 * tile, L.gu_stride, gu_w, NE, d2d);
-    if (!e) e = cudaMemcpy2D(dc, dc_w + dd_w, L.down_col + unit_begin * unit_col, L.dc_stride, dc_w, NE, d2d);
+    cudaError_t e = cudaMemcpy2D(g, gu_w, L.gate + unit_begin * 4 * tile, L.gu_stride, gu_w, NR, d2d);
+    if (!e) e = cudaMemcpy2D(u, gu_w, L.up + unit_begin * 4 * tile, L.gu_stride, gu_w, NR, d2d);
+    if (!e) e = cudaMemcpy2D(dc, dc_w + dd_w, L.down_col + unit_begin * unit_col, L.dc_stride, dc_w, NR, d2d);
     if (!e) e = cudaMemcpy2D(dc + dc_w, dc_w + dd_w, L.down_col + NU * unit_col + (int64_t)blk_lo * H * 2, L.dc_stride,
-                             dd_w, NE, d2d);
+                             dd_w, NR, d2d);
+    if (!e && s.n_shared) e = cudaMemcpy(g + gu_w * NR, L.gate + L.gu_stride * NR, sh_gu, d2d);
+    if (!e && s.n_shared) e = cudaMemcpy(u + gu_w * NR, L.up + L.gu_stride * NR, sh_gu, d2d);
+    if (!e && s.n_shared) e = cudaMemcpy(dc + (dc_w + dd_w) * NR, L.down_col + L.dc_stride * NR, sh_dc, d2d);
     if (e) {
         undo();
         return fail(GPEED_ERR_CUDA, "slicing layer %d: %s", layer, cudaGetErrorString(e));

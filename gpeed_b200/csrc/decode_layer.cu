@@ -500,35 +500,38 @@ __host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok) {
 GP_DEVINL int jobs_of(int c, int G, int total) { return c < total ? (total - 1 - c) / G + 1 : 0; }
 
 // One pipeline stage of work.  Job k of a launch, in the order: the shared
-// slots' gate/up tiles (no routing needed), the routed slots' gate/up tiles,
-// the shared slots' down chunks, the routed slots' down chunks; each slot
-// covers the launch's UC units (all NU of an expert, or the rank's slice when
-// every rank holds a slice of every expert).  A gate/up tile (slot, unit,
+// slot's gate/up tiles (no routing needed), the routed slots' gate/up tiles,
+// the shared slot's down chunks, the routed slots' down chunks.  The shared
+// slot (own_tok's shared expert) covers all NU units of the expert; a routed
+// slot covers the launch's UC units (all NU, or the rank's slice when every
+// rank holds a slice of every routed expert).  A gate/up tile (slot, unit,
 // j < TPU) gives h rows unit*32 + j*8 .. +7; a down chunk (slot, unit,
 // j < NCH) adds the unit's 32 input columns into output rows j*RC .. +RC-1
 // and needs the unit's 32 h rows, which tiles earlier in the order (on any
 // CTA) produced.
 struct Job {
     bool gu;
-    int slot, unit, j;  // slot < 0: shared slot -1 - slot; unit: index within the launch's unit range
+    int slot, unit, j;  // slot -1: the shared slot; unit: index within the slot's unit range
 };
-// UC units per slot (all NU of an expert, or a slice of them); nss shared
-// slots (one, or one per token) come before the nsr routed ones.  (Every
-// division is by a compile-time constant: the producer decodes a job on its
-// critical path, sharing issue slots with the compute warps.)
-template <int UC, int NCH>
-GP_DEVINL Job job_of(int k, int nss, int nsr) {
-    constexpr int GS = UC * TPU, DS = UC * NCH;  // jobs per slot, each kind
-    const int cyc = GS * (nss + nsr);
+// (Every division is by a compile-time constant: the producer decodes a job
+// on its critical path, sharing issue slots with the compute warps.)
+template <int UC, int NU, int NCH>
+GP_DEVINL Job job_of(int k, int nsr) {
+    constexpr int GSS = NU * TPU, GS = UC * TPU, DSS = NU * NCH, DS = UC * NCH;  // jobs per slot, each kind
+    const int cyc = GSS + GS * nsr;
     if (k < cyc) {
+        if (k < GSS) return {true, -1, k / TPU, k % TPU};
+        k -= GSS;
         const int si = k / GS;
         k -= si * GS;
-        return {true, si < nss ? -1 - si : si - nss, k / TPU, k % TPU};
+        return {true, si, k / TPU, k % TPU};
     }
     k -= cyc;
+    if (k < DSS) return {false, -1, k / NCH, k % NCH};
+    k -= DSS;
     const int si = k / DS;
     k -= si * DS;
-    return {false, si < nss ? -1 - si : si - nss, k / NCH, k % NCH};
+    return {false, si, k / NCH, k % NCH};
 }
 
 // Quantises the unit of h held one value per lane exactly as a lane quantises
@@ -546,9 +549,9 @@ GP_DEVINL void quantise_unit(float v, uint32_t* words, int lane) {
 }
 
 // EP: the expert-parallel exchange over peer memory (a separate instantiation,
-// so the one-GPU kernel carries none of its code).  UC: units of each slot's
-// expert that this launch runs (NU, or NU / N when each of N ranks holds a
-// slice of every expert).
+// so the one-GPU kernel carries none of its code).  UC: units of each routed
+// slot's expert that this launch runs (NU, or NU / N when each of N ranks
+// holds a slice of every routed expert).
 template <int HH, int II, int PG, int RPWG, bool EP, int UC>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
@@ -604,23 +607,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
     __syncthreads();
 
     // Jobs of this CTA: k = c + m*G.  Before the routing is known only the
-    // shared slots' gate/up tiles (k < nsh) can be decoded; the total needs
-    // the routed slot count.  Shared slot i is token i's shared expert when
-    // every token's runs here (nss = n_tok, from own_tok on), else own_tok's
-    // (nss = 1).
+    // shared slot's gate/up tiles (k < nsh) can be decoded; the total needs
+    // the routed slot count.
     static_assert(NU % UC == 0, "a slice is a whole fraction of the units");
-    const int nss = a.shared_all ? NT : 1;
-    const int nsh = nss * UC * TPU;
+    constexpr int nsh = NU * TPU;
     auto routed_slots = [&]() { return min(max(*s_nsr, 0), kDecodeMaxRouted); };
-    auto total_jobs = [&](int nsr) { return (nsr + nss) * UC * (TPU + NCH); };
-    auto hx_row = [&](int slot) { return slot < 0 ? kDecodeMaxRouted + (-1 - slot) : slot; };
-    // (shared slots from own_tok on: its activations are local in expert-parallel runs)
-    auto tok_of = [&](int slot) {
-        if (slot >= 0) return s_st[slot];
-        if (!a.shared_all) return a.own_tok;
-        const int t = -1 - slot + a.own_tok;
-        return t < NT ? t : t - NT;
-    };
+    auto total_jobs = [&](int nsr) { return (NU + nsr * UC) * (TPU + NCH); };
+    auto hx_row = [&](int slot) { return slot < 0 ? kDecodeMaxRouted : slot; };
+    auto tok_of = [&](int slot) { return slot < 0 ? a.own_tok : s_st[slot]; };
 
     if (warp == PROD) {
         // ================= producer (lane 0 issues) =================
@@ -639,18 +633,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
                 const uint8_t *p0, *p1, *p2;
             };
             auto job_src = [&](int m) -> Src {
-                const Job jb = job_of<UC, NCH>(c + m * G, nss, nsr);
-                const int e = jb.slot < 0 ? a.e_cnt : s_se[jb.slot];
+                const Job jb = job_of<UC, NU, NCH>(c + m * G, nsr);
+                const bool sh = jb.slot < 0;
+                // the shared expert (whole, after the routed ones) or a routed one (a slice of UC units)
+                const int e = sh ? a.e_cnt : s_se[jb.slot];
                 if (jb.gu) {
                     const int64_t o = (int64_t)e * a.gu_stride + (int64_t)(jb.unit * TPU + jb.j) * GU_BYTES;
                     return {a.gate + o, a.up + o, nullptr};
                 }
-                // the slab holds units u_lo .. u_lo+UC-1, then the d blocks from u_lo / 8 on
+                // the slab holds units u_lo .. u_lo+n-1, then the d blocks from u_lo / 8 on
                 const uint8_t* dc = a.down_col + (int64_t)e * a.dc_stride;
-                const int dblk = ((a.u_lo + jb.unit) >> 3) - (a.u_lo >> 3);
+                const int ulo = sh ? 0 : a.u_lo, nun = sh ? NU : UC;
+                const int dblk = ((ulo + jb.unit) >> 3) - (ulo >> 3);
                 return {dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)jb.j * RC * 8,
                         dc + (int64_t)jb.unit * UNIT_BYTES + (int64_t)H * 8 + (int64_t)jb.j * RC * 4,
-                        dc + (int64_t)UC * UNIT_BYTES + (int64_t)dblk * H * 2 + (int64_t)jb.j * RC * 2};
+                        dc + (int64_t)nun * UNIT_BYTES + (int64_t)dblk * H * 2 + (int64_t)jb.j * RC * 2};
             };
             for (int m = 0;; ++m) {
                 if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) need the slot list
@@ -868,9 +865,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
             // buffer of down job d was last read by down job d-2, whose stage
             // (two down jobs back, so before position m) this warp has seen done
             bool fetched = true;
-            const Job jb = job_of<UC, NCH>(c + m * G, nss, nsr);
+            const Job jb = job_of<UC, NU, NCH>(c + m * G, nsr);
             for (; fm <= m + 1 && fm < n && fetched; ++fm) {
-                const Job fj = job_of<UC, NCH>(c + fm * G, nss, nsr);
+                const Job fj = job_of<UC, NU, NCH>(c + fm * G, nsr);
                 if (fj.gu) continue;
                 // (not ahead of this CTA's own tile of the same unit, whose h
                 // this warp publishes only below)
@@ -973,26 +970,21 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
         uint32_t xq[16], hq[16];
         int cur = -1;  // the token whose activations xq holds
         float sx4 = 0.f, hs = 0.f;
-        // Expert-parallel, only own_tok's shared tiles are decoded before the
-        // routing: the other tokens' activations come over NVLink, and lanes
-        // waiting for them slow this SM's router and logit stores, which every
-        // CTA's top-k waits for (their weights are still fetched early).
-        const int nsh_c = EP ? UC * TPU : nsh;
-        int s = 0, n = jobs_of(c, G, nsh_c), nsr = 0, d = 0;
+        int s = 0, n = jobs_of(c, G, nsh), nsr = 0, d = 0;
         uint32_t ph = 0;
         bool have = false;
         auto give_up = [&]() {
             if (lane == 0) { *s_abort = 1; atomicOr(a.status, GP_DEV_TIMEOUT_FULL); }
         };
         for (int m = 0;; ++m) {
-            if (!have && c + m * G >= nsh_c) {  // routed jobs (and every down chunk) come after the routing
+            if (!have && c + m * G >= nsh) {  // routed jobs (and every down chunk) come after the routing
                 if (!__all_sync(0xffffffffu, mbar_wait(topk_bar, 0, a.spin_limit))) { give_up(); break; }
                 nsr = routed_slots();
                 n = jobs_of(c, G, total_jobs(nsr));
                 have = true;
             }
             if (m >= n) break;
-            const Job jb = job_of<UC, NCH>(c + m * G, nss, nsr);
+            const Job jb = job_of<UC, NU, NCH>(c + m * G, nsr);
             const int tok = tok_of(jb.slot);
             if (jb.gu) {
                 if (tok != cur) {  // that token's activations
@@ -1145,7 +1137,8 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
         !a.down_col || (reinterpret_cast<uintptr_t>(a.y) & 15))
         return cudaErrorInvalidValue;
     if (a.n_tok == 1 && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // one token: every expert
-    if (a.shared_all && (a.e_lo != 0 || a.e_cnt != a.E)) return cudaErrorInvalidValue;  // a slice of every expert
+    if (a.u_cnt && a.u_cnt != a.I / UNIT && (a.e_lo != 0 || a.e_cnt != a.E))
+        return cudaErrorInvalidValue;  // a slice of every routed expert
     if (a.ep_world > 1) {  // the peer-memory exchange: one token per rank, every rank's block mapped
         if (a.ep_world > kDecodeMaxTokens || a.n_tok != a.ep_world || a.ep_rank < 0 || a.ep_rank >= a.ep_world ||
             a.own_tok != a.ep_rank || !a.ep_x || !a.ep_sync || !a.ep_out || !a.ep_pk || a.K > 32 ||

@@ -193,13 +193,13 @@ struct DecodeLayerArgs {
     // tokens with nothing here); the ranks' parts sum to the layer output.
     int n_tok;                 // 1 .. kDecodeMaxTokens
     int e_lo, e_cnt;           // routed experts held (gate/up/down index e - e_lo; the shared expert at e_cnt)
-    int own_tok;               // token whose shared expert runs in this launch (shared_all = 0)
-    int shared_all;            // 1: every token's shared expert runs in this launch
-    int u_lo, u_cnt;           // units of 32 rows of each expert that the layer holds and this launch runs
-                               // (0, I/32: whole experts; a slice when each rank holds a slice of every expert)
+    int own_tok;               // token whose shared expert runs in this launch (the whole expert)
+    int u_lo, u_cnt;           // units of 32 rows of each routed expert that the layer holds and this launch
+                               // runs (0, I/32: whole experts; a slice when each rank holds a slice of every
+                               // routed expert: the shared expert, after them, stays whole)
     unsigned long long* logits;  // [decode_layer_logit_words(E)] router logits tagged with the launch generation
     unsigned long long* hx;      // [decode_layer_h_words(I)] h of every (slot, unit), tagged: rows of routed slot s
-                                 // at s * I, shared slot i's at (kDecodeMaxRouted + i) * I
+                                 // at s * I, the shared slot's at kDecodeMaxRouted * I
     unsigned* sync;            // [kDecodeSyncWords] launch generation and finished-CTA count
     const uint8_t* tables;
     uint32_t* status;
@@ -267,8 +267,8 @@ cudaError_t launch_ep_pack(const void* x, int x_bf16, int H, int n, int K, const
 // replicas of E tagged logits (every CTA reads every token's).
 inline size_t decode_layer_logit_words(int E) { return (size_t)kDecodeMaxTokens * 8 * E * 32; }
 // Words of DecodeLayerArgs::hx: one tagged h value per row of every slot's expert
-// (routed slots, then up to kDecodeMaxTokens shared slots).
-inline size_t decode_layer_h_words(int I) { return (size_t)(kDecodeMaxRouted + kDecodeMaxTokens) * I; }
+// (routed slots, then the shared slot).
+inline size_t decode_layer_h_words(int I) { return (size_t)(kDecodeMaxRouted + 1) * I; }
 // Whether the persistent decode kernel runs a slice of u_cnt of each expert's inter / 32 units.
 bool decode_layer_slice_supported(int I, int u_cnt);
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared);

@@ -248,10 +248,11 @@ class MoeLayer:
         return self
 
     def slice_units(self, unit_begin: int, unit_count: int) -> "MoeLayer":
-        """Keep units [unit_begin, unit_begin + unit_count) of every expert, a unit
-        being 32 intermediate rows (gpeed_moe_slice_units): one rank's share
-        of the tensor-parallel split of every expert.  The layer then serves
-        decode_partial and the expert-parallel decode only."""
+        """Keep units [unit_begin, unit_begin + unit_count) of every routed
+        expert, a unit being 32 intermediate rows (gpeed_moe_slice_units): one
+        rank's share of the tensor-parallel split of every routed expert; the
+        shared expert stays whole.  The layer then serves decode_partial and
+        the expert-parallel decode only."""
         call("gpeed_moe_slice_units", self.ctx.handle, self.layer_id, unit_begin, unit_count)
         return self
 
@@ -271,7 +272,7 @@ class MoeLayer:
         token's output that this layer's experts (plus own_tok's shared expert)
         contribute.  The ranks' parts sum to MoeLayer.forward of the whole layer.
         On a sliced layer (slice_units) the part is this slice of every pick
-        and of every token's shared expert, and own_tok is not used."""
+        plus own_tok's whole shared expert."""
         n = x_all.shape[0]
         if y_part is None:
             y_part = torch.empty(n, self.cfg.hidden, dtype=torch.float32, device=x_all.device)

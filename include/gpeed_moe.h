@@ -243,7 +243,7 @@ GPEED_API int gpeed_moe_forward(gpeed_ctx* ctx, int layer, const void* x_dev, in
  * of own_tok, and writes y_part[t] = sum of w_k D_k over those picks of token
  * t, in pick order, (+ D_shared for own_tok): zero rows for tokens with
  * nothing here.  On a layer sliced by units (gpeed_moe_slice_units) it runs
- * the slice of every pick and of every token's shared expert instead.  Summed over the ranks (a reduce-scatter), y_part gives
+ * this slice of every pick (and own_tok's whole shared expert).  Summed over the ranks (a reduce-scatter), y_part gives
  * gpeed_moe_forward's y up to the order of that sum.  forced_topk / topk_ids /
  * topk_w are [n_tok][K] as in gpeed_moe_forward.  No counterpart in the
  * reference (Model::moe_forward, model.cpp:692-756, runs every expert on one
@@ -265,7 +265,7 @@ GPEED_API int gpeed_moe_decode_partial(gpeed_ctx* ctx, int layer, const void* x_
  * shared expert (gpeed_moe_load_layer_range / _gguf / _synth_layer_range),
  * E/world routed experts per rank, or a whole layer sliced by units
  * (gpeed_moe_slice_units with unit_begin = rank * unit_count): every rank then
- * runs its slice of every pick and of every token's shared expert, the same
+ * runs its slice of every pick and its own token's shared expert, the same
  * work whatever the routing.  Inside one launch: the token goes to every rank as
  * tagged words, all world tokens are routed, this rank's picks of every token
  * run, and their down sums are added straight into the owning rank's
@@ -299,16 +299,18 @@ GPEED_API int gpeed_moe_synth_layer_range(gpeed_ctx* ctx, int layer, const gpeed
                                 int expert_count, const float* router_w, const float* corr_bias, int on_device,
                                 uint64_t seed, uint64_t stream0);
 /* Keeps only units [unit_begin, unit_begin + unit_count) of a loaded whole
- * layer's experts (routed and shared), a unit being 32 intermediate rows: the
- * gate/up rows unit*32 .. +31 and the same down columns.  The tensor-parallel
- * split of every expert: ranks r = 0 .. N-1 slicing [r*NU/N, (r+1)*NU/N) of
- * the NU = inter/32 units each compute, for every pick, a part of the down sum
- * (SwiGLU is row-wise, so the intermediate rows split exactly), and the parts
- * add up to the layer output.  unit_count: a divisor of NU the persistent
- * decode kernel has (48, 24, 12, 6 of inter 1536's 48 units); unit_begin a
- * multiple of it.  A sliced layer serves gpeed_moe_decode_partial (every
- * token's shared expert slice runs in each launch) and gpeed_moe_decode_ep;
- * the other entry points refuse it.  No counterpart in the reference. */
+ * layer's routed experts, a unit being 32 intermediate rows: the gate/up rows
+ * unit*32 .. +31 and the same down columns; the shared expert stays whole.
+ * The tensor-parallel split of every routed expert: ranks r = 0 .. N-1
+ * slicing [r*NU/N, (r+1)*NU/N) of the NU = inter/32 units each compute, for
+ * every pick, a part of the down sum (SwiGLU is row-wise, so the
+ * intermediate rows split exactly), and the parts add up to the layer output;
+ * each rank runs its own token's shared expert.  unit_count: a divisor of NU
+ * the persistent decode kernel has (48, 24, 12, 6 of inter 1536's 48 units);
+ * unit_begin a multiple of it.  A sliced layer serves
+ * gpeed_moe_decode_partial (the slice of every pick plus own_tok's shared
+ * expert) and gpeed_moe_decode_ep; the other entry points refuse it.  No
+ * counterpart in the reference. */
 GPEED_API int gpeed_moe_slice_units(gpeed_ctx* ctx, int layer, int unit_begin, int unit_count);
 /* Router + top-k only (model_batch.cpp:171-203): topk_ids/topk_w device [n_tok][K]. */
 GPEED_API int gpeed_moe_route(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, int n_tok,
