@@ -15,7 +15,9 @@ Other workloads: --workload ragged64 (config 3: 64 tokens, Zipf-skewed expert
 loads, quantised GEMV path), --workload prefill (config 4: 4096 tokens,
 tensor-core grouped GEMMs; with --ep and N >= 2 GPUs the experts are split over
 the GPUs with NCCL all-to-all dispatch and combine), --workload stack40 (config
-5 on one GPU: 40 layers, decode batches 1 to 256).
+5 on one GPU: 40 layers, decode batches 1 to 256), --workload glm5 (batch-1
+decode at the reference model's default MoE shape: hidden 4096, 288 experts,
+intermediate 2048).
 
 N > 1 (launched by torchrun): expert parallelism.  Every GPU holds 1/N of
 every routed expert's intermediate rows (units of 32 rows, the
@@ -592,6 +594,79 @@ def run_gpu_ep(args, rank, local_rank, world):
         pd.close()
     ctx.close()
     return line
+
+
+def run_glm5_decode(args):
+    """Batch-1 decode of one MoE layer at the reference model's own default
+    MoE shape (model_config.h:25, 59-60: hidden 4096, moe_inter 2048, 288
+    routed experts, top-8, one shared expert) through the same persistent
+    kernel: the kernel instantiated for H = 4096 (16 compute warps, down
+    chunks of 2048 rows).  Steps rotate over --layers layer copies (3.7 GB
+    each with the column-slab copy of W_down), captured back to back in CUDA
+    graphs as for decode1; algorithmic bytes per step: 9 experts x 3 matrices
+    of IQ3_XXS + the fp32 router + x and y."""
+    import torch
+
+    from gpeed_b200 import Context, MoeConfig, MoeLayer
+
+    Hg, Ig, Eg = 4096, 2048, 288
+    cfg = MoeConfig(hidden=Hg, inter=Ig, n_experts=Eg)
+    L = min(args.layers, 6)
+    ctx = Context(0)
+    rng = np.random.default_rng(7)
+    layers = [MoeLayer(ctx, cfg, layer_id=l).synth((rng.standard_normal((Eg, Hg)) * 0.02).astype(np.float32), None,
+                                                     seed=2000 + l, stream0=0) for l in range(L)]
+    xs = [torch.from_numpy(rng.standard_normal((1, Hg)).astype(np.float32)).to(torch.bfloat16).cuda() for _ in range(L)]
+    ys = [torch.empty(1, Hg, device="cuda") for _ in range(L)]
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for l in range(L):
+            layers[l].forward(xs[l], ys[l], stream=stream)
+    stream.synchronize()
+    ctx.check(stream)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        for l in range(L):
+            layers[l].forward(xs[l], ys[l], stream=stream)
+    reps = max(1, args.steps // L)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup // L)):
+            g.replay()
+    stream.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        with torch.cuda.stream(stream):
+            ev0.record(stream)
+            for _ in range(reps):
+                g.replay()
+            ev1.record(stream)
+        stream.synchronize()
+        soak_t0 = time.perf_counter()
+        with torch.cuda.stream(stream):
+            while time.perf_counter() - soak_t0 < 1.0:
+                for _ in range(25):
+                    g.replay()
+                stream.synchronize()
+    ctx.check(stream)
+    steps = reps * L
+    ms = ev0.elapsed_time(ev1) / steps
+    expert = 3 * Ig * (Hg // 256) * 98
+    step_bytes = 9 * expert + Eg * Hg * 4 + Hg * (2 + 4)
+    hbm_peak, _, peak_src = peaks()
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+    del g
+    ctx.close()
+    return {"metric": METRIC, "value": 1000.0 / ms, "unit": "tokens/s", "n_gpus": 1, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "iq3_xxs(int8)xint16->f32", "data": "synthetic",
+            "config": {"workload": "glm5: MoE layer decode, batch 1, at the reference model's default MoE shape",
+                       "hidden": Hg, "n_experts": Eg, "top_k": 8, "inter": Ig, "n_shared": 1, "quant": "IQ3_XXS",
+                       "layer_copies": L, "l2": "inputs larger than L2: steps rotate over the layer copies"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "traffic": None, "kernel": "decode_layer_kernel<4096, 2048> (batch 1)",
+                         "bytes_per_launch": step_bytes, "peak_source": peak_src},
+            "cpu_baseline": None, "e2e": None, "gpu_launches": steps, "clocks": clk.summary()}
 
 
 PREFILL_FLOPS_PER_TOKEN = (K_TOP + 1) * 3 * 2 * I * H + 2 * E * H   # experts + router, per token
@@ -1215,7 +1290,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--workload", default="decode1",
-                    choices=["decode1", "ragged64", "prefill", "stack40", "codecs", "dense", "mhc"],
+                    choices=["decode1", "ragged64", "prefill", "stack40", "codecs", "dense", "mhc", "glm5"],
                     help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
     ap.add_argument("--tokens", type=int, default=4096, help="batch of the prefill workload")
     ap.add_argument("--batch", type=int, default=64, help="tokens per step of the ragged64 workload")
@@ -1246,8 +1321,8 @@ def main():
         line = run_ragged(args, rank, local_rank, world)
     elif args.workload == "stack40":
         line = run_stack(args, rank, local_rank, world)
-    elif args.workload in ("codecs", "dense", "mhc"):
-        fn = {"codecs": run_codecs, "dense": run_dense, "mhc": run_mhc}[args.workload]
+    elif args.workload in ("codecs", "dense", "mhc", "glm5"):
+        fn = {"codecs": run_codecs, "dense": run_dense, "mhc": run_mhc, "glm5": run_glm5_decode}[args.workload]
         line = fn(args) if rank == 0 else None
     elif world > 1:
         line = run_gpu_ep(args, rank, local_rank, world)

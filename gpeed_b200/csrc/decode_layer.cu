@@ -65,17 +65,20 @@
 namespace gp {
 namespace {
 
-constexpr int NWC = 20;          // compute warps (gate/up: 32*20 lanes = 4 rows of 5120 per pass)
-constexpr int EPI = NWC;         // epilogue warp
-constexpr int PROD = NWC + 1;    // TMA producer warp
-constexpr int NTHREADS = 32 * (NWC + 2);
+// The CTA's shape follows the hidden size H (a multiple of 1024): H/256
+// compute warps, so one gate/up pass covers 4 whole rows (H/32 lanes per row,
+// a whole number of warps), and a down chunk is 4 rows per compute lane = H/2
+// rows.  H = 5120: 20 compute warps; H = 4096: 16.  Then one epilogue warp
+// and one TMA producer warp (warp indices NWC and NWC + 1).
+__host__ __device__ constexpr int nwc_of(int H) { return H / 256; }        // compute warps
+__host__ __device__ constexpr int nthreads_of(int H) { return 32 * (H / 256 + 2); }
+__host__ __device__ constexpr int rc_of(int H) { return H / 2; }            // down rows per chunk
 constexpr int TRG = 8;           // gate/up rows per matrix per tile
 constexpr int UNIT = 32;         // rows of h per unit = input columns of its down slice
 constexpr int TPU = UNIT / TRG;  // gate/up tiles per unit
-constexpr int RC = 4 * 32 * NWC; // down rows per chunk (four per compute lane)
 constexpr int RSPLIT = 8;        // router slices per expert
 constexpr int MAXK = 31;         // picks per token
-constexpr int kMaxEFused = 256;  // routed experts handled by the top-k warp
+constexpr int kMaxEFused = 512;  // routed experts handled by the top-k warp
 constexpr int kMaxOwned = 8;     // router experts per CTA (grid >= E/8)
 // Tagged logits: with one token every CTA polls all E of them, so one array
 // would send every poll of every CTA to the few L2 slices holding it.  Each
@@ -361,10 +364,86 @@ GP_DEVINL bool topk_token(const DecodeLayerArgs& a, const float* bias, uint32_t 
     return got;
 }
 
+// Top-K for many experts per lane (EJ > 8, up to 512 experts): the sort
+// below would hold EJ keys, ids and scores per lane at once.  Here each
+// round takes every lane's best remaining key (ties to the lower j, so the
+// lower id), the warp maximum (redux), the lowest id holding it, and that
+// lane marks the candidate taken and recomputes its score from the logit.
+// Same choices, order and weights as the sorted form.
+template <int EJ>
+GP_DEVINL void select_topk_wide(const DecodeLayerArgs& a, const float* bias, const uint32_t (&w)[EJ], int lane,
+                                int tok, bool write_out, int& my_e, float& my_w) {
+    const int E = a.E, K = a.K;
+    uint32_t key[EJ];
+#pragma unroll
+    for (int j = 0; j < EJ; ++j) {
+        const int e = lane + 32 * j;
+        const float sc = 1.0f / (1.0f + expf(-__uint_as_float(w[j])));
+        key[j] = e < E ? order_key(sc + bias[j]) : 0u;  // 0: below every float's key (and taken)
+    }
+    float denom = 1e-20f, my_s = 0.f;
+    my_e = 0;
+    if (a.forced) {
+        const int* forced = a.forced + (int64_t)tok * K;
+        for (int k = 0; k < K; ++k) {
+            int eb = forced[k];
+            if (eb < 0 || eb >= E) {
+                if (lane == 0) atomicOr(a.status, GP_DEV_BAD_EXPERT);
+                eb = 0;
+            }
+            float lg = 0.f;
+#pragma unroll
+            for (int j = 0; j < EJ; ++j)
+                if (lane + 32 * j == eb) lg = __uint_as_float(w[j]);
+            lg = __shfl_sync(0xffffffffu, lg, eb & 31);
+            const float sc = 1.0f / (1.0f + expf(-lg));
+            denom += sc;  // model.cpp:718-721 order
+            if (lane == k) { my_s = sc; my_e = eb; }
+        }
+    } else {
+        for (int k = 0; k < K; ++k) {
+            uint32_t bk = key[0];
+            int bj = 0;
+#pragma unroll
+            for (int j = 1; j < EJ; ++j)
+                if (key[j] > bk) { bk = key[j]; bj = j; }
+            const uint32_t m = __reduce_max_sync(0xffffffffu, bk);
+            const uint32_t eb = __reduce_min_sync(0xffffffffu, bk == m ? (uint32_t)(lane + 32 * bj) : 0xffffffffu);
+            float lg = 0.f;
+            if (lane == (int)(eb & 31u)) {
+#pragma unroll
+                for (int j = 0; j < EJ; ++j)
+                    if (j == (int)(eb >> 5)) { lg = __uint_as_float(w[j]); key[j] = 0u; }
+            }
+            lg = __shfl_sync(0xffffffffu, lg, eb & 31);
+            const float sc = 1.0f / (1.0f + expf(-lg));
+            denom += sc;  // model.cpp:718-721 order
+            if (lane == k) { my_s = sc; my_e = (int)eb; }
+        }
+    }
+    my_w = a.norm_topk ? (my_s / denom) * a.routed_scale : my_s * a.routed_scale;
+    if (write_out && a.topk_ids && lane < K) a.topk_ids[(int64_t)tok * K + lane] = my_e;
+    if (write_out && a.topk_w && lane < K) a.topk_w[(int64_t)tok * K + lane] = my_w;
+}
+
 // One token's top-K from its E logits (w, one tagged word per expert lane + 32j).
+template <int EJ>
+GP_DEVINL void select_topk_sorted(const DecodeLayerArgs& a, const float* bias, const uint32_t (&w)[EJ], int lane,
+                                  int tok, bool write_out, int& my_e, float& my_w);
 template <int EJ>
 GP_DEVINL void select_topk(const DecodeLayerArgs& a, const float* bias, const uint32_t (&w)[EJ], int lane, int tok,
                            bool write_out, int& my_e, float& my_w) {
+    if constexpr (EJ > 8)
+        select_topk_wide<EJ>(a, bias, w, lane, tok, write_out, my_e, my_w);
+    else
+        select_topk_sorted<EJ>(a, bias, w, lane, tok, write_out, my_e, my_w);
+}
+
+// The lane's EJ candidates sorted by (key desc, id asc), then K rounds of
+// warp maxima over the lanes' heads.
+template <int EJ>
+GP_DEVINL void select_topk_sorted(const DecodeLayerArgs& a, const float* bias, const uint32_t (&w)[EJ], int lane,
+                                  int tok, bool write_out, int& my_e, float& my_w) {
     const int E = a.E, K = a.K;
     float score[EJ];
     uint32_t key[EJ], id[EJ];
@@ -468,8 +547,12 @@ GP_DEVINL void build_slots(const DecodeLayerArgs& a, int lane, int e0, float w0,
     if (lane == 0) *s_nsr = __popc(b0) + __popc(b1);
 }
 
-// Per-stage partial sums of a gate/up tile: one per (row of the tile, covering warp).
-constexpr uint32_t kPartialFloats = 2 * TRG * LaneMap<5120, NWC, 4>::WPR;
+// Per-stage partial sums of a gate/up tile: one per (row of the tile, covering
+// warp); a row of H weights is covered by H/1024 warps.
+__host__ __device__ constexpr uint32_t partial_floats_of(int H) { return 2u * TRG * (uint32_t)(H / 1024); }
+static_assert(partial_floats_of(5120) == 2 * TRG * LaneMap<5120, 20, 4>::WPR &&
+                  partial_floats_of(4096) == 2 * TRG * LaneMap<4096, 16, 4>::WPR,
+              "partial sums per stage");
 
 struct Smem {
     uint32_t stage_bytes, stages_off, partial_off, bar_off, misc_off, total;
@@ -482,12 +565,12 @@ struct Smem {
 __host__ __device__ inline Smem decode_smem(int H, int I, int S, int n_tok) {
     Smem L;
     const uint32_t gu = 2u * TRG * 98u * (H / 256);
-    const uint32_t dn = (uint32_t)RC * 14u;
+    const uint32_t dn = (uint32_t)rc_of(H) * 14u;
     (void)I;
     L.stage_bytes = ((gu > dn ? gu : dn) + 15u) & ~15u;
     L.stages_off = GP_IQ3_TABLE_BYTES;
     L.partial_off = L.stages_off + S * L.stage_bytes;
-    const uint32_t pb = kPartialFloats * 4u;
+    const uint32_t pb = partial_floats_of(H) * 4u;
     L.bar_off = (L.partial_off + S * pb + 15u) & ~15u;
     // 16-byte aligned: the quantised h units are read with 16-byte loads (every
     // offset inside the block below is a multiple of 16)
@@ -553,11 +636,15 @@ GP_DEVINL void quantise_unit(float v, uint32_t* words, int lane) {
 // slot's expert that this launch runs (NU, or NU / N when each of N ranks
 // holds a slice of every routed expert).
 template <int HH, int II, int PG, int RPWG, bool EP, int UC>
-__global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeLayerArgs a) {
+__global__ void __launch_bounds__(nthreads_of(HH), 1) decode_layer_kernel(const DecodeLayerArgs a) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, c = blockIdx.x;
     constexpr int H = HH, I = II;
+    constexpr int NWC = nwc_of(HH), EPI = NWC, PROD = NWC + 1, RC = rc_of(HH);
+    constexpr uint32_t kPartialFloats = partial_floats_of(HH);
+    static_assert(HH % 1024 == 0 && LaneMap<HH, NWC, PG>::ROWSTEP == 4 && PG * 4 == 2 * TRG,
+                  "4 rows of a gate/up tile per pass");
     constexpr int NU = I / UNIT, NCH = H / RC;
     constexpr uint32_t GU_BYTES = TRG * 98u * (H / 256);
     constexpr uint32_t UNIT_BYTES = (uint32_t)H * 12u;  // one column unit of W_down: qs + aux of every row
@@ -689,7 +776,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
 
     if (warp == EPI) {
         // ================= routing, then the gate/up epilogues and h fetches =================
-        constexpr int EJ = kMaxEFused / 32;
+        // top-k candidates per lane: E <= 32 * EJ (the reference model's 288 experts at H = 4096)
+        constexpr int EJ = HH == 4096 ? kMaxEFused / 32 : 8;
         float bias[EJ];
 #pragma unroll
         for (int j = 0; j < EJ; ++j) bias[j] = a.corr && lane + 32 * j < E ? __ldg(a.corr + lane + 32 * j) : 0.f;
@@ -1116,15 +1204,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_layer_kernel(const DecodeL
 
 }  // namespace
 
+// Instantiated shapes: (H, I) = (5120, 1536) with up to 256 routed experts
+// (the BASELINE layer) and (4096, 2048) with up to 512 (the reference
+// model's default MoE shape, model_config.h:25, 59-60: 288 experts).
+static int max_experts_of(int H, int I) {
+    if (H == 5120 && I == 1536) return 256;
+    if (H == 4096 && I == 2048) return kMaxEFused;
+    return 0;
+}
+
 bool decode_layer_slice_supported(int I, int u_cnt) {
-    return I == 1536 && (u_cnt == 48 || u_cnt == 24 || u_cnt == 12 || u_cnt == 6);
+    const int nu = I / UNIT;
+    return (I == 1536 || I == 2048) && (u_cnt == nu || u_cnt == nu / 2 || u_cnt == nu / 4 || u_cnt == nu / 8);
 }
 
 bool decode_layer_supported(int H, int I, int E, int K, int with_shared) {
-    if (E > kMaxEFused || E < K) return false;
-    // the instantiated work mapping: gate/up 20 warps over 4 rows of H = 5120
-    // (4 passes), down chunks of 1280 rows
-    return H == 5120 && I == 1536 && K >= 1 && K <= MAXK && with_shared == 1;
+    if (E > max_experts_of(H, I) || E < K) return false;
+    // gate/up: H/256 compute warps over 4 rows of H per pass; down chunks of H/2 rows
+    return K >= 1 && K <= MAXK && with_shared == 1;
 }
 
 size_t decode_layer_smem(int H, int I, int stages, int n_tok) { return decode_smem(H, I, stages, n_tok).total; }
@@ -1162,30 +1259,43 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
     using Kern = void (*)(const DecodeLayerArgs);
     Kern kern = nullptr;
     int ki = -1;
-    constexpr int kH = 5120, kI = 1536;
-    if (!ep && uc == 48) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 48>; ki = 0; }
-    else if (!ep && uc == 24) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 24>; ki = 1; }
-    else if (!ep && uc == 12) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 12>; ki = 2; }
-    else if (!ep && uc == 6) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 6>; ki = 3; }
-    else if (ep && uc == 48) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 48>; ki = 4; }
-    else if (ep && uc == 24) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 24>; ki = 5; }
-    else if (ep && uc == 12) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 12>; ki = 6; }
-    else if (ep && uc == 6) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 6>; ki = 7; }
+    if (a.H == 5120) {
+        constexpr int kH = 5120, kI = 1536;
+        if (!ep && uc == 48) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 48>; ki = 0; }
+        else if (!ep && uc == 24) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 24>; ki = 1; }
+        else if (!ep && uc == 12) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 12>; ki = 2; }
+        else if (!ep && uc == 6) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 6>; ki = 3; }
+        else if (ep && uc == 48) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 48>; ki = 4; }
+        else if (ep && uc == 24) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 24>; ki = 5; }
+        else if (ep && uc == 12) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 12>; ki = 6; }
+        else if (ep && uc == 6) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 6>; ki = 7; }
+    } else {
+        constexpr int kH = 4096, kI = 2048;
+        if (!ep && uc == 64) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 64>; ki = 8; }
+        else if (!ep && uc == 32) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 32>; ki = 9; }
+        else if (!ep && uc == 16) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 16>; ki = 10; }
+        else if (!ep && uc == 8) { kern = decode_layer_kernel<kH, kI, 4, 1, false, 8>; ki = 11; }
+        else if (ep && uc == 64) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 64>; ki = 12; }
+        else if (ep && uc == 32) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 32>; ki = 13; }
+        else if (ep && uc == 16) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 16>; ki = 14; }
+        else if (ep && uc == 8) { kern = decode_layer_kernel<kH, kI, 4, 1, true, 8>; ki = 15; }
+    }
     if (!kern) return cudaErrorInvalidValue;
-    static std::atomic<unsigned long long> configured[8] = {};  // per device, per instantiation
+    const int nthreads = nthreads_of(a.H);
+    static std::atomic<unsigned long long> configured[16] = {};  // per device, per instantiation
     if (cudaError_t e0 = raise_smem_limit(kern, 227 * 1024, configured[ki])) return e0;
     // Co-residency: every CTA waits on data the others publish, so the grid
     // must fit the GPU at one CTA per SM.  Checked against the kernel's real
     // resource use (registers, shared memory) once per device; a grid larger
     // than the SMs that can hold a CTA is refused rather than left to time out.
-    static std::atomic<unsigned long long> fits_all[8] = {};
+    static std::atomic<unsigned long long> fits_all[16] = {};
     std::atomic<unsigned long long>& fits = fits_all[ki];
     int dev = 0;
     if (cudaError_t e1 = cudaGetDevice(&dev)) return e1;
     const unsigned long long bit = dev < 64 ? 1ull << dev : 0ull;
     if (!bit || !(fits.load(std::memory_order_acquire) & bit)) {
         int per_sm = 0, sms = 0;
-        if (cudaError_t e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, NTHREADS, 227 * 1024))
+        if (cudaError_t e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, nthreads, 227 * 1024))
             return e2;
         if (cudaError_t e3 = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) return e3;
         if (per_sm < 1 || grid > sms * per_sm) return cudaErrorCooperativeLaunchTooLarge;
@@ -1193,7 +1303,7 @@ cudaError_t launch_decode_layer(const DecodeLayerArgs& a, int grid, cudaStream_t
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(NTHREADS);
+    cfg.blockDim = dim3(nthreads);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;
     // One CTA per SM, all resident at once.  The default launch lets this

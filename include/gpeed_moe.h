@@ -84,8 +84,11 @@ GPEED_API int gpeed_ctx_check(gpeed_ctx* ctx, void* stream);
 
 /* Context options.  GPEED_OPT_FUSED_DECODE (default 1): run a batch-1
  * gpeed_moe_forward as one persistent kernel when the layer shape has a
- * compiled variant; 0 forces the multi-kernel path (same results within
- * rounding).  No counterpart in the reference. */
+ * compiled variant: hidden 5120 / inter 1536 with up to 256 routed experts,
+ * and hidden 4096 / inter 2048 with up to 512 (the reference model's default
+ * MoE shape, model_config.h:25, 59-60), one shared expert; 0 forces the
+ * multi-kernel path (same results within rounding).  No counterpart in the
+ * reference. */
 #define GPEED_OPT_FUSED_DECODE 1
 /* GPEED_OPT_FUSED_COOPERATIVE (default 0): launch that persistent kernel
  * cooperatively.  By default its CTAs start as the previous kernel's CTAs
@@ -306,7 +309,8 @@ GPEED_API int gpeed_moe_synth_layer_range(gpeed_ctx* ctx, int layer, const gpeed
  * every pick, a part of the down sum (SwiGLU is row-wise, so the
  * intermediate rows split exactly), and the parts add up to the layer output;
  * each rank runs its own token's shared expert.  unit_count: a divisor of NU
- * the persistent decode kernel has (48, 24, 12, 6 of inter 1536's 48 units);
+ * the persistent decode kernel has (NU, NU/2, NU/4, NU/8 for inter 1536 and
+ * 2048);
  * unit_begin a multiple of it.  A sliced layer serves
  * gpeed_moe_decode_partial (the slice of every pick plus own_tok's shared
  * expert) and gpeed_moe_decode_ep; the other entry points refuse it.  No
