@@ -102,7 +102,8 @@ __host__ __device__ inline TcSmem tc_smem(int kin) {
 }
 
 struct TcMaps {
-    CUtensorMap b;         // token rows, fp16 [positions][kin], box {64, 256}, 128-byte swizzle
+    CUtensorMap b;         // token rows, fp16 [positions][kin], box {64, TBN}, 128-byte swizzle
+    CUtensorMap bh[4];     // the same rows in boxes of 16, 32, 64 and 128 rows (slots of few tokens)
     CUtensorMap qs[2];     // per matrix: index bytes {64*NBLK, 8, groups}, box {16, 8, 16}
     CUtensorMap aux[2];    // sign/scale words {32*NBLK, 8, groups}, box {16, 8, 16}
     CUtensorMap dsc[2];    // fp16 scales {16*NBLK/q, q, groups}, box {16*NBLK/q, q, 16}
@@ -262,13 +263,19 @@ __global__ void __launch_bounds__(TcCfg<GU>::THREADS, 1)
             uint32_t bph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
-                const int row0 = a.slots[t / a.mt].begin;
+                const SlotDesc sd = a.slots[t / a.mt];
+                const int row0 = sd.begin;
+                // the smallest box holding the slot's rows (the MMA reads N = rows rounded up to 16):
+                // a slot of a few tokens moves a few KB per slice instead of TBN rows
+                const int hc = sd.ntok <= 16 ? 0 : sd.ntok <= 32 ? 1 : sd.ntok <= 64 ? 2 : sd.ntok <= 128 ? 3 : 4;
+                const CUtensorMap* bm = hc < 4 ? &maps.bh[hc] : &maps.b;
+                const uint32_t bbytes = (hc < 4 ? (16u << hc) : (uint32_t)TBN) * TBK * 2u;
                 for (int c = 0; c < nk; ++c) {
                     TC_MARK(t_se);
                     if (!mbar_wait(sb_empty + 8 * sb, bph ^ 1u)) { ok = false; break; }
                     TC_ACC(0, t_se);
-                    mbar_arrive_expect_tx(sb_full + 8 * sb, B_TILE);
-                    tma_load_2d(base + sb * B_TILE, &maps.b, c * TBK, row0, sb_full + 8 * sb);
+                    mbar_arrive_expect_tx(sb_full + 8 * sb, bbytes);
+                    tma_load_2d(base + sb * B_TILE, bm, c * TBK, row0, sb_full + 8 * sb);
                     if (++sb == TSB) { sb = 0; bph ^= 1u; }
                 }
             }
@@ -587,6 +594,11 @@ cudaError_t launch_tc_moe(bool gu, const uint8_t* w0, const uint8_t* w1, int64_t
         const cuuint32_t box[2] = {TBK, TBN};
         if (!encode(&m.b, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B))
             return cudaErrorInvalidValue;
+        for (int hc = 0; hc < 4; ++hc) {
+            const cuuint32_t boxh[2] = {TBK, 16u << hc};
+            if (!encode(&m.bh[hc], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b, dims, str, boxh, CU_TENSOR_MAP_SWIZZLE_128B))
+                return cudaErrorInvalidValue;
+        }
     }
     if (!encode_weight_maps(m, 0, w0, weight_rows / 8, kin)) return cudaErrorInvalidValue;
     if (gu && !encode_weight_maps(m, 1, w1, weight_rows / 8, kin)) return cudaErrorInvalidValue;
