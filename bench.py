@@ -209,6 +209,56 @@ def run_reference(args, world):
     print(json.dumps(line), flush=True)
 
 
+def prefill_side_timing(ctx, layers, stream, n=4096, reps=6):
+    """BASELINE config 4 timed once beside the decode workload (not the line's
+    value): `reps` forwards of an n-token bf16 batch through the already
+    resident layer copies, alternating, so each forward streams its experts
+    from HBM; CUDA events on the launching stream, after two warm-up
+    forwards.  Reports ms per layer forward, tokens/s, the grouped GEMMs'
+    share (per-stage events of one more forward) and the gate/up GEMM's
+    TFLOP/s.  Any failure here is reported in the dict instead of ending the
+    run."""
+    import torch
+
+    from gpeed_b200 import _capi
+    try:
+        x = tokens(n, 4242).cuda()
+        y = torch.empty(n, H, device="cuda")
+        with torch.cuda.stream(stream):
+            for l in range(2):
+                layers[l % len(layers)].forward(x, y, stream=stream)
+        stream.synchronize()
+        ctx.check(stream)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for i in range(reps):
+                layers[i % len(layers)].forward(x, y, stream=stream)
+            e1.record(stream)
+        stream.synchronize()
+        ctx.check(stream)
+        ms = e0.elapsed_time(e1) / reps
+        _capi.call("gpeed_ctx_profile", ctx.handle, 1)
+        try:
+            with torch.cuda.stream(stream):
+                layers[0].forward(x, y, stream=stream)
+            stage = (ctypes.c_float * 5)()
+            calls = ctypes.c_int()
+            _capi.call("gpeed_ctx_profile_read", ctx.handle, stage, ctypes.byref(calls))
+        finally:
+            _capi.call("gpeed_ctx_profile", ctx.handle, 0)
+        ctx.check(stream)
+        gu_flops = (K_TOP + 1) * 2 * 2 * I * H * n  # gate + up, every (token, pick) and the shared expert
+        out = {"tokens": n, "ms_per_layer": ms, "tokens_per_s": n / (ms / 1000.0),
+               "stage_ms": dict(zip(["router", "route+gather", "gateup", "down", "combine"], list(stage))),
+               "gateup_tflops": gu_flops / (stage[2] * 1e-3) / 1e12 if stage[2] > 0 else None,
+               "how": f"{reps} forwards alternating {len(layers)} resident layer copies, CUDA events"}
+        del x, y
+        return out
+    except Exception as exc:  # a side figure: the decode line stands without it
+        return {"error": str(exc)[:300]}
+
+
 def run_gpu(args, rank, local_rank, world):
     import torch
     import torch.distributed as dist
@@ -334,6 +384,8 @@ def run_gpu(args, rank, local_rank, world):
     e2e_value = world * args.steps / e2e_s
     ctx.check(stream)
 
+    prefill = prefill_side_timing(ctx, layers[:2], stream) if world == 1 and not args.no_prefill else None
+
     hbm_peak, _, peak_src = peaks()
     fused = stage_ms[0] == 0 and stage_ms[1] == 0 and stage_ms[3] == 0 and stage_ms[4] == 0
     if fused:  # the whole layer is one persistent kernel
@@ -370,7 +422,8 @@ def run_gpu(args, rank, local_rank, world):
                        "per_gpu_layer_hbm_gbs": layer_gbs,
                        "per_gpu_layer_hbm_frac": layer_gbs / hbm_peak,
                        "stage_ms": ({"layer_launched_alone": stage_ms[2]} if fused else
-                                    dict(zip(["router", "route", "gateup", "down", "combine"], stage_ms)))},
+                                    dict(zip(["router", "route", "gateup", "down", "combine"], stage_ms))),
+                       "prefill4096_side_timing": prefill},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": (achieved / hbm_peak) if achieved else None, "traffic": traffic,
                          "kernel": kern_name, "bytes_per_launch": kern_bytes,
@@ -1289,6 +1342,8 @@ def main():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="decode1 at N=1: skip the one-shot config-4 timing reported beside the line")
     ap.add_argument("--workload", default="decode1",
                     choices=["decode1", "ragged64", "prefill", "stack40", "codecs", "dense", "mhc", "glm5"],
                     help="decode1: BASELINE config 2 (default); ragged64: config 3; prefill: config 4")
