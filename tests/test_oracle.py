@@ -143,3 +143,31 @@ def test_port_equals_compiled_reference_at_full_width():
         np.testing.assert_array_equal(u, v)
     blocks = oracle.synth_iq3xxs(9, 9, 2000)
     np.testing.assert_array_equal(port.dequantize(blocks).view(np.uint32), ref.dequantize(blocks).view(np.uint32))
+
+
+@pytest.mark.skipif(not oracle.available("reference"), reason="oracle/_ref not built")
+def test_port_equals_compiled_reference_at_the_reference_model_shape():
+    """The reference model's default MoE widths (model_config.h:25, 59-60:
+    hidden 4096, moe_inter 2048), 8 experts, top-8 (every expert picked, in
+    the router's order) and the forced form of the same picks: the port and
+    the compiled reference agree bit for bit.  The GPU test at this shape
+    compares against the port on the picked experts only."""
+    port, ref = oracle.Checker("port"), oracle.Checker("reference")
+    rng = np.random.default_rng(6)
+    H, I, E, K = 4096, 2048, 8, 8
+    nb = lambda rows, inn: rows * inn // 256
+    layer = dict(gate=oracle.synth_iq3xxs(4, 1, nb(E * I, H)), up=oracle.synth_iq3xxs(4, 2, nb(E * I, H)),
+                 down=oracle.synth_iq3xxs(4, 3, nb(E * H, I)), gate_sh=oracle.synth_iq3xxs(4, 4, nb(I, H)),
+                 up_sh=oracle.synth_iq3xxs(4, 5, nb(I, H)), down_sh=oracle.synth_iq3xxs(4, 6, nb(H, I)),
+                 router=(rng.standard_normal((E, H)) * 0.02).astype(np.float32), corr=np.zeros(E, np.float32))
+    shape = oracle.Shape(H, I, E, K, 2.5, 1, 10.0)
+    x = rng.standard_normal(H).astype(np.float32)
+    a = port.moe_forward(shape, layer, x)
+    b = ref.moe_forward(shape, layer, x)
+    for u, v in zip(a, b):
+        np.testing.assert_array_equal(u, v)
+    forced = np.arange(K, dtype=np.int32)[::-1].copy()
+    a = port.moe_forward(shape, layer, x, forced=forced)
+    b = ref.moe_forward(shape, layer, x, forced=forced)
+    for u, v in zip(a, b):
+        np.testing.assert_array_equal(u, v)
