@@ -1297,6 +1297,17 @@ int gpeed_moe_decode_ep(gpeed_ctx* c, int layer, const void* x, int x_dtype, flo
     if (!gp::decode_layer_supported(H, I, E, K, s.n_shared))
         return fail(GPEED_ERR_UNSUPPORTED, "no persistent decode kernel for hidden %d, inter %d, %d experts, top-%d, "
                     "%d shared", H, I, E, K, s.n_shared);
+    // The ranks' shares must cover every pick exactly once: rank r holds the
+    // r-th of n equal unit slices of every routed expert, or the r-th of n
+    // equal expert ranges.  Any other share (a whole layer on every rank, or
+    // slices of another world size) would count picks twice or not at all.
+    const int NU = I / 32, r = c->ep.rank;
+    const bool by_units = L.sliced() && L.e_lo == 0 && L.e_cnt == E && NU % n == 0 && L.u_cnt == NU / n &&
+                          L.u_lo == r * L.u_cnt;
+    const bool by_experts = !L.sliced() && E % n == 0 && L.e_cnt == E / n && L.e_lo == r * L.e_cnt;
+    if (!by_units && !by_experts)
+        return fail(GPEED_ERR_INVALID, "layer %d is not rank %d's share of %d (units [%d, %d) of %d, experts [%d, %d) "
+                    "of %d)", layer, r, n, L.u_lo, L.u_lo + L.u_cnt, NU, L.e_lo, L.e_lo + L.e_cnt, E);
     int rc;
     if ((rc = set_device(c))) return rc;
     cudaStream_t st = (cudaStream_t)stream;

@@ -269,7 +269,9 @@ GPEED_API int gpeed_moe_decode_partial(gpeed_ctx* ctx, int layer, const void* x_
  * E/world routed experts per rank, or a whole layer sliced by units
  * (gpeed_moe_slice_units with unit_begin = rank * unit_count): every rank then
  * runs its slice of every pick and its own token's shared expert, the same
- * work whatever the routing.  Inside one launch: the token goes to every rank as
+ * work whatever the routing.  Any other share (a whole layer, or the share
+ * of another rank or world size) is refused with GPEED_ERR_INVALID: the
+ * ranks' shares must cover every pick exactly once.  Inside one launch: the token goes to every rank as
  * tagged words, all world tokens are routed, this rank's picks of every token
  * run, and their down sums are added straight into the owning rank's
  * accumulator; the kernel ends when every other rank has signalled that its
