@@ -75,6 +75,7 @@ SIGNATURES = {
     "gpeed_moe_synth_layer": [_vp, _i, ctypes.POINTER(MoeShape), _vp, _vp, _i, _u64, _u64],
     "gpeed_synth_iq3xxs": [_vp, _u64, _u64, _u64, _u64, _vp],
     "gpeed_moe_forward": [_vp, _i, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp],
+    "gpeed_moe_forward_host": [_vp, _i, _vp, _i, _i, _vp],
     "gpeed_moe_load_layer_range": [_vp, _i, ctypes.POINTER(MoeShape), _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                    _vp, _i],
     "gpeed_moe_synth_layer_range": [_vp, _i, ctypes.POINTER(MoeShape), _i, _i, _vp, _vp, _i, _u64, _u64],

@@ -878,6 +878,47 @@ int gpeed_matvec_quant_host(gpeed_ctx* c, int handle, uint64_t row0, int in_dim,
     return gpeed_matmul_quant_host(c, handle, row0, in_dim, out_dim, x, 1, dst);
 }
 
+int gpeed_moe_forward_host(gpeed_ctx* c, int layer, const void* x, int x_dtype, int n, float* y) {
+    if (!c) return fail(GPEED_ERR_INVALID, "ctx is NULL");
+    auto it = c->layers.find(layer);
+    if (it == c->layers.end()) return fail(GPEED_ERR_INVALID, "layer %d not loaded", layer);
+    if (n < 0) return fail(GPEED_ERR_INVALID, "n_tok < 0");
+    if (n == 0) return GPEED_OK;
+    if (x_dtype != GPEED_DTYPE_BF16 && x_dtype != GPEED_DTYPE_F32)
+        return fail(GPEED_ERR_UNSUPPORTED, "x_dtype %d: use GPEED_DTYPE_BF16 or GPEED_DTYPE_F32", x_dtype);
+    if (!x || !y) return fail(GPEED_ERR_INVALID, "x and y must be host buffers");
+    const int H = it->second.shape.hidden;
+    int rc;
+    if ((rc = set_device(c))) return rc;
+    std::lock_guard<std::mutex> lock(c->host_mu);
+    if (!c->host_stream) GP_CUDA(cudaStreamCreateWithFlags(&c->host_stream, cudaStreamNonBlocking));
+    // staging in floats: x (bf16 rows take half the room), then y from a
+    // 16-byte boundary, then the device status word (read back with y, so
+    // the call waits once)
+    const size_t xbytes = (size_t)n * H * (x_dtype == GPEED_DTYPE_BF16 ? 2 : 4), ny = (size_t)n * H;
+    const size_t nx = ((xbytes + 15) & ~(size_t)15) / sizeof(float);
+    if (c->host_pin_n < nx + ny + 4) {
+        if (c->host_pin) cudaFreeHost(c->host_pin);
+        c->host_pin = nullptr;
+        c->host_pin_n = 0;
+        GP_CUDA(cudaHostAlloc(&c->host_pin, (nx + ny + 4) * sizeof(float), cudaHostAllocDefault));
+        c->host_pin_n = nx + ny + 4;
+    }
+    if ((rc = c->host_x.ensure(nx)) || (rc = c->host_y.ensure(ny))) return rc;
+    cudaStream_t st = c->host_stream;
+    std::memcpy(c->host_pin, x, xbytes);
+    GP_CUDA(cudaMemcpyAsync(c->host_x.p, c->host_pin, xbytes, cudaMemcpyHostToDevice, st));
+    if ((rc = gpeed_moe_forward(c, layer, c->host_x.p, x_dtype, n, c->host_y.p, nullptr, nullptr, nullptr, st)))
+        return rc;
+    uint32_t* status_pin = reinterpret_cast<uint32_t*>(c->host_pin + nx + ny);
+    GP_CUDA(cudaMemcpyAsync(c->host_pin + nx, c->host_y.p, ny * sizeof(float), cudaMemcpyDeviceToHost, st));
+    GP_CUDA(cudaMemcpyAsync(status_pin, c->status, sizeof(uint32_t), cudaMemcpyDeviceToHost, st));
+    GP_CUDA(cudaStreamSynchronize(st));
+    std::memcpy(y, c->host_pin + nx, ny * sizeof(float));
+    if (*status_pin) return gpeed_ctx_check(c, st);  // reports and clears it
+    return GPEED_OK;
+}
+
 int gpeed_moe_load_layer_range(gpeed_ctx* c, int layer, const gpeed_moe_shape* s, int expert_begin, int expert_count,
                                const float* router_w, const float* corr, const void* gate, const void* up,
                                const void* down, const void* gate_sh, const void* up_sh, const void* down_sh,

@@ -297,3 +297,26 @@ class MoeLayer:
         call("gpeed_moe_forward", self.ctx.handle, self.layer_id, _ptr(x.contiguous()), dt, n, _ptr(y),
              _ptr(forced_topk), _ptr(topk_ids), _ptr(topk_w), _stream(stream))
         return y
+
+    def forward_host(self, x: torch.Tensor, y: torch.Tensor | None = None) -> torch.Tensor:
+        """x [n, H] bf16/fp32 in host memory -> y [n, H] fp32 in host memory
+        (gpeed_moe_forward_host: the reference's callers pass host vectors to
+        Model::moe_forward / moe_batch; the call returns with y filled)."""
+        if x.dim() == 1:
+            x = x.unsqueeze(0)
+        if x.is_cuda:
+            raise GpeedError(_capi.ERR_INVALID, "forward_host takes host tensors; use forward for device tensors")
+        n = x.shape[0]
+        if x.dtype == torch.bfloat16:
+            dt = _capi.DTYPE_BF16
+        elif x.dtype == torch.float32:
+            dt = _capi.DTYPE_F32
+        else:
+            raise GpeedError(_capi.ERR_UNSUPPORTED, f"x dtype {x.dtype}")
+        x = x.contiguous()
+        if y is None:
+            y = torch.empty(n, self.cfg.hidden, dtype=torch.float32)
+        if y.is_cuda or y.dtype != torch.float32 or not y.is_contiguous() or y.numel() < n * self.cfg.hidden:
+            raise GpeedError(_capi.ERR_INVALID, "y must be a contiguous fp32 host tensor of [n, hidden]")
+        call("gpeed_moe_forward_host", self.ctx.handle, self.layer_id, _ptr(x), dt, n, _ptr(y))
+        return y

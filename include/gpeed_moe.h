@@ -218,6 +218,15 @@ GPEED_API int gpeed_synth_iq3xxs(void* dst_dev, uint64_t seed, uint64_t stream, 
  * topk_w (device [n_tok][K] or NULL) receive the routing. */
 GPEED_API int gpeed_moe_forward(gpeed_ctx* ctx, int layer, const void* x_dev, int x_dtype, int n_tok, float* y_dev,
                       const int* forced_topk_dev, int* topk_ids_dev, float* topk_w_dev, void* stream);
+/* The same layer on the caller's HOST buffers, as the reference's callers
+ * hold them (Model::moe_forward / moe_batch, model.cpp:692-756 and
+ * model_batch.cpp:165-281, take and fill host vectors): x_host [n_tok][H]
+ * (bf16 or fp32 per x_dtype), y_host [n_tok][H] fp32.  The input goes to the
+ * device through the context's pinned staging on the context's own stream,
+ * and the call returns once y is on the host (synchronous, like the
+ * reference call).  Calls on one context are serialised. */
+GPEED_API int gpeed_moe_forward_host(gpeed_ctx* ctx, int layer, const void* x_host, int x_dtype, int n_tok,
+                                     float* y_host);
 
 /* ---- Expert parallelism (no counterpart in the reference: it runs every
  * expert on one host).  Experts split into equal contiguous ranges, one per

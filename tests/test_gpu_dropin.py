@@ -95,3 +95,35 @@ def test_reference_style_cpp_caller_on_host_buffers(tmp_path):
     assert rel_l2(g, want_g) < GEMV_TOL
     assert rel_l2(d, want_d) < GEMV_TOL
     assert rel_l2(gb, want_gb) < GEMV_TOL
+
+
+def test_moe_forward_host_buffers_match_the_device_forward():
+    """gpeed_moe_forward_host takes and fills host buffers, as the callers of
+    Model::moe_forward / moe_batch (model.cpp:692-756, model_batch.cpp:165-281)
+    hold them, and gives the device forward's result: one token (the fused
+    kernel), 5 tokens in fp32 (one fused launch per token) and 64 tokens (the
+    tensor-core path).  The fused kernel's sums into y land in launch order,
+    so the comparison is to rounding; the oracle checks of the device forward
+    are in test_gpu_parity.py."""
+    import torch
+
+    from gpeed_b200 import Context, GpeedError, MoeConfig, MoeLayer
+    ctx = Context(0)
+    try:
+        cfg = MoeConfig()
+        rng = np.random.default_rng(31)
+        router = (rng.standard_normal((cfg.n_experts, cfg.hidden)) * 0.02).astype(np.float32)
+        layer = MoeLayer(ctx, cfg).synth(router, None, 42, 100)
+        for n, dt in ((1, torch.bfloat16), (5, torch.float32), (64, torch.bfloat16)):
+            x = torch.from_numpy(rng.standard_normal((n, cfg.hidden)).astype(np.float32)).to(dt)
+            y_dev = layer.forward(x.cuda()).cpu().numpy()
+            y_host = layer.forward_host(x).numpy()
+            ctx.check()
+            assert np.isfinite(y_host).all()
+            assert rel_l2(y_host, y_dev) < 1e-5, (n, rel_l2(y_host, y_dev))
+            y_again = layer.forward_host(x).numpy()  # the staging is reused
+            assert rel_l2(y_again, y_dev) < 1e-5
+        with pytest.raises(GpeedError):
+            layer.forward_host(torch.zeros(1, cfg.hidden).cuda())
+    finally:
+        ctx.close()
