@@ -11,7 +11,6 @@ next forward gives the same result as before.  The reference has no device and
 only throws (weights.cpp:21,25)."""
 import re
 
-import numpy as np
 import pytest
 import torch
 
