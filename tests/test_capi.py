@@ -39,6 +39,10 @@ def test_argument_errors_need_no_device():
     assert b"multiple of block size" in lib.gpeed_last_error()
     rc = lib.gpeed_moe_forward(None, 0, None, 30, 1, None, None, None, None, None)
     assert rc == _capi.ERR_INVALID
+    rc = lib.gpeed_moe_forward_host(None, 0, None, 30, 1, None)
+    assert rc == _capi.ERR_INVALID
+    rc = lib.gpeed_moe_decode_ep(None, 0, None, 30, None, None, None, None)
+    assert rc == _capi.ERR_INVALID
 
 
 def test_ctx_create_fails_cleanly_without_a_device():
